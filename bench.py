@@ -1,0 +1,401 @@
+#!/usr/bin/env python
+"""Benchmark of the differentiable render path: rasterize -> interpolate -> texture -> antialias,
+forward and backward, in Mpixel/s, on BASELINE configuration 5.
+
+Workload (synthetic, seeded): icosphere level 8 (655,362 vertices, 1,310,720 triangles) with
+N(0, 0.01) radial displacement, 64 random orbit cameras at 1024x1024, interpolation of
+[u, v, nx, ny, nz] with all derivatives, a 4096x4096x3 uniform texture sampled trilinearly
+(its mip chain rebuilt every step, as the texture requires gradients), antialiasing, MSE against
+a random target, backward to the texture and the clip-space positions. The 64 views are sharded
+across the ranks (strong scaling); the texture gradient is summed with an NCCL all-reduce.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+One JSON line is printed by rank 0. ``--impl reference`` times the CPU oracle (the reference's
+algorithm restated on the host, all host threads) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "tests"))
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+METRIC = "fwd+bwd Mpixel/s of rasterize→interpolate→texture→antialias at 1/2/4/8 B200"
+UNIT = "Mpixel/s"
+ATTR_CHANNELS, DIFF_CHANNELS, TEX_CHANNELS = 5, 5, 3
+# Kernels each wrapper launches per call (the visibility stage adds 4 when it bins triangles).
+LAUNCHES = {
+    "raster_visibility": 2, "resolve_fwd": 1, "resolve_bwd": 1, "interpolate_fwd": 1,
+    "interpolate_bwd": 1, "texture_fwd": 1, "texture_bwd": 1, "mip_build": 1, "mip_adjoint": 1,
+    "edge_neighbours": 2, "antialias_fwd": 1, "antialias_bwd": 1,
+}  # fmt: skip
+
+
+def stage_bytes(pixels: int, num_vert: int, views: int, stack_bytes: int, tex_bytes: int) -> dict:
+    """Algorithmic bytes per launch of each stage: API-level tensor reads and writes, fp32.
+
+    Per pixel (C attribute channels, D differentiated channels, Ct texture channels):
+    rasterize writes rast + rast_db (32) and its backward reads their gradients (32);
+    interpolate reads rast, rast_db (32) and writes 4C + 8D, backward reads 4C + 8D + 32 and writes
+    32; texture reads uv, uv_da (24) and writes 4Ct, backward reads 4Ct + 24 and writes 24;
+    antialias reads colour and rast (4Ct + 16) and writes 4Ct, backward reads 8Ct + 16 and writes
+    4Ct. Per call: positions (16 B per vertex and view) for the rasterizer, the mip stack for the
+    build and its adjoint.
+    """
+    c, d, ct = ATTR_CHANNELS, DIFF_CHANNELS, TEX_CHANNELS
+    pos_bytes = views * num_vert * 16
+    return {
+        "raster_visibility": pos_bytes + pixels * 8,
+        "resolve_fwd": pixels * (8 + 32) + pos_bytes,
+        "interpolate_fwd": pixels * (32 + 4 * c + 8 * d),
+        "mip_build": stack_bytes + tex_bytes,
+        "texture_fwd": pixels * (24 + 4 * ct),
+        "antialias_fwd": pixels * (16 + 8 * ct),
+        "antialias_bwd": pixels * (16 + 12 * ct),
+        "texture_bwd": pixels * (48 + 4 * ct) + 2 * tex_bytes,
+        "mip_adjoint": 2 * stack_bytes + tex_bytes,
+        "interpolate_bwd": pixels * (64 + 4 * c + 8 * d),
+        "resolve_bwd": pixels * (8 + 32) + 2 * pos_bytes,
+    }
+
+
+def step_bytes(pixels, num_vert, views, stack_bytes, tex_bytes) -> int:
+    """Whole-step algorithmic bytes: 468 B per pixel at C=5, D=5, Ct=3 plus per-call terms."""
+    c, d, ct = ATTR_CHANNELS, DIFF_CHANNELS, TEX_CHANNELS
+    per_px = 32 + (32 + 4 * c + 8 * d) + (24 + 4 * ct) + (16 + 8 * ct)
+    per_px += (16 + 12 * ct) + (48 + 4 * ct) + (64 + 4 * c + 8 * d) + 32
+    return pixels * per_px + views * num_vert * 16 * 5 + 3 * stack_bytes
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons every 200 ms while active."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: str) -> None:
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )  # fmt: skip
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            if self.thread is not None:
+                self.thread.join(timeout=2)
+
+    def summary(self) -> dict:
+        mhz, max_mhz, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                max_mhz = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": max_mhz,
+                "reasons": sorted(reasons), "samples": len(mhz)}  # fmt: skip
+
+
+def gpu_id(dev: torch.device) -> str:
+    """nvidia-smi id of a torch device (its UUID, valid under CUDA_VISIBLE_DEVICES too)."""
+    try:
+        return "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:  # noqa: BLE001
+        return str(dev.index or 0)
+
+
+def peaks() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def build_scene(views_total: int, res: int, subdiv: int, tex_size: int, rank: int, world: int):
+    import scenes
+
+    sc = scenes.config5_scene(views=views_total, resolution=res, subdivisions=subdiv, tex_size=tex_size)
+    per = views_total // world
+    pos = sc["pos"][rank * per : (rank + 1) * per].contiguous()
+    gen = torch.Generator().manual_seed(1234)
+    target = torch.rand(views_total, res, res, TEX_CHANNELS, generator=gen)[rank * per : (rank + 1) * per]
+    return pos, sc["tri"], sc["attr"], sc["tex"], target.contiguous()
+
+
+def run_ours(args) -> None:
+    import diffrast_b200 as dr
+    from diffrast_b200 import _kernels as K
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    if args.views % world:
+        raise SystemExit(f"--views {args.views} must be divisible by the number of GPUs {world}")
+
+    pos_cpu, tri_cpu, attr_cpu, tex_cpu, target_cpu = build_scene(
+        args.views, args.res, args.subdiv, args.tex, rank, world)
+    views, res = pos_cpu.shape[0], args.res
+    ctx = dr.RasterizeContext(dev)
+    tri = tri_cpu.to(dev)
+    attr = attr_cpu.to(dev)
+    tex = tex_cpu.to(dev).requires_grad_(True)
+    pos = pos_cpu.to(dev).requires_grad_(True)
+    target = target_cpu.to(dev)
+    topo = dr.antialias_construct_topology_hash(tri)
+
+    def step(pos_in, target_in):
+        pos_in.grad = None
+        tex.grad = None
+        rast, rast_db = dr.rasterize(ctx, pos_in, tri, (res, res))
+        out, out_da = dr.interpolate(attr, rast, tri, rast_db=rast_db, diff_attrs="all")
+        color = dr.texture(tex, out[..., 0:2], out_da[..., 0:4], filter_mode="linear-mipmap-linear")
+        image = dr.antialias(color, rast, pos_in, tri, topology_hash=topo)
+        loss = ((image - target_in) ** 2).mean()
+        loss.backward()
+        if world > 1:
+            dist.all_reduce(tex.grad)
+        return loss
+
+    for _ in range(args.warmup):
+        step(pos, target)
+    torch.cuda.synchronize()
+
+    def timed_loop(body):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            body()
+        end.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ms = torch.tensor([start.elapsed_time(end)], device=dev)
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        return ms.item() / args.steps
+
+    with ClockSampler(gpu_id(dev)) as clocks:
+        with K.record_timings() as stages:
+            ms = timed_loop(lambda: step(pos, target))
+        torch.cuda.synchronize()
+    stage_ms = {name: sum(s.elapsed_time(e) for s, e in pairs) / args.steps for name, pairs in stages.items()}
+    stage_calls = {name: len(pairs) / args.steps for name, pairs in stages.items()}
+
+    # End to end through the public API: inputs copied from pinned host memory every step and the
+    # loss read back, all inside the timed region.
+    pos_host = pos_cpu.pin_memory()
+    target_host = target_cpu.pin_memory()
+    pos_e2e = torch.empty_like(pos_cpu, device=dev)
+    target_e2e = torch.empty_like(target_cpu, device=dev)
+
+    def e2e_step():
+        pos_e2e.copy_(pos_host, non_blocking=True)
+        target_e2e.copy_(target_host, non_blocking=True)
+        leaf = pos_e2e.requires_grad_(True)
+        loss = step(leaf, target_e2e)
+        loss.item()
+
+    e2e_ms = timed_loop(e2e_step)
+
+    pixels_total = args.views * res * res
+    value = pixels_total / (ms / 1e3) / 1e6
+    e2e_value = pixels_total / (e2e_ms / 1e3) / 1e6
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    tex_bytes = tex.numel() * 4
+    stack_bytes = int(tex_bytes * 4 / 3)
+    pixels = views * res * res
+    algo = stage_bytes(pixels, pos.shape[1], views, stack_bytes - tex_bytes, tex_bytes)
+    dominant = max(stage_ms, key=stage_ms.get)
+    per_launch_ms = stage_ms[dominant] / max(1.0, stage_calls[dominant])
+    # Stages launched several times per step (one mip level per launch) are costed per step.
+    per_launch_bytes = algo.get(dominant, 0) / max(1.0, stage_calls[dominant])
+    peak, peak_kind = peaks()
+    achieved = per_launch_bytes / (per_launch_ms / 1e3) / 1e9
+    launches = sum(LAUNCHES.get(n, 1) * c for n, c in stage_calls.items())
+    clock = clocks.summary()
+    line = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 3),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded icosphere-8, random orbit cameras, uniform texture and target)",
+        "config": {
+            "workload": f"BASELINE config 5: {args.views} views {res}x{res}, icosphere-{args.subdiv} "
+                        f"({tri.shape[0]} tris), tex {args.tex}^2x3 linear-mipmap-linear, antialias, "
+                        "MSE, fwd+bwd to tex and pos",
+            "views": args.views, "resolution": res, "triangles": int(tri.shape[0]),
+            "vertices": int(pos.shape[1]), "tex": args.tex, "parallelism": f"views sharded dp{world}",
+            "l2": "inputs larger than L2 (pos 671 MB, rast 1 GB per step), no flush",
+        },
+        "e2e": {"value": round(e2e_value, 1), "unit": UNIT,
+                "h2d_bytes_per_step": pos_cpu.numel() * 4 + target_cpu.numel() * 4,
+                "d2h_bytes_per_step": 4},
+        "gpu_launches": int(round(launches * args.steps)),
+        "roofline": {
+            "bound": "hbm", "kernel": dominant, "achieved": round(achieved, 1), "peak": peak,
+            "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+            "traffic": None, "algorithmic_bytes_per_launch": int(per_launch_bytes),
+            "ms_per_launch": round(per_launch_ms, 4),
+        },
+        "step_roofline": {
+            "algorithmic_bytes": step_bytes(pixels, pos.shape[1], views, stack_bytes - tex_bytes, tex_bytes),
+            "frac_of_peak": round(step_bytes(pixels, pos.shape[1], views, stack_bytes - tex_bytes,
+                                             tex_bytes) / (ms / 1e3) / 1e9 / peak, 4),
+        },
+        "stages_ms": {k: round(v, 3) for k, v in sorted(stage_ms.items(), key=lambda kv: -kv[1])},
+        "clocks": clock,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args, warmup=1, steps=1)
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def cpu_sample(args):
+    """A bounded CPU sample of the workload: one view of the same scene at a small resolution."""
+    import oracle
+
+    pos, tri, attr, tex, _ = build_scene(1, args.cpu_res, args.subdiv, args.tex, 0, 1)
+    target = torch.rand(1, args.cpu_res, args.cpu_res, 3, generator=torch.Generator().manual_seed(7))
+    res = (args.cpu_res, args.cpu_res)
+
+    def step():
+        p = pos.clone().requires_grad_(True)
+        t = tex.clone().requires_grad_(True)
+        rast, rast_db = oracle.rasterize(p, tri, res)
+        out, out_da = oracle.interpolate(attr, rast, tri, rast_db, list(range(5)))
+        color = oracle.texture(t, out[..., 0:2].contiguous(), out_da[..., 0:4].contiguous(), None,
+                               None, "linear-mipmap-linear", "wrap")
+        image = oracle.antialias(color, rast, p, tri)
+        loss = ((image - target) ** 2).mean()
+        loss.backward()
+        return loss.item()
+
+    return step, res
+
+
+def cpu_baseline(args, warmup: int, steps: int) -> dict:
+    torch.set_num_threads(os.cpu_count() or 1)
+    step, res = cpu_sample(args)
+    for _ in range(warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    sec = (time.perf_counter() - t0) / steps
+    return {
+        "value": round(res[0] * res[1] / sec / 1e6, 6),
+        "unit": UNIT,
+        "cores": torch.get_num_threads(),
+        "kind": "port",
+        "sample": f"1 of {args.views} views of the same scene at {res[0]}x{res[1]} px (full mesh and "
+                  f"texture), fwd+bwd, {sec:.2f} s per step, CPU oracle (brute-force visibility "
+                  "as the reference backend)",
+    }
+
+
+def run_reference(args) -> None:
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    base = cpu_baseline(args, warmup=args.warmup, steps=args.steps)
+    line = {
+        "metric": METRIC, "value": base["value"], "unit": UNIT, "impl": "reference",
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
+        "warmup": args.warmup, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded)",
+        "config": {"workload": f"BASELINE config 5 (sample: {base['sample']})"},
+        "cpu_baseline": base,
+        "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }  # fmt: skip
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=10)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    parser.add_argument("--views", type=int, default=64)
+    parser.add_argument("--res", type=int, default=1024)
+    parser.add_argument("--subdiv", type=int, default=8)
+    parser.add_argument("--tex", type=int, default=4096)
+    parser.add_argument("--cpu-res", type=int, default=8)
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,52 @@
+"""diffrast_b200: diffrast's differentiable render path on hand-written B200 (sm_100a) kernels.
+
+The public names are those of ``diffrast`` (``src/diffrast/__init__.py:21-41``): switching is
+changing the import (``import diffrast_b200 as dr``, or ``diffrast_b200.torch``).
+"""
+
+from diffrast_b200.backends import get_backend_name, set_backend
+from diffrast_b200.compat import (
+    install_as_diffrast,
+    install_as_nvdiffrast,
+    uninstall_as_diffrast,
+    uninstall_as_nvdiffrast,
+)
+from diffrast_b200.context import RasterizeContext, RasterizeCudaContext, RasterizeGLContext
+from diffrast_b200.log import get_log_level, set_log_level
+from diffrast_b200.ops import (
+    MipStack,
+    antialias,
+    antialias_construct_topology_hash,
+    interpolate,
+    rasterize,
+    texture,
+    texture_construct_mip,
+)
+from diffrast_b200.peeling import DepthPeeler
+from diffrast_b200.topology import TopologyHash
+
+__version__ = "0.1.0"
+
+__all__ = [
+    "DepthPeeler",
+    "MipStack",
+    "RasterizeContext",
+    "RasterizeCudaContext",
+    "RasterizeGLContext",
+    "TopologyHash",
+    "__version__",
+    "antialias",
+    "antialias_construct_topology_hash",
+    "get_backend_name",
+    "get_log_level",
+    "install_as_diffrast",
+    "install_as_nvdiffrast",
+    "interpolate",
+    "rasterize",
+    "set_backend",
+    "set_log_level",
+    "texture",
+    "texture_construct_mip",
+    "uninstall_as_diffrast",
+    "uninstall_as_nvdiffrast",
+]

@@ -1,0 +1,178 @@
+"""Autograd functions over the CUDA kernels. Inputs arrive validated (see ``ops.py``).
+
+Each backward runs hand-written kernels with no second-order terms, so a backward pass asked to
+build a graph (``create_graph=True``) raises, like the reference's first-order guard
+(diffrast backends/_autograd.py:11-35).
+"""
+
+from __future__ import annotations
+
+import functools
+
+import torch
+from torch import Tensor
+
+from diffrast_b200 import _kernels as K
+
+
+def first_order(op: str):
+    def decorate(backward):
+        @functools.wraps(backward)
+        def guarded(ctx, *grads):
+            if torch.is_grad_enabled():
+                raise RuntimeError(
+                    f"{op} in diffrast_b200 has no second-order gradients, but its backward pass "
+                    "was run with create_graph=True."
+                )
+            return backward(ctx, *grads)
+
+        return guarded
+
+    return decorate
+
+
+def _saveable(t: Tensor | None) -> Tensor | None:
+    # A tensor made in inference mode cannot be saved for backward, but a copy of it can.
+    return t.clone() if t is not None and t.is_inference() else t
+
+
+class Rasterize(torch.autograd.Function):
+    """Visibility, then rast / rast_db; gradients reach pos through the barycentric resolve."""
+
+    @staticmethod
+    def forward(ctx, pos: Tensor, tri: Tensor, height: int, width: int, grad_db: bool,
+                prev_keys: Tensor | None):
+        keys = K.raster_keys(pos, tri, height, width, prev_keys)
+        rast, rast_db = K.resolve_fwd(pos, tri, keys)
+        ctx.save_for_backward(_saveable(pos), _saveable(tri), keys)
+        ctx.grad_db = grad_db
+        ctx.mark_non_differentiable(keys)
+        if not grad_db:
+            ctx.mark_non_differentiable(rast_db)
+        return rast, rast_db, keys
+
+    @staticmethod
+    @first_order("rasterize")
+    def backward(ctx, grad_rast, grad_db, _grad_keys):
+        pos, tri, keys = ctx.saved_tensors
+        if grad_rast is None:
+            grad_rast = torch.zeros((*keys.shape, 4), dtype=pos.dtype, device=pos.device)
+        use_db = ctx.grad_db and grad_db is not None
+        grad_pos = K.resolve_bwd(pos, tri, keys, K.aligned(grad_rast),
+                                 K.aligned(grad_db) if use_db else None)
+        return grad_pos, None, None, None, None, None
+
+
+class Interpolate(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, attr: Tensor, rast: Tensor, rast_db: Tensor | None, tri: Tensor,
+                diff: Tensor | None):
+        attr3 = (attr if attr.ndim == 3 else attr[None]).contiguous()
+        out, out_da = K.interpolate_fwd(attr3, rast, rast_db, tri, diff)
+        ctx.save_for_backward(*(_saveable(t) for t in (attr3, rast, rast_db, tri, diff)))
+        ctx.attr_shape = attr.shape
+        ctx.has_da = diff is not None
+        ctx.rast_db_given = rast_db is not None
+        if diff is None:
+            ctx.mark_non_differentiable(out_da)
+        return out, out_da
+
+    @staticmethod
+    @first_order("interpolate")
+    def backward(ctx, grad_out, grad_out_da):
+        attr3, rast, rast_db, tri, diff = ctx.saved_tensors
+        if grad_out is None:
+            grad_out = torch.zeros((*rast.shape[:3], attr3.shape[2]), device=rast.device)
+        use_da = ctx.has_da and grad_out_da is not None
+        need_attr = ctx.needs_input_grad[0]
+        grad_attr, grad_rast, grad_db = K.interpolate_bwd(
+            attr3, rast, rast_db, tri, diff if use_da else None, grad_out.contiguous(),
+            grad_out_da.contiguous() if use_da else None, need_attr,
+        )
+        if ctx.rast_db_given and grad_db is None:
+            grad_db = torch.zeros_like(rast)
+        if not ctx.rast_db_given:
+            grad_db = None
+        if grad_attr is not None:
+            grad_attr = grad_attr.view(ctx.attr_shape)
+        return grad_attr, grad_rast, grad_db, None, None
+
+
+class MipChain(torch.autograd.Function):
+    """Levels 1.. of a texture by repeated area-weighted halving; backward is the adjoint chain."""
+
+    @staticmethod
+    def forward(ctx, tex: Tensor, count: int):
+        levels = []
+        level = tex
+        for _ in range(count):
+            level = K.mip_down(level)
+            levels.append(level)
+        ctx.shapes = [tex.shape, *(lv.shape for lv in levels)]
+        ctx.device = tex.device
+        return tuple(levels)
+
+    @staticmethod
+    @first_order("texture_construct_mip")
+    def backward(ctx, *grads):
+        shapes = ctx.shapes
+        # Gradient of the coarsest level first, pushed down one step at a time.
+        carry = None
+        for index in range(len(shapes) - 1, 0, -1):
+            g = grads[index - 1]
+            g = torch.zeros(shapes[index], device=ctx.device) if g is None else g.contiguous().clone()
+            if carry is not None:
+                g += carry
+            fine = torch.zeros(shapes[index - 1], device=ctx.device)
+            K.mip_down_bwd(g, fine)
+            carry = fine
+        return carry, None
+
+
+class Texture(torch.autograd.Function):
+    """Lookup in a list of levels (base texture first); gradients to every level and to uv,
+    uv_da and the level-of-detail bias as the filter mode allows."""
+
+    @staticmethod
+    def forward(ctx, uv, uv_da, bias, mode: int, boundary: int, *levels):
+        levels = [lv.contiguous() for lv in levels]
+        out = K.texture_fwd(list(levels), uv, uv_da, bias, mode, boundary)
+        ctx.save_for_backward(*(_saveable(t) for t in (uv, uv_da, bias, *levels)))
+        ctx.settings = (mode, boundary, uv_da is not None, bias is not None, len(levels))
+        return out
+
+    @staticmethod
+    @first_order("texture")
+    def backward(ctx, grad_out):
+        mode, boundary, has_da, has_bias, count = ctx.settings
+        saved = ctx.saved_tensors
+        uv, uv_da, bias, levels = saved[0], saved[1], saved[2], list(saved[3:])
+        need = ctx.needs_input_grad
+        want_uv = need[0] and mode > 0
+        want_da = need[1] and has_da and mode == 3
+        want_bias = need[2] and has_bias and mode == 3
+        grads, g_uv, g_da, g_bias = K.texture_bwd(levels, uv, uv_da, bias, mode, boundary,
+                                                  grad_out.contiguous(), want_uv, want_da,
+                                                  want_bias)
+        level_grads = [g if need[5 + i] else None for i, g in enumerate(grads)]
+        return (g_uv, g_da, g_bias, None, None, *level_grads)
+
+
+class Antialias(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, color: Tensor, rast: Tensor, pos: Tensor, tri: Tensor, neighbours: Tensor,
+                boost: float):
+        pos3 = pos if pos.ndim == 3 else pos[None]
+        out = K.antialias_fwd(color, rast, pos3, tri, neighbours)
+        ctx.save_for_backward(*(_saveable(t) for t in (color, rast, pos3, tri, neighbours)))
+        ctx.boost = boost
+        ctx.pos_shape = pos.shape
+        return out
+
+    @staticmethod
+    @first_order("antialias")
+    def backward(ctx, grad_out):
+        color, rast, pos3, tri, neighbours = ctx.saved_tensors
+        grad_color, grad_pos = K.antialias_bwd(color, rast, pos3, tri, neighbours,
+                                               grad_out.contiguous(), ctx.boost)
+        return grad_color, None, grad_pos.view(ctx.pos_shape), None, None, None

@@ -1,0 +1,309 @@
+"""Tensor-level calls of the C ABI: outputs and scratch come from PyTorch's caching allocator,
+launches go to the current CUDA stream of the tensors' device.
+
+Scratch tensors are released when a function returns while its kernels may still be queued; the
+caching allocator only hands that memory to later work on the same stream, so this is safe.
+"""
+
+from __future__ import annotations
+
+import contextlib
+import functools
+from ctypes import byref, c_int64
+
+import torch
+from torch import Tensor
+
+from diffrast_b200 import _native as N
+
+# Optional per-stage timing: when ``timings`` is a dict, every wrapper below records a pair of CUDA
+# events around its launches on the current stream, keyed by stage name. bench.py uses this to
+# time the dominant kernel inside its timed region.
+timings: dict[str, list] | None = None
+
+
+def timed(name: str):
+    def decorate(fn):
+        @functools.wraps(fn)
+        def wrapper(*args, **kwargs):
+            if timings is None:
+                return fn(*args, **kwargs)
+            start = torch.cuda.Event(enable_timing=True)
+            end = torch.cuda.Event(enable_timing=True)
+            start.record()
+            out = fn(*args, **kwargs)
+            end.record()
+            timings.setdefault(name, []).append((start, end))
+            return out
+
+        return wrapper
+
+    return decorate
+
+
+@contextlib.contextmanager
+def record_timings():
+    """Collect stage timings inside the block; yields the dict of event pairs."""
+    global timings
+    timings = {}
+    try:
+        yield timings
+    finally:
+        timings = None
+
+
+# Binned-triangle capacity of the rasterizer's setup list, remembered per problem shape so that
+# the list is sized right from the second call on.
+_capacity: dict[tuple, int] = {}
+
+
+def aligned(t: Tensor) -> Tensor:
+    """Contiguous and 16-byte aligned (rows of four floats are read as float4)."""
+    t = t.contiguous()
+    if t.data_ptr() % 16:
+        t = t.clone()
+    return t
+
+
+def _scratch(nbytes: int, device: torch.device) -> Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+@timed("raster_visibility")
+def raster_keys(pos: Tensor, tri: Tensor, height: int, width: int, prev_keys: Tensor | None) -> Tensor:
+    """Packed visibility keys ``[batch, height, width]`` int64 of the nearest layer behind
+    ``prev_keys`` (all layers when ``None``)."""
+    lib, dev = N.lib(), pos.device
+    s = N.stream(dev)
+    batch, num_vert, num_tri = pos.shape[0], pos.shape[1], tri.shape[0]
+    keys = torch.empty((batch, height, width), dtype=torch.int64, device=dev)
+    shape_key = (dev, batch, num_tri, height, width)
+    cap = _capacity.get(shape_key, max(1024, min(batch * num_tri, 1 << 16)))
+    binned, pairs = c_int64(0), c_int64(0)
+    for _ in range(2):
+        ws = _scratch(lib.dr_raster_setup_workspace_bytes(cap), dev)
+        N.check(
+            lib.dr_raster_setup(pos.data_ptr(), tri.data_ptr(), batch, num_vert, num_tri, height,
+                                width, N.ptr(prev_keys), keys.data_ptr(), ws.data_ptr(),
+                                ws.numel(), cap, s),
+            "dr_raster_setup",
+        )  # fmt: skip
+        N.check(lib.dr_raster_counts(ws.data_ptr(), byref(binned), byref(pairs), s), "dr_raster_counts")
+        if binned.value <= cap:
+            break
+        # The list overflowed: rerun with room for every binned triangle (the direct writes of
+        # the first run are repeated; they are idempotent minima).
+        cap = binned.value + binned.value // 4
+        _capacity[shape_key] = cap
+    if binned.value > cap:
+        raise RuntimeError("diffrast_b200: binned triangle count changed between identical runs")
+    if binned.value > 0 and pairs.value > 0:
+        bws = _scratch(lib.dr_raster_bin_workspace_bytes(batch, height, width, pairs.value), dev)
+        N.check(
+            lib.dr_raster_tiles(pos.data_ptr(), tri.data_ptr(), batch, num_vert, num_tri, height,
+                                width, N.ptr(prev_keys), keys.data_ptr(), ws.data_ptr(),
+                                binned.value, pairs.value, bws.data_ptr(), bws.numel(), s),
+            "dr_raster_tiles",
+        )  # fmt: skip
+    return keys
+
+
+@timed("resolve_fwd")
+def resolve_fwd(pos: Tensor, tri: Tensor, keys: Tensor) -> tuple[Tensor, Tensor]:
+    batch, height, width = keys.shape
+    rast = torch.empty((batch, height, width, 4), dtype=torch.float32, device=pos.device)
+    rast_db = torch.empty_like(rast)
+    N.check(
+        N.lib().dr_raster_resolve_fwd(pos.data_ptr(), tri.data_ptr(), keys.data_ptr(), batch,
+                                      pos.shape[1], tri.shape[0], height, width, rast.data_ptr(),
+                                      rast_db.data_ptr(), N.stream(pos.device)),
+        "dr_raster_resolve_fwd",
+    )  # fmt: skip
+    return rast, rast_db
+
+
+@timed("resolve_bwd")
+def resolve_bwd(pos: Tensor, tri: Tensor, keys: Tensor, grad_rast: Tensor,
+                grad_db: Tensor | None) -> Tensor:
+    batch, height, width = keys.shape
+    grad_pos = torch.zeros_like(pos)
+    N.check(
+        N.lib().dr_raster_resolve_bwd(pos.data_ptr(), tri.data_ptr(), keys.data_ptr(), batch,
+                                      pos.shape[1], tri.shape[0], height, width,
+                                      grad_rast.data_ptr(), N.ptr(grad_db), grad_pos.data_ptr(),
+                                      N.stream(pos.device)),
+        "dr_raster_resolve_bwd",
+    )  # fmt: skip
+    return grad_pos
+
+
+_diff_tables: dict[tuple, Tensor] = {}
+
+
+def diff_table(channels: tuple[int, ...], device: torch.device) -> Tensor | None:
+    """Device copy of the ``diff_attrs`` channel list, made once per list and device."""
+    if not channels:
+        return None
+    key = (channels, device)
+    table = _diff_tables.get(key)
+    if table is None:
+        table = torch.tensor(channels, dtype=torch.int32, device=device)
+        _diff_tables[key] = table
+    return table
+
+
+@timed("interpolate_fwd")
+def interpolate_fwd(attr3: Tensor, rast: Tensor, rast_db: Tensor | None, tri: Tensor,
+                    diff: Tensor | None) -> tuple[Tensor, Tensor]:
+    batch, height, width, _ = rast.shape
+    channels = attr3.shape[2]
+    num_diff = 0 if diff is None else diff.shape[0]
+    out = torch.empty((batch, height, width, channels), dtype=torch.float32, device=rast.device)
+    out_da = torch.empty((batch, height, width, 2 * num_diff), dtype=torch.float32, device=rast.device)
+    N.check(
+        N.lib().dr_interpolate_fwd(attr3.data_ptr(), attr3.shape[0], attr3.shape[1], channels,
+                                   rast.data_ptr(), N.ptr(rast_db), tri.data_ptr(), tri.shape[0],
+                                   N.ptr(diff), num_diff, batch, height, width, out.data_ptr(),
+                                   out_da.data_ptr(), N.stream(rast.device)),
+        "dr_interpolate_fwd",
+    )  # fmt: skip
+    return out, out_da
+
+
+@timed("interpolate_bwd")
+def interpolate_bwd(attr3, rast, rast_db, tri, diff, grad_out, grad_out_da, need_attr):
+    batch, height, width, _ = rast.shape
+    channels = attr3.shape[2]
+    num_diff = 0 if diff is None else diff.shape[0]
+    grad_attr = torch.zeros_like(attr3) if need_attr else None
+    grad_rast = torch.empty_like(rast)
+    grad_db = torch.empty_like(rast) if grad_out_da is not None else None
+    N.check(
+        N.lib().dr_interpolate_bwd(attr3.data_ptr(), attr3.shape[0], attr3.shape[1], channels,
+                                   rast.data_ptr(), N.ptr(rast_db), tri.data_ptr(), tri.shape[0],
+                                   N.ptr(diff), num_diff, batch, height, width,
+                                   grad_out.data_ptr(), N.ptr(grad_out_da), N.ptr(grad_attr),
+                                   grad_rast.data_ptr(), N.ptr(grad_db), N.stream(rast.device)),
+        "dr_interpolate_bwd",
+    )  # fmt: skip
+    return grad_attr, grad_rast, grad_db
+
+
+def _level_tables(levels: list[Tensor], cube: bool):
+    heights = [lv.shape[-3] for lv in levels]
+    widths = [lv.shape[-2] for lv in levels]
+    strides = [0 if lv.shape[0] == 1 else lv[0].numel() for lv in levels]
+    return N.int32_array(heights), N.int32_array(widths), N.int64_array(strides)
+
+
+@timed("texture_fwd")
+def texture_fwd(levels: list[Tensor], uv: Tensor, uv_da: Tensor | None, bias: Tensor | None,
+                mode: int, boundary: int) -> Tensor:
+    batch, height, width = uv.shape[:3]
+    channels = levels[0].shape[-1]
+    out = torch.empty((batch, height, width, channels), dtype=torch.float32, device=uv.device)
+    hs, ws, bs = _level_tables(levels, boundary == 3)
+    N.check(
+        N.lib().dr_texture_fwd(N.pointer_array([lv.data_ptr() for lv in levels]), hs, ws, bs,
+                               len(levels), channels, uv.data_ptr(), N.ptr(uv_da), N.ptr(bias),
+                               batch, height, width, mode, boundary, out.data_ptr(),
+                               N.stream(uv.device)),
+        "dr_texture_fwd",
+    )  # fmt: skip
+    return out
+
+
+@timed("texture_bwd")
+def texture_bwd(levels, uv, uv_da, bias, mode, boundary, grad_out, want_uv, want_da, want_bias):
+    batch, height, width = uv.shape[:3]
+    channels = levels[0].shape[-1]
+    grads = [torch.zeros_like(lv) for lv in levels]
+    grad_uv = torch.empty_like(uv) if want_uv else None
+    grad_da = torch.empty_like(uv_da) if want_da else None
+    grad_bias = torch.empty_like(bias) if want_bias else None
+    hs, ws, bs = _level_tables(levels, boundary == 3)
+    N.check(
+        N.lib().dr_texture_bwd(N.pointer_array([lv.data_ptr() for lv in levels]),
+                               N.pointer_array([g.data_ptr() for g in grads]), hs, ws, bs,
+                               len(levels), channels, uv.data_ptr(), N.ptr(uv_da), N.ptr(bias),
+                               batch, height, width, mode, boundary, grad_out.data_ptr(),
+                               N.ptr(grad_uv), N.ptr(grad_da), N.ptr(grad_bias),
+                               N.stream(uv.device)),
+        "dr_texture_bwd",
+    )  # fmt: skip
+    return grads, grad_uv, grad_da, grad_bias
+
+
+def _images(level: Tensor) -> int:
+    return level.shape[0] * (6 if level.ndim == 5 else 1)
+
+
+@timed("mip_build")
+def mip_down(level: Tensor) -> Tensor:
+    h, w, c = level.shape[-3], level.shape[-2], level.shape[-1]
+    out = torch.empty((*level.shape[:-3], (h + 1) // 2, (w + 1) // 2, c), dtype=torch.float32,
+                      device=level.device)
+    N.check(N.lib().dr_mip_downsample(level.data_ptr(), _images(level), h, w, c, out.data_ptr(),
+                                      N.stream(level.device)), "dr_mip_downsample")  # fmt: skip
+    return out
+
+
+@timed("mip_adjoint")
+def mip_down_bwd(grad_coarse: Tensor, grad_fine: Tensor) -> None:
+    """Adds the adjoint of one mip step of ``grad_coarse`` into ``grad_fine`` (in place)."""
+    h, w, c = grad_fine.shape[-3], grad_fine.shape[-2], grad_fine.shape[-1]
+    N.check(N.lib().dr_mip_downsample_bwd(grad_coarse.data_ptr(), _images(grad_fine), h, w, c,
+                                          grad_fine.data_ptr(), N.stream(grad_fine.device)),
+            "dr_mip_downsample_bwd")  # fmt: skip
+
+
+@timed("edge_neighbours")
+def edge_neighbours(tri: Tensor) -> Tensor:
+    num_tri = tri.shape[0]
+    out = torch.empty((num_tri, 3), dtype=torch.int64, device=tri.device)
+    if num_tri == 0:
+        return out
+    lib = N.lib()
+    ws = _scratch(lib.dr_edge_neighbours_workspace_bytes(num_tri), tri.device)
+    N.check(lib.dr_edge_neighbours(tri.data_ptr(), num_tri, out.data_ptr(), ws.data_ptr(),
+                                   ws.numel(), N.stream(tri.device)), "dr_edge_neighbours")  # fmt: skip
+    return out
+
+
+def silhouette_edges(pos3: Tensor, tri: Tensor, neighbours: Tensor) -> Tensor:
+    out = torch.empty((pos3.shape[0], tri.shape[0], 3), dtype=torch.uint8, device=pos3.device)
+    N.check(N.lib().dr_silhouette_edges(pos3.data_ptr(), pos3.shape[0], pos3.shape[1],
+                                        tri.data_ptr(), tri.shape[0], neighbours.data_ptr(),
+                                        out.data_ptr(), N.stream(pos3.device)),
+            "dr_silhouette_edges")  # fmt: skip
+    return out.bool()
+
+
+@timed("antialias_fwd")
+def antialias_fwd(color, rast, pos3, tri, neighbours) -> Tensor:
+    batch, height, width, channels = color.shape
+    out = torch.empty_like(color)
+    N.check(
+        N.lib().dr_antialias_fwd(color.data_ptr(), rast.data_ptr(), pos3.data_ptr(), pos3.shape[0],
+                                 pos3.shape[1], tri.data_ptr(), tri.shape[0],
+                                 neighbours.data_ptr(), batch, height, width, channels,
+                                 out.data_ptr(), N.stream(color.device)),
+        "dr_antialias_fwd",
+    )  # fmt: skip
+    return out
+
+
+@timed("antialias_bwd")
+def antialias_bwd(color, rast, pos3, tri, neighbours, grad_out, boost):
+    batch, height, width, channels = color.shape
+    grad_color = torch.empty_like(color)
+    grad_pos = torch.zeros_like(pos3)
+    N.check(
+        N.lib().dr_antialias_bwd(color.data_ptr(), rast.data_ptr(), pos3.data_ptr(), pos3.shape[0],
+                                 pos3.shape[1], tri.data_ptr(), tri.shape[0],
+                                 neighbours.data_ptr(), batch, height, width, channels,
+                                 grad_out.data_ptr(), float(boost), grad_color.data_ptr(),
+                                 grad_pos.data_ptr(), N.stream(color.device)),
+        "dr_antialias_bwd",
+    )  # fmt: skip
+    return grad_color, grad_pos

@@ -1,0 +1,135 @@
+"""ctypes binding of ``libdiffrast_b200.so``, the C ABI declared in ``include/diffrast_b200.h``.
+
+The library is loaded from ``diffrast_b200/_lib``; there is no fallback: if it is missing the
+first op raises ``ImportError`` with the command that builds it. Every entry point returns a status
+that :func:`check` turns into a ``RuntimeError`` naming the call.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_int64, c_size_t, c_void_p
+from pathlib import Path
+
+import torch
+
+LIBRARY = Path(__file__).resolve().parent / "_lib" / "libdiffrast_b200.so"
+
+FILTER_MODES = ("nearest", "linear", "linear-mipmap-nearest", "linear-mipmap-linear")
+BOUNDARY_MODES = ("wrap", "clamp", "zero", "cube")
+MAX_LEVELS = 32
+
+_P = c_void_p
+_SIGNATURES = {
+    "dr_version": (c_int, []),
+    "dr_status_string": (c_char_p, [c_int]),
+    "dr_raster_setup_workspace_bytes": (c_size_t, [c_int64]),
+    "dr_raster_setup": (
+        c_int,
+        [_P, _P, c_int64, c_int64, c_int64, c_int32, c_int32, _P, _P, _P, c_size_t, c_int64, _P],
+    ),
+    "dr_raster_counts": (c_int, [_P, POINTER(c_int64), POINTER(c_int64), _P]),
+    "dr_raster_bin_workspace_bytes": (c_size_t, [c_int64, c_int32, c_int32, c_int64]),
+    "dr_raster_tiles": (
+        c_int,
+        [_P, _P, c_int64, c_int64, c_int64, c_int32, c_int32, _P, _P, _P, c_int64, c_int64, _P,
+         c_size_t, _P],
+    ),
+    "dr_raster_resolve_fwd": (
+        c_int, [_P, _P, _P, c_int64, c_int64, c_int64, c_int32, c_int32, _P, _P, _P]
+    ),
+    "dr_raster_resolve_bwd": (
+        c_int, [_P, _P, _P, c_int64, c_int64, c_int64, c_int32, c_int32, _P, _P, _P, _P]
+    ),
+    "dr_interpolate_fwd": (
+        c_int,
+        [_P, c_int64, c_int64, c_int32, _P, _P, _P, c_int64, _P, c_int32, c_int64, c_int32,
+         c_int32, _P, _P, _P],
+    ),
+    "dr_interpolate_bwd": (
+        c_int,
+        [_P, c_int64, c_int64, c_int32, _P, _P, _P, c_int64, _P, c_int32, c_int64, c_int32,
+         c_int32, _P, _P, _P, _P, _P, _P],
+    ),
+    "dr_texture_fwd": (
+        c_int,
+        [_P, _P, _P, _P, c_int32, c_int32, _P, _P, _P, c_int64, c_int32, c_int32, c_int32,
+         c_int32, _P, _P],
+    ),
+    "dr_texture_bwd": (
+        c_int,
+        [_P, _P, _P, _P, _P, c_int32, c_int32, _P, _P, _P, c_int64, c_int32, c_int32, c_int32,
+         c_int32, _P, _P, _P, _P, _P],
+    ),
+    "dr_mip_downsample": (c_int, [_P, c_int64, c_int32, c_int32, c_int32, _P, _P]),
+    "dr_mip_downsample_bwd": (c_int, [_P, c_int64, c_int32, c_int32, c_int32, _P, _P]),
+    "dr_edge_neighbours_workspace_bytes": (c_size_t, [c_int64]),
+    "dr_edge_neighbours": (c_int, [_P, c_int64, _P, _P, c_size_t, _P]),
+    "dr_silhouette_edges": (c_int, [_P, c_int64, c_int64, _P, c_int64, _P, _P, _P]),
+    "dr_antialias_fwd": (
+        c_int,
+        [_P, _P, _P, c_int64, c_int64, _P, c_int64, _P, c_int64, c_int32, c_int32, c_int32, _P,
+         _P],
+    ),
+    "dr_antialias_bwd": (
+        c_int,
+        [_P, _P, _P, c_int64, c_int64, _P, c_int64, _P, c_int64, c_int32, c_int32, c_int32, _P,
+         c_float, _P, _P, _P],
+    ),
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def symbols() -> list[str]:
+    """Names of every C-ABI entry point this binding uses."""
+    return list(_SIGNATURES)
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library (loaded on first use)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIBRARY.exists():
+                raise ImportError(
+                    f"{LIBRARY} is missing; build it with `python -m diffrast_b200.build` "
+                    "(needs nvcc). diffrast_b200 has no CPU fallback."
+                )
+            handle = ctypes.CDLL(str(LIBRARY))
+            for name, (restype, argtypes) in _SIGNATURES.items():
+                fn = getattr(handle, name)
+                fn.restype = restype
+                fn.argtypes = argtypes
+            _lib = handle
+    return _lib
+
+
+def check(status: int, call: str) -> None:
+    if status != 0:
+        message = lib().dr_status_string(status).decode()
+        raise RuntimeError(f"diffrast_b200: {call} failed with status {status}: {message}")
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def int32_array(values) -> ctypes.Array:
+    return (c_int32 * len(values))(*values)
+
+
+def int64_array(values) -> ctypes.Array:
+    return (c_int64 * len(values))(*values)
+
+
+def pointer_array(values) -> ctypes.Array:
+    return (c_void_p * len(values))(*values)

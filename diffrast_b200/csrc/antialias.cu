@@ -1,0 +1,568 @@
+// Silhouette antialiasing on B200 (diffrast reference.py:202-265, :675-814).
+//
+// For every horizontally or vertically adjacent pixel pair showing different triangles, the
+// triangle seen at each pixel is followed towards the other pixel: the first of its edges crossed
+// on the way (within a rounding slack) gives the crossing t, which counts when the edge is a
+// silhouette and is handled by this axis; the nearer side wins when both find one. The pixel
+// whose half holds the crossing blends |t - 1/2| of the other's colour.
+//
+// B200 design:
+//   - Every pixel evaluates the (at most four) pairs it belongs to and writes only its own output,
+//     so the forward pass and the colour gradient need no atomics and are deterministic. The
+//     position gradient of a pair is scattered once, by its left or upper pixel.
+//   - The silhouette test runs on the fly for the one edge a pair crosses, from the edge
+//     adjacency (neighbours) and the two opposite vertices, instead of classifying every edge of
+//     every view beforehand.
+//   - Edge adjacency is built with a device hash table on 64-bit vertex-pair keys (count, first and
+//     second edge per key): no sort, deterministic, identical to the reference's result.
+// The edge tests use explicitly rounded operations in the reference's order so that the set of
+// blended edges matches it bit for bit; the side test of the silhouette classification rounds like
+// the CPU cross product of PyTorch, each component fma(a_i, b_j, -(a_j * b_i)).
+#include <cstdint>
+
+#include "common.cuh"
+#include "warp_reduce.cuh"
+
+namespace dr {
+namespace {
+
+struct AaCtx {
+  const float* color;
+  const float4* rast;
+  const float* pos;
+  const int* tri;
+  const long long* neighbours;
+  long long pos_batch, num_vert;
+  int num_tri;
+  int height, width, channels;
+};
+
+// Triangle id of a rast pixel as the reference reads it for antialiasing: round(id + 1) - 1, with
+// ids past the end of tri counted as background (-1). Values below -1 are kept distinct from -1
+// only as far as the outcome needs: they cover nothing, so all map to -2.
+__device__ __forceinline__ int aa_triangle(float id_plus_one, int num_tri) {
+  const float r = rintf(id_plus_one);
+  if (!(r >= 0.0f)) return -2;
+  if (r > static_cast<float>(num_tri)) return -1;
+  return static_cast<int>(r) - 1;
+}
+
+struct Tri2 {
+  int idx[3];
+  float x[3], y[3], w[3];
+};
+
+__device__ __forceinline__ Tri2 load_tri(const AaCtx& a, long long pb, int t) {
+  Tri2 v;
+  const long long base = pb * a.num_vert;
+  for (int k = 0; k < 3; ++k) {
+    v.idx[k] = __ldg(a.tri + 3 * static_cast<long long>(t) + k);
+    const float4 p = __ldg(reinterpret_cast<const float4*>(a.pos) + base + v.idx[k]);
+    v.x[k] = p.x;
+    v.y[k] = p.y;
+    v.w[k] = p.w;
+  }
+  return v;
+}
+
+// Edge function of edge k (from vertex k + 1 to k + 2) at (px, py), reference.py:274-278.
+__device__ __forceinline__ float edge_fn(const Tri2& v, int k, float px, float py) {
+  const int i = (k + 1) % 3, j = (k + 2) % 3;
+  const float ai = sub(v.x[i], mul(px, v.w[i])), aj = sub(v.x[j], mul(px, v.w[j]));
+  const float ci = sub(v.y[i], mul(py, v.w[i])), cj = sub(v.y[j], mul(py, v.w[j]));
+  return cross2(ai, cj, aj, ci);
+}
+
+// Rounding bound of edge_fn at (px, py), reference.py:730-746.
+__device__ __forceinline__ float edge_slack(const Tri2& v, int k, float px, float py) {
+  const int i = (k + 1) % 3, j = (k + 2) % 3;
+  const float ai = fabsf(sub(v.x[i], mul(px, v.w[i]))), aj = fabsf(sub(v.x[j], mul(px, v.w[j])));
+  const float ci = fabsf(sub(v.y[i], mul(py, v.w[i]))), cj = fabsf(sub(v.y[j], mul(py, v.w[j])));
+  const float rxi = add(fabsf(v.x[i]), fabsf(v.w[i])), rxj = add(fabsf(v.x[j]), fabsf(v.w[j]));
+  const float ryi = add(fabsf(v.y[i]), fabsf(v.w[i])), ryj = add(fabsf(v.y[j]), fabsf(v.w[j]));
+  const float terms = add(add(add(mul(add(rxi, ai), cj), mul(add(rxj, aj), ci)), mul(ryj, ai)),
+                          mul(ryi, aj));
+  return mul(terms, kEdgeTie);
+}
+
+// Sign test of the silhouette classification: sign((l . p) * p_w) with l = a x b in (x, y, w).
+__device__ __forceinline__ float side_sign(const float l[3], const float4& p) {
+  const float d = add(add(mul(l[0], p.x), mul(l[1], p.y)), mul(l[2], p.w));
+  const float s = mul(d, p.w);
+  return s > 0.0f ? 1.0f : (s < 0.0f ? -1.0f : (s == 0.0f ? 0.0f : s));
+}
+
+// Whether edge k of triangle t is a silhouette in view pb (reference.py:790-814): unshared, shared
+// by several, or shared with a triangle whose opposite vertex lies on the same side of it.
+__device__ __forceinline__ bool is_silhouette(const AaCtx& a, long long pb, int t, int k) {
+  const long long nb = __ldg(a.neighbours + 3 * static_cast<long long>(t) + k);
+  if (nb < 0) return true;
+  const long long base = pb * a.num_vert;
+  const float4* p4 = reinterpret_cast<const float4*>(a.pos);
+  const int start = __ldg(a.tri + 3 * static_cast<long long>(t) + (k + 1) % 3);
+  const int end = __ldg(a.tri + 3 * static_cast<long long>(t) + (k + 2) % 3);
+  const int opp1 = __ldg(a.tri + 3 * static_cast<long long>(t) + k);
+  const int opp2 = __ldg(a.tri + nb);  // edge nb = 3 t' + k' is opposite vertex tri[t'][k']
+  const float4 pa = __ldg(p4 + base + start), pb4 = __ldg(p4 + base + end);
+  const float A[3] = {pa.x, pa.y, pa.w}, B[3] = {pb4.x, pb4.y, pb4.w};
+  float l[3];
+  for (int c = 0; c < 3; ++c) {
+    const int i = (c + 1) % 3, j = (c + 2) % 3;
+    l[c] = __fmaf_rn(A[i], B[j], -mul(A[j], B[i]));
+  }
+  const float s1 = side_sign(l, __ldg(p4 + base + opp1));
+  const float s2 = side_sign(l, __ldg(p4 + base + opp2));
+  return mul(s1, s2) > 0.0f;
+}
+
+struct Crossing {
+  bool found;
+  float t;
+  int edge;
+};
+
+// reference.py:675-727 for one pixel pair side: triangle t seen at src, followed towards dst.
+__device__ __forceinline__ Crossing crossing(const AaCtx& a, long long pb, int t, float sx,
+                                             float sy, float dx, float dy, bool horizontal,
+                                             Tri2& v) {
+  Crossing r = {false, 0.0f, 0};
+  if (t < 0) return r;
+  v = load_tri(a, pb, t);
+  float es[3], ed[3];
+  for (int k = 0; k < 3; ++k) {
+    es[k] = edge_fn(v, k, sx, sy);
+    ed[k] = edge_fn(v, k, dx, dy);
+  }
+  const float sign = add(add(es[0], es[1]), es[2]) < 0.0f ? -1.0f : 1.0f;
+  bool any = false;
+  float best = __int_as_float(0x7f800000);
+  int edge = 0;
+  for (int k = 0; k < 3; ++k) {
+    const float span = sub(es[k], ed[k]);
+    const float slack = edge_slack(v, k, dx, dy);
+    const bool crossed = (mul(ed[k], sign) <= slack) && (mul(span, sign) > mul(2.0f, slack));
+    any |= crossed;
+    const float tk = crossed ? dvd(es[k], span) : __int_as_float(0x7f800000);
+    if (k == 0 || tk < best) {
+      best = tk;
+      edge = k;
+    }
+  }
+  if (!any) return r;
+  // Which axis handles the edge, from its two vertices alone (reference.py:749-765).
+  const int i = (edge + 1) % 3, j = (edge + 2) % 3;
+  const float steep = mul(mul(fabsf(cross2(v.w[j], v.y[i], v.w[i], v.y[j])),
+                              static_cast<float>(a.height)),
+                          kAxisTie);
+  const float flat = mul(fabsf(cross2(v.x[j], v.w[i], v.x[i], v.w[j])), static_cast<float>(a.width));
+  const bool along = horizontal ? (steep >= flat) : (flat > steep);
+  if (!along) return r;
+  if (!is_silhouette(a, pb, t, edge)) return r;
+  r.found = true;
+  r.t = best;
+  r.edge = edge;
+  return r;
+}
+
+struct Pair {
+  bool active, use_p;
+  float t, bp, bq;
+  int owner, edge;
+  float sx, sy, dx, dy;  // crossing measured from (sx, sy) towards (dx, dy)
+  Tri2 v;                // owner triangle
+};
+
+// Pair of pixel P = (row, col) and its right (horizontal) or lower neighbour Q in view b.
+__device__ __forceinline__ Pair eval_pair(const AaCtx& a, long long b, int row, int col,
+                                          bool horizontal) {
+  Pair r;
+  r.active = false;
+  r.bp = r.bq = 0.0f;
+  const long long hw = static_cast<long long>(a.height) * a.width;
+  const long long p = b * hw + static_cast<long long>(row) * a.width + col;
+  const long long q = p + (horizontal ? 1 : a.width);
+  const int row_q = horizontal ? row : row + 1, col_q = horizontal ? col + 1 : col;
+  const float4 rp = a.rast[p], rq = a.rast[q];
+  const int id_p = aa_triangle(rp.w, a.num_tri), id_q = aa_triangle(rq.w, a.num_tri);
+  if (id_p == id_q) return r;
+  const long long pb = a.pos_batch == 1 ? 0 : b;
+  const float xp = pixel_centre(col, a.width), yp = pixel_centre(row, a.height);
+  const float xq = pixel_centre(col_q, a.width), yq = pixel_centre(row_q, a.height);
+  Tri2 vp, vq;
+  const Crossing cp = crossing(a, pb, id_p, xp, yp, xq, yq, horizontal, vp);
+  const Crossing cq = crossing(a, pb, id_q, xq, yq, xp, yp, horizontal, vq);
+  r.use_p = cp.found && (!cq.found || rp.z <= rq.z);
+  const bool use_q = cq.found && !r.use_p;
+  r.active = r.use_p || use_q;
+  if (!r.active) return r;
+  r.t = r.use_p ? cp.t : sub(1.0f, cq.t);
+  if (r.t < 0.5f) r.bp = sub(0.5f, r.t); else r.bq = sub(r.t, 0.5f);
+  r.owner = r.use_p ? id_p : id_q;
+  r.edge = r.use_p ? cp.edge : cq.edge;
+  r.v = r.use_p ? vp : vq;
+  r.sx = r.use_p ? xp : xq;
+  r.sy = r.use_p ? yp : yq;
+  r.dx = r.use_p ? xq : xp;
+  r.dy = r.use_p ? yq : yp;
+  return r;
+}
+
+__global__ void __launch_bounds__(256) aa_fwd_kernel(const AaCtx a, long long total,
+                                                     float* __restrict__ out) {
+  const long long p = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (p >= total) return;
+  const long long hw = static_cast<long long>(a.height) * a.width;
+  const long long b = p / hw;
+  const int row = static_cast<int>((p - b * hw) / a.width);
+  const int col = static_cast<int>(p - b * hw - static_cast<long long>(row) * a.width);
+  // Blend coefficients and partners, in the reference's accumulation order: right pair, left
+  // pair, lower pair, upper pair.
+  float k[4] = {0.f, 0.f, 0.f, 0.f};
+  long long other[4] = {p, p, p, p};
+  if (col + 1 < a.width) {
+    const Pair r = eval_pair(a, b, row, col, true);
+    k[0] = r.bp;
+    other[0] = p + 1;
+  }
+  if (col > 0) {
+    const Pair r = eval_pair(a, b, row, col - 1, true);
+    k[1] = r.bq;
+    other[1] = p - 1;
+  }
+  if (row + 1 < a.height) {
+    const Pair r = eval_pair(a, b, row, col, false);
+    k[2] = r.bp;
+    other[2] = p + a.width;
+  }
+  if (row > 0) {
+    const Pair r = eval_pair(a, b, row - 1, col, false);
+    k[3] = r.bq;
+    other[3] = p - a.width;
+  }
+  const int C = a.channels;
+  for (int c = 0; c < C; ++c) {
+    const float self = __ldg(a.color + p * C + c);
+    float value = self;
+    for (int i = 0; i < 4; ++i) {
+      if (k[i] != 0.0f) value = add(value, mul(k[i], sub(__ldg(a.color + other[i] * C + c), self)));
+    }
+    out[p * C + c] = value;
+  }
+}
+
+// Position gradient of the crossing t of a pair, chained into the two vertices of its edge:
+// t = e_s / (e_s - e_d), e = a_i c_j - a_j c_i with a = x - px w, c = y - py w.
+__device__ __forceinline__ void add_edge_gradient(const AaCtx& a, float* grad_pos, long long pb,
+                                                  const Pair& r, float grad_t) {
+  const int i = (r.edge + 1) % 3, j = (r.edge + 2) % 3;
+  const Tri2& v = r.v;
+  const float ai_s = v.x[i] - r.sx * v.w[i], aj_s = v.x[j] - r.sx * v.w[j];
+  const float ci_s = v.y[i] - r.sy * v.w[i], cj_s = v.y[j] - r.sy * v.w[j];
+  const float ai_d = v.x[i] - r.dx * v.w[i], aj_d = v.x[j] - r.dx * v.w[j];
+  const float ci_d = v.y[i] - r.dy * v.w[i], cj_d = v.y[j] - r.dy * v.w[j];
+  const float e_s = ai_s * cj_s - aj_s * ci_s;
+  const float e_d = ai_d * cj_d - aj_d * ci_d;
+  float denom = e_s - e_d;
+  if (denom == 0.0f) denom = 1.0f;
+  const float g_s = grad_t * -e_d / (denom * denom);
+  const float g_d = grad_t * e_s / (denom * denom);
+  const float gx_i = g_s * cj_s + g_d * cj_d;
+  const float gx_j = -(g_s * ci_s + g_d * ci_d);
+  const float gy_i = -(g_s * aj_s + g_d * aj_d);
+  const float gy_j = g_s * ai_s + g_d * ai_d;
+  const float gw_i = g_s * (r.sy * aj_s - r.sx * cj_s) + g_d * (r.dy * aj_d - r.dx * cj_d);
+  const float gw_j = g_s * (r.sx * ci_s - r.sy * ai_s) + g_d * (r.dx * ci_d - r.dy * ai_d);
+  const long long base = pb * a.num_vert;
+  red_add_v4(grad_pos + (base + v.idx[i]) * 4, gx_i, gy_i, 0.0f, gw_i);
+  red_add_v4(grad_pos + (base + v.idx[j]) * 4, gx_j, gy_j, 0.0f, gw_j);
+}
+
+__global__ void __launch_bounds__(256) aa_bwd_kernel(const AaCtx a, long long total,
+                                                     const float* __restrict__ grad_out,
+                                                     float boost, float* __restrict__ grad_color,
+                                                     float* __restrict__ grad_pos) {
+  const long long p = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (p >= total) return;
+  const long long hw = static_cast<long long>(a.height) * a.width;
+  const long long b = p / hw;
+  const int row = static_cast<int>((p - b * hw) / a.width);
+  const int col = static_cast<int>(p - b * hw - static_cast<long long>(row) * a.width);
+  const long long pb = a.pos_batch == 1 ? 0 : b;
+  const int C = a.channels;
+  // As the first pixel of a pair P = p: grad_color[p] += -bp g[p] + bq g[q]; as the second pixel
+  // Q = p of a pair (P, p): grad_color[p] += bp g[P] - bq g[p].
+  float kp[4] = {0.f, 0.f, 0.f, 0.f}, kq[4] = {0.f, 0.f, 0.f, 0.f};
+  long long other[4] = {p, p, p, p};
+  Pair own[2];
+  own[0].active = own[1].active = false;
+  if (col + 1 < a.width) {
+    own[0] = eval_pair(a, b, row, col, true);
+    kp[0] = -own[0].bp;
+    kq[0] = own[0].bq;
+    other[0] = p + 1;
+  }
+  if (col > 0) {
+    const Pair r = eval_pair(a, b, row, col - 1, true);
+    kp[1] = -r.bq;
+    kq[1] = r.bp;
+    other[1] = p - 1;
+  }
+  if (row + 1 < a.height) {
+    own[1] = eval_pair(a, b, row, col, false);
+    kp[2] = -own[1].bp;
+    kq[2] = own[1].bq;
+    other[2] = p + a.width;
+  }
+  if (row > 0) {
+    const Pair r = eval_pair(a, b, row - 1, col, false);
+    kp[3] = -r.bq;
+    kq[3] = r.bp;
+    other[3] = p - a.width;
+  }
+  float grad_t[2] = {0.f, 0.f};
+  for (int c = 0; c < C; ++c) {
+    const float g_self = grad_out[p * C + c];
+    float value = g_self;
+    for (int i = 0; i < 4; ++i) {
+      if (kp[i] != 0.0f || kq[i] != 0.0f)
+        value += kp[i] * g_self + kq[i] * grad_out[other[i] * C + c];
+    }
+    grad_color[p * C + c] = value;
+    for (int d = 0; d < 2; ++d) {
+      if (!own[d].active) continue;
+      const long long q = other[d == 0 ? 0 : 2];
+      const float c_p = __ldg(a.color + p * C + c), c_q = __ldg(a.color + q * C + c);
+      // d/dt of (1/2 - t)(c_q - c_p) below the midpoint and (t - 1/2)(c_p - c_q) above it.
+      grad_t[d] += own[d].t < 0.5f ? -g_self * (c_q - c_p) : grad_out[q * C + c] * (c_p - c_q);
+    }
+  }
+  for (int d = 0; d < 2; ++d) {
+    if (!own[d].active) continue;
+    const float g = grad_t[d] * boost;
+    if (g == 0.0f) continue;
+    // When the edge belongs to Q's triangle, t = 1 - t_q.
+    add_edge_gradient(a, grad_pos, pb, own[d], own[d].use_p ? g : -g);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Edge adjacency (reference.py:768-787) with an open-addressing hash table.
+// ---------------------------------------------------------------------------------------------
+
+constexpr unsigned long long kNoKey = ~0ull;
+
+__device__ __forceinline__ unsigned long long mix64(unsigned long long x) {
+  x ^= x >> 30;
+  x *= 0xbf58476d1ce4e5b9ull;
+  x ^= x >> 27;
+  x *= 0x94d049bb133111ebull;
+  x ^= x >> 31;
+  return x;
+}
+
+__device__ __forceinline__ unsigned long long edge_key(const int* __restrict__ tri, long long e) {
+  const long long t = e / 3;
+  const int k = static_cast<int>(e - 3 * t);
+  const unsigned a = static_cast<unsigned>(__ldg(tri + 3 * t + (k + 1) % 3));
+  const unsigned b = static_cast<unsigned>(__ldg(tri + 3 * t + (k + 2) % 3));
+  const unsigned lo = min(a, b), hi = max(a, b);
+  return (static_cast<unsigned long long>(lo) << 32) | hi;
+}
+
+__global__ void __launch_bounds__(256) edge_insert_kernel(const int* __restrict__ tri,
+                                                          long long num_edges,
+                                                          unsigned long long* __restrict__ keys,
+                                                          int* __restrict__ count,
+                                                          int* __restrict__ first,
+                                                          int* __restrict__ second,
+                                                          unsigned long long mask) {
+  const long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (e >= num_edges) return;
+  const unsigned long long key = edge_key(tri, e);
+  unsigned long long h = mix64(key) & mask;
+  // The table holds at least twice as many slots as edges, so a free or matching slot is found
+  // within `mask + 1` probes.
+  for (unsigned long long probe = 0; probe <= mask; ++probe) {
+    const unsigned long long prev = atomicCAS(keys + h, kNoKey, key);
+    if (prev == kNoKey || prev == key) {
+      const int c = atomicAdd(count + h, 1);
+      if (c == 0) first[h] = static_cast<int>(e);
+      else if (c == 1) second[h] = static_cast<int>(e);
+      return;
+    }
+    h = (h + 1) & mask;
+  }
+}
+
+__global__ void __launch_bounds__(256) edge_lookup_kernel(const int* __restrict__ tri,
+                                                          long long num_edges,
+                                                          const unsigned long long* __restrict__ keys,
+                                                          const int* __restrict__ count,
+                                                          const int* __restrict__ first,
+                                                          const int* __restrict__ second,
+                                                          unsigned long long mask,
+                                                          long long* __restrict__ out) {
+  const long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (e >= num_edges) return;
+  const unsigned long long key = edge_key(tri, e);
+  unsigned long long h = mix64(key) & mask;
+  long long result = -1;
+  for (unsigned long long probe = 0; probe <= mask; ++probe) {
+    const unsigned long long k = keys[h];
+    if (k == key) {
+      if (count[h] == 2) result = first[h] == e ? second[h] : first[h];
+      break;
+    }
+    if (k == kNoKey) break;
+    h = (h + 1) & mask;
+  }
+  out[e] = result;
+}
+
+__global__ void __launch_bounds__(256) silhouette_kernel(const AaCtx a, long long total,
+                                                         uint8_t* __restrict__ out) {
+  const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (i >= total) return;
+  const long long per_view = 3LL * a.num_tri;
+  const long long pb = i / per_view;
+  const long long e = i - pb * per_view;
+  out[i] = is_silhouette(a, pb, static_cast<int>(e / 3), static_cast<int>(e % 3)) ? 1 : 0;
+}
+
+unsigned long long table_slots(int64_t num_tri) {
+  unsigned long long slots = 64;
+  while (slots < 2ull * 3ull * static_cast<unsigned long long>(num_tri)) slots <<= 1;
+  return slots;
+}
+
+bool bad_aa_args(const float* color, const float* rast, const float* pos, int64_t pos_batch,
+                 int64_t num_vert, const int32_t* tri, int64_t num_tri, const int64_t* neighbours,
+                 int64_t batch, int32_t height, int32_t width, int32_t channels) {
+  if (pos_batch < 1 || (pos_batch != 1 && pos_batch != batch)) return true;
+  if (num_vert < 0 || num_tri < 0 || num_tri >= (1LL << 29) || batch < 0 || height < 0 ||
+      width < 0 || channels < 0)
+    return true;
+  const long long total = batch * static_cast<long long>(height) * width;
+  if (total > 0 && (color == nullptr || rast == nullptr)) return true;
+  if ((reinterpret_cast<uintptr_t>(rast) & 15u) != 0 || (reinterpret_cast<uintptr_t>(pos) & 15u) != 0)
+    return true;
+  if (num_tri > 0 && (tri == nullptr || neighbours == nullptr || pos == nullptr)) return true;
+  return false;
+}
+
+AaCtx make_ctx(const float* color, const float* rast, const float* pos, int64_t pos_batch,
+               int64_t num_vert, const int32_t* tri, int64_t num_tri, const int64_t* neighbours,
+               int32_t height, int32_t width, int32_t channels) {
+  AaCtx a;
+  a.color = color;
+  a.rast = reinterpret_cast<const float4*>(rast);
+  a.pos = pos;
+  a.tri = tri;
+  a.neighbours = reinterpret_cast<const long long*>(neighbours);
+  a.pos_batch = pos_batch;
+  a.num_vert = num_vert;
+  a.num_tri = static_cast<int>(num_tri);
+  a.height = height;
+  a.width = width;
+  a.channels = channels;
+  return a;
+}
+
+}  // namespace
+}  // namespace dr
+
+using namespace dr;
+
+extern "C" size_t dr_edge_neighbours_workspace_bytes(int64_t num_tri) {
+  const unsigned long long slots = table_slots(num_tri < 0 ? 0 : num_tri);
+  return align256(8 * slots) + 3 * align256(4 * slots);
+}
+
+extern "C" int dr_edge_neighbours(const int32_t* tri, int64_t num_tri, int64_t* neighbours,
+                                  void* workspace, size_t workspace_bytes, void* stream) {
+  if (num_tri < 0 || num_tri >= (1LL << 29)) return DR_ERR_INVALID_ARGUMENT;
+  if (num_tri == 0) return DR_OK;
+  if (tri == nullptr || neighbours == nullptr || workspace == nullptr) return DR_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes < dr_edge_neighbours_workspace_bytes(num_tri)) return DR_ERR_WORKSPACE_TOO_SMALL;
+  const unsigned long long slots = table_slots(num_tri);
+  char* p = static_cast<char*>(workspace);
+  auto* keys = reinterpret_cast<unsigned long long*>(p);
+  p += align256(8 * slots);
+  int* count = reinterpret_cast<int*>(p);
+  p += align256(4 * slots);
+  int* first = reinterpret_cast<int*>(p);
+  p += align256(4 * slots);
+  int* second = reinterpret_cast<int*>(p);
+  cudaStream_t s = as_stream(stream);
+  cudaError_t err = cudaMemsetAsync(keys, 0xFF, 8 * slots, s);
+  if (err == cudaSuccess) err = cudaMemsetAsync(count, 0, 4 * slots, s);
+  if (err != cudaSuccess) return static_cast<int>(err);
+  const long long edges = 3 * num_tri;
+  edge_insert_kernel<<<blocks_for(edges, 256), 256, 0, s>>>(tri, edges, keys, count, first, second,
+                                                            slots - 1);
+  edge_lookup_kernel<<<blocks_for(edges, 256), 256, 0, s>>>(
+      tri, edges, keys, count, first, second, slots - 1, reinterpret_cast<long long*>(neighbours));
+  return launch_status();
+}
+
+extern "C" int dr_silhouette_edges(const float* pos, int64_t pos_batch, int64_t num_vert,
+                                   const int32_t* tri, int64_t num_tri, const int64_t* neighbours,
+                                   uint8_t* silhouette, void* stream) {
+  if (pos_batch < 1 || num_tri < 0 || num_tri >= (1LL << 29) || num_vert < 0)
+    return DR_ERR_INVALID_ARGUMENT;
+  const long long total = pos_batch * 3 * num_tri;
+  if (total == 0) return DR_OK;
+  if (pos == nullptr || tri == nullptr || neighbours == nullptr || silhouette == nullptr ||
+      (reinterpret_cast<uintptr_t>(pos) & 15u) != 0)
+    return DR_ERR_INVALID_ARGUMENT;
+  const AaCtx a = make_ctx(nullptr, nullptr, pos, pos_batch, num_vert, tri, num_tri, neighbours, 1, 1, 0);
+  silhouette_kernel<<<blocks_for(total, 256), 256, 0, as_stream(stream)>>>(a, total, silhouette);
+  return launch_status();
+}
+
+extern "C" int dr_antialias_fwd(const float* color, const float* rast, const float* pos,
+                                int64_t pos_batch, int64_t num_vert, const int32_t* tri,
+                                int64_t num_tri, const int64_t* neighbours, int64_t batch,
+                                int32_t height, int32_t width, int32_t channels, float* out,
+                                void* stream) {
+  if (bad_aa_args(color, rast, pos, pos_batch, num_vert, tri, num_tri, neighbours, batch, height,
+                  width, channels) ||
+      out == nullptr)
+    return DR_ERR_INVALID_ARGUMENT;
+  const long long total = batch * static_cast<long long>(height) * width;
+  if (total == 0 || channels == 0) return DR_OK;
+  if (num_tri == 0) {
+    cudaError_t err = cudaMemcpyAsync(out, color, sizeof(float) * total * channels,
+                                      cudaMemcpyDeviceToDevice, as_stream(stream));
+    return static_cast<int>(err);
+  }
+  const AaCtx a = make_ctx(color, rast, pos, pos_batch, num_vert, tri, num_tri, neighbours, height,
+                           width, channels);
+  aa_fwd_kernel<<<blocks_for(total, 256), 256, 0, as_stream(stream)>>>(a, total, out);
+  return launch_status();
+}
+
+extern "C" int dr_antialias_bwd(const float* color, const float* rast, const float* pos,
+                                int64_t pos_batch, int64_t num_vert, const int32_t* tri,
+                                int64_t num_tri, const int64_t* neighbours, int64_t batch,
+                                int32_t height, int32_t width, int32_t channels,
+                                const float* grad_out, float pos_gradient_boost,
+                                float* grad_color, float* grad_pos, void* stream) {
+  if (bad_aa_args(color, rast, pos, pos_batch, num_vert, tri, num_tri, neighbours, batch, height,
+                  width, channels) ||
+      grad_out == nullptr || grad_color == nullptr || (num_tri > 0 && grad_pos == nullptr))
+    return DR_ERR_INVALID_ARGUMENT;
+  const long long total = batch * static_cast<long long>(height) * width;
+  if (total == 0 || channels == 0) return DR_OK;
+  if (num_tri == 0) {
+    cudaError_t err = cudaMemcpyAsync(grad_color, grad_out, sizeof(float) * total * channels,
+                                      cudaMemcpyDeviceToDevice, as_stream(stream));
+    return static_cast<int>(err);
+  }
+  const AaCtx a = make_ctx(color, rast, pos, pos_batch, num_vert, tri, num_tri, neighbours, height,
+                           width, channels);
+  aa_bwd_kernel<<<blocks_for(total, 256), 256, 0, as_stream(stream)>>>(a, total, grad_out,
+                                                                        pos_gradient_boost,
+                                                                        grad_color, grad_pos);
+  return launch_status();
+}

@@ -1,0 +1,140 @@
+// Shared device helpers of the diffrast_b200 CUDA library (sm_100a).
+//
+// Visibility decisions (coverage, tie rules, area tolerance, antialias edge tests) are made with
+// explicitly rounded float32 operations (__fmul_rn / __fadd_rn / __fsub_rn / __fdiv_rn), which the
+// compiler never contracts into fused multiply-adds. They reproduce, operation for operation, the
+// float32 arithmetic of diffrast's reference backend (src/diffrast/backends/reference.py:293-365,
+// :675-765), so triangle ids and the antialias edge set agree bit for bit. Everything else (the
+// barycentric resolve, interpolation, texturing, gradients) uses ordinary float arithmetic.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "../../include/diffrast_b200.h"
+
+namespace dr {
+
+// Empty visibility key: no triangle covers the pixel (INT64_MAX, as a signed 64-bit key).
+constexpr long long kEmptyKey = 0x7FFFFFFFFFFFFFFFLL;
+// Two float32 epsilons: the area tolerance of the reference (reference.py:27).
+constexpr float kAreaTolerance = 2.0f * 1.1920928955078125e-07f;
+// Four float32 epsilons: the edge-tie slack of antialiasing (reference.py:35, :746).
+constexpr float kEdgeTie = 4.0f * 1.1920928955078125e-07f;
+// Slope margin deciding which axis handles a 45 degree edge (reference.py:32).
+constexpr float kAxisTie = 1.0001f;
+// Footprint and direction-derivative saturation (reference.py:402, _cube.py:36).
+constexpr float kLimit = 1e18f;
+// Screen tiles of the binned visibility pass.
+constexpr int kTile = 16;
+// Triangles per tile work item (one per thread of a 16x16 tile block).
+constexpr int kChunk = 256;
+// Triangles whose pixel box fits in kSmall x kSmall are rasterized directly by the setup pass.
+constexpr int kSmall = 4;
+
+__device__ __forceinline__ float mul(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float add(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ float sub(float a, float b) { return __fsub_rn(a, b); }
+__device__ __forceinline__ float dvd(float a, float b) { return __fdiv_rn(a, b); }
+// a * b - c * d with every product and difference rounded separately.
+__device__ __forceinline__ float cross2(float a, float b, float c, float d) {
+  return sub(mul(a, b), mul(c, d));
+}
+// torch.maximum semantics: NaN propagates.
+__device__ __forceinline__ float nanmax(float a, float b) {
+  return (a != a || b != b) ? __int_as_float(0x7fc00000) : fmaxf(a, b);
+}
+
+// NDC centre of pixel i of a row or column of n pixels: (2 i + 1) / n - 1, as in
+// reference.py:268-271 (float32 arange * 2 + 1, IEEE division, then minus one).
+__device__ __forceinline__ float pixel_centre(int i, int n) {
+  float v = add(mul(static_cast<float>(i), 2.0f), 1.0f);
+  return sub(dvd(v, static_cast<float>(n)), 1.0f);
+}
+
+struct Vert {
+  float x, y, z, w;
+};
+
+__device__ __forceinline__ Vert load_vert(const float* __restrict__ pos, long long index) {
+  float4 v = __ldg(reinterpret_cast<const float4*>(pos) + index);
+  return {v.x, v.y, v.z, v.w};
+}
+
+__device__ __forceinline__ bool finite4(const Vert& v) {
+  return isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w);
+}
+
+// Packed key of a covered pixel: order-preserving integer of the float32 depth in the high word
+// (negative floats have their magnitude bits flipped, -0 maps to 0) and the triangle index in
+// the low word. A signed 64-bit minimum then keeps the nearest triangle and, at equal depth,
+// the lowest index, which is the reference's rule (reference.py:368-397).
+__device__ __forceinline__ long long pack_key(float depth, int tri) {
+  int bits = __float_as_int(depth);
+  int ordered = bits >= 0 ? bits : (bits ^ 0x7FFFFFFF);
+  if (depth == 0.0f) ordered = 0;
+  return (static_cast<long long>(ordered) << 32) | static_cast<unsigned int>(tri);
+}
+
+// Coverage and depth of one triangle at one pixel centre, returning the packed key or the empty
+// key. The float32 operations and their order are those of the reference's coverage test
+// (reference.py:293-365): edge functions e = a x c with a = x - px w and c = y - py w, the
+// top-left rule for exact zeros from the sign of the edge's screen gradient, the area tolerance
+// against the magnitude of the terms, the sign of the interpolated w and -1 <= z/w <= 1.
+// Non-finite vertices are rejected by the caller.
+__device__ __forceinline__ long long coverage_key(const Vert& v0, const Vert& v1, const Vert& v2,
+                                                  float px, float py, int tri) {
+  const float a0 = sub(v0.x, mul(px, v0.w)), a1 = sub(v1.x, mul(px, v1.w)),
+              a2 = sub(v2.x, mul(px, v2.w));
+  const float c0 = sub(v0.y, mul(py, v0.w)), c1 = sub(v1.y, mul(py, v1.w)),
+              c2 = sub(v2.y, mul(py, v2.w));
+  const float e0 = cross2(a1, c2, a2, c1);
+  const float e1 = cross2(a2, c0, a0, c2);
+  const float e2 = cross2(a0, c1, a1, c0);
+  const float s = add(add(e0, e1), e2);
+  const float ew = add(add(mul(e0, v0.w), mul(e1, v1.w)), mul(e2, v2.w));
+  const float ez = add(add(mul(e0, v0.z), mul(e1, v1.z)), mul(e2, v2.z));
+  const float depth = dvd(ez, ew);
+  const bool positive = s > 0.0f;
+
+  // Edge k runs from vertex i = k + 1 to j = k + 2.
+  auto side = [&](float e, float ai, float ci, float wi, float aj, float cj, float wj) {
+    const float gx = cross2(ci, wj, cj, wi);
+    const float gy = cross2(aj, wi, ai, wj);
+    const float q = (e == 0.0f) ? ((gx == 0.0f) ? gy : gx) : e;
+    return positive ? (q > 0.0f) : (q < 0.0f);
+  };
+  bool inside = side(e0, a1, c1, v1.w, a2, c2, v2.w);
+  inside = inside & side(e1, a2, c2, v2.w, a0, c0, v0.w);
+  inside = inside & side(e2, a0, c0, v0.w, a1, c1, v1.w);
+
+  const float reach_x = nanmax(nanmax(add(fabsf(v0.x), fabsf(v0.w)), add(fabsf(v1.x), fabsf(v1.w))),
+                               add(fabsf(v2.x), fabsf(v2.w)));
+  const float reach_y = nanmax(nanmax(add(fabsf(v0.y), fabsf(v0.w)), add(fabsf(v1.y), fabsf(v1.w))),
+                               add(fabsf(v2.y), fabsf(v2.w)));
+  const float span_x = add(add(fabsf(a0), fabsf(a1)), fabsf(a2));
+  const float span_y = add(add(fabsf(c0), fabsf(c1)), fabsf(c2));
+  const float bound = mul(add(mul(reach_x, span_y), mul(span_x, add(reach_y, span_y))), kAreaTolerance);
+  inside = inside & (fabsf(s) > bound);
+  inside = inside & (positive ? (ew > 0.0f) : (ew < 0.0f));
+  inside = inside & (depth >= -1.0f) & (depth <= 1.0f);
+  return inside ? pack_key(depth, tri) : kEmptyKey;
+}
+
+// Status of the launches just made on this thread.
+inline int launch_status() {
+  cudaError_t err = cudaGetLastError();
+  return err == cudaSuccess ? DR_OK : static_cast<int>(err);
+}
+
+inline cudaStream_t as_stream(void* stream) { return reinterpret_cast<cudaStream_t>(stream); }
+
+inline unsigned int blocks_for(long long n, int threads) {
+  long long b = (n + threads - 1) / threads;
+  return static_cast<unsigned int>(b < 1 ? 1 : b);
+}
+
+// Bytes rounded up to the 256-byte alignment of every workspace sub-buffer.
+inline size_t align256(size_t bytes) { return (bytes + 255) & ~static_cast<size_t>(255); }
+
+}  // namespace dr

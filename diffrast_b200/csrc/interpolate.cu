@@ -1,0 +1,240 @@
+// Attribute interpolation on B200 (diffrast reference.py:117-146).
+//
+// One thread per pixel: the triangle id from rast selects three attribute rows, which are blended
+// with the barycentrics; the selected channels also get their screen-space derivatives from
+// rast_db. The forward weighted sums use explicitly rounded operations in the reference's order,
+// (u a0 + v a1) + ((1 - u) - v) a2, so they round as the reference does for the same rast.
+// The backward pass writes the gradients of rast and rast_db per pixel and, when attr needs them,
+// scatters attribute gradients with warp-aggregated atomics (lanes showing the same vertex sum
+// their contributions first).
+#include <cstdint>
+
+#include "common.cuh"
+#include "warp_reduce.cuh"
+
+namespace dr {
+namespace {
+
+// Triangle index of a rast pixel: round(id + 1) - 1 (round half to even, like torch.round), or
+// -1 for background, negative values and ids past the end of tri (reference.py:127-129).
+__device__ __forceinline__ int rast_triangle(float id_plus_one, int num_tri) {
+  const float r = rintf(id_plus_one);
+  if (!(r >= 1.0f) || r > static_cast<float>(num_tri)) return -1;
+  return static_cast<int>(r) - 1;
+}
+
+struct Corners {
+  bool covered;
+  long long row0, row1, row2;  // attribute rows (view * num_vert + vertex)
+};
+
+__device__ __forceinline__ Corners corners(const int* __restrict__ tri, int t, long long pixel,
+                                           long long pixels_per_image, long long attr_batch,
+                                           long long num_vert) {
+  Corners k;
+  k.covered = t >= 0;
+  k.row0 = k.row1 = k.row2 = 0;
+  if (k.covered) {
+    const long long view = attr_batch == 1 ? 0 : pixel / pixels_per_image;
+    const long long base = view * num_vert;
+    k.row0 = base + __ldg(tri + 3 * static_cast<long long>(t));
+    k.row1 = base + __ldg(tri + 3 * static_cast<long long>(t) + 1);
+    k.row2 = base + __ldg(tri + 3 * static_cast<long long>(t) + 2);
+  }
+  return k;
+}
+
+__global__ void __launch_bounds__(256) interp_fwd_kernel(
+    const float* __restrict__ attr, long long attr_batch, long long num_vert, int channels,
+    const float4* __restrict__ rast, const float4* __restrict__ rast_db, const int* __restrict__ tri,
+    int num_tri, const int* __restrict__ diff, int num_diff, long long total,
+    long long pixels_per_image, float* __restrict__ out, float* __restrict__ out_da) {
+  const long long p = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (p >= total) return;
+  const float4 r = rast[p];
+  const int t = rast_triangle(r.w, num_tri);
+  const Corners k = corners(tri, t, p, pixels_per_image, attr_batch, num_vert);
+  float* o = out + p * channels;
+  if (!k.covered) {
+    for (int c = 0; c < channels; ++c) o[c] = 0.0f;
+    if (num_diff > 0) {
+      float* od = out_da + p * 2 * num_diff;
+      for (int c = 0; c < 2 * num_diff; ++c) od[c] = 0.0f;
+    }
+    return;
+  }
+  const float u = r.x, v = r.y;
+  const float w2 = sub(sub(1.0f, u), v);
+  const float* a0 = attr + k.row0 * channels;
+  const float* a1 = attr + k.row1 * channels;
+  const float* a2 = attr + k.row2 * channels;
+  for (int c = 0; c < channels; ++c) {
+    o[c] = add(add(mul(u, __ldg(a0 + c)), mul(v, __ldg(a1 + c))), mul(w2, __ldg(a2 + c)));
+  }
+  if (num_diff > 0) {
+    const float4 d = rast_db[p];
+    float* od = out_da + p * 2 * num_diff;
+    for (int j = 0; j < num_diff; ++j) {
+      const int c = __ldg(diff + j);
+      const float x2 = __ldg(a2 + c);
+      const float du = sub(__ldg(a0 + c), x2), dv = sub(__ldg(a1 + c), x2);
+      od[2 * j] = add(mul(d.x, du), mul(d.z, dv));
+      od[2 * j + 1] = add(mul(d.y, du), mul(d.w, dv));
+    }
+  }
+}
+
+// Adds value to grad_attr[row * channels + c] with the lanes of the warp that share `row` summed
+// first. All lanes must call it together with the same c.
+__device__ __forceinline__ void scatter_attr(float* __restrict__ grad_attr, long long row,
+                                             unsigned peers, bool active, int channels, int c,
+                                             float value) {
+  float v[1] = {value};
+  segmented_sum<1>(peers, v);
+  const unsigned lane = threadIdx.x & 31u;
+  if (active && (peers & ((1u << lane) - 1u)) == 0u) red_add(grad_attr + row * channels + c, v[0]);
+}
+
+__global__ void __launch_bounds__(256) interp_bwd_kernel(
+    const float* __restrict__ attr, long long attr_batch, long long num_vert, int channels,
+    const float4* __restrict__ rast, const float4* __restrict__ rast_db, const int* __restrict__ tri,
+    int num_tri, const int* __restrict__ diff, int num_diff, long long total,
+    long long pixels_per_image, const float* __restrict__ grad_out,
+    const float* __restrict__ grad_out_da, float* __restrict__ grad_attr,
+    float4* __restrict__ grad_rast, float4* __restrict__ grad_db) {
+  const long long p = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  const bool in_range = p < total;
+  const float4 r = in_range ? rast[p] : make_float4(0.f, 0.f, 0.f, 0.f);
+  const int t = in_range ? rast_triangle(r.w, num_tri) : -1;
+  const Corners k = corners(tri, t, p, pixels_per_image, attr_batch, num_vert);
+  const float u = r.x, v = r.y, w2 = 1.0f - u - v;
+  const float* a0 = attr + k.row0 * channels;
+  const float* a1 = attr + k.row1 * channels;
+  const float* a2 = attr + k.row2 * channels;
+
+  // Lanes that share a vertex row; computed once, reused for every channel.
+  const unsigned lane = threadIdx.x & 31u;
+  unsigned peers[3] = {1u << lane, 1u << lane, 1u << lane};
+  if (grad_attr != nullptr) {
+    const unsigned act = __ballot_sync(0xffffffffu, k.covered);
+    if (k.covered) {
+      peers[0] = __match_any_sync(act, static_cast<unsigned long long>(k.row0));
+      peers[1] = __match_any_sync(act, static_cast<unsigned long long>(k.row1));
+      peers[2] = __match_any_sync(act, static_cast<unsigned long long>(k.row2));
+    }
+  }
+
+  float gu = 0.0f, gv = 0.0f;
+  for (int c = 0; c < channels; ++c) {
+    float g = 0.0f, x0 = 0.0f, x1 = 0.0f, x2 = 0.0f;
+    if (k.covered) {
+      g = grad_out[p * channels + c];
+      x0 = __ldg(a0 + c);
+      x1 = __ldg(a1 + c);
+      x2 = __ldg(a2 + c);
+      gu += g * (x0 - x2);
+      gv += g * (x1 - x2);
+    }
+    if (grad_attr != nullptr) {
+      scatter_attr(grad_attr, k.row0, peers[0], k.covered, channels, c, g * u);
+      scatter_attr(grad_attr, k.row1, peers[1], k.covered, channels, c, g * v);
+      scatter_attr(grad_attr, k.row2, peers[2], k.covered, channels, c, g * w2);
+    }
+  }
+  if (in_range) grad_rast[p] = make_float4(gu, gv, 0.0f, 0.0f);
+
+  if (grad_out_da == nullptr) return;
+  const float4 d = k.covered ? rast_db[p] : make_float4(0.f, 0.f, 0.f, 0.f);
+  float g_dudx = 0.0f, g_dudy = 0.0f, g_dvdx = 0.0f, g_dvdy = 0.0f;
+  for (int j = 0; j < num_diff; ++j) {
+    float gx = 0.0f, gy = 0.0f, du = 0.0f, dv = 0.0f;
+    int c = 0;
+    if (k.covered) {
+      c = __ldg(diff + j);
+      gx = grad_out_da[(p * num_diff + j) * 2];
+      gy = grad_out_da[(p * num_diff + j) * 2 + 1];
+      const float x2 = __ldg(a2 + c);
+      du = __ldg(a0 + c) - x2;
+      dv = __ldg(a1 + c) - x2;
+      g_dudx += gx * du;
+      g_dudy += gy * du;
+      g_dvdx += gx * dv;
+      g_dvdy += gy * dv;
+    }
+    if (grad_attr != nullptr) {
+      // All lanes agree on j; c differs only between covered and uncovered lanes, and an
+      // uncovered lane adds nothing, so a shared c per group holds.
+      const float g0 = gx * d.x + gy * d.y;
+      const float g1 = gx * d.z + gy * d.w;
+      scatter_attr(grad_attr, k.row0, peers[0], k.covered, channels, c, g0);
+      scatter_attr(grad_attr, k.row1, peers[1], k.covered, channels, c, g1);
+      scatter_attr(grad_attr, k.row2, peers[2], k.covered, channels, c, -(g0 + g1));
+    }
+  }
+  if (in_range) grad_db[p] = make_float4(g_dudx, g_dudy, g_dvdx, g_dvdy);
+}
+
+bool bad_interp_args(const float* attr, int64_t attr_batch, int64_t num_vert, int32_t channels,
+                     const float* rast, const float* rast_db, const int32_t* tri, int64_t num_tri,
+                     const int32_t* diff, int32_t num_diff, int64_t batch, int32_t height,
+                     int32_t width) {
+  if (attr_batch < 1 || num_vert < 0 || channels < 0 || num_tri < 0 || num_diff < 0 || batch < 0 ||
+      height < 0 || width < 0)
+    return true;
+  if (attr_batch != 1 && attr_batch != batch) return true;
+  if (num_tri >= (1LL << 31)) return true;
+  const long long total = batch * static_cast<long long>(height) * width;
+  if (total > 0 && (rast == nullptr || (reinterpret_cast<uintptr_t>(rast) & 15u) != 0)) return true;
+  if (num_diff > 0 && (diff == nullptr || rast_db == nullptr ||
+                       (reinterpret_cast<uintptr_t>(rast_db) & 15u) != 0))
+    return true;
+  if (num_tri > 0 && tri == nullptr) return true;
+  if (channels > 0 && num_vert > 0 && attr == nullptr) return true;
+  return false;
+}
+
+}  // namespace
+}  // namespace dr
+
+using namespace dr;
+
+extern "C" int dr_interpolate_fwd(const float* attr, int64_t attr_batch, int64_t num_vert,
+                                  int32_t channels, const float* rast, const float* rast_db,
+                                  const int32_t* tri, int64_t num_tri, const int32_t* diff,
+                                  int32_t num_diff, int64_t batch, int32_t height, int32_t width,
+                                  float* out, float* out_da, void* stream) {
+  if (bad_interp_args(attr, attr_batch, num_vert, channels, rast, rast_db, tri, num_tri, diff,
+                      num_diff, batch, height, width) ||
+      out == nullptr || (num_diff > 0 && out_da == nullptr))
+    return DR_ERR_INVALID_ARGUMENT;
+  const long long total = batch * static_cast<long long>(height) * width;
+  if (total == 0) return DR_OK;
+  interp_fwd_kernel<<<blocks_for(total, 256), 256, 0, as_stream(stream)>>>(
+      attr, attr_batch, num_vert, channels, reinterpret_cast<const float4*>(rast),
+      reinterpret_cast<const float4*>(rast_db), tri, static_cast<int>(num_tri), diff, num_diff,
+      total, static_cast<long long>(height) * width, out, out_da);
+  return launch_status();
+}
+
+extern "C" int dr_interpolate_bwd(const float* attr, int64_t attr_batch, int64_t num_vert,
+                                  int32_t channels, const float* rast, const float* rast_db,
+                                  const int32_t* tri, int64_t num_tri, const int32_t* diff,
+                                  int32_t num_diff, int64_t batch, int32_t height, int32_t width,
+                                  const float* grad_out, const float* grad_out_da,
+                                  float* grad_attr, float* grad_rast, float* grad_db,
+                                  void* stream) {
+  if (bad_interp_args(attr, attr_batch, num_vert, channels, rast, rast_db, tri, num_tri, diff,
+                      grad_out_da != nullptr ? num_diff : 0, batch, height, width) ||
+      grad_out == nullptr || grad_rast == nullptr ||
+      (grad_out_da != nullptr && (grad_db == nullptr || num_diff == 0)))
+    return DR_ERR_INVALID_ARGUMENT;
+  const long long total = batch * static_cast<long long>(height) * width;
+  if (total == 0) return DR_OK;
+  interp_bwd_kernel<<<blocks_for(total, 256), 256, 0, as_stream(stream)>>>(
+      attr, attr_batch, num_vert, channels, reinterpret_cast<const float4*>(rast),
+      reinterpret_cast<const float4*>(rast_db), tri, static_cast<int>(num_tri), diff,
+      grad_out_da != nullptr ? num_diff : 0, total, static_cast<long long>(height) * width,
+      grad_out, grad_out_da, grad_attr, reinterpret_cast<float4*>(grad_rast),
+      reinterpret_cast<float4*>(grad_db));
+  return launch_status();
+}

@@ -1,0 +1,667 @@
+// Rasterization on B200: visibility as packed 64-bit depth|triangle keys, then resolve.
+//
+// Visibility (result identical to diffrast's reference, backends/reference.py:368-397):
+//   1. setup_kernel, one thread per (view, triangle): culls, bounds the triangle in pixels, and
+//      rasterizes it directly when its box fits in kSmall x kSmall pixels (most triangles of dense
+//      meshes), merging keys with 64-bit atomicMin. Other triangles are appended (warp-aggregated)
+//      to a list with their 16x16-tile box.
+//   2. Device-side binning without host round trips beyond one counter read: per-tile counts,
+//      one exclusive scan (pair offsets and 256-triangle work items), and a scatter into per-tile
+//      triangle lists.
+//   3. tile_kernel, persistent (a few blocks per SM pull work items from an atomic counter): a
+//      16x16 block stages up to 256 triangles of its tile in shared memory (12 floats each), every
+//      thread keeps the minimum key of its pixel in a register and merges it with one atomicMin.
+// Resolve: one thread per pixel turns the key into rast = (u, v, z/w, id + 1) and rast_db; the
+// backward pass chains the gradients of rast and rast_db into the three vertices and scatters
+// them with warp-aggregated float4 reductions.
+#include <cstdint>
+
+#include "common.cuh"
+#include "warp_reduce.cuh"
+
+namespace dr {
+namespace {
+
+// One triangle that needs tile binning: flat view * num_tri + triangle, and its tile box packed as
+// (tx0 | tx1 << 16, ty0 | ty1 << 16). The record layout does not depend on the list capacity.
+struct Binned {
+  int g;
+  unsigned bx, by;
+};
+
+struct SetupLayout {
+  unsigned long long* counters;  // [0] binned triangles, [1] (triangle, tile) pairs
+  Binned* binned;
+};
+
+SetupLayout setup_layout(const void* ws) {
+  char* p = static_cast<char*>(const_cast<void*>(ws));
+  SetupLayout l;
+  l.counters = reinterpret_cast<unsigned long long*>(p);
+  l.binned = reinterpret_cast<Binned*>(p + 256);
+  return l;
+}
+
+size_t setup_bytes(int64_t capacity) {
+  return 256 + align256(sizeof(Binned) * static_cast<size_t>(capacity));
+}
+
+struct BinLayout {
+  unsigned* tile_count;   // [tiles]
+  unsigned* tile_cursor;  // [tiles]
+  unsigned* tile_offset;  // [tiles + 1]
+  unsigned* item_offset;  // [tiles + 1]
+  unsigned* work;         // [1]
+  int* pairs;             // [num_pairs]
+};
+
+BinLayout bin_layout(void* ws, int64_t tiles, int64_t num_pairs) {
+  char* p = static_cast<char*>(ws);
+  BinLayout l;
+  const size_t t = align256(sizeof(unsigned) * static_cast<size_t>(tiles + 1));
+  l.tile_count = reinterpret_cast<unsigned*>(p);
+  p += t;
+  l.tile_cursor = reinterpret_cast<unsigned*>(p);
+  p += t;
+  l.tile_offset = reinterpret_cast<unsigned*>(p);
+  p += t;
+  l.item_offset = reinterpret_cast<unsigned*>(p);
+  p += t;
+  l.work = reinterpret_cast<unsigned*>(p);
+  p += 256;
+  l.pairs = reinterpret_cast<int*>(p);
+  (void)num_pairs;
+  return l;
+}
+
+size_t bin_bytes(int64_t tiles, int64_t num_pairs) {
+  return 4 * align256(sizeof(unsigned) * static_cast<size_t>(tiles + 1)) + 256 +
+         align256(sizeof(int) * static_cast<size_t>(num_pairs));
+}
+
+__global__ void fill_keys_kernel(long long* __restrict__ keys, long long n) {
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n; i += stride)
+    keys[i] = kEmptyKey;
+}
+
+// Pixel centres within [lo, hi] (NDC) as an inclusive index range. The margin keeps centres on
+// the boundary despite the rounding of x / w, which grows with the image size; extra pixels are
+// tested exactly. Same margin as the reference's Triton setup (_triton_rasterize.py:113-123).
+__device__ __forceinline__ void pixel_range(float lo, float hi, int size, int& first, int& last) {
+  const float s = static_cast<float>(size);
+  const float margin = 1e-3f + s * 1e-6f;
+  float f = ceilf(((lo + 1.0f) * s - 1.0f) * 0.5f - margin);
+  float l = floorf(((hi + 1.0f) * s - 1.0f) * 0.5f + margin);
+  f = fminf(fmaxf(f, 0.0f), s);
+  l = fminf(fmaxf(l, -1.0f), s - 1.0f);
+  first = static_cast<int>(f);
+  last = static_cast<int>(l);
+}
+
+__global__ void __launch_bounds__(256) setup_kernel(
+    const float* __restrict__ pos, const int* __restrict__ tri, int num_vert, int num_tri,
+    long long total, int height, int width, const long long* __restrict__ prev,
+    long long* __restrict__ keys, unsigned long long* __restrict__ counters,
+    Binned* __restrict__ binned, long long capacity) {
+  const long long g = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  bool large = false;
+  unsigned pairs = 0;
+  uint2 tile_box = make_uint2(0, 0);
+  if (g < total) {
+    const int b = static_cast<int>(g / num_tri);
+    const int t = static_cast<int>(g - static_cast<long long>(b) * num_tri);
+    const int i0 = __ldg(tri + 3 * static_cast<long long>(t));
+    const int i1 = __ldg(tri + 3 * static_cast<long long>(t) + 1);
+    const int i2 = __ldg(tri + 3 * static_cast<long long>(t) + 2);
+    const long long base = static_cast<long long>(b) * num_vert;
+    const Vert v0 = load_vert(pos, base + i0), v1 = load_vert(pos, base + i1),
+               v2 = load_vert(pos, base + i2);
+    // A triangle is invisible when all vertices are behind the camera or outside the same side
+    // plane; every covered point is a non-negative combination of the vertices. Non-finite
+    // vertices are never drawn (reference.py:334).
+    bool culled = !(finite4(v0) && finite4(v1) && finite4(v2));
+    culled |= (v0.w <= 0.0f) && (v1.w <= 0.0f) && (v2.w <= 0.0f);
+    culled |= (v0.x > v0.w) && (v1.x > v1.w) && (v2.x > v2.w);
+    culled |= (v0.x < -v0.w) && (v1.x < -v1.w) && (v2.x < -v2.w);
+    culled |= (v0.y > v0.w) && (v1.y > v1.w) && (v2.y > v2.w);
+    culled |= (v0.y < -v0.w) && (v1.y < -v1.w) && (v2.y < -v2.w);
+    if (!culled) {
+      const bool in_front = (v0.w > 0.0f) && (v1.w > 0.0f) && (v2.w > 0.0f);
+      int c0 = 0, c1 = width - 1, r0 = 0, r1 = height - 1;
+      if (in_front) {
+        const float nx0 = v0.x / v0.w, nx1 = v1.x / v1.w, nx2 = v2.x / v2.w;
+        const float ny0 = v0.y / v0.w, ny1 = v1.y / v1.w, ny2 = v2.y / v2.w;
+        pixel_range(fminf(fminf(nx0, nx1), nx2), fmaxf(fmaxf(nx0, nx1), nx2), width, c0, c1);
+        pixel_range(fminf(fminf(ny0, ny1), ny2), fmaxf(fmaxf(ny0, ny1), ny2), height, r0, r1);
+      }
+      if (c0 <= c1 && r0 <= r1) {
+        if (in_front && c1 - c0 < kSmall && r1 - r0 < kSmall) {
+          for (int r = r0; r <= r1; ++r) {
+            const float py = pixel_centre(r, height);
+            for (int c = c0; c <= c1; ++c) {
+              const float px = pixel_centre(c, width);
+              const long long key = coverage_key(v0, v1, v2, px, py, t);
+              if (key == kEmptyKey) continue;
+              const long long off = (static_cast<long long>(b) * height + r) * width + c;
+              if (prev != nullptr && !(key > __ldg(prev + off))) continue;
+              atomicMin(keys + off, key);
+            }
+          }
+        } else {
+          large = true;
+          const unsigned tx0 = c0 / kTile, tx1 = c1 / kTile, ty0 = r0 / kTile, ty1 = r1 / kTile;
+          pairs = (tx1 - tx0 + 1) * (ty1 - ty0 + 1);
+          tile_box = make_uint2(tx0 | (tx1 << 16), ty0 | (ty1 << 16));
+        }
+      }
+    }
+  }
+  // Warp-aggregated append of the large triangles and of their pair counts.
+  const unsigned lane = threadIdx.x & 31u;
+  const unsigned mask = __ballot_sync(0xffffffffu, large);
+  unsigned long long warp_pairs = pairs;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) warp_pairs += __shfl_xor_sync(0xffffffffu, warp_pairs, o);
+  if (mask == 0u) return;
+  unsigned long long slot0 = 0;
+  if (lane == 0) {
+    slot0 = atomicAdd(counters, static_cast<unsigned long long>(__popc(mask)));
+    atomicAdd(counters + 1, warp_pairs);
+  }
+  slot0 = __shfl_sync(0xffffffffu, slot0, 0);
+  if (large) {
+    const unsigned long long slot = slot0 + __popc(mask & ((1u << lane) - 1u));
+    if (slot < static_cast<unsigned long long>(capacity)) {
+      binned[slot] = {static_cast<int>(g), tile_box.x, tile_box.y};
+    }
+  }
+}
+
+// One warp per binned triangle; its lanes walk the triangle's tiles.
+template <bool kScatter>
+__global__ void __launch_bounds__(256) bin_kernel(const Binned* __restrict__ binned,
+                                                  long long count,
+                                                  int num_tri, int tiles_x, int tiles_per_image,
+                                                  unsigned* __restrict__ tile_count,
+                                                  const unsigned* __restrict__ tile_offset,
+                                                  int* __restrict__ pairs) {
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x / 32);
+  const unsigned lane = threadIdx.x & 31u;
+  for (long long i = (blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x) / 32; i < count;
+       i += warps) {
+    const Binned rec = binned[i];
+    const int g = rec.g;
+    const int b = g / num_tri;
+    const int tx0 = rec.bx & 0xFFFF, tx1 = rec.bx >> 16, ty0 = rec.by & 0xFFFF, ty1 = rec.by >> 16;
+    const int nx = tx1 - tx0 + 1;
+    const int n = nx * (ty1 - ty0 + 1);
+    for (int k = lane; k < n; k += 32) {
+      const int tile = b * tiles_per_image + (ty0 + k / nx) * tiles_x + tx0 + k % nx;
+      if (kScatter) {
+        const unsigned slot = atomicAdd(tile_count + tile, 1u);
+        pairs[tile_offset[tile] + slot] = g;
+      } else {
+        atomicAdd(tile_count + tile, 1u);
+      }
+    }
+  }
+}
+
+// Exclusive scans of the per-tile pair counts and of their 256-triangle work items, in one block.
+__global__ void __launch_bounds__(1024) scan_kernel(const unsigned* __restrict__ count, int n,
+                                                    unsigned* __restrict__ offset,
+                                                    unsigned* __restrict__ item_offset) {
+  __shared__ unsigned warp_a[32], warp_b[32];
+  __shared__ unsigned carry_a, carry_b;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) carry_a = carry_b = 0;
+  __syncthreads();
+  constexpr int kPer = 4;
+  for (int base = 0; base < n; base += 1024 * kPer) {
+    unsigned a[kPer], b[kPer], sa = 0, sb = 0;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int i = base + tid * kPer + j;
+      const unsigned c = i < n ? count[i] : 0u;
+      a[j] = sa;
+      b[j] = sb;
+      sa += c;
+      sb += (c + kChunk - 1) / kChunk;
+    }
+    unsigned xa = sa, xb = sb;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned ya = __shfl_up_sync(0xffffffffu, xa, o);
+      const unsigned yb = __shfl_up_sync(0xffffffffu, xb, o);
+      if (lane >= o) {
+        xa += ya;
+        xb += yb;
+      }
+    }
+    if (lane == 31) {
+      warp_a[warp] = xa;
+      warp_b[warp] = xb;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      unsigned wa = warp_a[lane], wb = warp_b[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned ya = __shfl_up_sync(0xffffffffu, wa, o);
+        const unsigned yb = __shfl_up_sync(0xffffffffu, wb, o);
+        if (lane >= o) {
+          wa += ya;
+          wb += yb;
+        }
+      }
+      warp_a[lane] = wa;
+      warp_b[lane] = wb;
+    }
+    __syncthreads();
+    const unsigned pre_a = carry_a + (warp ? warp_a[warp - 1] : 0u) + xa - sa;
+    const unsigned pre_b = carry_b + (warp ? warp_b[warp - 1] : 0u) + xb - sb;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int i = base + tid * kPer + j;
+      if (i < n) {
+        offset[i] = pre_a + a[j];
+        item_offset[i] = pre_b + b[j];
+      }
+    }
+    __syncthreads();
+    if (tid == 0) {
+      carry_a += warp_a[31];
+      carry_b += warp_b[31];
+    }
+    __syncthreads();
+  }
+  if (tid == 0) {
+    offset[n] = carry_a;
+    item_offset[n] = carry_b;
+  }
+}
+
+__global__ void __launch_bounds__(256) tile_kernel(
+    const float* __restrict__ pos, const int* __restrict__ tri, int num_vert, int num_tri,
+    int height, int width, int tiles_x, int tiles_per_image, int num_tiles,
+    const long long* __restrict__ prev, long long* __restrict__ keys, const int* __restrict__ pairs,
+    const unsigned* __restrict__ tile_offset, const unsigned* __restrict__ item_offset,
+    unsigned* __restrict__ work) {
+  __shared__ float4 sv[3][kChunk];
+  __shared__ int st[kChunk];
+  __shared__ int s_tile;
+  __shared__ unsigned s_first, s_count;
+  const int lx = threadIdx.x % kTile, ly = threadIdx.x / kTile;
+  const unsigned total_items = item_offset[num_tiles];
+  for (;;) {
+    if (threadIdx.x == 0) {
+      const unsigned item = atomicAdd(work, 1u);
+      int tile = -1;
+      if (item < total_items) {
+        // Last tile whose first item is <= item.
+        int lo = 0, hi = num_tiles - 1;
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (item_offset[mid] <= item) lo = mid; else hi = mid - 1;
+        }
+        tile = lo;
+        const unsigned first = tile_offset[tile] + (item - item_offset[tile]) * kChunk;
+        const unsigned end = min(first + kChunk, tile_offset[tile + 1]);
+        s_first = first;
+        s_count = end - first;
+      }
+      s_tile = tile;
+    }
+    __syncthreads();
+    const int tile = s_tile;
+    if (tile < 0) break;
+    const int n = static_cast<int>(s_count);
+    if (threadIdx.x < n) {
+      const int g = pairs[s_first + threadIdx.x];
+      const int b = g / num_tri;
+      const int t = g - b * num_tri;
+      const long long base = static_cast<long long>(b) * num_vert;
+      const float4* p4 = reinterpret_cast<const float4*>(pos);
+      sv[0][threadIdx.x] = __ldg(p4 + base + __ldg(tri + 3 * static_cast<long long>(t)));
+      sv[1][threadIdx.x] = __ldg(p4 + base + __ldg(tri + 3 * static_cast<long long>(t) + 1));
+      sv[2][threadIdx.x] = __ldg(p4 + base + __ldg(tri + 3 * static_cast<long long>(t) + 2));
+      st[threadIdx.x] = t;
+    }
+    __syncthreads();
+    const int image = tile / tiles_per_image;
+    const int in_image = tile - image * tiles_per_image;
+    const int row = (in_image / tiles_x) * kTile + ly;
+    const int col = (in_image % tiles_x) * kTile + lx;
+    if (row < height && col < width) {
+      const float px = pixel_centre(col, width), py = pixel_centre(row, height);
+      const long long off = (static_cast<long long>(image) * height + row) * width + col;
+      const long long floor_key = prev != nullptr ? __ldg(prev + off) : -0x7FFFFFFFFFFFFFFFLL - 1;
+      long long best = kEmptyKey;
+      for (int i = 0; i < n; ++i) {
+        const float4 a = sv[0][i], b = sv[1][i], c = sv[2][i];
+        const long long key = coverage_key({a.x, a.y, a.z, a.w}, {b.x, b.y, b.z, b.w},
+                                           {c.x, c.y, c.z, c.w}, px, py, st[i]);
+        if (key > floor_key && key < best) best = key;
+      }
+      if (best != kEmptyKey) atomicMin(keys + off, best);
+    }
+    __syncthreads();
+  }
+}
+
+struct PixelTri {
+  bool covered;
+  int b, t;
+  int i0, i1, i2;
+  Vert v0, v1, v2;
+  float px, py;
+};
+
+__device__ __forceinline__ PixelTri pixel_triangle(const float* __restrict__ pos,
+                                                   const int* __restrict__ tri,
+                                                   const long long* __restrict__ keys,
+                                                   long long p, int num_vert, int height,
+                                                   int width) {
+  PixelTri r;
+  const long long key = keys[p];
+  r.covered = key != kEmptyKey;
+  const long long hw = static_cast<long long>(height) * width;
+  r.b = static_cast<int>(p / hw);
+  const long long in_image = p - r.b * hw;
+  const int row = static_cast<int>(in_image / width);
+  const int col = static_cast<int>(in_image - static_cast<long long>(row) * width);
+  r.px = pixel_centre(col, width);
+  r.py = pixel_centre(row, height);
+  r.t = static_cast<int>(key & 0xFFFFFFFFLL);
+  if (r.covered) {
+    r.i0 = __ldg(tri + 3 * static_cast<long long>(r.t));
+    r.i1 = __ldg(tri + 3 * static_cast<long long>(r.t) + 1);
+    r.i2 = __ldg(tri + 3 * static_cast<long long>(r.t) + 2);
+    const long long base = static_cast<long long>(r.b) * num_vert;
+    r.v0 = load_vert(pos, base + r.i0);
+    r.v1 = load_vert(pos, base + r.i1);
+    r.v2 = load_vert(pos, base + r.i2);
+  } else {
+    r.i0 = r.i1 = r.i2 = 0;
+    r.v0 = r.v1 = r.v2 = {0.0f, 0.0f, 0.0f, 1.0f};
+  }
+  return r;
+}
+
+__global__ void __launch_bounds__(256) resolve_fwd_kernel(
+    const float* __restrict__ pos, const int* __restrict__ tri, const long long* __restrict__ keys,
+    long long total, int num_vert, int height, int width, float4* __restrict__ rast,
+    float4* __restrict__ rast_db) {
+  const long long p = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (p >= total) return;
+  const PixelTri q = pixel_triangle(pos, tri, keys, p, num_vert, height, width);
+  if (!q.covered) {
+    rast[p] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (rast_db != nullptr) rast_db[p] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    return;
+  }
+  const Vert &v0 = q.v0, &v1 = q.v1, &v2 = q.v2;
+  const float a0 = v0.x - q.px * v0.w, a1 = v1.x - q.px * v1.w, a2 = v2.x - q.px * v2.w;
+  const float c0 = v0.y - q.py * v0.w, c1 = v1.y - q.py * v1.w, c2 = v2.y - q.py * v2.w;
+  const float e0 = a1 * c2 - a2 * c1, e1 = a2 * c0 - a0 * c2, e2 = a0 * c1 - a1 * c0;
+  const float s = e0 + e1 + e2;
+  const float b0 = e0 / s, b1 = e1 / s;
+  const float ew = e0 * v0.w + e1 * v1.w + e2 * v2.w;
+  const float depth = (e0 * v0.z + e1 * v1.z + e2 * v2.z) / ew;
+  rast[p] = make_float4(b0, b1, depth, static_cast<float>(q.t + 1));
+  if (rast_db != nullptr) {
+    // de/dpx = c x w and de/dpy = w x a (reference.py:281-290).
+    const float dx0 = c1 * v2.w - c2 * v1.w, dx1 = c2 * v0.w - c0 * v2.w;
+    const float dx2 = c0 * v1.w - c1 * v0.w;
+    const float dy0 = v1.w * a2 - v2.w * a1, dy1 = v2.w * a0 - v0.w * a2;
+    const float dy2 = v0.w * a1 - v1.w * a0;
+    const float sx = dx0 + dx1 + dx2, sy = dy0 + dy1 + dy2;
+    const float scale_x = 2.0f / static_cast<float>(width), scale_y = 2.0f / static_cast<float>(height);
+    rast_db[p] = make_float4((dx0 - b0 * sx) / s * scale_x, (dy0 - b0 * sy) / s * scale_y,
+                             (dx1 - b1 * sx) / s * scale_x, (dy1 - b1 * sy) / s * scale_y);
+  }
+}
+
+__device__ __forceinline__ void cross3(const float u[3], const float v[3], float out[3]) {
+  out[0] = u[1] * v[2] - u[2] * v[1];
+  out[1] = u[2] * v[0] - u[0] * v[2];
+  out[2] = u[0] * v[1] - u[1] * v[0];
+}
+
+__global__ void __launch_bounds__(256) resolve_bwd_kernel(
+    const float* __restrict__ pos, const int* __restrict__ tri, const long long* __restrict__ keys,
+    long long total, int num_vert, int height, int width, const float4* __restrict__ grad_rast,
+    const float4* __restrict__ grad_db, float* __restrict__ grad_pos) {
+  const long long p = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  const bool in_range = p < total;
+  PixelTri q;
+  if (in_range) {
+    q = pixel_triangle(pos, tri, keys, p, num_vert, height, width);
+  } else {
+    q.covered = false;
+    q.b = 0;
+    q.i0 = q.i1 = q.i2 = 0;
+  }
+  float gv[3][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  if (q.covered) {
+    const float w[3] = {q.v0.w, q.v1.w, q.v2.w};
+    const float z[3] = {q.v0.z, q.v1.z, q.v2.z};
+    const float a[3] = {q.v0.x - q.px * w[0], q.v1.x - q.px * w[1], q.v2.x - q.px * w[2]};
+    const float c[3] = {q.v0.y - q.py * w[0], q.v1.y - q.py * w[1], q.v2.y - q.py * w[2]};
+    float e[3];
+    cross3(a, c, e);
+    const float s = e[0] + e[1] + e[2];
+    const float b[3] = {e[0] / s, e[1] / s, e[2] / s};
+    const float ew = e[0] * w[0] + e[1] * w[1] + e[2] * w[2];
+    const float depth = (e[0] * z[0] + e[1] * z[1] + e[2] * z[2]) / ew;
+    const float4 gr = grad_rast[p];
+    float gb[3] = {gr.x, gr.y, 0.0f};
+    float gs = 0.0f;
+    float ga[3] = {0.f, 0.f, 0.f}, gc[3] = {0.f, 0.f, 0.f}, gw[3] = {0.f, 0.f, 0.f};
+    if (grad_db != nullptr) {
+      float dx[3], dy[3];
+      cross3(c, w, dx);
+      cross3(w, a, dy);
+      const float sx = dx[0] + dx[1] + dx[2], sy = dy[0] + dy[1] + dy[2];
+      const float4 gd = grad_db[p];
+      const float scale_x = 2.0f / static_cast<float>(width), scale_y = 2.0f / static_cast<float>(height);
+      // Gradients of db_dx_k = (dx_k - b_k sx) / s and db_dy_k, k = 0, 1.
+      const float gbx[3] = {gd.x * scale_x, gd.z * scale_x, 0.0f};
+      const float gby[3] = {gd.y * scale_y, gd.w * scale_y, 0.0f};
+      const float dbx0 = (dx[0] - b[0] * sx) / s, dbx1 = (dx[1] - b[1] * sx) / s;
+      const float dby0 = (dy[0] - b[0] * sy) / s, dby1 = (dy[1] - b[1] * sy) / s;
+      const float shared_x = (gbx[0] * b[0] + gbx[1] * b[1]) / s;
+      const float shared_y = (gby[0] * b[0] + gby[1] * b[1]) / s;
+      float gdx[3], gdy[3];
+      for (int k = 0; k < 3; ++k) {
+        gdx[k] = gbx[k] / s - shared_x;
+        gdy[k] = gby[k] / s - shared_y;
+      }
+      gb[0] -= (gbx[0] * sx + gby[0] * sy) / s;
+      gb[1] -= (gbx[1] * sx + gby[1] * sy) / s;
+      gs -= (gbx[0] * dbx0 + gbx[1] * dbx1 + gby[0] * dby0 + gby[1] * dby1) / s;
+      // dx = c x w: dL/dc += w x gdx, dL/dw += gdx x c. dy = w x a: dL/dw += a x gdy,
+      // dL/da += gdy x w.
+      float t[3];
+      cross3(w, gdx, t);
+      for (int k = 0; k < 3; ++k) gc[k] += t[k];
+      cross3(gdx, c, t);
+      for (int k = 0; k < 3; ++k) gw[k] += t[k];
+      cross3(a, gdy, t);
+      for (int k = 0; k < 3; ++k) gw[k] += t[k];
+      cross3(gdy, w, t);
+      for (int k = 0; k < 3; ++k) ga[k] += t[k];
+    }
+    // b = e / s with s = sum(e).
+    gs -= (gb[0] * b[0] + gb[1] * b[1] + gb[2] * b[2]) / s;
+    float ge[3];
+    for (int k = 0; k < 3; ++k) ge[k] = gb[k] / s + gs;
+    // depth = (e . z) / (e . w).
+    const float g_ew = gr.z / ew;
+    float gz[3];
+    for (int k = 0; k < 3; ++k) {
+      ge[k] += g_ew * (z[k] - depth * w[k]);
+      gz[k] = g_ew * e[k];
+      gw[k] -= g_ew * depth * e[k];
+    }
+    // e = a x c.
+    float t[3];
+    cross3(c, ge, t);
+    for (int k = 0; k < 3; ++k) ga[k] += t[k];
+    cross3(ge, a, t);
+    for (int k = 0; k < 3; ++k) gc[k] += t[k];
+    // a = x - px w, c = y - py w.
+    for (int k = 0; k < 3; ++k) {
+      gw[k] -= q.px * ga[k] + q.py * gc[k];
+      gv[k][0] = ga[k];
+      gv[k][1] = gc[k];
+      gv[k][2] = gz[k];
+      gv[k][3] = gw[k];
+    }
+  }
+  const long long base = static_cast<long long>(q.b) * num_vert;
+  scatter_row4(grad_pos, base + q.i0, q.covered, gv[0]);
+  scatter_row4(grad_pos, base + q.i1, q.covered, gv[1]);
+  scatter_row4(grad_pos, base + q.i2, q.covered, gv[2]);
+}
+
+bool bad_raster_args(const float* pos, const int32_t* tri, int64_t batch, int64_t num_vert,
+                     int64_t num_tri, int32_t height, int32_t width) {
+  if (batch < 0 || num_vert < 0 || num_tri < 0 || height <= 0 || width <= 0) return true;
+  if (height >= (1 << 20) || width >= (1 << 20)) return true;
+  if (batch * num_tri >= (1LL << 31)) return true;
+  if ((reinterpret_cast<uintptr_t>(pos) & 15u) != 0) return true;
+  if (batch * num_tri > 0 && (pos == nullptr || tri == nullptr)) return true;
+  return false;
+}
+
+}  // namespace
+}  // namespace dr
+
+using namespace dr;
+
+extern "C" size_t dr_raster_setup_workspace_bytes(int64_t capacity) {
+  return setup_bytes(capacity < 0 ? 0 : capacity);
+}
+
+extern "C" int dr_raster_setup(const float* pos, const int32_t* tri, int64_t batch,
+                               int64_t num_vert, int64_t num_tri, int32_t height, int32_t width,
+                               const int64_t* prev_keys, int64_t* keys, void* workspace,
+                               size_t workspace_bytes, int64_t capacity, void* stream) {
+  if (bad_raster_args(pos, tri, batch, num_vert, num_tri, height, width) || capacity < 0 ||
+      keys == nullptr || workspace == nullptr)
+    return DR_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes < setup_bytes(capacity)) return DR_ERR_WORKSPACE_TOO_SMALL;
+  cudaStream_t s = as_stream(stream);
+  SetupLayout l = setup_layout(workspace);
+  const long long pixels = batch * static_cast<long long>(height) * width;
+  cudaError_t err = cudaMemsetAsync(l.counters, 0, 2 * sizeof(unsigned long long), s);
+  if (err != cudaSuccess) return static_cast<int>(err);
+  if (pixels > 0) {
+    fill_keys_kernel<<<min(blocks_for(pixels, 256), 148u * 32u), 256, 0, s>>>(
+        reinterpret_cast<long long*>(keys), pixels);
+  }
+  const long long total = batch * num_tri;
+  if (total > 0) {
+    setup_kernel<<<blocks_for(total, 256), 256, 0, s>>>(
+        pos, tri, static_cast<int>(num_vert), static_cast<int>(num_tri), total, height, width,
+        reinterpret_cast<const long long*>(prev_keys), reinterpret_cast<long long*>(keys),
+        l.counters, l.binned, capacity);
+  }
+  return launch_status();
+}
+
+extern "C" int dr_raster_counts(const void* setup_workspace, int64_t* num_binned,
+                                int64_t* num_pairs, void* stream) {
+  if (setup_workspace == nullptr || num_binned == nullptr || num_pairs == nullptr)
+    return DR_ERR_INVALID_ARGUMENT;
+  unsigned long long host[2] = {0, 0};
+  cudaStream_t s = as_stream(stream);
+  cudaError_t err = cudaMemcpyAsync(host, setup_workspace, sizeof(host), cudaMemcpyDeviceToHost, s);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+  if (err != cudaSuccess) return static_cast<int>(err);
+  *num_binned = static_cast<int64_t>(host[0]);
+  *num_pairs = static_cast<int64_t>(host[1]);
+  return DR_OK;
+}
+
+extern "C" size_t dr_raster_bin_workspace_bytes(int64_t batch, int32_t height, int32_t width,
+                                                int64_t num_pairs) {
+  const int64_t tiles_x = (width + kTile - 1) / kTile, tiles_y = (height + kTile - 1) / kTile;
+  return bin_bytes(batch * tiles_x * tiles_y, num_pairs < 0 ? 0 : num_pairs);
+}
+
+extern "C" int dr_raster_tiles(const float* pos, const int32_t* tri, int64_t batch,
+                               int64_t num_vert, int64_t num_tri, int32_t height, int32_t width,
+                               const int64_t* prev_keys, int64_t* keys,
+                               const void* setup_workspace, int64_t num_binned, int64_t num_pairs,
+                               void* bin_workspace, size_t bin_workspace_bytes, void* stream) {
+  if (bad_raster_args(pos, tri, batch, num_vert, num_tri, height, width) || keys == nullptr ||
+      setup_workspace == nullptr || num_binned < 0 || num_pairs < 0)
+    return DR_ERR_INVALID_ARGUMENT;
+  if (num_pairs >= (1LL << 31)) return DR_ERR_TOO_LARGE;
+  if (num_binned == 0 || num_pairs == 0) return DR_OK;
+  const int tiles_x = (width + kTile - 1) / kTile, tiles_y = (height + kTile - 1) / kTile;
+  const int64_t tiles = batch * tiles_x * tiles_y;
+  if (tiles >= (1LL << 31)) return DR_ERR_TOO_LARGE;
+  if (bin_workspace == nullptr || bin_workspace_bytes < bin_bytes(tiles, num_pairs))
+    return DR_ERR_WORKSPACE_TOO_SMALL;
+  cudaStream_t s = as_stream(stream);
+  // Only the first num_binned records are read; the caller reran setup with enough capacity.
+  SetupLayout sl = setup_layout(setup_workspace);
+  BinLayout bl = bin_layout(bin_workspace, tiles, num_pairs);
+  const size_t tile_bytes = align256(sizeof(unsigned) * static_cast<size_t>(tiles + 1));
+  cudaError_t err = cudaMemsetAsync(bl.tile_count, 0, 2 * tile_bytes, s);  // counts and cursors
+  if (err == cudaSuccess) err = cudaMemsetAsync(bl.work, 0, sizeof(unsigned), s);
+  if (err != cudaSuccess) return static_cast<int>(err);
+  const int tiles_per_image = tiles_x * tiles_y;
+  const unsigned bin_blocks = min(blocks_for(num_binned * 32, 256), 148u * 16u);
+  bin_kernel<false><<<bin_blocks, 256, 0, s>>>(sl.binned, num_binned,
+                                               static_cast<int>(num_tri), tiles_x,
+                                               tiles_per_image, bl.tile_count, nullptr, nullptr);
+  scan_kernel<<<1, 1024, 0, s>>>(bl.tile_count, static_cast<int>(tiles), bl.tile_offset,
+                                 bl.item_offset);
+  bin_kernel<true><<<bin_blocks, 256, 0, s>>>(sl.binned, num_binned,
+                                              static_cast<int>(num_tri), tiles_x,
+                                              tiles_per_image, bl.tile_cursor, bl.tile_offset,
+                                              bl.pairs);
+  tile_kernel<<<148 * 8, 256, 0, s>>>(pos, tri, static_cast<int>(num_vert),
+                                      static_cast<int>(num_tri), height, width, tiles_x,
+                                      tiles_per_image, static_cast<int>(tiles),
+                                      reinterpret_cast<const long long*>(prev_keys),
+                                      reinterpret_cast<long long*>(keys), bl.pairs,
+                                      bl.tile_offset, bl.item_offset, bl.work);
+  return launch_status();
+}
+
+extern "C" int dr_raster_resolve_fwd(const float* pos, const int32_t* tri, const int64_t* keys,
+                                     int64_t batch, int64_t num_vert, int64_t num_tri,
+                                     int32_t height, int32_t width, float* rast, float* rast_db,
+                                     void* stream) {
+  if (bad_raster_args(pos, tri, batch, num_vert, num_tri, height, width) || keys == nullptr ||
+      rast == nullptr)
+    return DR_ERR_INVALID_ARGUMENT;
+  const long long total = batch * static_cast<long long>(height) * width;
+  if (total == 0) return DR_OK;
+  resolve_fwd_kernel<<<blocks_for(total, 256), 256, 0, as_stream(stream)>>>(
+      pos, tri, reinterpret_cast<const long long*>(keys), total, static_cast<int>(num_vert),
+      height, width, reinterpret_cast<float4*>(rast), reinterpret_cast<float4*>(rast_db));
+  return launch_status();
+}
+
+extern "C" int dr_raster_resolve_bwd(const float* pos, const int32_t* tri, const int64_t* keys,
+                                     int64_t batch, int64_t num_vert, int64_t num_tri,
+                                     int32_t height, int32_t width, const float* grad_rast,
+                                     const float* grad_db, float* grad_pos, void* stream) {
+  if (bad_raster_args(pos, tri, batch, num_vert, num_tri, height, width) || keys == nullptr ||
+      grad_rast == nullptr || grad_pos == nullptr)
+    return DR_ERR_INVALID_ARGUMENT;
+  const long long total = batch * static_cast<long long>(height) * width;
+  if (total == 0) return DR_OK;
+  resolve_bwd_kernel<<<blocks_for(total, 256), 256, 0, as_stream(stream)>>>(
+      pos, tri, reinterpret_cast<const long long*>(keys), total, static_cast<int>(num_vert),
+      height, width, reinterpret_cast<const float4*>(grad_rast),
+      reinterpret_cast<const float4*>(grad_db), grad_pos);
+  return launch_status();
+}

@@ -1,0 +1,778 @@
+// Texture sampling on B200: 2D and cube maps, nearest / bilinear / mipmapped / trilinear,
+// forward and backward, plus the area-weighted mip build and its adjoint.
+//
+// Semantics follow diffrast's reference backend (reference.py:149-194, :491-672; _cube.py):
+//   - texel [row, col] is centred at ((col + 0.5) / w, (row + 0.5) / h); wrap keeps the fractional
+//     part of a coordinate first; clamp and zero saturate the texel coordinate to [-1, size];
+//   - the level of detail is 0.5 log2 of the longer squared footprint axis in base-level texels,
+//     footprints saturating at 1e18, plus an optional per-pixel bias, clamped to the levels;
+//   - a pixel whose coordinates or level are NaN (or infinite under wrap) is NaN and passes no
+//     gradient; cube directions that select no point read zero;
+//   - cube lookups fold taps across face edges onto the neighbouring face and fill a tap beyond a
+//     cube corner with the mean of the other three.
+// Levels are addressed through a table of per-level pointers passed by value, so the base level is
+// the caller's texture tensor itself and no packed copy of the mip stack is ever made. The
+// coordinate arithmetic that decides which texels are read uses explicitly rounded operations in
+// the reference's order. Texel gradients are scattered with vector-free float reductions.
+#include <cstdint>
+#include <type_traits>
+
+#include "common.cuh"
+#include "warp_reduce.cuh"
+
+namespace dr {
+namespace {
+
+struct Levels {
+  const float* ptr[DR_MAX_LEVELS];
+  float* grad[DR_MAX_LEVELS];
+  long long bstride[DR_MAX_LEVELS];
+  int h[DR_MAX_LEVELS];
+  int w[DR_MAX_LEVELS];
+  int num_levels;
+};
+
+constexpr float kNaN = __builtin_nanf("");
+
+// torch.clamp(x, -1e18, 1e18) with NaN kept.
+__device__ __forceinline__ float saturate(float x) {
+  return x != x ? x : fminf(fmaxf(x, -kLimit), kLimit);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Cube-map projection (_cube.py:44-102).
+// ---------------------------------------------------------------------------------------------
+
+// Per face: axis and sign of the major direction, and of the directions of s and t.
+__device__ __forceinline__ void face_axes(int face, int& am, float& sm, int& as, float& ss, int& at,
+                                          float& st) {
+  switch (face) {
+    case 0: am = 0; sm = 1.f; as = 2; ss = -1.f; at = 1; st = -1.f; break;
+    case 1: am = 0; sm = -1.f; as = 2; ss = 1.f; at = 1; st = -1.f; break;
+    case 2: am = 1; sm = 1.f; as = 0; ss = 1.f; at = 2; st = 1.f; break;
+    case 3: am = 1; sm = -1.f; as = 0; ss = 1.f; at = 2; st = -1.f; break;
+    case 4: am = 2; sm = 1.f; as = 0; ss = 1.f; at = 1; st = -1.f; break;
+    default: am = 2; sm = -1.f; as = 0; ss = -1.f; at = 1; st = -1.f; break;
+  }
+}
+
+struct CubeProj {
+  bool valid, undefined;
+  int face, am, as, at;
+  float sm, ss, st;
+  float length, ma, rs, rt;
+  float s, t;
+  float dmask[3][2];
+  float dma[2], dsc[2], dtc[2];
+  float st_da[4];
+};
+
+__device__ __forceinline__ CubeProj cube_project(const float* dir, const float* dir_da) {
+  CubeProj c;
+  float d[3] = {dir[0], dir[1], dir[2]};
+  const float big = fmaxf(fmaxf(fabsf(d[0]), fabsf(d[1])), fabsf(d[2]));
+  c.valid = isfinite(d[0]) && isfinite(d[1]) && isfinite(d[2]) && big >= 1.17549435e-38f;
+  if (!c.valid) {
+    d[0] = 0.f;
+    d[1] = 0.f;
+    d[2] = 1.f;
+  }
+  const float ax = fabsf(d[0]), ay = fabsf(d[1]), az = fabsf(d[2]);
+  const bool x_major = (ax >= ay) && (ax >= az);
+  const bool y_major = !x_major && (ay >= az);
+  const int axis = x_major ? 0 : (y_major ? 1 : 2);
+  c.face = 2 * axis + (d[axis] < 0.f ? 1 : 0);
+  face_axes(c.face, c.am, c.sm, c.as, c.ss, c.at, c.st);
+  c.length = fmaxf(fmaxf(ax, ay), az);
+  const float unit[3] = {dvd(d[0], c.length), dvd(d[1], c.length), dvd(d[2], c.length)};
+  c.ma = mul(c.sm, unit[c.am]);
+  c.rs = dvd(mul(c.ss, unit[c.as]), c.ma);
+  c.rt = dvd(mul(c.st, unit[c.at]), c.ma);
+  c.s = mul(0.5f, add(c.rs, 1.0f));
+  c.t = mul(0.5f, add(c.rt, 1.0f));
+  c.undefined = false;
+  for (int k = 0; k < 3; ++k) c.dmask[k][0] = c.dmask[k][1] = 0.0f;
+  for (int xy = 0; xy < 2; ++xy) c.dma[xy] = c.dsc[xy] = c.dtc[xy] = 0.0f;
+  for (int i = 0; i < 4; ++i) c.st_da[i] = 0.0f;
+  if (dir_da != nullptr) {
+    float raw[6];
+    bool nan = false;
+    for (int i = 0; i < 6; ++i) {
+      raw[i] = dir_da[i];
+      nan |= raw[i] != raw[i];
+    }
+    c.undefined = c.valid && nan;
+    const bool use = c.valid && !c.undefined;
+    float da[3][2];
+    for (int k = 0; k < 3; ++k) {
+      for (int xy = 0; xy < 2; ++xy) {
+        const float v = dvd(use ? raw[2 * k + xy] : 0.0f, c.length);
+        c.dmask[k][xy] = (v >= -kLimit && v <= kLimit) ? 1.f : 0.f;
+        da[k][xy] = fminf(fmaxf(v, -kLimit), kLimit);
+      }
+    }
+    for (int xy = 0; xy < 2; ++xy) {
+      c.dma[xy] = mul(c.sm, da[c.am][xy]);
+      c.dsc[xy] = mul(c.ss, da[c.as][xy]);
+      c.dtc[xy] = mul(c.st, da[c.at][xy]);
+      const float ds = dvd(mul(0.5f, sub(c.dsc[xy], mul(c.rs, c.dma[xy]))), c.ma);
+      const float dt = dvd(mul(0.5f, sub(c.dtc[xy], mul(c.rt, c.dma[xy]))), c.ma);
+      c.st_da[xy] = c.undefined ? kNaN : ds;
+      c.st_da[2 + xy] = c.undefined ? kNaN : dt;
+    }
+  }
+  return c;
+}
+
+// Gradients of the directions (and their derivatives) from those of st and st_da.
+__device__ __forceinline__ void cube_project_bwd(const CubeProj& c, float g_s, float g_t,
+                                                 const float g_st_da[4], float g_dir[3],
+                                                 float g_dir_da[6]) {
+  float g_rs = 0.5f * g_s, g_rt = 0.5f * g_t, g_ma = 0.0f;
+  float g_da[3][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
+  if (g_st_da != nullptr) {
+    for (int xy = 0; xy < 2; ++xy) {
+      const float g_ds = g_st_da[xy], g_dt = g_st_da[2 + xy];
+      const float ds = 0.5f * (c.dsc[xy] - c.rs * c.dma[xy]) / c.ma;
+      const float dt = 0.5f * (c.dtc[xy] - c.rt * c.dma[xy]) / c.ma;
+      const float g_dsc = 0.5f * g_ds / c.ma;
+      const float g_dtc = 0.5f * g_dt / c.ma;
+      const float g_dma = -0.5f * (g_ds * c.rs + g_dt * c.rt) / c.ma;
+      g_rs -= 0.5f * g_ds * c.dma[xy] / c.ma;
+      g_rt -= 0.5f * g_dt * c.dma[xy] / c.ma;
+      g_ma -= (g_ds * ds + g_dt * dt) / c.ma;
+      g_da[c.am][xy] += c.sm * g_dma;
+      g_da[c.as][xy] += c.ss * g_dsc;
+      g_da[c.at][xy] += c.st * g_dtc;
+    }
+  }
+  float g_unit[3] = {0.f, 0.f, 0.f};
+  g_unit[c.as] += c.ss * g_rs / c.ma;
+  g_unit[c.at] += c.st * g_rt / c.ma;
+  g_ma -= (g_rs * c.rs + g_rt * c.rt) / c.ma;
+  g_unit[c.am] += c.sm * g_ma;
+  for (int k = 0; k < 3; ++k) g_dir[k] = g_unit[k] / c.length;
+  for (int k = 0; k < 3; ++k)
+    for (int xy = 0; xy < 2; ++xy) g_dir_da[2 * k + xy] = g_da[k][xy] * c.dmask[k][xy] / c.length;
+}
+
+// Texel one step outside its face moved onto the neighbouring face, in half-texel integer units
+// (_cube.py:105-143). `exists` is false beyond a cube corner.
+__device__ __forceinline__ void cube_fold(int face, int row, int col, int size, int& out_face,
+                                          int& out_row, int& out_col, bool& exists) {
+  const bool over_col = col < 0 || col >= size;
+  const bool over_row = row < 0 || row >= size;
+  exists = !(over_col && over_row);
+  if (!over_col && !over_row) {
+    out_face = face;
+    out_row = row;
+    out_col = col;
+    return;
+  }
+  int am, as, at;
+  float sm, ss, st;
+  face_axes(face, am, sm, as, ss, at, st);
+  int p[3] = {0, 0, 0};
+  p[am] += size * static_cast<int>(sm);
+  p[as] += (2 * col + 1 - size) * static_cast<int>(ss);
+  p[at] += (2 * row + 1 - size) * static_cast<int>(st);
+  for (int k = 0; k < 3; ++k) p[k] = min(max(p[k], -size), size);
+  p[am] -= static_cast<int>(sm);
+  int axis = 0;
+  if (abs(p[1]) > abs(p[axis])) axis = 1;
+  if (abs(p[2]) > abs(p[axis])) axis = 2;
+  out_face = 2 * axis + (p[axis] < 0 ? 1 : 0);
+  face_axes(out_face, am, sm, as, ss, at, st);
+  const int sc = p[as] * static_cast<int>(ss) + size - 1;
+  const int tc = p[at] * static_cast<int>(st) + size - 1;
+  // Floor division by 2 of possibly negative values.
+  out_col = max((sc >= 0 ? sc : sc - 1) / 2, 0);
+  out_row = max((tc >= 0 ? tc : tc - 1) / 2, 0);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Texel coordinates and footprints.
+// ---------------------------------------------------------------------------------------------
+
+// Continuous texel coordinate coord * size - shift under the boundary mode (reference.py:615-633),
+// with its derivative with respect to coord * size (0 where clamped) and whether it is unusable.
+template <int B>
+__device__ __forceinline__ float texel_coord(float coord, int size, float shift, bool& bad,
+                                             float& slope) {
+  const float s = static_cast<float>(size);
+  float x;
+  slope = 1.0f;
+  if (B == DR_BOUNDARY_WRAP) {
+    x = sub(mul(sub(coord, floorf(coord)), s), shift);
+    bad = !isfinite(x);
+  } else if (B == DR_BOUNDARY_CUBE) {
+    x = sub(mul(coord, s), shift);
+    bad = !isfinite(x);
+  } else {
+    x = sub(mul(coord, s), shift);
+    bad = x != x;
+    slope = (x >= -1.0f && x <= s) ? 1.0f : 0.0f;
+    x = fminf(fmaxf(x, -1.0f), s);
+  }
+  if (bad) {
+    x = 0.0f;
+    slope = 0.0f;
+  }
+  return x;
+}
+
+// Element offset (without channel) of texel (row, col) of level l for this view, or ok = false
+// for a texel that does not exist (zero boundary, beyond a cube corner).
+template <int B>
+__device__ __forceinline__ long long texel_offset(const Levels& L, int l, long long view, int face,
+                                                  int row, int col, int channels, bool& ok) {
+  const int h = L.h[l], w = L.w[l];
+  ok = true;
+  if (B == DR_BOUNDARY_WRAP) {
+    row %= h;
+    row += row < 0 ? h : 0;
+    col %= w;
+    col += col < 0 ? w : 0;
+  } else if (B == DR_BOUNDARY_CUBE) {
+    int f2, r2, c2;
+    cube_fold(face, row, col, w, f2, r2, c2, ok);
+    face = f2;
+    row = r2;
+    col = c2;
+  } else {
+    if (B == DR_BOUNDARY_ZERO) ok = row >= 0 && row < h && col >= 0 && col < w;
+    row = min(max(row, 0), h - 1);
+    col = min(max(col, 0), w - 1);
+  }
+  long long texel = static_cast<long long>(row) * w + col;
+  if (B == DR_BOUNDARY_CUBE) texel += static_cast<long long>(face) * h * w;
+  return view * L.bstride[l] + texel * channels;
+}
+
+struct Footprint {
+  long long off[4];
+  bool ok[4];
+  float fx, fy;
+  float slope_x, slope_y;  // d(texel coordinate) / d(coord * size)
+  float missing;           // weight of the taps that do not exist beyond a cube corner
+  float dmiss_dx, dmiss_dy;
+  bool bad;
+};
+
+// Bilinear footprint of (u, v) in level l (reference.py:576-612).
+template <int B>
+__device__ __forceinline__ Footprint bilinear_footprint(const Levels& L, int l, long long view,
+                                                        int face, float u, float v, int channels) {
+  Footprint f;
+  bool bad_x, bad_y;
+  const float x = texel_coord<B>(u, L.w[l], 0.5f, bad_x, f.slope_x);
+  const float y = texel_coord<B>(v, L.h[l], 0.5f, bad_y, f.slope_y);
+  f.bad = bad_x || bad_y;
+  const float x0 = floorf(x), y0 = floorf(y);
+  f.fx = sub(x, x0);
+  f.fy = sub(y, y0);
+  const int col = static_cast<int>(x0), row = static_cast<int>(y0);
+  f.off[0] = texel_offset<B>(L, l, view, face, row, col, channels, f.ok[0]);
+  f.off[1] = texel_offset<B>(L, l, view, face, row, col + 1, channels, f.ok[1]);
+  f.off[2] = texel_offset<B>(L, l, view, face, row + 1, col, channels, f.ok[2]);
+  f.off[3] = texel_offset<B>(L, l, view, face, row + 1, col + 1, channels, f.ok[3]);
+  f.missing = f.dmiss_dx = f.dmiss_dy = 0.0f;
+  if (B == DR_BOUNDARY_CUBE) {
+    const int w = L.w[l], h = L.h[l];
+    const float left = col < 0, right = col + 1 >= w, above = row < 0, below = row + 1 >= h;
+    const float m00 = left * above, m01 = right * above, m10 = left * below, m11 = right * below;
+    const float fx = f.fx, fy = f.fy;
+    f.missing = add(mul(sub(1.0f, fy), add(mul(sub(1.0f, fx), m00), mul(fx, m01))),
+                    mul(fy, add(mul(sub(1.0f, fx), m10), mul(fx, m11))));
+    f.dmiss_dx = (1.0f - fy) * (m01 - m00) + fy * (m11 - m10);
+    f.dmiss_dy = ((1.0f - fx) * m10 + fx * m11) - ((1.0f - fx) * m00 + fx * m01);
+  }
+  return f;
+}
+
+// Bilinear value of channel c with the reference's rounding order.
+template <int B>
+__device__ __forceinline__ float bilinear_value(const float* __restrict__ level, const Footprint& f,
+                                                int c, float t[4]) {
+  for (int k = 0; k < 4; ++k) t[k] = f.ok[k] ? __ldg(level + f.off[k] + c) : 0.0f;
+  const float gx = sub(1.0f, f.fx), gy = sub(1.0f, f.fy);
+  float out = add(mul(gy, add(mul(gx, t[0]), mul(f.fx, t[1]))),
+                  mul(f.fy, add(mul(gx, t[2]), mul(f.fx, t[3]))));
+  if (B == DR_BOUNDARY_CUBE) {
+    out = add(out, dvd(mul(f.missing, add(add(add(t[0], t[1]), t[2]), t[3])), 3.0f));
+  }
+  return out;
+}
+
+// Level of detail from the footprint (reference.py:491-501), NaN propagated, with the squared
+// axis lengths kept for the backward pass.
+__device__ __forceinline__ float level_of_detail(const float da[4], int h, int w, float& len_x,
+                                                 float& len_y) {
+  const float fw = static_cast<float>(w), fh = static_cast<float>(h);
+  const float ux = saturate(mul(da[0], fw)), uy = saturate(mul(da[1], fw));
+  const float vx = saturate(mul(da[2], fh)), vy = saturate(mul(da[3], fh));
+  len_x = add(mul(ux, ux), mul(vx, vx));
+  len_y = add(mul(uy, uy), mul(vy, vy));
+  float m = nanmax(len_x, len_y);
+  m = m != m ? m : fmaxf(m, 1e-30f);
+  return mul(0.5f, log2f(m));
+}
+
+__device__ __forceinline__ void level_of_detail_bwd(const float da[4], int h, int w, float g_lod,
+                                                    float g_da[4]) {
+  const float fw = static_cast<float>(w), fh = static_cast<float>(h);
+  const float raw[4] = {da[0] * fw, da[1] * fw, da[2] * fh, da[3] * fh};
+  const float scale[4] = {fw, fw, fh, fh};
+  float cl[4], mask[4];
+  for (int i = 0; i < 4; ++i) {
+    cl[i] = fminf(fmaxf(raw[i], -kLimit), kLimit);
+    mask[i] = (raw[i] >= -kLimit && raw[i] <= kLimit) ? 1.0f : 0.0f;
+  }
+  const float len_x = cl[0] * cl[0] + cl[2] * cl[2];
+  const float len_y = cl[1] * cl[1] + cl[3] * cl[3];
+  const float m = fmaxf(len_x, len_y);
+  const float g_m = m >= 1e-30f ? g_lod * 0.5f / (m * 0.6931471805599453f) : 0.0f;
+  const float share_x = len_x > len_y ? 1.0f : (len_x == len_y ? 0.5f : 0.0f);
+  const float g_lx = g_m * share_x, g_ly = g_m * (1.0f - share_x);
+  g_da[0] = g_lx * 2.0f * cl[0] * scale[0] * mask[0];
+  g_da[1] = g_ly * 2.0f * cl[1] * scale[1] * mask[1];
+  g_da[2] = g_lx * 2.0f * cl[2] * scale[2] * mask[2];
+  g_da[3] = g_ly * 2.0f * cl[3] * scale[3] * mask[3];
+}
+
+// Everything a pixel's lookup needs before the channel loop.
+template <int MODE, int B>
+struct Lookup {
+  bool bad, valid;
+  CubeProj cube;
+  float u, v;
+  int face;
+  float da[4];
+  bool has_da;
+  float lod_raw;  // level of detail before clamping (NaN replaced by 0)
+  int lo, hi;
+  float frac;
+  Footprint f_lo, f_hi;
+  long long near_off;
+  bool near_ok;
+};
+
+template <int MODE, int B>
+__device__ __forceinline__ void prepare(const Levels& L, int channels, const float* __restrict__ uv,
+                                        const float* __restrict__ uv_da,
+                                        const float* __restrict__ bias, long long p,
+                                        long long view, Lookup<MODE, B>& k) {
+  constexpr bool kMip = MODE >= DR_FILTER_LINEAR_MIPMAP_NEAREST;
+  k.valid = true;
+  k.face = 0;
+  k.has_da = kMip && uv_da != nullptr;
+  if (B == DR_BOUNDARY_CUBE) {
+    k.cube = cube_project(uv + p * 3, k.has_da ? uv_da + p * 6 : nullptr);
+    k.valid = k.cube.valid;
+    k.face = k.cube.face;
+    k.u = k.cube.s;
+    k.v = k.cube.t;
+    for (int i = 0; i < 4; ++i) k.da[i] = k.has_da ? k.cube.st_da[i] : 0.0f;
+  } else {
+    k.u = uv[p * 2];
+    k.v = uv[p * 2 + 1];
+    for (int i = 0; i < 4; ++i) k.da[i] = k.has_da ? uv_da[p * 4 + i] : 0.0f;
+  }
+  k.bad = false;
+  k.lo = k.hi = 0;
+  k.frac = 0.0f;
+  k.lod_raw = 0.0f;
+  if (kMip) {
+    float lod = 0.0f;
+    if (k.has_da) {
+      float lx, ly;
+      lod = add(lod, level_of_detail(k.da, L.h[0], L.w[0], lx, ly));
+    }
+    if (bias != nullptr) lod = add(lod, bias[p]);
+    k.bad = lod != lod;
+    if (k.bad) lod = 0.0f;
+    k.lod_raw = lod;
+    const float top = static_cast<float>(L.num_levels - 1);
+    lod = fminf(fmaxf(lod, 0.0f), top);
+    const bool blend = MODE == DR_FILTER_LINEAR_MIPMAP_LINEAR;
+    const float lower = floorf(blend ? lod : add(lod, 0.5f));
+    k.lo = static_cast<int>(lower);
+    k.hi = min(k.lo + 1, L.num_levels - 1);
+    k.frac = blend ? sub(lod, lower) : 0.0f;
+  }
+  if (MODE == DR_FILTER_NEAREST) {
+    bool bx, by;
+    float sx, sy;
+    const float x = texel_coord<B>(k.u, L.w[0], 0.0f, bx, sx);
+    const float y = texel_coord<B>(k.v, L.h[0], 0.0f, by, sy);
+    k.bad = k.bad || bx || by;
+    // A direction exactly on the far edge of a cube face stays on that face.
+    if (B == DR_BOUNDARY_CUBE) {
+      const int h = L.h[0], w = L.w[0];
+      const int row = min(max(static_cast<int>(floorf(y)), 0), h - 1);
+      const int col = min(max(static_cast<int>(floorf(x)), 0), w - 1);
+      k.near_ok = true;
+      k.near_off = view * L.bstride[0] +
+                   ((static_cast<long long>(k.face) * h + row) * w + col) * channels;
+    } else {
+      k.near_off = texel_offset<B>(L, 0, view, 0, static_cast<int>(floorf(y)),
+                                   static_cast<int>(floorf(x)), channels, k.near_ok);
+    }
+  } else {
+    k.f_lo = bilinear_footprint<B>(L, k.lo, view, k.face, k.u, k.v, channels);
+    k.bad = k.bad || k.f_lo.bad;
+    if (MODE == DR_FILTER_LINEAR_MIPMAP_LINEAR) {
+      k.f_hi = bilinear_footprint<B>(L, k.hi, view, k.face, k.u, k.v, channels);
+      k.bad = k.bad || k.f_hi.bad;
+    }
+  }
+}
+
+template <int MODE, int B>
+__global__ void __launch_bounds__(256) texture_fwd_kernel(
+    const Levels L, int channels, const float* __restrict__ uv, const float* __restrict__ uv_da,
+    const float* __restrict__ bias, long long total, long long pixels_per_image,
+    float* __restrict__ out) {
+  const long long p = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (p >= total) return;
+  const long long view = p / pixels_per_image;
+  Lookup<MODE, B> k;
+  prepare<MODE, B>(L, channels, uv, uv_da, bias, p, view, k);
+  float* o = out + p * channels;
+  for (int c = 0; c < channels; ++c) {
+    float value;
+    if (MODE == DR_FILTER_NEAREST) {
+      value = k.near_ok ? __ldg(L.ptr[0] + k.near_off + c) : 0.0f;
+    } else {
+      float t[4];
+      value = bilinear_value<B>(L.ptr[k.lo], k.f_lo, c, t);
+      if (MODE == DR_FILTER_LINEAR_MIPMAP_LINEAR) {
+        const float above = bilinear_value<B>(L.ptr[k.hi], k.f_hi, c, t);
+        value = add(mul(value, sub(1.0f, k.frac)), mul(above, k.frac));
+      }
+    }
+    if (k.bad) value = kNaN;
+    if (!k.valid) value = 0.0f;
+    o[c] = value;
+  }
+}
+
+// Scatter of g into the taps of a footprint, each tap weighted by its bilinear weight (plus the
+// cube-corner share of the missing taps).
+template <int B>
+__device__ __forceinline__ void scatter_footprint(float* __restrict__ grad, const Footprint& f,
+                                                  int c, float g) {
+  const float gx = 1.0f - f.fx, gy = 1.0f - f.fy;
+  const float wgt[4] = {gx * gy, f.fx * gy, gx * f.fy, f.fx * f.fy};
+  const float extra = B == DR_BOUNDARY_CUBE ? f.missing / 3.0f : 0.0f;
+  for (int t = 0; t < 4; ++t) {
+    const float value = g * (wgt[t] + extra);
+    if (f.ok[t] && value != 0.0f) red_add(grad + f.off[t] + c, value);
+  }
+}
+
+template <int MODE, int B>
+__global__ void __launch_bounds__(256) texture_bwd_kernel(
+    const Levels L, int channels, const float* __restrict__ uv, const float* __restrict__ uv_da,
+    const float* __restrict__ bias, long long total, long long pixels_per_image,
+    const float* __restrict__ grad_out, float* __restrict__ grad_uv,
+    float* __restrict__ grad_uv_da, float* __restrict__ grad_bias) {
+  const long long p = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (p >= total) return;
+  const long long view = p / pixels_per_image;
+  Lookup<MODE, B> k;
+  prepare<MODE, B>(L, channels, uv, uv_da, bias, p, view, k);
+  const bool live = !k.bad && k.valid;
+  const bool coord_grads = grad_uv != nullptr || grad_uv_da != nullptr || grad_bias != nullptr;
+  float g_fx_lo = 0.f, g_fy_lo = 0.f, g_fx_hi = 0.f, g_fy_hi = 0.f, g_frac = 0.f;
+  if (live) {
+    const float w_hi = k.frac, w_lo = 1.0f - k.frac;
+    for (int c = 0; c < channels; ++c) {
+      const float g = grad_out[p * channels + c];
+      if (MODE == DR_FILTER_NEAREST) {
+        if (k.near_ok && g != 0.0f) red_add(L.grad[0] + k.near_off + c, g);
+        continue;
+      }
+      const float g_lo = MODE == DR_FILTER_LINEAR_MIPMAP_LINEAR ? g * w_lo : g;
+      scatter_footprint<B>(L.grad[k.lo], k.f_lo, c, g_lo);
+      if (MODE == DR_FILTER_LINEAR_MIPMAP_LINEAR) scatter_footprint<B>(L.grad[k.hi], k.f_hi, c, g * w_hi);
+      if (!coord_grads) continue;
+      float t[4];
+      const float lower = bilinear_value<B>(L.ptr[k.lo], k.f_lo, c, t);
+      {
+        const Footprint& f = k.f_lo;
+        float dfx = (1.0f - f.fy) * (t[1] - t[0]) + f.fy * (t[3] - t[2]);
+        float dfy = (1.0f - f.fx) * (t[2] - t[0]) + f.fx * (t[3] - t[1]);
+        if (B == DR_BOUNDARY_CUBE) {
+          const float third = (t[0] + t[1] + t[2] + t[3]) / 3.0f;
+          dfx += f.dmiss_dx * third;
+          dfy += f.dmiss_dy * third;
+        }
+        g_fx_lo += g_lo * dfx;
+        g_fy_lo += g_lo * dfy;
+      }
+      if (MODE == DR_FILTER_LINEAR_MIPMAP_LINEAR) {
+        const float upper = bilinear_value<B>(L.ptr[k.hi], k.f_hi, c, t);
+        const Footprint& f = k.f_hi;
+        float dfx = (1.0f - f.fy) * (t[1] - t[0]) + f.fy * (t[3] - t[2]);
+        float dfy = (1.0f - f.fx) * (t[2] - t[0]) + f.fx * (t[3] - t[1]);
+        if (B == DR_BOUNDARY_CUBE) {
+          const float third = (t[0] + t[1] + t[2] + t[3]) / 3.0f;
+          dfx += f.dmiss_dx * third;
+          dfy += f.dmiss_dy * third;
+        }
+        g_fx_hi += g * w_hi * dfx;
+        g_fy_hi += g * w_hi * dfy;
+        g_frac += g * (upper - lower);
+      }
+    }
+  }
+  if (!coord_grads) return;
+  // Gradient of the coordinates (u, v) or, for a cube, of the face coordinates (s, t).
+  float g_u = 0.f, g_v = 0.f;
+  if (live && MODE != DR_FILTER_NEAREST) {
+    g_u = g_fx_lo * k.f_lo.slope_x * static_cast<float>(L.w[k.lo]);
+    g_v = g_fy_lo * k.f_lo.slope_y * static_cast<float>(L.h[k.lo]);
+    if (MODE == DR_FILTER_LINEAR_MIPMAP_LINEAR) {
+      g_u += g_fx_hi * k.f_hi.slope_x * static_cast<float>(L.w[k.hi]);
+      g_v += g_fy_hi * k.f_hi.slope_y * static_cast<float>(L.h[k.hi]);
+    }
+  }
+  // Gradient of the level of detail: only trilinear filtering depends on it smoothly; it is
+  // clamped to the available levels.
+  float g_lod = 0.f;
+  if (live && MODE == DR_FILTER_LINEAR_MIPMAP_LINEAR) {
+    const float top = static_cast<float>(L.num_levels - 1);
+    if (k.lod_raw >= 0.0f && k.lod_raw <= top) g_lod = g_frac;
+  }
+  if (grad_bias != nullptr) grad_bias[p] = g_lod;
+  float g_da[4] = {0.f, 0.f, 0.f, 0.f};
+  if (k.has_da && g_lod != 0.0f) level_of_detail_bwd(k.da, L.h[0], L.w[0], g_lod, g_da);
+  if (B == DR_BOUNDARY_CUBE) {
+    float g_dir[3] = {0.f, 0.f, 0.f}, g_dir_da[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (live) cube_project_bwd(k.cube, g_u, g_v, k.has_da ? g_da : nullptr, g_dir, g_dir_da);
+    if (grad_uv != nullptr)
+      for (int i = 0; i < 3; ++i) grad_uv[p * 3 + i] = g_dir[i];
+    if (grad_uv_da != nullptr)
+      for (int i = 0; i < 6; ++i) grad_uv_da[p * 6 + i] = g_dir_da[i];
+  } else {
+    if (grad_uv != nullptr) {
+      grad_uv[p * 2] = g_u;
+      grad_uv[p * 2 + 1] = g_v;
+    }
+    if (grad_uv_da != nullptr)
+      for (int i = 0; i < 4; ++i) grad_uv_da[p * 4 + i] = g_da[i];
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Mip chain (reference.py:449-488): bin j of the coarse level spans [j n, (j + 1) n] and texel i
+// of the fine level [i m, (i + 1) m] in units of 1 / (n m), m = ceil(n / 2); the weight is the
+// overlap divided by n (0.5 and 0.5 for even n, three taps for odd n).
+// ---------------------------------------------------------------------------------------------
+
+__device__ __forceinline__ float halving_weight(int j, int i, int n, int m) {
+  const long long lo = max(static_cast<long long>(j) * n, static_cast<long long>(i) * m);
+  const long long hi = min(static_cast<long long>(j + 1) * n, static_cast<long long>(i + 1) * m);
+  return hi > lo ? static_cast<float>(hi - lo) / static_cast<float>(n) : 0.0f;
+}
+
+__global__ void __launch_bounds__(256) mip_down_kernel(const float* __restrict__ src,
+                                                       long long images, int h, int w,
+                                                       int channels, float* __restrict__ dst) {
+  const int oh = (h + 1) / 2, ow = (w + 1) / 2;
+  const long long total = images * oh * ow * static_cast<long long>(channels);
+  const long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (e >= total) return;
+  const int c = static_cast<int>(e % channels);
+  long long rest = e / channels;
+  const int k = static_cast<int>(rest % ow);
+  rest /= ow;
+  const int j = static_cast<int>(rest % oh);
+  const long long img = rest / oh;
+  const int r0 = static_cast<int>(static_cast<long long>(j) * h / oh);
+  const int c0 = static_cast<int>(static_cast<long long>(k) * w / ow);
+  const float* base = src + img * h * static_cast<long long>(w) * channels + c;
+  float acc = 0.0f;
+  for (int r = r0; r < min(r0 + 3, h); ++r) {
+    const float wr = h > 1 ? halving_weight(j, r, h, oh) : 1.0f;
+    if (wr == 0.0f) continue;
+    float row = 0.0f;
+    for (int q = c0; q < min(c0 + 3, w); ++q) {
+      const float wc = w > 1 ? halving_weight(k, q, w, ow) : 1.0f;
+      if (wc != 0.0f) row += wc * __ldg(base + (static_cast<long long>(r) * w + q) * channels);
+    }
+    acc += wr * row;
+  }
+  dst[e] = acc;
+}
+
+__global__ void __launch_bounds__(256) mip_down_bwd_kernel(const float* __restrict__ grad_dst,
+                                                           long long images, int h, int w,
+                                                           int channels,
+                                                           float* __restrict__ grad_src) {
+  const int oh = (h + 1) / 2, ow = (w + 1) / 2;
+  const long long total = images * h * static_cast<long long>(w) * channels;
+  const long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (e >= total) return;
+  const int c = static_cast<int>(e % channels);
+  long long rest = e / channels;
+  const int q = static_cast<int>(rest % w);
+  rest /= w;
+  const int r = static_cast<int>(rest % h);
+  const long long img = rest / h;
+  // Coarse bins overlapping fine texel i: j in [floor(i m / n), ceil((i + 1) m / n) - 1].
+  const int j0 = static_cast<int>(static_cast<long long>(r) * oh / h);
+  const int j1 = static_cast<int>((static_cast<long long>(r + 1) * oh + h - 1) / h) - 1;
+  const int k0 = static_cast<int>(static_cast<long long>(q) * ow / w);
+  const int k1 = static_cast<int>((static_cast<long long>(q + 1) * ow + w - 1) / w) - 1;
+  const float* base = grad_dst + img * oh * static_cast<long long>(ow) * channels + c;
+  float acc = 0.0f;
+  for (int j = j0; j <= j1; ++j) {
+    const float wr = h > 1 ? halving_weight(j, r, h, oh) : 1.0f;
+    float row = 0.0f;
+    for (int k = k0; k <= k1; ++k) {
+      const float wc = w > 1 ? halving_weight(k, q, w, ow) : 1.0f;
+      row += wc * __ldg(base + (static_cast<long long>(j) * ow + k) * channels);
+    }
+    acc += wr * row;
+  }
+  grad_src[e] += acc;
+}
+
+template <int MODE, int B>
+void launch_fwd(const Levels& L, int channels, const float* uv, const float* uv_da,
+                const float* bias, long long total, long long ppi, float* out, cudaStream_t s) {
+  texture_fwd_kernel<MODE, B><<<blocks_for(total, 256), 256, 0, s>>>(L, channels, uv, uv_da, bias,
+                                                                      total, ppi, out);
+}
+
+template <int MODE, int B>
+void launch_bwd(const Levels& L, int channels, const float* uv, const float* uv_da,
+                const float* bias, long long total, long long ppi, const float* grad_out,
+                float* grad_uv, float* grad_uv_da, float* grad_bias, cudaStream_t s) {
+  texture_bwd_kernel<MODE, B><<<blocks_for(total, 256), 256, 0, s>>>(
+      L, channels, uv, uv_da, bias, total, ppi, grad_out, grad_uv, grad_uv_da, grad_bias);
+}
+
+template <int B, typename F>
+void dispatch_mode(int mode, F&& f) {
+  switch (mode) {
+    case 0: f(std::integral_constant<int, 0>{}, std::integral_constant<int, B>{}); break;
+    case 1: f(std::integral_constant<int, 1>{}, std::integral_constant<int, B>{}); break;
+    case 2: f(std::integral_constant<int, 2>{}, std::integral_constant<int, B>{}); break;
+    default: f(std::integral_constant<int, 3>{}, std::integral_constant<int, B>{}); break;
+  }
+}
+
+template <typename F>
+void dispatch(int mode, int boundary, F&& f) {
+  switch (boundary) {
+    case 0: dispatch_mode<0>(mode, f); break;
+    case 1: dispatch_mode<1>(mode, f); break;
+    case 2: dispatch_mode<2>(mode, f); break;
+    default: dispatch_mode<3>(mode, f); break;
+  }
+}
+
+int make_levels(const float* const* level_ptr, float* const* grad_ptr, const int32_t* level_h,
+                const int32_t* level_w, const int64_t* level_batch_stride, int32_t num_levels,
+                int32_t filter_mode, int32_t boundary_mode, Levels& L) {
+  if (num_levels < 1 || num_levels > DR_MAX_LEVELS || level_ptr == nullptr || level_h == nullptr ||
+      level_w == nullptr || level_batch_stride == nullptr)
+    return DR_ERR_INVALID_ARGUMENT;
+  if (filter_mode < 0 || filter_mode > 3 || boundary_mode < 0 || boundary_mode > 3)
+    return DR_ERR_INVALID_ARGUMENT;
+  L.num_levels = num_levels;
+  for (int l = 0; l < DR_MAX_LEVELS; ++l) {
+    const bool used = l < num_levels;
+    L.ptr[l] = used ? level_ptr[l] : nullptr;
+    L.grad[l] = used && grad_ptr != nullptr ? grad_ptr[l] : nullptr;
+    L.h[l] = used ? level_h[l] : 1;
+    L.w[l] = used ? level_w[l] : 1;
+    L.bstride[l] = used ? level_batch_stride[l] : 0;
+    if (used && (L.ptr[l] == nullptr || L.h[l] < 1 || L.w[l] < 1 || L.bstride[l] < 0))
+      return DR_ERR_INVALID_ARGUMENT;
+    if (used && grad_ptr != nullptr && L.grad[l] == nullptr) return DR_ERR_INVALID_ARGUMENT;
+    if (used && boundary_mode == DR_BOUNDARY_CUBE && L.h[l] != L.w[l]) return DR_ERR_INVALID_ARGUMENT;
+  }
+  return DR_OK;
+}
+
+}  // namespace
+}  // namespace dr
+
+using namespace dr;
+
+extern "C" int dr_texture_fwd(const float* const* level_ptr, const int32_t* level_h,
+                              const int32_t* level_w, const int64_t* level_batch_stride,
+                              int32_t num_levels, int32_t channels, const float* uv,
+                              const float* uv_da, const float* bias, int64_t batch,
+                              int32_t height, int32_t width, int32_t filter_mode,
+                              int32_t boundary_mode, float* out, void* stream) {
+  Levels L;
+  int status = make_levels(level_ptr, nullptr, level_h, level_w, level_batch_stride, num_levels,
+                           filter_mode, boundary_mode, L);
+  if (status != DR_OK) return status;
+  if (channels < 1 || batch < 0 || height < 0 || width < 0) return DR_ERR_INVALID_ARGUMENT;
+  const long long total = batch * static_cast<long long>(height) * width;
+  if (total == 0) return DR_OK;
+  if (uv == nullptr || out == nullptr) return DR_ERR_INVALID_ARGUMENT;
+  const long long ppi = static_cast<long long>(height) * width;
+  cudaStream_t s = as_stream(stream);
+  dispatch(filter_mode, boundary_mode, [&](auto m, auto b) {
+    launch_fwd<decltype(m)::value, decltype(b)::value>(L, channels, uv, uv_da, bias, total, ppi,
+                                                       out, s);
+  });
+  return launch_status();
+}
+
+extern "C" int dr_texture_bwd(const float* const* level_ptr, float* const* grad_level_ptr,
+                              const int32_t* level_h, const int32_t* level_w,
+                              const int64_t* level_batch_stride, int32_t num_levels,
+                              int32_t channels, const float* uv, const float* uv_da,
+                              const float* bias, int64_t batch, int32_t height, int32_t width,
+                              int32_t filter_mode, int32_t boundary_mode, const float* grad_out,
+                              float* grad_uv, float* grad_uv_da, float* grad_bias,
+                              void* stream) {
+  if (grad_level_ptr == nullptr) return DR_ERR_INVALID_ARGUMENT;
+  Levels L;
+  int status = make_levels(level_ptr, grad_level_ptr, level_h, level_w, level_batch_stride,
+                           num_levels, filter_mode, boundary_mode, L);
+  if (status != DR_OK) return status;
+  if (channels < 1 || batch < 0 || height < 0 || width < 0) return DR_ERR_INVALID_ARGUMENT;
+  const long long total = batch * static_cast<long long>(height) * width;
+  if (total == 0) return DR_OK;
+  if (uv == nullptr || grad_out == nullptr) return DR_ERR_INVALID_ARGUMENT;
+  if (grad_uv_da != nullptr && uv_da == nullptr) return DR_ERR_INVALID_ARGUMENT;
+  if (grad_bias != nullptr && bias == nullptr) return DR_ERR_INVALID_ARGUMENT;
+  const long long ppi = static_cast<long long>(height) * width;
+  cudaStream_t s = as_stream(stream);
+  dispatch(filter_mode, boundary_mode, [&](auto m, auto b) {
+    launch_bwd<decltype(m)::value, decltype(b)::value>(L, channels, uv, uv_da, bias, total, ppi,
+                                                       grad_out, grad_uv, grad_uv_da, grad_bias, s);
+  });
+  return launch_status();
+}
+
+extern "C" int dr_mip_downsample(const float* src, int64_t images, int32_t h, int32_t w,
+                                 int32_t channels, float* dst, void* stream) {
+  if (images < 0 || h < 1 || w < 1 || channels < 1 || src == nullptr || dst == nullptr)
+    return DR_ERR_INVALID_ARGUMENT;
+  const long long total = images * ((h + 1) / 2) * static_cast<long long>((w + 1) / 2) * channels;
+  if (total == 0) return DR_OK;
+  mip_down_kernel<<<blocks_for(total, 256), 256, 0, as_stream(stream)>>>(src, images, h, w,
+                                                                          channels, dst);
+  return launch_status();
+}
+
+extern "C" int dr_mip_downsample_bwd(const float* grad_dst, int64_t images, int32_t h, int32_t w,
+                                     int32_t channels, float* grad_src, void* stream) {
+  if (images < 0 || h < 1 || w < 1 || channels < 1 || grad_dst == nullptr || grad_src == nullptr)
+    return DR_ERR_INVALID_ARGUMENT;
+  const long long total = images * h * static_cast<long long>(w) * channels;
+  if (total == 0) return DR_OK;
+  mip_down_bwd_kernel<<<blocks_for(total, 256), 256, 0, as_stream(stream)>>>(grad_dst, images, h,
+                                                                              w, channels, grad_src);
+  return launch_status();
+}

@@ -1,0 +1,191 @@
+/*
+ * diffrast_b200: C ABI of the B200 (sm_100a) kernels behind the diffrast render path
+ * (rasterize -> interpolate -> texture -> antialias, forward and backward).
+ *
+ * Conventions
+ *   - Every function returns an int status: 0 on success, a cudaError_t value (1..999) when a
+ *     CUDA call or launch failed, or one of the DR_ERR_* codes below. dr_status_string() names it.
+ *   - Tensor pointers are DEVICE pointers to contiguous row-major float32 / int32 / int64 data,
+ *     16-byte aligned where a row has 4 floats (pos, rast, rast_db). Sizes are element counts.
+ *   - Optional inputs are NULL when absent. Work is enqueued on `stream` (a cudaStream_t; NULL is
+ *     the legacy default stream) and is asynchronous unless a function says otherwise.
+ *   - The library allocates nothing: scratch memory is passed in as `workspace`, sized by the
+ *     matching *_workspace_bytes() query.
+ *   - Outputs are fully written (no need to clear them) unless a function says it accumulates.
+ *
+ * Citations name the reference project's files (paths under src/diffrast/ of sennecools/diffrast)
+ * whose behaviour each entry point reproduces.
+ */
+#ifndef DIFFRAST_B200_H
+#define DIFFRAST_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DR_OK 0
+#define DR_ERR_INVALID_ARGUMENT 10001
+#define DR_ERR_WORKSPACE_TOO_SMALL 10002
+#define DR_ERR_TOO_LARGE 10003
+
+/* Filter modes (ops.py:22 FilterMode, without "auto", which the host resolves). */
+#define DR_FILTER_NEAREST 0
+#define DR_FILTER_LINEAR 1
+#define DR_FILTER_LINEAR_MIPMAP_NEAREST 2
+#define DR_FILTER_LINEAR_MIPMAP_LINEAR 3
+/* Boundary modes (ops.py:23 BoundaryMode). */
+#define DR_BOUNDARY_WRAP 0
+#define DR_BOUNDARY_CLAMP 1
+#define DR_BOUNDARY_ZERO 2
+#define DR_BOUNDARY_CUBE 3
+/* Most mip levels a lookup may use (a 2**31-texel-wide texture has 32). */
+#define DR_MAX_LEVELS 32
+
+int dr_version(void);
+const char* dr_status_string(int status);
+
+/* ---------------------------------------------------------------------------------------------
+ * Rasterize: visibility (three stages) and resolve.
+ * Replaces the visibility pass of backends/triton.py:21-40 (rasterize_layer) and
+ * backends/_triton_rasterize.py:295-307 (visible_keys); the result is the reference's
+ * backends/reference.py:368-397 (_visible_triangles) exactly, as packed 64-bit keys
+ * ((order-preserving depth bits << 32) | triangle, INT64_MAX where empty).
+ *
+ * pos [batch, num_vert, 4], tri [num_tri, 3], keys [batch, height, width],
+ * prev_keys: keys of the previous depth layer (DepthPeeler, peeling.py:68-92) or NULL.
+ * batch * num_tri must be below 2**31; height and width below 2**20.
+ * ------------------------------------------------------------------------------------------- */
+
+/* Scratch of stage 1 for up to `capacity` triangles that need tile binning. */
+size_t dr_raster_setup_workspace_bytes(int64_t capacity);
+
+/* Stage 1: fills `keys` (EMPTY, or the previous layer is excluded), culls, writes the keys of
+ * triangles whose pixel box fits in 4x4 directly, and lists the others for binning. If more than
+ * `capacity` triangles need binning the list is incomplete: dr_raster_counts() reports how many,
+ * and the caller reruns this stage with a larger workspace (the direct writes are idempotent). */
+int dr_raster_setup(const float* pos, const int32_t* tri, int64_t batch, int64_t num_vert,
+                    int64_t num_tri, int32_t height, int32_t width, const int64_t* prev_keys,
+                    int64_t* keys, void* workspace, size_t workspace_bytes, int64_t capacity,
+                    void* stream);
+
+/* Reads the two counters of stage 1: triangles to bin and (triangle, tile) pairs. Synchronises
+ * `stream`. */
+int dr_raster_counts(const void* setup_workspace, int64_t* num_binned, int64_t* num_pairs,
+                     void* stream);
+
+size_t dr_raster_bin_workspace_bytes(int64_t batch, int32_t height, int32_t width,
+                                     int64_t num_pairs);
+
+/* Stage 2: bins the listed triangles into 16x16 screen tiles and rasterizes each tile's list with
+ * the list staged in shared memory, merging into `keys` with 64-bit atomic minima. */
+int dr_raster_tiles(const float* pos, const int32_t* tri, int64_t batch, int64_t num_vert,
+                    int64_t num_tri, int32_t height, int32_t width, const int64_t* prev_keys,
+                    int64_t* keys, const void* setup_workspace, int64_t num_binned,
+                    int64_t num_pairs, void* bin_workspace, size_t bin_workspace_bytes,
+                    void* stream);
+
+/* rast [batch, h, w, 4] = (u, v, z/w, id + 1) and rast_db [.., 4] = (du/dx, du/dy, dv/dx, dv/dy),
+ * zeros where empty (reference.py:69-114; _triton_resolve.py:84-116). rast_db may be NULL. */
+int dr_raster_resolve_fwd(const float* pos, const int32_t* tri, const int64_t* keys,
+                          int64_t batch, int64_t num_vert, int64_t num_tri, int32_t height,
+                          int32_t width, float* rast, float* rast_db, void* stream);
+
+/* Gradient of rast (and rast_db unless grad_db is NULL) with respect to pos, ACCUMULATED into
+ * grad_pos [batch, num_vert, 4] (clear it first) (_triton_resolve.py:156-284). */
+int dr_raster_resolve_bwd(const float* pos, const int32_t* tri, const int64_t* keys,
+                          int64_t batch, int64_t num_vert, int64_t num_tri, int32_t height,
+                          int32_t width, const float* grad_rast, const float* grad_db,
+                          float* grad_pos, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Interpolate (reference.py:117-146; _triton_interpolate.py:38-254).
+ * attr [attr_batch, num_vert, channels] with attr_batch 1 (shared) or batch; rast, rast_db
+ * [batch, h, w, 4]; diff: DEVICE int32 [num_diff] channel indices (NULL when num_diff is 0);
+ * out [batch, h, w, channels]; out_da [batch, h, w, 2 * num_diff]. Ids past num_tri are empty.
+ * ------------------------------------------------------------------------------------------- */
+int dr_interpolate_fwd(const float* attr, int64_t attr_batch, int64_t num_vert, int32_t channels,
+                       const float* rast, const float* rast_db, const int32_t* tri,
+                       int64_t num_tri, const int32_t* diff, int32_t num_diff, int64_t batch,
+                       int32_t height, int32_t width, float* out, float* out_da, void* stream);
+
+/* grad_attr (NULL to skip) is ACCUMULATED (clear it first); grad_rast is written; grad_db is
+ * written when grad_out_da is given and ignored otherwise (may be NULL). */
+int dr_interpolate_bwd(const float* attr, int64_t attr_batch, int64_t num_vert, int32_t channels,
+                       const float* rast, const float* rast_db, const int32_t* tri,
+                       int64_t num_tri, const int32_t* diff, int32_t num_diff, int64_t batch,
+                       int32_t height, int32_t width, const float* grad_out,
+                       const float* grad_out_da, float* grad_attr, float* grad_rast,
+                       float* grad_db, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Texture (reference.py:149-194, :491-672; _cube.py:44-143; _triton_texture.py:37-549).
+ * Level l has `level_ptr[l]` -> [tex_batch(, 6), level_h[l], level_w[l], channels]; its batch
+ * stride in elements is `level_batch_stride[l]` (0 when that level is shared by all views).
+ * These four arrays are HOST arrays of `num_levels` entries (level 0 is the base texture).
+ * For DR_BOUNDARY_CUBE, uv holds directions [batch, h, w, 3] and uv_da [batch, h, w, 6].
+ * tex_batch_is_one: the texture is shared by all views (tex batch of 1).
+ * uv_da and bias may be NULL. out [batch, h, w, channels].
+ * ------------------------------------------------------------------------------------------- */
+int dr_texture_fwd(const float* const* level_ptr, const int32_t* level_h, const int32_t* level_w,
+                   const int64_t* level_batch_stride, int32_t num_levels, int32_t channels,
+                   const float* uv, const float* uv_da, const float* bias, int64_t batch,
+                   int32_t height, int32_t width, int32_t filter_mode, int32_t boundary_mode,
+                   float* out, void* stream);
+
+/* Texel gradients are ACCUMULATED into grad_level_ptr[l] (same layout as the levels; clear
+ * them first). grad_uv, grad_uv_da and grad_bias (each NULL to skip) are written. */
+int dr_texture_bwd(const float* const* level_ptr, float* const* grad_level_ptr,
+                   const int32_t* level_h, const int32_t* level_w,
+                   const int64_t* level_batch_stride, int32_t num_levels, int32_t channels,
+                   const float* uv, const float* uv_da, const float* bias, int64_t batch,
+                   int32_t height, int32_t width, int32_t filter_mode, int32_t boundary_mode,
+                   const float* grad_out, float* grad_uv, float* grad_uv_da, float* grad_bias,
+                   void* stream);
+
+/* One mip step (reference.py:449-488): dst [images, (h + 1) / 2, (w + 1) / 2, channels] from
+ * src [images, h, w, channels] by area weights; `images` = tex_batch, or 6 * tex_batch for a cube. */
+int dr_mip_downsample(const float* src, int64_t images, int32_t h, int32_t w, int32_t channels,
+                      float* dst, void* stream);
+
+/* Adjoint of dr_mip_downsample: ACCUMULATES the gradient of dst into grad_src. */
+int dr_mip_downsample_bwd(const float* grad_dst, int64_t images, int32_t h, int32_t w,
+                          int32_t channels, float* grad_src, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Antialias (reference.py:202-265, :675-814; topology.py; _triton_antialias.py).
+ * neighbours [num_tri, 3] int64 from dr_edge_neighbours (reference.py:768-787).
+ * pos [pos_batch, num_vert, 4] with pos_batch 1 (shared across views) or batch.
+ * ------------------------------------------------------------------------------------------- */
+size_t dr_edge_neighbours_workspace_bytes(int64_t num_tri);
+
+/* For edge 3 t + k (opposite vertex k) the other edge over the same vertex pair, or -1 when
+ * none or several share it. Deterministic; needs no sort. */
+int dr_edge_neighbours(const int32_t* tri, int64_t num_tri, int64_t* neighbours, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+/* Silhouette flags [pos_batch, num_tri, 3] as bytes (reference.py:790-814). The antialias
+ * kernels evaluate the same test on the fly for the edges they cross. */
+int dr_silhouette_edges(const float* pos, int64_t pos_batch, int64_t num_vert,
+                        const int32_t* tri, int64_t num_tri, const int64_t* neighbours,
+                        uint8_t* silhouette, void* stream);
+
+int dr_antialias_fwd(const float* color, const float* rast, const float* pos, int64_t pos_batch,
+                     int64_t num_vert, const int32_t* tri, int64_t num_tri,
+                     const int64_t* neighbours, int64_t batch, int32_t height, int32_t width,
+                     int32_t channels, float* out, void* stream);
+
+/* grad_color is written; grad_pos [pos_batch, num_vert, 4] is ACCUMULATED (clear it first). */
+int dr_antialias_bwd(const float* color, const float* rast, const float* pos, int64_t pos_batch,
+                     int64_t num_vert, const int32_t* tri, int64_t num_tri,
+                     const int64_t* neighbours, int64_t batch, int32_t height, int32_t width,
+                     int32_t channels, const float* grad_out, float pos_gradient_boost,
+                     float* grad_color, float* grad_pos, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DIFFRAST_B200_H */

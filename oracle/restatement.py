@@ -308,15 +308,31 @@ def _halving_weights(n: int) -> Tensor:
     return overlap.clamp(min=0).float() / n
 
 
+def _halve_dim(image: Tensor, dim: int) -> Tensor:
+    """One mip step along ``dim``: each coarse texel is a weighted sum of at most three taps.
+
+    The taps and weights are the nonzero entries of :func:`_halving_weights` (gathered, so large
+    textures cost O(texels)).
+    """
+    n = image.shape[dim]
+    if n == 1:
+        return image
+    weights = _halving_weights(n)
+    m = weights.shape[0]
+    first = torch.arange(m) * n // m
+    out = 0
+    for tap in range(3):
+        idx = (first + tap).clamp(max=n - 1)
+        wt = weights[torch.arange(m), idx] * (first + tap < n)
+        shape = [1] * image.ndim
+        shape[dim] = m
+        out = out + wt.view(shape) * image.index_select(dim, idx)
+    return out
+
+
 def _downsample(level: Tensor) -> Tensor:
     """Next mip level of ``[batch, h, w, C]`` as a separable weighted sum."""
-    h, w = level.shape[1:3]
-    out = level
-    if h > 1:
-        out = torch.einsum("jh,bhwc->bjwc", _halving_weights(h), out)
-    if w > 1:
-        out = torch.einsum("kw,bjwc->bjkc", _halving_weights(w), out)
-    return out
+    return _halve_dim(_halve_dim(level, 1), 2)
 
 
 def mip_chain(tex: Tensor, max_mip_level: int | None = None) -> list[Tensor]:

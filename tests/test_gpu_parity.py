@@ -1,0 +1,414 @@
+"""Parity of the CUDA kernels with the reference (golden fixtures) and the CPU oracle.
+
+Tolerances (stated per check): triangle ids, coverage, silhouettes and edge adjacency bit-exact;
+rast / rast_db within 1e-4 relative (floored at 1) of a float64 recomputation, as the reference's
+own backend-parity test does; other forward values rel 1e-4 / abs 1e-5; gradients that are
+accumulated with atomics rel/abs 1e-3 (scaled by the largest gradient where they reach large
+magnitudes).
+"""
+
+import pytest
+import torch
+
+import diffrast_b200 as dr
+import oracle
+import scenes
+from conftest import golden_names, load_golden
+
+pytestmark = pytest.mark.gpu
+CUDA = "cuda"
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    return dr.RasterizeContext(CUDA)
+
+
+def fwd_close(a, b, atol=1e-5, rtol=1e-4):
+    torch.testing.assert_close(a.cpu(), b.cpu(), atol=atol, rtol=rtol, equal_nan=True)
+
+
+def grad_close(a, b, tol=1e-3):
+    scale = max(1.0, b.abs().max().item()) if b.numel() else 1.0
+    torch.testing.assert_close(a.cpu(), b.cpu(), atol=tol * scale, rtol=tol, equal_nan=True)
+
+
+def check_rast_against_float64(pos, tri, rast, rast_db):
+    ids = rast[..., 3].cpu().long() - 1
+    exact, exact_db = oracle.resolve(pos.cpu().double(), tri.cpu(), ids)
+    for ours, truth in ((rast, exact), (rast_db, exact_db)):
+        err = (ours.cpu().double() - truth).abs() / truth.abs().clamp_min(1)
+        assert err.max() < 1e-4, err.max()
+
+
+# ---------------------------------------------------------------------------------------------
+# rasterize
+# ---------------------------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("name", golden_names("raster_"))
+def test_rasterize_matches_golden(ctx, name):
+    g = load_golden(name)
+    res = tuple(g["resolution"].tolist())
+    pos, tri = g["pos"].cuda(), g["tri"].cuda()
+    p = pos.clone().requires_grad_(True)
+    rast, rast_db = dr.rasterize(ctx, p, tri, res)
+    assert torch.equal(rast[..., 3].cpu(), g["rast"][..., 3]), "triangle ids must be bit-exact"
+    check_rast_against_float64(pos, tri, rast.detach(), rast_db.detach())
+    w_rast, w_db = g["w_rast"].cuda(), g["w_db"].cuda()
+    ((rast[..., :3] * w_rast[..., :3]).sum() + (rast_db * w_db).sum()).backward()
+    grad_close(p.grad, g["grad_pos"])
+    with dr.DepthPeeler(ctx, pos, tri, res) as peeler:
+        for k in range(g["layer_ids"].shape[0]):
+            r, _ = peeler.rasterize_next_layer()
+            assert torch.equal(r[..., 3].cpu(), g["layer_ids"][k]), f"layer {k}"
+
+
+SCENES = {
+    "random": lambda: scenes.random_mesh(200, torch.Generator().manual_seed(0), batch=2),
+    "crossing_camera": lambda: scenes.random_mesh(60, torch.Generator().manual_seed(2), w_range=(-1.0, 2.0)),
+    "clip_and_cull": lambda: scenes.random_mesh(100, torch.Generator().manual_seed(3), z_range=2.0, xy_range=3.0),
+    "tiny": lambda: scenes.tiny_mesh(3000, torch.Generator().manual_seed(6), 0.03, batch=2),
+    "grid": lambda: scenes.grid_mesh(20, torch.Generator().manual_seed(7), batch=3),
+}
+
+
+@pytest.mark.parametrize("scene", sorted(SCENES))
+@pytest.mark.parametrize("res", [(16, 16), (37, 61), (128, 96)])
+def test_rasterize_ids_match_oracle(ctx, scene, res):
+    pos, tri = SCENES[scene]()
+    rast, rast_db = dr.rasterize(ctx, pos.cuda(), tri.cuda(), res)
+    ref, _ = oracle.rasterize(pos, tri, res)
+    assert torch.equal(rast[..., 3].cpu(), ref[..., 3])
+    check_rast_against_float64(pos, tri, rast, rast_db)
+
+
+def test_rasterize_many_overlapping_large_triangles(ctx):
+    # Large overlapping triangles take the binned tile path; many per tile span several work items.
+    pos, tri = scenes.random_mesh(600, torch.Generator().manual_seed(4), xy_range=0.9)
+    for res in ((16, 16), (200, 180)):
+        rast, _ = dr.rasterize(ctx, pos.cuda(), tri.cuda(), res)
+        ref, _ = oracle.rasterize(pos, tri, res)
+        assert torch.equal(rast[..., 3].cpu(), ref[..., 3])
+
+
+def test_peeling_every_layer_matches_oracle(ctx):
+    gen = torch.Generator().manual_seed(9)
+    xy = torch.rand(2, 900, 2, generator=gen) * 3 - 1.5
+    z = torch.rand(2, 900, 1, generator=gen) * 2.4 - 1.2
+    w = torch.rand(2, 900, 1, generator=gen) * 3 - 1.0
+    pos = torch.cat([xy * w, z * w, w], -1)
+    tri = torch.arange(900, dtype=torch.int32).view(300, 3)
+    for res in ((64, 64), (37, 61)):
+        state = None
+        with dr.DepthPeeler(ctx, pos.cuda(), tri.cuda(), res) as peeler:
+            for layer in range(4):
+                rast, _ = peeler.rasterize_next_layer()
+                ref, _, state = oracle.rasterize_layer(pos, tri, res, True, state)
+                assert torch.equal(rast[..., 3].cpu(), ref[..., 3]), f"layer {layer}"
+
+
+def test_equal_depth_resolves_to_lower_id(ctx):
+    quad = [[-1.0, -1.0, 0.25, 1.0], [1.0, -1.0, 0.25, 1.0], [0.0, 1.0, 0.25, 1.0]]
+    pos = torch.tensor([quad * 3], device=CUDA)
+    tri = torch.tensor([[6, 7, 8], [0, 1, 2], [3, 4, 5]], dtype=torch.int32, device=CUDA)
+    rast, _ = dr.rasterize(ctx, pos, tri, (16, 16))
+    covered = rast[..., 3] > 0
+    assert covered.any() and (rast[..., 3][covered] == 1).all()
+
+
+def test_negative_and_zero_depth_ordering(ctx):
+    def flat(z):
+        return [[-1.0, -1.0, z, 1.0], [3.0, -1.0, z, 1.0], [-1.0, 3.0, z, 1.0]]
+
+    pos = torch.tensor([flat(0.5) + flat(-0.0) + flat(-0.5) + flat(0.0)], device=CUDA)
+    tri = torch.arange(12, dtype=torch.int32, device=CUDA).view(4, 3)
+    rast, _ = dr.rasterize(ctx, pos, tri, (8, 8))
+    assert (rast[..., 3] == 3).all()
+
+
+def test_empty_culled_and_non_finite(ctx):
+    pos = torch.tensor([[[-0.5, -0.5, 0.0, -1.0], [0.5, -0.5, 0.0, -1.0], [0.0, 0.5, 0.0, -1.0]]], device=CUDA)
+    tri = torch.tensor([[0, 1, 2]], dtype=torch.int32, device=CUDA)
+    for t in (tri, tri[:0]):
+        rast, rast_db = dr.rasterize(ctx, pos, t, (16, 16))
+        assert (rast == 0).all() and (rast_db == 0).all()
+    for value in (float("nan"), float("inf")):
+        broken = torch.tensor([[[-0.5, -0.5, 0.0, 1.0], [0.5, -0.5, 0.0, 1.0], [0.0, 0.5, value, 1.0]]], device=CUDA)
+        rast, rast_db = dr.rasterize(ctx, broken, tri, (16, 16))
+        assert (rast == 0).all() and torch.isfinite(rast_db).all()
+    zero = torch.zeros(0, 3, 4, device=CUDA)
+    rast, rast_db = dr.rasterize(ctx, zero, tri, (6, 8))
+    assert rast.shape == rast_db.shape == (0, 6, 8, 4)
+
+
+def test_area_tolerance_boundary(ctx):
+    # The pixel-(8, 8) centre lies inside a sliver whose area there is 2 * steps / 17 epsilons of
+    # its terms: 16 steps is below the two-epsilon tolerance (not drawn), 18 above (drawn).
+    eps = torch.finfo(torch.float32).eps
+    for steps, drawn in ((4, False), (16, False), (18, True), (64, True)):
+        half = 0.5
+        centre_x = (8 * 2 + 1) / 16 - 1
+        centre_y = (8 * 2 + 1) / 16 - 1
+        height = steps * eps * (1 + abs(centre_y)) / 17
+        xy = torch.tensor([[centre_x - half, centre_y - height], [centre_x + half, centre_y - height],
+                           [centre_x, centre_y + height]], dtype=torch.float64)
+        pos = torch.cat([xy.float(), torch.zeros(3, 1), torch.ones(3, 1)], -1)[None]
+        tri = torch.tensor([[0, 1, 2]], dtype=torch.int32)
+        rast, _ = dr.rasterize(ctx, pos.cuda(), tri.cuda(), (16, 16))
+        ref, _ = oracle.rasterize(pos, tri, (16, 16))
+        assert torch.equal(rast[..., 3].cpu(), ref[..., 3])
+
+
+def test_range_mode_matches_instanced_slices(ctx):
+    pos, tri = scenes.random_mesh(40, torch.Generator().manual_seed(11))
+    ranges = torch.tensor([[0, 10], [5, 20], [30, 10]], dtype=torch.int32)
+    rast, _ = dr.rasterize(ctx, pos[0].cuda(), tri.cuda(), (32, 32), ranges=ranges)
+    for item, (start, count) in enumerate(ranges.tolist()):
+        ref, _ = oracle.rasterize(pos, tri[start : start + count], (32, 32))
+        ids = ref[0, ..., 3]
+        expected = torch.where(ids > 0, ids + start, ids)
+        assert torch.equal(rast[item, ..., 3].cpu(), expected)
+
+
+def test_rasterize_gradients_match_oracle_random(ctx):
+    pos, tri = scenes.random_mesh(80, torch.Generator().manual_seed(1), batch=2, w_range=(-1.0, 2.0))
+    gen = torch.Generator().manual_seed(0)
+    w_rast = torch.randn(2, 40, 56, 4, generator=gen)
+    w_db = torch.randn(2, 40, 56, 4, generator=gen)
+    for grad_db in (True, False):
+        grads = []
+        for device in ("cpu", CUDA):
+            p = pos.to(device).clone().requires_grad_(True)
+            if device == "cpu":
+                rast, rast_db = oracle.rasterize(p, tri, (40, 56), grad_db)
+            else:
+                rast, rast_db = dr.rasterize(ctx, p, tri.cuda(), (40, 56), grad_db=grad_db)
+            loss = (rast[..., :3] * w_rast[..., :3].to(device)).sum()
+            if rast_db.requires_grad:
+                loss = loss + (rast_db * w_db.to(device)).sum()
+            loss.backward()
+            grads.append(p.grad.cpu())
+        grad_close(grads[1], grads[0])
+
+
+# ---------------------------------------------------------------------------------------------
+# interpolate
+# ---------------------------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("name", golden_names("interp_"))
+def test_interpolate_matches_golden(name):
+    g = load_golden(name)
+    diff = g["diff"].long().tolist()
+    a, r, d = (g[k].cuda().clone().requires_grad_(True) for k in ("attr", "rast", "rast_db"))
+    out, out_da = dr.interpolate(a, r, g["tri"].cuda(), rast_db=d, diff_attrs=diff or None)
+    fwd_close(out, g["out"])
+    fwd_close(out_da, g["out_da"])
+    ((out * g["g_out"].cuda()).sum() + (out_da * g["g_da"].cuda()).sum()).backward()
+    grad_close(a.grad, g["grad_attr"])
+    grad_close(r.grad, g["grad_rast"], 1e-4)
+    grad_close(d.grad if d.grad is not None else torch.zeros_like(d), g["grad_db"], 1e-4)
+
+
+def test_interpolate_ids_past_end_are_background():
+    rast = torch.zeros(1, 2, 2, 4)
+    rast[0, 0, 0] = torch.tensor([0.2, 0.3, 0.0, 1.0])
+    rast[0, 0, 1] = torch.tensor([0.2, 0.3, 0.0, 5.0])
+    attr = torch.randn(3, 2)
+    tri = torch.tensor([[0, 1, 2]], dtype=torch.int32)
+    out, _ = dr.interpolate(attr.cuda(), rast.cuda(), tri.cuda())
+    ref, _ = oracle.interpolate(attr, rast, tri)
+    fwd_close(out, ref)
+    assert (out[0, 0, 1] == 0).all()
+
+
+# ---------------------------------------------------------------------------------------------
+# texture
+# ---------------------------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("name", [n for n in golden_names("tex2d_") if "edge" not in n and "maxmip" not in n])
+def test_texture_matches_golden(name):
+    g = load_golden(name)
+    boundary, mode = name.split("_")[1], name.split("_")[2]
+    mip = "mipmap" in mode
+    use_bias = bool(g["use_bias"].item())
+    t, c, d, bb = (g[k].cuda().clone().requires_grad_(True) for k in ("tex", "uv", "uv_da", "bias"))
+    out = dr.texture(t, c, d if mip else None, mip_level_bias=bb if use_bias else None,
+                     filter_mode=mode, boundary_mode=boundary)
+    fwd_close(out, g["out"], atol=2e-5, rtol=2e-5)
+    (out.nan_to_num(0) * g["weights"].cuda()).sum().backward()
+    for x, key in ((t, "grad_tex"), (c, "grad_uv"), (d, "grad_uv_da"), (bb, "grad_bias")):
+        grad = x.grad if x.grad is not None else torch.zeros_like(x)
+        grad_close(grad, g[key])
+
+
+@pytest.mark.parametrize("boundary", ["wrap", "clamp", "zero"])
+def test_texture_non_finite_inputs_match_golden(boundary):
+    g = load_golden(f"tex2d_edge_{boundary}")
+    out = dr.texture(g["tex"].cuda(), g["uv"].cuda(), g["uv_da"].cuda(),
+                     filter_mode="linear-mipmap-linear", boundary_mode=boundary)
+    fwd_close(out, g["out"], atol=2e-5, rtol=2e-5)
+
+
+@pytest.mark.parametrize("level", [0, 2])
+def test_texture_max_mip_level_matches_golden(level):
+    g = load_golden(f"tex2d_maxmip{level}")
+    out = dr.texture(g["tex"].cuda(), g["uv"].cuda(), g["uv_da"].cuda(), max_mip_level=level)
+    fwd_close(out, g["out"], atol=2e-5, rtol=2e-5)
+    stack = dr.texture_construct_mip(g["tex"].cuda())
+    out2 = dr.texture(g["tex"].cuda(), g["uv"].cuda(), g["uv_da"].cuda(), mip=stack, max_mip_level=level)
+    fwd_close(out2, g["out"], atol=2e-5, rtol=2e-5)
+
+
+@pytest.mark.parametrize("name", golden_names("mip_"))
+def test_mip_chain_matches_golden(name):
+    g = load_golden(name)
+    stack = dr.texture_construct_mip(g["tex"].cuda())
+    fwd_close(torch.cat([lv.reshape(-1) for lv in stack.levels]), g["levels"])
+
+
+def test_mip_chain_gradient_matches_oracle():
+    gen = torch.Generator().manual_seed(3)
+    for h, w in ((37, 50), (16, 9), (1, 7), (64, 64)):
+        tex = torch.randn(2, h, w, 3, generator=gen)
+        weights = [torch.randn_like(lv) for lv in oracle.mip_chain(tex)[1:]]
+        grads = []
+        for device in ("cpu", CUDA):
+            t = tex.to(device).clone().requires_grad_(True)
+            levels = oracle.mip_chain(t)[1:] if device == "cpu" else dr.texture_construct_mip(t).levels
+            sum((lv * wt.to(device)).sum() for lv, wt in zip(levels, weights)).backward()
+            grads.append(t.grad.cpu())
+        grad_close(grads[1], grads[0], 1e-4)
+
+
+@pytest.mark.parametrize("name", golden_names("cube_"))
+def test_cube_texture_matches_golden(name):
+    g = load_golden(name)
+    mode = name[len("cube_"):]
+    mip = "mipmap" in mode
+    t, d, dd = (g[k].cuda().clone().requires_grad_(True) for k in ("tex", "dirs", "dirs_da"))
+    out = dr.texture(t, d, dd if mip else None, filter_mode=mode, boundary_mode="cube")
+    fwd_close(out, g["out"], atol=2e-5, rtol=2e-5)
+    (out * g["weights"].cuda()).sum().backward()
+    for x, key in ((t, "grad_tex"), (d, "grad_dirs"), (dd, "grad_dirs_da")):
+        grad = x.grad if x.grad is not None else torch.zeros_like(x)
+        grad_close(grad, g[key])
+
+
+def test_texture_shared_texels_gradients_match_oracle():
+    gen = torch.Generator().manual_seed(5)
+    tex = torch.randn(2, 37, 50, 3, generator=gen)
+    uv_da = (torch.rand(2, 20, 24, 4, generator=gen) * 0.2 - 0.1)
+    base_uv = torch.rand(2, 20, 24, 2, generator=gen) * 1.6 - 0.3
+    for pattern in ("constant", "magnified", "mixed"):
+        uv = base_uv.clone()
+        if pattern == "constant":
+            uv = torch.full_like(uv, 0.3)
+        elif pattern == "magnified":
+            uv = uv / 16 + 0.4
+        else:
+            uv[:, ::2] = 0.0
+        for mode in ("nearest", "linear", "linear-mipmap-nearest", "linear-mipmap-linear"):
+            mip = "mipmap" in mode
+            grads = []
+            for device in ("cpu", CUDA):
+                t = tex.to(device).clone().requires_grad_(True)
+                if device == "cpu":
+                    out = oracle.texture(t, uv, uv_da if mip else None, None, None, mode, "clamp")
+                else:
+                    out = dr.texture(t, uv.cuda(), uv_da.cuda() if mip else None, filter_mode=mode, boundary_mode="clamp")
+                out.sum().backward()
+                grads.append(t.grad.cpu())
+            grad_close(grads[1], grads[0])
+
+
+# ---------------------------------------------------------------------------------------------
+# antialias
+# ---------------------------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("name", golden_names("aa_"))
+def test_antialias_matches_golden(name):
+    g = load_golden(name)
+    tri = g["tri"].cuda()
+    nb = dr.antialias_construct_topology_hash(tri).neighbours(tri)
+    assert torch.equal(nb.cpu(), g["neighbours"]), "edge adjacency must be bit-exact"
+    from diffrast_b200 import _kernels as K
+
+    pos3 = g["pos"].cuda() if g["pos"].ndim == 3 else g["pos"].cuda()[None]
+    assert torch.equal(K.silhouette_edges(pos3, tri, nb).cpu(), g["silhouette"]), "silhouettes"
+    c = g["color"].cuda().clone().requires_grad_(True)
+    p = g["pos"].cuda().clone().requires_grad_(True)
+    out = dr.antialias(c, g["rast"].cuda(), p, tri, pos_gradient_boost=float(g["boost"]))
+    fwd_close(out, g["out"])
+    (out * g["weights"].cuda()).sum().backward()
+    grad_close(c.grad, g["grad_color"], 1e-5)
+    grad_close(p.grad, g["grad_pos"])
+
+
+def test_antialias_edge_set_matches_oracle_random():
+    for seed, mesh in ((0, {}), (1, {"w_range": (-1.0, 2.0)}), (2, {"z_range": 2.0, "xy_range": 3.0})):
+        pos, tri = scenes.random_mesh(60, torch.Generator().manual_seed(seed), batch=2, **mesh)
+        rast, _ = oracle.rasterize(pos, tri, (48, 64))
+        color = torch.rand(2, 48, 64, 3, generator=torch.Generator().manual_seed(seed + 10))
+        ref = oracle.antialias(color, rast, pos, tri)
+        out = dr.antialias(color.cuda(), rast.cuda(), pos.cuda(), tri.cuda())
+        # Same set of blended pixels, same values.
+        assert torch.equal((out.cpu() != color), (ref != color))
+        fwd_close(out, ref)
+
+
+def test_straight_edge_coverage_is_exact(ctx):
+    edge = 0.3
+    pos = torch.tensor([[[-2.0, -2.0, 0.0, 1.0], [edge, -2.0, 0.0, 1.0], [edge, 2.0, 0.0, 1.0],
+                         [-2.0, 2.0, 0.0, 1.0]]], device=CUDA)
+    tri = torch.tensor([[0, 1, 2], [0, 2, 3]], dtype=torch.int32, device=CUDA)
+    rast, _ = dr.rasterize(ctx, pos, tri, (16, 24))
+    out = dr.antialias((rast[..., 3:] > 0).float(), rast, pos, tri)
+    torch.testing.assert_close(out.sum().cpu(), torch.tensor(16 * (edge + 1) * 24 / 2))
+
+
+def test_edge_neighbours_match_golden():
+    g = load_golden("topology")
+    for key, nkey in (("tri", "neighbours"), ("tri_fan", "neighbours_fan")):
+        tri = g[key].cuda()
+        nb = dr.antialias_construct_topology_hash(tri).neighbours(tri)
+        assert torch.equal(nb.cpu(), g[nkey])
+
+
+# ---------------------------------------------------------------------------------------------
+# full pipeline
+# ---------------------------------------------------------------------------------------------
+
+
+def test_config1_pipeline_matches_oracle(ctx):
+    sc = scenes.config1_scene(seed=0)
+    res = (64, 64)
+    tex_small = sc["tex"][:, :64, :64].contiguous()
+    target = torch.rand(1, 64, 64, 3, generator=torch.Generator().manual_seed(1))
+
+    def run(device):
+        pos = sc["pos"].to(device).clone().requires_grad_(True)
+        tex = tex_small.to(device).clone().requires_grad_(True)
+        tri, uv = sc["tri"].to(device), sc["uv"].to(device)
+        if device == "cpu":
+            rast, rast_db = oracle.rasterize(pos, tri, res)
+            uvp, uv_da = oracle.interpolate(uv, rast, tri, rast_db, [0, 1])
+            color = oracle.texture(tex, uvp, uv_da, None, None, "linear-mipmap-linear", "wrap")
+            out = oracle.antialias(color, rast, pos, tri)
+        else:
+            rast, rast_db = dr.rasterize(ctx, pos, tri, res)
+            uvp, uv_da = dr.interpolate(uv, rast, tri, rast_db=rast_db, diff_attrs="all")
+            color = dr.texture(tex, uvp, uv_da, filter_mode="linear-mipmap-linear")
+            out = dr.antialias(color, rast, pos, tri)
+        loss = ((out - target.to(device)) ** 2).mean()
+        loss.backward()
+        return out.detach().cpu(), loss.item(), pos.grad.cpu(), tex.grad.cpu()
+
+    ref, ours = run("cpu"), run(CUDA)
+    fwd_close(ours[0], ref[0], atol=1e-4, rtol=1e-3)
+    assert abs(ours[1] - ref[1]) < 1e-5
+    grad_close(ours[2], ref[2], 2e-3)
+    grad_close(ours[3], ref[3], 1e-3)
