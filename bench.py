@@ -244,7 +244,7 @@ def run_ours(args) -> None:
     def e2e_step():
         pos_e2e.copy_(pos_host, non_blocking=True)
         target_e2e.copy_(target_host, non_blocking=True)
-        leaf = pos_e2e.requires_grad_(True)
+        leaf = pos_e2e.detach().requires_grad_(True)
         loss = step(leaf, target_e2e)
         loss.item()
 

@@ -29,8 +29,11 @@ constexpr float kLimit = 1e18f;
 constexpr int kTile = 16;
 // Triangles per tile work item (one per thread of a 16x16 tile block).
 constexpr int kChunk = 256;
-// Triangles whose pixel box fits in kSmall x kSmall are rasterized directly by the setup pass.
-constexpr int kSmall = 4;
+// Triangles whose pixel box holds at most kThreadPixels pixels are rasterized by their own setup
+// thread; up to kWarpPixels by the 32 lanes of the setup warp together; larger ones are binned
+// into screen tiles.
+constexpr int kThreadPixels = 4;
+constexpr int kWarpPixels = 512;
 
 __device__ __forceinline__ float mul(float a, float b) { return __fmul_rn(a, b); }
 __device__ __forceinline__ float add(float a, float b) { return __fadd_rn(a, b); }

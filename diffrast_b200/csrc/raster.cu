@@ -1,10 +1,10 @@
 // Rasterization on B200: visibility as packed 64-bit depth|triangle keys, then resolve.
 //
 // Visibility (result identical to diffrast's reference, backends/reference.py:368-397):
-//   1. setup_kernel, one thread per (view, triangle): culls, bounds the triangle in pixels, and
-//      rasterizes it directly when its box fits in kSmall x kSmall pixels (most triangles of dense
-//      meshes), merging keys with 64-bit atomicMin. Other triangles are appended (warp-aggregated)
-//      to a list with their 16x16-tile box.
+//   1. setup_kernel, one thread per (view, triangle): culls and bounds the triangle in pixels.
+//      A box of at most kThreadPixels pixels is rasterized by the thread itself, one of at most
+//      kWarpPixels by the whole warp (lanes sweep the box, one triangle after another); keys are
+//      merged with 64-bit atomicMin. Larger triangles are appended (warp-aggregated) to a list.
 //   2. Device-side binning without host round trips beyond one counter read: per-tile counts,
 //      one exclusive scan (pair offsets and 256-triangle work items), and a scatter into per-tile
 //      triangle lists.
@@ -22,11 +22,11 @@
 namespace dr {
 namespace {
 
-// One triangle that needs tile binning: flat view * num_tri + triangle, and its tile box packed as
-// (tx0 | tx1 << 16, ty0 | ty1 << 16). The record layout does not depend on the list capacity.
+// One triangle that needs tile binning: flat view * num_tri + triangle, and its inclusive pixel
+// box. The record layout does not depend on the list capacity.
 struct Binned {
   int g;
-  unsigned bx, by;
+  int c0, c1, r0, r1;
 };
 
 struct SetupLayout {
@@ -99,24 +99,37 @@ __device__ __forceinline__ void pixel_range(float lo, float hi, int size, int& f
   last = static_cast<int>(l);
 }
 
+__device__ __forceinline__ void raster_pixel(const Vert& v0, const Vert& v1, const Vert& v2, int t,
+                                             int b, int r, int c, int height, int width,
+                                             const long long* __restrict__ prev,
+                                             long long* __restrict__ keys) {
+  const long long key = coverage_key(v0, v1, v2, pixel_centre(c, width), pixel_centre(r, height), t);
+  if (key == kEmptyKey) return;
+  const long long off = (static_cast<long long>(b) * height + r) * width + c;
+  if (prev != nullptr && !(key > __ldg(prev + off))) return;
+  atomicMin(keys + off, key);
+}
+
 __global__ void __launch_bounds__(256) setup_kernel(
     const float* __restrict__ pos, const int* __restrict__ tri, int num_vert, int num_tri,
     long long total, int height, int width, const long long* __restrict__ prev,
     long long* __restrict__ keys, unsigned long long* __restrict__ counters,
     Binned* __restrict__ binned, long long capacity) {
   const long long g = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
-  bool large = false;
+  bool large = false, medium = false;
   unsigned pairs = 0;
-  uint2 tile_box = make_uint2(0, 0);
+  int b = 0, t = 0, c0 = 0, c1 = -1, r0 = 0, r1 = -1;
+  Vert v0 = {0.f, 0.f, 0.f, 1.f}, v1 = v0, v2 = v0;
   if (g < total) {
-    const int b = static_cast<int>(g / num_tri);
-    const int t = static_cast<int>(g - static_cast<long long>(b) * num_tri);
+    b = static_cast<int>(g / num_tri);
+    t = static_cast<int>(g - static_cast<long long>(b) * num_tri);
     const int i0 = __ldg(tri + 3 * static_cast<long long>(t));
     const int i1 = __ldg(tri + 3 * static_cast<long long>(t) + 1);
     const int i2 = __ldg(tri + 3 * static_cast<long long>(t) + 2);
     const long long base = static_cast<long long>(b) * num_vert;
-    const Vert v0 = load_vert(pos, base + i0), v1 = load_vert(pos, base + i1),
-               v2 = load_vert(pos, base + i2);
+    v0 = load_vert(pos, base + i0);
+    v1 = load_vert(pos, base + i1);
+    v2 = load_vert(pos, base + i2);
     // A triangle is invisible when all vertices are behind the camera or outside the same side
     // plane; every covered point is a non-negative combination of the vertices. Non-finite
     // vertices are never drawn (reference.py:334).
@@ -128,7 +141,10 @@ __global__ void __launch_bounds__(256) setup_kernel(
     culled |= (v0.y < -v0.w) && (v1.y < -v1.w) && (v2.y < -v2.w);
     if (!culled) {
       const bool in_front = (v0.w > 0.0f) && (v1.w > 0.0f) && (v2.w > 0.0f);
-      int c0 = 0, c1 = width - 1, r0 = 0, r1 = height - 1;
+      c0 = 0;
+      c1 = width - 1;
+      r0 = 0;
+      r1 = height - 1;
       if (in_front) {
         const float nx0 = v0.x / v0.w, nx1 = v1.x / v1.w, nx2 = v2.x / v2.w;
         const float ny0 = v0.y / v0.w, ny1 = v1.y / v1.w, ny2 = v2.y / v2.w;
@@ -136,29 +152,40 @@ __global__ void __launch_bounds__(256) setup_kernel(
         pixel_range(fminf(fminf(ny0, ny1), ny2), fmaxf(fmaxf(ny0, ny1), ny2), height, r0, r1);
       }
       if (c0 <= c1 && r0 <= r1) {
-        if (in_front && c1 - c0 < kSmall && r1 - r0 < kSmall) {
-          for (int r = r0; r <= r1; ++r) {
-            const float py = pixel_centre(r, height);
-            for (int c = c0; c <= c1; ++c) {
-              const float px = pixel_centre(c, width);
-              const long long key = coverage_key(v0, v1, v2, px, py, t);
-              if (key == kEmptyKey) continue;
-              const long long off = (static_cast<long long>(b) * height + r) * width + c;
-              if (prev != nullptr && !(key > __ldg(prev + off))) continue;
-              atomicMin(keys + off, key);
-            }
-          }
+        const long long area = static_cast<long long>(c1 - c0 + 1) * (r1 - r0 + 1);
+        if (in_front && area <= kThreadPixels) {
+          for (int r = r0; r <= r1; ++r)
+            for (int c = c0; c <= c1; ++c) raster_pixel(v0, v1, v2, t, b, r, c, height, width, prev, keys);
+        } else if (in_front && area <= kWarpPixels) {
+          medium = true;
         } else {
           large = true;
           const unsigned tx0 = c0 / kTile, tx1 = c1 / kTile, ty0 = r0 / kTile, ty1 = r1 / kTile;
           pairs = (tx1 - tx0 + 1) * (ty1 - ty0 + 1);
-          tile_box = make_uint2(tx0 | (tx1 << 16), ty0 | (ty1 << 16));
         }
       }
     }
   }
-  // Warp-aggregated append of the large triangles and of their pair counts.
   const unsigned lane = threadIdx.x & 31u;
+  // Medium triangles: the whole warp sweeps each one's pixel box, one triangle at a time.
+  unsigned todo = __ballot_sync(0xffffffffu, medium);
+  while (todo) {
+    const int src = __ffs(todo) - 1;
+    todo &= todo - 1;
+    const Vert w0 = {__shfl_sync(0xffffffffu, v0.x, src), __shfl_sync(0xffffffffu, v0.y, src),
+                     __shfl_sync(0xffffffffu, v0.z, src), __shfl_sync(0xffffffffu, v0.w, src)};
+    const Vert w1 = {__shfl_sync(0xffffffffu, v1.x, src), __shfl_sync(0xffffffffu, v1.y, src),
+                     __shfl_sync(0xffffffffu, v1.z, src), __shfl_sync(0xffffffffu, v1.w, src)};
+    const Vert w2 = {__shfl_sync(0xffffffffu, v2.x, src), __shfl_sync(0xffffffffu, v2.y, src),
+                     __shfl_sync(0xffffffffu, v2.z, src), __shfl_sync(0xffffffffu, v2.w, src)};
+    const int tt = __shfl_sync(0xffffffffu, t, src), bb = __shfl_sync(0xffffffffu, b, src);
+    const int cc0 = __shfl_sync(0xffffffffu, c0, src), rr0 = __shfl_sync(0xffffffffu, r0, src);
+    const int bw = __shfl_sync(0xffffffffu, c1, src) - cc0 + 1;
+    const int n = bw * (__shfl_sync(0xffffffffu, r1, src) - rr0 + 1);
+    for (int k = static_cast<int>(lane); k < n; k += 32)
+      raster_pixel(w0, w1, w2, tt, bb, rr0 + k / bw, cc0 + k % bw, height, width, prev, keys);
+  }
+  // Warp-aggregated append of the large triangles and of their pair counts.
   const unsigned mask = __ballot_sync(0xffffffffu, large);
   unsigned long long warp_pairs = pairs;
 #pragma unroll
@@ -172,9 +199,7 @@ __global__ void __launch_bounds__(256) setup_kernel(
   slot0 = __shfl_sync(0xffffffffu, slot0, 0);
   if (large) {
     const unsigned long long slot = slot0 + __popc(mask & ((1u << lane) - 1u));
-    if (slot < static_cast<unsigned long long>(capacity)) {
-      binned[slot] = {static_cast<int>(g), tile_box.x, tile_box.y};
-    }
+    if (slot < static_cast<unsigned long long>(capacity)) binned[slot] = {static_cast<int>(g), c0, c1, r0, r1};
   }
 }
 
@@ -193,14 +218,14 @@ __global__ void __launch_bounds__(256) bin_kernel(const Binned* __restrict__ bin
     const Binned rec = binned[i];
     const int g = rec.g;
     const int b = g / num_tri;
-    const int tx0 = rec.bx & 0xFFFF, tx1 = rec.bx >> 16, ty0 = rec.by & 0xFFFF, ty1 = rec.by >> 16;
+    const int tx0 = rec.c0 / kTile, tx1 = rec.c1 / kTile, ty0 = rec.r0 / kTile, ty1 = rec.r1 / kTile;
     const int nx = tx1 - tx0 + 1;
     const int n = nx * (ty1 - ty0 + 1);
     for (int k = lane; k < n; k += 32) {
       const int tile = b * tiles_per_image + (ty0 + k / nx) * tiles_x + tx0 + k % nx;
       if (kScatter) {
         const unsigned slot = atomicAdd(tile_count + tile, 1u);
-        pairs[tile_offset[tile] + slot] = g;
+        pairs[tile_offset[tile] + slot] = static_cast<int>(i);
       } else {
         atomicAdd(tile_count + tile, 1u);
       }
@@ -286,10 +311,11 @@ __global__ void __launch_bounds__(256) tile_kernel(
     const float* __restrict__ pos, const int* __restrict__ tri, int num_vert, int num_tri,
     int height, int width, int tiles_x, int tiles_per_image, int num_tiles,
     const long long* __restrict__ prev, long long* __restrict__ keys, const int* __restrict__ pairs,
-    const unsigned* __restrict__ tile_offset, const unsigned* __restrict__ item_offset,
-    unsigned* __restrict__ work) {
+    const Binned* __restrict__ binned, const unsigned* __restrict__ tile_offset,
+    const unsigned* __restrict__ item_offset, unsigned* __restrict__ work) {
   __shared__ float4 sv[3][kChunk];
   __shared__ int st[kChunk];
+  __shared__ int4 sbox[kChunk];
   __shared__ int s_tile;
   __shared__ unsigned s_first, s_count;
   const int lx = threadIdx.x % kTile, ly = threadIdx.x / kTile;
@@ -318,7 +344,8 @@ __global__ void __launch_bounds__(256) tile_kernel(
     if (tile < 0) break;
     const int n = static_cast<int>(s_count);
     if (threadIdx.x < n) {
-      const int g = pairs[s_first + threadIdx.x];
+      const Binned rec = binned[pairs[s_first + threadIdx.x]];
+      const int g = rec.g;
       const int b = g / num_tri;
       const int t = g - b * num_tri;
       const long long base = static_cast<long long>(b) * num_vert;
@@ -327,6 +354,7 @@ __global__ void __launch_bounds__(256) tile_kernel(
       sv[1][threadIdx.x] = __ldg(p4 + base + __ldg(tri + 3 * static_cast<long long>(t) + 1));
       sv[2][threadIdx.x] = __ldg(p4 + base + __ldg(tri + 3 * static_cast<long long>(t) + 2));
       st[threadIdx.x] = t;
+      sbox[threadIdx.x] = make_int4(rec.c0, rec.c1, rec.r0, rec.r1);
     }
     __syncthreads();
     const int image = tile / tiles_per_image;
@@ -339,6 +367,8 @@ __global__ void __launch_bounds__(256) tile_kernel(
       const long long floor_key = prev != nullptr ? __ldg(prev + off) : -0x7FFFFFFFFFFFFFFFLL - 1;
       long long best = kEmptyKey;
       for (int i = 0; i < n; ++i) {
+        const int4 box = sbox[i];
+        if (col < box.x || col > box.y || row < box.z || row > box.w) continue;
         const float4 a = sv[0][i], b = sv[1][i], c = sv[2][i];
         const long long key = coverage_key({a.x, a.y, a.z, a.w}, {b.x, b.y, b.z, b.w},
                                            {c.x, c.y, c.z, c.w}, px, py, st[i]);
@@ -630,7 +660,7 @@ extern "C" int dr_raster_tiles(const float* pos, const int32_t* tri, int64_t bat
                                       static_cast<int>(num_tri), height, width, tiles_x,
                                       tiles_per_image, static_cast<int>(tiles),
                                       reinterpret_cast<const long long*>(prev_keys),
-                                      reinterpret_cast<long long*>(keys), bl.pairs,
+                                      reinterpret_cast<long long*>(keys), bl.pairs, sl.binned,
                                       bl.tile_offset, bl.item_offset, bl.work);
   return launch_status();
 }

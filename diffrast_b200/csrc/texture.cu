@@ -457,46 +457,141 @@ __global__ void __launch_bounds__(256) texture_fwd_kernel(
   }
 }
 
-// Scatter of g into the taps of a footprint, each tap weighted by its bilinear weight (plus the
-// cube-corner share of the missing taps).
+// Texel-gradient staging: a 16x16 pixel tile adds its contributions into a shared-memory hash
+// table keyed by (level, texel offset), kTexGroup channels at a time, and flushes each distinct
+// texel to global memory once. Neighbouring pixels share most texels (a texel of the chosen levels
+// spans about a pixel), so this replaces heavily contended global atomics with shared-memory ones.
+// A texel that finds no free slot within kProbes probes goes straight to global memory.
+constexpr int kTexSlots = 1024;
+constexpr int kTexGroup = 4;
+constexpr int kProbes = 32;
+constexpr unsigned long long kNoTexel = ~0ull;
+
+struct TexTable {
+  unsigned long long key[kTexSlots];
+  float val[kTexSlots * kTexGroup];
+};
+
+__device__ __forceinline__ unsigned mix_key(unsigned long long x) {
+  x ^= x >> 33;
+  x *= 0xff51afd7ed558ccdull;
+  x ^= x >> 33;
+  return static_cast<unsigned>(x);
+}
+
+__device__ __forceinline__ int table_slot(TexTable& tb, unsigned long long key) {
+  unsigned h = mix_key(key) & (kTexSlots - 1);
+  for (int probe = 0; probe < kProbes; ++probe) {
+    const unsigned long long prev = atomicCAS(&tb.key[h], kNoTexel, key);
+    if (prev == kNoTexel || prev == key) return static_cast<int>(h);
+    h = (h + 1) & (kTexSlots - 1);
+  }
+  return -1;
+}
+
+// Taps of a pixel's lookup with their weights (bilinear weight times level weight, plus the
+// cube-corner share): up to 4 per level, 2 levels.
+struct Taps {
+  int n;
+  int level[8];
+  long long off[8];
+  float w[8];
+};
+
 template <int B>
-__device__ __forceinline__ void scatter_footprint(float* __restrict__ grad, const Footprint& f,
-                                                  int c, float g) {
+__device__ __forceinline__ void add_footprint_taps(Taps& taps, const Footprint& f, int level,
+                                                   float scale) {
   const float gx = 1.0f - f.fx, gy = 1.0f - f.fy;
   const float wgt[4] = {gx * gy, f.fx * gy, gx * f.fy, f.fx * f.fy};
   const float extra = B == DR_BOUNDARY_CUBE ? f.missing / 3.0f : 0.0f;
   for (int t = 0; t < 4; ++t) {
-    const float value = g * (wgt[t] + extra);
-    if (f.ok[t] && value != 0.0f) red_add(grad + f.off[t] + c, value);
+    if (!f.ok[t]) continue;
+    taps.level[taps.n] = level;
+    taps.off[taps.n] = f.off[t];
+    taps.w[taps.n] = scale * (wgt[t] + extra);
+    ++taps.n;
   }
 }
 
 template <int MODE, int B>
 __global__ void __launch_bounds__(256) texture_bwd_kernel(
     const Levels L, int channels, const float* __restrict__ uv, const float* __restrict__ uv_da,
-    const float* __restrict__ bias, long long total, long long pixels_per_image,
-    const float* __restrict__ grad_out, float* __restrict__ grad_uv,
-    float* __restrict__ grad_uv_da, float* __restrict__ grad_bias) {
-  const long long p = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
-  if (p >= total) return;
-  const long long view = p / pixels_per_image;
+    const float* __restrict__ bias, int height, int width, const float* __restrict__ grad_out,
+    float* __restrict__ grad_uv, float* __restrict__ grad_uv_da, float* __restrict__ grad_bias) {
+  __shared__ TexTable tb;
+  const int col = blockIdx.x * 16 + (threadIdx.x & 15);
+  const int row = blockIdx.y * 16 + (threadIdx.x >> 4);
+  const long long view = blockIdx.z;
+  const bool inside = row < height && col < width;
+  const long long p = (view * height + row) * width + col;
   Lookup<MODE, B> k;
-  prepare<MODE, B>(L, channels, uv, uv_da, bias, p, view, k);
-  const bool live = !k.bad && k.valid;
+  bool live = false;
+  Taps taps;
+  taps.n = 0;
+  if (inside) {
+    prepare<MODE, B>(L, channels, uv, uv_da, bias, p, view, k);
+    live = !k.bad && k.valid;
+    if (live) {
+      if (MODE == DR_FILTER_NEAREST) {
+        if (k.near_ok) {
+          taps.level[0] = 0;
+          taps.off[0] = k.near_off;
+          taps.w[0] = 1.0f;
+          taps.n = 1;
+        }
+      } else if (MODE == DR_FILTER_LINEAR_MIPMAP_LINEAR) {
+        add_footprint_taps<B>(taps, k.f_lo, k.lo, 1.0f - k.frac);
+        add_footprint_taps<B>(taps, k.f_hi, k.hi, k.frac);
+      } else {
+        add_footprint_taps<B>(taps, k.f_lo, k.lo, 1.0f);
+      }
+    }
+  }
+  // Texel gradients, staged in shared memory per group of channels.
+  for (int c0 = 0; c0 < channels; c0 += kTexGroup) {
+    const int group = min(kTexGroup, channels - c0);
+    for (int i = threadIdx.x; i < kTexSlots; i += blockDim.x) tb.key[i] = kNoTexel;
+    for (int i = threadIdx.x; i < kTexSlots * kTexGroup; i += blockDim.x) tb.val[i] = 0.0f;
+    __syncthreads();
+    int slot[8];
+    for (int t = 0; t < taps.n; ++t) {
+      const unsigned long long key =
+          (static_cast<unsigned long long>(taps.level[t]) << 48) | static_cast<unsigned long long>(taps.off[t]);
+      slot[t] = taps.w[t] != 0.0f ? table_slot(tb, key) : -2;
+    }
+    for (int cc = 0; cc < group; ++cc) {
+      const float g = live ? grad_out[p * channels + c0 + cc] : 0.0f;
+      if (g == 0.0f) continue;
+      for (int t = 0; t < taps.n; ++t) {
+        const float value = g * taps.w[t];
+        if (slot[t] >= 0) {
+          atomicAdd(&tb.val[slot[t] * kTexGroup + cc], value);
+        } else if (slot[t] == -1) {
+          red_add(L.grad[taps.level[t]] + taps.off[t] + c0 + cc, value);
+        }
+      }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < kTexSlots; i += blockDim.x) {
+      const unsigned long long key = tb.key[i];
+      if (key == kNoTexel) continue;
+      float* dst = L.grad[key >> 48] + static_cast<long long>(key & 0xFFFFFFFFFFFFull) + c0;
+      for (int cc = 0; cc < group; ++cc) {
+        const float v = tb.val[i * kTexGroup + cc];
+        if (v != 0.0f) red_add(dst + cc, v);
+      }
+    }
+    __syncthreads();
+  }
+  if (!inside) return;
   const bool coord_grads = grad_uv != nullptr || grad_uv_da != nullptr || grad_bias != nullptr;
+  if (!coord_grads) return;
   float g_fx_lo = 0.f, g_fy_lo = 0.f, g_fx_hi = 0.f, g_fy_hi = 0.f, g_frac = 0.f;
-  if (live) {
+  if (live && MODE != DR_FILTER_NEAREST) {
     const float w_hi = k.frac, w_lo = 1.0f - k.frac;
     for (int c = 0; c < channels; ++c) {
       const float g = grad_out[p * channels + c];
-      if (MODE == DR_FILTER_NEAREST) {
-        if (k.near_ok && g != 0.0f) red_add(L.grad[0] + k.near_off + c, g);
-        continue;
-      }
       const float g_lo = MODE == DR_FILTER_LINEAR_MIPMAP_LINEAR ? g * w_lo : g;
-      scatter_footprint<B>(L.grad[k.lo], k.f_lo, c, g_lo);
-      if (MODE == DR_FILTER_LINEAR_MIPMAP_LINEAR) scatter_footprint<B>(L.grad[k.hi], k.f_hi, c, g * w_hi);
-      if (!coord_grads) continue;
       float t[4];
       const float lower = bilinear_value<B>(L.ptr[k.lo], k.f_lo, c, t);
       {
@@ -527,7 +622,6 @@ __global__ void __launch_bounds__(256) texture_bwd_kernel(
       }
     }
   }
-  if (!coord_grads) return;
   // Gradient of the coordinates (u, v) or, for a cube, of the face coordinates (s, t).
   float g_u = 0.f, g_v = 0.f;
   if (live && MODE != DR_FILTER_NEAREST) {
@@ -649,10 +743,11 @@ void launch_fwd(const Levels& L, int channels, const float* uv, const float* uv_
 
 template <int MODE, int B>
 void launch_bwd(const Levels& L, int channels, const float* uv, const float* uv_da,
-                const float* bias, long long total, long long ppi, const float* grad_out,
+                const float* bias, int batch, int height, int width, const float* grad_out,
                 float* grad_uv, float* grad_uv_da, float* grad_bias, cudaStream_t s) {
-  texture_bwd_kernel<MODE, B><<<blocks_for(total, 256), 256, 0, s>>>(
-      L, channels, uv, uv_da, bias, total, ppi, grad_out, grad_uv, grad_uv_da, grad_bias);
+  const dim3 grid((width + 15) / 16, (height + 15) / 16, batch);
+  texture_bwd_kernel<MODE, B><<<grid, 256, 0, s>>>(L, channels, uv, uv_da, bias, height, width,
+                                                  grad_out, grad_uv, grad_uv_da, grad_bias);
 }
 
 template <int B, typename F>
@@ -746,10 +841,11 @@ extern "C" int dr_texture_bwd(const float* const* level_ptr, float* const* grad_
   if (uv == nullptr || grad_out == nullptr) return DR_ERR_INVALID_ARGUMENT;
   if (grad_uv_da != nullptr && uv_da == nullptr) return DR_ERR_INVALID_ARGUMENT;
   if (grad_bias != nullptr && bias == nullptr) return DR_ERR_INVALID_ARGUMENT;
-  const long long ppi = static_cast<long long>(height) * width;
+  if (batch > 65535 || height >= (1 << 20) || width >= (1 << 20)) return DR_ERR_TOO_LARGE;
   cudaStream_t s = as_stream(stream);
   dispatch(filter_mode, boundary_mode, [&](auto m, auto b) {
-    launch_bwd<decltype(m)::value, decltype(b)::value>(L, channels, uv, uv_da, bias, total, ppi,
+    launch_bwd<decltype(m)::value, decltype(b)::value>(L, channels, uv, uv_da, bias,
+                                                       static_cast<int>(batch), height, width,
                                                        grad_out, grad_uv, grad_uv_da, grad_bias, s);
   });
   return launch_status();
