@@ -81,7 +81,7 @@ def raster_keys(pos: Tensor, tri: Tensor, height: int, width: int, prev_keys: Te
     cap = _capacity.get(shape_key, max(1024, min(batch * num_tri, 1 << 16)))
     binned, pairs = c_int64(0), c_int64(0)
     for _ in range(2):
-        ws = _scratch(lib.dr_raster_setup_workspace_bytes(cap), dev)
+        ws = _scratch(lib.dr_raster_setup_workspace_bytes(cap, height, width), dev)
         N.check(
             lib.dr_raster_setup(pos.data_ptr(), tri.data_ptr(), batch, num_vert, num_tri, height,
                                 width, N.ptr(prev_keys), keys.data_ptr(), ws.data_ptr(),

@@ -24,7 +24,7 @@ _P = c_void_p
 _SIGNATURES = {
     "dr_version": (c_int, []),
     "dr_status_string": (c_char_p, [c_int]),
-    "dr_raster_setup_workspace_bytes": (c_size_t, [c_int64]),
+    "dr_raster_setup_workspace_bytes": (c_size_t, [c_int64, c_int32, c_int32]),
     "dr_raster_setup": (
         c_int,
         [_P, _P, c_int64, c_int64, c_int64, c_int32, c_int32, _P, _P, _P, c_size_t, c_int64, _P],

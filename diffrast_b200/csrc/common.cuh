@@ -29,10 +29,9 @@ constexpr float kLimit = 1e18f;
 constexpr int kTile = 16;
 // Triangles per tile work item (one per thread of a 16x16 tile block).
 constexpr int kChunk = 256;
-// Triangles whose pixel box holds at most kThreadPixels pixels are rasterized by their own setup
-// thread; up to kWarpPixels by the 32 lanes of the setup warp together; larger ones are binned
-// into screen tiles.
-constexpr int kThreadPixels = 4;
+// Triangles whose pixel box holds at most kWarpPixels pixels are rasterized directly by the setup
+// warp (its lanes share the (triangle, pixel) items of all such triangles of the warp); larger
+// ones are binned into screen tiles.
 constexpr int kWarpPixels = 512;
 
 __device__ __forceinline__ float mul(float a, float b) { return __fmul_rn(a, b); }
@@ -84,7 +83,9 @@ __device__ __forceinline__ long long pack_key(float depth, int tri) {
 // (reference.py:293-365): edge functions e = a x c with a = x - px w and c = y - py w, the
 // top-left rule for exact zeros from the sign of the edge's screen gradient, the area tolerance
 // against the magnitude of the terms, the sign of the interpolated w and -1 <= z/w <= 1.
-// Non-finite vertices are rejected by the caller.
+// Non-finite vertices are rejected by the caller. All conditions are conjunctions of pure
+// functions of the same rounded values, so testing the cheap edge signs first and returning early
+// changes no result; it only skips the tolerance and depth arithmetic for pixels outside.
 __device__ __forceinline__ long long coverage_key(const Vert& v0, const Vert& v1, const Vert& v2,
                                                   float px, float py, int tri) {
   const float a0 = sub(v0.x, mul(px, v0.w)), a1 = sub(v1.x, mul(px, v1.w)),
@@ -95,21 +96,22 @@ __device__ __forceinline__ long long coverage_key(const Vert& v0, const Vert& v1
   const float e1 = cross2(a2, c0, a0, c2);
   const float e2 = cross2(a0, c1, a1, c0);
   const float s = add(add(e0, e1), e2);
-  const float ew = add(add(mul(e0, v0.w), mul(e1, v1.w)), mul(e2, v2.w));
-  const float ez = add(add(mul(e0, v0.z), mul(e1, v1.z)), mul(e2, v2.z));
-  const float depth = dvd(ez, ew);
   const bool positive = s > 0.0f;
-
-  // Edge k runs from vertex i = k + 1 to j = k + 2.
-  auto side = [&](float e, float ai, float ci, float wi, float aj, float cj, float wj) {
+  // A nonzero edge function must have the sign of the area (NaN fails both tests).
+  if (positive ? !(e0 >= 0.0f && e1 >= 0.0f && e2 >= 0.0f)
+               : !(e0 <= 0.0f && e1 <= 0.0f && e2 <= 0.0f))
+    return kEmptyKey;
+  // Edge k runs from vertex i = k + 1 to j = k + 2; a pixel exactly on it is decided by the
+  // direction of its screen gradient.
+  auto on_edge_inside = [&](float ai, float ci, float wi, float aj, float cj, float wj) {
     const float gx = cross2(ci, wj, cj, wi);
     const float gy = cross2(aj, wi, ai, wj);
-    const float q = (e == 0.0f) ? ((gx == 0.0f) ? gy : gx) : e;
+    const float q = (gx == 0.0f) ? gy : gx;
     return positive ? (q > 0.0f) : (q < 0.0f);
   };
-  bool inside = side(e0, a1, c1, v1.w, a2, c2, v2.w);
-  inside = inside & side(e1, a2, c2, v2.w, a0, c0, v0.w);
-  inside = inside & side(e2, a0, c0, v0.w, a1, c1, v1.w);
+  if (e0 == 0.0f && !on_edge_inside(a1, c1, v1.w, a2, c2, v2.w)) return kEmptyKey;
+  if (e1 == 0.0f && !on_edge_inside(a2, c2, v2.w, a0, c0, v0.w)) return kEmptyKey;
+  if (e2 == 0.0f && !on_edge_inside(a0, c0, v0.w, a1, c1, v1.w)) return kEmptyKey;
 
   const float reach_x = nanmax(nanmax(add(fabsf(v0.x), fabsf(v0.w)), add(fabsf(v1.x), fabsf(v1.w))),
                                add(fabsf(v2.x), fabsf(v2.w)));
@@ -118,10 +120,13 @@ __device__ __forceinline__ long long coverage_key(const Vert& v0, const Vert& v1
   const float span_x = add(add(fabsf(a0), fabsf(a1)), fabsf(a2));
   const float span_y = add(add(fabsf(c0), fabsf(c1)), fabsf(c2));
   const float bound = mul(add(mul(reach_x, span_y), mul(span_x, add(reach_y, span_y))), kAreaTolerance);
-  inside = inside & (fabsf(s) > bound);
-  inside = inside & (positive ? (ew > 0.0f) : (ew < 0.0f));
-  inside = inside & (depth >= -1.0f) & (depth <= 1.0f);
-  return inside ? pack_key(depth, tri) : kEmptyKey;
+  if (!(fabsf(s) > bound)) return kEmptyKey;
+  const float ew = add(add(mul(e0, v0.w), mul(e1, v1.w)), mul(e2, v2.w));
+  if (positive ? !(ew > 0.0f) : !(ew < 0.0f)) return kEmptyKey;
+  const float ez = add(add(mul(e0, v0.z), mul(e1, v1.z)), mul(e2, v2.z));
+  const float depth = dvd(ez, ew);
+  if (!(depth >= -1.0f && depth <= 1.0f)) return kEmptyKey;
+  return pack_key(depth, tri);
 }
 
 // Status of the launches just made on this thread.

@@ -2,9 +2,11 @@
 //
 // Visibility (result identical to diffrast's reference, backends/reference.py:368-397):
 //   1. setup_kernel, one thread per (view, triangle): culls and bounds the triangle in pixels.
-//      A box of at most kThreadPixels pixels is rasterized by the thread itself, one of at most
-//      kWarpPixels by the whole warp (lanes sweep the box, one triangle after another); keys are
-//      merged with 64-bit atomicMin. Larger triangles are appended (warp-aggregated) to a list.
+//      Triangles whose box holds at most kWarpPixels pixels are rasterized by the warp directly:
+//      a warp prefix sum numbers the (triangle, pixel) items of all of them, the triangles are
+//      staged in shared memory and the 32 lanes take the items 32 at a time, so small and medium
+//      triangles cost work in proportion to their boxes with no divergence. Keys are merged with
+//      64-bit atomicMin. Larger triangles are appended (warp-aggregated) to a list.
 //   2. Device-side binning without host round trips beyond one counter read: per-tile counts,
 //      one exclusive scan (pair offsets and 256-triangle work items), and a scatter into per-tile
 //      triangle lists.
@@ -31,19 +33,28 @@ struct Binned {
 
 struct SetupLayout {
   unsigned long long* counters;  // [0] binned triangles, [1] (triangle, tile) pairs
+  float* centres;                // NDC x of every column, then y of every row
   Binned* binned;
 };
 
-SetupLayout setup_layout(const void* ws) {
+SetupLayout setup_layout(const void* ws, int height, int width) {
   char* p = static_cast<char*>(const_cast<void*>(ws));
   SetupLayout l;
   l.counters = reinterpret_cast<unsigned long long*>(p);
-  l.binned = reinterpret_cast<Binned*>(p + 256);
+  l.centres = reinterpret_cast<float*>(p + 256);
+  l.binned = reinterpret_cast<Binned*>(p + 256 + align256(sizeof(float) * (height + width)));
   return l;
 }
 
-size_t setup_bytes(int64_t capacity) {
-  return 256 + align256(sizeof(Binned) * static_cast<size_t>(capacity));
+size_t setup_bytes(int64_t capacity, int height, int width) {
+  return 256 + align256(sizeof(float) * static_cast<size_t>(height + width)) +
+         align256(sizeof(Binned) * static_cast<size_t>(capacity));
+}
+
+__global__ void centres_kernel(float* __restrict__ centres, int height, int width) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < width) centres[i] = pixel_centre(i, width);
+  else if (i < width + height) centres[i] = pixel_centre(i - width, height);
 }
 
 struct BinLayout {
@@ -99,25 +110,24 @@ __device__ __forceinline__ void pixel_range(float lo, float hi, int size, int& f
   last = static_cast<int>(l);
 }
 
-__device__ __forceinline__ void raster_pixel(const Vert& v0, const Vert& v1, const Vert& v2, int t,
-                                             int b, int r, int c, int height, int width,
-                                             const long long* __restrict__ prev,
-                                             long long* __restrict__ keys) {
-  const long long key = coverage_key(v0, v1, v2, pixel_centre(c, width), pixel_centre(r, height), t);
-  if (key == kEmptyKey) return;
-  const long long off = (static_cast<long long>(b) * height + r) * width + c;
-  if (prev != nullptr && !(key > __ldg(prev + off))) return;
-  atomicMin(keys + off, key);
-}
+// Triangles a warp rasterizes directly, staged so that any lane can work on any of them.
+struct WarpTris {
+  float4 v[3][32];
+  int t[32], b[32], c0[32], r0[32], bw[32], end[32];
+};
 
 __global__ void __launch_bounds__(256) setup_kernel(
     const float* __restrict__ pos, const int* __restrict__ tri, int num_vert, int num_tri,
-    long long total, int height, int width, const long long* __restrict__ prev,
-    long long* __restrict__ keys, unsigned long long* __restrict__ counters,
-    Binned* __restrict__ binned, long long capacity) {
+    long long total, int height, int width, const float* __restrict__ centres,
+    const long long* __restrict__ prev, long long* __restrict__ keys,
+    unsigned long long* __restrict__ counters, Binned* __restrict__ binned, long long capacity) {
+  __shared__ WarpTris staged[8];
   const long long g = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
-  bool large = false, medium = false;
+  const unsigned lane = threadIdx.x & 31u;
+  WarpTris& w = staged[threadIdx.x >> 5];
+  bool large = false;
   unsigned pairs = 0;
+  int items = 0;
   int b = 0, t = 0, c0 = 0, c1 = -1, r0 = 0, r1 = -1;
   Vert v0 = {0.f, 0.f, 0.f, 1.f}, v1 = v0, v2 = v0;
   if (g < total) {
@@ -153,11 +163,8 @@ __global__ void __launch_bounds__(256) setup_kernel(
       }
       if (c0 <= c1 && r0 <= r1) {
         const long long area = static_cast<long long>(c1 - c0 + 1) * (r1 - r0 + 1);
-        if (in_front && area <= kThreadPixels) {
-          for (int r = r0; r <= r1; ++r)
-            for (int c = c0; c <= c1; ++c) raster_pixel(v0, v1, v2, t, b, r, c, height, width, prev, keys);
-        } else if (in_front && area <= kWarpPixels) {
-          medium = true;
+        if (in_front && area <= kWarpPixels) {
+          items = static_cast<int>(area);
         } else {
           large = true;
           const unsigned tx0 = c0 / kTile, tx1 = c1 / kTile, ty0 = r0 / kTile, ty1 = r1 / kTile;
@@ -166,24 +173,43 @@ __global__ void __launch_bounds__(256) setup_kernel(
       }
     }
   }
-  const unsigned lane = threadIdx.x & 31u;
-  // Medium triangles: the whole warp sweeps each one's pixel box, one triangle at a time.
-  unsigned todo = __ballot_sync(0xffffffffu, medium);
-  while (todo) {
-    const int src = __ffs(todo) - 1;
-    todo &= todo - 1;
-    const Vert w0 = {__shfl_sync(0xffffffffu, v0.x, src), __shfl_sync(0xffffffffu, v0.y, src),
-                     __shfl_sync(0xffffffffu, v0.z, src), __shfl_sync(0xffffffffu, v0.w, src)};
-    const Vert w1 = {__shfl_sync(0xffffffffu, v1.x, src), __shfl_sync(0xffffffffu, v1.y, src),
-                     __shfl_sync(0xffffffffu, v1.z, src), __shfl_sync(0xffffffffu, v1.w, src)};
-    const Vert w2 = {__shfl_sync(0xffffffffu, v2.x, src), __shfl_sync(0xffffffffu, v2.y, src),
-                     __shfl_sync(0xffffffffu, v2.z, src), __shfl_sync(0xffffffffu, v2.w, src)};
-    const int tt = __shfl_sync(0xffffffffu, t, src), bb = __shfl_sync(0xffffffffu, b, src);
-    const int cc0 = __shfl_sync(0xffffffffu, c0, src), rr0 = __shfl_sync(0xffffffffu, r0, src);
-    const int bw = __shfl_sync(0xffffffffu, c1, src) - cc0 + 1;
-    const int n = bw * (__shfl_sync(0xffffffffu, r1, src) - rr0 + 1);
-    for (int k = static_cast<int>(lane); k < n; k += 32)
-      raster_pixel(w0, w1, w2, tt, bb, rr0 + k / bw, cc0 + k % bw, height, width, prev, keys);
+  // Direct rasterization, load-balanced over the warp: the (triangle, pixel) items of all its
+  // direct triangles are numbered by a prefix sum and the lanes take them 32 at a time.
+  w.v[0][lane] = make_float4(v0.x, v0.y, v0.z, v0.w);
+  w.v[1][lane] = make_float4(v1.x, v1.y, v1.z, v1.w);
+  w.v[2][lane] = make_float4(v2.x, v2.y, v2.z, v2.w);
+  w.t[lane] = t;
+  w.b[lane] = b;
+  w.c0[lane] = c0;
+  w.r0[lane] = r0;
+  w.bw[lane] = c1 - c0 + 1;
+  int end = items;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, end, o);
+    if (static_cast<int>(lane) >= o) end += y;
+  }
+  w.end[lane] = end;
+  const int all_items = __shfl_sync(0xffffffffu, end, 31);
+  __syncwarp();
+  for (int item = static_cast<int>(lane); item < all_items; item += 32) {
+    // Owner: the first lane whose items end after this one.
+    int lo = 0, hi = 31;
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (w.end[mid] > item) hi = mid; else lo = mid + 1;
+    }
+    const int local = item - (lo > 0 ? w.end[lo - 1] : 0);
+    const int bw = w.bw[lo];
+    const int row = w.r0[lo] + local / bw, col = w.c0[lo] + local % bw;
+    const float4 a = w.v[0][lo], bb = w.v[1][lo], cc = w.v[2][lo];
+    const long long key = coverage_key({a.x, a.y, a.z, a.w}, {bb.x, bb.y, bb.z, bb.w},
+                                       {cc.x, cc.y, cc.z, cc.w}, __ldg(centres + col),
+                                       __ldg(centres + width + row), w.t[lo]);
+    if (key == kEmptyKey) continue;
+    const long long off = (static_cast<long long>(w.b[lo]) * height + row) * width + col;
+    if (prev != nullptr && !(key > __ldg(prev + off))) continue;
+    atomicMin(keys + off, key);
   }
   // Warp-aggregated append of the large triangles and of their pair counts.
   const unsigned mask = __ballot_sync(0xffffffffu, large);
@@ -310,6 +336,7 @@ __global__ void __launch_bounds__(1024) scan_kernel(const unsigned* __restrict__
 __global__ void __launch_bounds__(256) tile_kernel(
     const float* __restrict__ pos, const int* __restrict__ tri, int num_vert, int num_tri,
     int height, int width, int tiles_x, int tiles_per_image, int num_tiles,
+    const float* __restrict__ centres,
     const long long* __restrict__ prev, long long* __restrict__ keys, const int* __restrict__ pairs,
     const Binned* __restrict__ binned, const unsigned* __restrict__ tile_offset,
     const unsigned* __restrict__ item_offset, unsigned* __restrict__ work) {
@@ -362,7 +389,7 @@ __global__ void __launch_bounds__(256) tile_kernel(
     const int row = (in_image / tiles_x) * kTile + ly;
     const int col = (in_image % tiles_x) * kTile + lx;
     if (row < height && col < width) {
-      const float px = pixel_centre(col, width), py = pixel_centre(row, height);
+      const float px = __ldg(centres + col), py = __ldg(centres + width + row);
       const long long off = (static_cast<long long>(image) * height + row) * width + col;
       const long long floor_key = prev != nullptr ? __ldg(prev + off) : -0x7FFFFFFFFFFFFFFFLL - 1;
       long long best = kEmptyKey;
@@ -571,8 +598,9 @@ bool bad_raster_args(const float* pos, const int32_t* tri, int64_t batch, int64_
 
 using namespace dr;
 
-extern "C" size_t dr_raster_setup_workspace_bytes(int64_t capacity) {
-  return setup_bytes(capacity < 0 ? 0 : capacity);
+extern "C" size_t dr_raster_setup_workspace_bytes(int64_t capacity, int32_t height,
+                                                  int32_t width) {
+  return setup_bytes(capacity < 0 ? 0 : capacity, height < 0 ? 0 : height, width < 0 ? 0 : width);
 }
 
 extern "C" int dr_raster_setup(const float* pos, const int32_t* tri, int64_t batch,
@@ -582,9 +610,9 @@ extern "C" int dr_raster_setup(const float* pos, const int32_t* tri, int64_t bat
   if (bad_raster_args(pos, tri, batch, num_vert, num_tri, height, width) || capacity < 0 ||
       keys == nullptr || workspace == nullptr)
     return DR_ERR_INVALID_ARGUMENT;
-  if (workspace_bytes < setup_bytes(capacity)) return DR_ERR_WORKSPACE_TOO_SMALL;
+  if (workspace_bytes < setup_bytes(capacity, height, width)) return DR_ERR_WORKSPACE_TOO_SMALL;
   cudaStream_t s = as_stream(stream);
-  SetupLayout l = setup_layout(workspace);
+  SetupLayout l = setup_layout(workspace, height, width);
   const long long pixels = batch * static_cast<long long>(height) * width;
   cudaError_t err = cudaMemsetAsync(l.counters, 0, 2 * sizeof(unsigned long long), s);
   if (err != cudaSuccess) return static_cast<int>(err);
@@ -592,12 +620,13 @@ extern "C" int dr_raster_setup(const float* pos, const int32_t* tri, int64_t bat
     fill_keys_kernel<<<min(blocks_for(pixels, 256), 148u * 32u), 256, 0, s>>>(
         reinterpret_cast<long long*>(keys), pixels);
   }
+  centres_kernel<<<blocks_for(height + width, 256), 256, 0, s>>>(l.centres, height, width);
   const long long total = batch * num_tri;
   if (total > 0) {
     setup_kernel<<<blocks_for(total, 256), 256, 0, s>>>(
         pos, tri, static_cast<int>(num_vert), static_cast<int>(num_tri), total, height, width,
-        reinterpret_cast<const long long*>(prev_keys), reinterpret_cast<long long*>(keys),
-        l.counters, l.binned, capacity);
+        l.centres, reinterpret_cast<const long long*>(prev_keys),
+        reinterpret_cast<long long*>(keys), l.counters, l.binned, capacity);
   }
   return launch_status();
 }
@@ -639,7 +668,7 @@ extern "C" int dr_raster_tiles(const float* pos, const int32_t* tri, int64_t bat
     return DR_ERR_WORKSPACE_TOO_SMALL;
   cudaStream_t s = as_stream(stream);
   // Only the first num_binned records are read; the caller reran setup with enough capacity.
-  SetupLayout sl = setup_layout(setup_workspace);
+  SetupLayout sl = setup_layout(setup_workspace, height, width);
   BinLayout bl = bin_layout(bin_workspace, tiles, num_pairs);
   const size_t tile_bytes = align256(sizeof(unsigned) * static_cast<size_t>(tiles + 1));
   cudaError_t err = cudaMemsetAsync(bl.tile_count, 0, 2 * tile_bytes, s);  // counts and cursors
@@ -658,7 +687,7 @@ extern "C" int dr_raster_tiles(const float* pos, const int32_t* tri, int64_t bat
                                               bl.pairs);
   tile_kernel<<<148 * 8, 256, 0, s>>>(pos, tri, static_cast<int>(num_vert),
                                       static_cast<int>(num_tri), height, width, tiles_x,
-                                      tiles_per_image, static_cast<int>(tiles),
+                                      tiles_per_image, static_cast<int>(tiles), sl.centres,
                                       reinterpret_cast<const long long*>(prev_keys),
                                       reinterpret_cast<long long*>(keys), bl.pairs, sl.binned,
                                       bl.tile_offset, bl.item_offset, bl.work);

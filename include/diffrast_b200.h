@@ -59,11 +59,12 @@ const char* dr_status_string(int status);
  * batch * num_tri must be below 2**31; height and width below 2**20.
  * ------------------------------------------------------------------------------------------- */
 
-/* Scratch of stage 1 for up to `capacity` triangles that need tile binning. */
-size_t dr_raster_setup_workspace_bytes(int64_t capacity);
+/* Scratch of stage 1 for up to `capacity` triangles that need tile binning, at this resolution. */
+size_t dr_raster_setup_workspace_bytes(int64_t capacity, int32_t height, int32_t width);
 
-/* Stage 1: fills `keys` (EMPTY, or the previous layer is excluded), culls, writes the keys of
- * triangles whose pixel box fits in 4x4 directly, and lists the others for binning. If more than
+/* Stage 1: fills `keys` with EMPTY, culls, writes the keys of triangles whose pixel box holds at
+ * most 512 pixels directly (keys not ordered after prev_keys are skipped), and lists the others
+ * for binning. If more than
  * `capacity` triangles need binning the list is incomplete: dr_raster_counts() reports how many,
  * and the caller reruns this stage with a larger workspace (the direct writes are idempotent). */
 int dr_raster_setup(const float* pos, const int32_t* tri, int64_t batch, int64_t num_vert,
