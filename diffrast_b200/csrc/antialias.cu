@@ -21,6 +21,7 @@
 #include <cstdint>
 
 #include "common.cuh"
+#include "edge_hash.cuh"
 #include "warp_reduce.cuh"
 
 namespace dr {
@@ -345,80 +346,6 @@ __global__ void __launch_bounds__(256) aa_bwd_kernel(const AaCtx a, long long to
   }
 }
 
-// ---------------------------------------------------------------------------------------------
-// Edge adjacency (reference.py:768-787) with an open-addressing hash table.
-// ---------------------------------------------------------------------------------------------
-
-constexpr unsigned long long kNoKey = ~0ull;
-
-__device__ __forceinline__ unsigned long long mix64(unsigned long long x) {
-  x ^= x >> 30;
-  x *= 0xbf58476d1ce4e5b9ull;
-  x ^= x >> 27;
-  x *= 0x94d049bb133111ebull;
-  x ^= x >> 31;
-  return x;
-}
-
-__device__ __forceinline__ unsigned long long edge_key(const int* __restrict__ tri, long long e) {
-  const long long t = e / 3;
-  const int k = static_cast<int>(e - 3 * t);
-  const unsigned a = static_cast<unsigned>(__ldg(tri + 3 * t + (k + 1) % 3));
-  const unsigned b = static_cast<unsigned>(__ldg(tri + 3 * t + (k + 2) % 3));
-  const unsigned lo = min(a, b), hi = max(a, b);
-  return (static_cast<unsigned long long>(lo) << 32) | hi;
-}
-
-__global__ void __launch_bounds__(256) edge_insert_kernel(const int* __restrict__ tri,
-                                                          long long num_edges,
-                                                          unsigned long long* __restrict__ keys,
-                                                          int* __restrict__ count,
-                                                          int* __restrict__ first,
-                                                          int* __restrict__ second,
-                                                          unsigned long long mask) {
-  const long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
-  if (e >= num_edges) return;
-  const unsigned long long key = edge_key(tri, e);
-  unsigned long long h = mix64(key) & mask;
-  // The table holds at least twice as many slots as edges, so a free or matching slot is found
-  // within `mask + 1` probes.
-  for (unsigned long long probe = 0; probe <= mask; ++probe) {
-    const unsigned long long prev = atomicCAS(keys + h, kNoKey, key);
-    if (prev == kNoKey || prev == key) {
-      const int c = atomicAdd(count + h, 1);
-      if (c == 0) first[h] = static_cast<int>(e);
-      else if (c == 1) second[h] = static_cast<int>(e);
-      return;
-    }
-    h = (h + 1) & mask;
-  }
-}
-
-__global__ void __launch_bounds__(256) edge_lookup_kernel(const int* __restrict__ tri,
-                                                          long long num_edges,
-                                                          const unsigned long long* __restrict__ keys,
-                                                          const int* __restrict__ count,
-                                                          const int* __restrict__ first,
-                                                          const int* __restrict__ second,
-                                                          unsigned long long mask,
-                                                          long long* __restrict__ out) {
-  const long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
-  if (e >= num_edges) return;
-  const unsigned long long key = edge_key(tri, e);
-  unsigned long long h = mix64(key) & mask;
-  long long result = -1;
-  for (unsigned long long probe = 0; probe <= mask; ++probe) {
-    const unsigned long long k = keys[h];
-    if (k == key) {
-      if (count[h] == 2) result = first[h] == e ? second[h] : first[h];
-      break;
-    }
-    if (k == kNoKey) break;
-    h = (h + 1) & mask;
-  }
-  out[e] = result;
-}
-
 __global__ void __launch_bounds__(256) silhouette_kernel(const AaCtx a, long long total,
                                                          uint8_t* __restrict__ out) {
   const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
@@ -429,11 +356,6 @@ __global__ void __launch_bounds__(256) silhouette_kernel(const AaCtx a, long lon
   out[i] = is_silhouette(a, pb, static_cast<int>(e / 3), static_cast<int>(e % 3)) ? 1 : 0;
 }
 
-unsigned long long table_slots(int64_t num_tri) {
-  unsigned long long slots = 64;
-  while (slots < 2ull * 3ull * static_cast<unsigned long long>(num_tri)) slots <<= 1;
-  return slots;
-}
 
 bool bad_aa_args(const float* color, const float* rast, const float* pos, int64_t pos_batch,
                  int64_t num_vert, const int32_t* tri, int64_t num_tri, const int64_t* neighbours,

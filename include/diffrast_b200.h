@@ -30,6 +30,7 @@ extern "C" {
 #define DR_ERR_INVALID_ARGUMENT 10001
 #define DR_ERR_WORKSPACE_TOO_SMALL 10002
 #define DR_ERR_TOO_LARGE 10003
+#define DR_ERR_EXCEEDS_STATIC_SCRATCH 10004
 
 /* Filter modes (ops.py:22 FilterMode, without "auto", which the host resolves). */
 #define DR_FILTER_NEAREST 0
@@ -166,6 +167,18 @@ size_t dr_edge_neighbours_workspace_bytes(int64_t num_tri);
  * none or several share it. Deterministic; needs no sort. */
 int dr_edge_neighbours(const int32_t* tri, int64_t num_tri, int64_t* neighbours, void* workspace,
                        size_t workspace_bytes, void* stream);
+
+/* Same result as dr_edge_neighbours for callers that cannot allocate device memory (a plain FFI
+ * binding without a device allocator, or a fixed device-memory budget): the hash table lives in a
+ * 10 MiB file-scope device array instead of a caller workspace. No counterpart in the reference.
+ * At most dr_edge_neighbours_noalloc_max_triangles() (65536) triangles; more is refused with
+ * DR_ERR_EXCEEDS_STATIC_SCRATCH. Every GPU where it is used keeps the array until process exit.
+ * All calls share the array (cleared as needed on each call), so calls that overlap on the GPU
+ * race. The first call on a device looks up the array's device address with that device
+ * current; make it before any stream capture. Allocates nothing. */
+int64_t dr_edge_neighbours_noalloc_max_triangles(void);
+int dr_edge_neighbours_noalloc(const int32_t* tri, int64_t num_tri, int64_t* neighbours,
+                               void* stream);
 
 /* Silhouette flags [pos_batch, num_tri, 3] as bytes (reference.py:790-814). The antialias
  * kernels evaluate the same test on the fly for the edges they cross. */
