@@ -7,9 +7,10 @@
 // whose half holds the crossing blends |t - 1/2| of the other's colour.
 //
 // B200 design:
-//   - Every pixel evaluates the (at most four) pairs it belongs to and writes only its own output,
-//     so the forward pass and the colour gradient need no atomics and are deterministic. The
-//     position gradient of a pair is scattered once, by its left or upper pixel.
+//   - Pixel tiles with a one-pixel halo: each pair is evaluated once per block into shared memory
+//     and every pixel writes only its own output, so the forward pass and the colour gradient need
+//     no atomics and are deterministic. The position gradient of a pair is scattered once, by the
+//     block where its left or upper pixel is an output pixel.
 //   - The silhouette test runs on the fly for the one edge a pair crosses, from the edge
 //     adjacency (neighbours) and the two opposite vertices, instead of classifying every edge of
 //     every view beforehand.
@@ -208,38 +209,38 @@ __device__ __forceinline__ Pair eval_pair(const AaCtx& a, long long b, int row, 
   return r;
 }
 
-__global__ void __launch_bounds__(256) aa_fwd_kernel(const AaCtx a, long long total,
-                                                     float* __restrict__ out) {
-  const long long p = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
-  if (p >= total) return;
-  const long long hw = static_cast<long long>(a.height) * a.width;
-  const long long b = p / hw;
-  const int row = static_cast<int>((p - b * hw) / a.width);
-  const int col = static_cast<int>(p - b * hw - static_cast<long long>(row) * a.width);
-  // Blend coefficients and partners, in the reference's accumulation order: right pair, left
-  // pair, lower pair, upper pair.
-  float k[4] = {0.f, 0.f, 0.f, 0.f};
-  long long other[4] = {p, p, p, p};
-  if (col + 1 < a.width) {
+// Pixel tiling of the antialias kernels: a block of 32 x 8 threads covers a 31 x 7 tile of output
+// pixels plus a one-pixel halo to the left and above. Each thread evaluates the right pair of its
+// pixel (unless it is in the halo row) and the lower pair (unless it is in the halo column) once,
+// into shared memory; every output pixel then reads its four pairs from there. Pairs are thus
+// evaluated once per block instead of once by each of their two pixels.
+constexpr int kAaThreadsX = 32, kAaThreadsY = 8;
+constexpr int kAaTileX = kAaThreadsX - 1, kAaTileY = kAaThreadsY - 1;
+
+__global__ void __launch_bounds__(256) aa_fwd_kernel(const AaCtx a, float* __restrict__ out) {
+  __shared__ float2 hk[kAaThreadsY][kAaThreadsX], vk[kAaThreadsY][kAaThreadsX];
+  const int tx = threadIdx.x % kAaThreadsX, ty = threadIdx.x / kAaThreadsX;
+  const int col = blockIdx.x * kAaTileX + tx - 1, row = blockIdx.y * kAaTileY + ty - 1;
+  const long long b = blockIdx.z;
+  const bool in_image = col >= 0 && col < a.width && row >= 0 && row < a.height;
+  float2 h = make_float2(0.f, 0.f), v = make_float2(0.f, 0.f);
+  if (in_image && ty >= 1 && col + 1 < a.width) {
     const Pair r = eval_pair(a, b, row, col, true);
-    k[0] = r.bp;
-    other[0] = p + 1;
+    h = make_float2(r.bp, r.bq);
   }
-  if (col > 0) {
-    const Pair r = eval_pair(a, b, row, col - 1, true);
-    k[1] = r.bq;
-    other[1] = p - 1;
-  }
-  if (row + 1 < a.height) {
+  if (in_image && tx >= 1 && row + 1 < a.height) {
     const Pair r = eval_pair(a, b, row, col, false);
-    k[2] = r.bp;
-    other[2] = p + a.width;
+    v = make_float2(r.bp, r.bq);
   }
-  if (row > 0) {
-    const Pair r = eval_pair(a, b, row - 1, col, false);
-    k[3] = r.bq;
-    other[3] = p - a.width;
-  }
+  hk[ty][tx] = h;
+  vk[ty][tx] = v;
+  __syncthreads();
+  if (!in_image || tx < 1 || ty < 1) return;
+  const long long p = (b * a.height + row) * a.width + col;
+  // Blend coefficients and partners, in the reference's accumulation order: right pair (this
+  // pixel first), left pair (second), lower pair (first), upper pair (second).
+  const float k[4] = {hk[ty][tx].x, hk[ty][tx - 1].y, vk[ty][tx].x, vk[ty - 1][tx].y};
+  const long long other[4] = {p + 1, p - 1, p + a.width, p - a.width};
   const int C = a.channels;
   for (int c = 0; c < C; ++c) {
     const float self = __ldg(a.color + p * C + c);
@@ -278,55 +279,40 @@ __device__ __forceinline__ void add_edge_gradient(const AaCtx& a, float* grad_po
   red_add_v4(grad_pos + (base + v.idx[j]) * 4, gx_j, gy_j, 0.0f, gw_j);
 }
 
-__global__ void __launch_bounds__(256) aa_bwd_kernel(const AaCtx a, long long total,
+__global__ void __launch_bounds__(256) aa_bwd_kernel(const AaCtx a,
                                                      const float* __restrict__ grad_out,
                                                      float boost, float* __restrict__ grad_color,
                                                      float* __restrict__ grad_pos) {
-  const long long p = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
-  if (p >= total) return;
-  const long long hw = static_cast<long long>(a.height) * a.width;
-  const long long b = p / hw;
-  const int row = static_cast<int>((p - b * hw) / a.width);
-  const int col = static_cast<int>(p - b * hw - static_cast<long long>(row) * a.width);
+  __shared__ float2 hk[kAaThreadsY][kAaThreadsX], vk[kAaThreadsY][kAaThreadsX];
+  const int tx = threadIdx.x % kAaThreadsX, ty = threadIdx.x / kAaThreadsX;
+  const int col = blockIdx.x * kAaTileX + tx - 1, row = blockIdx.y * kAaTileY + ty - 1;
+  const long long b = blockIdx.z;
+  const bool in_image = col >= 0 && col < a.width && row >= 0 && row < a.height;
+  const bool interior = in_image && tx >= 1 && ty >= 1;
   const long long pb = a.pos_batch == 1 ? 0 : b;
+  const long long p = (b * a.height + row) * a.width + col;
   const int C = a.channels;
-  // As the first pixel of a pair P = p: grad_color[p] += -bp g[p] + bq g[q]; as the second pixel
-  // Q = p of a pair (P, p): grad_color[p] += bp g[P] - bq g[p].
-  float kp[4] = {0.f, 0.f, 0.f, 0.f}, kq[4] = {0.f, 0.f, 0.f, 0.f};
-  long long other[4] = {p, p, p, p};
   Pair own[2];
   own[0].active = own[1].active = false;
-  if (col + 1 < a.width) {
-    own[0] = eval_pair(a, b, row, col, true);
-    kp[0] = -own[0].bp;
-    kq[0] = own[0].bq;
-    other[0] = p + 1;
-  }
-  if (col > 0) {
-    const Pair r = eval_pair(a, b, row, col - 1, true);
-    kp[1] = -r.bq;
-    kq[1] = r.bp;
-    other[1] = p - 1;
-  }
-  if (row + 1 < a.height) {
-    own[1] = eval_pair(a, b, row, col, false);
-    kp[2] = -own[1].bp;
-    kq[2] = own[1].bq;
-    other[2] = p + a.width;
-  }
-  if (row > 0) {
-    const Pair r = eval_pair(a, b, row - 1, col, false);
-    kp[3] = -r.bq;
-    kq[3] = r.bp;
-    other[3] = p - a.width;
-  }
+  own[0].bp = own[0].bq = own[1].bp = own[1].bq = 0.0f;
+  if (in_image && ty >= 1 && col + 1 < a.width) own[0] = eval_pair(a, b, row, col, true);
+  if (in_image && tx >= 1 && row + 1 < a.height) own[1] = eval_pair(a, b, row, col, false);
+  hk[ty][tx] = make_float2(own[0].bp, own[0].bq);
+  vk[ty][tx] = make_float2(own[1].bp, own[1].bq);
+  __syncthreads();
+  if (!interior) return;
+  // As the first pixel of a pair (P = p, Q): grad_color[p] += -bp g[p] + bq g[Q]; as the second
+  // pixel of a pair (P, Q = p): grad_color[p] += bp g[P] - bq g[p].
+  const float2 right = hk[ty][tx], left = hk[ty][tx - 1], down = vk[ty][tx], up = vk[ty - 1][tx];
+  const float kp[4] = {-right.x, -left.y, -down.x, -up.y};
+  const float kq[4] = {right.y, left.x, down.y, up.x};
+  const long long other[4] = {p + 1, p - 1, p + a.width, p - a.width};
   float grad_t[2] = {0.f, 0.f};
   for (int c = 0; c < C; ++c) {
     const float g_self = grad_out[p * C + c];
     float value = g_self;
     for (int i = 0; i < 4; ++i) {
-      if (kp[i] != 0.0f || kq[i] != 0.0f)
-        value += kp[i] * g_self + kq[i] * grad_out[other[i] * C + c];
+      if (kp[i] != 0.0f || kq[i] != 0.0f) value += kp[i] * g_self + kq[i] * grad_out[other[i] * C + c];
     }
     grad_color[p * C + c] = value;
     for (int d = 0; d < 2; ++d) {
@@ -337,6 +323,8 @@ __global__ void __launch_bounds__(256) aa_bwd_kernel(const AaCtx a, long long to
       grad_t[d] += own[d].t < 0.5f ? -g_self * (c_q - c_p) : grad_out[q * C + c] * (c_p - c_q);
     }
   }
+  // The pairs whose first pixel is interior here are owned by this block: scatter their
+  // position gradients once.
   for (int d = 0; d < 2; ++d) {
     if (!own[d].active) continue;
     const float g = grad_t[d] * boost;
@@ -460,7 +448,9 @@ extern "C" int dr_antialias_fwd(const float* color, const float* rast, const flo
   }
   const AaCtx a = make_ctx(color, rast, pos, pos_batch, num_vert, tri, num_tri, neighbours, height,
                            width, channels);
-  aa_fwd_kernel<<<blocks_for(total, 256), 256, 0, as_stream(stream)>>>(a, total, out);
+  if (batch > 65535) return DR_ERR_TOO_LARGE;
+  const dim3 grid((width + kAaTileX - 1) / kAaTileX, (height + kAaTileY - 1) / kAaTileY, batch);
+  aa_fwd_kernel<<<grid, 256, 0, as_stream(stream)>>>(a, out);
   return launch_status();
 }
 
@@ -483,7 +473,9 @@ extern "C" int dr_antialias_bwd(const float* color, const float* rast, const flo
   }
   const AaCtx a = make_ctx(color, rast, pos, pos_batch, num_vert, tri, num_tri, neighbours, height,
                            width, channels);
-  aa_bwd_kernel<<<blocks_for(total, 256), 256, 0, as_stream(stream)>>>(a, total, grad_out,
+  if (batch > 65535) return DR_ERR_TOO_LARGE;
+  const dim3 grid((width + kAaTileX - 1) / kAaTileX, (height + kAaTileY - 1) / kAaTileY, batch);
+  aa_bwd_kernel<<<grid, 256, 0, as_stream(stream)>>>(a, grad_out,
                                                                         pos_gradient_boost,
                                                                         grad_color, grad_pos);
   return launch_status();

@@ -272,10 +272,47 @@ __device__ __forceinline__ Footprint bilinear_footprint(const Levels& L, int l, 
   f.fx = sub(x, x0);
   f.fy = sub(y, y0);
   const int col = static_cast<int>(x0), row = static_cast<int>(y0);
-  f.off[0] = texel_offset<B>(L, l, view, face, row, col, channels, f.ok[0]);
-  f.off[1] = texel_offset<B>(L, l, view, face, row, col + 1, channels, f.ok[1]);
-  f.off[2] = texel_offset<B>(L, l, view, face, row + 1, col, channels, f.ok[2]);
-  f.off[3] = texel_offset<B>(L, l, view, face, row + 1, col + 1, channels, f.ok[3]);
+  if (B == DR_BOUNDARY_CUBE) {
+    f.off[0] = texel_offset<B>(L, l, view, face, row, col, channels, f.ok[0]);
+    f.off[1] = texel_offset<B>(L, l, view, face, row, col + 1, channels, f.ok[1]);
+    f.off[2] = texel_offset<B>(L, l, view, face, row + 1, col, channels, f.ok[2]);
+    f.off[3] = texel_offset<B>(L, l, view, face, row + 1, col + 1, channels, f.ok[3]);
+  } else {
+    // The two columns and two rows are resolved once each (one modulo per axis when wrapping).
+    const int w = L.w[l], h = L.h[l];
+    int c0, c1, r0, r1;
+    bool okc0 = true, okc1 = true, okr0 = true, okr1 = true;
+    if (B == DR_BOUNDARY_WRAP) {
+      c0 = col % w;
+      c0 += c0 < 0 ? w : 0;
+      c1 = c0 + 1 == w ? 0 : c0 + 1;
+      r0 = row % h;
+      r0 += r0 < 0 ? h : 0;
+      r1 = r0 + 1 == h ? 0 : r0 + 1;
+    } else {
+      if (B == DR_BOUNDARY_ZERO) {
+        okc0 = col >= 0 && col < w;
+        okc1 = col + 1 >= 0 && col + 1 < w;
+        okr0 = row >= 0 && row < h;
+        okr1 = row + 1 >= 0 && row + 1 < h;
+      }
+      c0 = min(max(col, 0), w - 1);
+      c1 = min(max(col + 1, 0), w - 1);
+      r0 = min(max(row, 0), h - 1);
+      r1 = min(max(row + 1, 0), h - 1);
+    }
+    const long long base = view * L.bstride[l];
+    const long long row0 = base + static_cast<long long>(r0) * w * channels;
+    const long long row1 = base + static_cast<long long>(r1) * w * channels;
+    f.off[0] = row0 + static_cast<long long>(c0) * channels;
+    f.off[1] = row0 + static_cast<long long>(c1) * channels;
+    f.off[2] = row1 + static_cast<long long>(c0) * channels;
+    f.off[3] = row1 + static_cast<long long>(c1) * channels;
+    f.ok[0] = okr0 && okc0;
+    f.ok[1] = okr0 && okc1;
+    f.ok[2] = okr1 && okc0;
+    f.ok[3] = okr1 && okc1;
+  }
   f.missing = f.dmiss_dx = f.dmiss_dy = 0.0f;
   if (B == DR_BOUNDARY_CUBE) {
     const int w = L.w[l], h = L.h[l];
@@ -559,16 +596,28 @@ __global__ void __launch_bounds__(256) texture_bwd_kernel(
           (static_cast<unsigned long long>(taps.level[t]) << 48) | static_cast<unsigned long long>(taps.off[t]);
       slot[t] = taps.w[t] != 0.0f ? table_slot(tb, key) : -2;
     }
-    for (int cc = 0; cc < group; ++cc) {
-      const float g = live ? grad_out[p * channels + c0 + cc] : 0.0f;
-      if (g == 0.0f) continue;
-      for (int t = 0; t < taps.n; ++t) {
-        const float value = g * taps.w[t];
-        if (slot[t] >= 0) {
-          atomicAdd(&tb.val[slot[t] * kTexGroup + cc], value);
-        } else if (slot[t] == -1) {
-          red_add(L.grad[taps.level[t]] + taps.off[t] + c0 + cc, value);
-        }
+    float g[kTexGroup];
+    for (int cc = 0; cc < kTexGroup; ++cc)
+      g[cc] = live && cc < group ? grad_out[p * channels + c0 + cc] : 0.0f;
+    // Tap by tap, lanes that add into the same slot sum first (background pixels all read the
+    // same few texels), so one lane per slot issues the shared-memory atomics.
+    const unsigned lane = threadIdx.x & 31u;
+    for (int t = 0; t < 8; ++t) {
+      const bool act = t < taps.n && slot[t] != -2;
+      const unsigned any = __ballot_sync(0xffffffffu, act);
+      if (any == 0u) continue;
+      // A lane without a slot adds to global memory on its own: give it a key nobody shares.
+      const int key = act ? (slot[t] >= 0 ? slot[t] : -1 - static_cast<int>(lane)) : 0;
+      unsigned peers = 1u << lane;
+      if (act) peers = __match_any_sync(any, key);
+      float v[kTexGroup];
+      for (int cc = 0; cc < kTexGroup; ++cc) v[cc] = act ? g[cc] * taps.w[t] : 0.0f;
+      segmented_sum<kTexGroup>(peers, v);
+      if (!act || (peers & ((1u << lane) - 1u)) != 0u) continue;
+      for (int cc = 0; cc < group; ++cc) {
+        if (v[cc] == 0.0f) continue;
+        if (slot[t] >= 0) atomicAdd(&tb.val[slot[t] * kTexGroup + cc], v[cc]);
+        else red_add(L.grad[taps.level[t]] + taps.off[t] + c0 + cc, v[cc]);
       }
     }
     __syncthreads();
