@@ -3,10 +3,12 @@
 // Visibility (result identical to diffrast's reference, backends/reference.py:368-397):
 //   1. setup_kernel, one thread per (view, triangle): culls and bounds the triangle in pixels.
 //      Triangles whose box holds at most kWarpPixels pixels are rasterized by the warp directly:
-//      a warp prefix sum numbers the (triangle, pixel) items of all of them, the triangles are
-//      staged in shared memory and the 32 lanes take the items 32 at a time, so small and medium
-//      triangles cost work in proportion to their boxes with no divergence. Keys are merged with
-//      64-bit atomicMin. Larger triangles are appended (warp-aggregated) to a list.
+//      a warp prefix sum numbers their (row, 8-column segment) work items, the triangles are
+//      staged in shared memory and the 32 lanes take the items 32 at a time. Each item first
+//      bounds its row by the projected triangle's half-planes, widened by a safety margin, and
+//      runs the exact test only on the pixels in that span, so thin diagonal triangles do not pay
+//      for their whole bounding box. Keys are merged with 64-bit atomicMin. Larger triangles are
+//      appended (warp-aggregated) to a list.
 //   2. Device-side binning without host round trips beyond one counter read: per-tile counts,
 //      one exclusive scan (pair offsets and 256-triangle work items), and a scatter into per-tile
 //      triangle lists.
@@ -110,11 +112,16 @@ __device__ __forceinline__ void pixel_range(float lo, float hi, int size, int& f
   last = static_cast<int>(l);
 }
 
-// Triangles a warp rasterizes directly, staged so that any lane can work on any of them.
+// Direct triangles of a warp, staged so that any lane can work on any of them (structure of
+// arrays, indexed by the triangle's rank among the warp's direct triangles).
 struct WarpTris {
-  float4 v[3][32];
-  int t[32], b[32], c0[32], r0[32], bw[32], end[32];
+  float4 v[3][32];     // clip-space vertices, for the exact test
+  float4 edge[3][32];  // NDC half-planes (A, B, C, D): inside where A x + B y + C >= -D
+  int t[32], b[32], c0[32], c1[32], r0[32], nseg[32], spans[32], end[32];
 };
+
+// Column segment width of the direct work items.
+constexpr int kSegment = 8;
 
 __global__ void __launch_bounds__(256) setup_kernel(
     const float* __restrict__ pos, const int* __restrict__ tri, int num_vert, int num_tri,
@@ -125,11 +132,11 @@ __global__ void __launch_bounds__(256) setup_kernel(
   const long long g = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   const unsigned lane = threadIdx.x & 31u;
   WarpTris& w = staged[threadIdx.x >> 5];
-  bool large = false;
+  bool large = false, direct = false;
   unsigned pairs = 0;
-  int items = 0;
   int b = 0, t = 0, c0 = 0, c1 = -1, r0 = 0, r1 = -1;
   Vert v0 = {0.f, 0.f, 0.f, 1.f}, v1 = v0, v2 = v0;
+  float nx[3] = {0.f, 0.f, 0.f}, ny[3] = {0.f, 0.f, 0.f};
   if (g < total) {
     b = static_cast<int>(g / num_tri);
     t = static_cast<int>(g - static_cast<long long>(b) * num_tri);
@@ -156,15 +163,19 @@ __global__ void __launch_bounds__(256) setup_kernel(
       r0 = 0;
       r1 = height - 1;
       if (in_front) {
-        const float nx0 = v0.x / v0.w, nx1 = v1.x / v1.w, nx2 = v2.x / v2.w;
-        const float ny0 = v0.y / v0.w, ny1 = v1.y / v1.w, ny2 = v2.y / v2.w;
-        pixel_range(fminf(fminf(nx0, nx1), nx2), fmaxf(fmaxf(nx0, nx1), nx2), width, c0, c1);
-        pixel_range(fminf(fminf(ny0, ny1), ny2), fmaxf(fmaxf(ny0, ny1), ny2), height, r0, r1);
+        nx[0] = v0.x / v0.w;
+        nx[1] = v1.x / v1.w;
+        nx[2] = v2.x / v2.w;
+        ny[0] = v0.y / v0.w;
+        ny[1] = v1.y / v1.w;
+        ny[2] = v2.y / v2.w;
+        pixel_range(fminf(fminf(nx[0], nx[1]), nx[2]), fmaxf(fmaxf(nx[0], nx[1]), nx[2]), width, c0, c1);
+        pixel_range(fminf(fminf(ny[0], ny[1]), ny[2]), fmaxf(fmaxf(ny[0], ny[1]), ny[2]), height, r0, r1);
       }
       if (c0 <= c1 && r0 <= r1) {
         const long long area = static_cast<long long>(c1 - c0 + 1) * (r1 - r0 + 1);
         if (in_front && area <= kWarpPixels) {
-          items = static_cast<int>(area);
+          direct = true;
         } else {
           large = true;
           const unsigned tx0 = c0 / kTile, tx1 = c1 / kTile, ty0 = r0 / kTile, ty1 = r1 / kTile;
@@ -173,43 +184,98 @@ __global__ void __launch_bounds__(256) setup_kernel(
       }
     }
   }
-  // Direct rasterization, load-balanced over the warp: the (triangle, pixel) items of all its
-  // direct triangles are numbered by a prefix sum and the lanes take them 32 at a time.
-  w.v[0][lane] = make_float4(v0.x, v0.y, v0.z, v0.w);
-  w.v[1][lane] = make_float4(v1.x, v1.y, v1.z, v1.w);
-  w.v[2][lane] = make_float4(v2.x, v2.y, v2.z, v2.w);
-  w.t[lane] = t;
-  w.b[lane] = b;
-  w.c0[lane] = c0;
-  w.r0[lane] = r0;
-  w.bw[lane] = c1 - c0 + 1;
+  // Stage the direct triangles in rank order. A triangle's work items are its rows times its
+  // 8-column segments; each item tests only the pixels of its segment that lie in the row's
+  // conservative span (below).
+  const unsigned direct_mask = __ballot_sync(0xffffffffu, direct);
+  const int rank = __popc(direct_mask & ((1u << lane) - 1u));
+  const int nseg = (c1 - c0 + kSegment) / kSegment;
+  const int items = direct ? (r1 - r0 + 1) * nseg : 0;
   int end = items;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const int y = __shfl_up_sync(0xffffffffu, end, o);
     if (static_cast<int>(lane) >= o) end += y;
   }
-  w.end[lane] = end;
   const int all_items = __shfl_sync(0xffffffffu, end, 31);
-  __syncwarp();
-  for (int item = static_cast<int>(lane); item < all_items; item += 32) {
-    // Owner: the first lane whose items end after this one.
-    int lo = 0, hi = 31;
-    while (lo < hi) {
-      const int mid = (lo + hi) >> 1;
-      if (w.end[mid] > item) hi = mid; else lo = mid + 1;
+  if (direct) {
+    w.v[0][rank] = make_float4(v0.x, v0.y, v0.z, v0.w);
+    w.v[1][rank] = make_float4(v1.x, v1.y, v1.z, v1.w);
+    w.v[2][rank] = make_float4(v2.x, v2.y, v2.z, v2.w);
+    w.t[rank] = t;
+    w.b[rank] = b;
+    w.c0[rank] = c0;
+    w.c1[rank] = c1;
+    w.r0[rank] = r0;
+    w.nseg[rank] = nseg;
+    w.end[rank] = end;
+    // Half-planes of the projected triangle, oriented inwards and widened by a margin that
+    // covers the rounding of x / w and of the exact homogeneous test many times over. A triangle
+    // whose projected orientation is not clear-cut keeps whole bounding-box rows.
+    const float ex = (nx[1] - nx[0]) * (ny[2] - ny[0]), ey = (ny[1] - ny[0]) * (nx[2] - nx[0]);
+    const float area2 = ex - ey;
+    const bool spans = fabsf(area2) > 1e-3f * (fabsf(ex) + fabsf(ey));
+    w.spans[rank] = spans ? 1 : 0;
+    const float o = area2 > 0.0f ? 1.0f : -1.0f;
+    const float size = static_cast<float>(max(width, height));
+    const float delta = (0.01f + size * 1e-6f) * 2.0f / static_cast<float>(min(width, height));
+    for (int k = 0; k < 3; ++k) {
+      const int i = (k + 1) % 3, j = (k + 2) % 3;
+      const float A = -o * (ny[j] - ny[i]), B = o * (nx[j] - nx[i]);
+      const float C = -(A * nx[i] + B * ny[i]);
+      const float D = delta * sqrtf(A * A + B * B) +
+                      4e-6f * (fabsf(A) + fabsf(B)) * (1.0f + fabsf(nx[i]) + fabsf(ny[i]));
+      w.edge[k][rank] = make_float4(A, B, C, D);
     }
-    const int local = item - (lo > 0 ? w.end[lo - 1] : 0);
-    const int bw = w.bw[lo];
-    const int row = w.r0[lo] + local / bw, col = w.c0[lo] + local % bw;
-    const float4 a = w.v[0][lo], bb = w.v[1][lo], cc = w.v[2][lo];
-    const long long key = coverage_key({a.x, a.y, a.z, a.w}, {bb.x, bb.y, bb.z, bb.w},
-                                       {cc.x, cc.y, cc.z, cc.w}, __ldg(centres + col),
-                                       __ldg(centres + width + row), w.t[lo]);
-    if (key == kEmptyKey) continue;
-    const long long off = (static_cast<long long>(w.b[lo]) * height + row) * width + col;
-    if (prev != nullptr && !(key > __ldg(prev + off))) continue;
-    atomicMin(keys + off, key);
+  }
+  __syncwarp();
+  int done = 0;  // direct triangles whose items all precede this iteration's first item
+  for (int base = 0; base < all_items; base += 32) {
+    // Bit e - base - 1 marks a triangle whose items end at e within (base, base + 32]; the
+    // owner of item base + lane is the number of triangles ending at or before it.
+    unsigned bit = 0u;
+    if (direct && end > base && end <= base + 32) bit = 1u << (end - base - 1);
+    const unsigned ends = __reduce_or_sync(0xffffffffu, bit);
+    const int item = base + static_cast<int>(lane);
+    const int k = done + __popc(ends & ((1u << lane) - 1u));
+    done += __popc(ends);
+    if (item >= all_items) continue;
+    const int local = item - (k > 0 ? w.end[k - 1] : 0);
+    const int segs = w.nseg[k];
+    const int row_off = segs == 1 ? local : local / segs;
+    const int seg = local - row_off * segs;
+    const int row = w.r0[k] + row_off;
+    const int first = w.c0[k] + seg * kSegment;
+    int cl = first, cr = min(first + kSegment - 1, w.c1[k]);
+    const float py = __ldg(centres + width + row);
+    if (w.spans[k]) {
+      float lo = -__int_as_float(0x7f800000), hi = __int_as_float(0x7f800000);
+      bool empty = false;
+      for (int e = 0; e < 3; ++e) {
+        const float4 h = w.edge[e][k];
+        const float rhs = -(h.y * py + h.z) - h.w;
+        if (h.x > 0.0f) lo = fmaxf(lo, rhs / h.x);
+        else if (h.x < 0.0f) hi = fminf(hi, rhs / h.x);
+        else empty |= rhs > 0.0f;
+      }
+      if (empty || !(lo <= hi)) continue;
+      int sl, sr;
+      pixel_range(lo, hi, width, sl, sr);
+      cl = max(cl, sl);
+      cr = min(cr, sr);
+    }
+    if (cl > cr) continue;
+    const float4 a = w.v[0][k], bb = w.v[1][k], cc = w.v[2][k];
+    const Vert va = {a.x, a.y, a.z, a.w}, vb = {bb.x, bb.y, bb.z, bb.w}, vc = {cc.x, cc.y, cc.z, cc.w};
+    const int tt = w.t[k];
+    const long long row_base = (static_cast<long long>(w.b[k]) * height + row) * width;
+    for (int col = cl; col <= cr; ++col) {
+      const long long key = coverage_key(va, vb, vc, __ldg(centres + col), py, tt);
+      if (key == kEmptyKey) continue;
+      const long long off = row_base + col;
+      if (prev != nullptr && !(key > __ldg(prev + off))) continue;
+      atomicMin(keys + off, key);
+    }
   }
   // Warp-aggregated append of the large triangles and of their pair counts.
   const unsigned mask = __ballot_sync(0xffffffffu, large);
