@@ -125,11 +125,10 @@ struct Crossing {
 
 // reference.py:675-727 for one pixel pair side: triangle t seen at src, followed towards dst.
 __device__ __forceinline__ Crossing crossing(const AaCtx& a, long long pb, int t, float sx,
-                                             float sy, float dx, float dy, bool horizontal,
-                                             Tri2& v) {
+                                             float sy, float dx, float dy, bool horizontal) {
   Crossing r = {false, 0.0f, 0};
   if (t < 0) return r;
-  v = load_tri(a, pb, t);
+  const Tri2 v = load_tri(a, pb, t);
   float es[3], ed[3];
   for (int k = 0; k < 3; ++k) {
     es[k] = edge_fn(v, k, sx, sy);
@@ -171,7 +170,6 @@ struct Pair {
   float t, bp, bq;
   int owner, edge;
   float sx, sy, dx, dy;  // crossing measured from (sx, sy) towards (dx, dy)
-  Tri2 v;                // owner triangle
 };
 
 // Pair of pixel P = (row, col) and its right (horizontal) or lower neighbour Q in view b.
@@ -190,9 +188,8 @@ __device__ __forceinline__ Pair eval_pair(const AaCtx& a, long long b, int row, 
   const long long pb = a.pos_batch == 1 ? 0 : b;
   const float xp = pixel_centre(col, a.width), yp = pixel_centre(row, a.height);
   const float xq = pixel_centre(col_q, a.width), yq = pixel_centre(row_q, a.height);
-  Tri2 vp, vq;
-  const Crossing cp = crossing(a, pb, id_p, xp, yp, xq, yq, horizontal, vp);
-  const Crossing cq = crossing(a, pb, id_q, xq, yq, xp, yp, horizontal, vq);
+  const Crossing cp = crossing(a, pb, id_p, xp, yp, xq, yq, horizontal);
+  const Crossing cq = crossing(a, pb, id_q, xq, yq, xp, yp, horizontal);
   r.use_p = cp.found && (!cq.found || rp.z <= rq.z);
   const bool use_q = cq.found && !r.use_p;
   r.active = r.use_p || use_q;
@@ -201,7 +198,6 @@ __device__ __forceinline__ Pair eval_pair(const AaCtx& a, long long b, int row, 
   if (r.t < 0.5f) r.bp = sub(0.5f, r.t); else r.bq = sub(r.t, 0.5f);
   r.owner = r.use_p ? id_p : id_q;
   r.edge = r.use_p ? cp.edge : cq.edge;
-  r.v = r.use_p ? vp : vq;
   r.sx = r.use_p ? xp : xq;
   r.sy = r.use_p ? yp : yq;
   r.dx = r.use_p ? xq : xp;
@@ -217,7 +213,7 @@ __device__ __forceinline__ Pair eval_pair(const AaCtx& a, long long b, int row, 
 constexpr int kAaThreadsX = 32, kAaThreadsY = 8;
 constexpr int kAaTileX = kAaThreadsX - 1, kAaTileY = kAaThreadsY - 1;
 
-__global__ void __launch_bounds__(256) aa_fwd_kernel(const AaCtx a, float* __restrict__ out) {
+__global__ void __launch_bounds__(256, 4) aa_fwd_kernel(const AaCtx a, float* __restrict__ out) {
   __shared__ float2 hk[kAaThreadsY][kAaThreadsX], vk[kAaThreadsY][kAaThreadsX];
   const int tx = threadIdx.x % kAaThreadsX, ty = threadIdx.x / kAaThreadsX;
   const int col = blockIdx.x * kAaTileX + tx - 1, row = blockIdx.y * kAaTileY + ty - 1;
@@ -257,7 +253,7 @@ __global__ void __launch_bounds__(256) aa_fwd_kernel(const AaCtx a, float* __res
 __device__ __forceinline__ void add_edge_gradient(const AaCtx& a, float* grad_pos, long long pb,
                                                   const Pair& r, float grad_t) {
   const int i = (r.edge + 1) % 3, j = (r.edge + 2) % 3;
-  const Tri2& v = r.v;
+  const Tri2 v = load_tri(a, pb, r.owner);
   const float ai_s = v.x[i] - r.sx * v.w[i], aj_s = v.x[j] - r.sx * v.w[j];
   const float ci_s = v.y[i] - r.sy * v.w[i], cj_s = v.y[j] - r.sy * v.w[j];
   const float ai_d = v.x[i] - r.dx * v.w[i], aj_d = v.x[j] - r.dx * v.w[j];
@@ -279,7 +275,7 @@ __device__ __forceinline__ void add_edge_gradient(const AaCtx& a, float* grad_po
   red_add_v4(grad_pos + (base + v.idx[j]) * 4, gx_j, gy_j, 0.0f, gw_j);
 }
 
-__global__ void __launch_bounds__(256) aa_bwd_kernel(const AaCtx a,
+__global__ void __launch_bounds__(256, 4) aa_bwd_kernel(const AaCtx a,
                                                      const float* __restrict__ grad_out,
                                                      float boost, float* __restrict__ grad_color,
                                                      float* __restrict__ grad_pos) {

@@ -465,33 +465,56 @@ __device__ __forceinline__ void prepare(const Levels& L, int channels, const flo
   }
 }
 
+// Copies `count` floats from shared memory to contiguous `dst`, with 16-byte stores where the
+// address allows.
+__device__ __forceinline__ void store_block(float* __restrict__ dst, const float* __restrict__ src,
+                                            int count) {
+  if ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+    const int vec = count / 4;
+    for (int i = threadIdx.x; i < vec; i += blockDim.x)
+      reinterpret_cast<float4*>(dst)[i] = reinterpret_cast<const float4*>(src)[i];
+    for (int i = vec * 4 + threadIdx.x; i < count; i += blockDim.x) dst[i] = src[i];
+  } else {
+    for (int i = threadIdx.x; i < count; i += blockDim.x) dst[i] = src[i];
+  }
+}
+
+// One thread per pixel; with `staged` the block's 256 output pixels (one contiguous range) go
+// through shared memory so that the global stores are coalesced float4s.
 template <int MODE, int B>
 __global__ void __launch_bounds__(256) texture_fwd_kernel(
     const Levels L, int channels, const float* __restrict__ uv, const float* __restrict__ uv_da,
     const float* __restrict__ bias, long long total, long long pixels_per_image,
-    float* __restrict__ out) {
-  const long long p = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
-  if (p >= total) return;
-  const long long view = p / pixels_per_image;
-  Lookup<MODE, B> k;
-  prepare<MODE, B>(L, channels, uv, uv_da, bias, p, view, k);
-  float* o = out + p * channels;
-  for (int c = 0; c < channels; ++c) {
-    float value;
-    if (MODE == DR_FILTER_NEAREST) {
-      value = k.near_ok ? __ldg(L.ptr[0] + k.near_off + c) : 0.0f;
-    } else {
-      float t[4];
-      value = bilinear_value<B>(L.ptr[k.lo], k.f_lo, c, t);
-      if (MODE == DR_FILTER_LINEAR_MIPMAP_LINEAR) {
-        const float above = bilinear_value<B>(L.ptr[k.hi], k.f_hi, c, t);
-        value = add(mul(value, sub(1.0f, k.frac)), mul(above, k.frac));
+    float* __restrict__ out, bool staged) {
+  extern __shared__ float stage[];
+  const long long first = blockIdx.x * static_cast<long long>(blockDim.x);
+  const long long p = first + threadIdx.x;
+  float* o = staged ? stage + threadIdx.x * channels : out + p * channels;
+  if (p < total) {
+    const long long view = p / pixels_per_image;
+    Lookup<MODE, B> k;
+    prepare<MODE, B>(L, channels, uv, uv_da, bias, p, view, k);
+    for (int c = 0; c < channels; ++c) {
+      float value;
+      if (MODE == DR_FILTER_NEAREST) {
+        value = k.near_ok ? __ldg(L.ptr[0] + k.near_off + c) : 0.0f;
+      } else {
+        float t[4];
+        value = bilinear_value<B>(L.ptr[k.lo], k.f_lo, c, t);
+        if (MODE == DR_FILTER_LINEAR_MIPMAP_LINEAR) {
+          const float above = bilinear_value<B>(L.ptr[k.hi], k.f_hi, c, t);
+          value = add(mul(value, sub(1.0f, k.frac)), mul(above, k.frac));
+        }
       }
+      if (k.bad) value = kNaN;
+      if (!k.valid) value = 0.0f;
+      o[c] = value;
     }
-    if (k.bad) value = kNaN;
-    if (!k.valid) value = 0.0f;
-    o[c] = value;
   }
+  if (!staged) return;
+  __syncthreads();
+  const int pixels = static_cast<int>(min(static_cast<long long>(blockDim.x), total - first));
+  store_block(out + first * channels, stage, pixels * channels);
 }
 
 // Texel-gradient staging: a 16x16 pixel tile adds its contributions into a shared-memory hash
@@ -786,8 +809,10 @@ __global__ void __launch_bounds__(256) mip_down_bwd_kernel(const float* __restri
 template <int MODE, int B>
 void launch_fwd(const Levels& L, int channels, const float* uv, const float* uv_da,
                 const float* bias, long long total, long long ppi, float* out, cudaStream_t s) {
-  texture_fwd_kernel<MODE, B><<<blocks_for(total, 256), 256, 0, s>>>(L, channels, uv, uv_da, bias,
-                                                                      total, ppi, out);
+  const size_t stage_bytes = sizeof(float) * 256 * static_cast<size_t>(channels);
+  const bool staged = stage_bytes <= 48 * 1024;
+  texture_fwd_kernel<MODE, B><<<blocks_for(total, 256), 256, staged ? stage_bytes : 0, s>>>(
+      L, channels, uv, uv_da, bias, total, ppi, out, staged);
 }
 
 template <int MODE, int B>
