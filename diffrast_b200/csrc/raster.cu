@@ -3,12 +3,12 @@
 // Visibility (result identical to diffrast's reference, backends/reference.py:368-397):
 //   1. setup_kernel, one thread per (view, triangle): culls and bounds the triangle in pixels.
 //      Triangles whose box holds at most kWarpPixels pixels are rasterized by the warp directly:
-//      a warp prefix sum numbers their (row, 8-column segment) work items, the triangles are
-//      staged in shared memory and the 32 lanes take the items 32 at a time. Each item first
-//      bounds its row by the projected triangle's half-planes, widened by a safety margin, and
-//      runs the exact test only on the pixels in that span, so thin diagonal triangles do not pay
-//      for their whole bounding box. Keys are merged with 64-bit atomicMin. Larger triangles are
-//      appended (warp-aggregated) to a list.
+//      the triangles are staged in shared memory, their rows are handed out to the lanes 32 at a
+//      time (warp prefix sums), each lane bounds its row by the projected triangle's half-planes
+//      widened by a safety margin, and the pixels inside those spans are handed out to the lanes
+//      again, one exact test each. Thin diagonal triangles thus do not pay for their bounding box
+//      and lanes stay busy. Keys are merged with 64-bit atomicMin. Larger triangles are appended
+//      (warp-aggregated) to a list.
 //   2. Device-side binning without host round trips beyond one counter read: per-tile counts,
 //      one exclusive scan (pair offsets and 256-triangle work items), and a scatter into per-tile
 //      triangle lists.
@@ -117,11 +117,11 @@ __device__ __forceinline__ void pixel_range(float lo, float hi, int size, int& f
 struct WarpTris {
   float4 v[3][32];     // clip-space vertices, for the exact test
   float4 edge[3][32];  // NDC half-planes (A, B, C, D): inside where A x + B y + C >= -D
-  int t[32], b[32], c0[32], c1[32], r0[32], nseg[32], spans[32], end[32];
+  int t[32], b[32], c0[32], c1[32], r0[32], spans[32], end[32];
+  // Rows of the current batch that have pixels to test: triangle rank, row, first column and
+  // the inclusive prefix sum of their pixel counts.
+  int row_tri[32], row_y[32], row_col[32], row_end[32];
 };
-
-// Column segment width of the direct work items.
-constexpr int kSegment = 8;
 
 __global__ void __launch_bounds__(256) setup_kernel(
     const float* __restrict__ pos, const int* __restrict__ tri, int num_vert, int num_tri,
@@ -184,20 +184,20 @@ __global__ void __launch_bounds__(256) setup_kernel(
       }
     }
   }
-  // Stage the direct triangles in rank order. A triangle's work items are its rows times its
-  // 8-column segments; each item tests only the pixels of its segment that lie in the row's
-  // conservative span (below).
+  // Stage the direct triangles in rank order. Their rows are distributed over the lanes (phase A:
+  // each lane bounds one row by the triangle's half-planes), then the pixels inside those row
+  // spans are distributed over the lanes again (phase B: one exact test per lane), so lanes stay
+  // busy whatever the shape of the triangles.
   const unsigned direct_mask = __ballot_sync(0xffffffffu, direct);
   const int rank = __popc(direct_mask & ((1u << lane) - 1u));
-  const int nseg = (c1 - c0 + kSegment) / kSegment;
-  const int items = direct ? (r1 - r0 + 1) * nseg : 0;
-  int end = items;
+  const int rows = direct ? r1 - r0 + 1 : 0;
+  int end = rows;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const int y = __shfl_up_sync(0xffffffffu, end, o);
     if (static_cast<int>(lane) >= o) end += y;
   }
-  const int all_items = __shfl_sync(0xffffffffu, end, 31);
+  const int all_rows = __shfl_sync(0xffffffffu, end, 31);
   if (direct) {
     w.v[0][rank] = make_float4(v0.x, v0.y, v0.z, v0.w);
     w.v[1][rank] = make_float4(v1.x, v1.y, v1.z, v1.w);
@@ -207,7 +207,6 @@ __global__ void __launch_bounds__(256) setup_kernel(
     w.c0[rank] = c0;
     w.c1[rank] = c1;
     w.r0[rank] = r0;
-    w.nseg[rank] = nseg;
     w.end[rank] = end;
     // Half-planes of the projected triangle, oriented inwards and widened by a margin that
     // covers the rounding of x / w and of the exact homogeneous test many times over. A triangle
@@ -229,53 +228,84 @@ __global__ void __launch_bounds__(256) setup_kernel(
     }
   }
   __syncwarp();
-  int done = 0;  // direct triangles whose items all precede this iteration's first item
-  for (int base = 0; base < all_items; base += 32) {
-    // Bit e - base - 1 marks a triangle whose items end at e within (base, base + 32]; the
-    // owner of item base + lane is the number of triangles ending at or before it.
+  int done = 0;  // triangles whose rows all precede this batch
+  for (int base = 0; base < all_rows; base += 32) {
+    // Phase A. Bit e - base - 1 marks a triangle whose rows end at e within (base, base + 32];
+    // the owner of row item base + lane is the number of triangles ending at or before it.
     unsigned bit = 0u;
     if (direct && end > base && end <= base + 32) bit = 1u << (end - base - 1);
     const unsigned ends = __reduce_or_sync(0xffffffffu, bit);
     const int item = base + static_cast<int>(lane);
     const int k = done + __popc(ends & ((1u << lane) - 1u));
     done += __popc(ends);
-    if (item >= all_items) continue;
-    const int local = item - (k > 0 ? w.end[k - 1] : 0);
-    const int segs = w.nseg[k];
-    const int row_off = segs == 1 ? local : local / segs;
-    const int seg = local - row_off * segs;
-    const int row = w.r0[k] + row_off;
-    const int first = w.c0[k] + seg * kSegment;
-    int cl = first, cr = min(first + kSegment - 1, w.c1[k]);
-    const float py = __ldg(centres + width + row);
-    if (w.spans[k]) {
-      float lo = -__int_as_float(0x7f800000), hi = __int_as_float(0x7f800000);
-      bool empty = false;
-      for (int e = 0; e < 3; ++e) {
-        const float4 h = w.edge[e][k];
-        const float rhs = -(h.y * py + h.z) - h.w;
-        if (h.x > 0.0f) lo = fmaxf(lo, rhs / h.x);
-        else if (h.x < 0.0f) hi = fminf(hi, rhs / h.x);
-        else empty |= rhs > 0.0f;
+    int count = 0, row = 0, cl = 0;
+    if (item < all_rows) {
+      row = w.r0[k] + item - (k > 0 ? w.end[k - 1] : 0);
+      cl = w.c0[k];
+      int cr = w.c1[k];
+      if (w.spans[k]) {
+        const float py = __ldg(centres + width + row);
+        float lo = -__int_as_float(0x7f800000), hi = __int_as_float(0x7f800000);
+        bool empty = false;
+        for (int e = 0; e < 3; ++e) {
+          const float4 h = w.edge[e][k];
+          const float rhs = -(h.y * py + h.z) - h.w;
+          if (h.x > 0.0f) lo = fmaxf(lo, rhs / h.x);
+          else if (h.x < 0.0f) hi = fminf(hi, rhs / h.x);
+          else empty |= rhs > 0.0f;
+        }
+        if (empty || !(lo <= hi)) {
+          cr = cl - 1;
+        } else {
+          int sl, sr;
+          pixel_range(lo, hi, width, sl, sr);
+          cl = max(cl, sl);
+          cr = min(cr, sr);
+        }
       }
-      if (empty || !(lo <= hi)) continue;
-      int sl, sr;
-      pixel_range(lo, hi, width, sl, sr);
-      cl = max(cl, sl);
-      cr = min(cr, sr);
+      count = max(0, cr - cl + 1);
     }
-    if (cl > cr) continue;
-    const float4 a = w.v[0][k], bb = w.v[1][k], cc = w.v[2][k];
-    const Vert va = {a.x, a.y, a.z, a.w}, vb = {bb.x, bb.y, bb.z, bb.w}, vc = {cc.x, cc.y, cc.z, cc.w};
-    const int tt = w.t[k];
-    const long long row_base = (static_cast<long long>(w.b[k]) * height + row) * width;
-    for (int col = cl; col <= cr; ++col) {
-      const long long key = coverage_key(va, vb, vc, __ldg(centres + col), py, tt);
+    // Compact the rows that have pixels and number their pixels.
+    const unsigned busy = __ballot_sync(0xffffffffu, count > 0);
+    const int slot = __popc(busy & ((1u << lane) - 1u));
+    int pix_end = count;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, pix_end, o);
+      if (static_cast<int>(lane) >= o) pix_end += y;
+    }
+    const int all_pixels = __shfl_sync(0xffffffffu, pix_end, 31);
+    __syncwarp();
+    if (count > 0) {
+      w.row_tri[slot] = k;
+      w.row_y[slot] = row;
+      w.row_col[slot] = cl;
+      w.row_end[slot] = pix_end;
+    }
+    __syncwarp();
+    // Phase B: one exact coverage test per lane.
+    int finished = 0;
+    for (int pbase = 0; pbase < all_pixels; pbase += 32) {
+      unsigned pbit = 0u;
+      if (count > 0 && pix_end > pbase && pix_end <= pbase + 32) pbit = 1u << (pix_end - pbase - 1);
+      const unsigned pends = __reduce_or_sync(0xffffffffu, pbit);
+      const int pitem = pbase + static_cast<int>(lane);
+      const int r = finished + __popc(pends & ((1u << lane) - 1u));
+      finished += __popc(pends);
+      if (pitem >= all_pixels) continue;
+      const int kk = w.row_tri[r];
+      const int y = w.row_y[r];
+      const int col = w.row_col[r] + pitem - (r > 0 ? w.row_end[r - 1] : 0);
+      const float4 a = w.v[0][kk], bb = w.v[1][kk], cc = w.v[2][kk];
+      const long long key = coverage_key({a.x, a.y, a.z, a.w}, {bb.x, bb.y, bb.z, bb.w},
+                                         {cc.x, cc.y, cc.z, cc.w}, __ldg(centres + col),
+                                         __ldg(centres + width + y), w.t[kk]);
       if (key == kEmptyKey) continue;
-      const long long off = row_base + col;
+      const long long off = (static_cast<long long>(w.b[kk]) * height + y) * width + col;
       if (prev != nullptr && !(key > __ldg(prev + off))) continue;
       atomicMin(keys + off, key);
     }
+    __syncwarp();
   }
   // Warp-aggregated append of the large triangles and of their pair counts.
   const unsigned mask = __ballot_sync(0xffffffffu, large);
