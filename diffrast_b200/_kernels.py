@@ -217,7 +217,11 @@ def texture_fwd(levels: list[Tensor], uv: Tensor, uv_da: Tensor | None, bias: Te
 def texture_bwd(levels, uv, uv_da, bias, mode, boundary, grad_out, want_uv, want_da, want_bias):
     batch, height, width = uv.shape[:3]
     channels = levels[0].shape[-1]
-    grads = [torch.zeros_like(lv) for lv in levels]
+    # Three-channel gradients are accumulated in four-channel buffers, so that each texel takes
+    # one 16-byte vector reduction; the padding is dropped afterwards.
+    stride = 4 if channels == 3 else channels
+    grads = [torch.zeros((*lv.shape[:-1], stride), dtype=torch.float32, device=lv.device)
+             for lv in levels]
     grad_uv = torch.empty_like(uv) if want_uv else None
     grad_da = torch.empty_like(uv_da) if want_da else None
     grad_bias = torch.empty_like(bias) if want_bias else None
@@ -225,12 +229,15 @@ def texture_bwd(levels, uv, uv_da, bias, mode, boundary, grad_out, want_uv, want
     N.check(
         N.lib().dr_texture_bwd(N.pointer_array([lv.data_ptr() for lv in levels]),
                                N.pointer_array([g.data_ptr() for g in grads]), hs, ws, bs,
-                               len(levels), channels, uv.data_ptr(), N.ptr(uv_da), N.ptr(bias),
+                               len(levels), channels, stride, uv.data_ptr(), N.ptr(uv_da),
+                               N.ptr(bias),
                                batch, height, width, mode, boundary, grad_out.data_ptr(),
                                N.ptr(grad_uv), N.ptr(grad_da), N.ptr(grad_bias),
                                N.stream(uv.device)),
         "dr_texture_bwd",
     )  # fmt: skip
+    if stride != channels:
+        grads = [g[..., :channels].contiguous() for g in grads]
     return grads, grad_uv, grad_da, grad_bias
 
 

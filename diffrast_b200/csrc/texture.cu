@@ -13,7 +13,8 @@
 // Levels are addressed through a table of per-level pointers passed by value, so the base level is
 // the caller's texture tensor itself and no packed copy of the mip stack is ever made. The
 // coordinate arithmetic that decides which texels are read uses explicitly rounded operations in
-// the reference's order. Texel gradients are scattered with vector-free float reductions.
+// the reference's order. Texel gradients are summed per warp and scattered with one reduction per
+// distinct texel.
 #include <cstdint>
 #include <type_traits>
 
@@ -26,7 +27,7 @@ namespace {
 struct Levels {
   const float* ptr[DR_MAX_LEVELS];
   float* grad[DR_MAX_LEVELS];
-  long long bstride[DR_MAX_LEVELS];
+  long long bstride[DR_MAX_LEVELS];  // batch stride in texels (0 when shared by all views)
   int h[DR_MAX_LEVELS];
   int w[DR_MAX_LEVELS];
   int num_levels;
@@ -246,7 +247,7 @@ __device__ __forceinline__ long long texel_offset(const Levels& L, int l, long l
   }
   long long texel = static_cast<long long>(row) * w + col;
   if (B == DR_BOUNDARY_CUBE) texel += static_cast<long long>(face) * h * w;
-  return view * L.bstride[l] + texel * channels;
+  return view * L.bstride[l] + texel;
 }
 
 struct Footprint {
@@ -302,12 +303,12 @@ __device__ __forceinline__ Footprint bilinear_footprint(const Levels& L, int l, 
       r1 = min(max(row + 1, 0), h - 1);
     }
     const long long base = view * L.bstride[l];
-    const long long row0 = base + static_cast<long long>(r0) * w * channels;
-    const long long row1 = base + static_cast<long long>(r1) * w * channels;
-    f.off[0] = row0 + static_cast<long long>(c0) * channels;
-    f.off[1] = row0 + static_cast<long long>(c1) * channels;
-    f.off[2] = row1 + static_cast<long long>(c0) * channels;
-    f.off[3] = row1 + static_cast<long long>(c1) * channels;
+    const long long row0 = base + static_cast<long long>(r0) * w;
+    const long long row1 = base + static_cast<long long>(r1) * w;
+    f.off[0] = row0 + c0;
+    f.off[1] = row0 + c1;
+    f.off[2] = row1 + c0;
+    f.off[3] = row1 + c1;
     f.ok[0] = okr0 && okc0;
     f.ok[1] = okr0 && okc1;
     f.ok[2] = okr1 && okc0;
@@ -330,8 +331,8 @@ __device__ __forceinline__ Footprint bilinear_footprint(const Levels& L, int l, 
 // Bilinear value of channel c with the reference's rounding order.
 template <int B>
 __device__ __forceinline__ float bilinear_value(const float* __restrict__ level, const Footprint& f,
-                                                int c, float t[4]) {
-  for (int k = 0; k < 4; ++k) t[k] = f.ok[k] ? __ldg(level + f.off[k] + c) : 0.0f;
+                                                int channels, int c, float t[4]) {
+  for (int k = 0; k < 4; ++k) t[k] = f.ok[k] ? __ldg(level + f.off[k] * channels + c) : 0.0f;
   const float gx = sub(1.0f, f.fx), gy = sub(1.0f, f.fy);
   float out = add(mul(gy, add(mul(gx, t[0]), mul(f.fx, t[1]))),
                   mul(f.fy, add(mul(gx, t[2]), mul(f.fx, t[3]))));
@@ -449,8 +450,7 @@ __device__ __forceinline__ void prepare(const Levels& L, int channels, const flo
       const int row = min(max(static_cast<int>(floorf(y)), 0), h - 1);
       const int col = min(max(static_cast<int>(floorf(x)), 0), w - 1);
       k.near_ok = true;
-      k.near_off = view * L.bstride[0] +
-                   ((static_cast<long long>(k.face) * h + row) * w + col) * channels;
+      k.near_off = view * L.bstride[0] + (static_cast<long long>(k.face) * h + row) * w + col;
     } else {
       k.near_off = texel_offset<B>(L, 0, view, 0, static_cast<int>(floorf(y)),
                                    static_cast<int>(floorf(x)), channels, k.near_ok);
@@ -497,12 +497,12 @@ __global__ void __launch_bounds__(256) texture_fwd_kernel(
     for (int c = 0; c < channels; ++c) {
       float value;
       if (MODE == DR_FILTER_NEAREST) {
-        value = k.near_ok ? __ldg(L.ptr[0] + k.near_off + c) : 0.0f;
+        value = k.near_ok ? __ldg(L.ptr[0] + k.near_off * channels + c) : 0.0f;
       } else {
         float t[4];
-        value = bilinear_value<B>(L.ptr[k.lo], k.f_lo, c, t);
+        value = bilinear_value<B>(L.ptr[k.lo], k.f_lo, channels, c, t);
         if (MODE == DR_FILTER_LINEAR_MIPMAP_LINEAR) {
-          const float above = bilinear_value<B>(L.ptr[k.hi], k.f_hi, c, t);
+          const float above = bilinear_value<B>(L.ptr[k.hi], k.f_hi, channels, c, t);
           value = add(mul(value, sub(1.0f, k.frac)), mul(above, k.frac));
         }
       }
@@ -515,38 +515,6 @@ __global__ void __launch_bounds__(256) texture_fwd_kernel(
   __syncthreads();
   const int pixels = static_cast<int>(min(static_cast<long long>(blockDim.x), total - first));
   store_block(out + first * channels, stage, pixels * channels);
-}
-
-// Texel-gradient staging: a 16x16 pixel tile adds its contributions into a shared-memory hash
-// table keyed by (level, texel offset), kTexGroup channels at a time, and flushes each distinct
-// texel to global memory once. Neighbouring pixels share most texels (a texel of the chosen levels
-// spans about a pixel), so this replaces heavily contended global atomics with shared-memory ones.
-// A texel that finds no free slot within kProbes probes goes straight to global memory.
-constexpr int kTexSlots = 1024;
-constexpr int kTexGroup = 4;
-constexpr int kProbes = 32;
-constexpr unsigned long long kNoTexel = ~0ull;
-
-struct TexTable {
-  unsigned long long key[kTexSlots];
-  float val[kTexSlots * kTexGroup];
-};
-
-__device__ __forceinline__ unsigned mix_key(unsigned long long x) {
-  x ^= x >> 33;
-  x *= 0xff51afd7ed558ccdull;
-  x ^= x >> 33;
-  return static_cast<unsigned>(x);
-}
-
-__device__ __forceinline__ int table_slot(TexTable& tb, unsigned long long key) {
-  unsigned h = mix_key(key) & (kTexSlots - 1);
-  for (int probe = 0; probe < kProbes; ++probe) {
-    const unsigned long long prev = atomicCAS(&tb.key[h], kNoTexel, key);
-    if (prev == kNoTexel || prev == key) return static_cast<int>(h);
-    h = (h + 1) & (kTexSlots - 1);
-  }
-  return -1;
 }
 
 // Taps of a pixel's lookup with their weights (bilinear weight times level weight, plus the
@@ -573,12 +541,17 @@ __device__ __forceinline__ void add_footprint_taps(Taps& taps, const Footprint& 
   }
 }
 
+// Texel gradients: a warp covers 16 x 2 pixels of a 16 x 16 tile, whose taps mostly land on the
+// same texels (a texel of the chosen levels spans about a pixel; background pixels all read the
+// same few). Tap by tap, lanes adding to the same texel sum their contributions with a shuffle
+// reduction and one lane issues a single reduction per texel: a 16-byte vector reduction into a
+// gradient level padded to 4 channels (grad_stride 4), scalar reductions otherwise.
 template <int MODE, int B>
 __global__ void __launch_bounds__(256) texture_bwd_kernel(
-    const Levels L, int channels, const float* __restrict__ uv, const float* __restrict__ uv_da,
-    const float* __restrict__ bias, int height, int width, const float* __restrict__ grad_out,
-    float* __restrict__ grad_uv, float* __restrict__ grad_uv_da, float* __restrict__ grad_bias) {
-  __shared__ TexTable tb;
+    const Levels L, int channels, int grad_stride, const float* __restrict__ uv,
+    const float* __restrict__ uv_da, const float* __restrict__ bias, int height, int width,
+    const float* __restrict__ grad_out, float* __restrict__ grad_uv,
+    float* __restrict__ grad_uv_da, float* __restrict__ grad_bias) {
   const int col = blockIdx.x * 16 + (threadIdx.x & 15);
   const int row = blockIdx.y * 16 + (threadIdx.x >> 4);
   const long long view = blockIdx.z;
@@ -607,53 +580,37 @@ __global__ void __launch_bounds__(256) texture_bwd_kernel(
       }
     }
   }
-  // Texel gradients, staged in shared memory per group of channels.
-  for (int c0 = 0; c0 < channels; c0 += kTexGroup) {
-    const int group = min(kTexGroup, channels - c0);
-    for (int i = threadIdx.x; i < kTexSlots; i += blockDim.x) tb.key[i] = kNoTexel;
-    for (int i = threadIdx.x; i < kTexSlots * kTexGroup; i += blockDim.x) tb.val[i] = 0.0f;
-    __syncthreads();
-    int slot[8];
-    for (int t = 0; t < taps.n; ++t) {
-      const unsigned long long key =
-          (static_cast<unsigned long long>(taps.level[t]) << 48) | static_cast<unsigned long long>(taps.off[t]);
-      slot[t] = taps.w[t] != 0.0f ? table_slot(tb, key) : -2;
-    }
-    float g[kTexGroup];
-    for (int cc = 0; cc < kTexGroup; ++cc)
+  const unsigned lane = threadIdx.x & 31u;
+  const bool vector = grad_stride == 4 && channels <= 4;
+  for (int c0 = 0; c0 < channels; c0 += 4) {
+    const int group = min(4, channels - c0);
+    float g[4];
+    bool any_g = false;
+    for (int cc = 0; cc < 4; ++cc) {
       g[cc] = live && cc < group ? grad_out[p * channels + c0 + cc] : 0.0f;
-    // Tap by tap, lanes that add into the same slot sum first (background pixels all read the
-    // same few texels), so one lane per slot issues the shared-memory atomics.
-    const unsigned lane = threadIdx.x & 31u;
+      any_g |= g[cc] != 0.0f;
+    }
     for (int t = 0; t < 8; ++t) {
-      const bool act = t < taps.n && slot[t] != -2;
+      const bool act = any_g && t < taps.n && taps.w[t] != 0.0f;
       const unsigned any = __ballot_sync(0xffffffffu, act);
       if (any == 0u) continue;
-      // A lane without a slot adds to global memory on its own: give it a key nobody shares.
-      const int key = act ? (slot[t] >= 0 ? slot[t] : -1 - static_cast<int>(lane)) : 0;
+      const unsigned long long key =
+          act ? (static_cast<unsigned long long>(taps.level[t]) << 48) | static_cast<unsigned long long>(taps.off[t])
+              : 0ull;
       unsigned peers = 1u << lane;
       if (act) peers = __match_any_sync(any, key);
-      float v[kTexGroup];
-      for (int cc = 0; cc < kTexGroup; ++cc) v[cc] = act ? g[cc] * taps.w[t] : 0.0f;
-      segmented_sum<kTexGroup>(peers, v);
+      float v[4];
+      for (int cc = 0; cc < 4; ++cc) v[cc] = act ? g[cc] * taps.w[t] : 0.0f;
+      segmented_sum<4>(peers, v);
       if (!act || (peers & ((1u << lane) - 1u)) != 0u) continue;
-      for (int cc = 0; cc < group; ++cc) {
-        if (v[cc] == 0.0f) continue;
-        if (slot[t] >= 0) atomicAdd(&tb.val[slot[t] * kTexGroup + cc], v[cc]);
-        else red_add(L.grad[taps.level[t]] + taps.off[t] + c0 + cc, v[cc]);
+      float* dst = L.grad[taps.level[t]] + taps.off[t] * grad_stride + c0;
+      if (vector) {
+        red_add_v4(dst, v[0], v[1], v[2], v[3]);
+      } else {
+        for (int cc = 0; cc < group; ++cc)
+          if (v[cc] != 0.0f) red_add(dst + cc, v[cc]);
       }
     }
-    __syncthreads();
-    for (int i = threadIdx.x; i < kTexSlots; i += blockDim.x) {
-      const unsigned long long key = tb.key[i];
-      if (key == kNoTexel) continue;
-      float* dst = L.grad[key >> 48] + static_cast<long long>(key & 0xFFFFFFFFFFFFull) + c0;
-      for (int cc = 0; cc < group; ++cc) {
-        const float v = tb.val[i * kTexGroup + cc];
-        if (v != 0.0f) red_add(dst + cc, v);
-      }
-    }
-    __syncthreads();
   }
   if (!inside) return;
   const bool coord_grads = grad_uv != nullptr || grad_uv_da != nullptr || grad_bias != nullptr;
@@ -665,7 +622,7 @@ __global__ void __launch_bounds__(256) texture_bwd_kernel(
       const float g = grad_out[p * channels + c];
       const float g_lo = MODE == DR_FILTER_LINEAR_MIPMAP_LINEAR ? g * w_lo : g;
       float t[4];
-      const float lower = bilinear_value<B>(L.ptr[k.lo], k.f_lo, c, t);
+      const float lower = bilinear_value<B>(L.ptr[k.lo], k.f_lo, channels, c, t);
       {
         const Footprint& f = k.f_lo;
         float dfx = (1.0f - f.fy) * (t[1] - t[0]) + f.fy * (t[3] - t[2]);
@@ -679,7 +636,7 @@ __global__ void __launch_bounds__(256) texture_bwd_kernel(
         g_fy_lo += g_lo * dfy;
       }
       if (MODE == DR_FILTER_LINEAR_MIPMAP_LINEAR) {
-        const float upper = bilinear_value<B>(L.ptr[k.hi], k.f_hi, c, t);
+        const float upper = bilinear_value<B>(L.ptr[k.hi], k.f_hi, channels, c, t);
         const Footprint& f = k.f_hi;
         float dfx = (1.0f - f.fy) * (t[1] - t[0]) + f.fy * (t[3] - t[2]);
         float dfy = (1.0f - f.fx) * (t[2] - t[0]) + f.fx * (t[3] - t[1]);
@@ -816,12 +773,14 @@ void launch_fwd(const Levels& L, int channels, const float* uv, const float* uv_
 }
 
 template <int MODE, int B>
-void launch_bwd(const Levels& L, int channels, const float* uv, const float* uv_da,
-                const float* bias, int batch, int height, int width, const float* grad_out,
-                float* grad_uv, float* grad_uv_da, float* grad_bias, cudaStream_t s) {
+void launch_bwd(const Levels& L, int channels, int grad_stride, const float* uv,
+                const float* uv_da, const float* bias, int batch, int height, int width,
+                const float* grad_out, float* grad_uv, float* grad_uv_da, float* grad_bias,
+                cudaStream_t s) {
   const dim3 grid((width + 15) / 16, (height + 15) / 16, batch);
-  texture_bwd_kernel<MODE, B><<<grid, 256, 0, s>>>(L, channels, uv, uv_da, bias, height, width,
-                                                  grad_out, grad_uv, grad_uv_da, grad_bias);
+  texture_bwd_kernel<MODE, B><<<grid, 256, 0, s>>>(L, channels, grad_stride, uv, uv_da, bias,
+                                                  height, width, grad_out, grad_uv, grad_uv_da,
+                                                  grad_bias);
 }
 
 template <int B, typename F>
@@ -846,7 +805,8 @@ void dispatch(int mode, int boundary, F&& f) {
 
 int make_levels(const float* const* level_ptr, float* const* grad_ptr, const int32_t* level_h,
                 const int32_t* level_w, const int64_t* level_batch_stride, int32_t num_levels,
-                int32_t filter_mode, int32_t boundary_mode, Levels& L) {
+                int32_t channels, int32_t filter_mode, int32_t boundary_mode, Levels& L) {
+  if (channels < 1) return DR_ERR_INVALID_ARGUMENT;
   if (num_levels < 1 || num_levels > DR_MAX_LEVELS || level_ptr == nullptr || level_h == nullptr ||
       level_w == nullptr || level_batch_stride == nullptr)
     return DR_ERR_INVALID_ARGUMENT;
@@ -859,7 +819,7 @@ int make_levels(const float* const* level_ptr, float* const* grad_ptr, const int
     L.grad[l] = used && grad_ptr != nullptr ? grad_ptr[l] : nullptr;
     L.h[l] = used ? level_h[l] : 1;
     L.w[l] = used ? level_w[l] : 1;
-    L.bstride[l] = used ? level_batch_stride[l] : 0;
+    L.bstride[l] = used ? level_batch_stride[l] / channels : 0;
     if (used && (L.ptr[l] == nullptr || L.h[l] < 1 || L.w[l] < 1 || L.bstride[l] < 0))
       return DR_ERR_INVALID_ARGUMENT;
     if (used && grad_ptr != nullptr && L.grad[l] == nullptr) return DR_ERR_INVALID_ARGUMENT;
@@ -881,7 +841,7 @@ extern "C" int dr_texture_fwd(const float* const* level_ptr, const int32_t* leve
                               int32_t boundary_mode, float* out, void* stream) {
   Levels L;
   int status = make_levels(level_ptr, nullptr, level_h, level_w, level_batch_stride, num_levels,
-                           filter_mode, boundary_mode, L);
+                           channels, filter_mode, boundary_mode, L);
   if (status != DR_OK) return status;
   if (channels < 1 || batch < 0 || height < 0 || width < 0) return DR_ERR_INVALID_ARGUMENT;
   const long long total = batch * static_cast<long long>(height) * width;
@@ -899,7 +859,8 @@ extern "C" int dr_texture_fwd(const float* const* level_ptr, const int32_t* leve
 extern "C" int dr_texture_bwd(const float* const* level_ptr, float* const* grad_level_ptr,
                               const int32_t* level_h, const int32_t* level_w,
                               const int64_t* level_batch_stride, int32_t num_levels,
-                              int32_t channels, const float* uv, const float* uv_da,
+                              int32_t channels, int32_t grad_channel_stride, const float* uv,
+                              const float* uv_da,
                               const float* bias, int64_t batch, int32_t height, int32_t width,
                               int32_t filter_mode, int32_t boundary_mode, const float* grad_out,
                               float* grad_uv, float* grad_uv_da, float* grad_bias,
@@ -907,7 +868,7 @@ extern "C" int dr_texture_bwd(const float* const* level_ptr, float* const* grad_
   if (grad_level_ptr == nullptr) return DR_ERR_INVALID_ARGUMENT;
   Levels L;
   int status = make_levels(level_ptr, grad_level_ptr, level_h, level_w, level_batch_stride,
-                           num_levels, filter_mode, boundary_mode, L);
+                           num_levels, channels, filter_mode, boundary_mode, L);
   if (status != DR_OK) return status;
   if (channels < 1 || batch < 0 || height < 0 || width < 0) return DR_ERR_INVALID_ARGUMENT;
   const long long total = batch * static_cast<long long>(height) * width;
@@ -916,11 +877,17 @@ extern "C" int dr_texture_bwd(const float* const* level_ptr, float* const* grad_
   if (grad_uv_da != nullptr && uv_da == nullptr) return DR_ERR_INVALID_ARGUMENT;
   if (grad_bias != nullptr && bias == nullptr) return DR_ERR_INVALID_ARGUMENT;
   if (batch > 65535 || height >= (1 << 20) || width >= (1 << 20)) return DR_ERR_TOO_LARGE;
+  if (grad_channel_stride < channels) return DR_ERR_INVALID_ARGUMENT;
+  if (grad_channel_stride == 4) {
+    for (int l = 0; l < num_levels; ++l)
+      if ((reinterpret_cast<uintptr_t>(grad_level_ptr[l]) & 15u) != 0) return DR_ERR_INVALID_ARGUMENT;
+  }
   cudaStream_t s = as_stream(stream);
   dispatch(filter_mode, boundary_mode, [&](auto m, auto b) {
-    launch_bwd<decltype(m)::value, decltype(b)::value>(L, channels, uv, uv_da, bias,
-                                                       static_cast<int>(batch), height, width,
-                                                       grad_out, grad_uv, grad_uv_da, grad_bias, s);
+    launch_bwd<decltype(m)::value, decltype(b)::value>(L, channels, grad_channel_stride, uv, uv_da,
+                                                       bias, static_cast<int>(batch), height,
+                                                       width, grad_out, grad_uv, grad_uv_da,
+                                                       grad_bias, s);
   });
   return launch_status();
 }

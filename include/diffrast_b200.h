@@ -137,12 +137,14 @@ int dr_texture_fwd(const float* const* level_ptr, const int32_t* level_h, const 
                    int32_t height, int32_t width, int32_t filter_mode, int32_t boundary_mode,
                    float* out, void* stream);
 
-/* Texel gradients are ACCUMULATED into grad_level_ptr[l] (same layout as the levels; clear
- * them first). grad_uv, grad_uv_da and grad_bias (each NULL to skip) are written. */
+/* Texel gradients are ACCUMULATED into grad_level_ptr[l] (clear them first), laid out like the
+ * levels but with grad_channel_stride (>= channels) floats per texel; with 4 (and channels <= 4,
+ * 16-byte aligned buffers) each texel's gradient is added with one vector reduction. grad_uv,
+ * grad_uv_da and grad_bias (each NULL to skip) are written. */
 int dr_texture_bwd(const float* const* level_ptr, float* const* grad_level_ptr,
                    const int32_t* level_h, const int32_t* level_w,
                    const int64_t* level_batch_stride, int32_t num_levels, int32_t channels,
-                   const float* uv, const float* uv_da, const float* bias, int64_t batch,
+                   int32_t grad_channel_stride, const float* uv, const float* uv_da, const float* bias, int64_t batch,
                    int32_t height, int32_t width, int32_t filter_mode, int32_t boundary_mode,
                    const float* grad_out, float* grad_uv, float* grad_uv_da, float* grad_bias,
                    void* stream);
