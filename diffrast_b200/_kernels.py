@@ -189,6 +189,20 @@ def interpolate_bwd(attr3, rast, rast_db, tri, diff, grad_out, grad_out_da, need
     return grad_attr, grad_rast, grad_db
 
 
+def pixel_rows(t: Tensor | None) -> tuple[Tensor | None, int]:
+    """``t`` (``[batch, h, w, k]``) with its pixel stride in floats, copied only when its pixels
+    are not equally spaced rows of contiguous channels."""
+    if t is None:
+        return None, 0
+    b, h, w, k = t.shape
+    sb, sh, sw, sk = t.stride()
+    uniform = sk == 1 and (h == 1 or sh == w * sw) and (b == 1 or sb == h * sh) and sw >= k
+    if not uniform:
+        t = t.contiguous()
+        sw = k
+    return t, sw
+
+
 def _level_tables(levels: list[Tensor], cube: bool):
     heights = [lv.shape[-3] for lv in levels]
     widths = [lv.shape[-2] for lv in levels]
@@ -203,11 +217,13 @@ def texture_fwd(levels: list[Tensor], uv: Tensor, uv_da: Tensor | None, bias: Te
     channels = levels[0].shape[-1]
     out = torch.empty((batch, height, width, channels), dtype=torch.float32, device=uv.device)
     hs, ws, bs = _level_tables(levels, boundary == 3)
+    uv, uv_stride = pixel_rows(uv)
+    uv_da, da_stride = pixel_rows(uv_da)
     N.check(
         N.lib().dr_texture_fwd(N.pointer_array([lv.data_ptr() for lv in levels]), hs, ws, bs,
-                               len(levels), channels, uv.data_ptr(), N.ptr(uv_da), N.ptr(bias),
-                               batch, height, width, mode, boundary, out.data_ptr(),
-                               N.stream(uv.device)),
+                               len(levels), channels, uv.data_ptr(), uv_stride, N.ptr(uv_da),
+                               da_stride, N.ptr(bias), batch, height, width, mode, boundary,
+                               out.data_ptr(), N.stream(uv.device)),
         "dr_texture_fwd",
     )  # fmt: skip
     return out
@@ -222,15 +238,17 @@ def texture_bwd(levels, uv, uv_da, bias, mode, boundary, grad_out, want_uv, want
     stride = 4 if channels == 3 else channels
     grads = [torch.zeros((*lv.shape[:-1], stride), dtype=torch.float32, device=lv.device)
              for lv in levels]
-    grad_uv = torch.empty_like(uv) if want_uv else None
-    grad_da = torch.empty_like(uv_da) if want_da else None
+    grad_uv = torch.empty(uv.shape, dtype=torch.float32, device=uv.device) if want_uv else None
+    grad_da = torch.empty(uv_da.shape, dtype=torch.float32, device=uv.device) if want_da else None
+    uv, uv_stride = pixel_rows(uv)
+    uv_da, da_stride = pixel_rows(uv_da)
     grad_bias = torch.empty_like(bias) if want_bias else None
     hs, ws, bs = _level_tables(levels, boundary == 3)
     N.check(
         N.lib().dr_texture_bwd(N.pointer_array([lv.data_ptr() for lv in levels]),
                                N.pointer_array([g.data_ptr() for g in grads]), hs, ws, bs,
-                               len(levels), channels, stride, uv.data_ptr(), N.ptr(uv_da),
-                               N.ptr(bias),
+                               len(levels), channels, stride, uv.data_ptr(), uv_stride,
+                               N.ptr(uv_da), da_stride, N.ptr(bias),
                                batch, height, width, mode, boundary, grad_out.data_ptr(),
                                N.ptr(grad_uv), N.ptr(grad_da), N.ptr(grad_bias),
                                N.stream(uv.device)),

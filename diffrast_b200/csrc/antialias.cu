@@ -213,7 +213,7 @@ __device__ __forceinline__ Pair eval_pair(const AaCtx& a, long long b, int row, 
 constexpr int kAaThreadsX = 32, kAaThreadsY = 8;
 constexpr int kAaTileX = kAaThreadsX - 1, kAaTileY = kAaThreadsY - 1;
 
-__global__ void __launch_bounds__(256, 4) aa_fwd_kernel(const AaCtx a, float* __restrict__ out) {
+__global__ void __launch_bounds__(256, 6) aa_fwd_kernel(const AaCtx a, float* __restrict__ out) {
   __shared__ float2 hk[kAaThreadsY][kAaThreadsX], vk[kAaThreadsY][kAaThreadsX];
   const int tx = threadIdx.x % kAaThreadsX, ty = threadIdx.x / kAaThreadsX;
   const int col = blockIdx.x * kAaTileX + tx - 1, row = blockIdx.y * kAaTileY + ty - 1;
@@ -275,7 +275,7 @@ __device__ __forceinline__ void add_edge_gradient(const AaCtx& a, float* grad_po
   red_add_v4(grad_pos + (base + v.idx[j]) * 4, gx_j, gy_j, 0.0f, gw_j);
 }
 
-__global__ void __launch_bounds__(256, 4) aa_bwd_kernel(const AaCtx a,
+__global__ void __launch_bounds__(256, 5) aa_bwd_kernel(const AaCtx a,
                                                      const float* __restrict__ grad_out,
                                                      float boost, float* __restrict__ grad_color,
                                                      float* __restrict__ grad_pos) {

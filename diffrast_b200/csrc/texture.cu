@@ -395,26 +395,32 @@ struct Lookup {
   bool near_ok;
 };
 
+// Pixel strides (floats between consecutive pixels) of uv and uv_da, which may be channel slices
+// of a wider tensor.
+struct Strides {
+  long long uv, uv_da;
+};
+
 template <int MODE, int B>
 __device__ __forceinline__ void prepare(const Levels& L, int channels, const float* __restrict__ uv,
                                         const float* __restrict__ uv_da,
-                                        const float* __restrict__ bias, long long p,
-                                        long long view, Lookup<MODE, B>& k) {
+                                        const float* __restrict__ bias, const Strides st,
+                                        long long p, long long view, Lookup<MODE, B>& k) {
   constexpr bool kMip = MODE >= DR_FILTER_LINEAR_MIPMAP_NEAREST;
   k.valid = true;
   k.face = 0;
   k.has_da = kMip && uv_da != nullptr;
   if (B == DR_BOUNDARY_CUBE) {
-    k.cube = cube_project(uv + p * 3, k.has_da ? uv_da + p * 6 : nullptr);
+    k.cube = cube_project(uv + p * st.uv, k.has_da ? uv_da + p * st.uv_da : nullptr);
     k.valid = k.cube.valid;
     k.face = k.cube.face;
     k.u = k.cube.s;
     k.v = k.cube.t;
     for (int i = 0; i < 4; ++i) k.da[i] = k.has_da ? k.cube.st_da[i] : 0.0f;
   } else {
-    k.u = uv[p * 2];
-    k.v = uv[p * 2 + 1];
-    for (int i = 0; i < 4; ++i) k.da[i] = k.has_da ? uv_da[p * 4 + i] : 0.0f;
+    k.u = uv[p * st.uv];
+    k.v = uv[p * st.uv + 1];
+    for (int i = 0; i < 4; ++i) k.da[i] = k.has_da ? uv_da[p * st.uv_da + i] : 0.0f;
   }
   k.bad = false;
   k.lo = k.hi = 0;
@@ -484,7 +490,7 @@ __device__ __forceinline__ void store_block(float* __restrict__ dst, const float
 template <int MODE, int B>
 __global__ void __launch_bounds__(256) texture_fwd_kernel(
     const Levels L, int channels, const float* __restrict__ uv, const float* __restrict__ uv_da,
-    const float* __restrict__ bias, long long total, long long pixels_per_image,
+    const float* __restrict__ bias, const Strides st, long long total, long long pixels_per_image,
     float* __restrict__ out, bool staged) {
   extern __shared__ float stage[];
   const long long first = blockIdx.x * static_cast<long long>(blockDim.x);
@@ -493,7 +499,7 @@ __global__ void __launch_bounds__(256) texture_fwd_kernel(
   if (p < total) {
     const long long view = p / pixels_per_image;
     Lookup<MODE, B> k;
-    prepare<MODE, B>(L, channels, uv, uv_da, bias, p, view, k);
+    prepare<MODE, B>(L, channels, uv, uv_da, bias, st, p, view, k);
     for (int c = 0; c < channels; ++c) {
       float value;
       if (MODE == DR_FILTER_NEAREST) {
@@ -549,7 +555,8 @@ __device__ __forceinline__ void add_footprint_taps(Taps& taps, const Footprint& 
 template <int MODE, int B>
 __global__ void __launch_bounds__(256) texture_bwd_kernel(
     const Levels L, int channels, int grad_stride, const float* __restrict__ uv,
-    const float* __restrict__ uv_da, const float* __restrict__ bias, int height, int width,
+    const float* __restrict__ uv_da, const float* __restrict__ bias, const Strides st, int height,
+    int width,
     const float* __restrict__ grad_out, float* __restrict__ grad_uv,
     float* __restrict__ grad_uv_da, float* __restrict__ grad_bias) {
   const int col = blockIdx.x * 16 + (threadIdx.x & 15);
@@ -562,7 +569,7 @@ __global__ void __launch_bounds__(256) texture_bwd_kernel(
   Taps taps;
   taps.n = 0;
   if (inside) {
-    prepare<MODE, B>(L, channels, uv, uv_da, bias, p, view, k);
+    prepare<MODE, B>(L, channels, uv, uv_da, bias, st, p, view, k);
     live = !k.bad && k.valid;
     if (live) {
       if (MODE == DR_FILTER_NEAREST) {
@@ -700,85 +707,99 @@ __device__ __forceinline__ float halving_weight(int j, int i, int n, int m) {
   return hi > lo ? static_cast<float>(hi - lo) / static_cast<float>(n) : 0.0f;
 }
 
-__global__ void __launch_bounds__(256) mip_down_kernel(const float* __restrict__ src,
-                                                       long long images, int h, int w,
+// One block per output row (image, row); its threads walk the row's (texel, channel) elements.
+// Even sizes take the pair-mean path: the area weights are all 1/2, which makes the sum exact in
+// either order.
+__global__ void __launch_bounds__(256) mip_down_kernel(const float* __restrict__ src, int h, int w,
                                                        int channels, float* __restrict__ dst) {
   const int oh = (h + 1) / 2, ow = (w + 1) / 2;
-  const long long total = images * oh * ow * static_cast<long long>(channels);
-  const long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
-  if (e >= total) return;
-  const int c = static_cast<int>(e % channels);
-  long long rest = e / channels;
-  const int k = static_cast<int>(rest % ow);
-  rest /= ow;
-  const int j = static_cast<int>(rest % oh);
-  const long long img = rest / oh;
+  const long long out_row = blockIdx.x;
+  const long long img = out_row / oh;
+  const int j = static_cast<int>(out_row - img * oh);
+  const float* image = src + img * h * static_cast<long long>(w) * channels;
+  float* out = dst + out_row * ow * channels;
+  const int n = ow * channels;
+  const bool even = (h % 2 == 0) && (w % 2 == 0);
   const int r0 = static_cast<int>(static_cast<long long>(j) * h / oh);
-  const int c0 = static_cast<int>(static_cast<long long>(k) * w / ow);
-  const float* base = src + img * h * static_cast<long long>(w) * channels + c;
-  float acc = 0.0f;
-  for (int r = r0; r < min(r0 + 3, h); ++r) {
-    const float wr = h > 1 ? halving_weight(j, r, h, oh) : 1.0f;
-    if (wr == 0.0f) continue;
-    float row = 0.0f;
-    for (int q = c0; q < min(c0 + 3, w); ++q) {
-      const float wc = w > 1 ? halving_weight(k, q, w, ow) : 1.0f;
-      if (wc != 0.0f) row += wc * __ldg(base + (static_cast<long long>(r) * w + q) * channels);
+  for (int e = threadIdx.x; e < n; e += blockDim.x) {
+    const int k = e / channels, c = e - k * channels;
+    if (even) {
+      const float* a = image + (static_cast<long long>(2 * j) * w + 2 * k) * channels + c;
+      const float* b = a + static_cast<long long>(w) * channels;
+      out[e] = 0.25f * ((__ldg(a) + __ldg(a + channels)) + (__ldg(b) + __ldg(b + channels)));
+      continue;
     }
-    acc += wr * row;
+    const int c0 = static_cast<int>(static_cast<long long>(k) * w / ow);
+    float acc = 0.0f;
+    for (int r = r0; r < min(r0 + 3, h); ++r) {
+      const float wr = h > 1 ? halving_weight(j, r, h, oh) : 1.0f;
+      if (wr == 0.0f) continue;
+      float row = 0.0f;
+      for (int q = c0; q < min(c0 + 3, w); ++q) {
+        const float wc = w > 1 ? halving_weight(k, q, w, ow) : 1.0f;
+        if (wc != 0.0f) row += wc * __ldg(image + (static_cast<long long>(r) * w + q) * channels + c);
+      }
+      acc += wr * row;
+    }
+    out[e] = acc;
   }
-  dst[e] = acc;
 }
 
+// Adjoint of mip_down_kernel in gather form: one block per fine row; each fine element adds the
+// weighted gradients of the coarse texels whose bins overlap it.
 __global__ void __launch_bounds__(256) mip_down_bwd_kernel(const float* __restrict__ grad_dst,
-                                                           long long images, int h, int w,
-                                                           int channels,
+                                                           int h, int w, int channels,
                                                            float* __restrict__ grad_src) {
   const int oh = (h + 1) / 2, ow = (w + 1) / 2;
-  const long long total = images * h * static_cast<long long>(w) * channels;
-  const long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
-  if (e >= total) return;
-  const int c = static_cast<int>(e % channels);
-  long long rest = e / channels;
-  const int q = static_cast<int>(rest % w);
-  rest /= w;
-  const int r = static_cast<int>(rest % h);
-  const long long img = rest / h;
+  const long long in_row = blockIdx.x;
+  const long long img = in_row / h;
+  const int r = static_cast<int>(in_row - img * h);
+  const float* coarse = grad_dst + img * oh * static_cast<long long>(ow) * channels;
+  float* fine = grad_src + in_row * w * channels;
+  const int n = w * channels;
+  const bool even = (h % 2 == 0) && (w % 2 == 0);
   // Coarse bins overlapping fine texel i: j in [floor(i m / n), ceil((i + 1) m / n) - 1].
   const int j0 = static_cast<int>(static_cast<long long>(r) * oh / h);
   const int j1 = static_cast<int>((static_cast<long long>(r + 1) * oh + h - 1) / h) - 1;
-  const int k0 = static_cast<int>(static_cast<long long>(q) * ow / w);
-  const int k1 = static_cast<int>((static_cast<long long>(q + 1) * ow + w - 1) / w) - 1;
-  const float* base = grad_dst + img * oh * static_cast<long long>(ow) * channels + c;
-  float acc = 0.0f;
-  for (int j = j0; j <= j1; ++j) {
-    const float wr = h > 1 ? halving_weight(j, r, h, oh) : 1.0f;
-    float row = 0.0f;
-    for (int k = k0; k <= k1; ++k) {
-      const float wc = w > 1 ? halving_weight(k, q, w, ow) : 1.0f;
-      row += wc * __ldg(base + (static_cast<long long>(j) * ow + k) * channels);
+  for (int e = threadIdx.x; e < n; e += blockDim.x) {
+    const int q = e / channels, c = e - q * channels;
+    if (even) {
+      fine[e] += 0.25f * __ldg(coarse + (static_cast<long long>(r / 2) * ow + q / 2) * channels + c);
+      continue;
     }
-    acc += wr * row;
+    const int k0 = static_cast<int>(static_cast<long long>(q) * ow / w);
+    const int k1 = static_cast<int>((static_cast<long long>(q + 1) * ow + w - 1) / w) - 1;
+    float acc = 0.0f;
+    for (int j = j0; j <= j1; ++j) {
+      const float wr = h > 1 ? halving_weight(j, r, h, oh) : 1.0f;
+      float row = 0.0f;
+      for (int k = k0; k <= k1; ++k) {
+        const float wc = w > 1 ? halving_weight(k, q, w, ow) : 1.0f;
+        row += wc * __ldg(coarse + (static_cast<long long>(j) * ow + k) * channels + c);
+      }
+      acc += wr * row;
+    }
+    fine[e] += acc;
   }
-  grad_src[e] += acc;
 }
 
 template <int MODE, int B>
 void launch_fwd(const Levels& L, int channels, const float* uv, const float* uv_da,
-                const float* bias, long long total, long long ppi, float* out, cudaStream_t s) {
+                const float* bias, Strides st, long long total, long long ppi, float* out,
+                cudaStream_t s) {
   const size_t stage_bytes = sizeof(float) * 256 * static_cast<size_t>(channels);
   const bool staged = stage_bytes <= 48 * 1024;
   texture_fwd_kernel<MODE, B><<<blocks_for(total, 256), 256, staged ? stage_bytes : 0, s>>>(
-      L, channels, uv, uv_da, bias, total, ppi, out, staged);
+      L, channels, uv, uv_da, bias, st, total, ppi, out, staged);
 }
 
 template <int MODE, int B>
 void launch_bwd(const Levels& L, int channels, int grad_stride, const float* uv,
-                const float* uv_da, const float* bias, int batch, int height, int width,
-                const float* grad_out, float* grad_uv, float* grad_uv_da, float* grad_bias,
-                cudaStream_t s) {
+                const float* uv_da, const float* bias, Strides st, int batch, int height,
+                int width, const float* grad_out, float* grad_uv, float* grad_uv_da,
+                float* grad_bias, cudaStream_t s) {
   const dim3 grid((width + 15) / 16, (height + 15) / 16, batch);
-  texture_bwd_kernel<MODE, B><<<grid, 256, 0, s>>>(L, channels, grad_stride, uv, uv_da, bias,
+  texture_bwd_kernel<MODE, B><<<grid, 256, 0, s>>>(L, channels, grad_stride, uv, uv_da, bias, st,
                                                   height, width, grad_out, grad_uv, grad_uv_da,
                                                   grad_bias);
 }
@@ -836,7 +857,8 @@ using namespace dr;
 extern "C" int dr_texture_fwd(const float* const* level_ptr, const int32_t* level_h,
                               const int32_t* level_w, const int64_t* level_batch_stride,
                               int32_t num_levels, int32_t channels, const float* uv,
-                              const float* uv_da, const float* bias, int64_t batch,
+                              int64_t uv_stride, const float* uv_da, int64_t uv_da_stride,
+                              const float* bias, int64_t batch,
                               int32_t height, int32_t width, int32_t filter_mode,
                               int32_t boundary_mode, float* out, void* stream) {
   Levels L;
@@ -848,10 +870,14 @@ extern "C" int dr_texture_fwd(const float* const* level_ptr, const int32_t* leve
   if (total == 0) return DR_OK;
   if (uv == nullptr || out == nullptr) return DR_ERR_INVALID_ARGUMENT;
   const long long ppi = static_cast<long long>(height) * width;
+  const int uv_width = boundary_mode == DR_BOUNDARY_CUBE ? 3 : 2;
+  const int da_width = boundary_mode == DR_BOUNDARY_CUBE ? 6 : 4;
+  const Strides st = {uv_stride > 0 ? uv_stride : uv_width, uv_da_stride > 0 ? uv_da_stride : da_width};
+  if (st.uv < uv_width || (uv_da != nullptr && st.uv_da < da_width)) return DR_ERR_INVALID_ARGUMENT;
   cudaStream_t s = as_stream(stream);
   dispatch(filter_mode, boundary_mode, [&](auto m, auto b) {
-    launch_fwd<decltype(m)::value, decltype(b)::value>(L, channels, uv, uv_da, bias, total, ppi,
-                                                       out, s);
+    launch_fwd<decltype(m)::value, decltype(b)::value>(L, channels, uv, uv_da, bias, st, total,
+                                                       ppi, out, s);
   });
   return launch_status();
 }
@@ -860,7 +886,7 @@ extern "C" int dr_texture_bwd(const float* const* level_ptr, float* const* grad_
                               const int32_t* level_h, const int32_t* level_w,
                               const int64_t* level_batch_stride, int32_t num_levels,
                               int32_t channels, int32_t grad_channel_stride, const float* uv,
-                              const float* uv_da,
+                              int64_t uv_stride, const float* uv_da, int64_t uv_da_stride,
                               const float* bias, int64_t batch, int32_t height, int32_t width,
                               int32_t filter_mode, int32_t boundary_mode, const float* grad_out,
                               float* grad_uv, float* grad_uv_da, float* grad_bias,
@@ -878,6 +904,10 @@ extern "C" int dr_texture_bwd(const float* const* level_ptr, float* const* grad_
   if (grad_bias != nullptr && bias == nullptr) return DR_ERR_INVALID_ARGUMENT;
   if (batch > 65535 || height >= (1 << 20) || width >= (1 << 20)) return DR_ERR_TOO_LARGE;
   if (grad_channel_stride < channels) return DR_ERR_INVALID_ARGUMENT;
+  const int uv_width = boundary_mode == DR_BOUNDARY_CUBE ? 3 : 2;
+  const int da_width = boundary_mode == DR_BOUNDARY_CUBE ? 6 : 4;
+  const Strides st = {uv_stride > 0 ? uv_stride : uv_width, uv_da_stride > 0 ? uv_da_stride : da_width};
+  if (st.uv < uv_width || (uv_da != nullptr && st.uv_da < da_width)) return DR_ERR_INVALID_ARGUMENT;
   if (grad_channel_stride == 4) {
     for (int l = 0; l < num_levels; ++l)
       if ((reinterpret_cast<uintptr_t>(grad_level_ptr[l]) & 15u) != 0) return DR_ERR_INVALID_ARGUMENT;
@@ -885,7 +915,7 @@ extern "C" int dr_texture_bwd(const float* const* level_ptr, float* const* grad_
   cudaStream_t s = as_stream(stream);
   dispatch(filter_mode, boundary_mode, [&](auto m, auto b) {
     launch_bwd<decltype(m)::value, decltype(b)::value>(L, channels, grad_channel_stride, uv, uv_da,
-                                                       bias, static_cast<int>(batch), height,
+                                                       bias, st, static_cast<int>(batch), height,
                                                        width, grad_out, grad_uv, grad_uv_da,
                                                        grad_bias, s);
   });
@@ -896,10 +926,11 @@ extern "C" int dr_mip_downsample(const float* src, int64_t images, int32_t h, in
                                  int32_t channels, float* dst, void* stream) {
   if (images < 0 || h < 1 || w < 1 || channels < 1 || src == nullptr || dst == nullptr)
     return DR_ERR_INVALID_ARGUMENT;
-  const long long total = images * ((h + 1) / 2) * static_cast<long long>((w + 1) / 2) * channels;
-  if (total == 0) return DR_OK;
-  mip_down_kernel<<<blocks_for(total, 256), 256, 0, as_stream(stream)>>>(src, images, h, w,
-                                                                          channels, dst);
+  const long long rows = images * ((h + 1) / 2);
+  if (rows == 0) return DR_OK;
+  if (rows >= (1LL << 31)) return DR_ERR_TOO_LARGE;
+  mip_down_kernel<<<static_cast<unsigned>(rows), 256, 0, as_stream(stream)>>>(src, h, w, channels,
+                                                                               dst);
   return launch_status();
 }
 
@@ -907,9 +938,10 @@ extern "C" int dr_mip_downsample_bwd(const float* grad_dst, int64_t images, int3
                                      int32_t channels, float* grad_src, void* stream) {
   if (images < 0 || h < 1 || w < 1 || channels < 1 || grad_dst == nullptr || grad_src == nullptr)
     return DR_ERR_INVALID_ARGUMENT;
-  const long long total = images * h * static_cast<long long>(w) * channels;
-  if (total == 0) return DR_OK;
-  mip_down_bwd_kernel<<<blocks_for(total, 256), 256, 0, as_stream(stream)>>>(grad_dst, images, h,
-                                                                              w, channels, grad_src);
+  const long long rows = images * h;
+  if (rows == 0) return DR_OK;
+  if (rows >= (1LL << 31)) return DR_ERR_TOO_LARGE;
+  mip_down_bwd_kernel<<<static_cast<unsigned>(rows), 256, 0, as_stream(stream)>>>(grad_dst, h, w,
+                                                                                  channels, grad_src);
   return launch_status();
 }

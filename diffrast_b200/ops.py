@@ -325,10 +325,11 @@ def texture(
     if mode < 3:
         uv_da = None if uv_da is None or mode < 2 else uv_da.detach()
         mip_level_bias = None if mip_level_bias is None or mode < 2 else mip_level_bias.detach()
+    # uv and uv_da may be channel slices of a wider tensor (such as interpolate's output): the
+    # kernels read them in place through their pixel stride.
     with torch.cuda.device(uv.device):
         return F.Texture.apply(
-            uv.contiguous(), None if uv_da is None else uv_da.contiguous(),
-            None if mip_level_bias is None else mip_level_bias.contiguous(), mode,
+            uv, uv_da, None if mip_level_bias is None else mip_level_bias.contiguous(), mode,
             _BOUNDARY_INDEX[boundary_mode], *levels,
         )
 

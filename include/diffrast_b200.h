@@ -128,12 +128,14 @@ int dr_interpolate_bwd(const float* attr, int64_t attr_batch, int64_t num_vert, 
  * stride in elements is `level_batch_stride[l]` (0 when that level is shared by all views).
  * These four arrays are HOST arrays of `num_levels` entries (level 0 is the base texture).
  * For DR_BOUNDARY_CUBE, uv holds directions [batch, h, w, 3] and uv_da [batch, h, w, 6].
- * tex_batch_is_one: the texture is shared by all views (tex batch of 1).
- * uv_da and bias may be NULL. out [batch, h, w, channels].
+ * uv_stride / uv_da_stride: floats between consecutive pixels of uv / uv_da (0 for packed), so
+ * channel slices of a wider tensor are read in place. uv_da and bias may be NULL.
+ * out [batch, h, w, channels]; grad_uv and grad_uv_da are packed.
  * ------------------------------------------------------------------------------------------- */
 int dr_texture_fwd(const float* const* level_ptr, const int32_t* level_h, const int32_t* level_w,
                    const int64_t* level_batch_stride, int32_t num_levels, int32_t channels,
-                   const float* uv, const float* uv_da, const float* bias, int64_t batch,
+                   const float* uv, int64_t uv_stride, const float* uv_da, int64_t uv_da_stride,
+                   const float* bias, int64_t batch,
                    int32_t height, int32_t width, int32_t filter_mode, int32_t boundary_mode,
                    float* out, void* stream);
 
@@ -144,7 +146,8 @@ int dr_texture_fwd(const float* const* level_ptr, const int32_t* level_h, const 
 int dr_texture_bwd(const float* const* level_ptr, float* const* grad_level_ptr,
                    const int32_t* level_h, const int32_t* level_w,
                    const int64_t* level_batch_stride, int32_t num_levels, int32_t channels,
-                   int32_t grad_channel_stride, const float* uv, const float* uv_da, const float* bias, int64_t batch,
+                   int32_t grad_channel_stride, const float* uv, int64_t uv_stride,
+                   const float* uv_da, int64_t uv_da_stride, const float* bias, int64_t batch,
                    int32_t height, int32_t width, int32_t filter_mode, int32_t boundary_mode,
                    const float* grad_out, float* grad_uv, float* grad_uv_da, float* grad_bias,
                    void* stream);
