@@ -140,6 +140,19 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(mhz)}  # fmt: skip
 
 
+def measured_traffic(stage: str, pixels: int) -> int | None:
+    """DRAM bytes of one launch of `stage`: bytes per pixel from a committed ncu capture
+    (profiles/dram_bytes_per_pixel.txt) times the pixels of the launch, or None."""
+    path = ROOT / "profiles" / "dram_bytes_per_pixel.txt"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        parts = line.split()
+        if len(parts) == 2 and not line.startswith("#") and parts[0] == stage:
+            return int(float(parts[1]) * pixels)
+    return None
+
+
 def gpu_id(dev: torch.device) -> str:
     """nvidia-smi id of a torch device (its UUID, valid under CUDA_VISIBLE_DEVICES too)."""
     try:
@@ -298,7 +311,10 @@ def run_ours(args) -> None:
         "roofline": {
             "bound": "hbm", "kernel": dominant, "achieved": round(achieved, 1), "peak": peak,
             "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
-            "traffic": None, "algorithmic_bytes_per_launch": int(per_launch_bytes),
+            "traffic": measured_traffic(dominant, pixels),
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per pixel on the "
+                              "8-view case, scaled to this launch's pixels",
+            "algorithmic_bytes_per_launch": int(per_launch_bytes),
             "ms_per_launch": round(per_launch_ms, 4),
         },
         "step_roofline": {
