@@ -171,17 +171,20 @@ def peaks() -> tuple[float, str]:
 def build_scene(views_total: int, res: int, subdiv: int, tex_size: int, rank: int, world: int):
     import scenes
 
+    from diffrast_b200.distributed import view_shard
+
     sc = scenes.config5_scene(views=views_total, resolution=res, subdivisions=subdiv, tex_size=tex_size)
-    per = views_total // world
-    pos = sc["pos"][rank * per : (rank + 1) * per].contiguous()
+    shard = view_shard(views_total, rank, world)
+    pos = sc["pos"][shard].contiguous()
     gen = torch.Generator().manual_seed(1234)
-    target = torch.rand(views_total, res, res, TEX_CHANNELS, generator=gen)[rank * per : (rank + 1) * per]
+    target = torch.rand(views_total, res, res, TEX_CHANNELS, generator=gen)[shard]
     return pos, sc["tri"], sc["attr"], sc["tex"], target.contiguous()
 
 
 def run_ours(args) -> None:
     import diffrast_b200 as dr
     from diffrast_b200 import _kernels as K
+    from diffrast_b200.distributed import sum_gradients
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -213,10 +216,10 @@ def run_ours(args) -> None:
         out, out_da = dr.interpolate(attr, rast, tri, rast_db=rast_db, diff_attrs="all")
         color = dr.texture(tex, out[..., 0:2], out_da[..., 0:4], filter_mode="linear-mipmap-linear")
         image = dr.antialias(color, rast, pos_in, tri, topology_hash=topo)
-        loss = ((image - target_in) ** 2).mean()
+        # Mean over the whole job's pixels, so that the ranks' gradients sum to the full batch's.
+        loss = ((image - target_in) ** 2).sum() / (args.views * res * res * TEX_CHANNELS)
         loss.backward()
-        if world > 1:
-            dist.all_reduce(tex.grad)
+        sum_gradients([tex])
         return loss
 
     for _ in range(args.warmup):

@@ -158,6 +158,49 @@ class Texture(torch.autograd.Function):
         return (g_uv, g_da, g_bias, None, None, *level_grads)
 
 
+class TextureChain(torch.autograd.Function):
+    """Mipmapped lookup with the mip chain of ``tex`` built inside the function.
+
+    The levels never enter the autograd graph: the backward pass accumulates the gradients of all
+    levels (in 4-channel buffers when the texture has 3 channels), pushes them down the chain with
+    the adjoint kernel in place, and returns only the base level's gradient.
+    """
+
+    @staticmethod
+    def forward(ctx, uv, uv_da, bias, mode: int, boundary: int, count: int, tex: Tensor):
+        tex = tex.contiguous()
+        levels = [tex]
+        for _ in range(count):
+            levels.append(K.mip_down(levels[-1]))
+        out = K.texture_fwd(levels, uv, uv_da, bias, mode, boundary)
+        ctx.save_for_backward(*(_saveable(t) for t in (uv, uv_da, bias, tex)))
+        ctx.levels = levels[1:]
+        ctx.settings = (mode, boundary)
+        return out
+
+    @staticmethod
+    @first_order("texture")
+    def backward(ctx, grad_out):
+        mode, boundary = ctx.settings
+        uv, uv_da, bias, tex = ctx.saved_tensors
+        levels = [tex, *ctx.levels]
+        need = ctx.needs_input_grad
+        want_uv = need[0] and mode > 0
+        want_da = need[1] and uv_da is not None and mode == 3
+        want_bias = need[2] and bias is not None and mode == 3
+        grads, g_uv, g_da, g_bias = K.texture_bwd(levels, uv, uv_da, bias, mode, boundary,
+                                                  grad_out.contiguous(), want_uv, want_da,
+                                                  want_bias, keep_padded=True)
+        grad_tex = None
+        if need[6]:
+            for level in range(len(grads) - 2, -1, -1):
+                K.mip_down_bwd(grads[level + 1], grads[level])
+            grad_tex = grads[0]
+            if grad_tex.shape[-1] != tex.shape[-1]:
+                grad_tex = grad_tex[..., : tex.shape[-1]].contiguous()
+        return g_uv, g_da, g_bias, None, None, None, grad_tex
+
+
 class Antialias(torch.autograd.Function):
     @staticmethod
     def forward(ctx, color: Tensor, rast: Tensor, pos: Tensor, tri: Tensor, neighbours: Tensor,

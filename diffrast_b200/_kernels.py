@@ -230,7 +230,8 @@ def texture_fwd(levels: list[Tensor], uv: Tensor, uv_da: Tensor | None, bias: Te
 
 
 @timed("texture_bwd")
-def texture_bwd(levels, uv, uv_da, bias, mode, boundary, grad_out, want_uv, want_da, want_bias):
+def texture_bwd(levels, uv, uv_da, bias, mode, boundary, grad_out, want_uv, want_da, want_bias,
+                keep_padded=False):
     batch, height, width = uv.shape[:3]
     channels = levels[0].shape[-1]
     # Three-channel gradients are accumulated in four-channel buffers, so that each texel takes
@@ -254,7 +255,7 @@ def texture_bwd(levels, uv, uv_da, bias, mode, boundary, grad_out, want_uv, want
                                N.stream(uv.device)),
         "dr_texture_bwd",
     )  # fmt: skip
-    if stride != channels:
+    if stride != channels and not keep_padded:
         grads = [g[..., :channels].contiguous() for g in grads]
     return grads, grad_uv, grad_da, grad_bias
 

@@ -1,0 +1,41 @@
+"""Data parallelism over views: one process per GPU, views sharded, shared gradients summed.
+
+Views are independent through the whole render path; the only coupling is the sum of gradients
+of tensors shared by all views (the texture, a shared vertex buffer). A job of B views on N ranks
+gives rank r the contiguous views ``view_shard(B, r, N)``; after the backward pass the gradients
+of the shared tensors are summed with one all-reduce each (NCCL on GPUs, gloo on CPUs), issued in
+buckets so that large textures pipeline over NVLink.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+from torch import Tensor
+
+
+def view_shard(num_views: int, rank: int, world_size: int) -> slice:
+    """Views of ``rank``: contiguous, sizes differing by at most one, covering all ``num_views``."""
+    if world_size < 1 or not 0 <= rank < world_size:
+        raise ValueError(f"rank {rank} is not in a world of size {world_size}.")
+    base, extra = divmod(num_views, world_size)
+    start = rank * base + min(rank, extra)
+    return slice(start, start + base + (1 if rank < extra else 0))
+
+
+def sum_gradients(tensors: list[Tensor], group=None, bucket_bytes: int = 64 << 20) -> None:
+    """All-reduce (sum) the ``.grad`` of every tensor in place, across ``group``.
+
+    Gradients are reduced in chunks of at most ``bucket_bytes`` so that a 200 MB texture gradient
+    is sent as several collectives that overlap each other's transfers. Tensors without a
+    gradient take part with zeros, so every rank issues the same collectives in the same order.
+    """
+    if not dist.is_available() or not dist.is_initialized():
+        return
+    for t in tensors:
+        if t.grad is None:
+            t.grad = torch.zeros_like(t)
+        flat = t.grad.view(-1)
+        step = max(1, bucket_bytes // flat.element_size())
+        for start in range(0, flat.numel(), step):
+            dist.all_reduce(flat[start : start + step], group=group)

@@ -310,6 +310,18 @@ def texture(
     mode = _MODE_INDEX[filter_mode]
     if uv.numel() == 0:
         return tex.new_zeros(*uv.shape[:3], tex.shape[-1])
+    if mipmapped and given is None:
+        # The chain is built inside the lookup's autograd function, whose backward pushes the
+        # level gradients down the chain without leaving the kernels' buffers.
+        count = _chain_length(tex.shape[-3], tex.shape[-2], max_mip_level)
+        if mode < 3:
+            uv_da = None if uv_da is None else uv_da.detach()
+            mip_level_bias = None if mip_level_bias is None else mip_level_bias.detach()
+        with torch.cuda.device(uv.device):
+            return F.TextureChain.apply(
+                uv, uv_da, None if mip_level_bias is None else mip_level_bias.contiguous(), mode,
+                _BOUNDARY_INDEX[boundary_mode], count, tex,
+            )
     if mipmapped:
         if given is None:
             levels = [tex, *_build_chain(tex, max_mip_level)]
