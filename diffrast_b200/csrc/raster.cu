@@ -116,7 +116,7 @@ __device__ __forceinline__ void pixel_range(float lo, float hi, int size, int& f
 // arrays, indexed by the triangle's rank among the warp's direct triangles).
 struct WarpTris {
   float4 v[3][32];     // clip-space vertices, for the exact test
-  float4 edge[3][32];  // NDC half-planes (A, B, C, D): inside where A x + B y + C >= -D
+  float4 edge[3][32];  // NDC half-planes A x + B y + C >= -D, stored as (1 / A, B, C + D, A)
   int t[32], b[32], c0[32], c1[32], r0[32], spans[32], end[32];
   // Rows of the current batch that have pixels to test: triangle rank, row, first column and
   // the inclusive prefix sum of their pixel counts.
@@ -163,12 +163,20 @@ __global__ void __launch_bounds__(256) setup_kernel(
       r0 = 0;
       r1 = height - 1;
       if (in_front) {
-        nx[0] = v0.x / v0.w;
-        nx[1] = v1.x / v1.w;
-        nx[2] = v2.x / v2.w;
-        ny[0] = v0.y / v0.w;
-        ny[1] = v1.y / v1.w;
-        ny[2] = v2.y / v2.w;
+        // Projected vertices bound the pixels to test, never decide coverage; bounds are widened
+        // by margins far above the error of the fast reciprocal used for ordinary w.
+        const Vert* vs[3] = {&v0, &v1, &v2};
+        for (int k = 0; k < 3; ++k) {
+          const float wk = vs[k]->w;
+          if (wk >= 1e-30f && wk <= 1e30f) {
+            const float iw = __fdividef(1.0f, wk);
+            nx[k] = vs[k]->x * iw;
+            ny[k] = vs[k]->y * iw;
+          } else {
+            nx[k] = vs[k]->x / wk;
+            ny[k] = vs[k]->y / wk;
+          }
+        }
         pixel_range(fminf(fminf(nx[0], nx[1]), nx[2]), fmaxf(fmaxf(nx[0], nx[1]), nx[2]), width, c0, c1);
         pixel_range(fminf(fminf(ny[0], ny[1]), ny[2]), fmaxf(fmaxf(ny[0], ny[1]), ny[2]), height, r0, r1);
       }
@@ -224,7 +232,8 @@ __global__ void __launch_bounds__(256) setup_kernel(
       const float C = -(A * nx[i] + B * ny[i]);
       const float D = delta * sqrtf(A * A + B * B) +
                       4e-6f * (fabsf(A) + fabsf(B)) * (1.0f + fabsf(nx[i]) + fabsf(ny[i]));
-      w.edge[k][rank] = make_float4(A, B, C, D);
+      // Row bounds are x >= (-(B y + C) - D) / A (A > 0) or x <= it (A < 0): keep 1 / A.
+      w.edge[k][rank] = make_float4(A != 0.0f ? 1.0f / A : 0.0f, B, C + D, A);
     }
   }
   __syncwarp();
@@ -248,10 +257,10 @@ __global__ void __launch_bounds__(256) setup_kernel(
         float lo = -__int_as_float(0x7f800000), hi = __int_as_float(0x7f800000);
         bool empty = false;
         for (int e = 0; e < 3; ++e) {
-          const float4 h = w.edge[e][k];
-          const float rhs = -(h.y * py + h.z) - h.w;
-          if (h.x > 0.0f) lo = fmaxf(lo, rhs / h.x);
-          else if (h.x < 0.0f) hi = fminf(hi, rhs / h.x);
+          const float4 h = w.edge[e][k];  // (1 / A, B, C + D, A)
+          const float rhs = -(h.y * py + h.z);
+          if (h.w > 0.0f) lo = fmaxf(lo, rhs * h.x);
+          else if (h.w < 0.0f) hi = fminf(hi, rhs * h.x);
           else empty |= rhs > 0.0f;
         }
         if (empty || !(lo <= hi)) {
