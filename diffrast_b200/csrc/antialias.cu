@@ -67,26 +67,6 @@ __device__ __forceinline__ Tri2 load_tri(const AaCtx& a, long long pb, int t) {
   return v;
 }
 
-// Edge function of edge k (from vertex k + 1 to k + 2) at (px, py), reference.py:274-278.
-__device__ __forceinline__ float edge_fn(const Tri2& v, int k, float px, float py) {
-  const int i = (k + 1) % 3, j = (k + 2) % 3;
-  const float ai = sub(v.x[i], mul(px, v.w[i])), aj = sub(v.x[j], mul(px, v.w[j]));
-  const float ci = sub(v.y[i], mul(py, v.w[i])), cj = sub(v.y[j], mul(py, v.w[j]));
-  return cross2(ai, cj, aj, ci);
-}
-
-// Rounding bound of edge_fn at (px, py), reference.py:730-746.
-__device__ __forceinline__ float edge_slack(const Tri2& v, int k, float px, float py) {
-  const int i = (k + 1) % 3, j = (k + 2) % 3;
-  const float ai = fabsf(sub(v.x[i], mul(px, v.w[i]))), aj = fabsf(sub(v.x[j], mul(px, v.w[j])));
-  const float ci = fabsf(sub(v.y[i], mul(py, v.w[i]))), cj = fabsf(sub(v.y[j], mul(py, v.w[j])));
-  const float rxi = add(fabsf(v.x[i]), fabsf(v.w[i])), rxj = add(fabsf(v.x[j]), fabsf(v.w[j]));
-  const float ryi = add(fabsf(v.y[i]), fabsf(v.w[i])), ryj = add(fabsf(v.y[j]), fabsf(v.w[j]));
-  const float terms = add(add(add(mul(add(rxi, ai), cj), mul(add(rxj, aj), ci)), mul(ryj, ai)),
-                          mul(ryi, aj));
-  return mul(terms, kEdgeTie);
-}
-
 // Sign test of the silhouette classification: sign((l . p) * p_w) with l = a x b in (x, y, w).
 __device__ __forceinline__ float side_sign(const float l[3], const float4& p) {
   const float d = add(add(mul(l[0], p.x), mul(l[1], p.y)), mul(l[2], p.w));
@@ -124,23 +104,42 @@ struct Crossing {
 };
 
 // reference.py:675-727 for one pixel pair side: triangle t seen at src, followed towards dst.
+// As in the reference, a = x - px w and c = y - py w are formed once per vertex and point and
+// shared by the three edge functions and the slack (reference.py:274-278, :730-746).
 __device__ __forceinline__ Crossing crossing(const AaCtx& a, long long pb, int t, float sx,
                                              float sy, float dx, float dy, bool horizontal) {
   Crossing r = {false, 0.0f, 0};
   if (t < 0) return r;
   const Tri2 v = load_tri(a, pb, t);
+  float as[3], cs[3], ad[3], cd[3];
+  for (int k = 0; k < 3; ++k) {
+    as[k] = sub(v.x[k], mul(sx, v.w[k]));
+    cs[k] = sub(v.y[k], mul(sy, v.w[k]));
+    ad[k] = sub(v.x[k], mul(dx, v.w[k]));
+    cd[k] = sub(v.y[k], mul(dy, v.w[k]));
+  }
   float es[3], ed[3];
   for (int k = 0; k < 3; ++k) {
-    es[k] = edge_fn(v, k, sx, sy);
-    ed[k] = edge_fn(v, k, dx, dy);
+    const int i = (k + 1) % 3, j = (k + 2) % 3;
+    es[k] = cross2(as[i], cs[j], as[j], cs[i]);
+    ed[k] = cross2(ad[i], cd[j], ad[j], cd[i]);
   }
   const float sign = add(add(es[0], es[1]), es[2]) < 0.0f ? -1.0f : 1.0f;
+  float rx[3], ry[3];
+  for (int k = 0; k < 3; ++k) {
+    rx[k] = add(fabsf(v.x[k]), fabsf(v.w[k]));
+    ry[k] = add(fabsf(v.y[k]), fabsf(v.w[k]));
+  }
   bool any = false;
   float best = __int_as_float(0x7f800000);
   int edge = 0;
   for (int k = 0; k < 3; ++k) {
+    const int i = (k + 1) % 3, j = (k + 2) % 3;
     const float span = sub(es[k], ed[k]);
-    const float slack = edge_slack(v, k, dx, dy);
+    const float ai = fabsf(ad[i]), aj = fabsf(ad[j]), ci = fabsf(cd[i]), cj = fabsf(cd[j]);
+    const float terms = add(add(add(mul(add(rx[i], ai), cj), mul(add(rx[j], aj), ci)), mul(ry[j], ai)),
+                            mul(ry[i], aj));
+    const float slack = mul(terms, kEdgeTie);
     const bool crossed = (mul(ed[k], sign) <= slack) && (mul(span, sign) > mul(2.0f, slack));
     any |= crossed;
     const float tk = crossed ? dvd(es[k], span) : __int_as_float(0x7f800000);
