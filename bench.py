@@ -250,21 +250,54 @@ def run_ours(args) -> None:
     stage_ms = {name: sum(s.elapsed_time(e) for s, e in pairs) / args.steps for name, pairs in stages.items()}
     stage_calls = {name: len(pairs) / args.steps for name, pairs in stages.items()}
 
-    # End to end through the public API: inputs copied from pinned host memory every step and the
-    # loss read back, all inside the timed region.
+    # End to end through the public API: every step's inputs are copied from pinned host memory
+    # and its loss is read back, all inside the timed region. As an input pipeline would, the copy
+    # of step i + 1's inputs runs on a side stream (into the other of two device buffers) while
+    # step i computes; the first step's copy is not overlapped.
     pos_host = pos_cpu.pin_memory()
     target_host = target_cpu.pin_memory()
-    pos_e2e = torch.empty_like(pos_cpu, device=dev)
-    target_e2e = torch.empty_like(target_cpu, device=dev)
+    buffers = [(torch.empty_like(pos_cpu, device=dev), torch.empty_like(target_cpu, device=dev))
+               for _ in range(2)]
+    copy_stream = torch.cuda.Stream(dev)
+    ready = [torch.cuda.Event() for _ in range(2)]
+    free = [torch.cuda.Event() for _ in range(2)]
 
-    def e2e_step():
-        pos_e2e.copy_(pos_host, non_blocking=True)
-        target_e2e.copy_(target_host, non_blocking=True)
-        leaf = pos_e2e.detach().requires_grad_(True)
-        loss = step(leaf, target_e2e)
-        loss.item()
+    def upload(slot):
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(free[slot])  # the step that last read this buffer is done
+            buffers[slot][0].copy_(pos_host, non_blocking=True)
+            buffers[slot][1].copy_(target_host, non_blocking=True)
+            ready[slot].record(copy_stream)
 
-    e2e_ms = timed_loop(e2e_step)
+    def e2e_loop():
+        main = torch.cuda.current_stream(dev)
+        for slot in range(2):
+            free[slot].record(main)
+        upload(0)
+        for i in range(args.steps):
+            slot = i % 2
+            main.wait_event(ready[slot])
+            if i + 1 < args.steps:
+                upload(1 - slot)
+            pos_in, target_in = buffers[slot]
+            loss = step(pos_in.detach().requires_grad_(True), target_in)
+            free[slot].record(main)
+            loss.item()
+
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e2e_start, e2e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_start.record()
+    e2e_loop()
+    e2e_end.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e2e_t = torch.tensor([e2e_start.elapsed_time(e2e_end)], device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    e2e_ms = e2e_t.item() / args.steps
 
     pixels_total = args.views * res * res
     value = pixels_total / (ms / 1e3) / 1e6

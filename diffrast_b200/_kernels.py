@@ -306,21 +306,29 @@ def silhouette_edges(pos3: Tensor, tri: Tensor, neighbours: Tensor) -> Tensor:
 
 
 @timed("antialias_fwd")
-def antialias_fwd(color, rast, pos3, tri, neighbours) -> Tensor:
+def antialias_fwd(color, rast, pos3, tri, neighbours, record_pairs: bool = False):
+    """Antialiased colour, and the pair records for the backward pass when ``record_pairs``."""
     batch, height, width, channels = color.shape
     out = torch.empty_like(color)
+    pairs = None
+    if record_pairs:
+        nbytes = N.lib().dr_antialias_pair_bytes(batch, height, width)
+        pairs = torch.empty(nbytes, dtype=torch.uint8, device=color.device)
     N.check(
         N.lib().dr_antialias_fwd(color.data_ptr(), rast.data_ptr(), pos3.data_ptr(), pos3.shape[0],
                                  pos3.shape[1], tri.data_ptr(), tri.shape[0],
                                  neighbours.data_ptr(), batch, height, width, channels,
-                                 out.data_ptr(), N.stream(color.device)),
+                                 out.data_ptr(), N.ptr(pairs), 0 if pairs is None else pairs.numel(),
+                                 N.stream(color.device)),
         "dr_antialias_fwd",
     )  # fmt: skip
-    return out
+    return out, pairs
 
 
 @timed("antialias_bwd")
-def antialias_bwd(color, rast, pos3, tri, neighbours, grad_out, boost):
+def antialias_bwd(color, rast, pos3, tri, neighbours, grad_out, boost, pairs=None):
+    """Gradients of colour and positions; ``pairs`` from :func:`antialias_fwd` skips the edge
+    tests (same result)."""
     batch, height, width, channels = color.shape
     grad_color = torch.empty_like(color)
     grad_pos = torch.zeros_like(pos3)
@@ -328,7 +336,8 @@ def antialias_bwd(color, rast, pos3, tri, neighbours, grad_out, boost):
         N.lib().dr_antialias_bwd(color.data_ptr(), rast.data_ptr(), pos3.data_ptr(), pos3.shape[0],
                                  pos3.shape[1], tri.data_ptr(), tri.shape[0],
                                  neighbours.data_ptr(), batch, height, width, channels,
-                                 grad_out.data_ptr(), float(boost), grad_color.data_ptr(),
+                                 grad_out.data_ptr(), float(boost), N.ptr(pairs),
+                                 0 if pairs is None else pairs.numel(), grad_color.data_ptr(),
                                  grad_pos.data_ptr(), N.stream(color.device)),
         "dr_antialias_bwd",
     )  # fmt: skip

@@ -204,6 +204,25 @@ __device__ __forceinline__ Pair eval_pair(const AaCtx& a, long long b, int row, 
   return r;
 }
 
+// The pairs of every pixel as the forward pass found them, so that the backward pass reads them
+// instead of repeating the edge tests: for the right (low nibble) and lower (high nibble) pair
+// of pixel p, bit 3 = active, bit 2 = the crossing was found from p's side, bits 0-1 = the edge
+// of the owning triangle; t[p] holds the two crossings t (zero when inactive).
+struct PairRecords {
+  float2* t;
+  uint8_t* code;
+};
+
+__device__ __forceinline__ unsigned pair_code(const Pair& r) {
+  return 8u | (r.use_p ? 4u : 0u) | static_cast<unsigned>(r.edge);
+}
+
+// Blend coefficients (bp, bq) of a recorded pair, as eval_pair forms them from t.
+__device__ __forceinline__ float2 recorded_blend(unsigned code, float t) {
+  if (!(code & 8u)) return make_float2(0.f, 0.f);
+  return t < 0.5f ? make_float2(sub(0.5f, t), 0.f) : make_float2(0.f, sub(t, 0.5f));
+}
+
 // Pixel tiling of the antialias kernels: a block of 32 x 8 threads covers a 31 x 7 tile of output
 // pixels plus a one-pixel halo to the left and above. Each thread evaluates the right pair of its
 // pixel (unless it is in the halo row) and the lower pair (unless it is in the halo column) once,
@@ -212,26 +231,41 @@ __device__ __forceinline__ Pair eval_pair(const AaCtx& a, long long b, int row, 
 constexpr int kAaThreadsX = 32, kAaThreadsY = 8;
 constexpr int kAaTileX = kAaThreadsX - 1, kAaTileY = kAaThreadsY - 1;
 
-__global__ void __launch_bounds__(256, 6) aa_fwd_kernel(const AaCtx a, float* __restrict__ out) {
+__global__ void __launch_bounds__(256, 6) aa_fwd_kernel(const AaCtx a, float* __restrict__ out,
+                                                        PairRecords rec) {
   __shared__ float2 hk[kAaThreadsY][kAaThreadsX], vk[kAaThreadsY][kAaThreadsX];
   const int tx = threadIdx.x % kAaThreadsX, ty = threadIdx.x / kAaThreadsX;
   const int col = blockIdx.x * kAaTileX + tx - 1, row = blockIdx.y * kAaTileY + ty - 1;
   const long long b = blockIdx.z;
   const bool in_image = col >= 0 && col < a.width && row >= 0 && row < a.height;
-  float2 h = make_float2(0.f, 0.f), v = make_float2(0.f, 0.f);
+  float2 h = make_float2(0.f, 0.f), v = make_float2(0.f, 0.f), t = make_float2(0.f, 0.f);
+  unsigned codes = 0u;
   if (in_image && ty >= 1 && col + 1 < a.width) {
     const Pair r = eval_pair(a, b, row, col, true);
     h = make_float2(r.bp, r.bq);
+    if (r.active) {
+      t.x = r.t;
+      codes = pair_code(r);
+    }
   }
   if (in_image && tx >= 1 && row + 1 < a.height) {
     const Pair r = eval_pair(a, b, row, col, false);
     v = make_float2(r.bp, r.bq);
+    if (r.active) {
+      t.y = r.t;
+      codes |= pair_code(r) << 4;
+    }
   }
   hk[ty][tx] = h;
   vk[ty][tx] = v;
   __syncthreads();
   if (!in_image || tx < 1 || ty < 1) return;
   const long long p = (b * a.height + row) * a.width + col;
+  if (rec.code != nullptr) {
+    // Interior threads evaluated both pairs of their pixel.
+    rec.t[p] = t;
+    rec.code[p] = static_cast<uint8_t>(codes);
+  }
   // Blend coefficients and partners, in the reference's accumulation order: right pair (this
   // pixel first), left pair (second), lower pair (first), upper pair (second).
   const float k[4] = {hk[ty][tx].x, hk[ty][tx - 1].y, vk[ty][tx].x, vk[ty - 1][tx].y};
@@ -329,6 +363,75 @@ __global__ void __launch_bounds__(256, 5) aa_bwd_kernel(const AaCtx a,
   }
 }
 
+// Backward pass from the pairs recorded by the forward pass: one thread per pixel, no edge
+// tests. Same arithmetic as aa_bwd_kernel for the colour gradient and for the crossings of the
+// pixel's own (right and lower) pairs, whose position gradients it scatters.
+__global__ void __launch_bounds__(256) aa_bwd_recorded_kernel(const AaCtx a,
+                                                              const float2* __restrict__ rec_t,
+                                                              const uint8_t* __restrict__ rec_code,
+                                                              long long total,
+                                                              const float* __restrict__ grad_out,
+                                                              float boost,
+                                                              float* __restrict__ grad_color,
+                                                              float* __restrict__ grad_pos) {
+  const long long p = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (p >= total) return;
+  const long long hw = static_cast<long long>(a.height) * a.width;
+  const long long b = p / hw;
+  const int rem = static_cast<int>(p - b * hw);
+  const int row = rem / a.width, col = rem - row * a.width;
+  const unsigned code = __ldg(rec_code + p);
+  const unsigned code_l = col > 0 ? __ldg(rec_code + p - 1) & 15u : 0u;
+  const unsigned code_u = row > 0 ? __ldg(rec_code + p - a.width) >> 4 : 0u;
+  const float2 t = (code & 0x88u) ? __ldg(rec_t + p) : make_float2(0.f, 0.f);
+  const float t_l = (code_l & 8u) ? __ldg(rec_t + p - 1).x : 0.f;
+  const float t_u = (code_u & 8u) ? __ldg(rec_t + p - a.width).y : 0.f;
+  const float2 right = recorded_blend(code & 15u, t.x), down = recorded_blend(code >> 4, t.y);
+  const float2 left = recorded_blend(code_l, t_l), up = recorded_blend(code_u, t_u);
+  const float kp[4] = {-right.x, -left.y, -down.x, -up.y};
+  const float kq[4] = {right.y, left.x, down.y, up.x};
+  const long long other[4] = {p + 1, p - 1, p + a.width, p - a.width};
+  const bool own[2] = {(code & 8u) != 0u, (code & 0x80u) != 0u};
+  const float own_t[2] = {t.x, t.y};
+  const int C = a.channels;
+  float grad_t[2] = {0.f, 0.f};
+  for (int c = 0; c < C; ++c) {
+    const float g_self = grad_out[p * C + c];
+    float value = g_self;
+    for (int i = 0; i < 4; ++i) {
+      if (kp[i] != 0.0f || kq[i] != 0.0f) value += kp[i] * g_self + kq[i] * grad_out[other[i] * C + c];
+    }
+    grad_color[p * C + c] = value;
+    for (int d = 0; d < 2; ++d) {
+      if (!own[d]) continue;
+      const long long q = other[d == 0 ? 0 : 2];
+      const float c_p = __ldg(a.color + p * C + c), c_q = __ldg(a.color + q * C + c);
+      grad_t[d] += own_t[d] < 0.5f ? -g_self * (c_q - c_p) : grad_out[q * C + c] * (c_p - c_q);
+    }
+  }
+  const long long pb = a.pos_batch == 1 ? 0 : b;
+  for (int d = 0; d < 2; ++d) {
+    if (!own[d]) continue;
+    const float g = grad_t[d] * boost;
+    if (g == 0.0f) continue;
+    const unsigned c4 = d == 0 ? code & 15u : code >> 4;
+    const bool horizontal = d == 0;
+    const int row_q = horizontal ? row : row + 1, col_q = horizontal ? col + 1 : col;
+    const long long q = other[d == 0 ? 0 : 2];
+    Pair r;
+    r.use_p = (c4 & 4u) != 0u;
+    r.edge = static_cast<int>(c4 & 3u);
+    r.owner = aa_triangle(a.rast[r.use_p ? p : q].w, a.num_tri);
+    const float xp = pixel_centre(col, a.width), yp = pixel_centre(row, a.height);
+    const float xq = pixel_centre(col_q, a.width), yq = pixel_centre(row_q, a.height);
+    r.sx = r.use_p ? xp : xq;
+    r.sy = r.use_p ? yp : yq;
+    r.dx = r.use_p ? xq : xp;
+    r.dy = r.use_p ? yq : yp;
+    add_edge_gradient(a, grad_pos, pb, r, r.use_p ? g : -g);
+  }
+}
+
 __global__ void __launch_bounds__(256) silhouette_kernel(const AaCtx a, long long total,
                                                          uint8_t* __restrict__ out) {
   const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
@@ -373,10 +476,26 @@ AaCtx make_ctx(const float* color, const float* rast, const float* pos, int64_t 
   return a;
 }
 
+size_t pair_record_bytes(long long pixels) {
+  return align256(sizeof(float2) * static_cast<size_t>(pixels)) + align256(static_cast<size_t>(pixels));
+}
+
+PairRecords pair_records(void* pairs, long long pixels) {
+  if (pairs == nullptr) return {nullptr, nullptr};
+  char* p = static_cast<char*>(pairs);
+  return {reinterpret_cast<float2*>(p),
+          reinterpret_cast<uint8_t*>(p + align256(sizeof(float2) * static_cast<size_t>(pixels)))};
+}
+
 }  // namespace
 }  // namespace dr
 
 using namespace dr;
+
+extern "C" size_t dr_antialias_pair_bytes(int64_t batch, int32_t height, int32_t width) {
+  if (batch < 0 || height < 0 || width < 0) return 0;
+  return pair_record_bytes(batch * static_cast<long long>(height) * width);
+}
 
 extern "C" size_t dr_edge_neighbours_workspace_bytes(int64_t num_tri) {
   const unsigned long long slots = table_slots(num_tri < 0 ? 0 : num_tri);
@@ -429,12 +548,13 @@ extern "C" int dr_antialias_fwd(const float* color, const float* rast, const flo
                                 int64_t pos_batch, int64_t num_vert, const int32_t* tri,
                                 int64_t num_tri, const int64_t* neighbours, int64_t batch,
                                 int32_t height, int32_t width, int32_t channels, float* out,
-                                void* stream) {
+                                void* pairs, size_t pair_bytes, void* stream) {
   if (bad_aa_args(color, rast, pos, pos_batch, num_vert, tri, num_tri, neighbours, batch, height,
                   width, channels) ||
       out == nullptr)
     return DR_ERR_INVALID_ARGUMENT;
   const long long total = batch * static_cast<long long>(height) * width;
+  if (pairs != nullptr && pair_bytes < pair_record_bytes(total)) return DR_ERR_WORKSPACE_TOO_SMALL;
   if (total == 0 || channels == 0) return DR_OK;
   if (num_tri == 0) {
     cudaError_t err = cudaMemcpyAsync(out, color, sizeof(float) * total * channels,
@@ -445,7 +565,7 @@ extern "C" int dr_antialias_fwd(const float* color, const float* rast, const flo
                            width, channels);
   if (batch > 65535) return DR_ERR_TOO_LARGE;
   const dim3 grid((width + kAaTileX - 1) / kAaTileX, (height + kAaTileY - 1) / kAaTileY, batch);
-  aa_fwd_kernel<<<grid, 256, 0, as_stream(stream)>>>(a, out);
+  aa_fwd_kernel<<<grid, 256, 0, as_stream(stream)>>>(a, out, pair_records(pairs, total));
   return launch_status();
 }
 
@@ -454,12 +574,14 @@ extern "C" int dr_antialias_bwd(const float* color, const float* rast, const flo
                                 int64_t num_tri, const int64_t* neighbours, int64_t batch,
                                 int32_t height, int32_t width, int32_t channels,
                                 const float* grad_out, float pos_gradient_boost,
-                                float* grad_color, float* grad_pos, void* stream) {
+                                const void* pairs, size_t pair_bytes, float* grad_color,
+                                float* grad_pos, void* stream) {
   if (bad_aa_args(color, rast, pos, pos_batch, num_vert, tri, num_tri, neighbours, batch, height,
                   width, channels) ||
       grad_out == nullptr || grad_color == nullptr || (num_tri > 0 && grad_pos == nullptr))
     return DR_ERR_INVALID_ARGUMENT;
   const long long total = batch * static_cast<long long>(height) * width;
+  if (pairs != nullptr && pair_bytes < pair_record_bytes(total)) return DR_ERR_WORKSPACE_TOO_SMALL;
   if (total == 0 || channels == 0) return DR_OK;
   if (num_tri == 0) {
     cudaError_t err = cudaMemcpyAsync(grad_color, grad_out, sizeof(float) * total * channels,
@@ -469,6 +591,12 @@ extern "C" int dr_antialias_bwd(const float* color, const float* rast, const flo
   const AaCtx a = make_ctx(color, rast, pos, pos_batch, num_vert, tri, num_tri, neighbours, height,
                            width, channels);
   if (batch > 65535) return DR_ERR_TOO_LARGE;
+  if (pairs != nullptr) {
+    const PairRecords rec = pair_records(const_cast<void*>(pairs), total);
+    aa_bwd_recorded_kernel<<<blocks_for(total, 256), 256, 0, as_stream(stream)>>>(
+        a, rec.t, rec.code, total, grad_out, pos_gradient_boost, grad_color, grad_pos);
+    return launch_status();
+  }
   const dim3 grid((width + kAaTileX - 1) / kAaTileX, (height + kAaTileY - 1) / kAaTileY, batch);
   aa_bwd_kernel<<<grid, 256, 0, as_stream(stream)>>>(a, grad_out,
                                                                         pos_gradient_boost,

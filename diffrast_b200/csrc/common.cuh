@@ -86,8 +86,12 @@ __device__ __forceinline__ long long pack_key(float depth, int tri) {
 // Non-finite vertices are rejected by the caller. All conditions are conjunctions of pure
 // functions of the same rounded values, so testing the cheap edge signs first and returning early
 // changes no result; it only skips the tolerance and depth arithmetic for pixels outside.
+//
+// reach_x and reach_y are the per-triangle maxima of |x| + |w| and |y| + |w| over the vertices
+// (coverage_reach), which callers testing many pixels of one triangle compute once.
 __device__ __forceinline__ long long coverage_key(const Vert& v0, const Vert& v1, const Vert& v2,
-                                                  float px, float py, int tri) {
+                                                  float px, float py, int tri, float reach_x,
+                                                  float reach_y) {
   const float a0 = sub(v0.x, mul(px, v0.w)), a1 = sub(v1.x, mul(px, v1.w)),
               a2 = sub(v2.x, mul(px, v2.w));
   const float c0 = sub(v0.y, mul(py, v0.w)), c1 = sub(v1.y, mul(py, v1.w)),
@@ -113,10 +117,6 @@ __device__ __forceinline__ long long coverage_key(const Vert& v0, const Vert& v1
   if (e1 == 0.0f && !on_edge_inside(a2, c2, v2.w, a0, c0, v0.w)) return kEmptyKey;
   if (e2 == 0.0f && !on_edge_inside(a0, c0, v0.w, a1, c1, v1.w)) return kEmptyKey;
 
-  const float reach_x = nanmax(nanmax(add(fabsf(v0.x), fabsf(v0.w)), add(fabsf(v1.x), fabsf(v1.w))),
-                               add(fabsf(v2.x), fabsf(v2.w)));
-  const float reach_y = nanmax(nanmax(add(fabsf(v0.y), fabsf(v0.w)), add(fabsf(v1.y), fabsf(v1.w))),
-                               add(fabsf(v2.y), fabsf(v2.w)));
   const float span_x = add(add(fabsf(a0), fabsf(a1)), fabsf(a2));
   const float span_y = add(add(fabsf(c0), fabsf(c1)), fabsf(c2));
   const float bound = mul(add(mul(reach_x, span_y), mul(span_x, add(reach_y, span_y))), kAreaTolerance);
@@ -127,6 +127,22 @@ __device__ __forceinline__ long long coverage_key(const Vert& v0, const Vert& v1
   const float depth = dvd(ez, ew);
   if (!(depth >= -1.0f && depth <= 1.0f)) return kEmptyKey;
   return pack_key(depth, tri);
+}
+
+// Largest |x| + |w| and |y| + |w| over the three vertices, the magnitude terms of the area
+// tolerance (reference.py:321-327).
+__device__ __forceinline__ float2 coverage_reach(const Vert& v0, const Vert& v1, const Vert& v2) {
+  return make_float2(
+      nanmax(nanmax(add(fabsf(v0.x), fabsf(v0.w)), add(fabsf(v1.x), fabsf(v1.w))),
+             add(fabsf(v2.x), fabsf(v2.w))),
+      nanmax(nanmax(add(fabsf(v0.y), fabsf(v0.w)), add(fabsf(v1.y), fabsf(v1.w))),
+             add(fabsf(v2.y), fabsf(v2.w))));
+}
+
+__device__ __forceinline__ long long coverage_key(const Vert& v0, const Vert& v1, const Vert& v2,
+                                                  float px, float py, int tri) {
+  const float2 r = coverage_reach(v0, v1, v2);
+  return coverage_key(v0, v1, v2, px, py, tri, r.x, r.y);
 }
 
 // Status of the launches just made on this thread.

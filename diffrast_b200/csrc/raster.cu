@@ -112,15 +112,33 @@ __device__ __forceinline__ void pixel_range(float lo, float hi, int size, int& f
   last = static_cast<int>(l);
 }
 
+// Hardware approximations (at most a few ulp from the exact results over the whole float range,
+// subnormals included) for the margins and bounds that only decide which pixels get an exact test.
+__device__ __forceinline__ float approx_rcp(float x) {
+  float r;
+  asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float approx_sqrt(float x) {
+  float r;
+  asm("sqrt.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
 // Direct triangles of a warp, staged so that any lane can work on any of them (structure of
 // arrays, indexed by the triangle's rank among the warp's direct triangles).
+// Rows a warp can have queued for exact tests (a power of two, at least 63).
+constexpr int kRing = 64;
+
 struct WarpTris {
   float4 v[3][32];     // clip-space vertices, for the exact test
   float4 edge[3][32];  // NDC half-planes A x + B y + C >= -D, stored as (1 / A, B, C + D, A)
+  float2 reach[32];    // coverage_reach of the triangle
   int t[32], b[32], c0[32], c1[32], r0[32], spans[32], end[32];
-  // Rows of the current batch that have pixels to test: triangle rank, row, first column and
-  // the inclusive prefix sum of their pixel counts.
-  int row_tri[32], row_y[32], row_col[32], row_end[32];
+  // Ring of rows with pixels to test: (triangle rank, row, column of the row's pixel number 0,
+  // number of pixels queued up to the row's end) and the row's NDC centre.
+  int4 row[kRing];
+  float row_py[kRing];
 };
 
 __global__ void __launch_bounds__(256) setup_kernel(
@@ -210,6 +228,7 @@ __global__ void __launch_bounds__(256) setup_kernel(
     w.v[0][rank] = make_float4(v0.x, v0.y, v0.z, v0.w);
     w.v[1][rank] = make_float4(v1.x, v1.y, v1.z, v1.w);
     w.v[2][rank] = make_float4(v2.x, v2.y, v2.z, v2.w);
+    w.reach[rank] = coverage_reach(v0, v1, v2);
     w.t[rank] = t;
     w.b[rank] = b;
     w.c0[rank] = c0;
@@ -230,14 +249,22 @@ __global__ void __launch_bounds__(256) setup_kernel(
       const int i = (k + 1) % 3, j = (k + 2) % 3;
       const float A = -o * (ny[j] - ny[i]), B = o * (nx[j] - nx[i]);
       const float C = -(A * nx[i] + B * ny[i]);
-      const float D = delta * sqrtf(A * A + B * B) +
+      const float D = delta * approx_sqrt(A * A + B * B) +
                       4e-6f * (fabsf(A) + fabsf(B)) * (1.0f + fabsf(nx[i]) + fabsf(ny[i]));
       // Row bounds are x >= (-(B y + C) - D) / A (A > 0) or x <= it (A < 0): keep 1 / A.
-      w.edge[k][rank] = make_float4(A != 0.0f ? 1.0f / A : 0.0f, B, C + D, A);
+      w.edge[k][rank] = make_float4(A != 0.0f ? approx_rcp(A) : 0.0f, B, C + D, A);
     }
   }
   __syncwarp();
-  int done = 0;  // triangles whose rows all precede this batch
+  // Rows with pixels to test join a ring of kRing records; exact tests run 32 pixels at a time as
+  // soon as 32 are queued (and once more at the end), so that the pixels of consecutive row
+  // batches share test iterations. After a drain fewer than 32 pixels (so at most 31 rows) are
+  // pending and a batch adds at most 32 rows, so the ring never overwrites a pending row.
+  int done = 0;           // triangles whose rows all precede this batch
+  int queued_rows = 0;    // rows appended to the ring so far
+  int consumed_rows = 0;  // rows whose pixels have all been tested
+  int queued_px = 0;      // pixels appended so far
+  int tested_px = 0;      // pixels tested so far
   for (int base = 0; base < all_rows; base += 32) {
     // Phase A. Bit e - base - 1 marks a triangle whose rows end at e within (base, base + 32];
     // the owner of row item base + lane is the number of triangles ending at or before it.
@@ -248,12 +275,13 @@ __global__ void __launch_bounds__(256) setup_kernel(
     const int k = done + __popc(ends & ((1u << lane) - 1u));
     done += __popc(ends);
     int count = 0, row = 0, cl = 0;
+    float py = 0.0f;
     if (item < all_rows) {
       row = w.r0[k] + item - (k > 0 ? w.end[k - 1] : 0);
       cl = w.c0[k];
       int cr = w.c1[k];
+      py = __ldg(centres + width + row);
       if (w.spans[k]) {
-        const float py = __ldg(centres + width + row);
         float lo = -__int_as_float(0x7f800000), hi = __int_as_float(0x7f800000);
         bool empty = false;
         for (int e = 0; e < 3; ++e) {
@@ -274,7 +302,7 @@ __global__ void __launch_bounds__(256) setup_kernel(
       }
       count = max(0, cr - cl + 1);
     }
-    // Compact the rows that have pixels and number their pixels.
+    // Append the rows that have pixels, numbering their pixels after those already queued.
     const unsigned busy = __ballot_sync(0xffffffffu, count > 0);
     const int slot = __popc(busy & ((1u << lane) - 1u));
     int pix_end = count;
@@ -283,37 +311,46 @@ __global__ void __launch_bounds__(256) setup_kernel(
       const int y = __shfl_up_sync(0xffffffffu, pix_end, o);
       if (static_cast<int>(lane) >= o) pix_end += y;
     }
-    const int all_pixels = __shfl_sync(0xffffffffu, pix_end, 31);
-    __syncwarp();
     if (count > 0) {
-      w.row_tri[slot] = k;
-      w.row_y[slot] = row;
-      w.row_col[slot] = cl;
-      w.row_end[slot] = pix_end;
+      const int q = (queued_rows + slot) & (kRing - 1);
+      const int last = queued_px + pix_end;  // pixels queued up to the end of this row
+      // (triangle rank, row, column of pixel number 0 of this row's numbering, end)
+      w.row[q] = make_int4(k, row, cl - (last - count), last);
+      w.row_py[q] = py;
     }
+    queued_rows += __popc(busy);
+    queued_px += __shfl_sync(0xffffffffu, pix_end, 31);
     __syncwarp();
     // Phase B: one exact coverage test per lane.
-    int finished = 0;
-    for (int pbase = 0; pbase < all_pixels; pbase += 32) {
+    const bool final_batch = base + 32 >= all_rows;
+    while (queued_px - tested_px >= 32 || (final_batch && queued_px > tested_px)) {
+      // Rows ending within (tested_px, tested_px + 32] mark their last pixel; the owner of pixel
+      // tested_px + lane is the number of such rows ending before it.
+      const int n = consumed_rows + static_cast<int>(lane);
       unsigned pbit = 0u;
-      if (count > 0 && pix_end > pbase && pix_end <= pbase + 32) pbit = 1u << (pix_end - pbase - 1);
+      if (n < queued_rows) {
+        const int e = w.row[n & (kRing - 1)].w;
+        if (e <= tested_px + 32) pbit = 1u << (e - tested_px - 1);
+      }
       const unsigned pends = __reduce_or_sync(0xffffffffu, pbit);
-      const int pitem = pbase + static_cast<int>(lane);
-      const int r = finished + __popc(pends & ((1u << lane) - 1u));
-      finished += __popc(pends);
-      if (pitem >= all_pixels) continue;
-      const int kk = w.row_tri[r];
-      const int y = w.row_y[r];
-      const int col = w.row_col[r] + pitem - (r > 0 ? w.row_end[r - 1] : 0);
+      const int pitem = tested_px + static_cast<int>(lane);
+      const int r = (consumed_rows + __popc(pends & ((1u << lane) - 1u))) & (kRing - 1);
+      consumed_rows += __popc(pends);
+      tested_px += 32;
+      if (pitem >= queued_px) continue;
+      const int4 rec = w.row[r];
+      const int kk = rec.x, y = rec.y, col = rec.z + pitem;
       const float4 a = w.v[0][kk], bb = w.v[1][kk], cc = w.v[2][kk];
+      const float2 reach = w.reach[kk];
       const long long key = coverage_key({a.x, a.y, a.z, a.w}, {bb.x, bb.y, bb.z, bb.w},
                                          {cc.x, cc.y, cc.z, cc.w}, __ldg(centres + col),
-                                         __ldg(centres + width + y), w.t[kk]);
+                                         w.row_py[r], w.t[kk], reach.x, reach.y);
       if (key == kEmptyKey) continue;
       const long long off = (static_cast<long long>(w.b[kk]) * height + y) * width + col;
       if (prev != nullptr && !(key > __ldg(prev + off))) continue;
       atomicMin(keys + off, key);
     }
+    tested_px = min(tested_px, queued_px);
     __syncwarp();
   }
   // Warp-aggregated append of the large triangles and of their pair counts.

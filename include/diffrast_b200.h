@@ -191,17 +191,27 @@ int dr_silhouette_edges(const float* pos, int64_t pos_batch, int64_t num_vert,
                         const int32_t* tri, int64_t num_tri, const int64_t* neighbours,
                         uint8_t* silhouette, void* stream);
 
+/* Bytes of the pair records that dr_antialias_fwd can leave for dr_antialias_bwd (about 9 bytes
+ * per pixel): per pixel, the crossing t and the outcome of its right and lower pixel pairs. */
+size_t dr_antialias_pair_bytes(int64_t batch, int32_t height, int32_t width);
+
+/* Forward pass (_triton_antialias.py:272-304). pairs may be NULL; otherwise the records of
+ * dr_antialias_pair_bytes() bytes (pair_bytes at least that) are written. */
 int dr_antialias_fwd(const float* color, const float* rast, const float* pos, int64_t pos_batch,
                      int64_t num_vert, const int32_t* tri, int64_t num_tri,
                      const int64_t* neighbours, int64_t batch, int32_t height, int32_t width,
-                     int32_t channels, float* out, void* stream);
+                     int32_t channels, float* out, void* pairs, size_t pair_bytes, void* stream);
 
-/* grad_color is written; grad_pos [pos_batch, num_vert, 4] is ACCUMULATED (clear it first). */
+/* Backward pass (_triton_antialias.py:306-320). grad_color is written; grad_pos
+ * [pos_batch, num_vert, 4] is ACCUMULATED (clear it first). With pairs from a dr_antialias_fwd
+ * call on the same color, rast, pos, tri and neighbours, the edge tests are not repeated; with
+ * pairs NULL they are. Both give the same result. */
 int dr_antialias_bwd(const float* color, const float* rast, const float* pos, int64_t pos_batch,
                      int64_t num_vert, const int32_t* tri, int64_t num_tri,
                      const int64_t* neighbours, int64_t batch, int32_t height, int32_t width,
                      int32_t channels, const float* grad_out, float pos_gradient_boost,
-                     float* grad_color, float* grad_pos, void* stream);
+                     const void* pairs, size_t pair_bytes, float* grad_color, float* grad_pos,
+                     void* stream);
 
 #ifdef __cplusplus
 }

@@ -360,6 +360,30 @@ def test_antialias_edge_set_matches_oracle_random():
         fwd_close(out, ref)
 
 
+def test_antialias_recorded_pairs_match_recomputed_pairs():
+    """The backward pass from the forward pass's pair records equals the one that repeats the
+    edge tests (the C ABI offers both)."""
+    from diffrast_b200 import _kernels as K
+
+    for seed in (0, 1):
+        pos, tri = scenes.random_mesh(80, torch.Generator().manual_seed(seed), batch=2)
+        rast, _ = oracle.rasterize(pos, tri, (40, 56))
+        gen = torch.Generator().manual_seed(seed + 20)
+        color = torch.rand(2, 40, 56, 3, generator=gen).cuda()
+        grad_out = torch.randn(2, 40, 56, 3, generator=gen).cuda()
+        pos, tri, rast = pos.cuda(), tri.cuda(), rast.cuda()
+        nb = dr.antialias_construct_topology_hash(tri).neighbours(tri)
+        out, pairs = K.antialias_fwd(color, rast, pos, tri, nb, record_pairs=True)
+        out_plain, none = K.antialias_fwd(color, rast, pos, tri, nb)
+        assert none is None and torch.equal(out, out_plain)
+        gc_rec, gp_rec = K.antialias_bwd(color, rast, pos, tri, nb, grad_out, 1.0, pairs)
+        gc, gp = K.antialias_bwd(color, rast, pos, tri, nb, grad_out, 1.0)
+        torch.testing.assert_close(gc_rec, gc, rtol=1e-6, atol=1e-7)
+        # Position gradients are sums of atomically added terms: only their order may differ.
+        torch.testing.assert_close(gp_rec, gp, rtol=1e-5, atol=1e-6)
+        assert (gp != 0).any()
+
+
 def test_straight_edge_coverage_is_exact(ctx):
     edge = 0.3
     pos = torch.tensor([[[-2.0, -2.0, 0.0, 1.0], [edge, -2.0, 0.0, 1.0], [edge, 2.0, 0.0, 1.0],
