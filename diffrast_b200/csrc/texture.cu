@@ -589,6 +589,62 @@ __global__ void __launch_bounds__(256) texture_bwd_kernel(
   }
   const unsigned lane = threadIdx.x & 31u;
   const bool vector = grad_stride == 4 && channels <= 4;
+  if (B != DR_BOUNDARY_CUBE && MODE != DR_FILTER_NEAREST) {
+    // Off a cube, a level's four taps form a quad that (off[0], off[3]) identifies (off[0] alone
+    // when wrapping): lanes sharing a quad sum all four taps' contributions at once, with one
+    // match per level instead of one per tap.
+    constexpr int kSides = MODE == DR_FILTER_LINEAR_MIPMAP_LINEAR ? 2 : 1;
+    for (int c0 = 0; c0 < channels; c0 += 4) {
+      const int group = min(4, channels - c0);
+      float g[4];
+      bool any_g = false;
+      for (int cc = 0; cc < 4; ++cc) {
+        g[cc] = live && cc < group ? grad_out[p * channels + c0 + cc] : 0.0f;
+        any_g |= g[cc] != 0.0f;
+      }
+#pragma unroll
+      for (int side = 0; side < kSides; ++side) {
+        const Footprint& f = side ? k.f_hi : k.f_lo;
+        const int level = side ? k.hi : k.lo;
+        const float scale =
+            MODE == DR_FILTER_LINEAR_MIPMAP_LINEAR ? (side ? k.frac : 1.0f - k.frac) : 1.0f;
+        const bool act = any_g && scale != 0.0f;
+        const unsigned any = __ballot_sync(0xffffffffu, act);
+        if (any == 0u) continue;
+        unsigned peers = 1u << lane;
+        if (act) {
+          peers = __match_any_sync(
+              any, (static_cast<unsigned long long>(level) << 48) | static_cast<unsigned long long>(f.off[0]));
+          if (B != DR_BOUNDARY_WRAP) peers &= __match_any_sync(any, static_cast<unsigned long long>(f.off[3]));
+        }
+        const float gx = 1.0f - f.fx, gy = 1.0f - f.fy;
+        const float wq[4] = {scale * (gx * gy), scale * (f.fx * gy), scale * (gx * f.fy),
+                             scale * (f.fx * f.fy)};
+        float v[16];
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) v[4 * t + cc] = act && f.ok[t] ? g[cc] * wq[t] : 0.0f;
+        segmented_sum<16>(peers, v);
+        if (!act || (peers & ((1u << lane) - 1u)) != 0u) continue;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          // The group's sum decides, not the leader's own weight or validity: other lanes of the
+          // quad have other bilinear weights, and with zero padding other valid taps (a quad's
+          // four offsets are the same for the whole group; invalid taps contributed zero).
+          if (v[4 * t] == 0.0f && v[4 * t + 1] == 0.0f && v[4 * t + 2] == 0.0f && v[4 * t + 3] == 0.0f)
+            continue;
+          float* dst = L.grad[level] + f.off[t] * grad_stride + c0;
+          if (vector) {
+            red_add_v4(dst, v[4 * t], v[4 * t + 1], v[4 * t + 2], v[4 * t + 3]);
+          } else {
+            for (int cc = 0; cc < group; ++cc)
+              if (v[4 * t + cc] != 0.0f) red_add(dst + cc, v[4 * t + cc]);
+          }
+        }
+      }
+    }
+  } else {
   for (int c0 = 0; c0 < channels; c0 += 4) {
     const int group = min(4, channels - c0);
     float g[4];
@@ -618,6 +674,7 @@ __global__ void __launch_bounds__(256) texture_bwd_kernel(
           if (v[cc] != 0.0f) red_add(dst + cc, v[cc]);
       }
     }
+  }
   }
   if (!inside) return;
   const bool coord_grads = grad_uv != nullptr || grad_uv_da != nullptr || grad_bias != nullptr;

@@ -379,8 +379,9 @@ def test_antialias_recorded_pairs_match_recomputed_pairs():
         gc_rec, gp_rec = K.antialias_bwd(color, rast, pos, tri, nb, grad_out, 1.0, pairs)
         gc, gp = K.antialias_bwd(color, rast, pos, tri, nb, grad_out, 1.0)
         torch.testing.assert_close(gc_rec, gc, rtol=1e-6, atol=1e-7)
-        # Position gradients are sums of atomically added terms: only their order may differ.
-        torch.testing.assert_close(gp_rec, gp, rtol=1e-5, atol=1e-6)
+        # Position gradients are sums of atomically added terms: only their order may differ
+        # (the atomic-gradient tolerance of this file).
+        grad_close(gp_rec, gp)
         assert (gp != 0).any()
 
 
