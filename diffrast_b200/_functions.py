@@ -203,13 +203,13 @@ class TextureChain(torch.autograd.Function):
 
 class Antialias(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, color: Tensor, rast: Tensor, pos: Tensor, tri: Tensor, neighbours: Tensor,
+    def forward(ctx, color: Tensor, rast: Tensor, pos: Tensor, tri: Tensor, opposite: Tensor,
                 boost: float):
         pos3 = pos if pos.ndim == 3 else pos[None]
         # The pair records (about 9 bytes per pixel) spare the backward pass the edge tests.
-        out, pairs = K.antialias_fwd(color, rast, pos3, tri, neighbours,
+        out, pairs = K.antialias_fwd(color, rast, pos3, tri, opposite,
                                      record_pairs=any(ctx.needs_input_grad[:3]))
-        saved = (color, rast, pos3, tri, neighbours, pairs)
+        saved = (color, rast, pos3, tri, opposite, pairs)
         ctx.save_for_backward(*(_saveable(t) for t in saved))
         ctx.boost = boost
         ctx.pos_shape = pos.shape
@@ -218,7 +218,7 @@ class Antialias(torch.autograd.Function):
     @staticmethod
     @first_order("antialias")
     def backward(ctx, grad_out):
-        color, rast, pos3, tri, neighbours, pairs = ctx.saved_tensors
-        grad_color, grad_pos = K.antialias_bwd(color, rast, pos3, tri, neighbours,
+        color, rast, pos3, tri, opposite, pairs = ctx.saved_tensors
+        grad_color, grad_pos = K.antialias_bwd(color, rast, pos3, tri, opposite,
                                                grad_out.contiguous(), ctx.boost, pairs)
         return grad_color, None, grad_pos.view(ctx.pos_shape), None, None, None

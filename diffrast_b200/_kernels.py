@@ -296,17 +296,30 @@ def edge_neighbours(tri: Tensor) -> Tensor:
     return out
 
 
+def edge_opposite(tri: Tensor, neighbours: Tensor) -> Tensor:
+    """Vertex opposite each edge in the adjacent triangle (-1 where there is no single one),
+    int32 ``[triangles, 3]``: the antialias kernels' form of the adjacency."""
+    out = torch.empty((tri.shape[0], 3), dtype=torch.int32, device=tri.device)
+    if tri.shape[0]:
+        N.check(N.lib().dr_edge_opposite_vertices(tri.data_ptr(), neighbours.data_ptr(),
+                                                  tri.shape[0], out.data_ptr(),
+                                                  N.stream(tri.device)),
+                "dr_edge_opposite_vertices")  # fmt: skip
+    return out
+
+
 def silhouette_edges(pos3: Tensor, tri: Tensor, neighbours: Tensor) -> Tensor:
+    opposite = edge_opposite(tri, neighbours)
     out = torch.empty((pos3.shape[0], tri.shape[0], 3), dtype=torch.uint8, device=pos3.device)
     N.check(N.lib().dr_silhouette_edges(pos3.data_ptr(), pos3.shape[0], pos3.shape[1],
-                                        tri.data_ptr(), tri.shape[0], neighbours.data_ptr(),
+                                        tri.data_ptr(), tri.shape[0], opposite.data_ptr(),
                                         out.data_ptr(), N.stream(pos3.device)),
             "dr_silhouette_edges")  # fmt: skip
     return out.bool()
 
 
 @timed("antialias_fwd")
-def antialias_fwd(color, rast, pos3, tri, neighbours, record_pairs: bool = False):
+def antialias_fwd(color, rast, pos3, tri, opposite, record_pairs: bool = False):
     """Antialiased colour, and the pair records for the backward pass when ``record_pairs``."""
     batch, height, width, channels = color.shape
     out = torch.empty_like(color)
@@ -317,7 +330,7 @@ def antialias_fwd(color, rast, pos3, tri, neighbours, record_pairs: bool = False
     N.check(
         N.lib().dr_antialias_fwd(color.data_ptr(), rast.data_ptr(), pos3.data_ptr(), pos3.shape[0],
                                  pos3.shape[1], tri.data_ptr(), tri.shape[0],
-                                 neighbours.data_ptr(), batch, height, width, channels,
+                                 opposite.data_ptr(), batch, height, width, channels,
                                  out.data_ptr(), N.ptr(pairs), 0 if pairs is None else pairs.numel(),
                                  N.stream(color.device)),
         "dr_antialias_fwd",
@@ -326,7 +339,7 @@ def antialias_fwd(color, rast, pos3, tri, neighbours, record_pairs: bool = False
 
 
 @timed("antialias_bwd")
-def antialias_bwd(color, rast, pos3, tri, neighbours, grad_out, boost, pairs=None):
+def antialias_bwd(color, rast, pos3, tri, opposite, grad_out, boost, pairs=None):
     """Gradients of colour and positions; ``pairs`` from :func:`antialias_fwd` skips the edge
     tests (same result)."""
     batch, height, width, channels = color.shape
@@ -335,7 +348,7 @@ def antialias_bwd(color, rast, pos3, tri, neighbours, grad_out, boost, pairs=Non
     N.check(
         N.lib().dr_antialias_bwd(color.data_ptr(), rast.data_ptr(), pos3.data_ptr(), pos3.shape[0],
                                  pos3.shape[1], tri.data_ptr(), tri.shape[0],
-                                 neighbours.data_ptr(), batch, height, width, channels,
+                                 opposite.data_ptr(), batch, height, width, channels,
                                  grad_out.data_ptr(), float(boost), N.ptr(pairs),
                                  0 if pairs is None else pairs.numel(), grad_color.data_ptr(),
                                  grad_pos.data_ptr(), N.stream(color.device)),

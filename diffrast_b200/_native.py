@@ -68,6 +68,7 @@ _SIGNATURES = {
     "dr_edge_neighbours": (c_int, [_P, c_int64, _P, _P, c_size_t, _P]),
     "dr_edge_neighbours_noalloc_max_triangles": (c_int64, []),
     "dr_edge_neighbours_noalloc": (c_int, [_P, c_int64, _P, _P]),
+    "dr_edge_opposite_vertices": (c_int, [_P, _P, c_int64, _P, _P]),
     "dr_silhouette_edges": (c_int, [_P, c_int64, c_int64, _P, c_int64, _P, _P, _P]),
     "dr_antialias_pair_bytes": (c_size_t, [c_int64, c_int32, c_int32]),
     "dr_antialias_fwd": (

@@ -11,9 +11,11 @@
 //     and every pixel writes only its own output, so the forward pass and the colour gradient need
 //     no atomics and are deterministic. The position gradient of a pair is scattered once, by the
 //     block where its left or upper pixel is an output pixel.
-//   - The silhouette test runs on the fly for the one edge a pair crosses, from the edge
-//     adjacency (neighbours) and the two opposite vertices, instead of classifying every edge of
-//     every view beforehand.
+//   - The silhouette test runs on the fly for the one edge a pair crosses, instead of classifying
+//     every edge of every view beforehand. It needs the crossed triangle's own vertices (already
+//     loaded for the crossing) and one more: the vertex opposite the edge in the adjacent
+//     triangle, read from a per-edge table (dr_edge_opposite_vertices) built once per index
+//     buffer from the adjacency, so the test costs one dependent load.
 //   - Edge adjacency is built with a device hash table on 64-bit vertex-pair keys (count, first and
 //     second edge per key): no sort, deterministic, identical to the reference's result.
 // The edge tests use explicitly rounded operations in the reference's order so that the set of
@@ -33,7 +35,7 @@ struct AaCtx {
   const float4* rast;
   const float* pos;
   const int* tri;
-  const long long* neighbours;
+  const int* opposite;  // [num_tri, 3] vertex across each edge, -1 for a silhouette by topology
   long long pos_batch, num_vert;
   int num_tri;
   int height, width, channels;
@@ -75,25 +77,21 @@ __device__ __forceinline__ float side_sign(const float l[3], const float4& p) {
 }
 
 // Whether edge k of triangle t is a silhouette in view pb (reference.py:790-814): unshared, shared
-// by several, or shared with a triangle whose opposite vertex lies on the same side of it.
-__device__ __forceinline__ bool is_silhouette(const AaCtx& a, long long pb, int t, int k) {
-  const long long nb = __ldg(a.neighbours + 3 * static_cast<long long>(t) + k);
-  if (nb < 0) return true;
-  const long long base = pb * a.num_vert;
-  const float4* p4 = reinterpret_cast<const float4*>(a.pos);
-  const int start = __ldg(a.tri + 3 * static_cast<long long>(t) + (k + 1) % 3);
-  const int end = __ldg(a.tri + 3 * static_cast<long long>(t) + (k + 2) % 3);
-  const int opp1 = __ldg(a.tri + 3 * static_cast<long long>(t) + k);
-  const int opp2 = __ldg(a.tri + nb);  // edge nb = 3 t' + k' is opposite vertex tri[t'][k']
-  const float4 pa = __ldg(p4 + base + start), pb4 = __ldg(p4 + base + end);
-  const float A[3] = {pa.x, pa.y, pa.w}, B[3] = {pb4.x, pb4.y, pb4.w};
+// by several, or shared with a triangle whose opposite vertex lies on the same side of it. v holds
+// t's vertex indices and clip-space x, y, w.
+__device__ __forceinline__ bool silhouette_of(const AaCtx& a, long long pb, const Tri2& v, int t,
+                                              int k) {
+  const int opp = __ldg(a.opposite + 3 * static_cast<long long>(t) + k);
+  if (opp < 0) return true;
+  const int i = (k + 1) % 3, j = (k + 2) % 3;
+  const float A[3] = {v.x[i], v.y[i], v.w[i]}, B[3] = {v.x[j], v.y[j], v.w[j]};
   float l[3];
   for (int c = 0; c < 3; ++c) {
-    const int i = (c + 1) % 3, j = (c + 2) % 3;
-    l[c] = __fmaf_rn(A[i], B[j], -mul(A[j], B[i]));
+    const int ci = (c + 1) % 3, cj = (c + 2) % 3;
+    l[c] = __fmaf_rn(A[ci], B[cj], -mul(A[cj], B[ci]));
   }
-  const float s1 = side_sign(l, __ldg(p4 + base + opp1));
-  const float s2 = side_sign(l, __ldg(p4 + base + opp2));
+  const float s1 = side_sign(l, make_float4(v.x[k], v.y[k], 0.0f, v.w[k]));
+  const float s2 = side_sign(l, __ldg(reinterpret_cast<const float4*>(a.pos) + pb * a.num_vert + opp));
   return mul(s1, s2) > 0.0f;
 }
 
@@ -157,7 +155,7 @@ __device__ __forceinline__ Crossing crossing(const AaCtx& a, long long pb, int t
   const float flat = mul(fabsf(cross2(v.x[j], v.w[i], v.x[i], v.w[j])), static_cast<float>(a.width));
   const bool along = horizontal ? (steep >= flat) : (flat > steep);
   if (!along) return r;
-  if (!is_silhouette(a, pb, t, edge)) return r;
+  if (!silhouette_of(a, pb, v, t, edge)) return r;
   r.found = true;
   r.t = best;
   r.edge = edge;
@@ -439,12 +437,24 @@ __global__ void __launch_bounds__(256) silhouette_kernel(const AaCtx a, long lon
   const long long per_view = 3LL * a.num_tri;
   const long long pb = i / per_view;
   const long long e = i - pb * per_view;
-  out[i] = is_silhouette(a, pb, static_cast<int>(e / 3), static_cast<int>(e % 3)) ? 1 : 0;
+  const int t = static_cast<int>(e / 3);
+  out[i] = silhouette_of(a, pb, load_tri(a, pb, t), t, static_cast<int>(e % 3)) ? 1 : 0;
 }
 
 
+// Vertex opposite each edge in the triangle across it: tri[neighbours[e]], or -1 without a single
+// adjacent triangle (and for an index outside the edge range, which dr_edge_neighbours never gives).
+__global__ void __launch_bounds__(256) opposite_kernel(const int* __restrict__ tri,
+                                                       const long long* __restrict__ neighbours,
+                                                       long long edges, int* __restrict__ opposite) {
+  const long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (e >= edges) return;
+  const long long n = neighbours[e];
+  opposite[e] = (n >= 0 && n < edges) ? tri[n] : -1;
+}
+
 bool bad_aa_args(const float* color, const float* rast, const float* pos, int64_t pos_batch,
-                 int64_t num_vert, const int32_t* tri, int64_t num_tri, const int64_t* neighbours,
+                 int64_t num_vert, const int32_t* tri, int64_t num_tri, const int32_t* opposite,
                  int64_t batch, int32_t height, int32_t width, int32_t channels) {
   if (pos_batch < 1 || (pos_batch != 1 && pos_batch != batch)) return true;
   if (num_vert < 0 || num_tri < 0 || num_tri >= (1LL << 29) || batch < 0 || height < 0 ||
@@ -454,19 +464,19 @@ bool bad_aa_args(const float* color, const float* rast, const float* pos, int64_
   if (total > 0 && (color == nullptr || rast == nullptr)) return true;
   if ((reinterpret_cast<uintptr_t>(rast) & 15u) != 0 || (reinterpret_cast<uintptr_t>(pos) & 15u) != 0)
     return true;
-  if (num_tri > 0 && (tri == nullptr || neighbours == nullptr || pos == nullptr)) return true;
+  if (num_tri > 0 && (tri == nullptr || opposite == nullptr || pos == nullptr)) return true;
   return false;
 }
 
 AaCtx make_ctx(const float* color, const float* rast, const float* pos, int64_t pos_batch,
-               int64_t num_vert, const int32_t* tri, int64_t num_tri, const int64_t* neighbours,
+               int64_t num_vert, const int32_t* tri, int64_t num_tri, const int32_t* opposite,
                int32_t height, int32_t width, int32_t channels) {
   AaCtx a;
   a.color = color;
   a.rast = reinterpret_cast<const float4*>(rast);
   a.pos = pos;
   a.tri = tri;
-  a.neighbours = reinterpret_cast<const long long*>(neighbours);
+  a.opposite = opposite;
   a.pos_batch = pos_batch;
   a.num_vert = num_vert;
   a.num_tri = static_cast<int>(num_tri);
@@ -529,27 +539,38 @@ extern "C" int dr_edge_neighbours(const int32_t* tri, int64_t num_tri, int64_t* 
   return launch_status();
 }
 
+extern "C" int dr_edge_opposite_vertices(const int32_t* tri, const int64_t* neighbours,
+                                         int64_t num_tri, int32_t* opposite, void* stream) {
+  if (num_tri < 0 || num_tri >= (1LL << 29)) return DR_ERR_INVALID_ARGUMENT;
+  if (num_tri == 0) return DR_OK;
+  if (tri == nullptr || neighbours == nullptr || opposite == nullptr) return DR_ERR_INVALID_ARGUMENT;
+  const long long edges = 3 * num_tri;
+  opposite_kernel<<<blocks_for(edges, 256), 256, 0, as_stream(stream)>>>(
+      tri, reinterpret_cast<const long long*>(neighbours), edges, opposite);
+  return launch_status();
+}
+
 extern "C" int dr_silhouette_edges(const float* pos, int64_t pos_batch, int64_t num_vert,
-                                   const int32_t* tri, int64_t num_tri, const int64_t* neighbours,
+                                   const int32_t* tri, int64_t num_tri, const int32_t* opposite,
                                    uint8_t* silhouette, void* stream) {
   if (pos_batch < 1 || num_tri < 0 || num_tri >= (1LL << 29) || num_vert < 0)
     return DR_ERR_INVALID_ARGUMENT;
   const long long total = pos_batch * 3 * num_tri;
   if (total == 0) return DR_OK;
-  if (pos == nullptr || tri == nullptr || neighbours == nullptr || silhouette == nullptr ||
+  if (pos == nullptr || tri == nullptr || opposite == nullptr || silhouette == nullptr ||
       (reinterpret_cast<uintptr_t>(pos) & 15u) != 0)
     return DR_ERR_INVALID_ARGUMENT;
-  const AaCtx a = make_ctx(nullptr, nullptr, pos, pos_batch, num_vert, tri, num_tri, neighbours, 1, 1, 0);
+  const AaCtx a = make_ctx(nullptr, nullptr, pos, pos_batch, num_vert, tri, num_tri, opposite, 1, 1, 0);
   silhouette_kernel<<<blocks_for(total, 256), 256, 0, as_stream(stream)>>>(a, total, silhouette);
   return launch_status();
 }
 
 extern "C" int dr_antialias_fwd(const float* color, const float* rast, const float* pos,
                                 int64_t pos_batch, int64_t num_vert, const int32_t* tri,
-                                int64_t num_tri, const int64_t* neighbours, int64_t batch,
+                                int64_t num_tri, const int32_t* opposite, int64_t batch,
                                 int32_t height, int32_t width, int32_t channels, float* out,
                                 void* pairs, size_t pair_bytes, void* stream) {
-  if (bad_aa_args(color, rast, pos, pos_batch, num_vert, tri, num_tri, neighbours, batch, height,
+  if (bad_aa_args(color, rast, pos, pos_batch, num_vert, tri, num_tri, opposite, batch, height,
                   width, channels) ||
       out == nullptr)
     return DR_ERR_INVALID_ARGUMENT;
@@ -561,7 +582,7 @@ extern "C" int dr_antialias_fwd(const float* color, const float* rast, const flo
                                       cudaMemcpyDeviceToDevice, as_stream(stream));
     return static_cast<int>(err);
   }
-  const AaCtx a = make_ctx(color, rast, pos, pos_batch, num_vert, tri, num_tri, neighbours, height,
+  const AaCtx a = make_ctx(color, rast, pos, pos_batch, num_vert, tri, num_tri, opposite, height,
                            width, channels);
   if (batch > 65535) return DR_ERR_TOO_LARGE;
   const dim3 grid((width + kAaTileX - 1) / kAaTileX, (height + kAaTileY - 1) / kAaTileY, batch);
@@ -571,12 +592,12 @@ extern "C" int dr_antialias_fwd(const float* color, const float* rast, const flo
 
 extern "C" int dr_antialias_bwd(const float* color, const float* rast, const float* pos,
                                 int64_t pos_batch, int64_t num_vert, const int32_t* tri,
-                                int64_t num_tri, const int64_t* neighbours, int64_t batch,
+                                int64_t num_tri, const int32_t* opposite, int64_t batch,
                                 int32_t height, int32_t width, int32_t channels,
                                 const float* grad_out, float pos_gradient_boost,
                                 const void* pairs, size_t pair_bytes, float* grad_color,
                                 float* grad_pos, void* stream) {
-  if (bad_aa_args(color, rast, pos, pos_batch, num_vert, tri, num_tri, neighbours, batch, height,
+  if (bad_aa_args(color, rast, pos, pos_batch, num_vert, tri, num_tri, opposite, batch, height,
                   width, channels) ||
       grad_out == nullptr || grad_color == nullptr || (num_tri > 0 && grad_pos == nullptr))
     return DR_ERR_INVALID_ARGUMENT;
@@ -588,7 +609,7 @@ extern "C" int dr_antialias_bwd(const float* color, const float* rast, const flo
                                       cudaMemcpyDeviceToDevice, as_stream(stream));
     return static_cast<int>(err);
   }
-  const AaCtx a = make_ctx(color, rast, pos, pos_batch, num_vert, tri, num_tri, neighbours, height,
+  const AaCtx a = make_ctx(color, rast, pos, pos_batch, num_vert, tri, num_tri, opposite, height,
                            width, channels);
   if (batch > 65535) return DR_ERR_TOO_LARGE;
   if (pairs != nullptr) {

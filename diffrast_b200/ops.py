@@ -21,7 +21,7 @@ from diffrast_b200 import _kernels as K
 from diffrast_b200._cache import TensorCache
 from diffrast_b200.backends import require_cuda
 from diffrast_b200.context import RasterizeContext
-from diffrast_b200.topology import TopologyHash, neighbours_for
+from diffrast_b200.topology import TopologyHash, topology_for
 
 FilterMode = Literal["auto", "nearest", "linear", "linear-mipmap-nearest", "linear-mipmap-linear"]
 BoundaryMode = Literal["wrap", "clamp", "zero", "cube"]
@@ -456,15 +456,15 @@ def antialias(
     _check_devices(color=color, rast=rast, pos=pos, tri=tri)
     _check_indices(tri, pos.shape[-2])
     require_cuda(color.device)
-    neighbours = None
+    topology = None
     if topology_hash is not None or tri.shape[0]:
-        neighbours = neighbours_for(tri, topology_hash)
+        topology = topology_for(tri, topology_hash)
     if tri.shape[0] == 0 or color.numel() == 0:
         return color.clone()
     with torch.cuda.device(color.device):
         return F.Antialias.apply(
             color.contiguous(), K.aligned(rast.detach()), K.aligned(pos), tri.contiguous(),
-            neighbours, float(pos_gradient_boost),
+            topology.opposite(tri), float(pos_gradient_boost),
         )
 
 

@@ -35,7 +35,12 @@ class TopologyHash:
     """
 
     def __init__(self, tri: Tensor) -> None:
+        from diffrast_b200 import _kernels as K
+
         self._neighbours = edge_neighbours(tri)
+        with torch.cuda.device(tri.device):
+            # The kernels' form: the vertex across each edge (-1: silhouette by topology).
+            self._opposite = K.edge_opposite(tri.contiguous(), self._neighbours)
         self._shape = tuple(tri.shape)
         self._device = tri.device
         self._source: weakref.ref | None = weakref.ref(tri)
@@ -49,6 +54,16 @@ class TopologyHash:
         return {**self.__dict__, "_source": None, "_stamp": None}
 
     def neighbours(self, tri: Tensor) -> Tensor:
+        self._check(tri)
+        return self._neighbours
+
+    def opposite(self, tri: Tensor) -> Tensor:
+        """For edge ``3 t + k`` the vertex opposite it in the adjacent triangle, -1 without one;
+        int32 ``[triangles, 3]``."""
+        self._check(tri)
+        return self._opposite
+
+    def _check(self, tri: Tensor) -> None:
         if tuple(tri.shape) != self._shape or tri.device != self._device:
             raise ValueError(
                 f"topology_hash was built for a tri of shape {self._shape} on {self._device}, "
@@ -59,20 +74,20 @@ class TopologyHash:
                 "tri was modified in place after topology_hash was built from it; build a new "
                 "one with antialias_construct_topology_hash."
             )
-        return self._neighbours
 
 
-# Each entry is twice the size of its index buffer, so only a few are kept.
-_neighbour_cache: TensorCache[Tensor] = TensorCache(edge_neighbours, max_entries=16)
+# Each entry holds three times the size of its index buffer, so only a few are kept.
+_topology_cache: TensorCache[TopologyHash] = TensorCache(TopologyHash, max_entries=16)
 
 
-def neighbours_for(tri: Tensor, topology_hash: TopologyHash | None) -> Tensor:
-    """Adjacency of ``tri`` from ``topology_hash`` if given, else from the cache."""
+def topology_for(tri: Tensor, topology_hash: TopologyHash | None) -> TopologyHash:
+    """``topology_hash`` if given (checked), else the cached adjacency of ``tri``."""
     if topology_hash is None:
-        return _neighbour_cache.get(tri)
+        return _topology_cache.get(tri)
     if not isinstance(topology_hash, TopologyHash):
         raise TypeError(
             "topology_hash must come from antialias_construct_topology_hash, got "
             f"{type(topology_hash).__name__}."
         )
-    return topology_hash.neighbours(tri)
+    topology_hash._check(tri)
+    return topology_hash

@@ -163,7 +163,8 @@ int dr_mip_downsample_bwd(const float* grad_dst, int64_t images, int32_t h, int3
 
 /* ---------------------------------------------------------------------------------------------
  * Antialias (reference.py:202-265, :675-814; topology.py; _triton_antialias.py).
- * neighbours [num_tri, 3] int64 from dr_edge_neighbours (reference.py:768-787).
+ * neighbours [num_tri, 3] int64 from dr_edge_neighbours (reference.py:768-787); opposite
+ * [num_tri, 3] int32 from dr_edge_opposite_vertices.
  * pos [pos_batch, num_vert, 4] with pos_batch 1 (shared across views) or batch.
  * ------------------------------------------------------------------------------------------- */
 size_t dr_edge_neighbours_workspace_bytes(int64_t num_tri);
@@ -185,10 +186,18 @@ int64_t dr_edge_neighbours_noalloc_max_triangles(void);
 int dr_edge_neighbours_noalloc(const int32_t* tri, int64_t num_tri, int64_t* neighbours,
                                void* stream);
 
+/* opposite [num_tri, 3] int32: for edge 3 t + k the vertex opposite it in the adjacent triangle,
+ * tri[neighbours[3 t + k]], or -1 where neighbours is -1 (no single adjacent triangle: a
+ * silhouette by topology). Built once per index buffer; the antialias entry points take it in
+ * place of neighbours, so that their silhouette test needs one dependent load
+ * (reference.py:790-814 reads tri[neighbours] there). No counterpart in the reference. */
+int dr_edge_opposite_vertices(const int32_t* tri, const int64_t* neighbours, int64_t num_tri,
+                              int32_t* opposite, void* stream);
+
 /* Silhouette flags [pos_batch, num_tri, 3] as bytes (reference.py:790-814). The antialias
  * kernels evaluate the same test on the fly for the edges they cross. */
 int dr_silhouette_edges(const float* pos, int64_t pos_batch, int64_t num_vert,
-                        const int32_t* tri, int64_t num_tri, const int64_t* neighbours,
+                        const int32_t* tri, int64_t num_tri, const int32_t* opposite,
                         uint8_t* silhouette, void* stream);
 
 /* Bytes of the pair records that dr_antialias_fwd can leave for dr_antialias_bwd (about 9 bytes
@@ -199,16 +208,16 @@ size_t dr_antialias_pair_bytes(int64_t batch, int32_t height, int32_t width);
  * dr_antialias_pair_bytes() bytes (pair_bytes at least that) are written. */
 int dr_antialias_fwd(const float* color, const float* rast, const float* pos, int64_t pos_batch,
                      int64_t num_vert, const int32_t* tri, int64_t num_tri,
-                     const int64_t* neighbours, int64_t batch, int32_t height, int32_t width,
+                     const int32_t* opposite, int64_t batch, int32_t height, int32_t width,
                      int32_t channels, float* out, void* pairs, size_t pair_bytes, void* stream);
 
 /* Backward pass (_triton_antialias.py:306-320). grad_color is written; grad_pos
  * [pos_batch, num_vert, 4] is ACCUMULATED (clear it first). With pairs from a dr_antialias_fwd
- * call on the same color, rast, pos, tri and neighbours, the edge tests are not repeated; with
+ * call on the same color, rast, pos, tri and opposite, the edge tests are not repeated; with
  * pairs NULL they are. Both give the same result. */
 int dr_antialias_bwd(const float* color, const float* rast, const float* pos, int64_t pos_batch,
                      int64_t num_vert, const int32_t* tri, int64_t num_tri,
-                     const int64_t* neighbours, int64_t batch, int32_t height, int32_t width,
+                     const int32_t* opposite, int64_t batch, int32_t height, int32_t width,
                      int32_t channels, const float* grad_out, float pos_gradient_boost,
                      const void* pairs, size_t pair_bytes, float* grad_color, float* grad_pos,
                      void* stream);

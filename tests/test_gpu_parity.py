@@ -372,12 +372,12 @@ def test_antialias_recorded_pairs_match_recomputed_pairs():
         color = torch.rand(2, 40, 56, 3, generator=gen).cuda()
         grad_out = torch.randn(2, 40, 56, 3, generator=gen).cuda()
         pos, tri, rast = pos.cuda(), tri.cuda(), rast.cuda()
-        nb = dr.antialias_construct_topology_hash(tri).neighbours(tri)
-        out, pairs = K.antialias_fwd(color, rast, pos, tri, nb, record_pairs=True)
-        out_plain, none = K.antialias_fwd(color, rast, pos, tri, nb)
+        opp = dr.antialias_construct_topology_hash(tri).opposite(tri)
+        out, pairs = K.antialias_fwd(color, rast, pos, tri, opp, record_pairs=True)
+        out_plain, none = K.antialias_fwd(color, rast, pos, tri, opp)
         assert none is None and torch.equal(out, out_plain)
-        gc_rec, gp_rec = K.antialias_bwd(color, rast, pos, tri, nb, grad_out, 1.0, pairs)
-        gc, gp = K.antialias_bwd(color, rast, pos, tri, nb, grad_out, 1.0)
+        gc_rec, gp_rec = K.antialias_bwd(color, rast, pos, tri, opp, grad_out, 1.0, pairs)
+        gc, gp = K.antialias_bwd(color, rast, pos, tri, opp, grad_out, 1.0)
         torch.testing.assert_close(gc_rec, gc, rtol=1e-6, atol=1e-7)
         # Position gradients are sums of atomically added terms: only their order may differ
         # (the atomic-gradient tolerance of this file).
@@ -399,8 +399,12 @@ def test_edge_neighbours_match_golden():
     g = load_golden("topology")
     for key, nkey in (("tri", "neighbours"), ("tri_fan", "neighbours_fan")):
         tri = g[key].cuda()
-        nb = dr.antialias_construct_topology_hash(tri).neighbours(tri)
+        topo = dr.antialias_construct_topology_hash(tri)
+        nb = topo.neighbours(tri)
         assert torch.equal(nb.cpu(), g[nkey])
+        # The kernels' form: tri[neighbours] (the vertex across each edge), -1 where unshared.
+        expected = torch.where(g[nkey] >= 0, g[key].reshape(-1)[g[nkey].clamp_min(0)], -1)
+        assert torch.equal(topo.opposite(tri).cpu(), expected.int())
 
 
 # ---------------------------------------------------------------------------------------------
