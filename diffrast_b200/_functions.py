@@ -206,7 +206,7 @@ class Antialias(torch.autograd.Function):
     def forward(ctx, color: Tensor, rast: Tensor, pos: Tensor, tri: Tensor, opposite: Tensor,
                 boost: float):
         pos3 = pos if pos.ndim == 3 else pos[None]
-        # The pair records (about 9 bytes per pixel) spare the backward pass the edge tests.
+        # The pair records (about 25 bytes per pixel) spare the backward pass the edge tests.
         out, pairs = K.antialias_fwd(color, rast, pos3, tri, opposite,
                                      record_pairs=any(ctx.needs_input_grad[:3]))
         saved = (color, rast, pos3, tri, opposite, pairs)

@@ -205,11 +205,19 @@ __device__ __forceinline__ Pair eval_pair(const AaCtx& a, long long b, int row, 
 // The pairs of every pixel as the forward pass found them, so that the backward pass reads them
 // instead of repeating the edge tests: for the right (low nibble) and lower (high nibble) pair
 // of pixel p, bit 3 = active, bit 2 = the crossing was found from p's side, bits 0-1 = the edge
-// of the owning triangle; t[p] holds the two crossings t (zero when inactive).
+// of the owning triangle; t[p] holds the two crossings t (zero when inactive) and verts[p] the
+// vertex indices of the two crossed edges (right pair in x, y; lower pair in z, w; written only
+// for pixels with an active pair).
 struct PairRecords {
   float2* t;
   uint8_t* code;
+  int4* verts;
 };
+
+// Vertex (edge + k) % 3 of the pair's owning triangle: k = 1, 2 give the crossed edge's ends.
+__device__ __forceinline__ int edge_vertex(const AaCtx& a, const Pair& r, int k) {
+  return __ldg(a.tri + 3 * static_cast<long long>(r.owner) + (r.edge + k) % 3);
+}
 
 __device__ __forceinline__ unsigned pair_code(const Pair& r) {
   return 8u | (r.use_p ? 4u : 0u) | static_cast<unsigned>(r.edge);
@@ -229,7 +237,7 @@ __device__ __forceinline__ float2 recorded_blend(unsigned code, float t) {
 constexpr int kAaThreadsX = 32, kAaThreadsY = 8;
 constexpr int kAaTileX = kAaThreadsX - 1, kAaTileY = kAaThreadsY - 1;
 
-__global__ void __launch_bounds__(256, 6) aa_fwd_kernel(const AaCtx a, float* __restrict__ out,
+__global__ void __launch_bounds__(256, 5) aa_fwd_kernel(const AaCtx a, float* __restrict__ out,
                                                         PairRecords rec) {
   __shared__ float2 hk[kAaThreadsY][kAaThreadsX], vk[kAaThreadsY][kAaThreadsX];
   const int tx = threadIdx.x % kAaThreadsX, ty = threadIdx.x / kAaThreadsX;
@@ -237,6 +245,7 @@ __global__ void __launch_bounds__(256, 6) aa_fwd_kernel(const AaCtx a, float* __
   const long long b = blockIdx.z;
   const bool in_image = col >= 0 && col < a.width && row >= 0 && row < a.height;
   float2 h = make_float2(0.f, 0.f), v = make_float2(0.f, 0.f), t = make_float2(0.f, 0.f);
+  int4 verts = make_int4(0, 0, 0, 0);
   unsigned codes = 0u;
   if (in_image && ty >= 1 && col + 1 < a.width) {
     const Pair r = eval_pair(a, b, row, col, true);
@@ -244,6 +253,8 @@ __global__ void __launch_bounds__(256, 6) aa_fwd_kernel(const AaCtx a, float* __
     if (r.active) {
       t.x = r.t;
       codes = pair_code(r);
+      verts.x = edge_vertex(a, r, 1);
+      verts.y = edge_vertex(a, r, 2);
     }
   }
   if (in_image && tx >= 1 && row + 1 < a.height) {
@@ -252,6 +263,8 @@ __global__ void __launch_bounds__(256, 6) aa_fwd_kernel(const AaCtx a, float* __
     if (r.active) {
       t.y = r.t;
       codes |= pair_code(r) << 4;
+      verts.z = edge_vertex(a, r, 1);
+      verts.w = edge_vertex(a, r, 2);
     }
   }
   hk[ty][tx] = h;
@@ -263,6 +276,8 @@ __global__ void __launch_bounds__(256, 6) aa_fwd_kernel(const AaCtx a, float* __
     // Interior threads evaluated both pairs of their pixel.
     rec.t[p] = t;
     rec.code[p] = static_cast<uint8_t>(codes);
+    // Edge vertices are read only for active pairs.
+    if (codes & 0x88u) rec.verts[p] = verts;
   }
   // Blend coefficients and partners, in the reference's accumulation order: right pair (this
   // pixel first), left pair (second), lower pair (first), upper pair (second).
@@ -281,14 +296,15 @@ __global__ void __launch_bounds__(256, 6) aa_fwd_kernel(const AaCtx a, float* __
 
 // Position gradient of the crossing t of a pair, chained into the two vertices of its edge:
 // t = e_s / (e_s - e_d), e = a_i c_j - a_j c_i with a = x - px w, c = y - py w.
-__device__ __forceinline__ void add_edge_gradient(const AaCtx& a, float* grad_pos, long long pb,
-                                                  const Pair& r, float grad_t) {
-  const int i = (r.edge + 1) % 3, j = (r.edge + 2) % 3;
-  const Tri2 v = load_tri(a, pb, r.owner);
-  const float ai_s = v.x[i] - r.sx * v.w[i], aj_s = v.x[j] - r.sx * v.w[j];
-  const float ci_s = v.y[i] - r.sy * v.w[i], cj_s = v.y[j] - r.sy * v.w[j];
-  const float ai_d = v.x[i] - r.dx * v.w[i], aj_d = v.x[j] - r.dx * v.w[j];
-  const float ci_d = v.y[i] - r.dy * v.w[i], cj_d = v.y[j] - r.dy * v.w[j];
+__device__ __forceinline__ void edge_gradient(const AaCtx& a, float* grad_pos, long long pb, int vi,
+                                              int vj, const Pair& r, float grad_t) {
+  const long long base = pb * a.num_vert;
+  const float4 pi = __ldg(reinterpret_cast<const float4*>(a.pos) + base + vi);
+  const float4 pj = __ldg(reinterpret_cast<const float4*>(a.pos) + base + vj);
+  const float ai_s = pi.x - r.sx * pi.w, aj_s = pj.x - r.sx * pj.w;
+  const float ci_s = pi.y - r.sy * pi.w, cj_s = pj.y - r.sy * pj.w;
+  const float ai_d = pi.x - r.dx * pi.w, aj_d = pj.x - r.dx * pj.w;
+  const float ci_d = pi.y - r.dy * pi.w, cj_d = pj.y - r.dy * pj.w;
   const float e_s = ai_s * cj_s - aj_s * ci_s;
   const float e_d = ai_d * cj_d - aj_d * ci_d;
   float denom = e_s - e_d;
@@ -301,9 +317,13 @@ __device__ __forceinline__ void add_edge_gradient(const AaCtx& a, float* grad_po
   const float gy_j = g_s * ai_s + g_d * ai_d;
   const float gw_i = g_s * (r.sy * aj_s - r.sx * cj_s) + g_d * (r.dy * aj_d - r.dx * cj_d);
   const float gw_j = g_s * (r.sx * ci_s - r.sy * ai_s) + g_d * (r.dx * ci_d - r.dy * ai_d);
-  const long long base = pb * a.num_vert;
-  red_add_v4(grad_pos + (base + v.idx[i]) * 4, gx_i, gy_i, 0.0f, gw_i);
-  red_add_v4(grad_pos + (base + v.idx[j]) * 4, gx_j, gy_j, 0.0f, gw_j);
+  red_add_v4(grad_pos + (base + vi) * 4, gx_i, gy_i, 0.0f, gw_i);
+  red_add_v4(grad_pos + (base + vj) * 4, gx_j, gy_j, 0.0f, gw_j);
+}
+
+__device__ __forceinline__ void add_edge_gradient(const AaCtx& a, float* grad_pos, long long pb,
+                                                  const Pair& r, float grad_t) {
+  edge_gradient(a, grad_pos, pb, edge_vertex(a, r, 1), edge_vertex(a, r, 2), r, grad_t);
 }
 
 __global__ void __launch_bounds__(256, 5) aa_bwd_kernel(const AaCtx a,
@@ -361,73 +381,106 @@ __global__ void __launch_bounds__(256, 5) aa_bwd_kernel(const AaCtx a,
   }
 }
 
-// Backward pass from the pairs recorded by the forward pass: one thread per pixel, no edge
-// tests. Same arithmetic as aa_bwd_kernel for the colour gradient and for the crossings of the
-// pixel's own (right and lower) pairs, whose position gradients it scatters.
+// Position gradient of pixel (row, col)'s own right (horizontal) or lower pair, recorded with
+// code c4 and crossing gradient g.
+__device__ __forceinline__ void recorded_edge_gradient(const AaCtx& a, float* grad_pos,
+                                                       long long pb, int row, int col, unsigned c4,
+                                                       int vi, int vj, bool horizontal, float g) {
+  const int row_q = horizontal ? row : row + 1, col_q = horizontal ? col + 1 : col;
+  Pair r;
+  r.use_p = (c4 & 4u) != 0u;
+  const float xp = pixel_centre(col, a.width), yp = pixel_centre(row, a.height);
+  const float xq = horizontal ? pixel_centre(col_q, a.width) : xp;
+  const float yq = horizontal ? yp : pixel_centre(row_q, a.height);
+  r.sx = r.use_p ? xp : xq;
+  r.sy = r.use_p ? yp : yq;
+  r.dx = r.use_p ? xq : xp;
+  r.dy = r.use_p ? yq : yp;
+  // When the edge belongs to Q's triangle, t = 1 - t_q.
+  edge_gradient(a, grad_pos, pb, vi, vj, r, r.use_p ? g : -g);
+}
+
+// Backward pass from the pairs recorded by the forward pass: one thread per pixel (grid: columns
+// in x, rows in y, views in z), no edge tests. Same arithmetic as aa_bwd_kernel for the colour
+// gradient and for the crossings of the pixel's own (right and lower) pairs, whose position
+// gradients it scatters. With K > 0 channels known at compile time, every input the pixel can
+// need is loaded up front, unconditionally, so that the loads overlap instead of each waiting for
+// the record that decides it; K = 0 handles any channel count.
+template <int K>
 __global__ void __launch_bounds__(256) aa_bwd_recorded_kernel(const AaCtx a,
                                                               const float2* __restrict__ rec_t,
                                                               const uint8_t* __restrict__ rec_code,
-                                                              long long total,
+                                                              const int4* __restrict__ rec_verts,
                                                               const float* __restrict__ grad_out,
                                                               float boost,
                                                               float* __restrict__ grad_color,
                                                               float* __restrict__ grad_pos) {
-  const long long p = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
-  if (p >= total) return;
-  const long long hw = static_cast<long long>(a.height) * a.width;
-  const long long b = p / hw;
-  const int rem = static_cast<int>(p - b * hw);
-  const int row = rem / a.width, col = rem - row * a.width;
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= a.width) return;
+  const int row = blockIdx.y;
+  const long long b = blockIdx.z;
+  const long long p = (b * a.height + row) * a.width + col;
+  const long long w = a.width;
+  const bool has_l = col > 0, has_r = col + 1 < a.width, has_u = row > 0, has_d = row + 1 < a.height;
   const unsigned code = __ldg(rec_code + p);
-  const unsigned code_l = col > 0 ? __ldg(rec_code + p - 1) & 15u : 0u;
-  const unsigned code_u = row > 0 ? __ldg(rec_code + p - a.width) >> 4 : 0u;
-  const float2 t = (code & 0x88u) ? __ldg(rec_t + p) : make_float2(0.f, 0.f);
-  const float t_l = (code_l & 8u) ? __ldg(rec_t + p - 1).x : 0.f;
-  const float t_u = (code_u & 8u) ? __ldg(rec_t + p - a.width).y : 0.f;
+  const unsigned code_l = has_l ? __ldg(rec_code + p - 1) & 15u : 0u;
+  const unsigned code_u = has_u ? __ldg(rec_code + p - w) >> 4 : 0u;
+  const float2 t = __ldg(rec_t + p);
+  const float t_l = has_l ? __ldg(rec_t + p - 1).x : 0.f;
+  const float t_u = has_u ? __ldg(rec_t + p - w).y : 0.f;
+  const int4 verts = __ldg(rec_verts + p);
+  const int C = K > 0 ? K : a.channels;
+  constexpr int R = K > 0 ? K : 1;
+  float gs[R], gl[R], gr[R], gu[R], gd[R], cs[R], cr[R], cd[R];
+  if (K > 0) {
+#pragma unroll
+    for (int c = 0; c < R; ++c) {
+      gs[c] = grad_out[p * C + c];
+      gl[c] = has_l ? grad_out[(p - 1) * C + c] : 0.f;
+      gr[c] = has_r ? grad_out[(p + 1) * C + c] : 0.f;
+      gu[c] = has_u ? grad_out[(p - w) * C + c] : 0.f;
+      gd[c] = has_d ? grad_out[(p + w) * C + c] : 0.f;
+      cs[c] = __ldg(a.color + p * C + c);
+      cr[c] = has_r ? __ldg(a.color + (p + 1) * C + c) : 0.f;
+      cd[c] = has_d ? __ldg(a.color + (p + w) * C + c) : 0.f;
+    }
+  }
   const float2 right = recorded_blend(code & 15u, t.x), down = recorded_blend(code >> 4, t.y);
   const float2 left = recorded_blend(code_l, t_l), up = recorded_blend(code_u, t_u);
-  const float kp[4] = {-right.x, -left.y, -down.x, -up.y};
-  const float kq[4] = {right.y, left.x, down.y, up.x};
-  const long long other[4] = {p + 1, p - 1, p + a.width, p - a.width};
-  const bool own[2] = {(code & 8u) != 0u, (code & 0x80u) != 0u};
-  const float own_t[2] = {t.x, t.y};
-  const int C = a.channels;
-  float grad_t[2] = {0.f, 0.f};
+  const bool own_r = (code & 8u) != 0u, own_d = (code & 0x80u) != 0u;
+  float grad_tr = 0.f, grad_td = 0.f;
+#pragma unroll
   for (int c = 0; c < C; ++c) {
-    const float g_self = grad_out[p * C + c];
+    const int i = K > 0 ? c : 0;
+    if (K == 0) {
+      gs[0] = grad_out[p * C + c];
+      gl[0] = has_l ? grad_out[(p - 1) * C + c] : 0.f;
+      gr[0] = has_r ? grad_out[(p + 1) * C + c] : 0.f;
+      gu[0] = has_u ? grad_out[(p - w) * C + c] : 0.f;
+      gd[0] = has_d ? grad_out[(p + w) * C + c] : 0.f;
+      cs[0] = __ldg(a.color + p * C + c);
+      cr[0] = has_r ? __ldg(a.color + (p + 1) * C + c) : 0.f;
+      cd[0] = has_d ? __ldg(a.color + (p + w) * C + c) : 0.f;
+    }
+    const float g_self = gs[i];
     float value = g_self;
-    for (int i = 0; i < 4; ++i) {
-      if (kp[i] != 0.0f || kq[i] != 0.0f) value += kp[i] * g_self + kq[i] * grad_out[other[i] * C + c];
-    }
+    // Right pair (first pixel), left (second), lower (first), upper (second), as aa_bwd_kernel.
+    if (right.x != 0.0f || right.y != 0.0f) value += -right.x * g_self + right.y * gr[i];
+    if (left.x != 0.0f || left.y != 0.0f) value += -left.y * g_self + left.x * gl[i];
+    if (down.x != 0.0f || down.y != 0.0f) value += -down.x * g_self + down.y * gd[i];
+    if (up.x != 0.0f || up.y != 0.0f) value += -up.y * g_self + up.x * gu[i];
     grad_color[p * C + c] = value;
-    for (int d = 0; d < 2; ++d) {
-      if (!own[d]) continue;
-      const long long q = other[d == 0 ? 0 : 2];
-      const float c_p = __ldg(a.color + p * C + c), c_q = __ldg(a.color + q * C + c);
-      grad_t[d] += own_t[d] < 0.5f ? -g_self * (c_q - c_p) : grad_out[q * C + c] * (c_p - c_q);
-    }
+    // d/dt of (1/2 - t)(c_q - c_p) below the midpoint and (t - 1/2)(c_p - c_q) above it.
+    if (own_r) grad_tr += t.x < 0.5f ? -g_self * (cr[i] - cs[i]) : gr[i] * (cs[i] - cr[i]);
+    if (own_d) grad_td += t.y < 0.5f ? -g_self * (cd[i] - cs[i]) : gd[i] * (cs[i] - cd[i]);
   }
   const long long pb = a.pos_batch == 1 ? 0 : b;
-  for (int d = 0; d < 2; ++d) {
-    if (!own[d]) continue;
-    const float g = grad_t[d] * boost;
-    if (g == 0.0f) continue;
-    const unsigned c4 = d == 0 ? code & 15u : code >> 4;
-    const bool horizontal = d == 0;
-    const int row_q = horizontal ? row : row + 1, col_q = horizontal ? col + 1 : col;
-    const long long q = other[d == 0 ? 0 : 2];
-    Pair r;
-    r.use_p = (c4 & 4u) != 0u;
-    r.edge = static_cast<int>(c4 & 3u);
-    r.owner = aa_triangle(a.rast[r.use_p ? p : q].w, a.num_tri);
-    const float xp = pixel_centre(col, a.width), yp = pixel_centre(row, a.height);
-    const float xq = pixel_centre(col_q, a.width), yq = pixel_centre(row_q, a.height);
-    r.sx = r.use_p ? xp : xq;
-    r.sy = r.use_p ? yp : yq;
-    r.dx = r.use_p ? xq : xp;
-    r.dy = r.use_p ? yq : yp;
-    add_edge_gradient(a, grad_pos, pb, r, r.use_p ? g : -g);
-  }
+  if (own_r && grad_tr * boost != 0.0f)
+    recorded_edge_gradient(a, grad_pos, pb, row, col, code & 15u, verts.x, verts.y, true,
+                           grad_tr * boost);
+  if (own_d && grad_td * boost != 0.0f)
+    recorded_edge_gradient(a, grad_pos, pb, row, col, code >> 4, verts.z, verts.w, false,
+                           grad_td * boost);
 }
 
 __global__ void __launch_bounds__(256) silhouette_kernel(const AaCtx a, long long total,
@@ -487,14 +540,16 @@ AaCtx make_ctx(const float* color, const float* rast, const float* pos, int64_t 
 }
 
 size_t pair_record_bytes(long long pixels) {
-  return align256(sizeof(float2) * static_cast<size_t>(pixels)) + align256(static_cast<size_t>(pixels));
+  const size_t n = static_cast<size_t>(pixels);
+  return align256(sizeof(float2) * n) + align256(n) + align256(sizeof(int4) * n);
 }
 
 PairRecords pair_records(void* pairs, long long pixels) {
-  if (pairs == nullptr) return {nullptr, nullptr};
+  if (pairs == nullptr) return {nullptr, nullptr, nullptr};
+  const size_t n = static_cast<size_t>(pixels);
   char* p = static_cast<char*>(pairs);
-  return {reinterpret_cast<float2*>(p),
-          reinterpret_cast<uint8_t*>(p + align256(sizeof(float2) * static_cast<size_t>(pixels)))};
+  return {reinterpret_cast<float2*>(p), reinterpret_cast<uint8_t*>(p + align256(sizeof(float2) * n)),
+          reinterpret_cast<int4*>(p + align256(sizeof(float2) * n) + align256(n))};
 }
 
 }  // namespace
@@ -614,8 +669,26 @@ extern "C" int dr_antialias_bwd(const float* color, const float* rast, const flo
   if (batch > 65535) return DR_ERR_TOO_LARGE;
   if (pairs != nullptr) {
     const PairRecords rec = pair_records(const_cast<void*>(pairs), total);
-    aa_bwd_recorded_kernel<<<blocks_for(total, 256), 256, 0, as_stream(stream)>>>(
-        a, rec.t, rec.code, total, grad_out, pos_gradient_boost, grad_color, grad_pos);
+    if (height > 65535) return DR_ERR_TOO_LARGE;
+    const dim3 grid((width + 255) / 256, height, batch);
+    const cudaStream_t s = as_stream(stream);
+    switch (channels) {
+      case 1:
+        aa_bwd_recorded_kernel<1><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, grad_out,
+                                                       pos_gradient_boost, grad_color, grad_pos);
+        break;
+      case 3:
+        aa_bwd_recorded_kernel<3><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, grad_out,
+                                                       pos_gradient_boost, grad_color, grad_pos);
+        break;
+      case 4:
+        aa_bwd_recorded_kernel<4><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, grad_out,
+                                                       pos_gradient_boost, grad_color, grad_pos);
+        break;
+      default:
+        aa_bwd_recorded_kernel<0><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, grad_out,
+                                                       pos_gradient_boost, grad_color, grad_pos);
+    }
     return launch_status();
   }
   const dim3 grid((width + kAaTileX - 1) / kAaTileX, (height + kAaTileY - 1) / kAaTileY, batch);

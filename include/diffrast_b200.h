@@ -200,8 +200,9 @@ int dr_silhouette_edges(const float* pos, int64_t pos_batch, int64_t num_vert,
                         const int32_t* tri, int64_t num_tri, const int32_t* opposite,
                         uint8_t* silhouette, void* stream);
 
-/* Bytes of the pair records that dr_antialias_fwd can leave for dr_antialias_bwd (about 9 bytes
- * per pixel): per pixel, the crossing t and the outcome of its right and lower pixel pairs. */
+/* Bytes of the pair records that dr_antialias_fwd can leave for dr_antialias_bwd (about 25 bytes
+ * per pixel): per pixel, the crossing t, the outcome and the crossed edge of its right and lower
+ * pixel pairs. */
 size_t dr_antialias_pair_bytes(int64_t batch, int32_t height, int32_t width);
 
 /* Forward pass (_triton_antialias.py:272-304). pairs may be NULL; otherwise the records of
