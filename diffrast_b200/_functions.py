@@ -36,6 +36,20 @@ def _saveable(t: Tensor | None) -> Tensor | None:
     return t.clone() if t is not None and t.is_inference() else t
 
 
+def _take(src: Tensor | None, spec: tuple[int, int] | None) -> Tensor | None:
+    """``src`` itself, or its channels ``spec = (first, count)`` when the lookup input was passed
+    as the wider tensor it is a slice of."""
+    return src if src is None or spec is None else src[..., spec[0]:spec[0] + spec[1]]
+
+
+def _slice_gradient(src: Tensor, spec: tuple[int, int] | None, want: bool):
+    """(gradient of ``src``, its first lookup channel) for an input passed with a channel ``spec``:
+    the kernel writes whole pixel records, zero outside the slice. (None, -1) otherwise."""
+    if not want or spec is None:
+        return None, -1
+    return torch.empty(src.shape, dtype=src.dtype, device=src.device), spec[0]
+
+
 class Rasterize(torch.autograd.Function):
     """Visibility, then rast / rast_db; gradients reach pos through the barycentric resolve."""
 
@@ -131,31 +145,45 @@ class MipChain(torch.autograd.Function):
 
 class Texture(torch.autograd.Function):
     """Lookup in a list of levels (base texture first); gradients to every level and to uv,
-    uv_da and the level-of-detail bias as the filter mode allows."""
+    uv_da and the level-of-detail bias as the filter mode allows.
+
+    uv and uv_da may be passed as the wider tensors they are channel slices of (``uv_spec`` /
+    ``da_spec`` = (first channel, count)), such as interpolate's outputs: their gradients are then
+    written straight into gradients of the wider tensors instead of being copied there by the
+    slices' own backward."""
 
     @staticmethod
-    def forward(ctx, uv, uv_da, bias, mode: int, boundary: int, *levels):
+    def forward(ctx, uv_src, da_src, bias, mode: int, boundary: int, uv_spec, da_spec, *levels):
         levels = [lv.contiguous() for lv in levels]
-        out = K.texture_fwd(list(levels), uv, uv_da, bias, mode, boundary)
-        ctx.save_for_backward(*(_saveable(t) for t in (uv, uv_da, bias, *levels)))
-        ctx.settings = (mode, boundary, uv_da is not None, bias is not None, len(levels))
+        out = K.texture_fwd(list(levels), _take(uv_src, uv_spec), _take(da_src, da_spec), bias,
+                            mode, boundary)
+        ctx.save_for_backward(*(_saveable(t) for t in (uv_src, da_src, bias, *levels)))
+        ctx.settings = (mode, boundary, da_src is not None, bias is not None, len(levels))
+        ctx.specs = (uv_spec, da_spec)
         return out
 
     @staticmethod
     @first_order("texture")
     def backward(ctx, grad_out):
         mode, boundary, has_da, has_bias, count = ctx.settings
+        uv_spec, da_spec = ctx.specs
         saved = ctx.saved_tensors
-        uv, uv_da, bias, levels = saved[0], saved[1], saved[2], list(saved[3:])
+        uv_src, da_src, bias, levels = saved[0], saved[1], saved[2], list(saved[3:])
         need = ctx.needs_input_grad
         want_uv = need[0] and mode > 0
         want_da = need[1] and has_da and mode == 3
         want_bias = need[2] and has_bias and mode == 3
-        grads, g_uv, g_da, g_bias = K.texture_bwd(levels, uv, uv_da, bias, mode, boundary,
+        g_uv_src, uv_first = _slice_gradient(uv_src, uv_spec, want_uv)
+        g_da_src, da_first = _slice_gradient(da_src, da_spec, want_da)
+        grads, g_uv, g_da, g_bias = K.texture_bwd(levels, _take(uv_src, uv_spec),
+                                                  _take(da_src, da_spec), bias, mode, boundary,
                                                   grad_out.contiguous(), want_uv, want_da,
-                                                  want_bias)
-        level_grads = [g if need[5 + i] else None for i, g in enumerate(grads)]
-        return (g_uv, g_da, g_bias, None, None, *level_grads)
+                                                  want_bias, grad_uv=g_uv_src, grad_da=g_da_src,
+                                                  uv_first=uv_first, da_first=da_first)
+        g_uv = g_uv_src if uv_spec is not None else g_uv
+        g_da = g_da_src if da_spec is not None else g_da
+        level_grads = [g if need[7 + i] else None for i, g in enumerate(grads)]
+        return (g_uv, g_da, g_bias, None, None, None, None, *level_grads)
 
 
 class TextureChain(torch.autograd.Function):
@@ -167,30 +195,41 @@ class TextureChain(torch.autograd.Function):
     """
 
     @staticmethod
-    def forward(ctx, uv, uv_da, bias, mode: int, boundary: int, count: int, tex: Tensor):
+    def forward(ctx, uv_src, da_src, bias, mode: int, boundary: int, count: int, tex: Tensor,
+                uv_spec=None, da_spec=None):
         tex = tex.contiguous()
         levels = [tex]
         for _ in range(count):
             levels.append(K.mip_down(levels[-1]))
-        out = K.texture_fwd(levels, uv, uv_da, bias, mode, boundary)
-        ctx.save_for_backward(*(_saveable(t) for t in (uv, uv_da, bias, tex)))
+        out = K.texture_fwd(levels, _take(uv_src, uv_spec), _take(da_src, da_spec), bias, mode,
+                            boundary)
+        ctx.save_for_backward(*(_saveable(t) for t in (uv_src, da_src, bias, tex)))
         ctx.levels = levels[1:]
         ctx.settings = (mode, boundary)
+        ctx.specs = (uv_spec, da_spec)
         return out
 
     @staticmethod
     @first_order("texture")
     def backward(ctx, grad_out):
         mode, boundary = ctx.settings
-        uv, uv_da, bias, tex = ctx.saved_tensors
+        uv_spec, da_spec = ctx.specs
+        uv_src, da_src, bias, tex = ctx.saved_tensors
         levels = [tex, *ctx.levels]
         need = ctx.needs_input_grad
         want_uv = need[0] and mode > 0
-        want_da = need[1] and uv_da is not None and mode == 3
+        want_da = need[1] and da_src is not None and mode == 3
         want_bias = need[2] and bias is not None and mode == 3
-        grads, g_uv, g_da, g_bias = K.texture_bwd(levels, uv, uv_da, bias, mode, boundary,
+        g_uv_src, uv_first = _slice_gradient(uv_src, uv_spec, want_uv)
+        g_da_src, da_first = _slice_gradient(da_src, da_spec, want_da)
+        grads, g_uv, g_da, g_bias = K.texture_bwd(levels, _take(uv_src, uv_spec),
+                                                  _take(da_src, da_spec), bias, mode, boundary,
                                                   grad_out.contiguous(), want_uv, want_da,
-                                                  want_bias, keep_padded=True)
+                                                  want_bias, keep_padded=True, grad_uv=g_uv_src,
+                                                  grad_da=g_da_src, uv_first=uv_first,
+                                                  da_first=da_first)
+        g_uv = g_uv_src if uv_spec is not None else g_uv
+        g_da = g_da_src if da_spec is not None else g_da
         grad_tex = None
         if need[6]:
             for level in range(len(grads) - 2, -1, -1):
@@ -198,7 +237,7 @@ class TextureChain(torch.autograd.Function):
             grad_tex = grads[0]
             if grad_tex.shape[-1] != tex.shape[-1]:
                 grad_tex = grad_tex[..., : tex.shape[-1]].contiguous()
-        return g_uv, g_da, g_bias, None, None, None, grad_tex
+        return g_uv, g_da, g_bias, None, None, None, grad_tex, None, None
 
 
 class Antialias(torch.autograd.Function):

@@ -203,6 +203,16 @@ def pixel_rows(t: Tensor | None) -> tuple[Tensor | None, int]:
     return t, sw
 
 
+def _pixel_stride(t: Tensor) -> int:
+    """Pixel stride of an output view ``[batch, h, w, k]`` whose pixels are equally spaced rows
+    of contiguous channels (checked)."""
+    b, h, w, k = t.shape
+    sb, sh, sw, sk = t.stride()
+    if not (sk == 1 and (h == 1 or sh == w * sw) and (b == 1 or sb == h * sh) and sw >= k):
+        raise ValueError("gradient output views must have equally spaced pixels")
+    return sw
+
+
 def _level_tables(levels: list[Tensor], cube: bool):
     heights = [lv.shape[-3] for lv in levels]
     widths = [lv.shape[-2] for lv in levels]
@@ -231,7 +241,11 @@ def texture_fwd(levels: list[Tensor], uv: Tensor, uv_da: Tensor | None, bias: Te
 
 @timed("texture_bwd")
 def texture_bwd(levels, uv, uv_da, bias, mode, boundary, grad_out, want_uv, want_da, want_bias,
-                keep_padded=False):
+                keep_padded=False, grad_uv=None, grad_da=None, uv_first=-1, da_first=-1):
+    """Level gradients and, as wanted, those of uv, uv_da and the bias. ``grad_uv`` / ``grad_da``
+    may be given as outputs: with ``uv_first`` / ``da_first`` = -1 a ``[batch, h, w, k]`` view
+    that receives the gradient; with c >= 0 a tensor of wider pixel records (``[batch, h, w, K]``)
+    whose channels c.. receive it and whose other channels are set to zero."""
     batch, height, width = uv.shape[:3]
     channels = levels[0].shape[-1]
     # Three-channel gradients are accumulated in four-channel buffers, so that each texel takes
@@ -239,8 +253,16 @@ def texture_bwd(levels, uv, uv_da, bias, mode, boundary, grad_out, want_uv, want
     stride = 4 if channels == 3 else channels
     grads = [torch.zeros((*lv.shape[:-1], stride), dtype=torch.float32, device=lv.device)
              for lv in levels]
-    grad_uv = torch.empty(uv.shape, dtype=torch.float32, device=uv.device) if want_uv else None
-    grad_da = torch.empty(uv_da.shape, dtype=torch.float32, device=uv.device) if want_da else None
+    if want_uv and grad_uv is None:
+        grad_uv = torch.empty(uv.shape, dtype=torch.float32, device=uv.device)
+    if want_da and grad_da is None:
+        grad_da = torch.empty(uv_da.shape, dtype=torch.float32, device=uv.device)
+    grad_uv = grad_uv if want_uv else None
+    grad_da = grad_da if want_da else None
+    guv_stride = 0 if grad_uv is None else _pixel_stride(grad_uv)
+    gda_stride = 0 if grad_da is None else _pixel_stride(grad_da)
+    uv_first = uv_first if grad_uv is not None else -1
+    da_first = da_first if grad_da is not None else -1
     uv, uv_stride = pixel_rows(uv)
     uv_da, da_stride = pixel_rows(uv_da)
     grad_bias = torch.empty_like(bias) if want_bias else None
@@ -251,8 +273,8 @@ def texture_bwd(levels, uv, uv_da, bias, mode, boundary, grad_out, want_uv, want
                                len(levels), channels, stride, uv.data_ptr(), uv_stride,
                                N.ptr(uv_da), da_stride, N.ptr(bias),
                                batch, height, width, mode, boundary, grad_out.data_ptr(),
-                               N.ptr(grad_uv), N.ptr(grad_da), N.ptr(grad_bias),
-                               N.stream(uv.device)),
+                               N.ptr(grad_uv), guv_stride, uv_first, N.ptr(grad_da),
+                               gda_stride, da_first, N.ptr(grad_bias), N.stream(uv.device)),
         "dr_texture_bwd",
     )  # fmt: skip
     if stride != channels and not keep_padded:

@@ -60,7 +60,8 @@ _SIGNATURES = {
     "dr_texture_bwd": (
         c_int,
         [_P, _P, _P, _P, _P, c_int32, c_int32, c_int32, _P, c_int64, _P, c_int64, _P, c_int64,
-         c_int32, c_int32, c_int32, c_int32, _P, _P, _P, _P, _P],
+         c_int32, c_int32, c_int32, c_int32, _P, _P, c_int64, c_int32, _P, c_int64, c_int32, _P,
+         _P],
     ),
     "dr_mip_downsample": (c_int, [_P, c_int64, c_int32, c_int32, c_int32, _P, _P]),
     "dr_mip_downsample_bwd": (c_int, [_P, c_int64, c_int32, c_int32, c_int32, _P, _P]),

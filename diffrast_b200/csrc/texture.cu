@@ -547,6 +547,34 @@ __device__ __forceinline__ void add_footprint_taps(Taps& taps, const Footprint& 
   }
 }
 
+// Where the coordinate gradients go: pixel strides and, when the gradient is a channel slice of
+// wider pixel records whose other channels get zero gradient, the slice's first channel (-1: a
+// plain strided output, nothing else written).
+struct GradLayout {
+  long long uv, uv_da;
+  int uv_first, da_first;
+};
+
+// The N gradient values of pixel p: into the record's channels [first, first + N) with the rest
+// of the record zeroed (whole records, so that stores cover full sectors), or at out + p stride.
+template <int N>
+__device__ __forceinline__ void write_record(float* __restrict__ out, long long p, long long stride,
+                                             int first, const float (&v)[N]) {
+  if (first < 0) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) out[p * stride + i] = v[i];
+    return;
+  }
+  float* rec = out + p * stride;
+  for (int i = 0; i < stride; ++i) {
+    float value = 0.0f;
+#pragma unroll
+    for (int j = 0; j < N; ++j)
+      if (i == first + j) value = v[j];
+    rec[i] = value;
+  }
+}
+
 // Texel gradients: a warp covers 16 x 2 pixels of a 16 x 16 tile, whose taps mostly land on the
 // same texels (a texel of the chosen levels spans about a pixel; background pixels all read the
 // same few). Tap by tap, lanes adding to the same texel sum their contributions with a shuffle
@@ -558,7 +586,7 @@ __global__ void __launch_bounds__(256) texture_bwd_kernel(
     const float* __restrict__ uv_da, const float* __restrict__ bias, const Strides st, int height,
     int width,
     const float* __restrict__ grad_out, float* __restrict__ grad_uv,
-    float* __restrict__ grad_uv_da, float* __restrict__ grad_bias) {
+    float* __restrict__ grad_uv_da, float* __restrict__ grad_bias, const GradLayout gst) {
   const int col = blockIdx.x * 16 + (threadIdx.x & 15);
   const int row = blockIdx.y * 16 + (threadIdx.x >> 4);
   const long long view = blockIdx.z;
@@ -738,17 +766,12 @@ __global__ void __launch_bounds__(256) texture_bwd_kernel(
   if (B == DR_BOUNDARY_CUBE) {
     float g_dir[3] = {0.f, 0.f, 0.f}, g_dir_da[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (live) cube_project_bwd(k.cube, g_u, g_v, k.has_da ? g_da : nullptr, g_dir, g_dir_da);
-    if (grad_uv != nullptr)
-      for (int i = 0; i < 3; ++i) grad_uv[p * 3 + i] = g_dir[i];
-    if (grad_uv_da != nullptr)
-      for (int i = 0; i < 6; ++i) grad_uv_da[p * 6 + i] = g_dir_da[i];
+    if (grad_uv != nullptr) write_record<3>(grad_uv, p, gst.uv, gst.uv_first, g_dir);
+    if (grad_uv_da != nullptr) write_record<6>(grad_uv_da, p, gst.uv_da, gst.da_first, g_dir_da);
   } else {
-    if (grad_uv != nullptr) {
-      grad_uv[p * 2] = g_u;
-      grad_uv[p * 2 + 1] = g_v;
-    }
-    if (grad_uv_da != nullptr)
-      for (int i = 0; i < 4; ++i) grad_uv_da[p * 4 + i] = g_da[i];
+    const float g_uv[2] = {g_u, g_v};
+    if (grad_uv != nullptr) write_record<2>(grad_uv, p, gst.uv, gst.uv_first, g_uv);
+    if (grad_uv_da != nullptr) write_record<4>(grad_uv_da, p, gst.uv_da, gst.da_first, g_da);
   }
 }
 
@@ -854,11 +877,11 @@ template <int MODE, int B>
 void launch_bwd(const Levels& L, int channels, int grad_stride, const float* uv,
                 const float* uv_da, const float* bias, Strides st, int batch, int height,
                 int width, const float* grad_out, float* grad_uv, float* grad_uv_da,
-                float* grad_bias, cudaStream_t s) {
+                float* grad_bias, GradLayout gst, cudaStream_t s) {
   const dim3 grid((width + 15) / 16, (height + 15) / 16, batch);
   texture_bwd_kernel<MODE, B><<<grid, 256, 0, s>>>(L, channels, grad_stride, uv, uv_da, bias, st,
                                                   height, width, grad_out, grad_uv, grad_uv_da,
-                                                  grad_bias);
+                                                  grad_bias, gst);
 }
 
 template <int B, typename F>
@@ -946,8 +969,9 @@ extern "C" int dr_texture_bwd(const float* const* level_ptr, float* const* grad_
                               int64_t uv_stride, const float* uv_da, int64_t uv_da_stride,
                               const float* bias, int64_t batch, int32_t height, int32_t width,
                               int32_t filter_mode, int32_t boundary_mode, const float* grad_out,
-                              float* grad_uv, float* grad_uv_da, float* grad_bias,
-                              void* stream) {
+                              float* grad_uv, int64_t grad_uv_stride, int32_t grad_uv_first,
+                              float* grad_uv_da, int64_t grad_uv_da_stride,
+                              int32_t grad_uv_da_first, float* grad_bias, void* stream) {
   if (grad_level_ptr == nullptr) return DR_ERR_INVALID_ARGUMENT;
   Levels L;
   int status = make_levels(level_ptr, grad_level_ptr, level_h, level_w, level_batch_stride,
@@ -965,6 +989,13 @@ extern "C" int dr_texture_bwd(const float* const* level_ptr, float* const* grad_
   const int da_width = boundary_mode == DR_BOUNDARY_CUBE ? 6 : 4;
   const Strides st = {uv_stride > 0 ? uv_stride : uv_width, uv_da_stride > 0 ? uv_da_stride : da_width};
   if (st.uv < uv_width || (uv_da != nullptr && st.uv_da < da_width)) return DR_ERR_INVALID_ARGUMENT;
+  const GradLayout gst = {grad_uv_stride > 0 ? grad_uv_stride : uv_width,
+                          grad_uv_da_stride > 0 ? grad_uv_da_stride : da_width,
+                          grad_uv_first < 0 ? -1 : grad_uv_first,
+                          grad_uv_da_first < 0 ? -1 : grad_uv_da_first};
+  if (gst.uv < uv_width || gst.uv_da < da_width) return DR_ERR_INVALID_ARGUMENT;
+  if (gst.uv_first + uv_width > gst.uv || gst.da_first + da_width > gst.uv_da)
+    return DR_ERR_INVALID_ARGUMENT;
   if (grad_channel_stride == 4) {
     for (int l = 0; l < num_levels; ++l)
       if ((reinterpret_cast<uintptr_t>(grad_level_ptr[l]) & 15u) != 0) return DR_ERR_INVALID_ARGUMENT;
@@ -974,7 +1005,7 @@ extern "C" int dr_texture_bwd(const float* const* level_ptr, float* const* grad_
     launch_bwd<decltype(m)::value, decltype(b)::value>(L, channels, grad_channel_stride, uv, uv_da,
                                                        bias, st, static_cast<int>(batch), height,
                                                        width, grad_out, grad_uv, grad_uv_da,
-                                                       grad_bias, s);
+                                                       grad_bias, gst, s);
   });
   return launch_status();
 }

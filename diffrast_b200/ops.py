@@ -317,10 +317,12 @@ def texture(
         if mode < 3:
             uv_da = None if uv_da is None else uv_da.detach()
             mip_level_bias = None if mip_level_bias is None else mip_level_bias.detach()
+        uv_src, uv_spec = _channel_slice(uv)
+        da_src, da_spec = _channel_slice(uv_da)
         with torch.cuda.device(uv.device):
             return F.TextureChain.apply(
-                uv, uv_da, None if mip_level_bias is None else mip_level_bias.contiguous(), mode,
-                _BOUNDARY_INDEX[boundary_mode], count, tex,
+                uv_src, da_src, None if mip_level_bias is None else mip_level_bias.contiguous(),
+                mode, _BOUNDARY_INDEX[boundary_mode], count, tex, uv_spec, da_spec,
             )
     if mipmapped:
         if given is None:
@@ -339,11 +341,30 @@ def texture(
         mip_level_bias = None if mip_level_bias is None or mode < 2 else mip_level_bias.detach()
     # uv and uv_da may be channel slices of a wider tensor (such as interpolate's output): the
     # kernels read them in place through their pixel stride.
+    uv_src, uv_spec = _channel_slice(uv)
+    da_src, da_spec = _channel_slice(uv_da)
     with torch.cuda.device(uv.device):
         return F.Texture.apply(
-            uv, uv_da, None if mip_level_bias is None else mip_level_bias.contiguous(), mode,
-            _BOUNDARY_INDEX[boundary_mode], *levels,
+            uv_src, da_src, None if mip_level_bias is None else mip_level_bias.contiguous(), mode,
+            _BOUNDARY_INDEX[boundary_mode], uv_spec, da_spec, *levels,
         )
+
+
+def _channel_slice(t: Tensor | None):
+    """``(base, (first channel, count))`` when ``t`` is a slice of the last dimension of a
+    contiguous tensor and gradients flow to it (interpolate's ``out[..., 0:2]``, say), so that
+    the lookup can write its gradient straight into the base's; ``(t, None)`` otherwise."""
+    if t is None or not t.requires_grad or not torch.is_grad_enabled():
+        return t, None
+    base = t._base
+    if (base is None or not base.requires_grad or base.ndim != t.ndim or base.dtype != t.dtype
+            or not base.is_contiguous() or base.shape[:-1] != t.shape[:-1]
+            or t.stride()[:-1] != base.stride()[:-1] or t.stride(-1) != 1):
+        return t, None
+    first = t.storage_offset() - base.storage_offset()
+    if first < 0 or first + t.shape[-1] > base.shape[-1]:
+        return t, None
+    return base, (first, t.shape[-1])
 
 
 def texture_construct_mip(

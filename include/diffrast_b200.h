@@ -142,15 +142,21 @@ int dr_texture_fwd(const float* const* level_ptr, const int32_t* level_h, const 
 /* Texel gradients are ACCUMULATED into grad_level_ptr[l] (clear them first), laid out like the
  * levels but with grad_channel_stride (>= channels) floats per texel; with 4 (and channels <= 4,
  * 16-byte aligned buffers) each texel's gradient is added with one vector reduction. grad_uv,
- * grad_uv_da and grad_bias (each NULL to skip) are written. */
+ * grad_uv_da and grad_bias (each NULL to skip) are written. grad_uv and grad_uv_da have their own
+ * pixel strides (0 = contiguous). With grad_uv_first = -1 the pointer addresses the gradient
+ * itself and nothing else is written; with grad_uv_first = c >= 0 it addresses pixel records of
+ * grad_uv_stride floats (such as the gradient of dr_interpolate_fwd's output, whose channels
+ * c, c + 1 are uv): the gradient goes to channels c.. and every other float of each record is
+ * set to zero, so that the caller need not clear them. Likewise grad_uv_da_first. */
 int dr_texture_bwd(const float* const* level_ptr, float* const* grad_level_ptr,
                    const int32_t* level_h, const int32_t* level_w,
                    const int64_t* level_batch_stride, int32_t num_levels, int32_t channels,
                    int32_t grad_channel_stride, const float* uv, int64_t uv_stride,
                    const float* uv_da, int64_t uv_da_stride, const float* bias, int64_t batch,
                    int32_t height, int32_t width, int32_t filter_mode, int32_t boundary_mode,
-                   const float* grad_out, float* grad_uv, float* grad_uv_da, float* grad_bias,
-                   void* stream);
+                   const float* grad_out, float* grad_uv, int64_t grad_uv_stride,
+                   int32_t grad_uv_first, float* grad_uv_da, int64_t grad_uv_da_stride,
+                   int32_t grad_uv_da_first, float* grad_bias, void* stream);
 
 /* One mip step (reference.py:449-488): dst [images, (h + 1) / 2, (w + 1) / 2, channels] from
  * src [images, h, w, channels] by area weights; `images` = tex_batch, or 6 * tex_batch for a cube. */

@@ -412,6 +412,34 @@ def test_edge_neighbours_match_golden():
 # ---------------------------------------------------------------------------------------------
 
 
+def test_texture_of_interpolated_slices_routes_gradients(ctx):
+    """uv = out[..., 0:2] and uv_da = out_da[..., 0:4] of interpolate: the lookup writes their
+    gradients straight into the gradients of out and out_da; the result equals passing copies."""
+    sc = scenes.config1_scene(seed=2)
+    pos, tri = sc["pos"].cuda(), sc["tri"].cuda()
+    gen = torch.Generator().manual_seed(5)
+    attr = torch.cat([sc["uv"], torch.rand(sc["uv"].shape[0], 3, generator=gen)], -1).cuda()
+    tex = torch.rand(1, 64, 64, 3, generator=gen).cuda()
+    weights = torch.randn(1, 48, 48, 3, generator=gen).cuda()
+    rast, rast_db = dr.rasterize(ctx, pos, tri, (48, 48))
+    for mode, mip in (("linear-mipmap-linear", None), ("linear-mipmap-linear", "stack"),
+                      ("linear", None)):
+        results = []
+        for copy in (False, True):
+            a = attr.clone().requires_grad_(True)
+            t = tex.clone().requires_grad_(True)
+            out, out_da = dr.interpolate(a, rast, tri, rast_db=rast_db, diff_attrs="all")
+            uv, uv_da = out[..., 0:2], out_da[..., 0:4]
+            if copy:
+                uv, uv_da = uv.clone(), uv_da.clone()
+            stack = dr.texture_construct_mip(t) if mip else None
+            color = dr.texture(t, uv, uv_da, mip=stack, filter_mode=mode)
+            grads = torch.autograd.grad((color * weights).sum(), [a, t])
+            results.append((color, *grads))
+        for ours, ref in zip(results[0], results[1]):
+            grad_close(ours, ref, 1e-5)
+
+
 def test_config1_pipeline_matches_oracle(ctx):
     sc = scenes.config1_scene(seed=0)
     res = (64, 64)
