@@ -217,7 +217,8 @@ def run_ours(args) -> None:
         color = dr.texture(tex, out[..., 0:2], out_da[..., 0:4], filter_mode="linear-mipmap-linear")
         image = dr.antialias(color, rast, pos_in, tri, topology_hash=topo)
         # Mean over the whole job's pixels, so that the ranks' gradients sum to the full batch's.
-        loss = ((image - target_in) ** 2).sum() / (args.views * res * res * TEX_CHANNELS)
+        loss = torch.nn.functional.mse_loss(image, target_in, reduction="sum") / (
+            args.views * res * res * TEX_CHANNELS)
         loss.backward()
         sum_gradients([tex])
         return loss
@@ -384,7 +385,7 @@ def cpu_sample(args):
         color = oracle.texture(t, out[..., 0:2].contiguous(), out_da[..., 0:4].contiguous(), None,
                                None, "linear-mipmap-linear", "wrap")
         image = oracle.antialias(color, rast, p, tri)
-        loss = ((image - target) ** 2).mean()
+        loss = torch.nn.functional.mse_loss(image, target)
         loss.backward()
         return loss.item()
 

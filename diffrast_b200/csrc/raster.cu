@@ -17,7 +17,7 @@
 //      thread keeps the minimum key of its pixel in a register and merges it with one atomicMin.
 // Resolve: one thread per pixel turns the key into rast = (u, v, z/w, id + 1) and rast_db; the
 // backward pass chains the gradients of rast and rast_db into the three vertices and scatters
-// them with warp-aggregated float4 reductions.
+// them with float4 reductions.
 #include <cstdint>
 
 #include "common.cuh"
@@ -557,19 +557,34 @@ struct PixelTri {
   float px, py;
 };
 
+// Pixel (view b, row, col) of the resolve kernels' grid: columns in x, rows in y, views in z
+// (from view b0 on).
+struct ResolvePixel {
+  int b, row, col;
+  long long p;
+  bool inside;
+};
+
+__device__ __forceinline__ ResolvePixel resolve_pixel(int b0, int height, int width) {
+  ResolvePixel r;
+  r.col = blockIdx.x * blockDim.x + threadIdx.x;
+  r.row = blockIdx.y;
+  r.b = b0 + static_cast<int>(blockIdx.z);
+  r.inside = r.col < width;
+  r.p = (static_cast<long long>(r.b) * height + r.row) * width + r.col;
+  return r;
+}
+
 __device__ __forceinline__ PixelTri pixel_triangle(const float* __restrict__ pos,
                                                    const int* __restrict__ tri,
                                                    const long long* __restrict__ keys,
-                                                   long long p, int num_vert, int height,
+                                                   const ResolvePixel& rp, int num_vert, int height,
                                                    int width) {
   PixelTri r;
-  const long long key = keys[p];
+  const long long key = keys[rp.p];
   r.covered = key != kEmptyKey;
-  const long long hw = static_cast<long long>(height) * width;
-  r.b = static_cast<int>(p / hw);
-  const long long in_image = p - r.b * hw;
-  const int row = static_cast<int>(in_image / width);
-  const int col = static_cast<int>(in_image - static_cast<long long>(row) * width);
+  r.b = rp.b;
+  const int row = rp.row, col = rp.col;
   r.px = pixel_centre(col, width);
   r.py = pixel_centre(row, height);
   r.t = static_cast<int>(key & 0xFFFFFFFFLL);
@@ -590,11 +605,12 @@ __device__ __forceinline__ PixelTri pixel_triangle(const float* __restrict__ pos
 
 __global__ void __launch_bounds__(256) resolve_fwd_kernel(
     const float* __restrict__ pos, const int* __restrict__ tri, const long long* __restrict__ keys,
-    long long total, int num_vert, int height, int width, float4* __restrict__ rast,
+    int b0, int num_vert, int height, int width, float4* __restrict__ rast,
     float4* __restrict__ rast_db) {
-  const long long p = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
-  if (p >= total) return;
-  const PixelTri q = pixel_triangle(pos, tri, keys, p, num_vert, height, width);
+  const ResolvePixel rp = resolve_pixel(b0, height, width);
+  if (!rp.inside) return;
+  const long long p = rp.p;
+  const PixelTri q = pixel_triangle(pos, tri, keys, rp, num_vert, height, width);
   if (!q.covered) {
     rast[p] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     if (rast_db != nullptr) rast_db[p] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
@@ -605,10 +621,10 @@ __global__ void __launch_bounds__(256) resolve_fwd_kernel(
   const float c0 = v0.y - q.py * v0.w, c1 = v1.y - q.py * v1.w, c2 = v2.y - q.py * v2.w;
   const float e0 = a1 * c2 - a2 * c1, e1 = a2 * c0 - a0 * c2, e2 = a0 * c1 - a1 * c0;
   const float s = e0 + e1 + e2;
-  const float b0 = e0 / s, b1 = e1 / s;
+  const float u = e0 / s, v = e1 / s;
   const float ew = e0 * v0.w + e1 * v1.w + e2 * v2.w;
   const float depth = (e0 * v0.z + e1 * v1.z + e2 * v2.z) / ew;
-  rast[p] = make_float4(b0, b1, depth, static_cast<float>(q.t + 1));
+  rast[p] = make_float4(u, v, depth, static_cast<float>(q.t + 1));
   if (rast_db != nullptr) {
     // de/dpx = c x w and de/dpy = w x a (reference.py:281-290).
     const float dx0 = c1 * v2.w - c2 * v1.w, dx1 = c2 * v0.w - c0 * v2.w;
@@ -616,9 +632,11 @@ __global__ void __launch_bounds__(256) resolve_fwd_kernel(
     const float dy0 = v1.w * a2 - v2.w * a1, dy1 = v2.w * a0 - v0.w * a2;
     const float dy2 = v0.w * a1 - v1.w * a0;
     const float sx = dx0 + dx1 + dx2, sy = dy0 + dy1 + dy2;
-    const float scale_x = 2.0f / static_cast<float>(width), scale_y = 2.0f / static_cast<float>(height);
-    rast_db[p] = make_float4((dx0 - b0 * sx) / s * scale_x, (dy0 - b0 * sy) / s * scale_y,
-                             (dx1 - b1 * sx) / s * scale_x, (dy1 - b1 * sy) / s * scale_y);
+    const float inv_s = 1.0f / s;
+    const float scale_x = 2.0f / static_cast<float>(width) * inv_s;
+    const float scale_y = 2.0f / static_cast<float>(height) * inv_s;
+    rast_db[p] = make_float4((dx0 - u * sx) * scale_x, (dy0 - u * sy) * scale_y,
+                             (dx1 - v * sx) * scale_x, (dy1 - v * sy) * scale_y);
   }
 }
 
@@ -630,13 +648,13 @@ __device__ __forceinline__ void cross3(const float u[3], const float v[3], float
 
 __global__ void __launch_bounds__(256) resolve_bwd_kernel(
     const float* __restrict__ pos, const int* __restrict__ tri, const long long* __restrict__ keys,
-    long long total, int num_vert, int height, int width, const float4* __restrict__ grad_rast,
+    int b0, int num_vert, int height, int width, const float4* __restrict__ grad_rast,
     const float4* __restrict__ grad_db, float* __restrict__ grad_pos) {
-  const long long p = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
-  const bool in_range = p < total;
+  const ResolvePixel rp = resolve_pixel(b0, height, width);
+  const long long p = rp.p;
   PixelTri q;
-  if (in_range) {
-    q = pixel_triangle(pos, tri, keys, p, num_vert, height, width);
+  if (rp.inside) {
+    q = pixel_triangle(pos, tri, keys, rp, num_vert, height, width);
   } else {
     q.covered = false;
     q.b = 0;
@@ -651,9 +669,11 @@ __global__ void __launch_bounds__(256) resolve_bwd_kernel(
     float e[3];
     cross3(a, c, e);
     const float s = e[0] + e[1] + e[2];
-    const float b[3] = {e[0] / s, e[1] / s, e[2] / s};
+    const float inv_s = 1.0f / s;
+    const float b[3] = {e[0] * inv_s, e[1] * inv_s, e[2] * inv_s};
     const float ew = e[0] * w[0] + e[1] * w[1] + e[2] * w[2];
-    const float depth = (e[0] * z[0] + e[1] * z[1] + e[2] * z[2]) / ew;
+    const float inv_ew = 1.0f / ew;
+    const float depth = (e[0] * z[0] + e[1] * z[1] + e[2] * z[2]) * inv_ew;
     const float4 gr = grad_rast[p];
     float gb[3] = {gr.x, gr.y, 0.0f};
     float gs = 0.0f;
@@ -668,18 +688,18 @@ __global__ void __launch_bounds__(256) resolve_bwd_kernel(
       // Gradients of db_dx_k = (dx_k - b_k sx) / s and db_dy_k, k = 0, 1.
       const float gbx[3] = {gd.x * scale_x, gd.z * scale_x, 0.0f};
       const float gby[3] = {gd.y * scale_y, gd.w * scale_y, 0.0f};
-      const float dbx0 = (dx[0] - b[0] * sx) / s, dbx1 = (dx[1] - b[1] * sx) / s;
-      const float dby0 = (dy[0] - b[0] * sy) / s, dby1 = (dy[1] - b[1] * sy) / s;
-      const float shared_x = (gbx[0] * b[0] + gbx[1] * b[1]) / s;
-      const float shared_y = (gby[0] * b[0] + gby[1] * b[1]) / s;
+      const float dbx0 = (dx[0] - b[0] * sx) * inv_s, dbx1 = (dx[1] - b[1] * sx) * inv_s;
+      const float dby0 = (dy[0] - b[0] * sy) * inv_s, dby1 = (dy[1] - b[1] * sy) * inv_s;
+      const float shared_x = (gbx[0] * b[0] + gbx[1] * b[1]) * inv_s;
+      const float shared_y = (gby[0] * b[0] + gby[1] * b[1]) * inv_s;
       float gdx[3], gdy[3];
       for (int k = 0; k < 3; ++k) {
-        gdx[k] = gbx[k] / s - shared_x;
-        gdy[k] = gby[k] / s - shared_y;
+        gdx[k] = gbx[k] * inv_s - shared_x;
+        gdy[k] = gby[k] * inv_s - shared_y;
       }
-      gb[0] -= (gbx[0] * sx + gby[0] * sy) / s;
-      gb[1] -= (gbx[1] * sx + gby[1] * sy) / s;
-      gs -= (gbx[0] * dbx0 + gbx[1] * dbx1 + gby[0] * dby0 + gby[1] * dby1) / s;
+      gb[0] -= (gbx[0] * sx + gby[0] * sy) * inv_s;
+      gb[1] -= (gbx[1] * sx + gby[1] * sy) * inv_s;
+      gs -= (gbx[0] * dbx0 + gbx[1] * dbx1 + gby[0] * dby0 + gby[1] * dby1) * inv_s;
       // dx = c x w: dL/dc += w x gdx, dL/dw += gdx x c. dy = w x a: dL/dw += a x gdy,
       // dL/da += gdy x w.
       float t[3];
@@ -693,11 +713,11 @@ __global__ void __launch_bounds__(256) resolve_bwd_kernel(
       for (int k = 0; k < 3; ++k) ga[k] += t[k];
     }
     // b = e / s with s = sum(e).
-    gs -= (gb[0] * b[0] + gb[1] * b[1] + gb[2] * b[2]) / s;
+    gs -= (gb[0] * b[0] + gb[1] * b[1] + gb[2] * b[2]) * inv_s;
     float ge[3];
-    for (int k = 0; k < 3; ++k) ge[k] = gb[k] / s + gs;
+    for (int k = 0; k < 3; ++k) ge[k] = gb[k] * inv_s + gs;
     // depth = (e . z) / (e . w).
-    const float g_ew = gr.z / ew;
+    const float g_ew = gr.z * inv_ew;
     float gz[3];
     for (int k = 0; k < 3; ++k) {
       ge[k] += g_ew * (z[k] - depth * w[k]);
@@ -720,9 +740,13 @@ __global__ void __launch_bounds__(256) resolve_bwd_kernel(
     }
   }
   const long long base = static_cast<long long>(q.b) * num_vert;
-  scatter_row4(grad_pos, base + q.i0, q.covered, gv[0]);
-  scatter_row4(grad_pos, base + q.i1, q.covered, gv[1]);
-  scatter_row4(grad_pos, base + q.i2, q.covered, gv[2]);
+  // Plain vector reductions: with triangles of about a pixel, lanes of a warp rarely share a
+  // vertex slot, so a warp-level match finds little to merge and costs more than it saves.
+  if (q.covered) {
+    red_add_v4(grad_pos + (base + q.i0) * 4, gv[0][0], gv[0][1], gv[0][2], gv[0][3]);
+    red_add_v4(grad_pos + (base + q.i1) * 4, gv[1][0], gv[1][1], gv[1][2], gv[1][3]);
+    red_add_v4(grad_pos + (base + q.i2) * 4, gv[2][0], gv[2][1], gv[2][2], gv[2][3]);
+  }
 }
 
 bool bad_raster_args(const float* pos, const int32_t* tri, int64_t batch, int64_t num_vert,
@@ -845,9 +869,14 @@ extern "C" int dr_raster_resolve_fwd(const float* pos, const int32_t* tri, const
     return DR_ERR_INVALID_ARGUMENT;
   const long long total = batch * static_cast<long long>(height) * width;
   if (total == 0) return DR_OK;
-  resolve_fwd_kernel<<<blocks_for(total, 256), 256, 0, as_stream(stream)>>>(
-      pos, tri, reinterpret_cast<const long long*>(keys), total, static_cast<int>(num_vert),
-      height, width, reinterpret_cast<float4*>(rast), reinterpret_cast<float4*>(rast_db));
+  if (height > 65535) return DR_ERR_TOO_LARGE;
+  for (long long b0 = 0; b0 < batch; b0 += 65535) {
+    const dim3 grid((width + 255) / 256, height, static_cast<unsigned>(min(batch - b0, 65535LL)));
+    resolve_fwd_kernel<<<grid, 256, 0, as_stream(stream)>>>(
+        pos, tri, reinterpret_cast<const long long*>(keys), static_cast<int>(b0),
+        static_cast<int>(num_vert), height, width, reinterpret_cast<float4*>(rast),
+        reinterpret_cast<float4*>(rast_db));
+  }
   return launch_status();
 }
 
@@ -860,9 +889,13 @@ extern "C" int dr_raster_resolve_bwd(const float* pos, const int32_t* tri, const
     return DR_ERR_INVALID_ARGUMENT;
   const long long total = batch * static_cast<long long>(height) * width;
   if (total == 0) return DR_OK;
-  resolve_bwd_kernel<<<blocks_for(total, 256), 256, 0, as_stream(stream)>>>(
-      pos, tri, reinterpret_cast<const long long*>(keys), total, static_cast<int>(num_vert),
-      height, width, reinterpret_cast<const float4*>(grad_rast),
-      reinterpret_cast<const float4*>(grad_db), grad_pos);
+  if (height > 65535) return DR_ERR_TOO_LARGE;
+  for (long long b0 = 0; b0 < batch; b0 += 65535) {
+    const dim3 grid((width + 255) / 256, height, static_cast<unsigned>(min(batch - b0, 65535LL)));
+    resolve_bwd_kernel<<<grid, 256, 0, as_stream(stream)>>>(
+        pos, tri, reinterpret_cast<const long long*>(keys), static_cast<int>(b0),
+        static_cast<int>(num_vert), height, width, reinterpret_cast<const float4*>(grad_rast),
+        reinterpret_cast<const float4*>(grad_db), grad_pos);
+  }
   return launch_status();
 }
