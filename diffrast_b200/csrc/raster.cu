@@ -603,40 +603,73 @@ __device__ __forceinline__ PixelTri pixel_triangle(const float* __restrict__ pos
   return r;
 }
 
-__global__ void __launch_bounds__(256) resolve_fwd_kernel(
+// Pixels per thread of the resolve forward pass: each thread walks kResolvePix pixels of a row,
+// 128 columns apart, one load phase at a time (keys, then vertex indices, then vertices), so that
+// the loads of all its pixels are in flight together.
+constexpr int kResolvePix = 2;
+constexpr int kResolveThreads = 128;
+
+__global__ void __launch_bounds__(kResolveThreads) resolve_fwd_kernel(
     const float* __restrict__ pos, const int* __restrict__ tri, const long long* __restrict__ keys,
     int b0, int num_vert, int height, int width, float4* __restrict__ rast,
     float4* __restrict__ rast_db) {
-  const ResolvePixel rp = resolve_pixel(b0, height, width);
-  if (!rp.inside) return;
-  const long long p = rp.p;
-  const PixelTri q = pixel_triangle(pos, tri, keys, rp, num_vert, height, width);
-  if (!q.covered) {
-    rast[p] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    if (rast_db != nullptr) rast_db[p] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    return;
+  const int row = blockIdx.y;
+  const long long b = b0 + static_cast<long long>(blockIdx.z);
+  const long long row_start = (b * height + row) * width;
+  const long long base = b * num_vert;
+  long long key[kResolvePix];
+#pragma unroll
+  for (int i = 0; i < kResolvePix; ++i) {
+    const int col = blockIdx.x * (kResolveThreads * kResolvePix) + i * kResolveThreads + threadIdx.x;
+    key[i] = col < width ? keys[row_start + col] : kEmptyKey;
   }
-  const Vert &v0 = q.v0, &v1 = q.v1, &v2 = q.v2;
-  const float a0 = v0.x - q.px * v0.w, a1 = v1.x - q.px * v1.w, a2 = v2.x - q.px * v2.w;
-  const float c0 = v0.y - q.py * v0.w, c1 = v1.y - q.py * v1.w, c2 = v2.y - q.py * v2.w;
-  const float e0 = a1 * c2 - a2 * c1, e1 = a2 * c0 - a0 * c2, e2 = a0 * c1 - a1 * c0;
-  const float s = e0 + e1 + e2;
-  const float u = e0 / s, v = e1 / s;
-  const float ew = e0 * v0.w + e1 * v1.w + e2 * v2.w;
-  const float depth = (e0 * v0.z + e1 * v1.z + e2 * v2.z) / ew;
-  rast[p] = make_float4(u, v, depth, static_cast<float>(q.t + 1));
-  if (rast_db != nullptr) {
-    // de/dpx = c x w and de/dpy = w x a (reference.py:281-290).
-    const float dx0 = c1 * v2.w - c2 * v1.w, dx1 = c2 * v0.w - c0 * v2.w;
-    const float dx2 = c0 * v1.w - c1 * v0.w;
-    const float dy0 = v1.w * a2 - v2.w * a1, dy1 = v2.w * a0 - v0.w * a2;
-    const float dy2 = v0.w * a1 - v1.w * a0;
-    const float sx = dx0 + dx1 + dx2, sy = dy0 + dy1 + dy2;
-    const float inv_s = 1.0f / s;
-    const float scale_x = 2.0f / static_cast<float>(width) * inv_s;
-    const float scale_y = 2.0f / static_cast<float>(height) * inv_s;
-    rast_db[p] = make_float4((dx0 - u * sx) * scale_x, (dy0 - u * sy) * scale_y,
-                             (dx1 - v * sx) * scale_x, (dy1 - v * sy) * scale_y);
+  int idx[kResolvePix][3];
+#pragma unroll
+  for (int i = 0; i < kResolvePix; ++i) {
+    const long long t3 = 3 * (key[i] & 0xFFFFFFFFLL);
+#pragma unroll
+    for (int k = 0; k < 3; ++k) idx[i][k] = key[i] != kEmptyKey ? __ldg(tri + t3 + k) : 0;
+  }
+  Vert v[kResolvePix][3];
+#pragma unroll
+  for (int i = 0; i < kResolvePix; ++i)
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+      v[i][k] = key[i] != kEmptyKey ? load_vert(pos, base + idx[i][k]) : Vert{0.f, 0.f, 0.f, 1.f};
+  const float py = pixel_centre(row, height);
+#pragma unroll
+  for (int i = 0; i < kResolvePix; ++i) {
+    const int col = blockIdx.x * (kResolveThreads * kResolvePix) + i * kResolveThreads + threadIdx.x;
+    if (col >= width) continue;
+    const long long p = row_start + col;
+    if (key[i] == kEmptyKey) {
+      rast[p] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      if (rast_db != nullptr) rast_db[p] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      continue;
+    }
+    const float px = pixel_centre(col, width);
+    const Vert &v0 = v[i][0], &v1 = v[i][1], &v2 = v[i][2];
+    const float a0 = v0.x - px * v0.w, a1 = v1.x - px * v1.w, a2 = v2.x - px * v2.w;
+    const float c0 = v0.y - py * v0.w, c1 = v1.y - py * v1.w, c2 = v2.y - py * v2.w;
+    const float e0 = a1 * c2 - a2 * c1, e1 = a2 * c0 - a0 * c2, e2 = a0 * c1 - a1 * c0;
+    const float s = e0 + e1 + e2;
+    const float u = e0 / s, vv = e1 / s;
+    const float ew = e0 * v0.w + e1 * v1.w + e2 * v2.w;
+    const float depth = (e0 * v0.z + e1 * v1.z + e2 * v2.z) / ew;
+    rast[p] = make_float4(u, vv, depth, static_cast<float>((key[i] & 0xFFFFFFFFLL) + 1));
+    if (rast_db != nullptr) {
+      // de/dpx = c x w and de/dpy = w x a (reference.py:281-290).
+      const float dx0 = c1 * v2.w - c2 * v1.w, dx1 = c2 * v0.w - c0 * v2.w;
+      const float dx2 = c0 * v1.w - c1 * v0.w;
+      const float dy0 = v1.w * a2 - v2.w * a1, dy1 = v2.w * a0 - v0.w * a2;
+      const float dy2 = v0.w * a1 - v1.w * a0;
+      const float sx = dx0 + dx1 + dx2, sy = dy0 + dy1 + dy2;
+      const float inv_s = 1.0f / s;
+      const float scale_x = 2.0f / static_cast<float>(width) * inv_s;
+      const float scale_y = 2.0f / static_cast<float>(height) * inv_s;
+      rast_db[p] = make_float4((dx0 - u * sx) * scale_x, (dy0 - u * sy) * scale_y,
+                               (dx1 - vv * sx) * scale_x, (dy1 - vv * sy) * scale_y);
+    }
   }
 }
 
@@ -871,8 +904,9 @@ extern "C" int dr_raster_resolve_fwd(const float* pos, const int32_t* tri, const
   if (total == 0) return DR_OK;
   if (height > 65535) return DR_ERR_TOO_LARGE;
   for (long long b0 = 0; b0 < batch; b0 += 65535) {
-    const dim3 grid((width + 255) / 256, height, static_cast<unsigned>(min(batch - b0, 65535LL)));
-    resolve_fwd_kernel<<<grid, 256, 0, as_stream(stream)>>>(
+    const dim3 grid((width + kResolveThreads * kResolvePix - 1) / (kResolveThreads * kResolvePix),
+                    height, static_cast<unsigned>(min(batch - b0, 65535LL)));
+    resolve_fwd_kernel<<<grid, kResolveThreads, 0, as_stream(stream)>>>(
         pos, tri, reinterpret_cast<const long long*>(keys), static_cast<int>(b0),
         static_cast<int>(num_vert), height, width, reinterpret_cast<float4*>(rast),
         reinterpret_cast<float4*>(rast_db));
