@@ -79,6 +79,19 @@ __device__ __forceinline__ float side_sign(const float l[3], const float4& p) {
 // Whether edge k of triangle t is a silhouette in view pb (reference.py:790-814): unshared, shared
 // by several, or shared with a triangle whose opposite vertex lies on the same side of it. v holds
 // t's vertex indices and clip-space x, y, w.
+// The side test with the opposite vertex's position po already loaded.
+__device__ __forceinline__ bool silhouette_side(const Tri2& v, int k, const float4& po) {
+  const int i = (k + 1) % 3, j = (k + 2) % 3;
+  const float A[3] = {v.x[i], v.y[i], v.w[i]}, B[3] = {v.x[j], v.y[j], v.w[j]};
+  float l[3];
+  for (int c = 0; c < 3; ++c) {
+    const int ci = (c + 1) % 3, cj = (c + 2) % 3;
+    l[c] = __fmaf_rn(A[ci], B[cj], -mul(A[cj], B[ci]));
+  }
+  const float s1 = side_sign(l, make_float4(v.x[k], v.y[k], 0.0f, v.w[k]));
+  return mul(s1, side_sign(l, po)) > 0.0f;
+}
+
 __device__ __forceinline__ bool silhouette_of(const AaCtx& a, long long pb, const Tri2& v, int t,
                                               int k) {
   const int opp = __ldg(a.opposite + 3 * static_cast<long long>(t) + k);
@@ -103,44 +116,64 @@ struct Crossing {
 
 // reference.py:675-727 for one pixel pair side: triangle t seen at src, followed towards dst.
 // As in the reference, a = x - px w and c = y - py w are formed once per vertex and point and
-// shared by the three edge functions and the slack (reference.py:274-278, :730-746).
-__device__ __forceinline__ Crossing crossing(const AaCtx& a, long long pb, int t, float sx,
-                                             float sy, float dx, float dy, bool horizontal) {
-  Crossing r = {false, 0.0f, 0};
-  if (t < 0) return r;
-  const Tri2 v = load_tri(a, pb, t);
-  float as[3], cs[3], ad[3], cd[3];
+// shared by the three edge functions and the slack (reference.py:274-278, :730-746). The terms of
+// the source point are computed once (SrcTerms) and shared by the directions a pixel's triangle is
+// followed in: for a horizontal step the destination's c equal the source's, for a vertical step
+// its a, bit for bit, so only the other half is formed again.
+struct SrcTerms {
+  float as[3], cs[3], es[3];
+  float sign;
+  float rx[3], ry[3];
+};
+
+__device__ __forceinline__ SrcTerms src_terms(const Tri2& v, float sx, float sy) {
+  SrcTerms S;
   for (int k = 0; k < 3; ++k) {
-    as[k] = sub(v.x[k], mul(sx, v.w[k]));
-    cs[k] = sub(v.y[k], mul(sy, v.w[k]));
-    ad[k] = sub(v.x[k], mul(dx, v.w[k]));
-    cd[k] = sub(v.y[k], mul(dy, v.w[k]));
+    S.as[k] = sub(v.x[k], mul(sx, v.w[k]));
+    S.cs[k] = sub(v.y[k], mul(sy, v.w[k]));
   }
-  float es[3], ed[3];
   for (int k = 0; k < 3; ++k) {
     const int i = (k + 1) % 3, j = (k + 2) % 3;
-    es[k] = cross2(as[i], cs[j], as[j], cs[i]);
-    ed[k] = cross2(ad[i], cd[j], ad[j], cd[i]);
+    S.es[k] = cross2(S.as[i], S.cs[j], S.as[j], S.cs[i]);
   }
-  const float sign = add(add(es[0], es[1]), es[2]) < 0.0f ? -1.0f : 1.0f;
-  float rx[3], ry[3];
+  S.sign = add(add(S.es[0], S.es[1]), S.es[2]) < 0.0f ? -1.0f : 1.0f;
   for (int k = 0; k < 3; ++k) {
-    rx[k] = add(fabsf(v.x[k]), fabsf(v.w[k]));
-    ry[k] = add(fabsf(v.y[k]), fabsf(v.w[k]));
+    S.rx[k] = add(fabsf(v.x[k]), fabsf(v.w[k]));
+    S.ry[k] = add(fabsf(v.y[k]), fabsf(v.w[k]));
+  }
+  return S;
+}
+
+// Crossing of triangle t (vertices v, source terms S) towards (d, sy) when horizontal, else
+// towards (sx, d), before the silhouette test: found means an edge is crossed and handled by this
+// axis; the caller completes it with the silhouette test of that edge.
+__device__ __forceinline__ Crossing crossing_candidate(const AaCtx& a, const Tri2& v,
+                                                       const SrcTerms& S, float d, bool horizontal) {
+  Crossing r = {false, 0.0f, 0};
+  float ad[3], cd[3];
+  for (int k = 0; k < 3; ++k) {
+    ad[k] = horizontal ? sub(v.x[k], mul(d, v.w[k])) : S.as[k];
+    cd[k] = horizontal ? S.cs[k] : sub(v.y[k], mul(d, v.w[k]));
+  }
+  float ed[3];
+  for (int k = 0; k < 3; ++k) {
+    const int i = (k + 1) % 3, j = (k + 2) % 3;
+    ed[k] = cross2(ad[i], cd[j], ad[j], cd[i]);
   }
   bool any = false;
   float best = __int_as_float(0x7f800000);
   int edge = 0;
   for (int k = 0; k < 3; ++k) {
     const int i = (k + 1) % 3, j = (k + 2) % 3;
-    const float span = sub(es[k], ed[k]);
+    const float span = sub(S.es[k], ed[k]);
     const float ai = fabsf(ad[i]), aj = fabsf(ad[j]), ci = fabsf(cd[i]), cj = fabsf(cd[j]);
-    const float terms = add(add(add(mul(add(rx[i], ai), cj), mul(add(rx[j], aj), ci)), mul(ry[j], ai)),
-                            mul(ry[i], aj));
+    const float terms = add(add(add(mul(add(S.rx[i], ai), cj), mul(add(S.rx[j], aj), ci)),
+                                mul(S.ry[j], ai)),
+                            mul(S.ry[i], aj));
     const float slack = mul(terms, kEdgeTie);
-    const bool crossed = (mul(ed[k], sign) <= slack) && (mul(span, sign) > mul(2.0f, slack));
+    const bool crossed = (mul(ed[k], S.sign) <= slack) && (mul(span, S.sign) > mul(2.0f, slack));
     any |= crossed;
-    const float tk = crossed ? dvd(es[k], span) : __int_as_float(0x7f800000);
+    const float tk = crossed ? dvd(S.es[k], span) : __int_as_float(0x7f800000);
     if (k == 0 || tk < best) {
       best = tk;
       edge = k;
@@ -155,11 +188,30 @@ __device__ __forceinline__ Crossing crossing(const AaCtx& a, long long pb, int t
   const float flat = mul(fabsf(cross2(v.x[j], v.w[i], v.x[i], v.w[j])), static_cast<float>(a.width));
   const bool along = horizontal ? (steep >= flat) : (flat > steep);
   if (!along) return r;
-  if (!silhouette_of(a, pb, v, t, edge)) return r;
   r.found = true;
   r.t = best;
   r.edge = edge;
   return r;
+}
+
+__device__ __forceinline__ Crossing crossing_dir(const AaCtx& a, long long pb, int t, const Tri2& v,
+                                                 const SrcTerms& S, float d, bool horizontal) {
+  Crossing r = crossing_candidate(a, v, S, d, horizontal);
+  if (r.found && !silhouette_of(a, pb, v, t, r.edge)) r.found = false;
+  return r;
+}
+
+// v holds triangle t's clip-space x, y, w and vertex indices.
+__device__ __forceinline__ Crossing crossing_of(const AaCtx& a, long long pb, int t, const Tri2& v,
+                                                float sx, float sy, float dx, float dy,
+                                                bool horizontal) {
+  return crossing_dir(a, pb, t, v, src_terms(v, sx, sy), horizontal ? dx : dy, horizontal);
+}
+
+__device__ __forceinline__ Crossing crossing(const AaCtx& a, long long pb, int t, float sx,
+                                             float sy, float dx, float dy, bool horizontal) {
+  if (t < 0) return {false, 0.0f, 0};
+  return crossing_of(a, pb, t, load_tri(a, pb, t), sx, sy, dx, dy, horizontal);
 }
 
 struct Pair {
@@ -219,69 +271,176 @@ __device__ __forceinline__ int edge_vertex(const AaCtx& a, const Pair& r, int k)
   return __ldg(a.tri + 3 * static_cast<long long>(r.owner) + (r.edge + k) % 3);
 }
 
-__device__ __forceinline__ unsigned pair_code(const Pair& r) {
-  return 8u | (r.use_p ? 4u : 0u) | static_cast<unsigned>(r.edge);
-}
-
 // Blend coefficients (bp, bq) of a recorded pair, as eval_pair forms them from t.
 __device__ __forceinline__ float2 recorded_blend(unsigned code, float t) {
   if (!(code & 8u)) return make_float2(0.f, 0.f);
   return t < 0.5f ? make_float2(sub(0.5f, t), 0.f) : make_float2(0.f, sub(t, 0.5f));
 }
 
-// Pixel tiling of the antialias kernels: a block of 32 x 8 threads covers a 31 x 7 tile of output
-// pixels plus a one-pixel halo to the left and above. Each thread evaluates the right pair of its
-// pixel (unless it is in the halo row) and the lower pair (unless it is in the halo column) once,
-// into shared memory; every output pixel then reads its four pairs from there. Pairs are thus
-// evaluated once per block instead of once by each of their two pixels.
+// Pixel tiling of the backward pass that repeats the edge tests (aa_bwd_kernel): a block of
+// 32 x 8 threads covers a 31 x 7 tile of output pixels plus a one-pixel halo to the left and above.
+// Each thread evaluates the right pair of its pixel (unless it is in the halo row) and the lower
+// pair (unless it is in the halo column) once, into shared memory; every output pixel then reads
+// its four pairs from there.
 constexpr int kAaThreadsX = 32, kAaThreadsY = 8;
 constexpr int kAaTileX = kAaThreadsX - 1, kAaTileY = kAaThreadsY - 1;
 
-__global__ void __launch_bounds__(256, 5) aa_fwd_kernel(const AaCtx a, float* __restrict__ out,
-                                                        PairRecords rec) {
-  __shared__ float2 hk[kAaThreadsY][kAaThreadsX], vk[kAaThreadsY][kAaThreadsX];
-  const int tx = threadIdx.x % kAaThreadsX, ty = threadIdx.x / kAaThreadsX;
-  const int col = blockIdx.x * kAaTileX + tx - 1, row = blockIdx.y * kAaTileY + ty - 1;
+// Forward pass. A block of 32 x 16 threads covers 30 x 14 output pixels plus a one-pixel halo all
+// round. Each thread follows its own pixel's triangle, loaded once, towards each neighbour that
+// shows another triangle (the source terms shared by the up to four directions) and leaves the
+// crossings in shared memory; each output pixel then decides its four pairs from both sides'
+// crossings, blends, writes only itself (no colour atomics, deterministic) and records its right
+// and lower pairs for the backward pass.
+constexpr int kFwdX = 32, kFwdY = 16;
+constexpr int kFwdTileX = kFwdX - 2, kFwdTileY = kFwdY - 2;
+enum AaDirection { kRight = 0, kLeft = 1, kDown = 2, kUp = 3 };
+
+struct PairOutcome {
+  bool active, use_p;
+  float t, bp, bq;
+  int edge;
+};
+
+// eval_pair's decision from the two sides' crossings: code bit 2 = found, bits 0-1 = edge.
+__device__ __forceinline__ PairOutcome decide_pair(int id_p, int id_q, float zp, float zq,
+                                                   unsigned cp, float tp, unsigned cq, float tq) {
+  PairOutcome r;
+  r.active = false;
+  r.use_p = false;
+  r.t = r.bp = r.bq = 0.0f;
+  r.edge = 0;
+  if (id_p == id_q) return r;
+  const bool fp = (cp & 4u) != 0u, fq = (cq & 4u) != 0u;
+  r.use_p = fp && (!fq || zp <= zq);
+  const bool use_q = fq && !r.use_p;
+  r.active = r.use_p || use_q;
+  if (!r.active) return r;
+  r.t = r.use_p ? tp : sub(1.0f, tq);
+  if (r.t < 0.5f) r.bp = sub(0.5f, r.t); else r.bq = sub(r.t, 0.5f);
+  r.edge = static_cast<int>((r.use_p ? cp : cq) & 3u);
+  return r;
+}
+
+__device__ __forceinline__ int owner_vertex(const AaCtx& a, int owner, int edge, int k) {
+  return __ldg(a.tri + 3 * static_cast<long long>(owner) + (edge + k) % 3);
+}
+
+__global__ void __launch_bounds__(kFwdX * kFwdY, 3) aa_fwd_kernel(const AaCtx a,
+                                                                   float* __restrict__ out,
+                                                                   PairRecords rec) {
+  __shared__ int s_id[kFwdY][kFwdX];
+  __shared__ float s_z[kFwdY][kFwdX];
+  __shared__ float s_t[4][kFwdY][kFwdX];
+  __shared__ unsigned char s_c[4][kFwdY][kFwdX];
+  __shared__ float s_cx[kFwdX], s_cy[kFwdY];
+  const int tx = threadIdx.x % kFwdX, ty = threadIdx.x / kFwdX;
+  const int col0 = blockIdx.x * kFwdTileX - 1, row0 = blockIdx.y * kFwdTileY - 1;
+  const int col = col0 + tx, row = row0 + ty;
   const long long b = blockIdx.z;
+  const long long pb = a.pos_batch == 1 ? 0 : b;
   const bool in_image = col >= 0 && col < a.width && row >= 0 && row < a.height;
-  float2 h = make_float2(0.f, 0.f), v = make_float2(0.f, 0.f), t = make_float2(0.f, 0.f);
-  int4 verts = make_int4(0, 0, 0, 0);
-  unsigned codes = 0u;
-  if (in_image && ty >= 1 && col + 1 < a.width) {
-    const Pair r = eval_pair(a, b, row, col, true);
-    h = make_float2(r.bp, r.bq);
-    if (r.active) {
-      t.x = r.t;
-      codes = pair_code(r);
-      verts.x = edge_vertex(a, r, 1);
-      verts.y = edge_vertex(a, r, 2);
-    }
-  }
-  if (in_image && tx >= 1 && row + 1 < a.height) {
-    const Pair r = eval_pair(a, b, row, col, false);
-    v = make_float2(r.bp, r.bq);
-    if (r.active) {
-      t.y = r.t;
-      codes |= pair_code(r) << 4;
-      verts.z = edge_vertex(a, r, 1);
-      verts.w = edge_vertex(a, r, 2);
-    }
-  }
-  hk[ty][tx] = h;
-  vk[ty][tx] = v;
-  __syncthreads();
-  if (!in_image || tx < 1 || ty < 1) return;
   const long long p = (b * a.height + row) * a.width + col;
+  int id = -3;
+  float z = 0.0f;
+  if (in_image) {
+    const float4 r = a.rast[p];
+    id = aa_triangle(r.w, a.num_tri);
+    z = r.z;
+  }
+  s_id[ty][tx] = id;
+  s_z[ty][tx] = z;
+  if (threadIdx.x < kFwdX) s_cx[threadIdx.x] = pixel_centre(col0 + threadIdx.x, a.width);
+  else if (threadIdx.x < kFwdX + kFwdY)
+    s_cy[threadIdx.x - kFwdX] = pixel_centre(row0 + threadIdx.x - kFwdX, a.height);
+  __syncthreads();
+  // Directions needed by the output pixels' pairs, towards a neighbour showing another triangle.
+  const bool out_row = ty >= 1 && ty <= kFwdY - 2, out_col = tx >= 1 && tx <= kFwdX - 2;
+  bool need[4];
+  need[kRight] = out_row && tx <= kFwdX - 2 && col + 1 < a.width && s_id[ty][tx + 1] != id;
+  need[kLeft] = out_row && tx >= 1 && col >= 1 && s_id[ty][tx - 1] != id;
+  need[kDown] = out_col && ty <= kFwdY - 2 && row + 1 < a.height && s_id[ty + 1][tx] != id;
+  need[kUp] = out_col && ty >= 1 && row >= 1 && s_id[ty - 1][tx] != id;
+  unsigned code[4] = {0u, 0u, 0u, 0u};
+  float tc[4] = {0.f, 0.f, 0.f, 0.f};
+  if (in_image && id >= 0 && (need[0] || need[1] || need[2] || need[3])) {
+    const Tri2 v = load_tri(a, pb, id);
+    const SrcTerms S = src_terms(v, s_cx[tx], s_cy[ty]);
+#pragma unroll
+    for (int d = 0; d < 4; ++d) {
+      if (!need[d]) continue;
+      const float dst = d == kRight ? s_cx[tx + 1]
+                        : d == kLeft ? s_cx[tx - 1]
+                        : d == kDown ? s_cy[ty + 1]
+                                     : s_cy[ty - 1];
+      const Crossing c = crossing_candidate(a, v, S, dst, d < 2);
+      if (c.found) {
+        code[d] = 4u | static_cast<unsigned>(c.edge);
+        tc[d] = c.t;
+      }
+    }
+    // Silhouette tests of the candidate edges, their loads issued together.
+    int opp[4];
+#pragma unroll
+    for (int d = 0; d < 4; ++d)
+      opp[d] = code[d] ? __ldg(a.opposite + 3 * static_cast<long long>(id) + (code[d] & 3u)) : -1;
+    float4 po[4];
+#pragma unroll
+    for (int d = 0; d < 4; ++d)
+      po[d] = opp[d] >= 0 ? __ldg(reinterpret_cast<const float4*>(a.pos) + pb * a.num_vert + opp[d])
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int d = 0; d < 4; ++d)
+      if (code[d] && opp[d] >= 0 && !silhouette_side(v, static_cast<int>(code[d] & 3u), po[d]))
+        code[d] = 0u;
+  }
+#pragma unroll
+  for (int d = 0; d < 4; ++d) {
+    s_c[d][ty][tx] = static_cast<unsigned char>(code[d]);
+    s_t[d][ty][tx] = tc[d];
+  }
+  __syncthreads();
+  if (!in_image || !out_row || !out_col) return;
+  const PairOutcome right =
+      col + 1 < a.width
+          ? decide_pair(id, s_id[ty][tx + 1], z, s_z[ty][tx + 1], code[kRight], tc[kRight],
+                        s_c[kLeft][ty][tx + 1], s_t[kLeft][ty][tx + 1])
+          : decide_pair(0, 0, 0.f, 0.f, 0u, 0.f, 0u, 0.f);
+  const PairOutcome left =
+      col >= 1 ? decide_pair(s_id[ty][tx - 1], id, s_z[ty][tx - 1], z, s_c[kRight][ty][tx - 1],
+                             s_t[kRight][ty][tx - 1], code[kLeft], tc[kLeft])
+               : decide_pair(0, 0, 0.f, 0.f, 0u, 0.f, 0u, 0.f);
+  const PairOutcome down =
+      row + 1 < a.height
+          ? decide_pair(id, s_id[ty + 1][tx], z, s_z[ty + 1][tx], code[kDown], tc[kDown],
+                        s_c[kUp][ty + 1][tx], s_t[kUp][ty + 1][tx])
+          : decide_pair(0, 0, 0.f, 0.f, 0u, 0.f, 0u, 0.f);
+  const PairOutcome up =
+      row >= 1 ? decide_pair(s_id[ty - 1][tx], id, s_z[ty - 1][tx], z, s_c[kDown][ty - 1][tx],
+                             s_t[kDown][ty - 1][tx], code[kUp], tc[kUp])
+               : decide_pair(0, 0, 0.f, 0.f, 0u, 0.f, 0u, 0.f);
   if (rec.code != nullptr) {
-    // Interior threads evaluated both pairs of their pixel.
-    rec.t[p] = t;
+    unsigned codes = 0u;
+    int4 verts = make_int4(0, 0, 0, 0);
+    if (right.active) {
+      codes = 8u | (right.use_p ? 4u : 0u) | static_cast<unsigned>(right.edge);
+      const int owner = right.use_p ? id : s_id[ty][tx + 1];
+      verts.x = owner_vertex(a, owner, right.edge, 1);
+      verts.y = owner_vertex(a, owner, right.edge, 2);
+    }
+    if (down.active) {
+      codes |= (8u | (down.use_p ? 4u : 0u) | static_cast<unsigned>(down.edge)) << 4;
+      const int owner = down.use_p ? id : s_id[ty + 1][tx];
+      verts.z = owner_vertex(a, owner, down.edge, 1);
+      verts.w = owner_vertex(a, owner, down.edge, 2);
+    }
+    rec.t[p] = make_float2(right.t, down.t);
     rec.code[p] = static_cast<uint8_t>(codes);
     // Edge vertices are read only for active pairs.
     if (codes & 0x88u) rec.verts[p] = verts;
   }
-  // Blend coefficients and partners, in the reference's accumulation order: right pair (this
-  // pixel first), left pair (second), lower pair (first), upper pair (second).
-  const float k[4] = {hk[ty][tx].x, hk[ty][tx - 1].y, vk[ty][tx].x, vk[ty - 1][tx].y};
+  // Blend in the reference's accumulation order: right pair (this pixel first), left pair
+  // (second), lower pair (first), upper pair (second).
+  const float k[4] = {right.bp, left.bq, down.bp, up.bq};
   const long long other[4] = {p + 1, p - 1, p + a.width, p - a.width};
   const int C = a.channels;
   for (int c = 0; c < C; ++c) {
@@ -640,8 +799,8 @@ extern "C" int dr_antialias_fwd(const float* color, const float* rast, const flo
   const AaCtx a = make_ctx(color, rast, pos, pos_batch, num_vert, tri, num_tri, opposite, height,
                            width, channels);
   if (batch > 65535) return DR_ERR_TOO_LARGE;
-  const dim3 grid((width + kAaTileX - 1) / kAaTileX, (height + kAaTileY - 1) / kAaTileY, batch);
-  aa_fwd_kernel<<<grid, 256, 0, as_stream(stream)>>>(a, out, pair_records(pairs, total));
+  const dim3 grid((width + kFwdTileX - 1) / kFwdTileX, (height + kFwdTileY - 1) / kFwdTileY, batch);
+  aa_fwd_kernel<<<grid, kFwdX * kFwdY, 0, as_stream(stream)>>>(a, out, pair_records(pairs, total));
   return launch_status();
 }
 
