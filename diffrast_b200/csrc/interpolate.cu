@@ -59,53 +59,71 @@ __device__ __forceinline__ void store_block(float* __restrict__ dst, const float
   }
 }
 
-// One thread per pixel. With `staged`, the block's outputs (out and out_da of its 256 pixels are
-// each one contiguous range) go through shared memory so that global stores are coalesced
-// float4s; otherwise each thread stores its own channels.
-__global__ void __launch_bounds__(256) interp_fwd_kernel(
+// Each block covers kInterpBlockPixels consecutive pixels with kInterpThreads threads, a thread
+// taking kInterpPix of them 128 apart, one load phase at a time (rast and rast_db, then the vertex
+// indices, then the attributes), so that the loads of all its pixels are in flight together. With
+// `staged`, the block's outputs (out and out_da of its pixels are each one contiguous range) go
+// through shared memory so that global stores are coalesced float4s; otherwise each thread
+// stores its own channels.
+constexpr int kInterpThreads = 128;
+constexpr int kInterpPix = 2;
+constexpr int kInterpBlockPixels = kInterpThreads * kInterpPix;
+
+__global__ void __launch_bounds__(kInterpThreads) interp_fwd_kernel(
     const float* __restrict__ attr, long long attr_batch, long long num_vert, int channels,
     const float4* __restrict__ rast, const float4* __restrict__ rast_db, const int* __restrict__ tri,
     int num_tri, const int* __restrict__ diff, int num_diff, long long total,
     long long pixels_per_image, float* __restrict__ out, float* __restrict__ out_da, bool staged) {
   extern __shared__ float stage[];
-  const long long first = blockIdx.x * static_cast<long long>(blockDim.x);
-  const long long p = first + threadIdx.x;
+  const long long first = blockIdx.x * static_cast<long long>(kInterpBlockPixels);
   const int nd = 2 * num_diff;
-  float* so = stage;                                 // [256][channels]
-  float* sd = stage + blockDim.x * channels;         // [256][2 * num_diff]
-  float* o = staged ? so + threadIdx.x * channels : out + p * channels;
-  float* od = staged ? sd + threadIdx.x * nd : out_da + p * nd;
-  if (p < total) {
-    const float4 r = rast[p];
-    const int t = rast_triangle(r.w, num_tri);
-    const Corners k = corners(tri, t, p, pixels_per_image, attr_batch, num_vert);
-    if (!k.covered) {
+  float* so = stage;                                  // [block pixels][channels]
+  float* sd = stage + kInterpBlockPixels * channels;  // [block pixels][2 * num_diff]
+  float4 r[kInterpPix], d[kInterpPix];
+#pragma unroll
+  for (int i = 0; i < kInterpPix; ++i) {
+    const long long p = first + i * kInterpThreads + threadIdx.x;
+    r[i] = p < total ? rast[p] : make_float4(0.f, 0.f, 0.f, 0.f);
+    d[i] = p < total && num_diff > 0 ? rast_db[p] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  Corners k[kInterpPix];
+#pragma unroll
+  for (int i = 0; i < kInterpPix; ++i) {
+    const long long p = first + i * kInterpThreads + threadIdx.x;
+    k[i] = corners(tri, p < total ? rast_triangle(r[i].w, num_tri) : -1, p, pixels_per_image,
+                   attr_batch, num_vert);
+  }
+#pragma unroll
+  for (int i = 0; i < kInterpPix; ++i) {
+    const int slot = i * kInterpThreads + threadIdx.x;
+    const long long p = first + slot;
+    if (p >= total) continue;
+    float* o = staged ? so + slot * channels : out + p * channels;
+    float* od = staged ? sd + slot * nd : out_da + p * nd;
+    if (!k[i].covered) {
       for (int c = 0; c < channels; ++c) o[c] = 0.0f;
       for (int c = 0; c < nd; ++c) od[c] = 0.0f;
-    } else {
-      const float u = r.x, v = r.y;
-      const float w2 = sub(sub(1.0f, u), v);
-      const float* a0 = attr + k.row0 * channels;
-      const float* a1 = attr + k.row1 * channels;
-      const float* a2 = attr + k.row2 * channels;
-      for (int c = 0; c < channels; ++c) {
-        o[c] = add(add(mul(u, __ldg(a0 + c)), mul(v, __ldg(a1 + c))), mul(w2, __ldg(a2 + c)));
-      }
-      if (num_diff > 0) {
-        const float4 d = rast_db[p];
-        for (int j = 0; j < num_diff; ++j) {
-          const int c = __ldg(diff + j);
-          const float x2 = __ldg(a2 + c);
-          const float du = sub(__ldg(a0 + c), x2), dv = sub(__ldg(a1 + c), x2);
-          od[2 * j] = add(mul(d.x, du), mul(d.z, dv));
-          od[2 * j + 1] = add(mul(d.y, du), mul(d.w, dv));
-        }
-      }
+      continue;
+    }
+    const float u = r[i].x, v = r[i].y;
+    const float w2 = sub(sub(1.0f, u), v);
+    const float* a0 = attr + k[i].row0 * channels;
+    const float* a1 = attr + k[i].row1 * channels;
+    const float* a2 = attr + k[i].row2 * channels;
+    for (int c = 0; c < channels; ++c) {
+      o[c] = add(add(mul(u, __ldg(a0 + c)), mul(v, __ldg(a1 + c))), mul(w2, __ldg(a2 + c)));
+    }
+    for (int j = 0; j < num_diff; ++j) {
+      const int c = __ldg(diff + j);
+      const float x2 = __ldg(a2 + c);
+      const float du = sub(__ldg(a0 + c), x2), dv = sub(__ldg(a1 + c), x2);
+      od[2 * j] = add(mul(d[i].x, du), mul(d[i].z, dv));
+      od[2 * j + 1] = add(mul(d[i].y, du), mul(d[i].w, dv));
     }
   }
   if (!staged) return;
   __syncthreads();
-  const int pixels = static_cast<int>(min(static_cast<long long>(blockDim.x), total - first));
+  const int pixels = static_cast<int>(min(static_cast<long long>(kInterpBlockPixels), total - first));
   store_block(out + first * channels, so, pixels * channels);
   if (nd > 0) store_block(out_da + first * nd, sd, pixels * nd);
 }
@@ -235,9 +253,11 @@ extern "C" int dr_interpolate_fwd(const float* attr, int64_t attr_batch, int64_t
     return DR_ERR_INVALID_ARGUMENT;
   const long long total = batch * static_cast<long long>(height) * width;
   if (total == 0) return DR_OK;
-  const size_t stage_bytes = sizeof(float) * 256 * (static_cast<size_t>(channels) + 2 * num_diff);
+  const size_t stage_bytes =
+      sizeof(float) * kInterpBlockPixels * (static_cast<size_t>(channels) + 2 * num_diff);
   const bool staged = stage_bytes <= 48 * 1024;
-  interp_fwd_kernel<<<blocks_for(total, 256), 256, staged ? stage_bytes : 0, as_stream(stream)>>>(
+  interp_fwd_kernel<<<blocks_for(total, kInterpBlockPixels), kInterpThreads,
+                      staged ? stage_bytes : 0, as_stream(stream)>>>(
       attr, attr_batch, num_vert, channels, reinterpret_cast<const float4*>(rast),
       reinterpret_cast<const float4*>(rast_db), tri, static_cast<int>(num_tri), diff, num_diff,
       total, static_cast<long long>(height) * width, out, out_da, staged);
