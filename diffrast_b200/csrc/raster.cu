@@ -773,13 +773,27 @@ __global__ void __launch_bounds__(256) resolve_bwd_kernel(
     }
   }
   const long long base = static_cast<long long>(q.b) * num_vert;
-  // Plain vector reductions: with triangles of about a pixel, lanes of a warp rarely share a
-  // vertex slot, so a warp-level match finds little to merge and costs more than it saves.
-  if (q.covered) {
-    red_add_v4(grad_pos + (base + q.i0) * 4, gv[0][0], gv[0][1], gv[0][2], gv[0][3]);
-    red_add_v4(grad_pos + (base + q.i1) * 4, gv[1][0], gv[1][1], gv[1][2], gv[1][3]);
-    red_add_v4(grad_pos + (base + q.i2) * 4, gv[2][0], gv[2][1], gv[2][2], gv[2][3]);
+  // A warp whose covered pixels all show one triangle (large triangles) sums its gradients first
+  // and adds them once; otherwise each lane adds its own with vector reductions (with triangles
+  // of about a pixel, lanes rarely share a vertex and a warp-level match costs more than it saves).
+  const unsigned act = __ballot_sync(0xffffffffu, q.covered);
+  if (act == 0u) return;
+  const int lead = __ffs(act) - 1;
+  const int t0 = __shfl_sync(0xffffffffu, q.t, lead);
+  if (__all_sync(0xffffffffu, !q.covered || q.t == t0)) {
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) gv[k][c] += __shfl_xor_sync(0xffffffffu, gv[k][c], o);
+    if (static_cast<int>(threadIdx.x & 31u) != lead) return;
+  } else if (!q.covered) {
+    return;
   }
+  red_add_v4(grad_pos + (base + q.i0) * 4, gv[0][0], gv[0][1], gv[0][2], gv[0][3]);
+  red_add_v4(grad_pos + (base + q.i1) * 4, gv[1][0], gv[1][1], gv[1][2], gv[1][3]);
+  red_add_v4(grad_pos + (base + q.i2) * 4, gv[2][0], gv[2][1], gv[2][2], gv[2][3]);
 }
 
 bool bad_raster_args(const float* pos, const int32_t* tri, int64_t batch, int64_t num_vert,

@@ -493,11 +493,21 @@ __global__ void __launch_bounds__(256) texture_fwd_kernel(
     const float* __restrict__ bias, const Strides st, long long total, long long pixels_per_image,
     float* __restrict__ out, bool staged) {
   extern __shared__ float stage[];
+  __shared__ long long block_view;
   const long long first = blockIdx.x * static_cast<long long>(blockDim.x);
   const long long p = first + threadIdx.x;
   float* o = staged ? stage + threadIdx.x * channels : out + p * channels;
+  // One 64-bit division per block: a block spans at most two views when an image has at least
+  // blockDim.x pixels.
+  if (threadIdx.x == 0) block_view = first / pixels_per_image;
+  __syncthreads();
   if (p < total) {
-    const long long view = p / pixels_per_image;
+    long long view = block_view;
+    if (pixels_per_image >= blockDim.x) {
+      if (p >= (view + 1) * pixels_per_image) ++view;
+    } else {
+      view = p / pixels_per_image;
+    }
     Lookup<MODE, B> k;
     prepare<MODE, B>(L, channels, uv, uv_da, bias, st, p, view, k);
     for (int c = 0; c < channels; ++c) {
