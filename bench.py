@@ -82,62 +82,98 @@ def step_bytes(pixels, num_vert, views, stack_bytes, tex_bytes) -> int:
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons every 200 ms while active."""
+    """Samples the GPU's SM clock and clock-event (throttle) reasons while active: through NVML
+    every 20 ms when the nvidia-ml-py binding loads (read-only queries), else with nvidia-smi every
+    200 ms. Nothing is ever set."""
 
+    # NVML clock-event reason bits (nvml.h): the ones a timing must report.
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: str) -> None:
-        self.gpu = gpu_index
+    def __init__(self, gpu_uuid: str) -> None:
+        self.gpu = gpu_uuid
         self.proc = None
-        self.lines: list[str] = []
+        self.samples: list[tuple[float, float | None, set]] = []
         self.thread = None
+        self.stop = threading.Event()
+        self.nvml = None
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
-            )  # fmt: skip
-            self.thread = threading.Thread(target=self._read, daemon=True)
+            import pynvml
+
+            pynvml.nvmlInit()
+            handle = pynvml.nvmlDeviceGetHandleByUUID(self.gpu.encode())
+            reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.nvml = (pynvml, handle, reasons)
+            self.thread = threading.Thread(target=self._poll_nvml, daemon=True)
+        except Exception:  # noqa: BLE001 - no binding or no NVML: fall back to nvidia-smi
+            self.nvml = None
+            try:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                     "--format=csv,noheader,nounits", "-lms", "200"],
+                    stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+                )  # fmt: skip
+                self.thread = threading.Thread(target=self._read_smi, daemon=True)
+            except OSError:
+                self.proc = None
+        if self.thread is not None:
             self.thread.start()
-        except OSError:
-            self.proc = None
         return self
 
-    def _read(self):
+    def _poll_nvml(self):
+        pynvml, handle, reasons = self.nvml
+        max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM))
+        while not self.stop.is_set():
+            try:
+                mhz = float(pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM))
+                bits = int(reasons(handle))
+            except Exception:  # noqa: BLE001
+                break
+            self.samples.append((mhz, max_mhz, {n for b, n in self.REASONS.items() if bits & b}))
+            self.stop.wait(0.02)
+
+    def _read_smi(self):
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            parts = [p.strip() for p in line.strip().split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                mhz, max_mhz = float(parts[1]), float(parts[2])
+            except ValueError:
+                continue
+            active = {n for n, flag in zip(names, parts[5:9]) if flag.lower() == "active"}
+            self.samples.append((mhz, max_mhz, active))
 
     def __exit__(self, *exc):
+        self.stop.set()
         if self.proc is not None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-            if self.thread is not None:
-                self.thread.join(timeout=2)
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+        if self.nvml is not None:
+            try:
+                self.nvml[0].nvmlShutdown()
+            except Exception:  # noqa: BLE001
+                pass
 
     def summary(self) -> dict:
-        mhz, max_mhz, reasons = [], None, set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                mhz.append(float(parts[1]))
-                max_mhz = float(parts[2])
-            except ValueError:
-                continue
-            for name, flag in zip(names, parts[5:9]):
-                if flag.lower() == "active":
-                    reasons.add(name)
+        mhz = [m for m, _, _ in self.samples]
+        max_mhz = next((x for _, x, _ in self.samples if x), None)
+        reasons = set().union(*(r for _, _, r in self.samples)) if self.samples else set()
         return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": max_mhz,
-                "reasons": sorted(reasons), "samples": len(mhz)}  # fmt: skip
+                "reasons": sorted(reasons), "samples": len(mhz),
+                "source": "nvml" if self.nvml is not None else "nvidia-smi"}  # fmt: skip
 
 
 def measured_traffic(stage: str, pixels: int) -> int | None:
@@ -184,7 +220,7 @@ def build_scene(views_total: int, res: int, subdiv: int, tex_size: int, rank: in
 def run_ours(args) -> None:
     import diffrast_b200 as dr
     from diffrast_b200 import _kernels as K
-    from diffrast_b200.distributed import sum_gradients
+    from diffrast_b200.distributed import OverlappedGradientSum
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -208,6 +244,9 @@ def run_ours(args) -> None:
     pos = pos_cpu.to(dev).requires_grad_(True)
     target = target_cpu.to(dev)
     topo = dr.antialias_construct_topology_hash(tri)
+    # The texture gradient's all-reduce starts as soon as the texture backward has produced it and
+    # overlaps the interpolation and rasterization backward passes (no-op on one GPU).
+    reducer = OverlappedGradientSum([tex])
 
     def step(pos_in, target_in):
         pos_in.grad = None
@@ -220,7 +259,7 @@ def run_ours(args) -> None:
         loss = torch.nn.functional.mse_loss(image, target_in, reduction="sum") / (
             args.views * res * res * TEX_CHANNELS)
         loss.backward()
-        sum_gradients([tex])
+        reducer.wait()
         return loss
 
     for _ in range(args.warmup):

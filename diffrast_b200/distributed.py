@@ -39,3 +39,58 @@ def sum_gradients(tensors: list[Tensor], group=None, bucket_bytes: int = 64 << 2
         step = max(1, bucket_bytes // flat.element_size())
         for start in range(0, flat.numel(), step):
             dist.all_reduce(flat[start : start + step], group=group)
+
+
+class OverlappedGradientSum:
+    """Sums the gradients of shared tensors across ranks while the backward pass runs.
+
+    A post-accumulate-grad hook on each tensor issues its bucketed all-reduces asynchronously as
+    soon as the tensor's gradient is complete (the texture's, say, before the interpolation and
+    rasterization backward passes run), so the transfers overlap the remaining kernels. Call
+    :meth:`wait` after ``backward()`` and before reading the gradients; it also reduces, with
+    zeros, the tensors that received no gradient, so that every rank issues the same
+    collectives. Every rank must run the same graph (the hooks then fire in the same order).
+    Without an initialised process group it does nothing.
+    """
+
+    def __init__(self, tensors: list[Tensor], group=None, bucket_bytes: int = 64 << 20) -> None:
+        self.tensors = list(tensors)
+        self.group = group
+        self.bucket_bytes = bucket_bytes
+        self._pending: list = []
+        self._done: set[int] = set()
+        self._hooks = [t.register_post_accumulate_grad_hook(self._reduce) for t in self.tensors]
+
+    def _active(self) -> bool:
+        return dist.is_available() and dist.is_initialized()
+
+    def _reduce(self, t: Tensor) -> None:
+        if not self._active() or id(t) in self._done:
+            return
+        self._done.add(id(t))
+        flat = t.grad.view(-1)
+        step = max(1, self.bucket_bytes // flat.element_size())
+        for start in range(0, flat.numel(), step):
+            self._pending.append(
+                dist.all_reduce(flat[start : start + step], group=self.group, async_op=True)
+            )
+
+    def wait(self) -> None:
+        """Completes the reductions of this backward pass (the current stream waits for them)."""
+        if not self._active():
+            return
+        for t in self.tensors:
+            if id(t) not in self._done:
+                if t.grad is None:
+                    t.grad = torch.zeros_like(t)
+                self._reduce(t)
+        for work in self._pending:
+            work.wait()
+        self._pending.clear()
+        self._done.clear()
+
+    def remove(self) -> None:
+        """Detaches the hooks."""
+        for h in self._hooks:
+            h.remove()
+        self._hooks.clear()

@@ -12,7 +12,7 @@ import torch.multiprocessing as mp
 
 import oracle
 import scenes
-from diffrast_b200.distributed import sum_gradients, view_shard
+from diffrast_b200.distributed import OverlappedGradientSum, sum_gradients, view_shard
 
 
 def test_view_shard_covers_every_view_once():
@@ -56,7 +56,19 @@ def _rank(rank: int, world: int, port: int, results) -> None:
         p = pos[shard].clone().requires_grad_(True)
         _loss(p, tri, tex, uv, target[shard]).backward()
         sum_gradients([tex])
-        results[rank] = (tex.grad.clone(), shard, p.grad.clone())
+        # The same sum with the all-reduce issued from the gradient hook during backward, twice
+        # (the reducer is reusable across steps), plus a tensor that gets no gradient.
+        tex2 = tex.detach().clone().requires_grad_(True)
+        unused = torch.ones(3, requires_grad=True)
+        reducer = OverlappedGradientSum([tex2, unused], bucket_bytes=256)
+        overlapped = []
+        for _ in range(2):
+            tex2.grad = None
+            _loss(pos[shard].clone(), tri, tex2, uv, target[shard]).backward()
+            reducer.wait()
+            overlapped.append(tex2.grad.clone())
+        reducer.remove()
+        results[rank] = (tex.grad.clone(), shard, p.grad.clone(), overlapped, unused.grad.clone())
     finally:
         dist.destroy_process_group()
 
@@ -76,6 +88,9 @@ def test_two_ranks_sum_to_the_full_batch_gradient():
     p = pos.clone().requires_grad_(True)
     _loss(p, tri, tex, uv, target).backward()
     for rank in range(2):
-        tex_grad, shard, pos_grad = results[rank]
+        tex_grad, shard, pos_grad, overlapped, unused_grad = results[rank]
         torch.testing.assert_close(tex_grad, tex.grad, atol=1e-5, rtol=1e-5)
         torch.testing.assert_close(pos_grad, p.grad[shard], atol=1e-5, rtol=1e-5)
+        for g in overlapped:
+            torch.testing.assert_close(g, tex.grad, atol=1e-5, rtol=1e-5)
+        assert torch.equal(unused_grad, torch.zeros(3))
