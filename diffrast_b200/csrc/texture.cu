@@ -284,11 +284,21 @@ __device__ __forceinline__ Footprint bilinear_footprint(const Levels& L, int l, 
     int c0, c1, r0, r1;
     bool okc0 = true, okc1 = true, okr0 = true, okr1 = true;
     if (B == DR_BOUNDARY_WRAP) {
-      c0 = col % w;
-      c0 += c0 < 0 ? w : 0;
+      // Positive remainders; a mask for power-of-two sizes (two's complement makes it exact for
+      // negative coordinates too).
+      if ((w & (w - 1)) == 0) {
+        c0 = col & (w - 1);
+      } else {
+        c0 = col % w;
+        c0 += c0 < 0 ? w : 0;
+      }
       c1 = c0 + 1 == w ? 0 : c0 + 1;
-      r0 = row % h;
-      r0 += r0 < 0 ? h : 0;
+      if ((h & (h - 1)) == 0) {
+        r0 = row & (h - 1);
+      } else {
+        r0 = row % h;
+        r0 += r0 < 0 ? h : 0;
+      }
       r1 = r0 + 1 == h ? 0 : r0 + 1;
     } else {
       if (B == DR_BOUNDARY_ZERO) {
@@ -839,7 +849,8 @@ __global__ void __launch_bounds__(256) mip_down_kernel(const float* __restrict__
 // weighted gradients of the coarse texels whose bins overlap it.
 __global__ void __launch_bounds__(256) mip_down_bwd_kernel(const float* __restrict__ grad_dst,
                                                            int h, int w, int channels,
-                                                           float* __restrict__ grad_src) {
+                                                           float* __restrict__ grad_src,
+                                                           bool aligned16) {
   const int oh = (h + 1) / 2, ow = (w + 1) / 2;
   const long long in_row = blockIdx.x;
   const long long img = in_row / h;
@@ -848,6 +859,22 @@ __global__ void __launch_bounds__(256) mip_down_bwd_kernel(const float* __restri
   float* fine = grad_src + in_row * w * channels;
   const int n = w * channels;
   const bool even = (h % 2 == 0) && (w % 2 == 0);
+  if (even && channels == 4 && aligned16) {
+    // Four-channel texels (the padded gradients of three-channel textures): one 16-byte load of
+    // the coarse texel and one 16-byte read-modify-write per fine texel.
+    const float4* c4 = reinterpret_cast<const float4*>(coarse) + static_cast<long long>(r / 2) * ow;
+    float4* f4 = reinterpret_cast<float4*>(fine);
+    for (int q = threadIdx.x; q < w; q += blockDim.x) {
+      const float4 g = __ldg(c4 + q / 2);
+      float4 v = f4[q];
+      v.x += 0.25f * g.x;
+      v.y += 0.25f * g.y;
+      v.z += 0.25f * g.z;
+      v.w += 0.25f * g.w;
+      f4[q] = v;
+    }
+    return;
+  }
   // Coarse bins overlapping fine texel i: j in [floor(i m / n), ceil((i + 1) m / n) - 1].
   const int j0 = static_cast<int>(static_cast<long long>(r) * oh / h);
   const int j1 = static_cast<int>((static_cast<long long>(r + 1) * oh + h - 1) / h) - 1;
@@ -1039,7 +1066,8 @@ extern "C" int dr_mip_downsample_bwd(const float* grad_dst, int64_t images, int3
   const long long rows = images * h;
   if (rows == 0) return DR_OK;
   if (rows >= (1LL << 31)) return DR_ERR_TOO_LARGE;
-  mip_down_bwd_kernel<<<static_cast<unsigned>(rows), 256, 0, as_stream(stream)>>>(grad_dst, h, w,
-                                                                                  channels, grad_src);
+  const bool aligned16 = ((reinterpret_cast<uintptr_t>(grad_dst) | reinterpret_cast<uintptr_t>(grad_src)) & 15u) == 0;
+  mip_down_bwd_kernel<<<static_cast<unsigned>(rows), 256, 0, as_stream(stream)>>>(
+      grad_dst, h, w, channels, grad_src, aligned16);
   return launch_status();
 }
