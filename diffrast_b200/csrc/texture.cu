@@ -586,13 +586,10 @@ __device__ __forceinline__ void write_record(float* __restrict__ out, long long 
     return;
   }
   float* rec = out + p * stride;
-  for (int i = 0; i < stride; ++i) {
-    float value = 0.0f;
+  for (int i = 0; i < first; ++i) rec[i] = 0.0f;
 #pragma unroll
-    for (int j = 0; j < N; ++j)
-      if (i == first + j) value = v[j];
-    rec[i] = value;
-  }
+  for (int j = 0; j < N; ++j) rec[first + j] = v[j];
+  for (int i = first + N; i < stride; ++i) rec[i] = 0.0f;
 }
 
 // Texel gradients: a warp covers 16 x 2 pixels of a 16 x 16 tile, whose taps mostly land on the
