@@ -82,9 +82,13 @@ class Interpolate(torch.autograd.Function):
     def forward(ctx, attr: Tensor, rast: Tensor, rast_db: Tensor | None, tri: Tensor,
                 diff: Tensor | None):
         attr3 = (attr if attr.ndim == 3 else attr[None]).contiguous()
-        out, out_da = K.interpolate_fwd(attr3, rast, rast_db, tri, diff)
+        channels = attr3.shape[2]
+        # Rows padded to 16 bytes for the forward kernel's vector loads.
+        attr_rows, _ = K.padded_rows(attr3)
+        out, out_da = K.interpolate_fwd(attr_rows, rast, rast_db, tri, diff, channels)
         ctx.save_for_backward(*(_saveable(t) for t in (attr3, rast, rast_db, tri, diff)))
         ctx.attr_shape = attr.shape
+        ctx.channels = channels
         ctx.has_da = diff is not None
         ctx.rast_db_given = rast_db is not None
         if diff is None:
@@ -96,7 +100,7 @@ class Interpolate(torch.autograd.Function):
     def backward(ctx, grad_out, grad_out_da):
         attr3, rast, rast_db, tri, diff = ctx.saved_tensors
         if grad_out is None:
-            grad_out = torch.zeros((*rast.shape[:3], attr3.shape[2]), device=rast.device)
+            grad_out = torch.zeros((*rast.shape[:3], ctx.channels), device=rast.device)
         use_da = ctx.has_da and grad_out_da is not None
         need_attr = ctx.needs_input_grad[0]
         grad_attr, grad_rast, grad_db = K.interpolate_bwd(

@@ -152,17 +152,30 @@ def diff_table(channels: tuple[int, ...], device: torch.device) -> Tensor | None
     return table
 
 
+def padded_rows(attr3: Tensor) -> tuple[Tensor, int]:
+    """``attr3`` with its vertex rows padded to a multiple of 4 floats when that lets the kernels
+    read them with 16-byte loads (at most 8 channels), and the row stride."""
+    channels = attr3.shape[2]
+    stride = (channels + 3) // 4 * 4
+    if stride == channels or channels > 8:
+        return attr3, channels
+    return torch.nn.functional.pad(attr3, (0, stride - channels)), stride
+
+
 @timed("interpolate_fwd")
 def interpolate_fwd(attr3: Tensor, rast: Tensor, rast_db: Tensor | None, tri: Tensor,
-                    diff: Tensor | None) -> tuple[Tensor, Tensor]:
+                    diff: Tensor | None, channels: int | None = None) -> tuple[Tensor, Tensor]:
+    """``attr3`` ``[attr_batch, V, S]``: rows of S floats whose first ``channels`` (default S) are
+    the attributes (S > channels for rows padded by :func:`padded_rows`)."""
     batch, height, width, _ = rast.shape
-    channels = attr3.shape[2]
+    attr_stride = attr3.shape[2]
+    channels = attr_stride if channels is None else channels
     num_diff = 0 if diff is None else diff.shape[0]
     out = torch.empty((batch, height, width, channels), dtype=torch.float32, device=rast.device)
     out_da = torch.empty((batch, height, width, 2 * num_diff), dtype=torch.float32, device=rast.device)
     N.check(
         N.lib().dr_interpolate_fwd(attr3.data_ptr(), attr3.shape[0], attr3.shape[1], channels,
-                                   rast.data_ptr(), N.ptr(rast_db), tri.data_ptr(), tri.shape[0],
+                                   attr_stride, rast.data_ptr(), N.ptr(rast_db), tri.data_ptr(), tri.shape[0],
                                    N.ptr(diff), num_diff, batch, height, width, out.data_ptr(),
                                    out_da.data_ptr(), N.stream(rast.device)),
         "dr_interpolate_fwd",
@@ -172,6 +185,7 @@ def interpolate_fwd(attr3: Tensor, rast: Tensor, rast_db: Tensor | None, tri: Te
 
 @timed("interpolate_bwd")
 def interpolate_bwd(attr3, rast, rast_db, tri, diff, grad_out, grad_out_da, need_attr):
+    """Gradients of attr (``attr3`` unpadded, ``[attr_batch, V, channels]``), rast and rast_db."""
     batch, height, width, _ = rast.shape
     channels = attr3.shape[2]
     num_diff = 0 if diff is None else diff.shape[0]

@@ -44,8 +44,8 @@ _SIGNATURES = {
     ),
     "dr_interpolate_fwd": (
         c_int,
-        [_P, c_int64, c_int64, c_int32, _P, _P, _P, c_int64, _P, c_int32, c_int64, c_int32,
-         c_int32, _P, _P, _P],
+        [_P, c_int64, c_int64, c_int32, c_int32, _P, _P, _P, c_int64, _P, c_int32, c_int64,
+         c_int32, c_int32, _P, _P, _P],
     ),
     "dr_interpolate_bwd": (
         c_int,

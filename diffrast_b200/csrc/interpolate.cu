@@ -44,6 +44,40 @@ __device__ __forceinline__ Corners corners(const int* __restrict__ tri, int t, l
   return k;
 }
 
+// Up to kRowCache channels of an attribute row held in registers: read once per pixel (with
+// 16-byte loads when rows are 16-byte aligned) and reused by the value and derivative outputs.
+constexpr int kRowCache = 8;
+
+struct AttrRow {
+  float v[kRowCache];
+};
+
+__device__ __forceinline__ AttrRow load_row(const float* __restrict__ attr, long long row,
+                                            int stride, int channels, bool vec4) {
+  AttrRow r;
+  const float* p = attr + row * stride;
+  if (vec4) {
+    const float4 lo = __ldg(reinterpret_cast<const float4*>(p));
+    const float4 hi = channels > 4 ? __ldg(reinterpret_cast<const float4*>(p) + 1)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    r.v[0] = lo.x; r.v[1] = lo.y; r.v[2] = lo.z; r.v[3] = lo.w;
+    r.v[4] = hi.x; r.v[5] = hi.y; r.v[6] = hi.z; r.v[7] = hi.w;
+  } else {
+#pragma unroll
+    for (int c = 0; c < kRowCache; ++c) r.v[c] = c < channels ? __ldg(p + c) : 0.0f;
+  }
+  return r;
+}
+
+// r.v[c] for a channel index known only at run time, without local memory.
+__device__ __forceinline__ float pick(const AttrRow& r, int c) {
+  float x = r.v[0];
+#pragma unroll
+  for (int i = 1; i < kRowCache; ++i)
+    if (c == i) x = r.v[i];
+  return x;
+}
+
 // Copies `count` floats of a block's pixel outputs from shared memory to `dst` (contiguous),
 // with 16-byte stores where the addresses allow it.
 __device__ __forceinline__ void store_block(float* __restrict__ dst, const float* __restrict__ src,
@@ -71,6 +105,7 @@ constexpr int kInterpBlockPixels = kInterpThreads * kInterpPix;
 
 __global__ void __launch_bounds__(kInterpThreads) interp_fwd_kernel(
     const float* __restrict__ attr, long long attr_batch, long long num_vert, int channels,
+    int attr_stride, bool vec4,
     const float4* __restrict__ rast, const float4* __restrict__ rast_db, const int* __restrict__ tri,
     int num_tri, const int* __restrict__ diff, int num_diff, long long total,
     long long pixels_per_image, float* __restrict__ out, float* __restrict__ out_da, bool staged) {
@@ -107,9 +142,25 @@ __global__ void __launch_bounds__(kInterpThreads) interp_fwd_kernel(
     }
     const float u = r[i].x, v = r[i].y;
     const float w2 = sub(sub(1.0f, u), v);
-    const float* a0 = attr + k[i].row0 * channels;
-    const float* a1 = attr + k[i].row1 * channels;
-    const float* a2 = attr + k[i].row2 * channels;
+    if (channels <= kRowCache) {
+      const AttrRow x0 = load_row(attr, k[i].row0, attr_stride, channels, vec4);
+      const AttrRow x1 = load_row(attr, k[i].row1, attr_stride, channels, vec4);
+      const AttrRow x2 = load_row(attr, k[i].row2, attr_stride, channels, vec4);
+#pragma unroll
+      for (int c = 0; c < kRowCache; ++c)
+        if (c < channels) o[c] = add(add(mul(u, x0.v[c]), mul(v, x1.v[c])), mul(w2, x2.v[c]));
+      for (int j = 0; j < num_diff; ++j) {
+        const int c = __ldg(diff + j);
+        const float b2 = pick(x2, c);
+        const float du = sub(pick(x0, c), b2), dv = sub(pick(x1, c), b2);
+        od[2 * j] = add(mul(d[i].x, du), mul(d[i].z, dv));
+        od[2 * j + 1] = add(mul(d[i].y, du), mul(d[i].w, dv));
+      }
+      continue;
+    }
+    const float* a0 = attr + k[i].row0 * attr_stride;
+    const float* a1 = attr + k[i].row1 * attr_stride;
+    const float* a2 = attr + k[i].row2 * attr_stride;
     for (int c = 0; c < channels; ++c) {
       o[c] = add(add(mul(u, __ldg(a0 + c)), mul(v, __ldg(a1 + c))), mul(w2, __ldg(a2 + c)));
     }
@@ -243,7 +294,8 @@ bool bad_interp_args(const float* attr, int64_t attr_batch, int64_t num_vert, in
 using namespace dr;
 
 extern "C" int dr_interpolate_fwd(const float* attr, int64_t attr_batch, int64_t num_vert,
-                                  int32_t channels, const float* rast, const float* rast_db,
+                                  int32_t channels, int32_t attr_stride, const float* rast,
+                                  const float* rast_db,
                                   const int32_t* tri, int64_t num_tri, const int32_t* diff,
                                   int32_t num_diff, int64_t batch, int32_t height, int32_t width,
                                   float* out, float* out_da, void* stream) {
@@ -251,14 +303,17 @@ extern "C" int dr_interpolate_fwd(const float* attr, int64_t attr_batch, int64_t
                       num_diff, batch, height, width) ||
       out == nullptr || (num_diff > 0 && out_da == nullptr))
     return DR_ERR_INVALID_ARGUMENT;
+  if (attr_stride == 0) attr_stride = channels;
+  if (attr_stride < channels) return DR_ERR_INVALID_ARGUMENT;
   const long long total = batch * static_cast<long long>(height) * width;
   if (total == 0) return DR_OK;
+  const bool vec4 = attr_stride % 4 == 0 && (reinterpret_cast<uintptr_t>(attr) & 15u) == 0;
   const size_t stage_bytes =
       sizeof(float) * kInterpBlockPixels * (static_cast<size_t>(channels) + 2 * num_diff);
   const bool staged = stage_bytes <= 48 * 1024;
   interp_fwd_kernel<<<blocks_for(total, kInterpBlockPixels), kInterpThreads,
                       staged ? stage_bytes : 0, as_stream(stream)>>>(
-      attr, attr_batch, num_vert, channels, reinterpret_cast<const float4*>(rast),
+      attr, attr_batch, num_vert, channels, attr_stride, vec4, reinterpret_cast<const float4*>(rast),
       reinterpret_cast<const float4*>(rast_db), tri, static_cast<int>(num_tri), diff, num_diff,
       total, static_cast<long long>(height) * width, out, out_da, staged);
   return launch_status();

@@ -104,12 +104,17 @@ int dr_raster_resolve_bwd(const float* pos, const int32_t* tri, const int64_t* k
 
 /* ---------------------------------------------------------------------------------------------
  * Interpolate (reference.py:117-146; _triton_interpolate.py:38-254).
- * attr [attr_batch, num_vert, channels] with attr_batch 1 (shared) or batch; rast, rast_db
- * [batch, h, w, 4]; diff: DEVICE int32 [num_diff] channel indices (NULL when num_diff is 0);
- * out [batch, h, w, channels]; out_da [batch, h, w, 2 * num_diff]. Ids past num_tri are empty.
+ * attr [attr_batch, num_vert, channels] with attr_batch 1 (shared) or batch, its vertex rows
+ * attr_stride floats apart (0 = channels; a multiple of 4 with a 16-byte aligned attr lets the
+ * kernels read rows of up to 8 channels with 16-byte loads, so callers may pad rows); rast,
+ * rast_db [batch, h, w, 4]; diff: DEVICE int32 [num_diff] channel indices in [0, channels) (NULL
+ * when num_diff is 0); out [batch, h, w, channels]; out_da [batch, h, w, 2 * num_diff].
+ * dr_interpolate_bwd reads attr and writes grad_attr with rows of `channels` floats. Ids past
+ * num_tri are empty.
  * ------------------------------------------------------------------------------------------- */
 int dr_interpolate_fwd(const float* attr, int64_t attr_batch, int64_t num_vert, int32_t channels,
-                       const float* rast, const float* rast_db, const int32_t* tri,
+                       int32_t attr_stride, const float* rast, const float* rast_db,
+                       const int32_t* tri,
                        int64_t num_tri, const int32_t* diff, int32_t num_diff, int64_t batch,
                        int32_t height, int32_t width, float* out, float* out_da, void* stream);
 

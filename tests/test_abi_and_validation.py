@@ -41,7 +41,7 @@ def test_invalid_arguments_are_rejected_without_a_gpu():
     lib = _native.lib()
     # Negative sizes and null pointers fail validation before any CUDA call.
     assert lib.dr_raster_setup(None, None, -1, 0, 0, 4, 4, None, None, None, 0, 0, None) == 10001
-    assert lib.dr_interpolate_fwd(None, 0, 0, 1, None, None, None, 0, None, 0, 1, 1, 1, None, None, None) == 10001
+    assert lib.dr_interpolate_fwd(None, 0, 0, 1, 0, None, None, None, 0, None, 0, 1, 1, 1, None, None, None) == 10001
     assert lib.dr_edge_neighbours(None, -5, None, None, 0, None) == 10001
     assert lib.dr_raster_setup_workspace_bytes(1000, 64, 64) >= 20000
     assert lib.dr_edge_neighbours_workspace_bytes(100) > 0
