@@ -65,8 +65,11 @@ struct BinLayout {
   unsigned* tile_offset;  // [tiles + 1]
   unsigned* item_offset;  // [tiles + 1]
   unsigned* work;         // [1]
+  unsigned* scan_totals;  // [2 (scan chunks + 1)]
   int* pairs;             // [num_pairs]
 };
+
+long long scan_chunks(int64_t tiles) { return (tiles + 4095) / 4096; }
 
 BinLayout bin_layout(void* ws, int64_t tiles, int64_t num_pairs) {
   char* p = static_cast<char*>(ws);
@@ -82,6 +85,8 @@ BinLayout bin_layout(void* ws, int64_t tiles, int64_t num_pairs) {
   p += t;
   l.work = reinterpret_cast<unsigned*>(p);
   p += 256;
+  l.scan_totals = reinterpret_cast<unsigned*>(p);
+  p += align256(sizeof(unsigned) * 2 * static_cast<size_t>(scan_chunks(tiles) + 1));
   l.pairs = reinterpret_cast<int*>(p);
   (void)num_pairs;
   return l;
@@ -89,6 +94,7 @@ BinLayout bin_layout(void* ws, int64_t tiles, int64_t num_pairs) {
 
 size_t bin_bytes(int64_t tiles, int64_t num_pairs) {
   return 4 * align256(sizeof(unsigned) * static_cast<size_t>(tiles + 1)) + 256 +
+         align256(sizeof(unsigned) * 2 * static_cast<size_t>(scan_chunks(tiles) + 1)) +
          align256(sizeof(int) * static_cast<size_t>(num_pairs));
 }
 
@@ -401,77 +407,129 @@ __global__ void __launch_bounds__(256) bin_kernel(const Binned* __restrict__ bin
   }
 }
 
-// Exclusive scans of the per-tile pair counts and of their 256-triangle work items, in one block.
-__global__ void __launch_bounds__(1024) scan_kernel(const unsigned* __restrict__ count, int n,
-                                                    unsigned* __restrict__ offset,
-                                                    unsigned* __restrict__ item_offset) {
+// Exclusive scans of the per-tile pair counts and of their 256-triangle work items, in three
+// passes over chunks of kScanChunk tiles: chunk totals (scan_totals_kernel), an exclusive scan of
+// the totals in one block (scan_chunks_kernel), and each chunk's scan from its carry
+// (scan_kernel).
+constexpr int kScanPer = 4;
+constexpr int kScanChunk = 1024 * kScanPer;
+
+__device__ __forceinline__ unsigned work_items(unsigned pairs) { return (pairs + kChunk - 1) / kChunk; }
+
+// Block-wide inclusive scan of (xa, xb) over 1024 threads; returns the block totals too.
+__device__ __forceinline__ void block_scan2(unsigned& xa, unsigned& xb, unsigned& total_a,
+                                            unsigned& total_b) {
   __shared__ unsigned warp_a[32], warp_b[32];
-  __shared__ unsigned carry_a, carry_b;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) carry_a = carry_b = 0;
-  __syncthreads();
-  constexpr int kPer = 4;
-  for (int base = 0; base < n; base += 1024 * kPer) {
-    unsigned a[kPer], b[kPer], sa = 0, sb = 0;
 #pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      const int i = base + tid * kPer + j;
-      const unsigned c = i < n ? count[i] : 0u;
-      a[j] = sa;
-      b[j] = sb;
-      sa += c;
-      sb += (c + kChunk - 1) / kChunk;
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned ya = __shfl_up_sync(0xffffffffu, xa, o);
+    const unsigned yb = __shfl_up_sync(0xffffffffu, xb, o);
+    if (lane >= o) {
+      xa += ya;
+      xb += yb;
     }
-    unsigned xa = sa, xb = sb;
+  }
+  if (lane == 31) {
+    warp_a[warp] = xa;
+    warp_b[warp] = xb;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    unsigned wa = warp_a[lane], wb = warp_b[lane];
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const unsigned ya = __shfl_up_sync(0xffffffffu, xa, o);
-      const unsigned yb = __shfl_up_sync(0xffffffffu, xb, o);
+      const unsigned ya = __shfl_up_sync(0xffffffffu, wa, o);
+      const unsigned yb = __shfl_up_sync(0xffffffffu, wb, o);
       if (lane >= o) {
-        xa += ya;
-        xb += yb;
+        wa += ya;
+        wb += yb;
       }
     }
-    if (lane == 31) {
-      warp_a[warp] = xa;
-      warp_b[warp] = xb;
-    }
-    __syncthreads();
-    if (warp == 0) {
-      unsigned wa = warp_a[lane], wb = warp_b[lane];
+    warp_a[lane] = wa;
+    warp_b[lane] = wb;
+  }
+  __syncthreads();
+  if (warp > 0) {
+    xa += warp_a[warp - 1];
+    xb += warp_b[warp - 1];
+  }
+  total_a = warp_a[31];
+  total_b = warp_b[31];
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(1024) scan_totals_kernel(const unsigned* __restrict__ count, int n,
+                                                           unsigned* __restrict__ totals) {
+  unsigned sa = 0, sb = 0;
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const unsigned ya = __shfl_up_sync(0xffffffffu, wa, o);
-        const unsigned yb = __shfl_up_sync(0xffffffffu, wb, o);
-        if (lane >= o) {
-          wa += ya;
-          wb += yb;
-        }
-      }
-      warp_a[lane] = wa;
-      warp_b[lane] = wb;
+  for (int j = 0; j < kScanPer; ++j) {
+    const long long i = static_cast<long long>(blockIdx.x) * kScanChunk + threadIdx.x * kScanPer + j;
+    const unsigned c = i < n ? count[i] : 0u;
+    sa += c;
+    sb += work_items(c);
+  }
+  unsigned ta, tb;
+  block_scan2(sa, sb, ta, tb);
+  if (threadIdx.x == 0) {
+    totals[2 * blockIdx.x] = ta;
+    totals[2 * blockIdx.x + 1] = tb;
+  }
+}
+
+// Exclusive scan of the chunk totals in place; the grand totals go to totals[2 chunks, + 1].
+__global__ void __launch_bounds__(1024) scan_chunks_kernel(unsigned* __restrict__ totals,
+                                                           int chunks) {
+  unsigned carry_a = 0, carry_b = 0;
+  for (int base = 0; base < chunks; base += 1024) {
+    const int i = base + static_cast<int>(threadIdx.x);
+    const unsigned ca = i < chunks ? totals[2 * i] : 0u, cb = i < chunks ? totals[2 * i + 1] : 0u;
+    unsigned xa = ca, xb = cb, ta, tb;
+    block_scan2(xa, xb, ta, tb);
+    if (i < chunks) {
+      totals[2 * i] = carry_a + xa - ca;
+      totals[2 * i + 1] = carry_b + xb - cb;
     }
-    __syncthreads();
-    const unsigned pre_a = carry_a + (warp ? warp_a[warp - 1] : 0u) + xa - sa;
-    const unsigned pre_b = carry_b + (warp ? warp_b[warp - 1] : 0u) + xb - sb;
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      const int i = base + tid * kPer + j;
-      if (i < n) {
-        offset[i] = pre_a + a[j];
-        item_offset[i] = pre_b + b[j];
-      }
-    }
-    __syncthreads();
-    if (tid == 0) {
-      carry_a += warp_a[31];
-      carry_b += warp_b[31];
-    }
+    carry_a += ta;
+    carry_b += tb;
     __syncthreads();
   }
-  if (tid == 0) {
-    offset[n] = carry_a;
-    item_offset[n] = carry_b;
+  if (threadIdx.x == 0) {
+    totals[2 * chunks] = carry_a;
+    totals[2 * chunks + 1] = carry_b;
+  }
+}
+
+__global__ void __launch_bounds__(1024) scan_kernel(const unsigned* __restrict__ count, int n,
+                                                    const unsigned* __restrict__ totals, int chunks,
+                                                    unsigned* __restrict__ offset,
+                                                    unsigned* __restrict__ item_offset) {
+  const long long base = static_cast<long long>(blockIdx.x) * kScanChunk + threadIdx.x * kScanPer;
+  unsigned a[kScanPer], b[kScanPer], sa = 0, sb = 0;
+#pragma unroll
+  for (int j = 0; j < kScanPer; ++j) {
+    const long long i = base + j;
+    const unsigned c = i < n ? count[i] : 0u;
+    a[j] = sa;
+    b[j] = sb;
+    sa += c;
+    sb += work_items(c);
+  }
+  unsigned xa = sa, xb = sb, ta, tb;
+  block_scan2(xa, xb, ta, tb);
+  const unsigned pre_a = totals[2 * blockIdx.x] + xa - sa;
+  const unsigned pre_b = totals[2 * blockIdx.x + 1] + xb - sb;
+#pragma unroll
+  for (int j = 0; j < kScanPer; ++j) {
+    const long long i = base + j;
+    if (i < n) {
+      offset[i] = pre_a + a[j];
+      item_offset[i] = pre_b + b[j];
+    }
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    offset[n] = totals[2 * chunks];
+    item_offset[n] = totals[2 * chunks + 1];
   }
 }
 
@@ -892,8 +950,12 @@ extern "C" int dr_raster_tiles(const float* pos, const int32_t* tri, int64_t bat
   bin_kernel<false><<<bin_blocks, 256, 0, s>>>(sl.binned, num_binned,
                                                static_cast<int>(num_tri), tiles_x,
                                                tiles_per_image, bl.tile_count, nullptr, nullptr);
-  scan_kernel<<<1, 1024, 0, s>>>(bl.tile_count, static_cast<int>(tiles), bl.tile_offset,
-                                 bl.item_offset);
+  const int chunks = static_cast<int>(scan_chunks(tiles));
+  scan_totals_kernel<<<chunks, 1024, 0, s>>>(bl.tile_count, static_cast<int>(tiles),
+                                             bl.scan_totals);
+  scan_chunks_kernel<<<1, 1024, 0, s>>>(bl.scan_totals, chunks);
+  scan_kernel<<<chunks, 1024, 0, s>>>(bl.tile_count, static_cast<int>(tiles), bl.scan_totals,
+                                      chunks, bl.tile_offset, bl.item_offset);
   bin_kernel<true><<<bin_blocks, 256, 0, s>>>(sl.binned, num_binned,
                                               static_cast<int>(num_tri), tiles_x,
                                               tiles_per_image, bl.tile_cursor, bl.tile_offset,
