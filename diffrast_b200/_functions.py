@@ -58,6 +58,8 @@ class Rasterize(torch.autograd.Function):
                 prev_keys: Tensor | None):
         keys = K.raster_keys(pos, tri, height, width, prev_keys)
         rast, rast_db = K.resolve_fwd(pos, tri, keys)
+        # Unused outputs (keys always, rast_db often) get no zero-filled gradient.
+        ctx.set_materialize_grads(False)
         ctx.save_for_backward(_saveable(pos), _saveable(tri), keys)
         ctx.grad_db = grad_db
         ctx.mark_non_differentiable(keys)
@@ -86,6 +88,7 @@ class Interpolate(torch.autograd.Function):
         # Rows padded to 16 bytes for the forward kernel's vector loads.
         attr_rows, _ = K.padded_rows(attr3)
         out, out_da = K.interpolate_fwd(attr_rows, rast, rast_db, tri, diff, channels)
+        ctx.set_materialize_grads(False)
         ctx.save_for_backward(*(_saveable(t) for t in (attr3, rast, rast_db, tri, diff)))
         ctx.attr_shape = attr.shape
         ctx.channels = channels
@@ -107,8 +110,6 @@ class Interpolate(torch.autograd.Function):
             attr3, rast, rast_db, tri, diff if use_da else None, grad_out.contiguous(),
             grad_out_da.contiguous() if use_da else None, need_attr,
         )
-        if ctx.rast_db_given and grad_db is None:
-            grad_db = torch.zeros_like(rast)
         if not ctx.rast_db_given:
             grad_db = None
         if grad_attr is not None:
