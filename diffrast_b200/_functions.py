@@ -237,8 +237,14 @@ class TextureChain(torch.autograd.Function):
         g_da = g_da_src if da_spec is not None else g_da
         grad_tex = None
         if need[6]:
+            padded = grads[0].shape[-1] != tex.shape[-1]
             for level in range(len(grads) - 2, -1, -1):
-                K.mip_down_bwd(grads[level + 1], grads[level])
+                # The last step writes the base gradient without the padding channel.
+                last = level == 0 and padded
+                out = torch.empty(tex.shape, dtype=torch.float32, device=tex.device) if last else None
+                K.mip_down_bwd(grads[level + 1], grads[level], out)
+                if last:
+                    grads[0] = out
             grad_tex = grads[0]
             if grad_tex.shape[-1] != tex.shape[-1]:
                 grad_tex = grad_tex[..., : tex.shape[-1]].contiguous()

@@ -311,11 +311,14 @@ def mip_down(level: Tensor) -> Tensor:
 
 
 @timed("mip_adjoint")
-def mip_down_bwd(grad_coarse: Tensor, grad_fine: Tensor) -> None:
-    """Adds the adjoint of one mip step of ``grad_coarse`` into ``grad_fine`` (in place)."""
+def mip_down_bwd(grad_coarse: Tensor, grad_fine: Tensor, out: Tensor | None = None) -> None:
+    """Adds the adjoint of one mip step of ``grad_coarse`` into ``grad_fine`` (in place), or,
+    given ``out`` (fewer channels, e.g. without the padding), writes the sum there instead."""
     h, w, c = grad_fine.shape[-3], grad_fine.shape[-2], grad_fine.shape[-1]
     N.check(N.lib().dr_mip_downsample_bwd(grad_coarse.data_ptr(), _images(grad_fine), h, w, c,
-                                          grad_fine.data_ptr(), N.stream(grad_fine.device)),
+                                          grad_fine.data_ptr(), N.ptr(out),
+                                          0 if out is None else out.shape[-1],
+                                          N.stream(grad_fine.device)),
             "dr_mip_downsample_bwd")  # fmt: skip
 
 

@@ -847,13 +847,16 @@ __global__ void __launch_bounds__(256) mip_down_kernel(const float* __restrict__
 __global__ void __launch_bounds__(256) mip_down_bwd_kernel(const float* __restrict__ grad_dst,
                                                            int h, int w, int channels,
                                                            float* __restrict__ grad_src,
-                                                           bool aligned16) {
+                                                           bool aligned16, float* __restrict__ out,
+                                                           int out_channels) {
   const int oh = (h + 1) / 2, ow = (w + 1) / 2;
   const long long in_row = blockIdx.x;
   const long long img = in_row / h;
   const int r = static_cast<int>(in_row - img * h);
   const float* coarse = grad_dst + img * oh * static_cast<long long>(ow) * channels;
   float* fine = grad_src + in_row * w * channels;
+  // With `out`, the sum goes to its first out_channels channels instead of back into grad_src.
+  float* out_row = out == nullptr ? nullptr : out + in_row * w * out_channels;
   const int n = w * channels;
   const bool even = (h % 2 == 0) && (w % 2 == 0);
   if (even && channels == 4 && aligned16) {
@@ -868,7 +871,12 @@ __global__ void __launch_bounds__(256) mip_down_bwd_kernel(const float* __restri
       v.y += 0.25f * g.y;
       v.z += 0.25f * g.z;
       v.w += 0.25f * g.w;
-      f4[q] = v;
+      if (out_row == nullptr) {
+        f4[q] = v;
+      } else {
+        const float vv[4] = {v.x, v.y, v.z, v.w};
+        for (int c = 0; c < out_channels; ++c) out_row[q * out_channels + c] = vv[c];
+      }
     }
     return;
   }
@@ -878,7 +886,9 @@ __global__ void __launch_bounds__(256) mip_down_bwd_kernel(const float* __restri
   for (int e = threadIdx.x; e < n; e += blockDim.x) {
     const int q = e / channels, c = e - q * channels;
     if (even) {
-      fine[e] += 0.25f * __ldg(coarse + (static_cast<long long>(r / 2) * ow + q / 2) * channels + c);
+      const float v = fine[e] + 0.25f * __ldg(coarse + (static_cast<long long>(r / 2) * ow + q / 2) * channels + c);
+      if (out_row == nullptr) fine[e] = v;
+      else if (c < out_channels) out_row[q * out_channels + c] = v;
       continue;
     }
     const int k0 = static_cast<int>(static_cast<long long>(q) * ow / w);
@@ -893,7 +903,8 @@ __global__ void __launch_bounds__(256) mip_down_bwd_kernel(const float* __restri
       }
       acc += wr * row;
     }
-    fine[e] += acc;
+    if (out_row == nullptr) fine[e] += acc;
+    else if (c < out_channels) out_row[q * out_channels + c] = fine[e] + acc;
   }
 }
 
@@ -1057,14 +1068,16 @@ extern "C" int dr_mip_downsample(const float* src, int64_t images, int32_t h, in
 }
 
 extern "C" int dr_mip_downsample_bwd(const float* grad_dst, int64_t images, int32_t h, int32_t w,
-                                     int32_t channels, float* grad_src, void* stream) {
+                                     int32_t channels, float* grad_src, float* out,
+                                     int32_t out_channels, void* stream) {
   if (images < 0 || h < 1 || w < 1 || channels < 1 || grad_dst == nullptr || grad_src == nullptr)
     return DR_ERR_INVALID_ARGUMENT;
+  if (out != nullptr && (out_channels < 1 || out_channels > channels)) return DR_ERR_INVALID_ARGUMENT;
   const long long rows = images * h;
   if (rows == 0) return DR_OK;
   if (rows >= (1LL << 31)) return DR_ERR_TOO_LARGE;
   const bool aligned16 = ((reinterpret_cast<uintptr_t>(grad_dst) | reinterpret_cast<uintptr_t>(grad_src)) & 15u) == 0;
   mip_down_bwd_kernel<<<static_cast<unsigned>(rows), 256, 0, as_stream(stream)>>>(
-      grad_dst, h, w, channels, grad_src, aligned16);
+      grad_dst, h, w, channels, grad_src, aligned16, out, out_channels);
   return launch_status();
 }

@@ -168,9 +168,13 @@ int dr_texture_bwd(const float* const* level_ptr, float* const* grad_level_ptr,
 int dr_mip_downsample(const float* src, int64_t images, int32_t h, int32_t w, int32_t channels,
                       float* dst, void* stream);
 
-/* Adjoint of dr_mip_downsample: ACCUMULATES the gradient of dst into grad_src. */
+/* Adjoint of dr_mip_downsample: ACCUMULATES the gradient of dst into grad_src; or, with out
+ * non-NULL, writes grad_src + that adjoint to out [images, h, w, out_channels] (the first
+ * out_channels <= channels channels, dropping the padding of 4-channel gradients) and leaves
+ * grad_src unchanged. */
 int dr_mip_downsample_bwd(const float* grad_dst, int64_t images, int32_t h, int32_t w,
-                          int32_t channels, float* grad_src, void* stream);
+                          int32_t channels, float* grad_src, float* out, int32_t out_channels,
+                          void* stream);
 
 /* ---------------------------------------------------------------------------------------------
  * Antialias (reference.py:202-265, :675-814; topology.py; _triton_antialias.py).
