@@ -842,6 +842,25 @@ __global__ void __launch_bounds__(256) mip_down_kernel(const float* __restrict__
   }
 }
 
+// Even sizes with at most 4 channels: one thread per coarse texel (grid: coarse columns in x,
+// coarse rows in y, images in z), the pair sums in the order of mip_down_kernel, so the values
+// are the same.
+template <int C>
+__global__ void __launch_bounds__(256) mip_down_even_kernel(const float* __restrict__ src, int h,
+                                                            int w, float* __restrict__ dst) {
+  const int ow = w / 2, oh = h / 2;
+  const int k = blockIdx.x * blockDim.x + threadIdx.x;
+  const int j = blockIdx.y;
+  if (k >= ow) return;
+  const long long img = blockIdx.z;
+  const float* a = src + ((img * h + 2 * j) * w + 2 * k) * C;
+  const float* b = a + static_cast<long long>(w) * C;
+  float* out = dst + ((img * oh + j) * ow + k) * C;
+#pragma unroll
+  for (int c = 0; c < C; ++c)
+    out[c] = 0.25f * ((__ldg(a + c) + __ldg(a + C + c)) + (__ldg(b + c) + __ldg(b + C + c)));
+}
+
 // Adjoint of mip_down_kernel in gather form: one block per fine row; each fine element adds the
 // weighted gradients of the coarse texels whose bins overlap it.
 __global__ void __launch_bounds__(256) mip_down_bwd_kernel(const float* __restrict__ grad_dst,
@@ -1062,8 +1081,18 @@ extern "C" int dr_mip_downsample(const float* src, int64_t images, int32_t h, in
   const long long rows = images * ((h + 1) / 2);
   if (rows == 0) return DR_OK;
   if (rows >= (1LL << 31)) return DR_ERR_TOO_LARGE;
-  mip_down_kernel<<<static_cast<unsigned>(rows), 256, 0, as_stream(stream)>>>(src, h, w, channels,
-                                                                               dst);
+  cudaStream_t s = as_stream(stream);
+  if (h % 2 == 0 && w % 2 == 0 && channels <= 4 && h / 2 <= 65535 && images <= 65535) {
+    const dim3 grid((w / 2 + 255) / 256, h / 2, static_cast<unsigned>(images));
+    switch (channels) {
+      case 1: mip_down_even_kernel<1><<<grid, 256, 0, s>>>(src, h, w, dst); break;
+      case 2: mip_down_even_kernel<2><<<grid, 256, 0, s>>>(src, h, w, dst); break;
+      case 3: mip_down_even_kernel<3><<<grid, 256, 0, s>>>(src, h, w, dst); break;
+      default: mip_down_even_kernel<4><<<grid, 256, 0, s>>>(src, h, w, dst); break;
+    }
+    return launch_status();
+  }
+  mip_down_kernel<<<static_cast<unsigned>(rows), 256, 0, s>>>(src, h, w, channels, dst);
   return launch_status();
 }
 
