@@ -206,3 +206,67 @@ def config5_scene(views=64, resolution=1024, subdivisions=8, tex_size=4096, seed
     attr = torch.cat([spherical_uv(verts), normals], -1).contiguous()
     tex = torch.rand(1, tex_size, tex_size, 3, generator=gen)
     return dict(pos=pos, tri=tri, attr=attr, tex=tex, resolution=(resolution, resolution), gen=gen)
+
+
+# Reduced versions of BASELINE configs 2-5 for parity tests against the CPU oracle: the same
+# generators and parameters, fewer views, triangles and pixels, so that the oracle's brute-force
+# visibility finishes in seconds.
+
+
+def config2_small(views=2, resolution=64, segments=96, sides=12, seed=2):
+    """Config 2 shape: (2, 3) torus knot with N(0, 0.01) jitter, orbit cameras at distance 4,
+    fov 40 degrees; rasterize only, with N(0, 1) upstream gradients on rast and rast_db."""
+    gen = torch.Generator().manual_seed(seed)
+    verts, tri = torus_knot(2, 3, segments, sides)
+    verts = verts + 0.01 * torch.randn(verts.shape, generator=gen)
+    mvp = perspective(40.0) @ look_at(orbit_cameras(views, 4.0, gen))
+    pos = to_clip(verts, mvp)
+    g_rast = torch.randn(views, resolution, resolution, 4, generator=gen)
+    g_db = torch.randn(views, resolution, resolution, 4, generator=gen)
+    return dict(pos=pos, tri=tri, resolution=(resolution, resolution), g_rast=g_rast, g_db=g_db)
+
+
+def config3_small(views=2, resolution=64, subdivisions=3, tex_size=64, seed=3):
+    """Config 3 shape: icosphere with N(0, 0.02) radial displacement, random orbit cameras,
+    attr = [u, v, 8 channels N(0, 1)] with all channels differentiated, a 4-channel texture
+    sampled trilinearly through a texture_construct_mip stack."""
+    gen = torch.Generator().manual_seed(seed)
+    verts, tri = icosphere(subdivisions)
+    world = verts * (1 + 0.02 * torch.randn(verts.shape[0], 1, generator=gen))
+    mvp = perspective(45.0) @ look_at(orbit_cameras(views, 3.0, gen))
+    pos = to_clip(world, mvp)
+    attr = torch.cat([spherical_uv(verts), torch.randn(verts.shape[0], 8, generator=gen)], -1)
+    tex = torch.rand(1, tex_size, tex_size, 4, generator=gen)
+    target = torch.rand(views, resolution, resolution, 4, generator=gen)
+    return dict(pos=pos, tri=tri, attr=attr.contiguous(), tex=tex, target=target,
+                resolution=(resolution, resolution))
+
+
+def config4_small(views=2, resolution=48, segments=64, sides=10, cube_size=16, layers=4, seed=4):
+    """Config 4 shape: (3, 4) torus knot, a [1, 6, s, s, 3] cube map looked up with interpolated
+    normals (directions) and their screen derivatives, antialiasing, and depth peeling."""
+    gen = torch.Generator().manual_seed(seed)
+    verts, tri = torus_knot(3, 4, segments, sides)
+    mvp = perspective(45.0) @ look_at(orbit_cameras(views, 3.5, gen))
+    pos = to_clip(verts, mvp)
+    normals = F.normalize(verts - verts.mean(0, keepdim=True), dim=-1)
+    cube = torch.rand(1, 6, cube_size, cube_size, 3, generator=gen)
+    target = torch.rand(views, resolution, resolution, 3, generator=gen)
+    return dict(pos=pos, tri=tri, normals=normals.contiguous(), cube=cube, target=target,
+                resolution=(resolution, resolution), layers=layers)
+
+
+def config5_small(views=2, resolution=64, subdivisions=4, noise=0.15, tex_size=64, seed=5):
+    """Config 5 character at small size: an icosphere whose radial N(0, noise) displacement is
+    about twice its edge length (as N(0, 0.01) is for icosphere-8), so that triangles are spiky
+    and overlap several deep, with attr [u, v, normal], a trilinear texture and antialiasing."""
+    gen = torch.Generator().manual_seed(seed)
+    verts, tri = icosphere(subdivisions)
+    world = verts * (1 + noise * torch.randn(verts.shape[0], 1, generator=gen))
+    mvp = perspective(45.0) @ look_at(orbit_cameras(views, 3.0, gen))
+    pos = to_clip(world, mvp)
+    attr = torch.cat([spherical_uv(verts), verts], -1).contiguous()
+    tex = torch.rand(1, tex_size, tex_size, 3, generator=gen)
+    target = torch.rand(views, resolution, resolution, 3, generator=gen)
+    return dict(pos=pos, tri=tri, attr=attr, tex=tex, target=target,
+                resolution=(resolution, resolution))
