@@ -566,7 +566,7 @@ __device__ __forceinline__ void recorded_edge_gradient(const AaCtx& a, float* gr
 // need is loaded up front, unconditionally, so that the loads overlap instead of each waiting for
 // the record that decides it; K = 0 handles any channel count.
 template <int K>
-__global__ void __launch_bounds__(256) aa_bwd_recorded_kernel(const AaCtx a,
+__global__ void __launch_bounds__(256, 5) aa_bwd_recorded_kernel(const AaCtx a,
                                                               const float2* __restrict__ rec_t,
                                                               const uint8_t* __restrict__ rec_code,
                                                               const int4* __restrict__ rec_verts,
