@@ -190,7 +190,7 @@ __device__ __forceinline__ void scatter_attr(float* __restrict__ grad_attr, long
   if (active && (peers & ((1u << lane) - 1u)) == 0u) red_add(grad_attr + row * channels + c, v[0]);
 }
 
-__global__ void __launch_bounds__(256) interp_bwd_kernel(
+__global__ void __launch_bounds__(256, 6) interp_bwd_kernel(
     const float* __restrict__ attr, long long attr_batch, long long num_vert, int channels,
     const float4* __restrict__ rast, const float4* __restrict__ rast_db, const int* __restrict__ tri,
     int num_tri, const int* __restrict__ diff, int num_diff, long long total,
