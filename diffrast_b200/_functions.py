@@ -55,8 +55,8 @@ class Rasterize(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, pos: Tensor, tri: Tensor, height: int, width: int, grad_db: bool,
-                prev_keys: Tensor | None):
-        keys = K.raster_keys(pos, tri, height, width, prev_keys)
+                prev_keys: Tensor | None, ranges: K.RangeTable | None):
+        keys = K.raster_keys(pos, tri, height, width, prev_keys, ranges)
         rast, rast_db = K.resolve_fwd(pos, tri, keys)
         # Unused outputs (keys always, rast_db often) get no zero-filled gradient.
         ctx.set_materialize_grads(False)
@@ -76,7 +76,7 @@ class Rasterize(torch.autograd.Function):
         use_db = ctx.grad_db and grad_db is not None
         grad_pos = K.resolve_bwd(pos, tri, keys, K.aligned(grad_rast),
                                  K.aligned(grad_db) if use_db else None)
-        return grad_pos, None, None, None, None, None
+        return grad_pos, None, None, None, None, None, None
 
 
 class Interpolate(torch.autograd.Function):

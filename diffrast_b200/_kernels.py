@@ -10,6 +10,7 @@ from __future__ import annotations
 import contextlib
 import functools
 from ctypes import byref, c_int64
+from typing import NamedTuple
 
 import torch
 from torch import Tensor
@@ -69,23 +70,52 @@ def _scratch(nbytes: int, device: torch.device) -> Tensor:
     return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
 
 
+class RangeTable(NamedTuple):
+    """Range mode on the device: item ``i`` draws triangles ``start[i] .. start[i] + count``,
+    whose flat indices are ``first[i] .. first[i] + count - 1`` (exclusive prefix sums of the
+    counts, int64); ``total`` is the sum of the counts."""
+
+    start: Tensor
+    first: Tensor
+    total: int
+
+    @property
+    def items(self) -> int:
+        return self.start.shape[0]
+
+
+def range_table(ranges: Tensor, device: torch.device) -> RangeTable:
+    """Device table of a validated ``ranges`` ``[items, 2]`` int32 (start, count)."""
+    host = ranges.detach().cpu().to(torch.int64)
+    first = torch.zeros(host.shape[0], dtype=torch.int64)
+    if host.shape[0] > 1:
+        first[1:] = torch.cumsum(host[:-1, 1], 0)
+    total = int(host[:, 1].sum()) if host.shape[0] else 0
+    return RangeTable(host[:, 0].to(torch.int32).to(device), first.to(device), total)
+
+
 @timed("raster_visibility")
-def raster_keys(pos: Tensor, tri: Tensor, height: int, width: int, prev_keys: Tensor | None) -> Tensor:
-    """Packed visibility keys ``[batch, height, width]`` int64 of the nearest layer behind
-    ``prev_keys`` (all layers when ``None``)."""
+def raster_keys(pos: Tensor, tri: Tensor, height: int, width: int, prev_keys: Tensor | None,
+                ranges: RangeTable | None = None) -> Tensor:
+    """Packed visibility keys ``[views, height, width]`` int64 of the nearest layer behind
+    ``prev_keys`` (all layers when ``None``). ``pos`` is ``[views, V, 4]``, or ``[1, V, 4]``
+    shared by every view; with ``ranges`` the views are its items."""
     lib, dev = N.lib(), pos.device
     s = N.stream(dev)
-    batch, num_vert, num_tri = pos.shape[0], pos.shape[1], tri.shape[0]
+    pos_batch, num_vert, num_tri = pos.shape[0], pos.shape[1], tri.shape[0]
+    batch = ranges.items if ranges is not None else pos_batch
+    total = ranges.total if ranges is not None else batch * num_tri
     keys = torch.empty((batch, height, width), dtype=torch.int64, device=dev)
-    shape_key = (dev, batch, num_tri, height, width)
-    cap = _capacity.get(shape_key, max(1024, min(batch * num_tri, 1 << 16)))
+    shape_key = (dev, batch, total, height, width)
+    cap = _capacity.get(shape_key, max(1024, min(total, 1 << 16)))
+    rs, rf = (N.ptr(ranges.start), N.ptr(ranges.first)) if ranges is not None else (None, None)
     binned, pairs = c_int64(0), c_int64(0)
     for _ in range(2):
         ws = _scratch(lib.dr_raster_setup_workspace_bytes(cap, height, width), dev)
         N.check(
-            lib.dr_raster_setup(pos.data_ptr(), tri.data_ptr(), batch, num_vert, num_tri, height,
-                                width, N.ptr(prev_keys), keys.data_ptr(), ws.data_ptr(),
-                                ws.numel(), cap, s),
+            lib.dr_raster_setup(pos.data_ptr(), pos_batch, tri.data_ptr(), batch, num_vert,
+                                num_tri, rs, rf, total, height, width, N.ptr(prev_keys),
+                                keys.data_ptr(), ws.data_ptr(), ws.numel(), cap, s),
             "dr_raster_setup",
         )  # fmt: skip
         N.check(lib.dr_raster_counts(ws.data_ptr(), byref(binned), byref(pairs), s), "dr_raster_counts")
@@ -100,9 +130,10 @@ def raster_keys(pos: Tensor, tri: Tensor, height: int, width: int, prev_keys: Te
     if binned.value > 0 and pairs.value > 0:
         bws = _scratch(lib.dr_raster_bin_workspace_bytes(batch, height, width, pairs.value), dev)
         N.check(
-            lib.dr_raster_tiles(pos.data_ptr(), tri.data_ptr(), batch, num_vert, num_tri, height,
-                                width, N.ptr(prev_keys), keys.data_ptr(), ws.data_ptr(),
-                                binned.value, pairs.value, bws.data_ptr(), bws.numel(), s),
+            lib.dr_raster_tiles(pos.data_ptr(), pos_batch, tri.data_ptr(), batch, num_vert,
+                                num_tri, height, width, N.ptr(prev_keys), keys.data_ptr(),
+                                ws.data_ptr(), binned.value, pairs.value, bws.data_ptr(),
+                                bws.numel(), s),
             "dr_raster_tiles",
         )  # fmt: skip
     return keys
@@ -114,9 +145,10 @@ def resolve_fwd(pos: Tensor, tri: Tensor, keys: Tensor) -> tuple[Tensor, Tensor]
     rast = torch.empty((batch, height, width, 4), dtype=torch.float32, device=pos.device)
     rast_db = torch.empty_like(rast)
     N.check(
-        N.lib().dr_raster_resolve_fwd(pos.data_ptr(), tri.data_ptr(), keys.data_ptr(), batch,
-                                      pos.shape[1], tri.shape[0], height, width, rast.data_ptr(),
-                                      rast_db.data_ptr(), N.stream(pos.device)),
+        N.lib().dr_raster_resolve_fwd(pos.data_ptr(), pos.shape[0], tri.data_ptr(),
+                                      keys.data_ptr(), batch, pos.shape[1], tri.shape[0], height,
+                                      width, rast.data_ptr(), rast_db.data_ptr(),
+                                      N.stream(pos.device)),
         "dr_raster_resolve_fwd",
     )  # fmt: skip
     return rast, rast_db
@@ -128,10 +160,10 @@ def resolve_bwd(pos: Tensor, tri: Tensor, keys: Tensor, grad_rast: Tensor,
     batch, height, width = keys.shape
     grad_pos = torch.zeros_like(pos)
     N.check(
-        N.lib().dr_raster_resolve_bwd(pos.data_ptr(), tri.data_ptr(), keys.data_ptr(), batch,
-                                      pos.shape[1], tri.shape[0], height, width,
-                                      grad_rast.data_ptr(), N.ptr(grad_db), grad_pos.data_ptr(),
-                                      N.stream(pos.device)),
+        N.lib().dr_raster_resolve_bwd(pos.data_ptr(), pos.shape[0], tri.data_ptr(),
+                                      keys.data_ptr(), batch, pos.shape[1], tri.shape[0], height,
+                                      width, grad_rast.data_ptr(), N.ptr(grad_db),
+                                      grad_pos.data_ptr(), N.stream(pos.device)),
         "dr_raster_resolve_bwd",
     )  # fmt: skip
     return grad_pos

@@ -27,20 +27,21 @@ _SIGNATURES = {
     "dr_raster_setup_workspace_bytes": (c_size_t, [c_int64, c_int32, c_int32]),
     "dr_raster_setup": (
         c_int,
-        [_P, _P, c_int64, c_int64, c_int64, c_int32, c_int32, _P, _P, _P, c_size_t, c_int64, _P],
+        [_P, c_int64, _P, c_int64, c_int64, c_int64, _P, _P, c_int64, c_int32, c_int32, _P, _P, _P,
+         c_size_t, c_int64, _P],
     ),
     "dr_raster_counts": (c_int, [_P, POINTER(c_int64), POINTER(c_int64), _P]),
     "dr_raster_bin_workspace_bytes": (c_size_t, [c_int64, c_int32, c_int32, c_int64]),
     "dr_raster_tiles": (
         c_int,
-        [_P, _P, c_int64, c_int64, c_int64, c_int32, c_int32, _P, _P, _P, c_int64, c_int64, _P,
-         c_size_t, _P],
+        [_P, c_int64, _P, c_int64, c_int64, c_int64, c_int32, c_int32, _P, _P, _P, c_int64,
+         c_int64, _P, c_size_t, _P],
     ),
     "dr_raster_resolve_fwd": (
-        c_int, [_P, _P, _P, c_int64, c_int64, c_int64, c_int32, c_int32, _P, _P, _P]
+        c_int, [_P, c_int64, _P, _P, c_int64, c_int64, c_int64, c_int32, c_int32, _P, _P, _P]
     ),
     "dr_raster_resolve_bwd": (
-        c_int, [_P, _P, _P, c_int64, c_int64, c_int64, c_int32, c_int32, _P, _P, _P, _P]
+        c_int, [_P, c_int64, _P, _P, c_int64, c_int64, c_int64, c_int32, c_int32, _P, _P, _P, _P]
     ),
     "dr_interpolate_fwd": (
         c_int,

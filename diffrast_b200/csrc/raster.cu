@@ -26,12 +26,41 @@
 namespace dr {
 namespace {
 
-// One triangle that needs tile binning: flat view * num_tri + triangle, and its inclusive pixel
+// One triangle that needs tile binning: its view (item) and triangle, and its inclusive pixel
 // box. The record layout does not depend on the list capacity.
 struct Binned {
-  int g;
+  int b, t;
   int c0, c1, r0, r1;
 };
+
+// The (view, triangle) pairs a visibility pass draws. Instanced mode: every triangle in every
+// view, flat index g = view * num_tri + triangle, positions per view. Range mode (range_start
+// non-null): item b draws triangles range_start[b] .. + count, flat indices range_first[b] ..
+// range_first[b + 1] - 1 (exclusive prefix sums of the counts), all items sharing one position
+// buffer (pos_stride 0).
+struct Items {
+  int num_tri;
+  int items;
+  const int* range_start;
+  const long long* range_first;
+  long long pos_stride;  // vertices between the positions of consecutive views
+};
+
+__device__ __forceinline__ void locate(const Items& it, long long g, int& b, int& t) {
+  if (it.range_start == nullptr) {
+    b = static_cast<int>(g / it.num_tri);
+    t = static_cast<int>(g - static_cast<long long>(b) * it.num_tri);
+    return;
+  }
+  // Last item whose first flat index is <= g (empty items share their successor's).
+  int lo = 0, hi = it.items - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(it.range_first + mid) <= g) lo = mid; else hi = mid - 1;
+  }
+  b = lo;
+  t = __ldg(it.range_start + lo) + static_cast<int>(g - __ldg(it.range_first + lo));
+}
 
 struct SetupLayout {
   unsigned long long* counters;  // [0] binned triangles, [1] (triangle, tile) pairs
@@ -148,7 +177,7 @@ struct WarpTris {
 };
 
 __global__ void __launch_bounds__(256) setup_kernel(
-    const float* __restrict__ pos, const int* __restrict__ tri, int num_vert, int num_tri,
+    const float* __restrict__ pos, const int* __restrict__ tri, const Items items,
     long long total, int height, int width, const float* __restrict__ centres,
     const long long* __restrict__ prev, long long* __restrict__ keys,
     unsigned long long* __restrict__ counters, Binned* __restrict__ binned, long long capacity) {
@@ -162,12 +191,11 @@ __global__ void __launch_bounds__(256) setup_kernel(
   Vert v0 = {0.f, 0.f, 0.f, 1.f}, v1 = v0, v2 = v0;
   float nx[3] = {0.f, 0.f, 0.f}, ny[3] = {0.f, 0.f, 0.f};
   if (g < total) {
-    b = static_cast<int>(g / num_tri);
-    t = static_cast<int>(g - static_cast<long long>(b) * num_tri);
+    locate(items, g, b, t);
     const int i0 = __ldg(tri + 3 * static_cast<long long>(t));
     const int i1 = __ldg(tri + 3 * static_cast<long long>(t) + 1);
     const int i2 = __ldg(tri + 3 * static_cast<long long>(t) + 2);
-    const long long base = static_cast<long long>(b) * num_vert;
+    const long long base = static_cast<long long>(b) * items.pos_stride;
     v0 = load_vert(pos, base + i0);
     v1 = load_vert(pos, base + i1);
     v2 = load_vert(pos, base + i2);
@@ -373,15 +401,14 @@ __global__ void __launch_bounds__(256) setup_kernel(
   slot0 = __shfl_sync(0xffffffffu, slot0, 0);
   if (large) {
     const unsigned long long slot = slot0 + __popc(mask & ((1u << lane) - 1u));
-    if (slot < static_cast<unsigned long long>(capacity)) binned[slot] = {static_cast<int>(g), c0, c1, r0, r1};
+    if (slot < static_cast<unsigned long long>(capacity)) binned[slot] = {b, t, c0, c1, r0, r1};
   }
 }
 
 // One warp per binned triangle; its lanes walk the triangle's tiles.
 template <bool kScatter>
 __global__ void __launch_bounds__(256) bin_kernel(const Binned* __restrict__ binned,
-                                                  long long count,
-                                                  int num_tri, int tiles_x, int tiles_per_image,
+                                                  long long count, int tiles_x, int tiles_per_image,
                                                   unsigned* __restrict__ tile_count,
                                                   const unsigned* __restrict__ tile_offset,
                                                   int* __restrict__ pairs) {
@@ -390,8 +417,7 @@ __global__ void __launch_bounds__(256) bin_kernel(const Binned* __restrict__ bin
   for (long long i = (blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x) / 32; i < count;
        i += warps) {
     const Binned rec = binned[i];
-    const int g = rec.g;
-    const int b = g / num_tri;
+    const int b = rec.b;
     const int tx0 = rec.c0 / kTile, tx1 = rec.c1 / kTile, ty0 = rec.r0 / kTile, ty1 = rec.r1 / kTile;
     const int nx = tx1 - tx0 + 1;
     const int n = nx * (ty1 - ty0 + 1);
@@ -534,7 +560,7 @@ __global__ void __launch_bounds__(1024) scan_kernel(const unsigned* __restrict__
 }
 
 __global__ void __launch_bounds__(256) tile_kernel(
-    const float* __restrict__ pos, const int* __restrict__ tri, int num_vert, int num_tri,
+    const float* __restrict__ pos, const int* __restrict__ tri, long long pos_stride,
     int height, int width, int tiles_x, int tiles_per_image, int num_tiles,
     const float* __restrict__ centres,
     const long long* __restrict__ prev, long long* __restrict__ keys, const int* __restrict__ pairs,
@@ -572,10 +598,8 @@ __global__ void __launch_bounds__(256) tile_kernel(
     const int n = static_cast<int>(s_count);
     if (threadIdx.x < n) {
       const Binned rec = binned[pairs[s_first + threadIdx.x]];
-      const int g = rec.g;
-      const int b = g / num_tri;
-      const int t = g - b * num_tri;
-      const long long base = static_cast<long long>(b) * num_vert;
+      const int b = rec.b, t = rec.t;
+      const long long base = static_cast<long long>(b) * pos_stride;
       const float4* p4 = reinterpret_cast<const float4*>(pos);
       sv[0][threadIdx.x] = __ldg(p4 + base + __ldg(tri + 3 * static_cast<long long>(t)));
       sv[1][threadIdx.x] = __ldg(p4 + base + __ldg(tri + 3 * static_cast<long long>(t) + 1));
@@ -636,7 +660,7 @@ __device__ __forceinline__ ResolvePixel resolve_pixel(int b0, int height, int wi
 __device__ __forceinline__ PixelTri pixel_triangle(const float* __restrict__ pos,
                                                    const int* __restrict__ tri,
                                                    const long long* __restrict__ keys,
-                                                   const ResolvePixel& rp, int num_vert, int height,
+                                                   const ResolvePixel& rp, long long pos_stride, int height,
                                                    int width) {
   PixelTri r;
   const long long key = keys[rp.p];
@@ -650,7 +674,7 @@ __device__ __forceinline__ PixelTri pixel_triangle(const float* __restrict__ pos
     r.i0 = __ldg(tri + 3 * static_cast<long long>(r.t));
     r.i1 = __ldg(tri + 3 * static_cast<long long>(r.t) + 1);
     r.i2 = __ldg(tri + 3 * static_cast<long long>(r.t) + 2);
-    const long long base = static_cast<long long>(r.b) * num_vert;
+    const long long base = static_cast<long long>(r.b) * pos_stride;
     r.v0 = load_vert(pos, base + r.i0);
     r.v1 = load_vert(pos, base + r.i1);
     r.v2 = load_vert(pos, base + r.i2);
@@ -669,12 +693,12 @@ constexpr int kResolveThreads = 128;
 
 __global__ void __launch_bounds__(kResolveThreads) resolve_fwd_kernel(
     const float* __restrict__ pos, const int* __restrict__ tri, const long long* __restrict__ keys,
-    int b0, int num_vert, int height, int width, float4* __restrict__ rast,
+    int b0, long long pos_stride, int height, int width, float4* __restrict__ rast,
     float4* __restrict__ rast_db) {
   const int row = blockIdx.y;
   const long long b = b0 + static_cast<long long>(blockIdx.z);
   const long long row_start = (b * height + row) * width;
-  const long long base = b * num_vert;
+  const long long base = b * pos_stride;
   long long key[kResolvePix];
 #pragma unroll
   for (int i = 0; i < kResolvePix; ++i) {
@@ -739,13 +763,13 @@ __device__ __forceinline__ void cross3(const float u[3], const float v[3], float
 
 __global__ void __launch_bounds__(256) resolve_bwd_kernel(
     const float* __restrict__ pos, const int* __restrict__ tri, const long long* __restrict__ keys,
-    int b0, int num_vert, int height, int width, const float4* __restrict__ grad_rast,
+    int b0, long long pos_stride, int height, int width, const float4* __restrict__ grad_rast,
     const float4* __restrict__ grad_db, float* __restrict__ grad_pos) {
   const ResolvePixel rp = resolve_pixel(b0, height, width);
   const long long p = rp.p;
   PixelTri q;
   if (rp.inside) {
-    q = pixel_triangle(pos, tri, keys, rp, num_vert, height, width);
+    q = pixel_triangle(pos, tri, keys, rp, pos_stride, height, width);
   } else {
     q.covered = false;
     q.b = 0;
@@ -830,7 +854,7 @@ __global__ void __launch_bounds__(256) resolve_bwd_kernel(
       gv[k][3] = gw[k];
     }
   }
-  const long long base = static_cast<long long>(q.b) * num_vert;
+  const long long base = static_cast<long long>(q.b) * pos_stride;
   // A warp whose covered pixels all show one triangle (large triangles) sums its gradients first
   // and adds them once; otherwise each lane adds its own with vector reductions (with triangles
   // of about a pixel, lanes rarely share a vertex and a warp-level match costs more than it saves).
@@ -855,14 +879,18 @@ __global__ void __launch_bounds__(256) resolve_bwd_kernel(
 }
 
 bool bad_raster_args(const float* pos, const int32_t* tri, int64_t batch, int64_t num_vert,
-                     int64_t num_tri, int32_t height, int32_t width) {
+                     int64_t num_tri, int32_t height, int32_t width, int64_t pos_batch) {
   if (batch < 0 || num_vert < 0 || num_tri < 0 || height <= 0 || width <= 0) return true;
+  if (pos_batch != 1 && pos_batch != batch) return true;
   if (height >= (1 << 20) || width >= (1 << 20)) return true;
-  if (batch * num_tri >= (1LL << 31)) return true;
+  if (num_tri >= (1LL << 31)) return true;
   if ((reinterpret_cast<uintptr_t>(pos) & 15u) != 0) return true;
-  if (batch * num_tri > 0 && (pos == nullptr || tri == nullptr)) return true;
+  if (batch > 0 && num_tri > 0 && (pos == nullptr || tri == nullptr)) return true;
   return false;
 }
+
+// Vertices between the positions of consecutive views: 0 when all views share pos.
+long long pos_stride(int64_t pos_batch, int64_t num_vert) { return pos_batch == 1 ? 0 : num_vert; }
 
 }  // namespace
 }  // namespace dr
@@ -874,13 +902,19 @@ extern "C" size_t dr_raster_setup_workspace_bytes(int64_t capacity, int32_t heig
   return setup_bytes(capacity < 0 ? 0 : capacity, height < 0 ? 0 : height, width < 0 ? 0 : width);
 }
 
-extern "C" int dr_raster_setup(const float* pos, const int32_t* tri, int64_t batch,
-                               int64_t num_vert, int64_t num_tri, int32_t height, int32_t width,
+extern "C" int dr_raster_setup(const float* pos, int64_t pos_batch, const int32_t* tri,
+                               int64_t batch, int64_t num_vert, int64_t num_tri,
+                               const int32_t* range_start, const int64_t* range_first,
+                               int64_t range_total, int32_t height, int32_t width,
                                const int64_t* prev_keys, int64_t* keys, void* workspace,
                                size_t workspace_bytes, int64_t capacity, void* stream) {
-  if (bad_raster_args(pos, tri, batch, num_vert, num_tri, height, width) || capacity < 0 ||
-      keys == nullptr || workspace == nullptr)
+  const bool ranged = range_start != nullptr;
+  if (bad_raster_args(pos, tri, batch, num_vert, num_tri, height, width, pos_batch) ||
+      capacity < 0 || keys == nullptr || workspace == nullptr)
     return DR_ERR_INVALID_ARGUMENT;
+  if (ranged && (range_first == nullptr || range_total < 0 || range_total >= (1LL << 31)))
+    return DR_ERR_INVALID_ARGUMENT;
+  if (!ranged && batch * num_tri >= (1LL << 31)) return DR_ERR_INVALID_ARGUMENT;
   if (workspace_bytes < setup_bytes(capacity, height, width)) return DR_ERR_WORKSPACE_TOO_SMALL;
   cudaStream_t s = as_stream(stream);
   SetupLayout l = setup_layout(workspace, height, width);
@@ -892,12 +926,15 @@ extern "C" int dr_raster_setup(const float* pos, const int32_t* tri, int64_t bat
         reinterpret_cast<long long*>(keys), pixels);
   }
   centres_kernel<<<blocks_for(height + width, 256), 256, 0, s>>>(l.centres, height, width);
-  const long long total = batch * num_tri;
-  if (total > 0) {
+  const long long total = ranged ? range_total : batch * num_tri;
+  const Items items = {static_cast<int>(num_tri), static_cast<int>(batch), range_start,
+                       reinterpret_cast<const long long*>(range_first),
+                       pos_stride(pos_batch, num_vert)};
+  if (total > 0 && batch > 0) {
     setup_kernel<<<blocks_for(total, 256), 256, 0, s>>>(
-        pos, tri, static_cast<int>(num_vert), static_cast<int>(num_tri), total, height, width,
-        l.centres, reinterpret_cast<const long long*>(prev_keys),
-        reinterpret_cast<long long*>(keys), l.counters, l.binned, capacity);
+        pos, tri, items, total, height, width, l.centres,
+        reinterpret_cast<const long long*>(prev_keys), reinterpret_cast<long long*>(keys),
+        l.counters, l.binned, capacity);
   }
   return launch_status();
 }
@@ -922,12 +959,13 @@ extern "C" size_t dr_raster_bin_workspace_bytes(int64_t batch, int32_t height, i
   return bin_bytes(batch * tiles_x * tiles_y, num_pairs < 0 ? 0 : num_pairs);
 }
 
-extern "C" int dr_raster_tiles(const float* pos, const int32_t* tri, int64_t batch,
-                               int64_t num_vert, int64_t num_tri, int32_t height, int32_t width,
-                               const int64_t* prev_keys, int64_t* keys,
+extern "C" int dr_raster_tiles(const float* pos, int64_t pos_batch, const int32_t* tri,
+                               int64_t batch, int64_t num_vert, int64_t num_tri, int32_t height,
+                               int32_t width, const int64_t* prev_keys, int64_t* keys,
                                const void* setup_workspace, int64_t num_binned, int64_t num_pairs,
                                void* bin_workspace, size_t bin_workspace_bytes, void* stream) {
-  if (bad_raster_args(pos, tri, batch, num_vert, num_tri, height, width) || keys == nullptr ||
+  if (bad_raster_args(pos, tri, batch, num_vert, num_tri, height, width, pos_batch) ||
+      keys == nullptr ||
       setup_workspace == nullptr || num_binned < 0 || num_pairs < 0)
     return DR_ERR_INVALID_ARGUMENT;
   if (num_pairs >= (1LL << 31)) return DR_ERR_TOO_LARGE;
@@ -947,21 +985,18 @@ extern "C" int dr_raster_tiles(const float* pos, const int32_t* tri, int64_t bat
   if (err != cudaSuccess) return static_cast<int>(err);
   const int tiles_per_image = tiles_x * tiles_y;
   const unsigned bin_blocks = min(blocks_for(num_binned * 32, 256), 148u * 16u);
-  bin_kernel<false><<<bin_blocks, 256, 0, s>>>(sl.binned, num_binned,
-                                               static_cast<int>(num_tri), tiles_x,
-                                               tiles_per_image, bl.tile_count, nullptr, nullptr);
+  bin_kernel<false><<<bin_blocks, 256, 0, s>>>(sl.binned, num_binned, tiles_x, tiles_per_image,
+                                               bl.tile_count, nullptr, nullptr);
   const int chunks = static_cast<int>(scan_chunks(tiles));
   scan_totals_kernel<<<chunks, 1024, 0, s>>>(bl.tile_count, static_cast<int>(tiles),
                                              bl.scan_totals);
   scan_chunks_kernel<<<1, 1024, 0, s>>>(bl.scan_totals, chunks);
   scan_kernel<<<chunks, 1024, 0, s>>>(bl.tile_count, static_cast<int>(tiles), bl.scan_totals,
                                       chunks, bl.tile_offset, bl.item_offset);
-  bin_kernel<true><<<bin_blocks, 256, 0, s>>>(sl.binned, num_binned,
-                                              static_cast<int>(num_tri), tiles_x,
-                                              tiles_per_image, bl.tile_cursor, bl.tile_offset,
-                                              bl.pairs);
-  tile_kernel<<<148 * 8, 256, 0, s>>>(pos, tri, static_cast<int>(num_vert),
-                                      static_cast<int>(num_tri), height, width, tiles_x,
+  bin_kernel<true><<<bin_blocks, 256, 0, s>>>(sl.binned, num_binned, tiles_x, tiles_per_image,
+                                              bl.tile_cursor, bl.tile_offset, bl.pairs);
+  tile_kernel<<<148 * 8, 256, 0, s>>>(pos, tri, pos_stride(pos_batch, num_vert), height, width,
+                                      tiles_x,
                                       tiles_per_image, static_cast<int>(tiles), sl.centres,
                                       reinterpret_cast<const long long*>(prev_keys),
                                       reinterpret_cast<long long*>(keys), bl.pairs, sl.binned,
@@ -969,12 +1004,13 @@ extern "C" int dr_raster_tiles(const float* pos, const int32_t* tri, int64_t bat
   return launch_status();
 }
 
-extern "C" int dr_raster_resolve_fwd(const float* pos, const int32_t* tri, const int64_t* keys,
-                                     int64_t batch, int64_t num_vert, int64_t num_tri,
+extern "C" int dr_raster_resolve_fwd(const float* pos, int64_t pos_batch, const int32_t* tri,
+                                     const int64_t* keys, int64_t batch, int64_t num_vert,
+                                     int64_t num_tri,
                                      int32_t height, int32_t width, float* rast, float* rast_db,
                                      void* stream) {
-  if (bad_raster_args(pos, tri, batch, num_vert, num_tri, height, width) || keys == nullptr ||
-      rast == nullptr)
+  if (bad_raster_args(pos, tri, batch, num_vert, num_tri, height, width, pos_batch) ||
+      keys == nullptr || rast == nullptr)
     return DR_ERR_INVALID_ARGUMENT;
   const long long total = batch * static_cast<long long>(height) * width;
   if (total == 0) return DR_OK;
@@ -984,18 +1020,19 @@ extern "C" int dr_raster_resolve_fwd(const float* pos, const int32_t* tri, const
                     height, static_cast<unsigned>(min(batch - b0, 65535LL)));
     resolve_fwd_kernel<<<grid, kResolveThreads, 0, as_stream(stream)>>>(
         pos, tri, reinterpret_cast<const long long*>(keys), static_cast<int>(b0),
-        static_cast<int>(num_vert), height, width, reinterpret_cast<float4*>(rast),
+        pos_stride(pos_batch, num_vert), height, width, reinterpret_cast<float4*>(rast),
         reinterpret_cast<float4*>(rast_db));
   }
   return launch_status();
 }
 
-extern "C" int dr_raster_resolve_bwd(const float* pos, const int32_t* tri, const int64_t* keys,
-                                     int64_t batch, int64_t num_vert, int64_t num_tri,
+extern "C" int dr_raster_resolve_bwd(const float* pos, int64_t pos_batch, const int32_t* tri,
+                                     const int64_t* keys, int64_t batch, int64_t num_vert,
+                                     int64_t num_tri,
                                      int32_t height, int32_t width, const float* grad_rast,
                                      const float* grad_db, float* grad_pos, void* stream) {
-  if (bad_raster_args(pos, tri, batch, num_vert, num_tri, height, width) || keys == nullptr ||
-      grad_rast == nullptr || grad_pos == nullptr)
+  if (bad_raster_args(pos, tri, batch, num_vert, num_tri, height, width, pos_batch) ||
+      keys == nullptr || grad_rast == nullptr || grad_pos == nullptr)
     return DR_ERR_INVALID_ARGUMENT;
   const long long total = batch * static_cast<long long>(height) * width;
   if (total == 0) return DR_OK;
@@ -1004,7 +1041,7 @@ extern "C" int dr_raster_resolve_bwd(const float* pos, const int32_t* tri, const
     const dim3 grid((width + 255) / 256, height, static_cast<unsigned>(min(batch - b0, 65535LL)));
     resolve_bwd_kernel<<<grid, 256, 0, as_stream(stream)>>>(
         pos, tri, reinterpret_cast<const long long*>(keys), static_cast<int>(b0),
-        static_cast<int>(num_vert), height, width, reinterpret_cast<const float4*>(grad_rast),
+        pos_stride(pos_batch, num_vert), height, width, reinterpret_cast<const float4*>(grad_rast),
         reinterpret_cast<const float4*>(grad_db), grad_pos);
   }
   return launch_status();

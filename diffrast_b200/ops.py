@@ -59,33 +59,33 @@ def rasterize(
     resolution = check_rasterize_inputs(glctx, pos, tri, resolution, ranges)
     output_db = getattr(glctx, "output_db", True)
     grad_db = grad_db and output_db
-    if pos.ndim == 2:
-        layers = [
-            rasterize_layer(pos[None], triangles, resolution, grad_db, None)[:2]
-            for triangles in split_ranges(tri, ranges)
-        ]
-        rast, rast_db = join_ranges(pos, resolution, ranges, layers)
-    else:
-        rast, rast_db, _ = rasterize_layer(pos, tri, resolution, grad_db, None)
+    table = K.range_table(ranges, pos.device) if pos.ndim == 2 else None
+    rast, rast_db, _ = rasterize_layer(pos, tri, resolution, grad_db, None, table)
     return rast, (rast_db if output_db else rast.new_zeros(*rast.shape[:3], 0))
 
 
 def rasterize_layer(
-    pos: Tensor, tri: Tensor, resolution: tuple[int, int], grad_db: bool, previous: Tensor | None
+    pos: Tensor, tri: Tensor, resolution: tuple[int, int], grad_db: bool, previous: Tensor | None,
+    ranges: K.RangeTable | None = None,
 ) -> tuple[Tensor, Tensor, Tensor]:
     """The depth layer behind ``previous`` (packed keys of the layer before, or ``None``).
 
+    ``pos`` is ``[views, V, 4]``, or ``[V, 4]`` with a device range table (range mode: one launch
+    draws every item, ids counted from the start of ``tri`` as diffrast ops.py:490-508 does).
     Returns ``(rast, rast_db, keys)``; ``keys`` is the state for the next layer.
     """
     height, width = resolution
     require_cuda(pos.device)
-    if tri.shape[0] == 0 or pos.shape[0] == 0:
-        empty = pos.new_zeros(pos.shape[0], height, width, 4)
-        keys = torch.full((pos.shape[0], height, width), EMPTY_KEY, dtype=torch.int64, device=pos.device)
+    views = ranges.items if ranges is not None else pos.shape[0]
+    drawn = ranges.total if ranges is not None else tri.shape[0] * views
+    if drawn == 0:
+        empty = pos.new_zeros(views, height, width, 4)
+        keys = torch.full((views, height, width), EMPTY_KEY, dtype=torch.int64, device=pos.device)
         return empty, empty.clone(), keys
     with torch.cuda.device(pos.device):
         rast, rast_db, keys = F.Rasterize.apply(
-            K.aligned(pos), tri.contiguous(), height, width, bool(grad_db), previous
+            K.aligned(pos if ranges is None else pos[None]), tri.contiguous(), height, width,
+            bool(grad_db), previous, ranges,
         )
     return rast, rast_db, keys
 
@@ -123,23 +123,6 @@ def _check_ranges(ranges: Tensor | None, num_tri: int) -> None:
                 f"ranges[{item}] = (start {start}, count {count}) does not lie within the "
                 f"{num_tri} triangles of tri."
             )
-
-
-def split_ranges(tri: Tensor, ranges: Tensor) -> list[Tensor]:
-    """Triangles each item draws in range mode, as slices of ``tri`` (diffrast ops.py:482-487)."""
-    return [tri[start : start + count] for start, count in ranges.tolist()]
-
-
-def join_ranges(pos: Tensor, resolution, ranges: Tensor, layers) -> tuple[Tensor, Tensor]:
-    """Stack per-item ``(rast, rast_db)`` of range mode, with ids counted from the start of ``tri``
-    (diffrast ops.py:490-508)."""
-    empty = pos.new_zeros(0, *resolution, 4)
-    rasts, rast_dbs = [empty], [empty]
-    for (start, _), (rast, rast_db) in zip(ranges.tolist(), layers, strict=True):
-        ids = rast[..., 3:]
-        rasts.append(torch.cat([rast[..., :3], torch.where(ids > 0, ids + start, ids)], -1))
-        rast_dbs.append(rast_db)
-    return torch.cat(rasts), torch.cat(rast_dbs)
 
 
 # ---------------------------------------------------------------------------------------------

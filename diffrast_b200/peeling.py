@@ -11,7 +11,8 @@ from types import TracebackType
 from torch import Tensor
 
 from diffrast_b200.context import RasterizeContext
-from diffrast_b200.ops import check_rasterize_inputs, join_ranges, rasterize_layer, split_ranges
+from diffrast_b200 import _kernels as K
+from diffrast_b200.ops import check_rasterize_inputs, rasterize_layer
 
 
 class DepthPeeler:
@@ -33,7 +34,7 @@ class DepthPeeler:
         self._output_db = getattr(glctx, "output_db", True)
         self._grad_db = grad_db and self._output_db
         self._pos, self._tri = pos.clone(), tri.clone()
-        self._ranges = ranges.clone() if pos.ndim == 2 else None
+        self._ranges = K.range_table(ranges, pos.device) if pos.ndim == 2 else None
         self._state = None
         self._closed = False
 
@@ -52,19 +53,7 @@ class DepthPeeler:
                 "This DepthPeeler was closed when its with block exited; create a new one to "
                 "rasterize more layers."
             )
-        if self._ranges is None:
-            rast, rast_db, self._state = rasterize_layer(
-                self._pos, self._tri, self._resolution, self._grad_db, self._state
-            )
-        else:
-            items = split_ranges(self._tri, self._ranges)
-            states = self._state or [None] * len(items)
-            layers = [
-                rasterize_layer(self._pos[None], item, self._resolution, self._grad_db, state)
-                for item, state in zip(items, states, strict=True)
-            ]
-            self._state = [layer[2] for layer in layers]
-            rast, rast_db = join_ranges(
-                self._pos, self._resolution, self._ranges, [layer[:2] for layer in layers]
-            )
+        rast, rast_db, self._state = rasterize_layer(
+            self._pos, self._tri, self._resolution, self._grad_db, self._state, self._ranges
+        )
         return rast, (rast_db if self._output_db else rast.new_zeros(*rast.shape[:3], 0))

@@ -55,9 +55,15 @@ const char* dr_status_string(int status);
  * backends/reference.py:368-397 (_visible_triangles) exactly, as packed 64-bit keys
  * ((order-preserving depth bits << 32) | triangle, INT64_MAX where empty).
  *
- * pos [batch, num_vert, 4], tri [num_tri, 3], keys [batch, height, width],
- * prev_keys: keys of the previous depth layer (DepthPeeler, peeling.py:68-92) or NULL.
- * batch * num_tri must be below 2**31; height and width below 2**20.
+ * pos [pos_batch, num_vert, 4] with pos_batch = batch, or 1 when all views share one position
+ * buffer; tri [num_tri, 3], keys [batch, height, width], prev_keys: keys of the previous depth
+ * layer (DepthPeeler, peeling.py:68-92) or NULL. height and width below 2**20.
+ * Instanced mode (range_start NULL): every view draws every triangle; batch * num_tri below 2**31.
+ * Range mode (ops.py:482-508, one pass for all items instead of one per item): view (item) b
+ * draws tri[range_start[b] .. range_start[b] + count_b - 1], with range_first [batch + 1] the
+ * exclusive prefix sums of the counts (range_first[batch] = range_total < 2**31); both are DEVICE
+ * arrays, range_start int32 and range_first int64, checked by the caller (ranges inside tri).
+ * Keys and rast ids hold indices into the whole tri, as range mode's ids are counted.
  * ------------------------------------------------------------------------------------------- */
 
 /* Scratch of stage 1 for up to `capacity` triangles that need tile binning, at this resolution. */
@@ -68,10 +74,11 @@ size_t dr_raster_setup_workspace_bytes(int64_t capacity, int32_t height, int32_t
  * for binning. If more than
  * `capacity` triangles need binning the list is incomplete: dr_raster_counts() reports how many,
  * and the caller reruns this stage with a larger workspace (the direct writes are idempotent). */
-int dr_raster_setup(const float* pos, const int32_t* tri, int64_t batch, int64_t num_vert,
-                    int64_t num_tri, int32_t height, int32_t width, const int64_t* prev_keys,
-                    int64_t* keys, void* workspace, size_t workspace_bytes, int64_t capacity,
-                    void* stream);
+int dr_raster_setup(const float* pos, int64_t pos_batch, const int32_t* tri, int64_t batch,
+                    int64_t num_vert, int64_t num_tri, const int32_t* range_start,
+                    const int64_t* range_first, int64_t range_total, int32_t height,
+                    int32_t width, const int64_t* prev_keys, int64_t* keys, void* workspace,
+                    size_t workspace_bytes, int64_t capacity, void* stream);
 
 /* Reads the two counters of stage 1: triangles to bin and (triangle, tile) pairs. Synchronises
  * `stream`. */
@@ -83,24 +90,26 @@ size_t dr_raster_bin_workspace_bytes(int64_t batch, int32_t height, int32_t widt
 
 /* Stage 2: bins the listed triangles into 16x16 screen tiles and rasterizes each tile's list with
  * the list staged in shared memory, merging into `keys` with 64-bit atomic minima. */
-int dr_raster_tiles(const float* pos, const int32_t* tri, int64_t batch, int64_t num_vert,
-                    int64_t num_tri, int32_t height, int32_t width, const int64_t* prev_keys,
+int dr_raster_tiles(const float* pos, int64_t pos_batch, const int32_t* tri, int64_t batch,
+                    int64_t num_vert, int64_t num_tri, int32_t height, int32_t width,
+                    const int64_t* prev_keys,
                     int64_t* keys, const void* setup_workspace, int64_t num_binned,
                     int64_t num_pairs, void* bin_workspace, size_t bin_workspace_bytes,
                     void* stream);
 
 /* rast [batch, h, w, 4] = (u, v, z/w, id + 1) and rast_db [.., 4] = (du/dx, du/dy, dv/dx, dv/dy),
  * zeros where empty (reference.py:69-114; _triton_resolve.py:84-116). rast_db may be NULL. */
-int dr_raster_resolve_fwd(const float* pos, const int32_t* tri, const int64_t* keys,
-                          int64_t batch, int64_t num_vert, int64_t num_tri, int32_t height,
-                          int32_t width, float* rast, float* rast_db, void* stream);
+int dr_raster_resolve_fwd(const float* pos, int64_t pos_batch, const int32_t* tri,
+                          const int64_t* keys, int64_t batch, int64_t num_vert, int64_t num_tri,
+                          int32_t height, int32_t width, float* rast, float* rast_db,
+                          void* stream);
 
 /* Gradient of rast (and rast_db unless grad_db is NULL) with respect to pos, ACCUMULATED into
- * grad_pos [batch, num_vert, 4] (clear it first) (_triton_resolve.py:156-284). */
-int dr_raster_resolve_bwd(const float* pos, const int32_t* tri, const int64_t* keys,
-                          int64_t batch, int64_t num_vert, int64_t num_tri, int32_t height,
-                          int32_t width, const float* grad_rast, const float* grad_db,
-                          float* grad_pos, void* stream);
+ * grad_pos [pos_batch, num_vert, 4] (clear it first) (_triton_resolve.py:156-284). */
+int dr_raster_resolve_bwd(const float* pos, int64_t pos_batch, const int32_t* tri,
+                          const int64_t* keys, int64_t batch, int64_t num_vert, int64_t num_tri,
+                          int32_t height, int32_t width, const float* grad_rast,
+                          const float* grad_db, float* grad_pos, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
  * Interpolate (reference.py:117-146; _triton_interpolate.py:38-254).
