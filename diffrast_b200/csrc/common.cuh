@@ -158,6 +158,19 @@ inline unsigned int blocks_for(long long n, int threads) {
   return static_cast<unsigned int>(b < 1 ? 1 : b);
 }
 
+// Blocks of `kernel` that fit on the current device at once (all SMs, `threads` per block): the
+// grid of a persistent kernel.
+template <typename Kernel>
+unsigned int resident_blocks(Kernel kernel, int threads, size_t shared_bytes = 0) {
+  int device = 0, sms = 0, per_sm = 0;
+  if (cudaGetDevice(&device) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, shared_bytes) !=
+          cudaSuccess)
+    return 148u;
+  return static_cast<unsigned int>(max(sms, 1) * max(per_sm, 1));
+}
+
 // Bytes rounded up to the 256-byte alignment of every workspace sub-buffer.
 inline size_t align256(size_t bytes) { return (bytes + 255) & ~static_cast<size_t>(255); }
 

@@ -592,21 +592,56 @@ __device__ __forceinline__ void write_record(float* __restrict__ out, long long 
   for (int i = first + N; i < stride; ++i) rec[i] = 0.0f;
 }
 
+// A quad that a whole warp added to (lane 0 keeps it): pixels that all read the same four texels
+// (a background that samples one point, a magnified region) accumulate here across the tiles a
+// warp visits and reach global memory once, instead of every warp reducing into the same four
+// addresses. Each warp has two: the one held and the one that replaces it, flushed between tiles
+// (where the tile's registers are free).
+struct HotQuad {
+  long long off[4];
+  float v[16];  // 4 taps x up to 4 channels of group c0
+  int level, c0;
+};
+
+// Reduces a held quad into the texel gradients and empties it.
+template <int NC>
+__device__ __forceinline__ void flush_quad(const Levels& L, HotQuad& h, int channels,
+                                           int grad_stride) {
+  if (h.level < 0) return;
+  const int group = min(4, channels - h.c0);
+  const bool vector = grad_stride == 4 && channels <= 4;
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    bool zero = true;
+#pragma unroll
+    for (int cc = 0; cc < NC; ++cc) zero = zero && h.v[NC * t + cc] == 0.0f;
+    if (zero) continue;
+    float* dst = L.grad[h.level] + h.off[t] * grad_stride + h.c0;
+    if constexpr (NC == 3) {
+      red_add_v4(dst, h.v[3 * t], h.v[3 * t + 1], h.v[3 * t + 2], 0.0f);
+    } else if (vector) {
+      red_add_v4(dst, h.v[4 * t], h.v[4 * t + 1], h.v[4 * t + 2], h.v[4 * t + 3]);
+    } else {
+      for (int cc = 0; cc < group; ++cc)
+        if (h.v[4 * t + cc] != 0.0f) red_add(dst + cc, h.v[4 * t + cc]);
+    }
+  }
+  h.level = -1;
+}
+
 // Texel gradients: a warp covers 16 x 2 pixels of a 16 x 16 tile, whose taps mostly land on the
 // same texels (a texel of the chosen levels spans about a pixel; background pixels all read the
 // same few). Tap by tap, lanes adding to the same texel sum their contributions with a shuffle
 // reduction and one lane issues a single reduction per texel: a 16-byte vector reduction into a
-// gradient level padded to 4 channels (grad_stride 4), scalar reductions otherwise.
-template <int MODE, int B>
-__global__ void __launch_bounds__(256) texture_bwd_kernel(
-    const Levels L, int channels, int grad_stride, const float* __restrict__ uv,
-    const float* __restrict__ uv_da, const float* __restrict__ bias, const Strides st, int height,
-    int width,
-    const float* __restrict__ grad_out, float* __restrict__ grad_uv,
-    float* __restrict__ grad_uv_da, float* __restrict__ grad_bias, const GradLayout gst) {
-  const int col = blockIdx.x * 16 + (threadIdx.x & 15);
-  const int row = blockIdx.y * 16 + (threadIdx.x >> 4);
-  const long long view = blockIdx.z;
+// gradient level padded to 4 channels (grad_stride 4), scalar reductions otherwise. RGB: exactly
+// three channels into a padded level, so the lanes reduce 3 values per tap instead of 4.
+template <int MODE, int B, bool RGB>
+__device__ __forceinline__ void texture_bwd_tile(
+    const Levels& L, int channels, int grad_stride, const float* __restrict__ uv,
+    const float* __restrict__ uv_da, const float* __restrict__ bias, const Strides& st, int height,
+    int width, const float* __restrict__ grad_out, float* __restrict__ grad_uv,
+    float* __restrict__ grad_uv_da, float* __restrict__ grad_bias, const GradLayout& gst,
+    int col, int row, long long view, HotQuad& hot, HotQuad& incoming, bool& pending) {
   const bool inside = row < height && col < width;
   const long long p = (view * height + row) * width + col;
   Lookup<MODE, B> k;
@@ -665,22 +700,46 @@ __global__ void __launch_bounds__(256) texture_bwd_kernel(
         const float gx = 1.0f - f.fx, gy = 1.0f - f.fy;
         const float wq[4] = {scale * (gx * gy), scale * (f.fx * gy), scale * (gx * f.fy),
                              scale * (f.fx * f.fy)};
-        float v[16];
+        constexpr int NC = RGB ? 3 : 4;  // values per tap
+        float v[4 * NC];
 #pragma unroll
         for (int t = 0; t < 4; ++t)
 #pragma unroll
-          for (int cc = 0; cc < 4; ++cc) v[4 * t + cc] = act && f.ok[t] ? g[cc] * wq[t] : 0.0f;
-        segmented_sum<16>(peers, v);
+          for (int cc = 0; cc < NC; ++cc) v[NC * t + cc] = act && f.ok[t] ? g[cc] * wq[t] : 0.0f;
+        segmented_sum<4 * NC>(peers, v);
         if (!act || (peers & ((1u << lane) - 1u)) != 0u) continue;
+        if (peers == 0xffffffffu) {  // the whole warp on one quad (lane 0)
+          const bool same = hot.level == level && hot.c0 == c0 && hot.off[0] == f.off[0] &&
+                            hot.off[3] == f.off[3];
+          if (same) {
+#pragma unroll
+            for (int i = 0; i < 4 * NC; ++i) hot.v[i] += v[i];
+            continue;
+          }
+          if (!pending) {
+            incoming.level = level;
+            incoming.c0 = c0;
+#pragma unroll
+            for (int t = 0; t < 4; ++t) incoming.off[t] = f.off[t];
+#pragma unroll
+            for (int i = 0; i < 4 * NC; ++i) incoming.v[i] = v[i];
+            pending = true;
+            continue;
+          }
+        }
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
           // The group's sum decides, not the leader's own weight or validity: other lanes of the
           // quad have other bilinear weights, and with zero padding other valid taps (a quad's
           // four offsets are the same for the whole group; invalid taps contributed zero).
-          if (v[4 * t] == 0.0f && v[4 * t + 1] == 0.0f && v[4 * t + 2] == 0.0f && v[4 * t + 3] == 0.0f)
-            continue;
+          bool zero = true;
+#pragma unroll
+          for (int cc = 0; cc < NC; ++cc) zero = zero && v[NC * t + cc] == 0.0f;
+          if (zero) continue;
           float* dst = L.grad[level] + f.off[t] * grad_stride + c0;
-          if (vector) {
+          if constexpr (RGB) {
+            red_add_v4(dst, v[3 * t], v[3 * t + 1], v[3 * t + 2], 0.0f);
+          } else if (vector) {
             red_add_v4(dst, v[4 * t], v[4 * t + 1], v[4 * t + 2], v[4 * t + 3]);
           } else {
             for (int cc = 0; cc < group; ++cc)
@@ -790,6 +849,42 @@ __global__ void __launch_bounds__(256) texture_bwd_kernel(
     if (grad_uv != nullptr) write_record<2>(grad_uv, p, gst.uv, gst.uv_first, g_uv);
     if (grad_uv_da != nullptr) write_record<4>(grad_uv_da, p, gst.uv_da, gst.da_first, g_da);
   }
+}
+
+// Persistent blocks walk the 16 x 16 pixel tiles of all views; each warp keeps its hot quad across
+// the tiles it visits and flushes it at the end.
+template <int MODE, int B, bool RGB>
+__global__ void __launch_bounds__(256, B == DR_BOUNDARY_CUBE ? 2 : 4) texture_bwd_kernel(
+    const Levels L, int channels, int grad_stride, const float* __restrict__ uv,
+    const float* __restrict__ uv_da, const float* __restrict__ bias, const Strides st, int height,
+    int width, const float* __restrict__ grad_out, float* __restrict__ grad_uv,
+    float* __restrict__ grad_uv_da, float* __restrict__ grad_bias, const GradLayout gst,
+    long long tiles_x, long long tiles_per_view, long long tiles) {
+  constexpr int NC = RGB ? 3 : 4;
+  __shared__ HotQuad hot[8][2];
+  const int warp = threadIdx.x >> 5;
+  const bool leader = (threadIdx.x & 31u) == 0u;
+  if (leader) hot[warp][0].level = hot[warp][1].level = -1;
+  __syncwarp();
+  int held = 0;
+  bool pending = false;
+  for (long long tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    const long long view = tile / tiles_per_view;
+    const long long in_view = tile - view * tiles_per_view;
+    const long long ty = in_view / tiles_x;
+    const int col = static_cast<int>((in_view - ty * tiles_x) * 16) + (threadIdx.x & 15);
+    const int row = static_cast<int>(ty * 16) + (threadIdx.x >> 4);
+    texture_bwd_tile<MODE, B, RGB>(L, channels, grad_stride, uv, uv_da, bias, st, height, width,
+                                   grad_out, grad_uv, grad_uv_da, grad_bias, gst, col, row, view,
+                                   hot[warp][held], hot[warp][held ^ 1], pending);
+    if (pending) {  // lane 0 only: the new quad replaces the held one
+      flush_quad<NC>(L, hot[warp][held], channels, grad_stride);
+      held ^= 1;
+      pending = false;
+    }
+  }
+  __syncwarp();
+  if (leader) flush_quad<NC>(L, hot[warp][held], channels, grad_stride);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -942,10 +1037,21 @@ void launch_bwd(const Levels& L, int channels, int grad_stride, const float* uv,
                 const float* uv_da, const float* bias, Strides st, int batch, int height,
                 int width, const float* grad_out, float* grad_uv, float* grad_uv_da,
                 float* grad_bias, GradLayout gst, cudaStream_t s) {
-  const dim3 grid((width + 15) / 16, (height + 15) / 16, batch);
-  texture_bwd_kernel<MODE, B><<<grid, 256, 0, s>>>(L, channels, grad_stride, uv, uv_da, bias, st,
-                                                  height, width, grad_out, grad_uv, grad_uv_da,
-                                                  grad_bias, gst);
+  const long long tiles_x = (width + 15) / 16;
+  const long long tiles_per_view = tiles_x * ((height + 15) / 16);
+  const long long tiles = tiles_per_view * batch;
+  constexpr bool quads = B != DR_BOUNDARY_CUBE && MODE != DR_FILTER_NEAREST;
+  auto launch = [&](auto kernel) {
+    const long long grid = min(tiles, static_cast<long long>(resident_blocks(kernel, 256)));
+    kernel<<<static_cast<unsigned>(grid), 256, 0, s>>>(L, channels, grad_stride, uv, uv_da, bias,
+                                                      st, height, width, grad_out, grad_uv,
+                                                      grad_uv_da, grad_bias, gst, tiles_x,
+                                                      tiles_per_view, tiles);
+  };
+  if (quads && channels == 3 && grad_stride == 4)
+    launch(texture_bwd_kernel<MODE, B, quads>);
+  else
+    launch(texture_bwd_kernel<MODE, B, false>);
 }
 
 template <int B, typename F>
