@@ -6,8 +6,11 @@ Workload (synthetic, seeded): icosphere level 8 (655,362 vertices, 1,310,720 tri
 N(0, 0.01) radial displacement, 64 random orbit cameras at 1024x1024, interpolation of
 [u, v, nx, ny, nz] with all derivatives, a 4096x4096x3 uniform texture sampled trilinearly
 (its mip chain rebuilt every step, as the texture requires gradients), antialiasing, MSE against
-a random target, backward to the texture and the clip-space positions. The 64 views are sharded
-across the ranks (strong scaling); the texture gradient is summed with an NCCL all-reduce.
+a random target, backward to the texture and the world-space vertex positions. The mesh and the
+texture are parameters resident on the GPU; each step's inputs are the cameras' matrices and the
+target images, and the step starts with the world-to-clip transform (``to_clip``). The 64 views
+are sharded across the ranks (strong scaling); the texture and position gradients are summed with
+NCCL all-reduces.
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
 
@@ -41,7 +44,8 @@ ATTR_CHANNELS, DIFF_CHANNELS, TEX_CHANNELS = 5, 5, 3
 LAUNCHES = {
     "raster_visibility": 2, "resolve_fwd": 1, "resolve_bwd": 1, "interpolate_fwd": 1,
     "interpolate_bwd": 1, "texture_fwd": 1, "texture_bwd": 1, "mip_build": 1, "mip_adjoint": 1,
-    "edge_neighbours": 2, "antialias_fwd": 1, "antialias_bwd": 1,
+    "edge_neighbours": 2, "antialias_fwd": 1, "antialias_bwd": 1, "to_clip_fwd": 1,
+    "to_clip_bwd": 1,
 }  # fmt: skip
 
 
@@ -53,8 +57,9 @@ def stage_bytes(pixels: int, num_vert: int, views: int, stack_bytes: int, tex_by
     interpolate reads rast, rast_db (32) and writes 4C + 8D, backward reads 4C + 8D + 32 and writes
     32; texture reads uv, uv_da (24) and writes 4Ct, backward reads 4Ct + 24 and writes 24;
     antialias reads colour and rast (4Ct + 16) and writes 4Ct, backward reads 8Ct + 16 and writes
-    4Ct. Per call: positions (16 B per vertex and view) for the rasterizer, the mip stack for the
-    build and its adjoint.
+    4Ct. Per call: clip positions (16 B per vertex and view) for the rasterizer and the transform
+    that writes them (its backward reads their gradient), the mip stack for the build and its
+    adjoint.
     """
     c, d, ct = ATTR_CHANNELS, DIFF_CHANNELS, TEX_CHANNELS
     pos_bytes = views * num_vert * 16
@@ -70,6 +75,8 @@ def stage_bytes(pixels: int, num_vert: int, views: int, stack_bytes: int, tex_by
         "mip_adjoint": 2 * stack_bytes + tex_bytes,
         "interpolate_bwd": pixels * (64 + 4 * c + 8 * d),
         "resolve_bwd": pixels * (8 + 32) + 2 * pos_bytes,
+        "to_clip_fwd": pos_bytes + num_vert * 12,
+        "to_clip_bwd": pos_bytes + num_vert * 24,
     }
 
 
@@ -78,7 +85,7 @@ def step_bytes(pixels, num_vert, views, stack_bytes, tex_bytes) -> int:
     c, d, ct = ATTR_CHANNELS, DIFF_CHANNELS, TEX_CHANNELS
     per_px = 32 + (32 + 4 * c + 8 * d) + (24 + 4 * ct) + (16 + 8 * ct)
     per_px += (16 + 12 * ct) + (48 + 4 * ct) + (64 + 4 * c + 8 * d) + 32
-    return pixels * per_px + views * num_vert * 16 * 5 + 3 * stack_bytes
+    return pixels * per_px + views * num_vert * 16 * 7 + num_vert * 36 + 3 * stack_bytes
 
 
 class ClockSampler:
@@ -211,10 +218,10 @@ def build_scene(views_total: int, res: int, subdiv: int, tex_size: int, rank: in
 
     sc = scenes.config5_scene(views=views_total, resolution=res, subdivisions=subdiv, tex_size=tex_size)
     shard = view_shard(views_total, rank, world)
-    pos = sc["pos"][shard].contiguous()
+    mvp = sc["mvp"][shard].contiguous()
     gen = torch.Generator().manual_seed(1234)
     target = torch.rand(views_total, res, res, TEX_CHANNELS, generator=gen)[shard]
-    return pos, sc["tri"], sc["attr"], sc["tex"], target.contiguous()
+    return sc["world"].contiguous(), mvp, sc["tri"], sc["attr"], sc["tex"], target.contiguous()
 
 
 def run_ours(args) -> None:
@@ -234,27 +241,30 @@ def run_ours(args) -> None:
     if args.views % world:
         raise SystemExit(f"--views {args.views} must be divisible by the number of GPUs {world}")
 
-    pos_cpu, tri_cpu, attr_cpu, tex_cpu, target_cpu = build_scene(
+    world_cpu, mvp_cpu, tri_cpu, attr_cpu, tex_cpu, target_cpu = build_scene(
         args.views, args.res, args.subdiv, args.tex, rank, world)
-    views, res = pos_cpu.shape[0], args.res
+    views, res = mvp_cpu.shape[0], args.res
     ctx = dr.RasterizeContext(dev)
     tri = tri_cpu.to(dev)
     attr = attr_cpu.to(dev)
     tex = tex_cpu.to(dev).requires_grad_(True)
-    pos = pos_cpu.to(dev).requires_grad_(True)
+    verts = world_cpu.to(dev).requires_grad_(True)
+    mvp = mvp_cpu.to(dev)
     target = target_cpu.to(dev)
     topo = dr.antialias_construct_topology_hash(tri)
     # The texture gradient's all-reduce starts as soon as the texture backward has produced it and
-    # overlaps the interpolation and rasterization backward passes (no-op on one GPU).
-    reducer = OverlappedGradientSum([tex])
+    # overlaps the interpolation and rasterization backward passes; the positions' follows the
+    # transform's backward at the end of the step (no-ops on one GPU).
+    reducer = OverlappedGradientSum([tex, verts])
 
-    def step(pos_in, target_in):
-        pos_in.grad = None
+    def step(mvp_in, target_in):
+        verts.grad = None
         tex.grad = None
-        rast, rast_db = dr.rasterize(ctx, pos_in, tri, (res, res))
+        pos = dr.to_clip(verts, mvp_in)
+        rast, rast_db = dr.rasterize(ctx, pos, tri, (res, res))
         out, out_da = dr.interpolate(attr, rast, tri, rast_db=rast_db, diff_attrs="all")
         color = dr.texture(tex, out[..., 0:2], out_da[..., 0:4], filter_mode="linear-mipmap-linear")
-        image = dr.antialias(color, rast, pos_in, tri, topology_hash=topo)
+        image = dr.antialias(color, rast, pos, tri, topology_hash=topo)
         # Mean over the whole job's pixels, so that the ranks' gradients sum to the full batch's.
         loss = torch.nn.functional.mse_loss(image, target_in, reduction="sum") / (
             args.views * res * res * TEX_CHANNELS)
@@ -263,7 +273,7 @@ def run_ours(args) -> None:
         return loss
 
     for _ in range(args.warmup):
-        step(pos, target)
+        step(mvp, target)
     torch.cuda.synchronize()
 
     def timed_loop(body):
@@ -285,7 +295,7 @@ def run_ours(args) -> None:
 
     with ClockSampler(gpu_id(dev)) as clocks:
         with K.record_timings() as stages:
-            ms = timed_loop(lambda: step(pos, target))
+            ms = timed_loop(lambda: step(mvp, target))
         torch.cuda.synchronize()
     stage_ms = {name: sum(s.elapsed_time(e) for s, e in pairs) / args.steps for name, pairs in stages.items()}
     stage_calls = {name: len(pairs) / args.steps for name, pairs in stages.items()}
@@ -294,9 +304,9 @@ def run_ours(args) -> None:
     # and its loss is read back, all inside the timed region. As an input pipeline would, the copy
     # of step i + 1's inputs runs on a side stream (into the other of two device buffers) while
     # step i computes; the first step's copy is not overlapped.
-    pos_host = pos_cpu.pin_memory()
+    mvp_host = mvp_cpu.pin_memory()
     target_host = target_cpu.pin_memory()
-    buffers = [(torch.empty_like(pos_cpu, device=dev), torch.empty_like(target_cpu, device=dev))
+    buffers = [(torch.empty_like(mvp_cpu, device=dev), torch.empty_like(target_cpu, device=dev))
                for _ in range(2)]
     copy_stream = torch.cuda.Stream(dev)
     ready = [torch.cuda.Event() for _ in range(2)]
@@ -305,7 +315,7 @@ def run_ours(args) -> None:
     def upload(slot):
         with torch.cuda.stream(copy_stream):
             copy_stream.wait_event(free[slot])  # the step that last read this buffer is done
-            buffers[slot][0].copy_(pos_host, non_blocking=True)
+            buffers[slot][0].copy_(mvp_host, non_blocking=True)
             buffers[slot][1].copy_(target_host, non_blocking=True)
             ready[slot].record(copy_stream)
 
@@ -319,8 +329,8 @@ def run_ours(args) -> None:
             main.wait_event(ready[slot])
             if i + 1 < args.steps:
                 upload(1 - slot)
-            pos_in, target_in = buffers[slot]
-            loss = step(pos_in.detach().requires_grad_(True), target_in)
+            mvp_in, target_in = buffers[slot]
+            loss = step(mvp_in, target_in)
             free[slot].record(main)
             loss.item()
 
@@ -350,7 +360,8 @@ def run_ours(args) -> None:
     tex_bytes = tex.numel() * 4
     stack_bytes = int(tex_bytes * 4 / 3)
     pixels = views * res * res
-    algo = stage_bytes(pixels, pos.shape[1], views, stack_bytes - tex_bytes, tex_bytes)
+    num_vert = verts.shape[0]
+    algo = stage_bytes(pixels, num_vert, views, stack_bytes - tex_bytes, tex_bytes)
     dominant = max(stage_ms, key=stage_ms.get)
     per_launch_ms = stage_ms[dominant] / max(1.0, stage_calls[dominant])
     # Stages launched several times per step (one mip level per launch) are costed per step.
@@ -377,11 +388,13 @@ def run_ours(args) -> None:
                         f"({tri.shape[0]} tris), tex {args.tex}^2x3 linear-mipmap-linear, antialias, "
                         "MSE, fwd+bwd to tex and pos",
             "views": args.views, "resolution": res, "triangles": int(tri.shape[0]),
-            "vertices": int(pos.shape[1]), "tex": args.tex, "parallelism": f"views sharded dp{world}",
-            "l2": "inputs larger than L2 (pos 671 MB, rast 1 GB per step), no flush",
+            "vertices": num_vert, "tex": args.tex, "parallelism": f"views sharded dp{world}",
+            "inputs": "per step: the views' 4x4 camera matrices and target images; mesh (world "
+                      "positions) and texture are parameters resident on the GPU",
+            "l2": "working set larger than L2 (clip positions 671 MB, rast 1 GB per step), no flush",
         },
         "e2e": {"value": round(e2e_value, 1), "unit": UNIT,
-                "h2d_bytes_per_step": pos_cpu.numel() * 4 + target_cpu.numel() * 4,
+                "h2d_bytes_per_step": mvp_cpu.numel() * 4 + target_cpu.numel() * 4,
                 "d2h_bytes_per_step": 4},
         "gpu_launches": int(round(launches * args.steps)),
         "roofline": {
@@ -394,8 +407,8 @@ def run_ours(args) -> None:
             "ms_per_launch": round(per_launch_ms, 4),
         },
         "step_roofline": {
-            "algorithmic_bytes": step_bytes(pixels, pos.shape[1], views, stack_bytes - tex_bytes, tex_bytes),
-            "frac_of_peak": round(step_bytes(pixels, pos.shape[1], views, stack_bytes - tex_bytes,
+            "algorithmic_bytes": step_bytes(pixels, num_vert, views, stack_bytes - tex_bytes, tex_bytes),
+            "frac_of_peak": round(step_bytes(pixels, num_vert, views, stack_bytes - tex_bytes,
                                              tex_bytes) / (ms / 1e3) / 1e9 / peak, 4),
         },
         "stages_ms": {k: round(v, 3) for k, v in sorted(stage_ms.items(), key=lambda kv: -kv[1])},
@@ -412,13 +425,15 @@ def cpu_sample(args):
     """A bounded CPU sample of the workload: one view of the same scene at a small resolution."""
     import oracle
 
-    pos, tri, attr, tex, _ = build_scene(1, args.cpu_res, args.subdiv, args.tex, 0, 1)
+    world, mvp, tri, attr, tex, _ = build_scene(1, args.cpu_res, args.subdiv, args.tex, 0, 1)
     target = torch.rand(1, args.cpu_res, args.cpu_res, 3, generator=torch.Generator().manual_seed(7))
     res = (args.cpu_res, args.cpu_res)
 
     def step():
-        p = pos.clone().requires_grad_(True)
+        w = world.clone().requires_grad_(True)
         t = tex.clone().requires_grad_(True)
+        # World to clip as diffrast's examples do it (examples/common.py:320-323).
+        p = torch.nn.functional.pad(w, (0, 1), value=1.0) @ mvp.transpose(-1, -2)
         rast, rast_db = oracle.rasterize(p, tri, res)
         out, out_da = oracle.interpolate(attr, rast, tri, rast_db, list(range(5)))
         color = oracle.texture(t, out[..., 0:2].contiguous(), out_da[..., 0:4].contiguous(), None,
@@ -441,7 +456,7 @@ def cpu_baseline(args, warmup: int, steps: int) -> dict:
         step()
     sec = (time.perf_counter() - t0) / steps
     return {
-        "value": round(res[0] * res[1] / sec / 1e6, 6),
+        "value": float(f"{res[0] * res[1] / sec / 1e6:.4g}"),
         "unit": UNIT,
         "cores": torch.get_num_threads(),
         "kind": "port",

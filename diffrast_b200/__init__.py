@@ -1,7 +1,8 @@
 """diffrast_b200: diffrast's differentiable render path on hand-written B200 (sm_100a) kernels.
 
 The public names are those of ``diffrast`` (``src/diffrast/__init__.py:21-41``): switching is
-changing the import (``import diffrast_b200 as dr``, or ``diffrast_b200.torch``).
+changing the import (``import diffrast_b200 as dr``, or ``diffrast_b200.torch``). ``to_clip`` is an
+addition: the world-to-clip transform of diffrast's examples as a CUDA kernel pair.
 """
 
 from diffrast_b200.backends import get_backend_name, set_backend
@@ -21,6 +22,7 @@ from diffrast_b200.ops import (
     rasterize,
     texture,
     texture_construct_mip,
+    to_clip,
 )
 from diffrast_b200.peeling import DepthPeeler
 from diffrast_b200.topology import TopologyHash
@@ -47,6 +49,7 @@ __all__ = [
     "set_log_level",
     "texture",
     "texture_construct_mip",
+    "to_clip",
     "uninstall_as_diffrast",
     "uninstall_as_nvdiffrast",
 ]

@@ -272,3 +272,21 @@ class Antialias(torch.autograd.Function):
         grad_color, grad_pos = K.antialias_bwd(color, rast, pos3, tri, opposite,
                                                grad_out.contiguous(), ctx.boost, pairs)
         return grad_color, None, grad_pos.view(ctx.pos_shape), None, None, None
+
+
+class ToClip(torch.autograd.Function):
+    """World-to-clip transform of shared positions by per-view matrices."""
+
+    @staticmethod
+    def forward(ctx, positions: Tensor, matrix: Tensor):
+        clip = K.to_clip_fwd(positions, matrix)
+        ctx.save_for_backward(_saveable(positions), _saveable(matrix))
+        return clip
+
+    @staticmethod
+    @first_order("to_clip")
+    def backward(ctx, grad_clip):
+        positions, matrix = ctx.saved_tensors
+        grad_p, grad_m = K.to_clip_bwd(K.aligned(grad_clip), positions, matrix,
+                                       ctx.needs_input_grad[0], ctx.needs_input_grad[1])
+        return grad_p, grad_m

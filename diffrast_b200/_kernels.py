@@ -426,3 +426,31 @@ def antialias_bwd(color, rast, pos3, tri, opposite, grad_out, boost, pairs=None)
         "dr_antialias_bwd",
     )  # fmt: skip
     return grad_color, grad_pos
+
+
+@timed("to_clip_fwd")
+def to_clip_fwd(positions: Tensor, matrix: Tensor) -> Tensor:
+    """``[batch, V, 4]`` clip positions of ``positions`` ``[V, 3]`` under ``matrix``
+    ``[batch, 4, 4]``."""
+    clip = torch.empty((matrix.shape[0], positions.shape[0], 4), dtype=torch.float32,
+                       device=positions.device)
+    N.check(
+        N.lib().dr_to_clip_fwd(positions.data_ptr(), positions.shape[0], matrix.data_ptr(),
+                               matrix.shape[0], clip.data_ptr(), N.stream(positions.device)),
+        "dr_to_clip_fwd",
+    )  # fmt: skip
+    return clip
+
+
+@timed("to_clip_bwd")
+def to_clip_bwd(grad_clip: Tensor, positions: Tensor, matrix: Tensor, want_positions: bool,
+                want_matrix: bool) -> tuple[Tensor | None, Tensor | None]:
+    grad_p = torch.empty_like(positions) if want_positions else None
+    grad_m = torch.empty_like(matrix) if want_matrix else None
+    N.check(
+        N.lib().dr_to_clip_bwd(grad_clip.data_ptr(), positions.data_ptr(), positions.shape[0],
+                               matrix.data_ptr(), matrix.shape[0], N.ptr(grad_p), N.ptr(grad_m),
+                               N.stream(positions.device)),
+        "dr_to_clip_bwd",
+    )  # fmt: skip
+    return grad_p, grad_m

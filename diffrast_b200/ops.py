@@ -479,6 +479,29 @@ def antialias_construct_topology_hash(tri: Tensor) -> TopologyHash:
 
 
 # ---------------------------------------------------------------------------------------------
+# world-to-clip transform
+# ---------------------------------------------------------------------------------------------
+
+
+def to_clip(positions: Tensor, matrix: Tensor) -> Tensor:
+    """Transform ``[vertices, 3]`` positions by ``[batch, 4, 4]`` matrices to clip space.
+
+    Returns ``[batch, vertices, 4]``, the homogeneous positions ``(x, y, z, 1)`` times the
+    transposed matrices, as diffrast's examples compute it with a matmul (examples/common.py:
+    320-323); differentiable in both inputs. One shared vertex buffer seen by many cameras thus
+    gets a single gradient, summed over the views (and ready for an all-reduce across ranks).
+    """
+    _check(positions, "positions", ndim=2, last=3, dtype=torch.float32, layout="[vertices, 3]")
+    _check(matrix, "matrix", ndim=3, dtype=torch.float32, layout="[batch, 4, 4]")
+    if matrix.shape[1:] != (4, 4):
+        raise ValueError(f"matrix must have shape [batch, 4, 4], got {tuple(matrix.shape)}.")
+    _check_devices(positions=positions, matrix=matrix)
+    require_cuda(positions.device)
+    with torch.cuda.device(positions.device):
+        return F.ToClip.apply(positions.contiguous(), matrix.contiguous())
+
+
+# ---------------------------------------------------------------------------------------------
 # validation helpers (messages as in diffrast ops.py:511-638)
 # ---------------------------------------------------------------------------------------------
 

@@ -247,6 +247,21 @@ int dr_antialias_bwd(const float* color, const float* rast, const float* pos, in
                      const void* pairs, size_t pair_bytes, float* grad_color, float* grad_pos,
                      void* stream);
 
+/* ---- World-to-clip transform (the step ahead of the rasterizer in a multi-view fit) -------- */
+
+/* clip [batch, num_vert, 4] = matrices [batch, 4, 4] (row-major) applied to the homogeneous
+ * positions (p, 1), p [num_vert, 3]: diffrast examples/common.py:320-323 (to_clip), which the
+ * reference computes with a torch matmul. clip must be 16-byte aligned. */
+int dr_to_clip_fwd(const float* positions, int64_t num_vert, const float* matrices, int64_t batch,
+                   float* clip, void* stream);
+
+/* Gradients of dr_to_clip_fwd from grad_clip [batch, num_vert, 4] (16-byte aligned):
+ * grad_positions [num_vert, 3] (written; sums over the views) and grad_matrices [batch, 4, 4]
+ * (written). Either may be NULL. */
+int dr_to_clip_bwd(const float* grad_clip, const float* positions, int64_t num_vert,
+                   const float* matrices, int64_t batch, float* grad_positions,
+                   float* grad_matrices, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -205,7 +205,8 @@ def config5_scene(views=64, resolution=1024, subdivisions=8, tex_size=4096, seed
     pos = to_clip(world, mvp)
     attr = torch.cat([spherical_uv(verts), normals], -1).contiguous()
     tex = torch.rand(1, tex_size, tex_size, 3, generator=gen)
-    return dict(pos=pos, tri=tri, attr=attr, tex=tex, resolution=(resolution, resolution), gen=gen)
+    return dict(pos=pos, tri=tri, attr=attr, tex=tex, resolution=(resolution, resolution), gen=gen,
+                world=world, mvp=mvp)
 
 
 # Reduced versions of BASELINE configs 2-5 for parity tests against the CPU oracle: the same

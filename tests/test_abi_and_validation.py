@@ -143,3 +143,16 @@ def test_contexts_and_compat():
     dr.set_log_level(2)
     assert dr.get_log_level() == 2
     dr.set_log_level(1)
+
+
+def test_to_clip_validation():
+    p = torch.zeros(5, 3)
+    m = torch.zeros(2, 4, 4)
+    with pytest.raises(ValueError, match=r"positions must have shape \[vertices, 3\]"):
+        dr.to_clip(torch.zeros(5, 4), m)
+    with pytest.raises(ValueError, match=r"matrix must have shape \[batch, 4, 4\]"):
+        dr.to_clip(p, torch.zeros(2, 3, 4))
+    with pytest.raises(TypeError, match="positions must be torch.float32"):
+        dr.to_clip(p.double(), m)
+    with pytest.raises(RuntimeError, match="CUDA devices only"):
+        dr.to_clip(p, m)
