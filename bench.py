@@ -264,10 +264,11 @@ def run_ours(args) -> None:
         rast, rast_db = dr.rasterize(ctx, pos, tri, (res, res))
         out, out_da = dr.interpolate(attr, rast, tri, rast_db=rast_db, diff_attrs="all")
         color = dr.texture(tex, out[..., 0:2], out_da[..., 0:4], filter_mode="linear-mipmap-linear")
-        image = dr.antialias(color, rast, pos, tri, topology_hash=topo)
-        # Mean over the whole job's pixels, so that the ranks' gradients sum to the full batch's.
-        loss = torch.nn.functional.mse_loss(image, target_in, reduction="sum") / (
-            args.views * res * res * TEX_CHANNELS)
+        # Antialias and the MSE against the target in one pass (dr.antialias_mse fuses the loss
+        # into the antialias kernels); the mean runs over the whole job's pixels, so that the
+        # ranks' gradients sum to the full batch's.
+        _, loss = dr.antialias_mse(color, rast, pos, tri, target_in, topology_hash=topo,
+                                   scale=1.0 / (args.views * res * res * TEX_CHANNELS))
         loss.backward()
         reducer.wait()
         return loss

@@ -1,8 +1,9 @@
 """diffrast_b200: diffrast's differentiable render path on hand-written B200 (sm_100a) kernels.
 
 The public names are those of ``diffrast`` (``src/diffrast/__init__.py:21-41``): switching is
-changing the import (``import diffrast_b200 as dr``, or ``diffrast_b200.torch``). ``to_clip`` is an
-addition: the world-to-clip transform of diffrast's examples as a CUDA kernel pair.
+changing the import (``import diffrast_b200 as dr``, or ``diffrast_b200.torch``). ``to_clip`` (the
+world-to-clip transform of diffrast's examples) and ``antialias_mse`` (antialias with a fused
+squared-error loss) are additions.
 """
 
 from diffrast_b200.backends import get_backend_name, set_backend
@@ -18,6 +19,7 @@ from diffrast_b200.ops import (
     MipStack,
     antialias,
     antialias_construct_topology_hash,
+    antialias_mse,
     interpolate,
     rasterize,
     texture,
@@ -39,6 +41,7 @@ __all__ = [
     "__version__",
     "antialias",
     "antialias_construct_topology_hash",
+    "antialias_mse",
     "get_backend_name",
     "get_log_level",
     "install_as_diffrast",

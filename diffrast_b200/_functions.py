@@ -274,6 +274,34 @@ class Antialias(torch.autograd.Function):
         return grad_color, None, grad_pos.view(ctx.pos_shape), None, None, None
 
 
+class AntialiasMSE(torch.autograd.Function):
+    """Antialias with the squared-error loss ``scale * sum (out - target)^2`` fused into its
+    passes; returns ``(out, loss)``."""
+
+    @staticmethod
+    def forward(ctx, color: Tensor, rast: Tensor, pos: Tensor, tri: Tensor, opposite: Tensor,
+                target: Tensor, scale: float, boost: float):
+        pos3 = pos if pos.ndim == 3 else pos[None]
+        out, residual, pairs, partial = K.antialias_mse_fwd(color, rast, pos3, tri, opposite, target)
+        loss = partial.sum() * scale
+        ctx.set_materialize_grads(False)
+        saved = (color, rast, pos3, tri, opposite, pairs, residual)
+        ctx.save_for_backward(*(_saveable(t) for t in saved))
+        ctx.scale, ctx.boost, ctx.pos_shape = scale, boost, pos.shape
+        return out, loss
+
+    @staticmethod
+    @first_order("antialias_mse")
+    def backward(ctx, grad_out, grad_loss):
+        color, rast, pos3, tri, opposite, pairs, residual = ctx.saved_tensors
+        if grad_loss is None:
+            grad_loss = torch.zeros((), dtype=torch.float32, device=color.device)
+        grad_color, grad_pos = K.antialias_mse_bwd(
+            color, rast, pos3, tri, opposite, residual, grad_loss.detach().float().contiguous(),
+            ctx.scale, None if grad_out is None else grad_out.contiguous(), ctx.boost, pairs)
+        return grad_color, None, grad_pos.view(ctx.pos_shape), None, None, None, None, None
+
+
 class ToClip(torch.autograd.Function):
     """World-to-clip transform of shared positions by per-view matrices."""
 

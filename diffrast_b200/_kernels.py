@@ -454,3 +454,47 @@ def to_clip_bwd(grad_clip: Tensor, positions: Tensor, matrix: Tensor, want_posit
         "dr_to_clip_bwd",
     )  # fmt: skip
     return grad_p, grad_m
+
+
+@timed("antialias_fwd")
+def antialias_mse_fwd(color, rast, pos3, tri, opposite, target):
+    """Antialiased colour, the residual out - target, the pair records and the per-block partial
+    sums of the squared residual."""
+    batch, height, width, channels = color.shape
+    lib = N.lib()
+    out = torch.empty_like(color)
+    residual = torch.empty_like(color)
+    pairs = torch.empty(lib.dr_antialias_pair_bytes(batch, height, width), dtype=torch.uint8,
+                        device=color.device)
+    partial = torch.zeros(max(1, lib.dr_antialias_loss_partials(batch, height, width)),
+                          dtype=torch.float32, device=color.device)
+    N.check(
+        lib.dr_antialias_mse_fwd(color.data_ptr(), rast.data_ptr(), pos3.data_ptr(), pos3.shape[0],
+                                 pos3.shape[1], tri.data_ptr(), tri.shape[0], opposite.data_ptr(),
+                                 batch, height, width, channels, target.data_ptr(), out.data_ptr(),
+                                 residual.data_ptr(), pairs.data_ptr(), pairs.numel(), partial.data_ptr(),
+                                 partial.numel(), N.stream(color.device)),
+        "dr_antialias_mse_fwd",
+    )  # fmt: skip
+    return out, residual, pairs, partial
+
+
+@timed("antialias_bwd")
+def antialias_mse_bwd(color, rast, pos3, tri, opposite, residual, loss_grad, scale, grad_out, boost,
+                      pairs):
+    """Gradients of colour and positions of ``scale * sum (out - target)^2`` (upstream gradient
+    ``loss_grad``, a device scalar) plus ``grad_out`` (the output's own gradient, or None)."""
+    batch, height, width, channels = color.shape
+    grad_color = torch.empty_like(color)
+    grad_pos = torch.zeros_like(pos3)
+    N.check(
+        N.lib().dr_antialias_mse_bwd(color.data_ptr(), rast.data_ptr(), pos3.data_ptr(),
+                                     pos3.shape[0], pos3.shape[1], tri.data_ptr(), tri.shape[0],
+                                     opposite.data_ptr(), batch, height, width, channels,
+                                     residual.data_ptr(), loss_grad.data_ptr(), float(scale),
+                                     N.ptr(grad_out), float(boost), pairs.data_ptr(),
+                                     pairs.numel(), grad_color.data_ptr(), grad_pos.data_ptr(),
+                                     N.stream(color.device)),
+        "dr_antialias_mse_bwd",
+    )  # fmt: skip
+    return grad_color, grad_pos

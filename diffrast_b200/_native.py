@@ -83,6 +83,17 @@ _SIGNATURES = {
         [_P, _P, _P, c_int64, c_int64, _P, c_int64, _P, c_int64, c_int32, c_int32, c_int32, _P,
          c_float, _P, c_size_t, _P, _P, _P],
     ),
+    "dr_antialias_loss_partials": (c_size_t, [c_int64, c_int32, c_int32]),
+    "dr_antialias_mse_fwd": (
+        c_int,
+        [_P, _P, _P, c_int64, c_int64, _P, c_int64, _P, c_int64, c_int32, c_int32, c_int32, _P,
+         _P, _P, _P, c_size_t, _P, c_size_t, _P],
+    ),
+    "dr_antialias_mse_bwd": (
+        c_int,
+        [_P, _P, _P, c_int64, c_int64, _P, c_int64, _P, c_int64, c_int32, c_int32, c_int32, _P,
+         _P, c_float, _P, c_float, _P, c_size_t, _P, _P, _P],
+    ),
     "dr_to_clip_fwd": (c_int, [_P, c_int64, _P, c_int64, _P, _P]),
     "dr_to_clip_bwd": (c_int, [_P, _P, c_int64, _P, c_int64, _P, _P, _P]),
 }

@@ -325,9 +325,21 @@ __device__ __forceinline__ int owner_vertex(const AaCtx& a, int owner, int edge,
   return __ldg(a.tri + 3 * static_cast<long long>(owner) + (edge + k) % 3);
 }
 
+// Squared-error loss fused into the antialias passes: the forward pass writes the residual
+// out - target and adds up its squares per block into partial[block]; the backward pass takes the
+// upstream gradient grad_out (when given) plus s residual, s = 2 scale dL.
+struct FusedLoss {
+  const float* target;
+  float* residual;
+  float* partial;
+};
+
+// One block per 30 x 14 output pixels of a view (a 32 x 16 thread tile with a one-pixel halo).
+template <bool kLoss>
 __global__ void __launch_bounds__(kFwdX * kFwdY, 3) aa_fwd_kernel(const AaCtx a,
                                                                    float* __restrict__ out,
-                                                                   PairRecords rec) {
+                                                                   PairRecords rec,
+                                                                   FusedLoss loss) {
   __shared__ int s_id[kFwdY][kFwdX];
   __shared__ float s_z[kFwdY][kFwdX];
   __shared__ float s_t[4][kFwdY][kFwdX];
@@ -399,57 +411,79 @@ __global__ void __launch_bounds__(kFwdX * kFwdY, 3) aa_fwd_kernel(const AaCtx a,
     s_t[d][ty][tx] = tc[d];
   }
   __syncthreads();
-  if (!in_image || !out_row || !out_col) return;
-  const PairOutcome right =
-      col + 1 < a.width
-          ? decide_pair(id, s_id[ty][tx + 1], z, s_z[ty][tx + 1], code[kRight], tc[kRight],
-                        s_c[kLeft][ty][tx + 1], s_t[kLeft][ty][tx + 1])
-          : decide_pair(0, 0, 0.f, 0.f, 0u, 0.f, 0u, 0.f);
-  const PairOutcome left =
-      col >= 1 ? decide_pair(s_id[ty][tx - 1], id, s_z[ty][tx - 1], z, s_c[kRight][ty][tx - 1],
-                             s_t[kRight][ty][tx - 1], code[kLeft], tc[kLeft])
-               : decide_pair(0, 0, 0.f, 0.f, 0u, 0.f, 0u, 0.f);
-  const PairOutcome down =
-      row + 1 < a.height
-          ? decide_pair(id, s_id[ty + 1][tx], z, s_z[ty + 1][tx], code[kDown], tc[kDown],
-                        s_c[kUp][ty + 1][tx], s_t[kUp][ty + 1][tx])
-          : decide_pair(0, 0, 0.f, 0.f, 0u, 0.f, 0u, 0.f);
-  const PairOutcome up =
-      row >= 1 ? decide_pair(s_id[ty - 1][tx], id, s_z[ty - 1][tx], z, s_c[kDown][ty - 1][tx],
-                             s_t[kDown][ty - 1][tx], code[kUp], tc[kUp])
-               : decide_pair(0, 0, 0.f, 0.f, 0u, 0.f, 0u, 0.f);
-  if (rec.code != nullptr) {
-    unsigned codes = 0u;
-    int4 verts = make_int4(0, 0, 0, 0);
-    if (right.active) {
-      codes = 8u | (right.use_p ? 4u : 0u) | static_cast<unsigned>(right.edge);
-      const int owner = right.use_p ? id : s_id[ty][tx + 1];
-      verts.x = owner_vertex(a, owner, right.edge, 1);
-      verts.y = owner_vertex(a, owner, right.edge, 2);
+  const bool emit = in_image && out_row && out_col;
+  if (!kLoss && !emit) return;
+  float sq = 0.0f;
+  if (emit) {
+    const PairOutcome right =
+        col + 1 < a.width
+            ? decide_pair(id, s_id[ty][tx + 1], z, s_z[ty][tx + 1], code[kRight], tc[kRight],
+                          s_c[kLeft][ty][tx + 1], s_t[kLeft][ty][tx + 1])
+            : decide_pair(0, 0, 0.f, 0.f, 0u, 0.f, 0u, 0.f);
+    const PairOutcome left =
+        col >= 1 ? decide_pair(s_id[ty][tx - 1], id, s_z[ty][tx - 1], z, s_c[kRight][ty][tx - 1],
+                               s_t[kRight][ty][tx - 1], code[kLeft], tc[kLeft])
+                 : decide_pair(0, 0, 0.f, 0.f, 0u, 0.f, 0u, 0.f);
+    const PairOutcome down =
+        row + 1 < a.height
+            ? decide_pair(id, s_id[ty + 1][tx], z, s_z[ty + 1][tx], code[kDown], tc[kDown],
+                          s_c[kUp][ty + 1][tx], s_t[kUp][ty + 1][tx])
+            : decide_pair(0, 0, 0.f, 0.f, 0u, 0.f, 0u, 0.f);
+    const PairOutcome up =
+        row >= 1 ? decide_pair(s_id[ty - 1][tx], id, s_z[ty - 1][tx], z, s_c[kDown][ty - 1][tx],
+                               s_t[kDown][ty - 1][tx], code[kUp], tc[kUp])
+                 : decide_pair(0, 0, 0.f, 0.f, 0u, 0.f, 0u, 0.f);
+    if (rec.code != nullptr) {
+      unsigned codes = 0u;
+      int4 verts = make_int4(0, 0, 0, 0);
+      if (right.active) {
+        codes = 8u | (right.use_p ? 4u : 0u) | static_cast<unsigned>(right.edge);
+        const int owner = right.use_p ? id : s_id[ty][tx + 1];
+        verts.x = owner_vertex(a, owner, right.edge, 1);
+        verts.y = owner_vertex(a, owner, right.edge, 2);
+      }
+      if (down.active) {
+        codes |= (8u | (down.use_p ? 4u : 0u) | static_cast<unsigned>(down.edge)) << 4;
+        const int owner = down.use_p ? id : s_id[ty + 1][tx];
+        verts.z = owner_vertex(a, owner, down.edge, 1);
+        verts.w = owner_vertex(a, owner, down.edge, 2);
+      }
+      rec.t[p] = make_float2(right.t, down.t);
+      rec.code[p] = static_cast<uint8_t>(codes);
+      // Edge vertices are read only for active pairs.
+      if (codes & 0x88u) rec.verts[p] = verts;
     }
-    if (down.active) {
-      codes |= (8u | (down.use_p ? 4u : 0u) | static_cast<unsigned>(down.edge)) << 4;
-      const int owner = down.use_p ? id : s_id[ty + 1][tx];
-      verts.z = owner_vertex(a, owner, down.edge, 1);
-      verts.w = owner_vertex(a, owner, down.edge, 2);
+    // Blend in the reference's accumulation order: right pair (this pixel first), left pair
+    // (second), lower pair (first), upper pair (second).
+    const float k[4] = {right.bp, left.bq, down.bp, up.bq};
+    const long long other[4] = {p + 1, p - 1, p + a.width, p - a.width};
+    const int C = a.channels;
+    for (int c = 0; c < C; ++c) {
+      const float self = __ldg(a.color + p * C + c);
+      float value = self;
+      for (int i = 0; i < 4; ++i) {
+        if (k[i] != 0.0f) value = add(value, mul(k[i], sub(__ldg(a.color + other[i] * C + c), self)));
+      }
+      out[p * C + c] = value;
+      if (kLoss) {
+        const float d = value - __ldg(loss.target + p * C + c);
+        loss.residual[p * C + c] = d;
+        sq = fmaf(d, d, sq);
+      }
     }
-    rec.t[p] = make_float2(right.t, down.t);
-    rec.code[p] = static_cast<uint8_t>(codes);
-    // Edge vertices are read only for active pairs.
-    if (codes & 0x88u) rec.verts[p] = verts;
   }
-  // Blend in the reference's accumulation order: right pair (this pixel first), left pair
-  // (second), lower pair (first), upper pair (second).
-  const float k[4] = {right.bp, left.bq, down.bp, up.bq};
-  const long long other[4] = {p + 1, p - 1, p + a.width, p - a.width};
-  const int C = a.channels;
-  for (int c = 0; c < C; ++c) {
-    const float self = __ldg(a.color + p * C + c);
-    float value = self;
-    for (int i = 0; i < 4; ++i) {
-      if (k[i] != 0.0f) value = add(value, mul(k[i], sub(__ldg(a.color + other[i] * C + c), self)));
+  if (kLoss) {
+    __shared__ float warp_sq[kFwdX * kFwdY / 32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    if ((threadIdx.x & 31u) == 0u) warp_sq[threadIdx.x >> 5] = sq;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float total = 0.0f;
+      for (int i = 0; i < kFwdX * kFwdY / 32; ++i) total += warp_sq[i];
+      loss.partial[(static_cast<long long>(blockIdx.z) * gridDim.y + blockIdx.y) * gridDim.x +
+                   blockIdx.x] = total;
     }
-    out[p * C + c] = value;
   }
 }
 
@@ -559,19 +593,35 @@ __device__ __forceinline__ void recorded_edge_gradient(const AaCtx& a, float* gr
   edge_gradient(a, grad_pos, pb, vi, vj, r, r.use_p ? g : -g);
 }
 
+// The upstream gradient of output element i: grad (when given) plus, with a fused squared-error
+// loss, s residual[i] with s = 2 scale dL.
+struct Upstream {
+  const float* grad;
+  const float* residual;
+  const float* loss_grad;  // device scalar dL
+  float scale2;
+};
+
+template <bool kLoss>
+__device__ __forceinline__ float upstream(const Upstream& u, float s, long long i) {
+  if (!kLoss) return u.grad[i];
+  const float g = u.grad != nullptr ? u.grad[i] : 0.0f;
+  return fmaf(s, __ldg(u.residual + i), g);
+}
+
 // Backward pass from the pairs recorded by the forward pass: one thread per pixel (grid: columns
 // in x, rows in y, views in z), no edge tests. Same arithmetic as aa_bwd_kernel for the colour
 // gradient and for the crossings of the pixel's own (right and lower) pairs, whose position
 // gradients it scatters. With K > 0 channels known at compile time, every input the pixel can
 // need is loaded up front, unconditionally, so that the loads overlap instead of each waiting for
-// the record that decides it; K = 0 handles any channel count.
-template <int K>
+// the record that decides it; K = 0 handles any channel count. With kLoss the upstream gradient
+// of the output is formed on the fly from the fused squared-error loss.
+template <int K, bool kLoss>
 __global__ void __launch_bounds__(256, 5) aa_bwd_recorded_kernel(const AaCtx a,
                                                               const float2* __restrict__ rec_t,
                                                               const uint8_t* __restrict__ rec_code,
                                                               const int4* __restrict__ rec_verts,
-                                                              const float* __restrict__ grad_out,
-                                                              float boost,
+                                                              const Upstream u, float boost,
                                                               float* __restrict__ grad_color,
                                                               float* __restrict__ grad_pos) {
   const int col = blockIdx.x * blockDim.x + threadIdx.x;
@@ -588,17 +638,18 @@ __global__ void __launch_bounds__(256, 5) aa_bwd_recorded_kernel(const AaCtx a,
   const float t_l = has_l ? __ldg(rec_t + p - 1).x : 0.f;
   const float t_u = has_u ? __ldg(rec_t + p - w).y : 0.f;
   const int4 verts = __ldg(rec_verts + p);
+  const float s = kLoss ? u.scale2 * __ldg(u.loss_grad) : 0.0f;
   const int C = K > 0 ? K : a.channels;
   constexpr int R = K > 0 ? K : 1;
   float gs[R], gl[R], gr[R], gu[R], gd[R], cs[R], cr[R], cd[R];
   if (K > 0) {
 #pragma unroll
     for (int c = 0; c < R; ++c) {
-      gs[c] = grad_out[p * C + c];
-      gl[c] = has_l ? grad_out[(p - 1) * C + c] : 0.f;
-      gr[c] = has_r ? grad_out[(p + 1) * C + c] : 0.f;
-      gu[c] = has_u ? grad_out[(p - w) * C + c] : 0.f;
-      gd[c] = has_d ? grad_out[(p + w) * C + c] : 0.f;
+      gs[c] = upstream<kLoss>(u, s, p * C + c);
+      gl[c] = has_l ? upstream<kLoss>(u, s, (p - 1) * C + c) : 0.f;
+      gr[c] = has_r ? upstream<kLoss>(u, s, (p + 1) * C + c) : 0.f;
+      gu[c] = has_u ? upstream<kLoss>(u, s, (p - w) * C + c) : 0.f;
+      gd[c] = has_d ? upstream<kLoss>(u, s, (p + w) * C + c) : 0.f;
       cs[c] = __ldg(a.color + p * C + c);
       cr[c] = has_r ? __ldg(a.color + (p + 1) * C + c) : 0.f;
       cd[c] = has_d ? __ldg(a.color + (p + w) * C + c) : 0.f;
@@ -612,11 +663,11 @@ __global__ void __launch_bounds__(256, 5) aa_bwd_recorded_kernel(const AaCtx a,
   for (int c = 0; c < C; ++c) {
     const int i = K > 0 ? c : 0;
     if (K == 0) {
-      gs[0] = grad_out[p * C + c];
-      gl[0] = has_l ? grad_out[(p - 1) * C + c] : 0.f;
-      gr[0] = has_r ? grad_out[(p + 1) * C + c] : 0.f;
-      gu[0] = has_u ? grad_out[(p - w) * C + c] : 0.f;
-      gd[0] = has_d ? grad_out[(p + w) * C + c] : 0.f;
+      gs[0] = upstream<kLoss>(u, s, p * C + c);
+      gl[0] = has_l ? upstream<kLoss>(u, s, (p - 1) * C + c) : 0.f;
+      gr[0] = has_r ? upstream<kLoss>(u, s, (p + 1) * C + c) : 0.f;
+      gu[0] = has_u ? upstream<kLoss>(u, s, (p - w) * C + c) : 0.f;
+      gd[0] = has_d ? upstream<kLoss>(u, s, (p + w) * C + c) : 0.f;
       cs[0] = __ldg(a.color + p * C + c);
       cr[0] = has_r ? __ldg(a.color + (p + 1) * C + c) : 0.f;
       cd[0] = has_d ? __ldg(a.color + (p + w) * C + c) : 0.f;
@@ -711,10 +762,44 @@ PairRecords pair_records(void* pairs, long long pixels) {
           reinterpret_cast<int4*>(p + align256(sizeof(float2) * n) + align256(n))};
 }
 
+template <bool kLoss>
+void launch_recorded(const AaCtx& a, const PairRecords& rec, const Upstream& u, float boost,
+                     float* grad_color, float* grad_pos, long long batch, cudaStream_t s) {
+  const dim3 grid((a.width + 255) / 256, a.height, static_cast<unsigned>(batch));
+  switch (a.channels) {
+    case 1:
+      aa_bwd_recorded_kernel<1, kLoss><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, u, boost,
+                                                            grad_color, grad_pos);
+      break;
+    case 3:
+      aa_bwd_recorded_kernel<3, kLoss><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, u, boost,
+                                                            grad_color, grad_pos);
+      break;
+    case 4:
+      aa_bwd_recorded_kernel<4, kLoss><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, u, boost,
+                                                            grad_color, grad_pos);
+      break;
+    default:
+      aa_bwd_recorded_kernel<0, kLoss><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, u, boost,
+                                                            grad_color, grad_pos);
+  }
+}
+
+dim3 fwd_grid(int64_t batch, int32_t height, int32_t width) {
+  return dim3((width + kFwdTileX - 1) / kFwdTileX, (height + kFwdTileY - 1) / kFwdTileY,
+              static_cast<unsigned>(batch));
+}
+
 }  // namespace
 }  // namespace dr
 
 using namespace dr;
+
+extern "C" size_t dr_antialias_loss_partials(int64_t batch, int32_t height, int32_t width) {
+  if (batch <= 0 || height <= 0 || width <= 0) return 0;
+  const dim3 g = fwd_grid(batch, height, width);
+  return static_cast<size_t>(g.x) * g.y * g.z;
+}
 
 extern "C" size_t dr_antialias_pair_bytes(int64_t batch, int32_t height, int32_t width) {
   if (batch < 0 || height < 0 || width < 0) return 0;
@@ -799,8 +884,60 @@ extern "C" int dr_antialias_fwd(const float* color, const float* rast, const flo
   const AaCtx a = make_ctx(color, rast, pos, pos_batch, num_vert, tri, num_tri, opposite, height,
                            width, channels);
   if (batch > 65535) return DR_ERR_TOO_LARGE;
-  const dim3 grid((width + kFwdTileX - 1) / kFwdTileX, (height + kFwdTileY - 1) / kFwdTileY, batch);
-  aa_fwd_kernel<<<grid, kFwdX * kFwdY, 0, as_stream(stream)>>>(a, out, pair_records(pairs, total));
+  aa_fwd_kernel<false><<<fwd_grid(batch, height, width), kFwdX * kFwdY, 0, as_stream(stream)>>>(
+      a, out, pair_records(pairs, total), FusedLoss{nullptr, nullptr, nullptr});
+  return launch_status();
+}
+
+extern "C" int dr_antialias_mse_fwd(const float* color, const float* rast, const float* pos,
+                                    int64_t pos_batch, int64_t num_vert, const int32_t* tri,
+                                    int64_t num_tri, const int32_t* opposite, int64_t batch,
+                                    int32_t height, int32_t width, int32_t channels,
+                                    const float* target, float* out, float* residual,
+                                    void* pairs, size_t pair_bytes, float* partial_sums,
+                                    size_t partial_count, void* stream) {
+  if (bad_aa_args(color, rast, pos, pos_batch, num_vert, tri, num_tri, opposite, batch, height,
+                  width, channels))
+    return DR_ERR_INVALID_ARGUMENT;
+  const long long total = batch * static_cast<long long>(height) * width;
+  if (total == 0 || channels == 0) return DR_OK;
+  if (out == nullptr || target == nullptr || residual == nullptr || pairs == nullptr ||
+      partial_sums == nullptr)
+    return DR_ERR_INVALID_ARGUMENT;
+  if (pair_bytes < pair_record_bytes(total) ||
+      partial_count < dr_antialias_loss_partials(batch, height, width))
+    return DR_ERR_WORKSPACE_TOO_SMALL;
+  if (batch > 65535) return DR_ERR_TOO_LARGE;
+  const AaCtx a = make_ctx(color, rast, pos, pos_batch, num_vert, tri, num_tri, opposite, height,
+                           width, channels);
+  aa_fwd_kernel<true><<<fwd_grid(batch, height, width), kFwdX * kFwdY, 0, as_stream(stream)>>>(
+      a, out, pair_records(pairs, total), FusedLoss{target, residual, partial_sums});
+  return launch_status();
+}
+
+extern "C" int dr_antialias_mse_bwd(const float* color, const float* rast, const float* pos,
+                                    int64_t pos_batch, int64_t num_vert, const int32_t* tri,
+                                    int64_t num_tri, const int32_t* opposite, int64_t batch,
+                                    int32_t height, int32_t width, int32_t channels,
+                                    const float* residual, const float* loss_grad, float scale,
+                                    const float* grad_out, float pos_gradient_boost,
+                                    const void* pairs, size_t pair_bytes, float* grad_color,
+                                    float* grad_pos, void* stream) {
+  if (bad_aa_args(color, rast, pos, pos_batch, num_vert, tri, num_tri, opposite, batch, height,
+                  width, channels))
+    return DR_ERR_INVALID_ARGUMENT;
+  const long long total = batch * static_cast<long long>(height) * width;
+  if (total == 0 || channels == 0) return DR_OK;
+  if (residual == nullptr || loss_grad == nullptr || pairs == nullptr || grad_color == nullptr ||
+      (num_tri > 0 && grad_pos == nullptr))
+    return DR_ERR_INVALID_ARGUMENT;
+  if (pair_bytes < pair_record_bytes(total)) return DR_ERR_WORKSPACE_TOO_SMALL;
+  if (batch > 65535 || height > 65535) return DR_ERR_TOO_LARGE;
+  const AaCtx a = make_ctx(color, rast, pos, pos_batch, num_vert, tri, num_tri, opposite, height,
+                           width, channels);
+  launch_recorded<true>(a, pair_records(const_cast<void*>(pairs), total),
+                        Upstream{grad_out, residual, loss_grad, 2.0f * scale},
+                        pos_gradient_boost, grad_color, grad_pos, batch, as_stream(stream));
   return launch_status();
 }
 
@@ -827,27 +964,10 @@ extern "C" int dr_antialias_bwd(const float* color, const float* rast, const flo
                            width, channels);
   if (batch > 65535) return DR_ERR_TOO_LARGE;
   if (pairs != nullptr) {
-    const PairRecords rec = pair_records(const_cast<void*>(pairs), total);
     if (height > 65535) return DR_ERR_TOO_LARGE;
-    const dim3 grid((width + 255) / 256, height, batch);
-    const cudaStream_t s = as_stream(stream);
-    switch (channels) {
-      case 1:
-        aa_bwd_recorded_kernel<1><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, grad_out,
-                                                       pos_gradient_boost, grad_color, grad_pos);
-        break;
-      case 3:
-        aa_bwd_recorded_kernel<3><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, grad_out,
-                                                       pos_gradient_boost, grad_color, grad_pos);
-        break;
-      case 4:
-        aa_bwd_recorded_kernel<4><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, grad_out,
-                                                       pos_gradient_boost, grad_color, grad_pos);
-        break;
-      default:
-        aa_bwd_recorded_kernel<0><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, grad_out,
-                                                       pos_gradient_boost, grad_color, grad_pos);
-    }
+    launch_recorded<false>(a, pair_records(const_cast<void*>(pairs), total),
+                           Upstream{grad_out, nullptr, nullptr, 0.0f}, pos_gradient_boost,
+                           grad_color, grad_pos, batch, as_stream(stream));
     return launch_status();
   }
   const dim3 grid((width + kAaTileX - 1) / kAaTileX, (height + kAaTileY - 1) / kAaTileY, batch);

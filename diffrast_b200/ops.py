@@ -440,6 +440,59 @@ def antialias(
     or ``[V, 4]`` (shared), ``tri`` the position indices. The edge adjacency of ``tri`` comes from
     ``topology_hash`` or is built on the first call and cached per tensor object.
     """
+    topology = _check_antialias_inputs(color, rast, pos, tri, topology_hash, pos_gradient_boost)
+    if tri.shape[0] == 0 or color.numel() == 0:
+        return color.clone()
+    with torch.cuda.device(color.device):
+        return F.Antialias.apply(
+            color.contiguous(), K.aligned(rast.detach()), K.aligned(pos), tri.contiguous(),
+            topology.opposite(tri), float(pos_gradient_boost),
+        )
+
+
+def antialias_mse(
+    color: Tensor,
+    rast: Tensor,
+    pos: Tensor,
+    tri: Tensor,
+    target: Tensor,
+    topology_hash: TopologyHash | None = None,
+    pos_gradient_boost: float = 1.0,
+    scale: float | None = None,
+) -> tuple[Tensor, Tensor]:
+    """:func:`antialias` followed by the squared-error loss against ``target``, fused.
+
+    Returns ``(image, loss)``: ``image`` equals ``antialias(color, rast, pos, tri, ...)`` and
+    ``loss`` is ``scale * ((image - target) ** 2).sum()``, a 0-dim tensor; ``scale`` defaults to
+    ``1 / image.numel()`` (``torch.nn.functional.mse_loss``'s mean). The loss is summed inside the
+    antialias kernel and its backward pass forms the image's gradient on the fly, so no loss
+    kernels run and no gradient image is stored; gradients reaching ``image`` from elsewhere are
+    added. Not part of diffrast's API: a fit that ends in an MSE can call this in place of
+    ``antialias`` plus ``mse_loss``.
+    """
+    _check(color, "color", ndim=4, dtype=torch.float32)
+    _check(target, "target", ndim=4, dtype=torch.float32, layout="[batch, height, width, channels]")
+    if target.shape != color.shape:
+        raise ValueError(f"target must match color, got {tuple(target.shape)} and {tuple(color.shape)}.")
+    _check_devices(color=color, target=target)
+    if scale is None:
+        scale = 1.0 / max(1, color.numel())
+    if not isinstance(scale, SupportsFloat):
+        raise TypeError(f"scale must be a number, got {scale!r}.")
+    topology = _check_antialias_inputs(color, rast, pos, tri, topology_hash, pos_gradient_boost)
+    if color.numel() == 0:
+        return color.clone(), color.new_zeros(()) + 0.0 * color.sum()
+    opposite = topology.opposite(tri) if topology is not None else tri.new_zeros(0)
+    with torch.cuda.device(color.device):
+        return F.AntialiasMSE.apply(
+            color.contiguous(), K.aligned(rast.detach()), K.aligned(pos), tri.contiguous(),
+            opposite, target.detach().contiguous(), float(scale), float(pos_gradient_boost),
+        )
+
+
+def _check_antialias_inputs(color, rast, pos, tri, topology_hash, pos_gradient_boost):
+    """Validate the arguments of :func:`antialias`; returns the topology (None without
+    triangles)."""
     _check(color, "color", ndim=4, dtype=torch.float32)
     _check(rast, "rast", ndim=4, last=4, dtype=torch.float32)
     shared = isinstance(pos, Tensor) and pos.ndim == 2
@@ -460,16 +513,9 @@ def antialias(
     _check_devices(color=color, rast=rast, pos=pos, tri=tri)
     _check_indices(tri, pos.shape[-2])
     require_cuda(color.device)
-    topology = None
     if topology_hash is not None or tri.shape[0]:
-        topology = topology_for(tri, topology_hash)
-    if tri.shape[0] == 0 or color.numel() == 0:
-        return color.clone()
-    with torch.cuda.device(color.device):
-        return F.Antialias.apply(
-            color.contiguous(), K.aligned(rast.detach()), K.aligned(pos), tri.contiguous(),
-            topology.opposite(tri), float(pos_gradient_boost),
-        )
+        return topology_for(tri, topology_hash)
+    return None
 
 
 def antialias_construct_topology_hash(tri: Tensor) -> TopologyHash:

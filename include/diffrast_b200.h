@@ -247,6 +247,37 @@ int dr_antialias_bwd(const float* color, const float* rast, const float* pos, in
                      const void* pairs, size_t pair_bytes, float* grad_color, float* grad_pos,
                      void* stream);
 
+/* ---- Antialias with a fused squared-error loss ------------------------------------------------
+ * The loss a fit puts right after antialias (the examples of diffrast take an MSE of the
+ * antialiased image), computed inside the antialias passes: no separate loss kernels; the forward
+ * pass leaves the residual out - target, from which the backward pass forms the output's
+ * gradient on the fly. */
+
+/* Number of floats of per-block partial sums of (out - target)^2 that dr_antialias_mse_fwd
+ * writes; the loss is their sum times the caller's scale. */
+size_t dr_antialias_loss_partials(int64_t batch, int32_t height, int32_t width);
+
+/* dr_antialias_fwd (pairs required) that also writes residual = out - target and the partial
+ * sums of residual^2; target and residual are [batch, height, width, channels]. */
+int dr_antialias_mse_fwd(const float* color, const float* rast, const float* pos,
+                         int64_t pos_batch, int64_t num_vert, const int32_t* tri, int64_t num_tri,
+                         const int32_t* opposite, int64_t batch, int32_t height, int32_t width,
+                         int32_t channels, const float* target, float* out, float* residual,
+                         void* pairs, size_t pair_bytes, float* partial_sums, size_t partial_count,
+                         void* stream);
+
+/* Backward pass of loss = scale * sum (out - target)^2 (plus grad_out, the gradient of out, when
+ * not NULL): the output's gradient is grad_out + 2 scale dL residual, dL the device scalar
+ * *loss_grad, with residual and pairs from the dr_antialias_mse_fwd call. grad_color is written;
+ * grad_pos is ACCUMULATED (clear it first). */
+int dr_antialias_mse_bwd(const float* color, const float* rast, const float* pos,
+                         int64_t pos_batch, int64_t num_vert, const int32_t* tri, int64_t num_tri,
+                         const int32_t* opposite, int64_t batch, int32_t height, int32_t width,
+                         int32_t channels, const float* residual, const float* loss_grad,
+                         float scale, const float* grad_out, float pos_gradient_boost,
+                         const void* pairs, size_t pair_bytes, float* grad_color, float* grad_pos,
+                         void* stream);
+
 /* ---- World-to-clip transform (the step ahead of the rasterizer in a multi-view fit) -------- */
 
 /* clip [batch, num_vert, 4] = matrices [batch, 4, 4] (row-major) applied to the homogeneous

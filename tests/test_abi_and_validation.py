@@ -156,3 +156,16 @@ def test_to_clip_validation():
         dr.to_clip(p.double(), m)
     with pytest.raises(RuntimeError, match="CUDA devices only"):
         dr.to_clip(p, m)
+
+
+def test_antialias_mse_validation():
+    color = torch.zeros(1, 4, 4, 3)
+    rast = torch.zeros(1, 4, 4, 4)
+    pos = torch.zeros(1, 3, 4)
+    tri = torch.tensor([[0, 1, 2]], dtype=torch.int32)
+    with pytest.raises(ValueError, match="target must match color"):
+        dr.antialias_mse(color, rast, pos, tri, torch.zeros(1, 4, 4, 4))
+    with pytest.raises(TypeError, match="scale must be a number"):
+        dr.antialias_mse(color, rast, pos, tri, torch.zeros(1, 4, 4, 3), scale="x")
+    with pytest.raises(RuntimeError, match="CUDA devices only"):
+        dr.antialias_mse(color, rast, pos, tri, torch.zeros(1, 4, 4, 3))
