@@ -602,11 +602,16 @@ struct Upstream {
   float scale2;
 };
 
-template <bool kLoss>
+// Upstream modes of the recorded backward pass: the output's gradient only, the fused loss only
+// (the pass is linear in the upstream gradient, so it runs on the residual and scales its results
+// by s once), or both.
+enum UpstreamMode { kGradOnly = 0, kLossOnly = 1, kGradAndLoss = 2 };
+
+template <int kMode>
 __device__ __forceinline__ float upstream(const Upstream& u, float s, long long i) {
-  if (!kLoss) return u.grad[i];
-  const float g = u.grad != nullptr ? u.grad[i] : 0.0f;
-  return fmaf(s, __ldg(u.residual + i), g);
+  if (kMode == kGradOnly) return u.grad[i];
+  if (kMode == kLossOnly) return __ldg(u.residual + i);
+  return fmaf(s, __ldg(u.residual + i), u.grad[i]);
 }
 
 // Backward pass from the pairs recorded by the forward pass: one thread per pixel (grid: columns
@@ -614,9 +619,9 @@ __device__ __forceinline__ float upstream(const Upstream& u, float s, long long 
 // gradient and for the crossings of the pixel's own (right and lower) pairs, whose position
 // gradients it scatters. With K > 0 channels known at compile time, every input the pixel can
 // need is loaded up front, unconditionally, so that the loads overlap instead of each waiting for
-// the record that decides it; K = 0 handles any channel count. With kLoss the upstream gradient
-// of the output is formed on the fly from the fused squared-error loss.
-template <int K, bool kLoss>
+// the record that decides it; K = 0 handles any channel count. kMode (UpstreamMode) says where the
+// upstream gradient comes from.
+template <int K, int kMode>
 __global__ void __launch_bounds__(256, 5) aa_bwd_recorded_kernel(const AaCtx a,
                                                               const float2* __restrict__ rec_t,
                                                               const uint8_t* __restrict__ rec_code,
@@ -638,18 +643,18 @@ __global__ void __launch_bounds__(256, 5) aa_bwd_recorded_kernel(const AaCtx a,
   const float t_l = has_l ? __ldg(rec_t + p - 1).x : 0.f;
   const float t_u = has_u ? __ldg(rec_t + p - w).y : 0.f;
   const int4 verts = __ldg(rec_verts + p);
-  const float s = kLoss ? u.scale2 * __ldg(u.loss_grad) : 0.0f;
+  const float s = kMode == kGradAndLoss ? u.scale2 * __ldg(u.loss_grad) : 0.0f;
   const int C = K > 0 ? K : a.channels;
   constexpr int R = K > 0 ? K : 1;
   float gs[R], gl[R], gr[R], gu[R], gd[R], cs[R], cr[R], cd[R];
   if (K > 0) {
 #pragma unroll
     for (int c = 0; c < R; ++c) {
-      gs[c] = upstream<kLoss>(u, s, p * C + c);
-      gl[c] = has_l ? upstream<kLoss>(u, s, (p - 1) * C + c) : 0.f;
-      gr[c] = has_r ? upstream<kLoss>(u, s, (p + 1) * C + c) : 0.f;
-      gu[c] = has_u ? upstream<kLoss>(u, s, (p - w) * C + c) : 0.f;
-      gd[c] = has_d ? upstream<kLoss>(u, s, (p + w) * C + c) : 0.f;
+      gs[c] = upstream<kMode>(u, s, p * C + c);
+      gl[c] = has_l ? upstream<kMode>(u, s, (p - 1) * C + c) : 0.f;
+      gr[c] = has_r ? upstream<kMode>(u, s, (p + 1) * C + c) : 0.f;
+      gu[c] = has_u ? upstream<kMode>(u, s, (p - w) * C + c) : 0.f;
+      gd[c] = has_d ? upstream<kMode>(u, s, (p + w) * C + c) : 0.f;
       cs[c] = __ldg(a.color + p * C + c);
       cr[c] = has_r ? __ldg(a.color + (p + 1) * C + c) : 0.f;
       cd[c] = has_d ? __ldg(a.color + (p + w) * C + c) : 0.f;
@@ -658,16 +663,17 @@ __global__ void __launch_bounds__(256, 5) aa_bwd_recorded_kernel(const AaCtx a,
   const float2 right = recorded_blend(code & 15u, t.x), down = recorded_blend(code >> 4, t.y);
   const float2 left = recorded_blend(code_l, t_l), up = recorded_blend(code_u, t_u);
   const bool own_r = (code & 8u) != 0u, own_d = (code & 0x80u) != 0u;
+  const float s_end = kMode == kLossOnly ? u.scale2 * __ldg(u.loss_grad) : 1.0f;
   float grad_tr = 0.f, grad_td = 0.f;
 #pragma unroll
   for (int c = 0; c < C; ++c) {
     const int i = K > 0 ? c : 0;
     if (K == 0) {
-      gs[0] = upstream<kLoss>(u, s, p * C + c);
-      gl[0] = has_l ? upstream<kLoss>(u, s, (p - 1) * C + c) : 0.f;
-      gr[0] = has_r ? upstream<kLoss>(u, s, (p + 1) * C + c) : 0.f;
-      gu[0] = has_u ? upstream<kLoss>(u, s, (p - w) * C + c) : 0.f;
-      gd[0] = has_d ? upstream<kLoss>(u, s, (p + w) * C + c) : 0.f;
+      gs[0] = upstream<kMode>(u, s, p * C + c);
+      gl[0] = has_l ? upstream<kMode>(u, s, (p - 1) * C + c) : 0.f;
+      gr[0] = has_r ? upstream<kMode>(u, s, (p + 1) * C + c) : 0.f;
+      gu[0] = has_u ? upstream<kMode>(u, s, (p - w) * C + c) : 0.f;
+      gd[0] = has_d ? upstream<kMode>(u, s, (p + w) * C + c) : 0.f;
       cs[0] = __ldg(a.color + p * C + c);
       cr[0] = has_r ? __ldg(a.color + (p + 1) * C + c) : 0.f;
       cd[0] = has_d ? __ldg(a.color + (p + w) * C + c) : 0.f;
@@ -679,12 +685,16 @@ __global__ void __launch_bounds__(256, 5) aa_bwd_recorded_kernel(const AaCtx a,
     if (left.x != 0.0f || left.y != 0.0f) value += -left.y * g_self + left.x * gl[i];
     if (down.x != 0.0f || down.y != 0.0f) value += -down.x * g_self + down.y * gd[i];
     if (up.x != 0.0f || up.y != 0.0f) value += -up.y * g_self + up.x * gu[i];
-    grad_color[p * C + c] = value;
+    grad_color[p * C + c] = kMode == kLossOnly ? value * s_end : value;
     // d/dt of (1/2 - t)(c_q - c_p) below the midpoint and (t - 1/2)(c_p - c_q) above it.
     if (own_r) grad_tr += t.x < 0.5f ? -g_self * (cr[i] - cs[i]) : gr[i] * (cs[i] - cr[i]);
     if (own_d) grad_td += t.y < 0.5f ? -g_self * (cd[i] - cs[i]) : gd[i] * (cs[i] - cd[i]);
   }
   const long long pb = a.pos_batch == 1 ? 0 : b;
+  if (kMode == kLossOnly) {
+    grad_tr *= s_end;
+    grad_td *= s_end;
+  }
   if (own_r && grad_tr * boost != 0.0f)
     recorded_edge_gradient(a, grad_pos, pb, row, col, code & 15u, verts.x, verts.y, true,
                            grad_tr * boost);
@@ -762,25 +772,25 @@ PairRecords pair_records(void* pairs, long long pixels) {
           reinterpret_cast<int4*>(p + align256(sizeof(float2) * n) + align256(n))};
 }
 
-template <bool kLoss>
+template <int kMode>
 void launch_recorded(const AaCtx& a, const PairRecords& rec, const Upstream& u, float boost,
                      float* grad_color, float* grad_pos, long long batch, cudaStream_t s) {
   const dim3 grid((a.width + 255) / 256, a.height, static_cast<unsigned>(batch));
   switch (a.channels) {
     case 1:
-      aa_bwd_recorded_kernel<1, kLoss><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, u, boost,
+      aa_bwd_recorded_kernel<1, kMode><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, u, boost,
                                                             grad_color, grad_pos);
       break;
     case 3:
-      aa_bwd_recorded_kernel<3, kLoss><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, u, boost,
+      aa_bwd_recorded_kernel<3, kMode><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, u, boost,
                                                             grad_color, grad_pos);
       break;
     case 4:
-      aa_bwd_recorded_kernel<4, kLoss><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, u, boost,
+      aa_bwd_recorded_kernel<4, kMode><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, u, boost,
                                                             grad_color, grad_pos);
       break;
     default:
-      aa_bwd_recorded_kernel<0, kLoss><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, u, boost,
+      aa_bwd_recorded_kernel<0, kMode><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, u, boost,
                                                             grad_color, grad_pos);
   }
 }
@@ -935,9 +945,14 @@ extern "C" int dr_antialias_mse_bwd(const float* color, const float* rast, const
   if (batch > 65535 || height > 65535) return DR_ERR_TOO_LARGE;
   const AaCtx a = make_ctx(color, rast, pos, pos_batch, num_vert, tri, num_tri, opposite, height,
                            width, channels);
-  launch_recorded<true>(a, pair_records(const_cast<void*>(pairs), total),
-                        Upstream{grad_out, residual, loss_grad, 2.0f * scale},
-                        pos_gradient_boost, grad_color, grad_pos, batch, as_stream(stream));
+  const PairRecords rec = pair_records(const_cast<void*>(pairs), total);
+  const Upstream u{grad_out, residual, loss_grad, 2.0f * scale};
+  if (grad_out == nullptr)
+    launch_recorded<kLossOnly>(a, rec, u, pos_gradient_boost, grad_color, grad_pos, batch,
+                               as_stream(stream));
+  else
+    launch_recorded<kGradAndLoss>(a, rec, u, pos_gradient_boost, grad_color, grad_pos, batch,
+                                  as_stream(stream));
   return launch_status();
 }
 
@@ -965,7 +980,7 @@ extern "C" int dr_antialias_bwd(const float* color, const float* rast, const flo
   if (batch > 65535) return DR_ERR_TOO_LARGE;
   if (pairs != nullptr) {
     if (height > 65535) return DR_ERR_TOO_LARGE;
-    launch_recorded<false>(a, pair_records(const_cast<void*>(pairs), total),
+    launch_recorded<kGradOnly>(a, pair_records(const_cast<void*>(pairs), total),
                            Upstream{grad_out, nullptr, nullptr, 0.0f}, pos_gradient_boost,
                            grad_color, grad_pos, batch, as_stream(stream));
     return launch_status();
