@@ -56,6 +56,25 @@ def record_timings():
 # Binned-triangle capacity of the rasterizer's setup list, remembered per problem shape so that
 # the list is sized right from the second call on.
 _capacity: dict[tuple, int] = {}
+# Binned-triangle and pair capacities for calls captured into a CUDA graph (which cannot read the
+# counts back): twice the largest counts seen by eager calls of the same shape, plus slack.
+_graph_capacity: dict[tuple, tuple[int, int]] = {}
+# Per device: a word that captured visibility passes set when their counts exceeded those
+# capacities (see RasterizeContext.capture_overflowed).
+_overflow: dict[torch.device, Tensor] = {}
+
+
+def overflow_word(device: torch.device) -> Tensor:
+    word = _overflow.get(device)
+    if word is None:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError(
+                "diffrast_b200: run rasterize once without CUDA graph capture before capturing it "
+                "(the captured call reuses capacities measured by an eager call)."
+            )
+        word = torch.zeros(1, dtype=torch.int64, device=device)
+        _overflow[device] = word
+    return word
 
 
 def aligned(t: Tensor) -> Tensor:
@@ -109,6 +128,34 @@ def raster_keys(pos: Tensor, tri: Tensor, height: int, width: int, prev_keys: Te
     shape_key = (dev, batch, total, height, width)
     cap = _capacity.get(shape_key, max(1024, min(total, 1 << 16)))
     rs, rf = (N.ptr(ranges.start), N.ptr(ranges.first)) if ranges is not None else (None, None)
+    if torch.cuda.is_current_stream_capturing():
+        # No host round trip: the counts stay on the device, bounded by capacities measured by
+        # eager calls; an overflow is flagged on the device.
+        word = overflow_word(dev)
+        caps = _graph_capacity.get(shape_key)
+        if caps is None:
+            raise RuntimeError(
+                "diffrast_b200: run rasterize once without CUDA graph capture on the same shapes "
+                "before capturing it (the captured call reuses capacities measured eagerly)."
+            )
+        cap, pair_cap = caps
+        ws = _scratch(lib.dr_raster_setup_workspace_bytes(cap, height, width), dev)
+        N.check(
+            lib.dr_raster_setup(pos.data_ptr(), pos_batch, tri.data_ptr(), batch, num_vert,
+                                num_tri, rs, rf, total, height, width, N.ptr(prev_keys),
+                                keys.data_ptr(), ws.data_ptr(), ws.numel(), cap, s),
+            "dr_raster_setup",
+        )  # fmt: skip
+        bws = _scratch(lib.dr_raster_bin_workspace_bytes(batch, height, width, pair_cap), dev)
+        N.check(
+            lib.dr_raster_tiles_device(pos.data_ptr(), pos_batch, tri.data_ptr(), batch, num_vert,
+                                       num_tri, height, width, N.ptr(prev_keys), keys.data_ptr(),
+                                       ws.data_ptr(), cap, pair_cap, bws.data_ptr(), bws.numel(),
+                                       word.data_ptr(), s),
+            "dr_raster_tiles_device",
+        )  # fmt: skip
+        return keys
+    overflow_word(dev)
     binned, pairs = c_int64(0), c_int64(0)
     for _ in range(2):
         ws = _scratch(lib.dr_raster_setup_workspace_bytes(cap, height, width), dev)
@@ -127,6 +174,9 @@ def raster_keys(pos: Tensor, tri: Tensor, height: int, width: int, prev_keys: Te
         _capacity[shape_key] = cap
     if binned.value > cap:
         raise RuntimeError("diffrast_b200: binned triangle count changed between identical runs")
+    old_caps = _graph_capacity.get(shape_key, (0, 0))
+    _graph_capacity[shape_key] = (max(old_caps[0], 2 * binned.value + 1024),
+                                  max(old_caps[1], 2 * pairs.value + 4096))
     if binned.value > 0 and pairs.value > 0:
         bws = _scratch(lib.dr_raster_bin_workspace_bytes(batch, height, width, pairs.value), dev)
         N.check(
@@ -498,3 +548,16 @@ def antialias_mse_bwd(color, rast, pos3, tri, opposite, residual, loss_grad, sca
         "dr_antialias_mse_bwd",
     )  # fmt: skip
     return grad_color, grad_pos
+
+
+def capture_overflowed(device: torch.device) -> bool:
+    """Whether a captured visibility pass on ``device`` exceeded its capacities since the last
+    call (synchronizes); if so, the capacities for later captures are doubled."""
+    word = _overflow.get(device)
+    if word is None or int(word.item()) == 0:
+        return False
+    word.zero_()
+    for key, (cap, pair_cap) in list(_graph_capacity.items()):
+        if key[0] == device:
+            _graph_capacity[key] = (2 * cap, 2 * pair_cap)
+    return True

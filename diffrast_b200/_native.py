@@ -37,6 +37,11 @@ _SIGNATURES = {
         [_P, c_int64, _P, c_int64, c_int64, c_int64, c_int32, c_int32, _P, _P, _P, c_int64,
          c_int64, _P, c_size_t, _P],
     ),
+    "dr_raster_tiles_device": (
+        c_int,
+        [_P, c_int64, _P, c_int64, c_int64, c_int64, c_int32, c_int32, _P, _P, _P, c_int64,
+         c_int64, _P, c_size_t, _P, _P],
+    ),
     "dr_raster_resolve_fwd": (
         c_int, [_P, c_int64, _P, _P, c_int64, c_int64, c_int64, c_int32, c_int32, _P, _P, _P]
     ),

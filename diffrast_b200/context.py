@@ -27,6 +27,20 @@ class RasterizeContext:
     def __repr__(self) -> str:
         return f"{type(self).__name__}(device={str(self.device)!r})"
 
+    def capture_overflowed(self) -> bool:
+        """Whether a rasterization replayed from a CUDA graph on this device ran out of binning
+        capacity since the last call (this synchronizes the device).
+
+        A call captured into a CUDA graph cannot read its binned-triangle counts back, so it uses
+        capacities measured by an eager call of the same shapes (twice the counts seen). Triangles
+        whose pixel box exceeds 512 pixels beyond that capacity are then missing from the result.
+        On ``True`` the results of the replays since the last check are incomplete; the
+        capacities of later captures are doubled, so capture the graph again and rerun.
+        """
+        from diffrast_b200._kernels import capture_overflowed
+
+        return capture_overflowed(self.device)
+
 
 # nvdiffrast's name for the same context.
 RasterizeCudaContext = RasterizeContext

@@ -406,12 +406,32 @@ __global__ void __launch_bounds__(256) setup_kernel(
 }
 
 // One warp per binned triangle; its lanes walk the triangle's tiles.
+// Device-driven variant (count_on_device non-null): the count is the setup counter, and a list
+// or pair total above its capacity (an incomplete list) is flagged in *overflow and nothing is
+// scattered.
+struct DeviceCounts {
+  const unsigned long long* count_on_device;  // setup counter [0], or null
+  long long capacity;                         // records in the binned list
+  long long pair_capacity;                    // entries of the pair list
+  unsigned long long* overflow;
+};
+
 template <bool kScatter>
 __global__ void __launch_bounds__(256) bin_kernel(const Binned* __restrict__ binned,
                                                   long long count, int tiles_x, int tiles_per_image,
                                                   unsigned* __restrict__ tile_count,
                                                   const unsigned* __restrict__ tile_offset,
-                                                  int* __restrict__ pairs) {
+                                                  int* __restrict__ pairs, const DeviceCounts dc,
+                                                  int num_tiles) {
+  if (dc.count_on_device != nullptr) {
+    count = static_cast<long long>(*dc.count_on_device);
+    const bool over = count > dc.capacity ||
+                      (kScatter && static_cast<long long>(tile_offset[num_tiles]) > dc.pair_capacity);
+    if (over) {
+      if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(dc.overflow, 1ull);
+      return;
+    }
+  }
   const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x / 32);
   const unsigned lane = threadIdx.x & 31u;
   for (long long i = (blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x) / 32; i < count;
@@ -565,7 +585,7 @@ __global__ void __launch_bounds__(256) tile_kernel(
     const float* __restrict__ centres,
     const long long* __restrict__ prev, long long* __restrict__ keys, const int* __restrict__ pairs,
     const Binned* __restrict__ binned, const unsigned* __restrict__ tile_offset,
-    const unsigned* __restrict__ item_offset, unsigned* __restrict__ work) {
+    const unsigned* __restrict__ item_offset, unsigned* __restrict__ work, const DeviceCounts dc) {
   __shared__ float4 sv[3][kChunk];
   __shared__ int st[kChunk];
   __shared__ int4 sbox[kChunk];
@@ -573,6 +593,10 @@ __global__ void __launch_bounds__(256) tile_kernel(
   __shared__ unsigned s_first, s_count;
   const int lx = threadIdx.x % kTile, ly = threadIdx.x / kTile;
   const unsigned total_items = item_offset[num_tiles];
+  if (dc.count_on_device != nullptr &&
+      (static_cast<long long>(*dc.count_on_device) > dc.capacity ||
+       static_cast<long long>(tile_offset[num_tiles]) > dc.pair_capacity))
+    return;  // flagged by bin_kernel
   for (;;) {
     if (threadIdx.x == 0) {
       const unsigned item = atomicAdd(work, 1u);
@@ -959,23 +983,21 @@ extern "C" size_t dr_raster_bin_workspace_bytes(int64_t batch, int32_t height, i
   return bin_bytes(batch * tiles_x * tiles_y, num_pairs < 0 ? 0 : num_pairs);
 }
 
-extern "C" int dr_raster_tiles(const float* pos, int64_t pos_batch, const int32_t* tri,
-                               int64_t batch, int64_t num_vert, int64_t num_tri, int32_t height,
-                               int32_t width, const int64_t* prev_keys, int64_t* keys,
-                               const void* setup_workspace, int64_t num_binned, int64_t num_pairs,
-                               void* bin_workspace, size_t bin_workspace_bytes, void* stream) {
-  if (bad_raster_args(pos, tri, batch, num_vert, num_tri, height, width, pos_batch) ||
-      keys == nullptr ||
-      setup_workspace == nullptr || num_binned < 0 || num_pairs < 0)
-    return DR_ERR_INVALID_ARGUMENT;
-  if (num_pairs >= (1LL << 31)) return DR_ERR_TOO_LARGE;
-  if (num_binned == 0 || num_pairs == 0) return DR_OK;
+namespace dr {
+namespace {
+
+// Stage 2 with either host counts (dc.count_on_device null: num_binned and num_pairs exact) or the
+// setup counters read on the device (num_binned and num_pairs are then capacities).
+int launch_tiles(const float* pos, int64_t pos_batch, const int32_t* tri, int64_t batch,
+                 int64_t num_vert, int32_t height, int32_t width, const int64_t* prev_keys,
+                 int64_t* keys, const void* setup_workspace, int64_t num_binned,
+                 int64_t num_pairs, void* bin_workspace, size_t bin_workspace_bytes,
+                 const DeviceCounts& dc, cudaStream_t s) {
   const int tiles_x = (width + kTile - 1) / kTile, tiles_y = (height + kTile - 1) / kTile;
   const int64_t tiles = batch * tiles_x * tiles_y;
   if (tiles >= (1LL << 31)) return DR_ERR_TOO_LARGE;
   if (bin_workspace == nullptr || bin_workspace_bytes < bin_bytes(tiles, num_pairs))
     return DR_ERR_WORKSPACE_TOO_SMALL;
-  cudaStream_t s = as_stream(stream);
   // Only the first num_binned records are read; the caller reran setup with enough capacity.
   SetupLayout sl = setup_layout(setup_workspace, height, width);
   BinLayout bl = bin_layout(bin_workspace, tiles, num_pairs);
@@ -984,24 +1006,62 @@ extern "C" int dr_raster_tiles(const float* pos, int64_t pos_batch, const int32_
   if (err == cudaSuccess) err = cudaMemsetAsync(bl.work, 0, sizeof(unsigned), s);
   if (err != cudaSuccess) return static_cast<int>(err);
   const int tiles_per_image = tiles_x * tiles_y;
+  const int nt = static_cast<int>(tiles);
   const unsigned bin_blocks = min(blocks_for(num_binned * 32, 256), 148u * 16u);
   bin_kernel<false><<<bin_blocks, 256, 0, s>>>(sl.binned, num_binned, tiles_x, tiles_per_image,
-                                               bl.tile_count, nullptr, nullptr);
+                                               bl.tile_count, nullptr, nullptr, dc, nt);
   const int chunks = static_cast<int>(scan_chunks(tiles));
-  scan_totals_kernel<<<chunks, 1024, 0, s>>>(bl.tile_count, static_cast<int>(tiles),
-                                             bl.scan_totals);
+  scan_totals_kernel<<<chunks, 1024, 0, s>>>(bl.tile_count, nt, bl.scan_totals);
   scan_chunks_kernel<<<1, 1024, 0, s>>>(bl.scan_totals, chunks);
-  scan_kernel<<<chunks, 1024, 0, s>>>(bl.tile_count, static_cast<int>(tiles), bl.scan_totals,
-                                      chunks, bl.tile_offset, bl.item_offset);
+  scan_kernel<<<chunks, 1024, 0, s>>>(bl.tile_count, nt, bl.scan_totals, chunks, bl.tile_offset,
+                                      bl.item_offset);
   bin_kernel<true><<<bin_blocks, 256, 0, s>>>(sl.binned, num_binned, tiles_x, tiles_per_image,
-                                              bl.tile_cursor, bl.tile_offset, bl.pairs);
+                                              bl.tile_cursor, bl.tile_offset, bl.pairs, dc, nt);
   tile_kernel<<<148 * 8, 256, 0, s>>>(pos, tri, pos_stride(pos_batch, num_vert), height, width,
-                                      tiles_x,
-                                      tiles_per_image, static_cast<int>(tiles), sl.centres,
+                                      tiles_x, tiles_per_image, nt, sl.centres,
                                       reinterpret_cast<const long long*>(prev_keys),
                                       reinterpret_cast<long long*>(keys), bl.pairs, sl.binned,
-                                      bl.tile_offset, bl.item_offset, bl.work);
+                                      bl.tile_offset, bl.item_offset, bl.work, dc);
   return launch_status();
+}
+
+}  // namespace
+}  // namespace dr
+
+extern "C" int dr_raster_tiles(const float* pos, int64_t pos_batch, const int32_t* tri,
+                               int64_t batch, int64_t num_vert, int64_t num_tri, int32_t height,
+                               int32_t width, const int64_t* prev_keys, int64_t* keys,
+                               const void* setup_workspace, int64_t num_binned, int64_t num_pairs,
+                               void* bin_workspace, size_t bin_workspace_bytes, void* stream) {
+  if (bad_raster_args(pos, tri, batch, num_vert, num_tri, height, width, pos_batch) ||
+      keys == nullptr || setup_workspace == nullptr || num_binned < 0 || num_pairs < 0)
+    return DR_ERR_INVALID_ARGUMENT;
+  if (num_pairs >= (1LL << 31)) return DR_ERR_TOO_LARGE;
+  if (num_binned == 0 || num_pairs == 0) return DR_OK;
+  return launch_tiles(pos, pos_batch, tri, batch, num_vert, height, width, prev_keys, keys,
+                      setup_workspace, num_binned, num_pairs, bin_workspace, bin_workspace_bytes,
+                      DeviceCounts{nullptr, 0, 0, nullptr}, as_stream(stream));
+}
+
+extern "C" int dr_raster_tiles_device(const float* pos, int64_t pos_batch, const int32_t* tri,
+                                      int64_t batch, int64_t num_vert, int64_t num_tri,
+                                      int32_t height, int32_t width, const int64_t* prev_keys,
+                                      int64_t* keys, const void* setup_workspace,
+                                      int64_t binned_capacity, int64_t pair_capacity,
+                                      void* bin_workspace, size_t bin_workspace_bytes,
+                                      uint64_t* overflow, void* stream) {
+  if (bad_raster_args(pos, tri, batch, num_vert, num_tri, height, width, pos_batch) ||
+      keys == nullptr || setup_workspace == nullptr || overflow == nullptr ||
+      binned_capacity < 0 || pair_capacity < 0)
+    return DR_ERR_INVALID_ARGUMENT;
+  if (pair_capacity >= (1LL << 31)) return DR_ERR_TOO_LARGE;
+  if (batch == 0 || num_tri == 0) return DR_OK;
+  SetupLayout sl = setup_layout(setup_workspace, height, width);
+  const DeviceCounts dc{sl.counters, binned_capacity, pair_capacity,
+                        reinterpret_cast<unsigned long long*>(overflow)};
+  return launch_tiles(pos, pos_batch, tri, batch, num_vert, height, width, prev_keys, keys,
+                      setup_workspace, binned_capacity > 0 ? binned_capacity : 1, pair_capacity,
+                      bin_workspace, bin_workspace_bytes, dc, as_stream(stream));
 }
 
 extern "C" int dr_raster_resolve_fwd(const float* pos, int64_t pos_batch, const int32_t* tri,

@@ -59,7 +59,7 @@ def rasterize(
     resolution = check_rasterize_inputs(glctx, pos, tri, resolution, ranges)
     output_db = getattr(glctx, "output_db", True)
     grad_db = grad_db and output_db
-    table = K.range_table(ranges, pos.device) if pos.ndim == 2 else None
+    table = _range_table(ranges, pos.device) if pos.ndim == 2 else None
     rast, rast_db, _ = rasterize_layer(pos, tri, resolution, grad_db, None, table)
     return rast, (rast_db if output_db else rast.new_zeros(*rast.shape[:3], 0))
 
@@ -108,6 +108,18 @@ def check_rasterize_inputs(glctx, pos, tri, resolution, ranges) -> tuple[int, in
     if range_mode:
         _check_ranges(ranges, tri.shape[0])
     return _check_resolution(resolution)
+
+
+_range_tables: dict[torch.device, TensorCache[K.RangeTable]] = {}
+
+
+def _range_table(ranges: Tensor, device: torch.device) -> K.RangeTable:
+    """Device table of ``ranges``, made once per tensor object and device (so that a call
+    captured into a CUDA graph copies nothing from the host)."""
+    cache = _range_tables.get(device)
+    if cache is None:
+        cache = _range_tables[device] = TensorCache(lambda r: K.range_table(r, device))
+    return cache.get(ranges)
 
 
 def _check_ranges(ranges: Tensor | None, num_tri: int) -> None:

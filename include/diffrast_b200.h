@@ -97,6 +97,18 @@ int dr_raster_tiles(const float* pos, int64_t pos_batch, const int32_t* tri, int
                     int64_t num_pairs, void* bin_workspace, size_t bin_workspace_bytes,
                     void* stream);
 
+/* Stage 2 without the host round trip of dr_raster_counts (so that a CUDA graph can capture the
+ * rasterizer): the counts are read on the device from the setup workspace. binned_capacity is the
+ * capacity dr_raster_setup was given and pair_capacity the pair count bin_workspace is sized for
+ * (dr_raster_bin_workspace_bytes). When a count exceeds its capacity nothing is binned, 1 is
+ * OR-ed into the device word *overflow and the keys lack the binned triangles: the caller then
+ * reruns with larger capacities. Launches the same kernels whether or not anything is binned. */
+int dr_raster_tiles_device(const float* pos, int64_t pos_batch, const int32_t* tri, int64_t batch,
+                           int64_t num_vert, int64_t num_tri, int32_t height, int32_t width,
+                           const int64_t* prev_keys, int64_t* keys, const void* setup_workspace,
+                           int64_t binned_capacity, int64_t pair_capacity, void* bin_workspace,
+                           size_t bin_workspace_bytes, uint64_t* overflow, void* stream);
+
 /* rast [batch, h, w, 4] = (u, v, z/w, id + 1) and rast_db [.., 4] = (du/dx, du/dy, dv/dx, dv/dy),
  * zeros where empty (reference.py:69-114; _triton_resolve.py:84-116). rast_db may be NULL. */
 int dr_raster_resolve_fwd(const float* pos, int64_t pos_batch, const int32_t* tri,
