@@ -303,12 +303,13 @@ def run_ours(args) -> None:
     stage_ms = {name: sum(s.elapsed_time(e) for s, e in pairs) / args.steps for name, pairs in stages.items()}
     stage_calls = {name: len(pairs) / args.steps for name, pairs in stages.items()}
 
-    # On one GPU each step then replays a CUDA graph of the whole forward and backward pass: no op
-    # reads anything back to the host, so the step captures as a unit. A graph is bound to its
-    # input buffers, so each input buffer gets its own (each with its own memory pool). Several
-    # GPUs launch eagerly.
-    use_graph = world == 1 and not args.eager
+    # Each step then replays a CUDA graph of the whole forward and backward pass, the gradient
+    # all-reduces included: no op reads anything back to the host, so the step captures as a
+    # unit. A graph is bound to its input buffers, so each input buffer gets its own (each with its
+    # own memory pool). The graphs are released before the process group is destroyed.
+    use_graph = not args.eager
     runners: dict[int, object] = {}
+    graphs: list = []
 
     def runner(mvp_in, target_in):
         if not use_graph:
@@ -318,6 +319,7 @@ def run_ours(args) -> None:
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
                 loss = step(mvp_in, target_in)
+            graphs.append(graph)
             runners[key] = lambda: (graph.replay(), loss)[1]
         return runners[key]
 
@@ -328,8 +330,6 @@ def run_ours(args) -> None:
         torch.cuda.synchronize()
         with ClockSampler(gpu_id(dev)) as graph_clocks:
             ms = timed_loop(run_resident)
-        if ctx.capture_overflowed():
-            raise SystemExit("a captured visibility pass outgrew its binning capacity; rerun")
         clocks = graph_clocks
 
     # End to end through the public API: every step's inputs are copied from pinned host memory
@@ -386,9 +386,21 @@ def run_ours(args) -> None:
         dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
     e2e_ms = e2e_t.item() / args.steps
 
+    # A captured visibility pass that outgrew its binning capacity would have dropped triangles.
+    overflow = torch.tensor([1.0 if ctx.capture_overflowed() else 0.0], device=dev)
+    if world > 1:
+        dist.all_reduce(overflow, op=dist.ReduceOp.MAX)
+    if overflow.item():
+        raise SystemExit("a captured visibility pass outgrew its binning capacity; rerun")
+
     pixels_total = args.views * res * res
     value = pixels_total / (ms / 1e3) / 1e6
     e2e_value = pixels_total / (e2e_ms / 1e3) / 1e6
+    torch.cuda.synchronize()
+    runners.clear()
+    for graph in graphs:
+        graph.reset()
+    graphs.clear()
     if rank != 0:
         if world > 1:
             dist.destroy_process_group()
@@ -536,7 +548,7 @@ def main() -> None:
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--eager", action="store_true",
                         help="launch every step's kernels from Python instead of replaying a CUDA "
-                             "graph of the step (graphs are used on one GPU only)")
+                             "graph of the step")
     args = parser.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
