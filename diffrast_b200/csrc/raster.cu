@@ -48,8 +48,11 @@ struct Items {
 
 __device__ __forceinline__ void locate(const Items& it, long long g, int& b, int& t) {
   if (it.range_start == nullptr) {
-    b = static_cast<int>(g / it.num_tri);
-    t = static_cast<int>(g - static_cast<long long>(b) * it.num_tri);
+    // g < 2^31 (checked by the host): a 32-bit division.
+    const unsigned gu = static_cast<unsigned>(g), n = static_cast<unsigned>(it.num_tri);
+    const unsigned q = gu / n;
+    b = static_cast<int>(q);
+    t = static_cast<int>(gu - q * n);
     return;
   }
   // Last item whose first flat index is <= g (empty items share their successor's).
@@ -168,12 +171,13 @@ constexpr int kRing = 64;
 struct WarpTris {
   float4 v[3][32];     // clip-space vertices, for the exact test
   float4 edge[3][32];  // NDC half-planes A x + B y + C >= -D, stored as (1 / A, B, C + D, A)
-  float2 reach[32];    // coverage_reach of the triangle
-  int t[32], b[32], c0[32], c1[32], r0[32], spans[32], end[32];
-  // Ring of rows with pixels to test: (triangle rank, row, column of the row's pixel number 0,
-  // number of pixels queued up to the row's end) and the row's NDC centre.
+  float4 aux[32];      // coverage_reach of the triangle (x, y), its index and view (as bits)
+  // (first row - number of the triangle's first row among the warp's rows, first column, last
+  // column, whether rows are bounded by the half-planes)
+  int4 info[32];
+  // Ring of rows with pixels to test: (triangle rank | row << 5, column of the row's pixel number
+  // 0, number of pixels queued up to the row's end, the row's NDC centre as bits).
   int4 row[kRing];
-  float row_py[kRing];
 };
 
 __global__ void __launch_bounds__(256) setup_kernel(
@@ -262,20 +266,15 @@ __global__ void __launch_bounds__(256) setup_kernel(
     w.v[0][rank] = make_float4(v0.x, v0.y, v0.z, v0.w);
     w.v[1][rank] = make_float4(v1.x, v1.y, v1.z, v1.w);
     w.v[2][rank] = make_float4(v2.x, v2.y, v2.z, v2.w);
-    w.reach[rank] = coverage_reach(v0, v1, v2);
-    w.t[rank] = t;
-    w.b[rank] = b;
-    w.c0[rank] = c0;
-    w.c1[rank] = c1;
-    w.r0[rank] = r0;
-    w.end[rank] = end;
+    const float2 reach = coverage_reach(v0, v1, v2);
+    w.aux[rank] = make_float4(reach.x, reach.y, __int_as_float(t), __int_as_float(b));
     // Half-planes of the projected triangle, oriented inwards and widened by a margin that
     // covers the rounding of x / w and of the exact homogeneous test many times over. A triangle
     // whose projected orientation is not clear-cut keeps whole bounding-box rows.
     const float ex = (nx[1] - nx[0]) * (ny[2] - ny[0]), ey = (ny[1] - ny[0]) * (nx[2] - nx[0]);
     const float area2 = ex - ey;
     const bool spans = fabsf(area2) > 1e-3f * (fabsf(ex) + fabsf(ey));
-    w.spans[rank] = spans ? 1 : 0;
+    w.info[rank] = make_int4(r0 - (end - rows), c0, c1, spans ? 1 : 0);
     const float o = area2 > 0.0f ? 1.0f : -1.0f;
     const float size = static_cast<float>(max(width, height));
     const float delta = (0.01f + size * 1e-6f) * 2.0f / static_cast<float>(min(width, height));
@@ -311,11 +310,12 @@ __global__ void __launch_bounds__(256) setup_kernel(
     int count = 0, row = 0, cl = 0;
     float py = 0.0f;
     if (item < all_rows) {
-      row = w.r0[k] + item - (k > 0 ? w.end[k - 1] : 0);
-      cl = w.c0[k];
-      int cr = w.c1[k];
+      const int4 info = w.info[k];
+      row = info.x + item;
+      cl = info.y;
+      int cr = info.z;
       py = __ldg(centres + width + row);
-      if (w.spans[k]) {
+      if (info.w) {
         float lo = -__int_as_float(0x7f800000), hi = __int_as_float(0x7f800000);
         bool empty = false;
         for (int e = 0; e < 3; ++e) {
@@ -349,8 +349,7 @@ __global__ void __launch_bounds__(256) setup_kernel(
       const int q = (queued_rows + slot) & (kRing - 1);
       const int last = queued_px + pix_end;  // pixels queued up to the end of this row
       // (triangle rank, row, column of pixel number 0 of this row's numbering, end)
-      w.row[q] = make_int4(k, row, cl - (last - count), last);
-      w.row_py[q] = py;
+      w.row[q] = make_int4(k | (row << 5), cl - (last - count), last, __float_as_int(py));
     }
     queued_rows += __popc(busy);
     queued_px += __shfl_sync(0xffffffffu, pix_end, 31);
@@ -363,7 +362,7 @@ __global__ void __launch_bounds__(256) setup_kernel(
       const int n = consumed_rows + static_cast<int>(lane);
       unsigned pbit = 0u;
       if (n < queued_rows) {
-        const int e = w.row[n & (kRing - 1)].w;
+        const int e = w.row[n & (kRing - 1)].z;
         if (e <= tested_px + 32) pbit = 1u << (e - tested_px - 1);
       }
       const unsigned pends = __reduce_or_sync(0xffffffffu, pbit);
@@ -373,14 +372,16 @@ __global__ void __launch_bounds__(256) setup_kernel(
       tested_px += 32;
       if (pitem >= queued_px) continue;
       const int4 rec = w.row[r];
-      const int kk = rec.x, y = rec.y, col = rec.z + pitem;
+      const int kk = rec.x & 31, y = rec.x >> 5, col = rec.y + pitem;
       const float4 a = w.v[0][kk], bb = w.v[1][kk], cc = w.v[2][kk];
-      const float2 reach = w.reach[kk];
+      const float4 aux = w.aux[kk];
       const long long key = coverage_key({a.x, a.y, a.z, a.w}, {bb.x, bb.y, bb.z, bb.w},
                                          {cc.x, cc.y, cc.z, cc.w}, __ldg(centres + col),
-                                         w.row_py[r], w.t[kk], reach.x, reach.y);
+                                         __int_as_float(rec.w), __float_as_int(aux.z), aux.x,
+                                         aux.y);
       if (key == kEmptyKey) continue;
-      const long long off = (static_cast<long long>(w.b[kk]) * height + y) * width + col;
+      const long long off =
+          (static_cast<long long>(__float_as_int(aux.w)) * height + y) * width + col;
       if (prev != nullptr && !(key > __ldg(prev + off))) continue;
       atomicMin(keys + off, key);
     }
