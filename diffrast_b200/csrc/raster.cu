@@ -880,24 +880,24 @@ __global__ void __launch_bounds__(256) resolve_bwd_kernel(
     }
   }
   const long long base = static_cast<long long>(q.b) * pos_stride;
-  // A warp whose covered pixels all show one triangle (large triangles) sums its gradients first
-  // and adds them once; otherwise each lane adds its own with vector reductions (with triangles
-  // of about a pixel, lanes rarely share a vertex and a warp-level match costs more than it saves).
+  // Lanes showing the same triangle (a warp covers 32 pixels of one row) sum their vertex
+  // gradients first; one of them adds the sums with three vector reductions.
   const unsigned act = __ballot_sync(0xffffffffu, q.covered);
   if (act == 0u) return;
-  const int lead = __ffs(act) - 1;
-  const int t0 = __shfl_sync(0xffffffffu, q.t, lead);
-  if (__all_sync(0xffffffffu, !q.covered || q.t == t0)) {
+  const unsigned lane = threadIdx.x & 31u;
+  unsigned peers = 1u << lane;
+  if (q.covered) peers = __match_any_sync(act, q.t);
+  float v[12];
 #pragma unroll
-    for (int k = 0; k < 3; ++k)
+  for (int k = 0; k < 3; ++k)
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+    for (int c = 0; c < 4; ++c) v[4 * k + c] = gv[k][c];
+  segmented_sum<12>(peers, v);
+  if (!q.covered || (peers & ((1u << lane) - 1u)) != 0u) return;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) gv[k][c] += __shfl_xor_sync(0xffffffffu, gv[k][c], o);
-    if (static_cast<int>(threadIdx.x & 31u) != lead) return;
-  } else if (!q.covered) {
-    return;
-  }
+  for (int k = 0; k < 3; ++k)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) gv[k][c] = v[4 * k + c];
   red_add_v4(grad_pos + (base + q.i0) * 4, gv[0][0], gv[0][1], gv[0][2], gv[0][3]);
   red_add_v4(grad_pos + (base + q.i1) * 4, gv[1][0], gv[1][1], gv[1][2], gv[1][3]);
   red_add_v4(grad_pos + (base + q.i2) * 4, gv[2][0], gv[2][1], gv[2][2], gv[2][3]);
