@@ -28,7 +28,13 @@ _SIGNATURES = {
     "dr_raster_setup": (
         c_int,
         [_P, c_int64, _P, c_int64, c_int64, c_int64, _P, _P, c_int64, c_int32, c_int32, _P, _P, _P,
-         c_size_t, c_int64, _P],
+         c_size_t, c_int64, _P, c_size_t, _P],
+    ),
+    "dr_raster_occlusion_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int32, c_int32]),
+    "dr_raster_occluded": (
+        c_int,
+        [_P, c_int64, _P, c_int64, c_int64, c_int64, _P, _P, c_int64, c_int32, c_int32, _P, _P, _P,
+         _P, c_size_t, _P],
     ),
     "dr_raster_counts": (c_int, [_P, POINTER(c_int64), POINTER(c_int64), _P]),
     "dr_raster_bin_workspace_bytes": (c_size_t, [c_int64, c_int32, c_int32, c_int64]),

@@ -180,15 +180,89 @@ struct WarpTris {
   int4 row[kRing];
 };
 
+// Occlusion pass state. The first visibility pass sets aside small triangles that face away in
+// screen space (negative orientation: the far side of a closed, outward-facing mesh) as records
+// (flat index, tile box x0 | x1 << 16, y0 | y1 << 16, ordered lower bound of their depth); once
+// everything else is in the keys, the largest key of every 16 x 16 tile is taken, and a set-aside
+// triangle whose depth bound lies above the largest key of every tile it touches cannot be the
+// nearest anywhere and is skipped; the others are drawn as usual.
+struct Occlusion {
+  unsigned long long* count;   // records set aside
+  int4* list;                  // [capacity]
+  const long long* tile_max;   // [views, tiles_per_view]
+  int tiles_x, tiles_per_view;
+};
+
+// Largest key of each 16 x 16 tile (grid: tiles x, tiles y, views).
+__global__ void __launch_bounds__(256) tile_max_kernel(const long long* __restrict__ keys,
+                                                       int height, int width,
+                                                       long long* __restrict__ tile_max) {
+  __shared__ long long warp_max[8];
+  const int row = blockIdx.y * kTile + static_cast<int>(threadIdx.x) / kTile;
+  const int col = blockIdx.x * kTile + static_cast<int>(threadIdx.x) % kTile;
+  const long long b = blockIdx.z;
+  long long m = -0x7FFFFFFFFFFFFFFFLL - 1;
+  if (row < height && col < width) m = __ldg(keys + (b * height + row) * width + col);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const long long other = __shfl_xor_sync(0xffffffffu, m, o);
+    m = other > m ? other : m;
+  }
+  if ((threadIdx.x & 31u) == 0u) warp_max[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 1; i < 8; ++i) m = warp_max[i] > m ? warp_max[i] : m;
+    tile_max[(b * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x] = m;
+  }
+}
+
+// Lower bound of the depth z / w that the exact test can give anywhere inside a triangle whose
+// vertices all have w > 0: the interpolated depth is a convex combination of the vertex depths
+// (the edge functions share one sign and so do the weights e_k w_k), up to a few float32
+// roundings of terms no larger than the largest |z_k / w_k|; 1e-5 of it covers them many times.
+// Returned as the ordered high word of the packed key.
+__device__ __forceinline__ int depth_floor_word(const Vert& v0, const Vert& v1, const Vert& v2) {
+  const float d0 = v0.z / v0.w, d1 = v1.z / v1.w, d2 = v2.z / v2.w;
+  const float mag = fmaxf(fmaxf(fabsf(d0), fabsf(d1)), fabsf(d2));
+  const float lb = fminf(fminf(d0, d1), d2) - (1e-5f * mag + 1e-30f);
+  if (!(lb == lb)) return -0x7FFFFFFF - 1;  // never set aside with a NaN bound
+  return static_cast<int>(pack_key(lb, 0) >> 32);
+}
+
+template <int kPass>
 __global__ void __launch_bounds__(256) setup_kernel(
     const float* __restrict__ pos, const int* __restrict__ tri, const Items items,
     long long total, int height, int width, const float* __restrict__ centres,
     const long long* __restrict__ prev, long long* __restrict__ keys,
-    unsigned long long* __restrict__ counters, Binned* __restrict__ binned, long long capacity) {
+    unsigned long long* __restrict__ counters, Binned* __restrict__ binned, long long capacity,
+    const Occlusion oc) {
   __shared__ WarpTris staged[8];
-  const long long g = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   const unsigned lane = threadIdx.x & 31u;
   WarpTris& w = staged[threadIdx.x >> 5];
+  // Passes 0 (everything) and 1 (setting aside) take one item per thread; pass 2 walks the
+  // records set aside with a grid-stride loop.
+  const long long items_n = kPass == 2 ? static_cast<long long>(*oc.count) : total;
+  const long long step = kPass == 2 ? static_cast<long long>(gridDim.x) * blockDim.x : items_n;
+  for (long long first = blockIdx.x * static_cast<long long>(blockDim.x); first < items_n;
+       first += step) {
+  const long long item = first + threadIdx.x;
+  long long g = item < items_n ? item : total;
+  if (kPass == 2 && item < items_n) {
+    const int4 rec = oc.list[item];
+    g = rec.x;
+    int vb, vt;
+    locate(items, g, vb, vt);
+    const long long* tm = oc.tile_max + static_cast<long long>(vb) * oc.tiles_per_view;
+    const int tx0 = rec.y & 0xFFFF, tx1 = static_cast<int>(static_cast<unsigned>(rec.y) >> 16);
+    const int ty0 = rec.z & 0xFFFF, ty1 = static_cast<int>(static_cast<unsigned>(rec.z) >> 16);
+    long long m = -0x7FFFFFFFFFFFFFFFLL - 1;
+    for (int ty = ty0; ty <= ty1; ++ty)
+      for (int tx = tx0; tx <= tx1; ++tx) {
+        const long long k = __ldg(tm + ty * oc.tiles_x + tx);
+        m = k > m ? k : m;
+      }
+    if ((static_cast<long long>(rec.w) << 32) > m) g = total;  // behind every pixel it touches
+  }
   bool large = false, direct = false;
   unsigned pairs = 0;
   int b = 0, t = 0, c0 = 0, c1 = -1, r0 = 0, r1 = -1;
@@ -240,6 +314,24 @@ __global__ void __launch_bounds__(256) setup_kernel(
         const long long area = static_cast<long long>(c1 - c0 + 1) * (r1 - r0 + 1);
         if (in_front && area <= kWarpPixels) {
           direct = true;
+          if (kPass == 1) {
+            const float ex = (nx[1] - nx[0]) * (ny[2] - ny[0]), ey = (ny[1] - ny[0]) * (nx[2] - nx[0]);
+            const float area2 = ex - ey;
+            if (area2 < -1e-3f * (fabsf(ex) + fabsf(ey))) {
+              direct = false;
+              const unsigned aside = __activemask();
+              const int rank_aside = __popc(aside & ((1u << lane) - 1u));
+              const int leader = __ffs(aside) - 1;
+              unsigned long long slot0 = 0;
+              if (static_cast<int>(lane) == leader)
+                slot0 = atomicAdd(oc.count, static_cast<unsigned long long>(__popc(aside)));
+              slot0 = __shfl_sync(aside, slot0, leader);
+              const int tx0 = c0 / kTile, tx1 = c1 / kTile, ty0 = r0 / kTile, ty1 = r1 / kTile;
+              oc.list[slot0 + rank_aside] =
+                  make_int4(static_cast<int>(g), tx0 | (tx1 << 16), ty0 | (ty1 << 16),
+                            depth_floor_word(v0, v1, v2));
+            }
+          }
         } else {
           large = true;
           const unsigned tx0 = c0 / kTile, tx1 = c1 / kTile, ty0 = r0 / kTile, ty1 = r1 / kTile;
@@ -393,16 +485,18 @@ __global__ void __launch_bounds__(256) setup_kernel(
   unsigned long long warp_pairs = pairs;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) warp_pairs += __shfl_xor_sync(0xffffffffu, warp_pairs, o);
-  if (mask == 0u) return;
-  unsigned long long slot0 = 0;
-  if (lane == 0) {
-    slot0 = atomicAdd(counters, static_cast<unsigned long long>(__popc(mask)));
-    atomicAdd(counters + 1, warp_pairs);
+  if (mask != 0u) {
+    unsigned long long slot0 = 0;
+    if (lane == 0) {
+      slot0 = atomicAdd(counters, static_cast<unsigned long long>(__popc(mask)));
+      atomicAdd(counters + 1, warp_pairs);
+    }
+    slot0 = __shfl_sync(0xffffffffu, slot0, 0);
+    if (large) {
+      const unsigned long long slot = slot0 + __popc(mask & ((1u << lane) - 1u));
+      if (slot < static_cast<unsigned long long>(capacity)) binned[slot] = {b, t, c0, c1, r0, r1};
+    }
   }
-  slot0 = __shfl_sync(0xffffffffu, slot0, 0);
-  if (large) {
-    const unsigned long long slot = slot0 + __popc(mask & ((1u << lane) - 1u));
-    if (slot < static_cast<unsigned long long>(capacity)) binned[slot] = {b, t, c0, c1, r0, r1};
   }
 }
 
@@ -927,12 +1021,56 @@ extern "C" size_t dr_raster_setup_workspace_bytes(int64_t capacity, int32_t heig
   return setup_bytes(capacity < 0 ? 0 : capacity, height < 0 ? 0 : height, width < 0 ? 0 : width);
 }
 
+namespace dr {
+namespace {
+
+// Occlusion workspace: the record count, the tile maxima, the records (one per item at most).
+struct OcclusionLayout {
+  unsigned long long* count;
+  long long* tile_max;
+  int4* list;
+};
+
+OcclusionLayout occlusion_layout(void* ws, int64_t batch, int height, int width) {
+  char* p = static_cast<char*>(ws);
+  const long long tiles = batch * static_cast<long long>((height + kTile - 1) / kTile) *
+                          ((width + kTile - 1) / kTile);
+  OcclusionLayout l;
+  l.count = reinterpret_cast<unsigned long long*>(p);
+  l.tile_max = reinterpret_cast<long long*>(p + 256);
+  l.list = reinterpret_cast<int4*>(p + 256 + align256(sizeof(long long) * static_cast<size_t>(tiles)));
+  return l;
+}
+
+size_t occlusion_bytes(int64_t total, int64_t batch, int height, int width) {
+  const long long tiles = batch * static_cast<long long>((height + kTile - 1) / kTile) *
+                          ((width + kTile - 1) / kTile);
+  return 256 + align256(sizeof(long long) * static_cast<size_t>(tiles)) +
+         align256(sizeof(int4) * static_cast<size_t>(total));
+}
+
+Occlusion make_occlusion(const OcclusionLayout& l, int height, int width) {
+  const int tiles_x = (width + kTile - 1) / kTile, tiles_y = (height + kTile - 1) / kTile;
+  return Occlusion{l.count, l.list, l.tile_max, tiles_x, tiles_x * tiles_y};
+}
+
+}  // namespace
+}  // namespace dr
+
+extern "C" size_t dr_raster_occlusion_workspace_bytes(int64_t total, int64_t batch,
+                                                      int32_t height, int32_t width) {
+  if (total < 0 || batch < 0 || height <= 0 || width <= 0) return 0;
+  return occlusion_bytes(total, batch, height, width);
+}
+
 extern "C" int dr_raster_setup(const float* pos, int64_t pos_batch, const int32_t* tri,
                                int64_t batch, int64_t num_vert, int64_t num_tri,
                                const int32_t* range_start, const int64_t* range_first,
                                int64_t range_total, int32_t height, int32_t width,
                                const int64_t* prev_keys, int64_t* keys, void* workspace,
-                               size_t workspace_bytes, int64_t capacity, void* stream) {
+                               size_t workspace_bytes, int64_t capacity,
+                               void* occlusion_workspace, size_t occlusion_workspace_bytes,
+                               void* stream) {
   const bool ranged = range_start != nullptr;
   if (bad_raster_args(pos, tri, batch, num_vert, num_tri, height, width, pos_batch) ||
       capacity < 0 || keys == nullptr || workspace == nullptr)
@@ -941,6 +1079,10 @@ extern "C" int dr_raster_setup(const float* pos, int64_t pos_batch, const int32_
     return DR_ERR_INVALID_ARGUMENT;
   if (!ranged && batch * num_tri >= (1LL << 31)) return DR_ERR_INVALID_ARGUMENT;
   if (workspace_bytes < setup_bytes(capacity, height, width)) return DR_ERR_WORKSPACE_TOO_SMALL;
+  const long long total = ranged ? range_total : batch * num_tri;
+  if (occlusion_workspace != nullptr &&
+      occlusion_workspace_bytes < occlusion_bytes(total, batch, height, width))
+    return DR_ERR_WORKSPACE_TOO_SMALL;
   cudaStream_t s = as_stream(stream);
   SetupLayout l = setup_layout(workspace, height, width);
   const long long pixels = batch * static_cast<long long>(height) * width;
@@ -951,16 +1093,65 @@ extern "C" int dr_raster_setup(const float* pos, int64_t pos_batch, const int32_
         reinterpret_cast<long long*>(keys), pixels);
   }
   centres_kernel<<<blocks_for(height + width, 256), 256, 0, s>>>(l.centres, height, width);
-  const long long total = ranged ? range_total : batch * num_tri;
   const Items items = {static_cast<int>(num_tri), static_cast<int>(batch), range_start,
                        reinterpret_cast<const long long*>(range_first),
                        pos_stride(pos_batch, num_vert)};
-  if (total > 0 && batch > 0) {
-    setup_kernel<<<blocks_for(total, 256), 256, 0, s>>>(
+  if (occlusion_workspace != nullptr) {
+    const OcclusionLayout ol = occlusion_layout(occlusion_workspace, batch, height, width);
+    err = cudaMemsetAsync(ol.count, 0, sizeof(unsigned long long), s);
+    if (err != cudaSuccess) return static_cast<int>(err);
+    if (total > 0 && batch > 0) {
+      setup_kernel<1><<<blocks_for(total, 256), 256, 0, s>>>(
+          pos, tri, items, total, height, width, l.centres,
+          reinterpret_cast<const long long*>(prev_keys), reinterpret_cast<long long*>(keys),
+          l.counters, l.binned, capacity, make_occlusion(ol, height, width));
+    }
+  } else if (total > 0 && batch > 0) {
+    setup_kernel<0><<<blocks_for(total, 256), 256, 0, s>>>(
         pos, tri, items, total, height, width, l.centres,
         reinterpret_cast<const long long*>(prev_keys), reinterpret_cast<long long*>(keys),
-        l.counters, l.binned, capacity);
+        l.counters, l.binned, capacity, Occlusion{nullptr, nullptr, nullptr, 0, 0});
   }
+  return launch_status();
+}
+
+extern "C" int dr_raster_occluded(const float* pos, int64_t pos_batch, const int32_t* tri,
+                                  int64_t batch, int64_t num_vert, int64_t num_tri,
+                                  const int32_t* range_start, const int64_t* range_first,
+                                  int64_t range_total, int32_t height, int32_t width,
+                                  const int64_t* prev_keys, int64_t* keys,
+                                  const void* setup_workspace, void* occlusion_workspace,
+                                  size_t occlusion_workspace_bytes, void* stream) {
+  const bool ranged = range_start != nullptr;
+  if (bad_raster_args(pos, tri, batch, num_vert, num_tri, height, width, pos_batch) ||
+      keys == nullptr || setup_workspace == nullptr || occlusion_workspace == nullptr)
+    return DR_ERR_INVALID_ARGUMENT;
+  if (ranged && (range_first == nullptr || range_total < 0 || range_total >= (1LL << 31)))
+    return DR_ERR_INVALID_ARGUMENT;
+  const long long total = ranged ? range_total : batch * num_tri;
+  if (!ranged && total >= (1LL << 31)) return DR_ERR_INVALID_ARGUMENT;
+  if (occlusion_workspace_bytes < occlusion_bytes(total, batch, height, width))
+    return DR_ERR_WORKSPACE_TOO_SMALL;
+  if (total == 0 || batch == 0) return DR_OK;
+  if (batch > 65535 || height >= (1 << 20)) return DR_ERR_TOO_LARGE;
+  cudaStream_t s = as_stream(stream);
+  SetupLayout l = setup_layout(setup_workspace, height, width);
+  const OcclusionLayout ol = occlusion_layout(occlusion_workspace, batch, height, width);
+  const Occlusion oc = make_occlusion(ol, height, width);
+  tile_max_kernel<<<dim3(oc.tiles_x, oc.tiles_per_view / oc.tiles_x, static_cast<unsigned>(batch)),
+                    256, 0, s>>>(reinterpret_cast<const long long*>(keys), height, width,
+                                 ol.tile_max);
+  const Items items = {static_cast<int>(num_tri), static_cast<int>(batch), range_start,
+                       reinterpret_cast<const long long*>(range_first),
+                       pos_stride(pos_batch, num_vert)};
+  // Nothing is binned here (every record is a small triangle), so the list is not touched.
+  const unsigned grid = static_cast<unsigned>(
+      min(static_cast<long long>(blocks_for(total, 256)),
+          static_cast<long long>(resident_blocks(setup_kernel<2>, 256))));
+  setup_kernel<2><<<grid, 256, 0, s>>>(pos, tri, items, total, height, width, l.centres,
+                                       reinterpret_cast<const long long*>(prev_keys),
+                                       reinterpret_cast<long long*>(keys), l.counters, l.binned, 0,
+                                       oc);
   return launch_status();
 }
 

@@ -78,7 +78,27 @@ int dr_raster_setup(const float* pos, int64_t pos_batch, const int32_t* tri, int
                     int64_t num_vert, int64_t num_tri, const int32_t* range_start,
                     const int64_t* range_first, int64_t range_total, int32_t height,
                     int32_t width, const int64_t* prev_keys, int64_t* keys, void* workspace,
-                    size_t workspace_bytes, int64_t capacity, void* stream);
+                    size_t workspace_bytes, int64_t capacity, void* occlusion_workspace,
+                    size_t occlusion_workspace_bytes, void* stream);
+
+/* Scratch of the occlusion pass for `total` (view, triangle) items (batch * num_tri, or the
+ * range total) at this resolution: about 16 bytes per item. */
+size_t dr_raster_occlusion_workspace_bytes(int64_t total, int64_t batch, int32_t height,
+                                           int32_t width);
+
+/* Occlusion pass. Given an occlusion workspace, dr_raster_setup sets aside the small triangles
+ * whose projection has negative orientation (the far side of a closed mesh whose front faces are
+ * counter-clockwise) instead of drawing them. After stage 2, dr_raster_occluded takes the largest
+ * key of every 16 x 16 tile and draws the set-aside triangles, skipping each one whose depth,
+ * bounded below from its vertices, lies above the largest key of every tile its pixel box
+ * touches: such a triangle is behind what every one of its pixels already shows, so the keys are
+ * exactly those of a single pass. Same arguments as dr_raster_setup otherwise. */
+int dr_raster_occluded(const float* pos, int64_t pos_batch, const int32_t* tri, int64_t batch,
+                       int64_t num_vert, int64_t num_tri, const int32_t* range_start,
+                       const int64_t* range_first, int64_t range_total, int32_t height,
+                       int32_t width, const int64_t* prev_keys, int64_t* keys,
+                       const void* setup_workspace, void* occlusion_workspace,
+                       size_t occlusion_workspace_bytes, void* stream);
 
 /* Reads the two counters of stage 1: triangles to bin and (triangle, tile) pairs. Synchronises
  * `stream`. */

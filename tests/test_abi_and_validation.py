@@ -41,13 +41,17 @@ def test_invalid_arguments_are_rejected_without_a_gpu():
     lib = _native.lib()
     # Negative sizes and null pointers fail validation before any CUDA call.
     assert lib.dr_raster_setup(None, 1, None, -1, 0, 0, None, None, 0, 4, 4, None, None, None, 0, 0,
-                               None) == 10001
+                               None, 0, None) == 10001
     # pos_batch must be 1 or the view count; range mode needs its prefix table.
     pos = ctypes.c_void_p(16)
     assert lib.dr_raster_setup(pos, 3, pos, 2, 3, 1, None, None, 0, 4, 4, None, pos, pos, 1 << 20,
-                               1024, None) == 10001
+                               1024, None, 0, None) == 10001
     assert lib.dr_raster_setup(pos, 1, pos, 2, 3, 1, pos, None, 1, 4, 4, None, pos, pos, 1 << 20,
-                               1024, None) == 10001
+                               1024, None, 0, None) == 10001
+    # An occlusion workspace too small for the items is refused before any launch.
+    assert lib.dr_raster_setup(pos, 2, pos, 2, 3, 1, None, None, 0, 4, 4, None, pos, pos, 1 << 20,
+                               1024, pos, 16, None) == 10002
+    assert lib.dr_raster_occlusion_workspace_bytes(1000, 2, 64, 64) >= 16000
     assert lib.dr_raster_resolve_fwd(pos, 3, pos, pos, 2, 3, 1, 4, 4, pos, pos, None) == 10001
     assert lib.dr_interpolate_fwd(None, 0, 0, 1, 0, None, None, None, 0, None, 0, 1, 1, 1, None, None, None) == 10001
     assert lib.dr_edge_neighbours(None, -5, None, None, 0, None) == 10001
