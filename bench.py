@@ -234,6 +234,10 @@ def run_ours(args) -> None:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    # All work, eager and captured, runs on one non-default stream, so that the gradient
+    # accumulators autograd keeps between steps belong to the stream the graphs capture on.
+    work = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(work)
     if world > 1:
         from datetime import timedelta
 
@@ -257,7 +261,7 @@ def run_ours(args) -> None:
     # transform's backward at the end of the step (no-ops on one GPU).
     reducer = OverlappedGradientSum([tex, verts])
 
-    def step(mvp_in, target_in):
+    def step(mvp_in, target_in, before_loss=None):
         verts.grad = None
         tex.grad = None
         pos = dr.to_clip(verts, mvp_in)
@@ -267,6 +271,8 @@ def run_ours(args) -> None:
         # Antialias and the MSE against the target in one pass (dr.antialias_mse fuses the loss
         # into the antialias kernels); the mean runs over the whole job's pixels, so that the
         # ranks' gradients sum to the full batch's.
+        if before_loss is not None:
+            before_loss()
         _, loss = dr.antialias_mse(color, rast, pos, tri, target_in, topology_hash=topo,
                                    scale=1.0 / (args.views * res * res * TEX_CHANNELS))
         loss.backward()
@@ -317,7 +323,7 @@ def run_ours(args) -> None:
         key = mvp_in.data_ptr()
         if key not in runners:
             graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
+            with torch.cuda.graph(graph, stream=work):
                 loss = step(mvp_in, target_in)
             graphs.append(graph)
             runners[key] = lambda: (graph.replay(), loss)[1]
@@ -357,17 +363,30 @@ def run_ours(args) -> None:
             buffers[slot][1].copy_(target_host, non_blocking=True)
             ready[slot].record(copy_stream)
 
+    target_ready = torch.cuda.Event()
+
     def e2e_loop():
         main = torch.cuda.current_stream(dev)
         for slot in range(2):
             free[slot].record(main)
-        upload(0)
+        # The first step's target is needed only by the antialias pass, so its copy overlaps the
+        # step's first kernels (the matrices, 4 KB, go first); that step launches eagerly to wait
+        # for it there. Later steps' inputs arrive during the step before.
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(free[0])
+            buffers[0][0].copy_(mvp_host, non_blocking=True)
+            ready[0].record(copy_stream)
+            buffers[0][1].copy_(target_host, non_blocking=True)
+            target_ready.record(copy_stream)
         for i in range(args.steps):
             slot = i % 2
             main.wait_event(ready[slot])
             if i + 1 < args.steps:
                 upload(1 - slot)
-            loss = slot_runs[slot]()
+            if i == 0:
+                loss = step(*buffers[0], before_loss=lambda: main.wait_event(target_ready))
+            else:
+                loss = slot_runs[slot]()
             free[slot].record(main)
             loss.item()
 
