@@ -316,6 +316,7 @@ def run_ours(args) -> None:
     use_graph = not args.eager
     runners: dict[int, object] = {}
     graphs: list = []
+    launch_note = "CUDA graph of the step" if use_graph else "eager"
 
     def runner(mvp_in, target_in):
         if not use_graph:
@@ -331,7 +332,14 @@ def run_ours(args) -> None:
 
     ms = ms_eager
     if use_graph:
-        run_resident = runner(mvp, target)
+        try:
+            run_resident = runner(mvp, target)
+        except RuntimeError as exc:  # every rank captures the same step, so all fall back alike
+            print(f"bench.py: CUDA graph capture failed, launching eagerly: {exc}", file=sys.stderr)
+            use_graph = False
+            launch_note = "eager (graph capture failed)"
+            torch.cuda.synchronize()
+    if use_graph:
         run_resident()
         torch.cuda.synchronize()
         with ClockSampler(gpu_id(dev)) as graph_clocks:
@@ -458,7 +466,7 @@ def run_ours(args) -> None:
                         "MSE, fwd+bwd to tex and pos",
             "views": args.views, "resolution": res, "triangles": int(tri.shape[0]),
             "vertices": num_vert, "tex": args.tex, "parallelism": f"views sharded dp{world}",
-            "launch": "CUDA graph of the step" if use_graph else "eager",
+            "launch": launch_note,
             "inputs": "per step: the views' 4x4 camera matrices and target images; mesh (world "
                       "positions) and texture are parameters resident on the GPU",
             "l2": "working set larger than L2 (clip positions 671 MB, rast 1 GB per step), no flush",
