@@ -854,7 +854,7 @@ __device__ __forceinline__ void texture_bwd_tile(
 // Persistent blocks walk the 16 x 16 pixel tiles of all views; each warp keeps its hot quad across
 // the tiles it visits and flushes it at the end.
 template <int MODE, int B, bool RGB>
-__global__ void __launch_bounds__(256, B == DR_BOUNDARY_CUBE ? 2 : 4) texture_bwd_kernel(
+__global__ void __launch_bounds__(256, B == DR_BOUNDARY_CUBE ? 2 : 3) texture_bwd_kernel(
     const Levels L, int channels, int grad_stride, const float* __restrict__ uv,
     const float* __restrict__ uv_da, const float* __restrict__ bias, const Strides st, int height,
     int width, const float* __restrict__ grad_out, float* __restrict__ grad_uv,
