@@ -141,6 +141,17 @@ def raster_keys(pos: Tensor, tri: Tensor, height: int, width: int, prev_keys: Te
         occl = _scratch(lib.dr_raster_occlusion_workspace_bytes(total, batch, height, width), dev)
     occl_ptr, occl_bytes = (occl.data_ptr(), occl.numel()) if occl is not None else (None, 0)
 
+    def setup(cap):
+        ws = _scratch(lib.dr_raster_setup_workspace_bytes(cap, height, width), dev)
+        N.check(
+            lib.dr_raster_setup(pos.data_ptr(), pos_batch, tri.data_ptr(), batch, num_vert,
+                                num_tri, rs, rf, total, height, width, N.ptr(prev_keys),
+                                keys.data_ptr(), ws.data_ptr(), ws.numel(), cap, occl_ptr,
+                                occl_bytes, s),
+            "dr_raster_setup",
+        )  # fmt: skip
+        return ws
+
     def occluded(setup_ws):
         if occl is None:
             return
@@ -162,14 +173,7 @@ def raster_keys(pos: Tensor, tri: Tensor, height: int, width: int, prev_keys: Te
                 "before capturing it (the captured call reuses capacities measured eagerly)."
             )
         cap, pair_cap = caps
-        ws = _scratch(lib.dr_raster_setup_workspace_bytes(cap, height, width), dev)
-        N.check(
-            lib.dr_raster_setup(pos.data_ptr(), pos_batch, tri.data_ptr(), batch, num_vert,
-                                num_tri, rs, rf, total, height, width, N.ptr(prev_keys),
-                                keys.data_ptr(), ws.data_ptr(), ws.numel(), cap, occl_ptr,
-                                occl_bytes, s),
-            "dr_raster_setup",
-        )  # fmt: skip
+        ws = setup(cap)
         bws = _scratch(lib.dr_raster_bin_workspace_bytes(batch, height, width, pair_cap), dev)
         N.check(
             lib.dr_raster_tiles_device(pos.data_ptr(), pos_batch, tri.data_ptr(), batch, num_vert,
@@ -183,14 +187,7 @@ def raster_keys(pos: Tensor, tri: Tensor, height: int, width: int, prev_keys: Te
     overflow_word(dev)
     binned, pairs = c_int64(0), c_int64(0)
     for _ in range(2):
-        ws = _scratch(lib.dr_raster_setup_workspace_bytes(cap, height, width), dev)
-        N.check(
-            lib.dr_raster_setup(pos.data_ptr(), pos_batch, tri.data_ptr(), batch, num_vert,
-                                num_tri, rs, rf, total, height, width, N.ptr(prev_keys),
-                                keys.data_ptr(), ws.data_ptr(), ws.numel(), cap, occl_ptr,
-                                occl_bytes, s),
-            "dr_raster_setup",
-        )  # fmt: skip
+        ws = setup(cap)
         N.check(lib.dr_raster_counts(ws.data_ptr(), byref(binned), byref(pairs), s), "dr_raster_counts")
         if binned.value <= cap:
             break
