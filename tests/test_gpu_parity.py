@@ -537,3 +537,27 @@ def test_config1_pipeline_matches_oracle(ctx):
     assert abs(ours[1] - ref[1]) < 1e-5
     grad_close(ours[2], ref[2], 2e-3)
     grad_close(ours[3], ref[3], 1e-3)
+
+
+def test_second_order_gradients_are_refused(ctx):
+    """Every op's backward is first-order only, like the reference's guard
+    (diffrast backends/_autograd.py:11-35): asking it to build a graph raises."""
+    pos, tri = scenes.random_mesh(20, torch.Generator().manual_seed(5))
+    pos = pos.cuda().requires_grad_(True)
+    tri = tri.cuda()
+    tex = torch.rand(1, 16, 16, 3, device=CUDA, requires_grad=True)
+    world = torch.rand(9, 3, device=CUDA, requires_grad=True)
+    mats = torch.eye(4, device=CUDA)[None].repeat(2, 1, 1)
+    rast = dr.rasterize(ctx, pos.detach(), tri, (16, 16))[0]
+    cases = [
+        lambda: dr.rasterize(ctx, pos, tri, (16, 16))[0][..., :3],
+        lambda: dr.interpolate(pos[0, :, :3].contiguous(), rast, tri)[0],
+        lambda: dr.texture(tex, torch.rand(1, 8, 8, 2, device=CUDA)),
+        lambda: dr.antialias(torch.rand(1, 16, 16, 3, device=CUDA, requires_grad=True), rast, pos,
+                             tri),
+        lambda: dr.to_clip(world, mats),
+    ]
+    for make in cases:
+        out = make()
+        with pytest.raises(RuntimeError, match="no second-order gradients"):
+            torch.autograd.grad(out.sum(), [pos, tex, world], create_graph=True, allow_unused=True)
