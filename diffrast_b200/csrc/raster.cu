@@ -245,258 +245,261 @@ __global__ void __launch_bounds__(256) setup_kernel(
   const long long step = kPass == 2 ? static_cast<long long>(gridDim.x) * blockDim.x : items_n;
   for (long long first = blockIdx.x * static_cast<long long>(blockDim.x); first < items_n;
        first += step) {
-  const long long item = first + threadIdx.x;
-  long long g = item < items_n ? item : total;
-  if (kPass == 2 && item < items_n) {
-    const int4 rec = oc.list[item];
-    g = rec.x;
-    int vb, vt;
-    locate(items, g, vb, vt);
-    const long long* tm = oc.tile_max + static_cast<long long>(vb) * oc.tiles_per_view;
-    const int tx0 = rec.y & 0xFFFF, tx1 = static_cast<int>(static_cast<unsigned>(rec.y) >> 16);
-    const int ty0 = rec.z & 0xFFFF, ty1 = static_cast<int>(static_cast<unsigned>(rec.z) >> 16);
-    long long m = -0x7FFFFFFFFFFFFFFFLL - 1;
-    for (int ty = ty0; ty <= ty1; ++ty)
-      for (int tx = tx0; tx <= tx1; ++tx) {
-        const long long k = __ldg(tm + ty * oc.tiles_x + tx);
-        m = k > m ? k : m;
-      }
-    if ((static_cast<long long>(rec.w) << 32) > m) g = total;  // behind every pixel it touches
-  }
-  bool large = false, direct = false;
-  unsigned pairs = 0;
-  int b = 0, t = 0, c0 = 0, c1 = -1, r0 = 0, r1 = -1;
-  Vert v0 = {0.f, 0.f, 0.f, 1.f}, v1 = v0, v2 = v0;
-  float nx[3] = {0.f, 0.f, 0.f}, ny[3] = {0.f, 0.f, 0.f};
-  if (g < total) {
-    locate(items, g, b, t);
-    const int i0 = __ldg(tri + 3 * static_cast<long long>(t));
-    const int i1 = __ldg(tri + 3 * static_cast<long long>(t) + 1);
-    const int i2 = __ldg(tri + 3 * static_cast<long long>(t) + 2);
-    const long long base = static_cast<long long>(b) * items.pos_stride;
-    v0 = load_vert(pos, base + i0);
-    v1 = load_vert(pos, base + i1);
-    v2 = load_vert(pos, base + i2);
-    // A triangle is invisible when all vertices are behind the camera or outside the same side
-    // plane; every covered point is a non-negative combination of the vertices. Non-finite
-    // vertices are never drawn (reference.py:334).
-    bool culled = !(finite4(v0) && finite4(v1) && finite4(v2));
-    culled |= (v0.w <= 0.0f) && (v1.w <= 0.0f) && (v2.w <= 0.0f);
-    culled |= (v0.x > v0.w) && (v1.x > v1.w) && (v2.x > v2.w);
-    culled |= (v0.x < -v0.w) && (v1.x < -v1.w) && (v2.x < -v2.w);
-    culled |= (v0.y > v0.w) && (v1.y > v1.w) && (v2.y > v2.w);
-    culled |= (v0.y < -v0.w) && (v1.y < -v1.w) && (v2.y < -v2.w);
-    if (!culled) {
-      const bool in_front = (v0.w > 0.0f) && (v1.w > 0.0f) && (v2.w > 0.0f);
-      c0 = 0;
-      c1 = width - 1;
-      r0 = 0;
-      r1 = height - 1;
-      if (in_front) {
-        // Projected vertices bound the pixels to test, never decide coverage; bounds are widened
-        // by margins far above the error of the fast reciprocal used for ordinary w.
-        const Vert* vs[3] = {&v0, &v1, &v2};
-        for (int k = 0; k < 3; ++k) {
-          const float wk = vs[k]->w;
-          if (wk >= 1e-30f && wk <= 1e30f) {
-            const float iw = __fdividef(1.0f, wk);
-            nx[k] = vs[k]->x * iw;
-            ny[k] = vs[k]->y * iw;
-          } else {
-            nx[k] = vs[k]->x / wk;
-            ny[k] = vs[k]->y / wk;
-          }
+    const long long item = first + threadIdx.x;
+    long long g = item < items_n ? item : total;
+    if (kPass == 2 && item < items_n) {
+      const int4 rec = oc.list[item];
+      g = rec.x;
+      int vb, vt;
+      locate(items, g, vb, vt);
+      const long long* tm = oc.tile_max + static_cast<long long>(vb) * oc.tiles_per_view;
+      const int tx0 = rec.y & 0xFFFF, tx1 = static_cast<int>(static_cast<unsigned>(rec.y) >> 16);
+      const int ty0 = rec.z & 0xFFFF, ty1 = static_cast<int>(static_cast<unsigned>(rec.z) >> 16);
+      long long m = -0x7FFFFFFFFFFFFFFFLL - 1;
+      for (int ty = ty0; ty <= ty1; ++ty)
+        for (int tx = tx0; tx <= tx1; ++tx) {
+          const long long k = __ldg(tm + ty * oc.tiles_x + tx);
+          m = k > m ? k : m;
         }
-        pixel_range(fminf(fminf(nx[0], nx[1]), nx[2]), fmaxf(fmaxf(nx[0], nx[1]), nx[2]), width, c0, c1);
-        pixel_range(fminf(fminf(ny[0], ny[1]), ny[2]), fmaxf(fmaxf(ny[0], ny[1]), ny[2]), height, r0, r1);
-      }
-      if (c0 <= c1 && r0 <= r1) {
-        const long long area = static_cast<long long>(c1 - c0 + 1) * (r1 - r0 + 1);
-        if (in_front && area <= kWarpPixels) {
-          direct = true;
-          if (kPass == 1) {
-            const float ex = (nx[1] - nx[0]) * (ny[2] - ny[0]), ey = (ny[1] - ny[0]) * (nx[2] - nx[0]);
-            const float area2 = ex - ey;
-            if (area2 < -1e-3f * (fabsf(ex) + fabsf(ey))) {
-              direct = false;
-              const unsigned aside = __activemask();
-              const int rank_aside = __popc(aside & ((1u << lane) - 1u));
-              const int leader = __ffs(aside) - 1;
-              unsigned long long slot0 = 0;
-              if (static_cast<int>(lane) == leader)
-                slot0 = atomicAdd(oc.count, static_cast<unsigned long long>(__popc(aside)));
-              slot0 = __shfl_sync(aside, slot0, leader);
-              const int tx0 = c0 / kTile, tx1 = c1 / kTile, ty0 = r0 / kTile, ty1 = r1 / kTile;
-              oc.list[slot0 + rank_aside] =
-                  make_int4(static_cast<int>(g), tx0 | (tx1 << 16), ty0 | (ty1 << 16),
-                            depth_floor_word(v0, v1, v2));
+      if ((static_cast<long long>(rec.w) << 32) > m) g = total;  // behind every pixel it touches
+    }
+    bool large = false, direct = false;
+    unsigned pairs = 0;
+    int b = 0, t = 0, c0 = 0, c1 = -1, r0 = 0, r1 = -1;
+    Vert v0 = {0.f, 0.f, 0.f, 1.f}, v1 = v0, v2 = v0;
+    float nx[3] = {0.f, 0.f, 0.f}, ny[3] = {0.f, 0.f, 0.f};
+    if (g < total) {
+      locate(items, g, b, t);
+      const int i0 = __ldg(tri + 3 * static_cast<long long>(t));
+      const int i1 = __ldg(tri + 3 * static_cast<long long>(t) + 1);
+      const int i2 = __ldg(tri + 3 * static_cast<long long>(t) + 2);
+      const long long base = static_cast<long long>(b) * items.pos_stride;
+      v0 = load_vert(pos, base + i0);
+      v1 = load_vert(pos, base + i1);
+      v2 = load_vert(pos, base + i2);
+      // A triangle is invisible when all vertices are behind the camera or outside the same side
+      // plane; every covered point is a non-negative combination of the vertices. Non-finite
+      // vertices are never drawn (reference.py:334).
+      bool culled = !(finite4(v0) && finite4(v1) && finite4(v2));
+      culled |= (v0.w <= 0.0f) && (v1.w <= 0.0f) && (v2.w <= 0.0f);
+      culled |= (v0.x > v0.w) && (v1.x > v1.w) && (v2.x > v2.w);
+      culled |= (v0.x < -v0.w) && (v1.x < -v1.w) && (v2.x < -v2.w);
+      culled |= (v0.y > v0.w) && (v1.y > v1.w) && (v2.y > v2.w);
+      culled |= (v0.y < -v0.w) && (v1.y < -v1.w) && (v2.y < -v2.w);
+      if (!culled) {
+        const bool in_front = (v0.w > 0.0f) && (v1.w > 0.0f) && (v2.w > 0.0f);
+        c0 = 0;
+        c1 = width - 1;
+        r0 = 0;
+        r1 = height - 1;
+        if (in_front) {
+          // Projected vertices bound the pixels to test, never decide coverage; bounds are widened
+          // by margins far above the error of the fast reciprocal used for ordinary w.
+          const Vert* vs[3] = {&v0, &v1, &v2};
+          for (int k = 0; k < 3; ++k) {
+            const float wk = vs[k]->w;
+            if (wk >= 1e-30f && wk <= 1e30f) {
+              const float iw = __fdividef(1.0f, wk);
+              nx[k] = vs[k]->x * iw;
+              ny[k] = vs[k]->y * iw;
+            } else {
+              nx[k] = vs[k]->x / wk;
+              ny[k] = vs[k]->y / wk;
             }
           }
-        } else {
-          large = true;
-          const unsigned tx0 = c0 / kTile, tx1 = c1 / kTile, ty0 = r0 / kTile, ty1 = r1 / kTile;
-          pairs = (tx1 - tx0 + 1) * (ty1 - ty0 + 1);
+          pixel_range(fminf(fminf(nx[0], nx[1]), nx[2]), fmaxf(fmaxf(nx[0], nx[1]), nx[2]), width,
+                      c0, c1);
+          pixel_range(fminf(fminf(ny[0], ny[1]), ny[2]), fmaxf(fmaxf(ny[0], ny[1]), ny[2]), height,
+                      r0, r1);
+        }
+        if (c0 <= c1 && r0 <= r1) {
+          const long long area = static_cast<long long>(c1 - c0 + 1) * (r1 - r0 + 1);
+          if (in_front && area <= kWarpPixels) {
+            direct = true;
+            if (kPass == 1) {
+              const float ex = (nx[1] - nx[0]) * (ny[2] - ny[0]);
+              const float ey = (ny[1] - ny[0]) * (nx[2] - nx[0]);
+              const float area2 = ex - ey;
+              if (area2 < -1e-3f * (fabsf(ex) + fabsf(ey))) {
+                direct = false;
+                const unsigned aside = __activemask();
+                const int rank_aside = __popc(aside & ((1u << lane) - 1u));
+                const int leader = __ffs(aside) - 1;
+                unsigned long long slot0 = 0;
+                if (static_cast<int>(lane) == leader)
+                  slot0 = atomicAdd(oc.count, static_cast<unsigned long long>(__popc(aside)));
+                slot0 = __shfl_sync(aside, slot0, leader);
+                const int tx0 = c0 / kTile, tx1 = c1 / kTile, ty0 = r0 / kTile, ty1 = r1 / kTile;
+                oc.list[slot0 + rank_aside] =
+                    make_int4(static_cast<int>(g), tx0 | (tx1 << 16), ty0 | (ty1 << 16),
+                              depth_floor_word(v0, v1, v2));
+              }
+            }
+          } else {
+            large = true;
+            const unsigned tx0 = c0 / kTile, tx1 = c1 / kTile, ty0 = r0 / kTile, ty1 = r1 / kTile;
+            pairs = (tx1 - tx0 + 1) * (ty1 - ty0 + 1);
+          }
         }
       }
     }
-  }
-  // Stage the direct triangles in rank order. Their rows are distributed over the lanes (phase A:
-  // each lane bounds one row by the triangle's half-planes), then the pixels inside those row
-  // spans are distributed over the lanes again (phase B: one exact test per lane), so lanes stay
-  // busy whatever the shape of the triangles.
-  const unsigned direct_mask = __ballot_sync(0xffffffffu, direct);
-  const int rank = __popc(direct_mask & ((1u << lane) - 1u));
-  const int rows = direct ? r1 - r0 + 1 : 0;
-  int end = rows;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xffffffffu, end, o);
-    if (static_cast<int>(lane) >= o) end += y;
-  }
-  const int all_rows = __shfl_sync(0xffffffffu, end, 31);
-  if (direct) {
-    w.v[0][rank] = make_float4(v0.x, v0.y, v0.z, v0.w);
-    w.v[1][rank] = make_float4(v1.x, v1.y, v1.z, v1.w);
-    w.v[2][rank] = make_float4(v2.x, v2.y, v2.z, v2.w);
-    const float2 reach = coverage_reach(v0, v1, v2);
-    w.aux[rank] = make_float4(reach.x, reach.y, __int_as_float(t), __int_as_float(b));
-    // Half-planes of the projected triangle, oriented inwards and widened by a margin that
-    // covers the rounding of x / w and of the exact homogeneous test many times over. A triangle
-    // whose projected orientation is not clear-cut keeps whole bounding-box rows.
-    const float ex = (nx[1] - nx[0]) * (ny[2] - ny[0]), ey = (ny[1] - ny[0]) * (nx[2] - nx[0]);
-    const float area2 = ex - ey;
-    const bool spans = fabsf(area2) > 1e-3f * (fabsf(ex) + fabsf(ey));
-    w.info[rank] = make_int4(r0 - (end - rows), c0, c1, spans ? 1 : 0);
-    const float o = area2 > 0.0f ? 1.0f : -1.0f;
-    const float size = static_cast<float>(max(width, height));
-    const float delta = (0.01f + size * 1e-6f) * 2.0f / static_cast<float>(min(width, height));
-    for (int k = 0; k < 3; ++k) {
-      const int i = (k + 1) % 3, j = (k + 2) % 3;
-      const float A = -o * (ny[j] - ny[i]), B = o * (nx[j] - nx[i]);
-      const float C = -(A * nx[i] + B * ny[i]);
-      const float D = delta * approx_sqrt(A * A + B * B) +
-                      4e-6f * (fabsf(A) + fabsf(B)) * (1.0f + fabsf(nx[i]) + fabsf(ny[i]));
-      // Row bounds are x >= (-(B y + C) - D) / A (A > 0) or x <= it (A < 0): keep 1 / A.
-      w.edge[k][rank] = make_float4(A != 0.0f ? approx_rcp(A) : 0.0f, B, C + D, A);
-    }
-  }
-  __syncwarp();
-  // Rows with pixels to test join a ring of kRing records; exact tests run 32 pixels at a time as
-  // soon as 32 are queued (and once more at the end), so that the pixels of consecutive row
-  // batches share test iterations. After a drain fewer than 32 pixels (so at most 31 rows) are
-  // pending and a batch adds at most 32 rows, so the ring never overwrites a pending row.
-  int done = 0;           // triangles whose rows all precede this batch
-  int queued_rows = 0;    // rows appended to the ring so far
-  int consumed_rows = 0;  // rows whose pixels have all been tested
-  int queued_px = 0;      // pixels appended so far
-  int tested_px = 0;      // pixels tested so far
-  for (int base = 0; base < all_rows; base += 32) {
-    // Phase A. Bit e - base - 1 marks a triangle whose rows end at e within (base, base + 32];
-    // the owner of row item base + lane is the number of triangles ending at or before it.
-    unsigned bit = 0u;
-    if (direct && end > base && end <= base + 32) bit = 1u << (end - base - 1);
-    const unsigned ends = __reduce_or_sync(0xffffffffu, bit);
-    const int item = base + static_cast<int>(lane);
-    const int k = done + __popc(ends & ((1u << lane) - 1u));
-    done += __popc(ends);
-    int count = 0, row = 0, cl = 0;
-    float py = 0.0f;
-    if (item < all_rows) {
-      const int4 info = w.info[k];
-      row = info.x + item;
-      cl = info.y;
-      int cr = info.z;
-      py = __ldg(centres + width + row);
-      if (info.w) {
-        float lo = -__int_as_float(0x7f800000), hi = __int_as_float(0x7f800000);
-        bool empty = false;
-        for (int e = 0; e < 3; ++e) {
-          const float4 h = w.edge[e][k];  // (1 / A, B, C + D, A)
-          const float rhs = -(h.y * py + h.z);
-          if (h.w > 0.0f) lo = fmaxf(lo, rhs * h.x);
-          else if (h.w < 0.0f) hi = fminf(hi, rhs * h.x);
-          else empty |= rhs > 0.0f;
-        }
-        if (empty || !(lo <= hi)) {
-          cr = cl - 1;
-        } else {
-          int sl, sr;
-          pixel_range(lo, hi, width, sl, sr);
-          cl = max(cl, sl);
-          cr = min(cr, sr);
-        }
-      }
-      count = max(0, cr - cl + 1);
-    }
-    // Append the rows that have pixels, numbering their pixels after those already queued.
-    const unsigned busy = __ballot_sync(0xffffffffu, count > 0);
-    const int slot = __popc(busy & ((1u << lane) - 1u));
-    int pix_end = count;
+    // Stage the direct triangles in rank order. Their rows are distributed over the lanes (phase A:
+    // each lane bounds one row by the triangle's half-planes), then the pixels inside those row
+    // spans are distributed over the lanes again (phase B: one exact test per lane), so lanes stay
+    // busy whatever the shape of the triangles.
+    const unsigned direct_mask = __ballot_sync(0xffffffffu, direct);
+    const int rank = __popc(direct_mask & ((1u << lane) - 1u));
+    const int rows = direct ? r1 - r0 + 1 : 0;
+    int end = rows;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, pix_end, o);
-      if (static_cast<int>(lane) >= o) pix_end += y;
+      const int y = __shfl_up_sync(0xffffffffu, end, o);
+      if (static_cast<int>(lane) >= o) end += y;
     }
-    if (count > 0) {
-      const int q = (queued_rows + slot) & (kRing - 1);
-      const int last = queued_px + pix_end;  // pixels queued up to the end of this row
-      // (triangle rank, row, column of pixel number 0 of this row's numbering, end)
-      w.row[q] = make_int4(k | (row << 5), cl - (last - count), last, __float_as_int(py));
-    }
-    queued_rows += __popc(busy);
-    queued_px += __shfl_sync(0xffffffffu, pix_end, 31);
-    __syncwarp();
-    // Phase B: one exact coverage test per lane.
-    const bool final_batch = base + 32 >= all_rows;
-    while (queued_px - tested_px >= 32 || (final_batch && queued_px > tested_px)) {
-      // Rows ending within (tested_px, tested_px + 32] mark their last pixel; the owner of pixel
-      // tested_px + lane is the number of such rows ending before it.
-      const int n = consumed_rows + static_cast<int>(lane);
-      unsigned pbit = 0u;
-      if (n < queued_rows) {
-        const int e = w.row[n & (kRing - 1)].z;
-        if (e <= tested_px + 32) pbit = 1u << (e - tested_px - 1);
+    const int all_rows = __shfl_sync(0xffffffffu, end, 31);
+    if (direct) {
+      w.v[0][rank] = make_float4(v0.x, v0.y, v0.z, v0.w);
+      w.v[1][rank] = make_float4(v1.x, v1.y, v1.z, v1.w);
+      w.v[2][rank] = make_float4(v2.x, v2.y, v2.z, v2.w);
+      const float2 reach = coverage_reach(v0, v1, v2);
+      w.aux[rank] = make_float4(reach.x, reach.y, __int_as_float(t), __int_as_float(b));
+      // Half-planes of the projected triangle, oriented inwards and widened by a margin that
+      // covers the rounding of x / w and of the exact homogeneous test many times over. A triangle
+      // whose projected orientation is not clear-cut keeps whole bounding-box rows.
+      const float ex = (nx[1] - nx[0]) * (ny[2] - ny[0]), ey = (ny[1] - ny[0]) * (nx[2] - nx[0]);
+      const float area2 = ex - ey;
+      const bool spans = fabsf(area2) > 1e-3f * (fabsf(ex) + fabsf(ey));
+      w.info[rank] = make_int4(r0 - (end - rows), c0, c1, spans ? 1 : 0);
+      const float o = area2 > 0.0f ? 1.0f : -1.0f;
+      const float size = static_cast<float>(max(width, height));
+      const float delta = (0.01f + size * 1e-6f) * 2.0f / static_cast<float>(min(width, height));
+      for (int k = 0; k < 3; ++k) {
+        const int i = (k + 1) % 3, j = (k + 2) % 3;
+        const float A = -o * (ny[j] - ny[i]), B = o * (nx[j] - nx[i]);
+        const float C = -(A * nx[i] + B * ny[i]);
+        const float D = delta * approx_sqrt(A * A + B * B) +
+                        4e-6f * (fabsf(A) + fabsf(B)) * (1.0f + fabsf(nx[i]) + fabsf(ny[i]));
+        // Row bounds are x >= (-(B y + C) - D) / A (A > 0) or x <= it (A < 0): keep 1 / A.
+        w.edge[k][rank] = make_float4(A != 0.0f ? approx_rcp(A) : 0.0f, B, C + D, A);
       }
-      const unsigned pends = __reduce_or_sync(0xffffffffu, pbit);
-      const int pitem = tested_px + static_cast<int>(lane);
-      const int r = (consumed_rows + __popc(pends & ((1u << lane) - 1u))) & (kRing - 1);
-      consumed_rows += __popc(pends);
-      tested_px += 32;
-      if (pitem >= queued_px) continue;
-      const int4 rec = w.row[r];
-      const int kk = rec.x & 31, y = rec.x >> 5, col = rec.y + pitem;
-      const float4 a = w.v[0][kk], bb = w.v[1][kk], cc = w.v[2][kk];
-      const float4 aux = w.aux[kk];
-      const long long key = coverage_key({a.x, a.y, a.z, a.w}, {bb.x, bb.y, bb.z, bb.w},
-                                         {cc.x, cc.y, cc.z, cc.w}, __ldg(centres + col),
-                                         __int_as_float(rec.w), __float_as_int(aux.z), aux.x,
-                                         aux.y);
-      if (key == kEmptyKey) continue;
-      const long long off =
-          (static_cast<long long>(__float_as_int(aux.w)) * height + y) * width + col;
-      if (prev != nullptr && !(key > __ldg(prev + off))) continue;
-      atomicMin(keys + off, key);
     }
-    tested_px = min(tested_px, queued_px);
     __syncwarp();
-  }
-  // Warp-aggregated append of the large triangles and of their pair counts.
-  const unsigned mask = __ballot_sync(0xffffffffu, large);
-  unsigned long long warp_pairs = pairs;
+    // Rows with pixels to test join a ring of kRing records; exact tests run 32 pixels at a time as
+    // soon as 32 are queued (and once more at the end), so that the pixels of consecutive row
+    // batches share test iterations. After a drain fewer than 32 pixels (so at most 31 rows) are
+    // pending and a batch adds at most 32 rows, so the ring never overwrites a pending row.
+    int done = 0;           // triangles whose rows all precede this batch
+    int queued_rows = 0;    // rows appended to the ring so far
+    int consumed_rows = 0;  // rows whose pixels have all been tested
+    int queued_px = 0;      // pixels appended so far
+    int tested_px = 0;      // pixels tested so far
+    for (int base = 0; base < all_rows; base += 32) {
+      // Phase A. Bit e - base - 1 marks a triangle whose rows end at e within (base, base + 32];
+      // the owner of row item base + lane is the number of triangles ending at or before it.
+      unsigned bit = 0u;
+      if (direct && end > base && end <= base + 32) bit = 1u << (end - base - 1);
+      const unsigned ends = __reduce_or_sync(0xffffffffu, bit);
+      const int item = base + static_cast<int>(lane);
+      const int k = done + __popc(ends & ((1u << lane) - 1u));
+      done += __popc(ends);
+      int count = 0, row = 0, cl = 0;
+      float py = 0.0f;
+      if (item < all_rows) {
+        const int4 info = w.info[k];
+        row = info.x + item;
+        cl = info.y;
+        int cr = info.z;
+        py = __ldg(centres + width + row);
+        if (info.w) {
+          float lo = -__int_as_float(0x7f800000), hi = __int_as_float(0x7f800000);
+          bool empty = false;
+          for (int e = 0; e < 3; ++e) {
+            const float4 h = w.edge[e][k];  // (1 / A, B, C + D, A)
+            const float rhs = -(h.y * py + h.z);
+            if (h.w > 0.0f) lo = fmaxf(lo, rhs * h.x);
+            else if (h.w < 0.0f) hi = fminf(hi, rhs * h.x);
+            else empty |= rhs > 0.0f;
+          }
+          if (empty || !(lo <= hi)) {
+            cr = cl - 1;
+          } else {
+            int sl, sr;
+            pixel_range(lo, hi, width, sl, sr);
+            cl = max(cl, sl);
+            cr = min(cr, sr);
+          }
+        }
+        count = max(0, cr - cl + 1);
+      }
+      // Append the rows that have pixels, numbering their pixels after those already queued.
+      const unsigned busy = __ballot_sync(0xffffffffu, count > 0);
+      const int slot = __popc(busy & ((1u << lane) - 1u));
+      int pix_end = count;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) warp_pairs += __shfl_xor_sync(0xffffffffu, warp_pairs, o);
-  if (mask != 0u) {
-    unsigned long long slot0 = 0;
-    if (lane == 0) {
-      slot0 = atomicAdd(counters, static_cast<unsigned long long>(__popc(mask)));
-      atomicAdd(counters + 1, warp_pairs);
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, pix_end, o);
+        if (static_cast<int>(lane) >= o) pix_end += y;
+      }
+      if (count > 0) {
+        const int q = (queued_rows + slot) & (kRing - 1);
+        const int last = queued_px + pix_end;  // pixels queued up to the end of this row
+        // (triangle rank, row, column of pixel number 0 of this row's numbering, end)
+        w.row[q] = make_int4(k | (row << 5), cl - (last - count), last, __float_as_int(py));
+      }
+      queued_rows += __popc(busy);
+      queued_px += __shfl_sync(0xffffffffu, pix_end, 31);
+      __syncwarp();
+      // Phase B: one exact coverage test per lane.
+      const bool final_batch = base + 32 >= all_rows;
+      while (queued_px - tested_px >= 32 || (final_batch && queued_px > tested_px)) {
+        // Rows ending within (tested_px, tested_px + 32] mark their last pixel; the owner of pixel
+        // tested_px + lane is the number of such rows ending before it.
+        const int n = consumed_rows + static_cast<int>(lane);
+        unsigned pbit = 0u;
+        if (n < queued_rows) {
+          const int e = w.row[n & (kRing - 1)].z;
+          if (e <= tested_px + 32) pbit = 1u << (e - tested_px - 1);
+        }
+        const unsigned pends = __reduce_or_sync(0xffffffffu, pbit);
+        const int pitem = tested_px + static_cast<int>(lane);
+        const int r = (consumed_rows + __popc(pends & ((1u << lane) - 1u))) & (kRing - 1);
+        consumed_rows += __popc(pends);
+        tested_px += 32;
+        if (pitem >= queued_px) continue;
+        const int4 rec = w.row[r];
+        const int kk = rec.x & 31, y = rec.x >> 5, col = rec.y + pitem;
+        const float4 a = w.v[0][kk], bb = w.v[1][kk], cc = w.v[2][kk];
+        const float4 aux = w.aux[kk];
+        const long long key = coverage_key({a.x, a.y, a.z, a.w}, {bb.x, bb.y, bb.z, bb.w},
+                                           {cc.x, cc.y, cc.z, cc.w}, __ldg(centres + col),
+                                           __int_as_float(rec.w), __float_as_int(aux.z), aux.x,
+                                           aux.y);
+        if (key == kEmptyKey) continue;
+        const long long off =
+            (static_cast<long long>(__float_as_int(aux.w)) * height + y) * width + col;
+        if (prev != nullptr && !(key > __ldg(prev + off))) continue;
+        atomicMin(keys + off, key);
+      }
+      tested_px = min(tested_px, queued_px);
+      __syncwarp();
     }
-    slot0 = __shfl_sync(0xffffffffu, slot0, 0);
-    if (large) {
-      const unsigned long long slot = slot0 + __popc(mask & ((1u << lane) - 1u));
-      if (slot < static_cast<unsigned long long>(capacity)) binned[slot] = {b, t, c0, c1, r0, r1};
+    // Warp-aggregated append of the large triangles and of their pair counts.
+    const unsigned mask = __ballot_sync(0xffffffffu, large);
+    unsigned long long warp_pairs = pairs;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) warp_pairs += __shfl_xor_sync(0xffffffffu, warp_pairs, o);
+    if (mask != 0u) {
+      unsigned long long slot0 = 0;
+      if (lane == 0) {
+        slot0 = atomicAdd(counters, static_cast<unsigned long long>(__popc(mask)));
+        atomicAdd(counters + 1, warp_pairs);
+      }
+      slot0 = __shfl_sync(0xffffffffu, slot0, 0);
+      if (large) {
+        const unsigned long long slot = slot0 + __popc(mask & ((1u << lane) - 1u));
+        if (slot < static_cast<unsigned long long>(capacity)) binned[slot] = {b, t, c0, c1, r0, r1};
+      }
     }
-  }
   }
 }
 
