@@ -86,7 +86,8 @@ int dr_raster_setup(const float* pos, int64_t pos_batch, const int32_t* tri, int
 size_t dr_raster_occlusion_workspace_bytes(int64_t total, int64_t batch, int32_t height,
                                            int32_t width);
 
-/* Occlusion pass. Given an occlusion workspace, dr_raster_setup sets aside the small triangles
+/* Occlusion pass (no counterpart in the reference, which tests every triangle at every pixel of
+ * its box). Given an occlusion workspace, dr_raster_setup sets aside the small triangles
  * whose projection has negative orientation (the far side of a closed mesh whose front faces are
  * counter-clockwise) instead of drawing them. After stage 2, dr_raster_occluded takes the largest
  * key of every 16 x 16 tile and draws the set-aside triangles, skipping each one whose depth,
@@ -118,7 +119,7 @@ int dr_raster_tiles(const float* pos, int64_t pos_batch, const int32_t* tri, int
                     void* stream);
 
 /* Stage 2 without the host round trip of dr_raster_counts (so that a CUDA graph can capture the
- * rasterizer): the counts are read on the device from the setup workspace. binned_capacity is the
+ * rasterizer; no counterpart in the reference, whose Triton path reads its counts back too): the counts are read on the device from the setup workspace. binned_capacity is the
  * capacity dr_raster_setup was given and pair_capacity the pair count bin_workspace is sized for
  * (dr_raster_bin_workspace_bytes). When a count exceeds its capacity nothing is binned, 1 is
  * OR-ed into the device word *overflow and the keys lack the binned triangles: the caller then
@@ -279,7 +280,7 @@ int dr_antialias_bwd(const float* color, const float* rast, const float* pos, in
                      const void* pairs, size_t pair_bytes, float* grad_color, float* grad_pos,
                      void* stream);
 
-/* ---- Antialias with a fused squared-error loss ------------------------------------------------
+/* ---- Antialias with a fused squared-error loss (no counterpart in the reference) -------------
  * The loss a fit puts right after antialias (the examples of diffrast take an MSE of the
  * antialiased image), computed inside the antialias passes: no separate loss kernels; the forward
  * pass leaves the residual out - target, from which the backward pass forms the output's
