@@ -118,8 +118,9 @@ int dr_raster_tiles(const float* pos, int64_t pos_batch, const int32_t* tri, int
                     int64_t num_pairs, void* bin_workspace, size_t bin_workspace_bytes,
                     void* stream);
 
-/* Stage 2 without the host round trip of dr_raster_counts (so that a CUDA graph can capture the
- * rasterizer; no counterpart in the reference, whose Triton path reads its counts back too): the counts are read on the device from the setup workspace. binned_capacity is the
+/* Stage 2 without the host round trip of dr_raster_counts, so that a CUDA graph can capture the
+ * rasterizer (no counterpart in the reference): the counts are read on the device from the setup
+ * workspace. binned_capacity is the
  * capacity dr_raster_setup was given and pair_capacity the pair count bin_workspace is sized for
  * (dr_raster_bin_workspace_bytes). When a count exceeds its capacity nothing is binned, 1 is
  * OR-ed into the device word *overflow and the keys lack the binned triangles: the caller then
