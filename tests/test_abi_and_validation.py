@@ -173,3 +173,35 @@ def test_antialias_mse_validation():
         dr.antialias_mse(color, rast, pos, tri, torch.zeros(1, 4, 4, 3), scale="x")
     with pytest.raises(RuntimeError, match="CUDA devices only"):
         dr.antialias_mse(color, rast, pos, tri, torch.zeros(1, 4, 4, 3))
+
+
+def declared_parameters() -> dict[str, list[str]]:
+    """Parameter types of every function declared in the header, by name."""
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    out = {}
+    for name, params in re.findall(r"\b(dr_[a-z0-9_]+)\s*\(([^;{]*?)\)\s*;", text):
+        params = " ".join(params.split())
+        out[name] = [] if params in ("", "void") else [p.strip() for p in params.split(",")]
+    return out
+
+
+def test_binding_matches_the_header_argument_by_argument():
+    """Every ctypes signature has the header's argument count, and each pointer, 64-bit, 32-bit
+    or float argument is bound as one: a signature that drifted from the library would pass
+    arguments into the wrong registers."""
+    declared = declared_parameters()
+    for name, (_, argtypes) in _native._SIGNATURES.items():
+        params = declared[name]
+        assert len(params) == len(argtypes), name
+        for param, ctype in zip(params, argtypes, strict=True):
+            if "*" in param:
+                expected = {ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64)}
+            elif param.startswith(("int64_t", "size_t")):
+                expected = {ctypes.c_int64, ctypes.c_size_t}
+            elif param.startswith(("int32_t", "int ")):
+                expected = {ctypes.c_int32, ctypes.c_int}
+            elif param.startswith("float"):
+                expected = {ctypes.c_float}
+            else:
+                raise AssertionError(f"{name}: unexpected parameter {param!r}")
+            assert ctype in expected, (name, param, ctype)
