@@ -1,68 +1,119 @@
-"""Per-tensor cache of derived values (diffrast _cache.py:16-82).
+"""Per-tensor memo of values derived from a tensor's contents (index ranges, range tables, edge
+adjacency), with the caching behaviour diffrast documents for its ``TensorCache``
+(diffrast ``_cache.py:30-82``): a value is reused only for the same tensor object while its
+contents are unchanged, and is forgotten when that tensor is freed.
 
-An entry is keyed on the tensor object's identity and remembers a weak reference and a stamp
-(version counter, data pointer, shape). It is reused only while both match, so a tensor edited
-in place, or a new tensor with the same contents, is computed again; the entry goes away with
-the tensor. Writes that bypass the version counter (``tensor.data``, memory shared with NumPy)
-are not noticed.
+"Unchanged" is judged by a :class:`Signature`: the autograd version counter (bumped by every
+in-place op, also through a view), the data address and the shape and strides. A tensor given
+new storage, or edited in place, is therefore computed again. Writes that bypass the version
+counter (through ``tensor.data`` or memory shared with NumPy) cannot be seen. Inference tensors
+have no version counter and are never cached.
+
+The memo is bounded: once ``max_entries`` tensors are remembered, the least recently used entry
+is dropped (a hit counts as a use).
 """
 
 from __future__ import annotations
 
 import threading
 import weakref
-from collections import OrderedDict
 from collections.abc import Callable
-from typing import Generic, TypeVar
+from typing import Generic, NamedTuple, TypeVar
 
 from torch import Tensor
 
 T = TypeVar("T")
 
 
-def stamp(tensor: Tensor) -> tuple | None:
-    """What changes when ``tensor`` is modified or re-allocated; ``None`` for inference tensors."""
+class Signature(NamedTuple):
+    """What identifies the contents of a tensor object between two lookups."""
+
+    version: int
+    address: int
+    shape: tuple
+    strides: tuple
+
+
+def signature(tensor: Tensor) -> Signature | None:
+    """The :class:`Signature` of ``tensor``, or ``None`` when it has no version counter."""
     if tensor.is_inference():
         return None
-    return tensor._version, tensor.data_ptr(), tensor.shape
+    return Signature(tensor._version, tensor.data_ptr(), tuple(tensor.shape), tensor.stride())
+
+
+class _Memo:
+    """One remembered value: the tensor it belongs to (weakly) and the signature it had."""
+
+    __slots__ = ("owner", "sig", "value")
+
+    def __init__(self, owner: weakref.ref, sig: Signature, value) -> None:
+        self.owner = owner
+        self.sig = sig
+        self.value = value
+
+    def valid_for(self, tensor: Tensor, sig: Signature) -> bool:
+        return self.owner() is tensor and self.sig == sig
 
 
 class TensorCache(Generic[T]):
-    """``compute(tensor)`` remembered per tensor object, at most ``max_entries`` of them (LRU)."""
+    """``compute(tensor)``, remembered for up to ``max_entries`` live tensor objects.
+
+    ``compute``'s result must not hold a reference to the tensor, or the tensor is never freed.
+    Lookups from several threads are safe; two threads that miss on the same tensor at once may
+    both compute it.
+    """
 
     def __init__(self, compute: Callable[[Tensor], T], max_entries: int = 64) -> None:
+        if max_entries < 1:
+            raise ValueError(f"max_entries must be at least 1, got {max_entries}.")
         self._compute = compute
-        self._max_entries = max_entries
-        self._entries: OrderedDict[int, tuple[weakref.ref, tuple, T]] = OrderedDict()
-        # Re-entrant: a weak-reference callback may run while this thread holds the lock.
-        self._lock = threading.RLock()
+        self._limit = max_entries
+        # id(tensor) -> _Memo, least recently used first (dicts keep insertion order).
+        self._memos: dict[int, _Memo] = {}
+        # A weak-reference callback can run in the middle of a locked section of the same thread
+        # (the garbage collector frees a tensor there), hence re-entrant.
+        self._mutex = threading.RLock()
 
     def __len__(self) -> int:
-        return len(self._entries)
+        return len(self._memos)
 
     def get(self, tensor: Tensor) -> T:
-        current = stamp(tensor)
-        if current is None:
+        sig = signature(tensor)
+        if sig is None:
             return self._compute(tensor)
-        key = id(tensor)
-        entry = self._entries.get(key)
-        if entry is not None and entry[0]() is tensor and entry[1] == current:
-            return entry[2]
+        slot = id(tensor)
+        with self._mutex:
+            memo = self._memos.pop(slot, None)
+            if memo is not None and memo.valid_for(tensor, sig):
+                self._memos[slot] = memo  # now the most recently used
+                return memo.value
         value = self._compute(tensor)
-        ref = weakref.ref(tensor, lambda r: self._discard(key, r))
-        with self._lock:
-            self._entries.pop(key, None)
-            self._entries[key] = (ref, current, value)
-            while len(self._entries) > self._max_entries:
-                self._entries.popitem(last=False)
+        owner = weakref.ref(tensor, self._forget_callback(slot))
+        with self._mutex:
+            self._memos.pop(slot, None)
+            self._memos[slot] = _Memo(owner, sig, value)
+            excess = len(self._memos) - self._limit
+            for stale in list(self._memos)[:max(0, excess)]:
+                del self._memos[stale]
         return value
 
     def clear(self) -> None:
-        with self._lock:
-            self._entries.clear()
+        with self._mutex:
+            self._memos.clear()
 
-    def _discard(self, key: int, ref: weakref.ref) -> None:
-        with self._lock:
-            entry = self._entries.get(key)
-            if entry is not None and entry[0] is ref:
-                del self._entries[key]
+    def _forget_callback(self, slot: int) -> Callable[[weakref.ref], None]:
+        # The callback holds the cache weakly, so a cache that goes away is not kept alive by the
+        # tensors it once saw.
+        cache = weakref.ref(self)
+
+        def forget(dead: weakref.ref) -> None:
+            owner = cache()
+            if owner is None:
+                return
+            with owner._mutex:
+                memo = owner._memos.get(slot)
+                # The slot may already hold a newer tensor that got the same id.
+                if memo is not None and memo.owner is dead:
+                    del owner._memos[slot]
+
+        return forget

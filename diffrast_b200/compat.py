@@ -1,8 +1,11 @@
-"""Run code written for nvdiffrast (or diffrast) on diffrast_b200 without editing it.
+"""Run code written for nvdiffrast (or diffrast) on diffrast_b200 without editing it
+(diffrast ``compat.py``).
 
-:func:`install_as_nvdiffrast` registers this package under the module names ``nvdiffrast`` and
-``nvdiffrast.torch`` (diffrast compat.py:15-74); :func:`install_as_diffrast` does the same for
-``diffrast`` and ``diffrast.torch``, so switching from diffrast is a one-line change.
+:func:`install_as_nvdiffrast` makes ``import nvdiffrast.torch as dr`` resolve to this package;
+:func:`install_as_diffrast` does the same for ``import diffrast``, so switching from diffrast is a
+one-line change. Each registers two ``sys.modules`` entries (the package and its ``.torch``
+module) and can be undone. Without ``force=True`` an alias refuses to shadow a real package of
+that name, imported or merely installed.
 """
 
 from __future__ import annotations
@@ -14,74 +17,97 @@ from types import ModuleType
 
 from diffrast_b200 import log
 
-_displaced: dict[str, ModuleType] = {}
 
+class _ModuleAlias:
+    """The pair of ``sys.modules`` entries that make ``name`` and ``name.torch`` this package."""
 
-def _modules(name: str) -> dict[str, ModuleType]:
-    return {
-        name: importlib.import_module("diffrast_b200"),
-        f"{name}.torch": importlib.import_module("diffrast_b200.torch"),
-    }
+    def __init__(self, name: str) -> None:
+        self.name = name
+        self.saved: dict[str, ModuleType] = {}  # real modules set aside by a forced install
 
+    def targets(self) -> dict[str, ModuleType]:
+        return {
+            self.name: importlib.import_module("diffrast_b200"),
+            f"{self.name}.torch": importlib.import_module("diffrast_b200.torch"),
+        }
 
-def _install(name: str, force: bool) -> None:
-    ours = _modules(name)
-    current = {n: sys.modules.get(n) for n in ours}
-    if all(current[n] is m for n, m in ours.items()):
-        return
-    imported = [n for n, m in ours.items() if current[n] not in (None, m)]
-    if not force:
-        if imported:
-            raise RuntimeError(
-                f"{imported[0]} is already imported; pass force=True to replace it with diffrast_b200."
+    def install(self, force: bool) -> None:
+        targets = self.targets()
+        # Entries that hold something other than this package (a real, imported package).
+        occupied = {key: sys.modules[key] for key, ours in targets.items()
+                    if sys.modules.get(key, ours) is not ours}
+        active = all(sys.modules.get(key) is ours for key, ours in targets.items())
+        if active:
+            return
+        if not force:
+            self._refuse(occupied)
+        if occupied:
+            log.warn(
+                f"Replacing the imported {self.name} with diffrast_b200; modules that imported "
+                "it earlier keep using it.",
+                stacklevel=3,
             )
-        if current[name] is None and _is_installed(name):
+            self.saved.update(occupied)
+        sys.modules.update(targets)
+
+    def _refuse(self, occupied: dict[str, ModuleType]) -> None:
+        if occupied:
+            first = next(key for key in self.targets() if key in occupied)
             raise RuntimeError(
-                f"A {name} package is installed; pass force=True to use diffrast_b200 in its place."
+                f"{first} is already imported; pass force=True to replace it with diffrast_b200."
             )
-    if imported:
-        log.warn(
-            f"Replacing the imported {name} with diffrast_b200; modules that imported it "
-            "earlier keep using it.",
-            stacklevel=3,
-        )
-    for n, m in ours.items():
-        if n in imported:
-            _displaced[n] = current[n]
-        sys.modules[n] = m
+        if self.name not in sys.modules and _findable(self.name):
+            raise RuntimeError(
+                f"A {self.name} package is installed; pass force=True to use diffrast_b200 in its "
+                "place."
+            )
+
+    def uninstall(self) -> None:
+        for key, ours in self.targets().items():
+            displaced = self.saved.pop(key, None)
+            if sys.modules.get(key) is not ours:
+                continue
+            if displaced is None:
+                del sys.modules[key]
+            else:
+                sys.modules[key] = displaced
 
 
-def _uninstall(name: str) -> None:
-    for n, m in _modules(name).items():
-        previous = _displaced.pop(n, None)
-        if sys.modules.get(n) is m:
-            del sys.modules[n]
-            if previous is not None:
-                sys.modules[n] = previous
-
-
-def install_as_nvdiffrast(force: bool = False) -> None:
-    """Make ``import nvdiffrast.torch as dr`` resolve to diffrast_b200 in this process."""
-    _install("nvdiffrast", force)
-
-
-def uninstall_as_nvdiffrast() -> None:
-    """Undo :func:`install_as_nvdiffrast`, restoring any modules it replaced."""
-    _uninstall("nvdiffrast")
-
-
-def install_as_diffrast(force: bool = False) -> None:
-    """Make ``import diffrast`` resolve to diffrast_b200 in this process."""
-    _install("diffrast", force)
-
-
-def uninstall_as_diffrast() -> None:
-    """Undo :func:`install_as_diffrast`."""
-    _uninstall("diffrast")
-
-
-def _is_installed(name: str) -> bool:
+def _findable(name: str) -> bool:
+    """Whether an importable package ``name`` exists (not counting a ``sys.modules`` entry)."""
     try:
         return importlib.util.find_spec(name) is not None
     except (ImportError, ValueError):
         return False
+
+
+_ALIASES = {name: _ModuleAlias(name) for name in ("nvdiffrast", "diffrast")}
+
+
+def install_as_nvdiffrast(force: bool = False) -> None:
+    """Make ``import nvdiffrast.torch as dr`` resolve to diffrast_b200 in this process.
+
+    Call it before importing code that uses nvdiffrast; modules that imported the real package
+    earlier keep it. A second call does nothing.
+
+    Args:
+        force: Take the place of a real nvdiffrast that is installed or already imported (with a
+            warning in the second case) instead of raising ``RuntimeError``.
+    """
+    _ALIASES["nvdiffrast"].install(force)
+
+
+def uninstall_as_nvdiffrast() -> None:
+    """Undo :func:`install_as_nvdiffrast`, putting back any modules it replaced."""
+    _ALIASES["nvdiffrast"].uninstall()
+
+
+def install_as_diffrast(force: bool = False) -> None:
+    """Make ``import diffrast`` (and ``diffrast.torch``) resolve to diffrast_b200 in this
+    process; ``force`` as for :func:`install_as_nvdiffrast`."""
+    _ALIASES["diffrast"].install(force)
+
+
+def uninstall_as_diffrast() -> None:
+    """Undo :func:`install_as_diffrast`, putting back any modules it replaced."""
+    _ALIASES["diffrast"].uninstall()

@@ -1,33 +1,47 @@
-"""Log level of the library's own messages, numbered as in nvdiffrast (diffrast log.py:1-38)."""
+"""Verbosity of the library's own messages, with nvdiffrast's numbering (diffrast ``log.py``):
+0 info, 1 warning (the default), 2 error, 3 fatal. Messages at warning level are issued as
+``UserWarning`` while the level is at most 1; errors are exceptions and are raised whatever the
+level is.
+"""
 
 from __future__ import annotations
 
-import operator
 import warnings
 
-INFO, WARNING, ERROR, FATAL = range(4)
+LEVELS = ("info", "warning", "error", "fatal")
+INFO, WARNING, ERROR, FATAL = (LEVELS.index(name) for name in LEVELS)
 
-_level = WARNING
+
+class _Verbosity:
+    """Holder of the process-wide level (one object, so no ``global`` statements are needed)."""
+
+    value = WARNING
+
+
+def _parse_level(level) -> int:
+    message = f"level must be an int from 0 to 3, got {level!r}."
+    index = getattr(type(level), "__index__", None)
+    if index is None:
+        raise TypeError(message)
+    value = index(level)
+    if value not in range(len(LEVELS)):
+        raise ValueError(message)
+    return value
 
 
 def get_log_level() -> int:
-    """Current log level: 0 info, 1 warning (default), 2 error, 3 fatal."""
-    return _level
+    """The lowest level of message reported: 0 info, 1 warning, 2 error, 3 fatal."""
+    return _Verbosity.value
 
 
 def set_log_level(level: int) -> None:
-    """Set the lowest level reported; warnings show at 0 and 1, errors always raise."""
-    global _level
-    try:
-        value = operator.index(level)
-    except TypeError:
-        raise TypeError(f"level must be an int from 0 to 3, got {level!r}.") from None
-    if not INFO <= value <= FATAL:
-        raise ValueError(f"level must be an int from 0 to 3, got {level!r}.")
-    _level = value
+    """Report messages from ``level`` (an int from 0 to 3) upwards."""
+    _Verbosity.value = _parse_level(level)
 
 
 def warn(message: str, stacklevel: int = 1) -> None:
-    """``UserWarning`` attributed to the caller unless the level silences warnings."""
-    if _level <= WARNING:
-        warnings.warn(message, stacklevel=stacklevel + 1)
+    """Issue ``message`` as a ``UserWarning`` pointing at the caller's caller (``stacklevel``
+    counts from the function that calls this one), unless the level is above warning."""
+    if _Verbosity.value > WARNING:
+        return
+    warnings.warn(message, UserWarning, stacklevel=stacklevel + 1)

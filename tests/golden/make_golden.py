@@ -22,7 +22,9 @@ HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parent))
 import scenes  # noqa: E402
 
-SRC = os.environ.get("DIFFRAST_REFERENCE_SRC", "/root/reference/src")
+SRC = os.environ.get("DIFFRAST_REFERENCE_SRC")
+if not SRC:
+    raise SystemExit("set DIFFRAST_REFERENCE_SRC to the reference diffrast's src directory")
 sys.path.insert(0, SRC)
 import diffrast as ref  # noqa: E402
 from diffrast.backends import reference as ref_backend  # noqa: E402
