@@ -10,15 +10,19 @@
 // Limits and sharing:
 //   - At most kMaxTriangles (65536) triangles; larger inputs are refused with
 //     DR_ERR_EXCEEDS_STATIC_SCRATCH before any GPU work.
-//   - The array takes kScratchBytes (10 MiB) on every GPU where this entry point is used, held
-//     until the process exits.
+//   - The array takes kScratchBytes (10 MiB) of device memory on a GPU from the moment this
+//     file's device code is loaded there until the process exits. Under CUDA's lazy module loading
+//     (the default) that is the first call of this entry point on that GPU; with
+//     CUDA_MODULE_LOADING=EAGER it is every GPU the library is loaded on.
 //   - Every call uses the same array and finds the previous call's contents in it; the part the
 //     call uses is cleared first. Two calls whose work overlaps on the GPU (on different streams,
 //     or from different threads) race on the array and give wrong results.
-//   - The first call on a device looks up the device address of the array (cudaGetSymbolAddress)
-//     with that device current and remembers it; make that first call before any stream capture.
+//   - In host code the array's name stands for a host-side shadow, not device memory, so each
+//     call looks up the array's device address on the current device (cudaGetSymbolAddress) and
+//     passes that to the kernels. Nothing is cached, so the address stays right after a
+//     cudaDeviceReset or on another context. The first call on a GPU also loads the module there;
+//     make that first call before any stream capture.
 #include <cstdint>
-#include <mutex>
 
 #include "common.cuh"
 #include "edge_hash.cuh"
@@ -35,26 +39,10 @@ constexpr size_t kScratchBytes = 20 * kMaxSlots;
 
 static __device__ __align__(256) unsigned char g_edge_scratch[kScratchBytes];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_address_mutex;
-void* g_scratch_address[kMaxDevices] = {};
-
-// Device address of g_edge_scratch on the current device. In host code the symbol names a host
-// stand-in, not device memory, so the address is looked up once per device and cached.
+// Device address of g_edge_scratch on the current device, looked up on every call.
 int scratch_address(void** out) {
-  int device = 0;
-  cudaError_t err = cudaGetDevice(&device);
-  if (err != cudaSuccess) return static_cast<int>(err);
-  if (device < 0 || device >= kMaxDevices) return DR_ERR_INVALID_ARGUMENT;
-  std::lock_guard<std::mutex> lock(g_address_mutex);
-  if (g_scratch_address[device] == nullptr) {
-    void* address = nullptr;
-    err = cudaGetSymbolAddress(&address, g_edge_scratch);
-    if (err != cudaSuccess) return static_cast<int>(err);
-    g_scratch_address[device] = address;
-  }
-  *out = g_scratch_address[device];
-  return DR_OK;
+  cudaError_t err = cudaGetSymbolAddress(out, g_edge_scratch);
+  return err == cudaSuccess ? DR_OK : static_cast<int>(err);
 }
 
 }  // namespace

@@ -236,10 +236,13 @@ int dr_edge_neighbours(const int32_t* tri, int64_t num_tri, int64_t* neighbours,
  * binding without a device allocator, or a fixed device-memory budget): the hash table lives in a
  * 10 MiB file-scope device array instead of a caller workspace. No counterpart in the reference.
  * At most dr_edge_neighbours_noalloc_max_triangles() (65536) triangles; more is refused with
- * DR_ERR_EXCEEDS_STATIC_SCRATCH. Every GPU where it is used keeps the array until process exit.
- * All calls share the array (cleared as needed on each call), so calls that overlap on the GPU
- * race. The first call on a device looks up the array's device address with that device
- * current; make it before any stream capture. Allocates nothing. */
+ * DR_ERR_EXCEEDS_STATIC_SCRATCH. The array is taken on a GPU when the library's module for it
+ * loads there (with CUDA's default lazy loading, at this entry point's first call on that GPU;
+ * with CUDA_MODULE_LOADING=EAGER, on every GPU the library loads on) and kept until process
+ * exit. All calls share the array (each clears the part it uses), so calls that overlap on the
+ * GPU race. Each call looks up the array's device address on the current device, so nothing
+ * goes stale after a cudaDeviceReset; the first call on a device also loads the module there,
+ * so make it before any stream capture. Allocates nothing. */
 int64_t dr_edge_neighbours_noalloc_max_triangles(void);
 int dr_edge_neighbours_noalloc(const int32_t* tri, int64_t num_tri, int64_t* neighbours,
                                void* stream);
