@@ -183,6 +183,9 @@ def raster_keys(pos: Tensor, tri: Tensor, height: int, width: int, prev_keys: Te
             "dr_raster_tiles_device",
         )  # fmt: skip
         occluded(ws)
+        # While the device's overflow word is set, the keys are poisoned (NaN downstream).
+        N.check(lib.dr_raster_poison_keys(word.data_ptr(), keys.data_ptr(), keys.numel(), s),
+                "dr_raster_poison_keys")
         return keys
     overflow_word(dev)
     binned, pairs = c_int64(0), c_int64(0)

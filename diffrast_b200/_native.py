@@ -48,6 +48,7 @@ _SIGNATURES = {
         [_P, c_int64, _P, c_int64, c_int64, c_int64, c_int32, c_int32, _P, _P, _P, c_int64,
          c_int64, _P, c_size_t, _P, _P],
     ),
+    "dr_raster_poison_keys": (c_int, [_P, _P, c_int64, _P]),
     "dr_raster_resolve_fwd": (
         c_int, [_P, c_int64, _P, _P, c_int64, c_int64, c_int64, c_int32, c_int32, _P, _P, _P]
     ),

@@ -40,10 +40,12 @@ class RasterizeContext:
 
         A rasterization captured into a CUDA graph cannot read its binned-triangle counts back,
         so it bins into capacities taken from an eager call of the same shapes. A replay whose
-        binned triangles exceed them marks the views it could not finish as invalid: their
-        triangle ids become -1 (and the image and gradients of those pixels are zero). On
-        ``True``, the results of the replays since the last check are invalid in those views;
-        later captures get doubled capacities, so capture the graph again and rerun.
+        binned triangles exceed them sets a device word, and while that word is set every
+        captured rasterization on the device is poisoned: the barycentrics, depth and ``rast_db``
+        of its covered pixels are NaN, so the attributes, texture lookups, images and losses
+        computed from them are NaN too. On ``True`` (which clears the word) the results of the
+        replays since the last check are invalid; later captures get doubled capacities, so
+        capture the graph again and rerun.
         """
         from diffrast_b200._kernels import capture_overflowed
 

@@ -17,6 +17,11 @@ namespace dr {
 
 // Empty visibility key: no triangle covers the pixel (INT64_MAX, as a signed 64-bit key).
 constexpr long long kEmptyKey = 0x7FFFFFFFFFFFFFFFLL;
+// Depth field (upper 32 bits) of a poisoned key: the ordered bits of a quiet NaN, which no
+// covered pixel can have (its depth lies in [-1, 1]) and which sorts below the empty key. Keys
+// of a graph-captured pass that outgrew its binning capacity carry it, and the resolve pass
+// turns it into NaN barycentrics, depth and derivatives.
+constexpr int kPoisonDepth = 0x7FC00000;
 // Two float32 epsilons: the area tolerance of the reference (reference.py:27).
 constexpr float kAreaTolerance = 2.0f * 1.1920928955078125e-07f;
 // Four float32 epsilons: the edge-tie slack of antialiasing (reference.py:35, :746).

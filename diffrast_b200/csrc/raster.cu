@@ -815,6 +815,26 @@ __device__ __forceinline__ PixelTri pixel_triangle(const float* __restrict__ pos
 constexpr int kResolvePix = 2;
 constexpr int kResolveThreads = 128;
 
+// Graph-captured passes only: when the device word `overflow` is set (a captured pass outgrew
+// its binning capacity since the host last cleared the word), the depth field of every covered
+// pixel's key becomes kPoisonDepth; the triangle field, which the resolve passes index with, is
+// kept. One 8-byte read per block when the word is clear.
+__global__ void __launch_bounds__(256) poison_keys_kernel(const unsigned long long* __restrict__ overflow,
+                                                          long long* __restrict__ keys,
+                                                          long long count) {
+  __shared__ unsigned long long flag;
+  if (threadIdx.x == 0) flag = *overflow;
+  __syncthreads();
+  if (flag == 0) return;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < count;
+       i += stride) {
+    const long long key = keys[i];
+    if (key == kEmptyKey) continue;
+    keys[i] = (static_cast<long long>(kPoisonDepth) << 32) | (key & 0xFFFFFFFFLL);
+  }
+}
+
 __global__ void __launch_bounds__(kResolveThreads) resolve_fwd_kernel(
     const float* __restrict__ pos, const int* __restrict__ tri, const long long* __restrict__ keys,
     int b0, long long pos_stride, int height, int width, float4* __restrict__ rast,
@@ -851,6 +871,12 @@ __global__ void __launch_bounds__(kResolveThreads) resolve_fwd_kernel(
     if (key[i] == kEmptyKey) {
       rast[p] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       if (rast_db != nullptr) rast_db[p] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      continue;
+    }
+    if (static_cast<int>(key[i] >> 32) == kPoisonDepth) {
+      const float nan = __int_as_float(0x7FC00000);
+      rast[p] = make_float4(nan, nan, nan, static_cast<float>((key[i] & 0xFFFFFFFFLL) + 1));
+      if (rast_db != nullptr) rast_db[p] = make_float4(nan, nan, nan, nan);
       continue;
     }
     const float px = pixel_centre(col, width);
@@ -1259,6 +1285,17 @@ extern "C" int dr_raster_tiles_device(const float* pos, int64_t pos_batch, const
   return launch_tiles(pos, pos_batch, tri, batch, num_vert, height, width, prev_keys, keys,
                       setup_workspace, binned_capacity > 0 ? binned_capacity : 1, pair_capacity,
                       bin_workspace, bin_workspace_bytes, dc, as_stream(stream));
+}
+
+extern "C" int dr_raster_poison_keys(const uint64_t* overflow, int64_t* keys, int64_t count,
+                                     void* stream) {
+  if (overflow == nullptr || count < 0 || (count > 0 && keys == nullptr))
+    return DR_ERR_INVALID_ARGUMENT;
+  if (count == 0) return DR_OK;
+  poison_keys_kernel<<<min(blocks_for(count, 256), 148u * 4u), 256, 0, as_stream(stream)>>>(
+      reinterpret_cast<const unsigned long long*>(overflow), reinterpret_cast<long long*>(keys),
+      count);
+  return launch_status();
 }
 
 extern "C" int dr_raster_resolve_fwd(const float* pos, int64_t pos_batch, const int32_t* tri,

@@ -131,8 +131,18 @@ int dr_raster_tiles_device(const float* pos, int64_t pos_batch, const int32_t* t
                            int64_t binned_capacity, int64_t pair_capacity, void* bin_workspace,
                            size_t bin_workspace_bytes, uint64_t* overflow, void* stream);
 
+/* For CUDA-graph-captured rasterization (no counterpart in the reference): if the device word
+ * *overflow is non-zero, marks every covered key of `keys` [count] as poisoned (its triangle index
+ * kept, its depth replaced by a value no covered pixel has), so that dr_raster_resolve_fwd writes
+ * NaN barycentrics, depth and derivatives there and everything computed from them is NaN. Called
+ * after dr_raster_tiles_device (and dr_raster_occluded) with the same word; *overflow stays set
+ * until the host clears it, so every captured pass replayed until then is poisoned. A no-op
+ * (one read per block) while the word is zero. */
+int dr_raster_poison_keys(const uint64_t* overflow, int64_t* keys, int64_t count, void* stream);
+
 /* rast [batch, h, w, 4] = (u, v, z/w, id + 1) and rast_db [.., 4] = (du/dx, du/dy, dv/dx, dv/dy),
- * zeros where empty (reference.py:69-114; _triton_resolve.py:84-116). rast_db may be NULL. */
+ * zeros where empty (reference.py:69-114; _triton_resolve.py:84-116). rast_db may be NULL.
+ * A poisoned key (dr_raster_poison_keys) gives (NaN, NaN, NaN, id + 1) and a NaN rast_db. */
 int dr_raster_resolve_fwd(const float* pos, int64_t pos_batch, const int32_t* tri,
                           const int64_t* keys, int64_t batch, int64_t num_vert, int64_t num_tri,
                           int32_t height, int32_t width, float* rast, float* rast_db,

@@ -42,8 +42,10 @@ __all__ = [
     "rasterize",
     "rasterize_layer",
     "resolve",
+    "resolve_at_pixels",
     "silhouette_edges",
     "texture",
+    "visible_at_pixels",
     "visible_triangles",
 ]
 
@@ -176,6 +178,61 @@ def visible_triangles(
     return best_depth, best_id
 
 
+def visible_at_pixels(
+    pos: Tensor, tri: Tensor, height: int, width: int, rows: Tensor, cols: Tensor,
+    margin_px: float = 2.0,
+) -> tuple[Tensor, Tensor]:
+    """``visible_triangles`` of one view (``pos [V, 4]``) at listed pixels only.
+
+    Returns ``(depth, tri_id)`` of shape ``[N]`` for the pixels ``(rows[n], cols[n])`` of an
+    ``height x width`` image. Coverage is the exact ``coverage`` test, run for each pixel on every
+    triangle that can reach it: those with a vertex at ``w <= 0`` or non-finite, and those whose
+    projected bounding box, grown by ``margin_px`` pixels, contains the pixel centre. A triangle
+    with all ``w > 0`` covers only points of its projected triangle, which lies inside that box
+    (the margin is far above the rounding of the projection), so the result equals
+    ``visible_triangles`` at those pixels; it exists so that images of a million triangles can be
+    checked at a few thousand pixels.
+    """
+    pos = pos.detach().float()
+    tri = tri.long()
+    num_tri = tri.shape[0]
+    px_all, py_all = pixel_centres(height, width)
+    px, py = px_all[cols.long()], py_all[rows.long()]
+    v = pos[tri]  # [T, 3, 4]
+    w = v[..., 3]
+    finite = torch.isfinite(v).all(-1).all(-1)
+    front = (w > 0).all(-1) & finite
+    safe_w = torch.where(front[:, None], w, torch.ones_like(w))
+    sx, sy = v[..., 0] / safe_w, v[..., 1] / safe_w
+    mx, my = 2.0 * margin_px / width, 2.0 * margin_px / height
+    x0, x1 = sx.amin(-1) - mx, sx.amax(-1) + mx
+    y0, y1 = sy.amin(-1) - my, sy.amax(-1) + my
+    always = (~front).nonzero().flatten()
+    depth_out = torch.full((px.shape[0],), math.inf)
+    id_out = torch.full((px.shape[0],), -1, dtype=torch.long)
+    # Pixels are handled in groups of one 8 x 8 cell: the candidates of a cell are the triangles
+    # whose grown box meets the cell's pixel-centre rectangle.
+    cell = (rows.long() // 8) * ((width + 7) // 8) + cols.long() // 8
+    for c in cell.unique().tolist():
+        members = (cell == c).nonzero().flatten()
+        cx, cy = px[members], py[members]
+        reach = front & (x0 <= cx.max()) & (x1 >= cx.min()) & (y0 <= cy.max()) & (y1 >= cy.min())
+        cand = torch.cat([reach.nonzero().flatten(), always]).unique()
+        if cand.numel() == 0:
+            continue
+        vc = v[cand][:, :, None, :]  # [n, 3, 1, 4] against [members]
+        coords = [[vc[:, k, :, comp] for k in range(3)] for comp in range(4)]
+        inside, depth = coverage(*coords, cx[None], cy[None])  # [n, members]
+        depth = torch.where(inside, depth, torch.full_like(depth, math.inf))
+        near = depth.amin(0)
+        ids = cand[:, None].expand_as(depth)
+        first = torch.where(inside & (depth == near[None]), ids, torch.full_like(ids, num_tri)).amin(0)
+        hit = near < math.inf
+        depth_out[members[hit]] = near[hit]
+        id_out[members[hit]] = first[hit]
+    return depth_out, id_out
+
+
 def keys_from_state(depth: Tensor, tri_id: Tensor) -> Tensor:
     """Packed 64-bit visibility keys ``(ordered depth bits << 32) | id`` from a layer's state.
 
@@ -202,8 +259,34 @@ def resolve(pos: Tensor, tri: Tensor, tri_id: Tensor, grad_db: bool = True) -> t
     bi, ri, ci = (tri_id >= 0).nonzero(as_tuple=True)
     seen = tri_id[bi, ri, ci]
     v = pos[bi[:, None], tri.long()[seen]]  # [N, 3, 4]
+    values, derivs = _resolve_points(v, px[ci].to(pos.dtype), py[ri].to(pos.dtype), seen, height,
+                                     width, grad_db)
+    rast = pos.new_zeros(batch, height, width, 4).index_put((bi, ri, ci), values)
+    rast_db = pos.new_zeros(batch, height, width, 4).index_put((bi, ri, ci), derivs)
+    return rast, rast_db
+
+
+def resolve_at_pixels(pos: Tensor, tri: Tensor, height: int, width: int, rows: Tensor,
+                      cols: Tensor, tri_id: Tensor) -> tuple[Tensor, Tensor]:
+    """``rast`` and ``rast_db`` ``[N, 4]`` of one view (``pos [V, 4]``) at listed pixels whose
+    visible triangles are ``tri_id [N]`` (-1: empty, zeros), in ``pos``'s dtype (float64 gives the
+    reference values the CUDA results are compared with)."""
+    px, py = pixel_centres(height, width)
+    hit = (tri_id >= 0).nonzero().flatten()
+    seen = tri_id[hit]
+    v = pos[tri.long()[seen]]  # [N, 3, 4]
+    values, derivs = _resolve_points(v, px[cols[hit].long()].to(pos.dtype),
+                                     py[rows[hit].long()].to(pos.dtype), seen, height, width, True)
+    rast = pos.new_zeros(tri_id.shape[0], 4)
+    rast_db = pos.new_zeros(tri_id.shape[0], 4)
+    rast[hit], rast_db[hit] = values, derivs
+    return rast, rast_db
+
+
+def _resolve_points(v, pxn, pyn, seen, height, width, grad_db):
+    """Barycentrics, depth, id + 1 and their screen derivatives of triangles ``v [N, 3, 4]`` at
+    the pixel centres ``(pxn, pyn)``."""
     x, y, z, w = ([v[:, k, comp] for k in range(3)] for comp in range(4))
-    pxn, pyn = px[ci], py[ri]
     a, c, e = _edge_terms(x, y, w, pxn, pyn)
     area = e[0] + e[1] + e[2]
     b = [ek / area for ek in e]
@@ -216,14 +299,12 @@ def resolve(pos: Tensor, tri: Tensor, tri_id: Tensor, grad_db: bool = True) -> t
     if not grad_db:
         dbdx = [t.detach() for t in dbdx]
         dbdy = [t.detach() for t in dbdy]
-    values = torch.stack([b[0], b[1], depth, (seen + 1).to(pos.dtype)], -1)
+    values = torch.stack([b[0], b[1], depth, (seen + 1).to(v.dtype)], -1)
     derivs = torch.stack(
         [dbdx[0] * (2 / width), dbdy[0] * (2 / height), dbdx[1] * (2 / width), dbdy[1] * (2 / height)],
         -1,
     )
-    rast = pos.new_zeros(batch, height, width, 4).index_put((bi, ri, ci), values)
-    rast_db = pos.new_zeros(batch, height, width, 4).index_put((bi, ri, ci), derivs)
-    return rast, rast_db
+    return values, derivs
 
 
 def rasterize_layer(
