@@ -12,10 +12,15 @@ target images, and the step starts with the world-to-clip transform (``to_clip``
 are sharded across the ranks (strong scaling); the texture and position gradients are summed with
 NCCL all-reduces.
 
-    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference | --impl triton]
 
-One JSON line is printed by rank 0. ``--impl reference`` times the CPU oracle (the reference's
-algorithm restated on the host, all host threads) on a bounded sample of the same workload.
+One JSON line is printed by rank 0. ``--impl reference`` times the reference's CPU backend (the
+unmodified reference package when it is installed under ``baseline/_ref``, else the golden-pinned
+CPU restatement in ``oracle/``) with all host threads on a bounded sample of the same workload.
+``--impl triton`` times the reference's own GPU backend (Triton, unmodified, from
+``baseline/_ref``) on the same workload on one GPU; the default run does that too, in a
+subprocess, and reports it as ``gpu_reference``, together with a same-configuration pair on
+BASELINE configuration 1 (this library on the GPU against the reference's CPU backend).
 """
 
 from __future__ import annotations
@@ -209,6 +214,67 @@ def peaks() -> tuple[float, str]:
     if path.exists():
         return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+REF_DIR = ROOT / "baseline" / "_ref"
+
+
+def reference_package(backend: str):
+    """The unmodified reference package installed under ``baseline/_ref`` with ``backend``
+    selected ("reference": its PyTorch CPU backend; "triton": its GPU backend), or None when it
+    is not installed there."""
+    if not (REF_DIR / "diffrast" / "__init__.py").exists():
+        return None
+    if str(REF_DIR) not in sys.path:
+        sys.path.insert(0, str(REF_DIR))
+    import diffrast
+
+    diffrast.set_backend(backend)
+    return diffrast
+
+
+class CpuPath:
+    """The render path on the host: the reference package's CPU backend when installed
+    (``kind`` "reference"), else the CPU restatement in ``oracle/`` (``kind`` "port")."""
+
+    def __init__(self) -> None:
+        self.ref = reference_package("reference")
+        self.kind = "reference" if self.ref is not None else "port"
+        if self.ref is not None:
+            self.ctx = self.ref.RasterizeContext("cpu")
+        else:
+            import oracle
+
+            self.oracle = oracle
+
+    def rasterize(self, pos, tri, res):
+        if self.ref is not None:
+            return self.ref.rasterize(self.ctx, pos, tri, res)
+        return self.oracle.rasterize(pos, tri, res)
+
+    def interpolate(self, attr, rast, tri, rast_db=None):
+        if self.ref is not None:
+            if rast_db is None:
+                return self.ref.interpolate(attr, rast, tri)
+            return self.ref.interpolate(attr, rast, tri, rast_db=rast_db, diff_attrs="all")
+        diff = [] if rast_db is None else list(range(attr.shape[-1]))
+        return self.oracle.interpolate(attr, rast, tri, rast_db, diff)
+
+    def texture(self, tex, uv, uv_da, mode):
+        if self.ref is not None:
+            return self.ref.texture(tex, uv, uv_da, filter_mode=mode)
+        return self.oracle.texture(tex, uv.contiguous(), None if uv_da is None else uv_da.contiguous(),
+                                   None, None, mode, "wrap")
+
+    def antialias(self, color, rast, pos, tri):
+        if self.ref is not None:
+            return self.ref.antialias(color, rast, pos, tri)
+        return self.oracle.antialias(color, rast, pos, tri)
+
+    def describe(self) -> str:
+        if self.ref is not None:
+            return "the reference package's PyTorch CPU backend (unmodified, baseline/_ref)"
+        return "the golden-pinned CPU restatement of the reference backend (oracle/)"
 
 
 def build_scene(views_total: int, res: int, subdiv: int, tex_size: int, rank: int, world: int):
@@ -500,15 +566,24 @@ def run_ours(args) -> None:
     }
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args, warmup=1, steps=1)
+    if world == 1 and not args.no_gpu_reference:
+        # A same-configuration pair: BASELINE configuration 1 in full, this library on the GPU
+        # against the reference's CPU backend on the host cores.
+        line["config1"] = {
+            "workload": "BASELINE config 1: 1 view 256x256, icosphere-3 (1280 tris), tex 256^2x3 "
+                        "linear, antialias, MSE, fwd+bwd to tex and pos",
+            "gpu": config1_gpu(dev), "cpu_reference": config1_cpu(), "same_config": True,
+        }
+        # The reference's own GPU backend on this workload, in its own process.
+        torch.cuda.empty_cache()
+        line["gpu_reference"] = gpu_reference_line(args)
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
 
 
-def cpu_sample(args):
+def cpu_sample(args, path: CpuPath):
     """A bounded CPU sample of the workload: one view of the same scene at a small resolution."""
-    import oracle
-
     world, mvp, tri, attr, tex, _ = build_scene(1, args.cpu_res, args.subdiv, args.tex, 0, 1)
     target = torch.rand(1, args.cpu_res, args.cpu_res, 3, generator=torch.Generator().manual_seed(7))
     res = (args.cpu_res, args.cpu_res)
@@ -518,11 +593,10 @@ def cpu_sample(args):
         t = tex.clone().requires_grad_(True)
         # World to clip as diffrast's examples do it (examples/common.py:320-323).
         p = torch.nn.functional.pad(w, (0, 1), value=1.0) @ mvp.transpose(-1, -2)
-        rast, rast_db = oracle.rasterize(p, tri, res)
-        out, out_da = oracle.interpolate(attr, rast, tri, rast_db, list(range(5)))
-        color = oracle.texture(t, out[..., 0:2].contiguous(), out_da[..., 0:4].contiguous(), None,
-                               None, "linear-mipmap-linear", "wrap")
-        image = oracle.antialias(color, rast, p, tri)
+        rast, rast_db = path.rasterize(p, tri, res)
+        out, out_da = path.interpolate(attr, rast, tri, rast_db)
+        color = path.texture(t, out[..., 0:2], out_da[..., 0:4], "linear-mipmap-linear")
+        image = path.antialias(color, rast, p, tri)
         loss = torch.nn.functional.mse_loss(image, target)
         loss.backward()
         return loss.item()
@@ -532,7 +606,8 @@ def cpu_sample(args):
 
 def cpu_baseline(args, warmup: int, steps: int) -> dict:
     torch.set_num_threads(os.cpu_count() or 1)
-    step, res = cpu_sample(args)
+    path = CpuPath()
+    step, res = cpu_sample(args, path)
     for _ in range(warmup):
         step()
     t0 = time.perf_counter()
@@ -543,11 +618,172 @@ def cpu_baseline(args, warmup: int, steps: int) -> dict:
         "value": float(f"{res[0] * res[1] / sec / 1e6:.4g}"),
         "unit": UNIT,
         "cores": torch.get_num_threads(),
-        "kind": "port",
+        "kind": path.kind,
         "sample": f"1 of {args.views} views of the same scene at {res[0]}x{res[1]} px (full mesh and "
-                  f"texture), fwd+bwd, {sec:.2f} s per step, CPU oracle (brute-force visibility "
-                  "as the reference backend)",
+                  f"texture), fwd+bwd, {sec:.2f} s per step, {path.describe()}; the full "
+                  "configuration is far beyond the reference CPU backend's brute-force visibility "
+                  "(its own benchmark skips it above 2e10 triangle-pixels; this one is 8.8e16)",
     }
+
+
+def config1_cpu(steps: int = 2, warmup: int = 1) -> dict:
+    """BASELINE configuration 1 in full on the host: the reference's CPU backend, all threads."""
+    import scenes
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    path = CpuPath()
+    sc = scenes.config1_scene(seed=0)
+    res = sc["resolution"]
+
+    def step():
+        pos = sc["pos"].clone().requires_grad_(True)
+        tex = sc["tex"].clone().requires_grad_(True)
+        rast, _ = path.rasterize(pos, sc["tri"], res)
+        uv, _ = path.interpolate(sc["uv"], rast, sc["tri"])
+        color = path.texture(tex, uv, None, "linear")
+        image = path.antialias(color, rast, pos, sc["tri"])
+        torch.nn.functional.mse_loss(image, sc["target"]).backward()
+
+    for _ in range(warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    sec = (time.perf_counter() - t0) / steps
+    return {"value": float(f"{res[0] * res[1] / sec / 1e6:.4g}"), "unit": UNIT,
+            "ms_per_step": round(sec * 1e3, 1), "cores": torch.get_num_threads(),
+            "kind": path.kind, "impl": path.describe()}  # fmt: skip
+
+
+def config1_gpu(dev: torch.device, steps: int = 200) -> dict:
+    """BASELINE configuration 1 in full on one GPU through this library: rasterize, interpolate,
+    texture ('linear'), antialias with the fused MSE, backward to texture and positions; each step
+    a replay of a CUDA graph of the step, timed with CUDA events."""
+    import scenes
+
+    import diffrast_b200 as dr
+
+    sc = scenes.config1_scene(seed=0)
+    res = sc["resolution"]
+    ctx = dr.RasterizeContext(dev)
+    pos = sc["pos"].to(dev).requires_grad_(True)
+    tex = sc["tex"].to(dev).requires_grad_(True)
+    tri, uv, target = sc["tri"].to(dev), sc["uv"].to(dev), sc["target"].to(dev)
+
+    def step():
+        pos.grad = None
+        tex.grad = None
+        rast, _ = dr.rasterize(ctx, pos, tri, res)
+        uvp, _ = dr.interpolate(uv, rast, tri)
+        color = dr.texture(tex, uvp, filter_mode="linear")
+        _, loss = dr.antialias_mse(color, rast, pos, tri, target)
+        loss.backward()
+        return loss
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=torch.cuda.current_stream(dev)):
+        step()
+    for _ in range(10):
+        graph.replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        graph.replay()
+    end.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / steps
+    overflowed = ctx.capture_overflowed()
+    graph.reset()
+    if overflowed:
+        raise SystemExit("config 1: a captured visibility pass outgrew its binning capacity")
+    return {"value": round(res[0] * res[1] / (ms / 1e3) / 1e6, 1), "unit": UNIT,
+            "ms_per_step": round(ms, 4), "steps": steps, "launch": "CUDA graph of the step"}
+
+
+def gpu_reference_line(args) -> dict:
+    """``bench.py --impl triton`` on the same workload, run in a subprocess (its own CUDA context
+    and Triton compilation), or why it could not run."""
+    cmd = [sys.executable, str(Path(__file__).resolve()), "--impl", "triton", "--steps",
+           str(args.triton_steps), "--warmup", "2", "--views", str(args.views), "--res",
+           str(args.res), "--subdiv", str(args.subdiv), "--tex", str(args.tex)]
+    env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK")}
+    try:
+        done = subprocess.run(cmd, capture_output=True, text=True, timeout=900, env=env)
+    except subprocess.TimeoutExpired:
+        return {"impl": "triton", "unavailable": "timed out after 900 s"}
+    for row in reversed(done.stdout.splitlines()):
+        if row.startswith("{"):
+            return json.loads(row)
+    tail = (done.stderr or done.stdout).strip().splitlines()[-1:] or ["no output"]
+    return {"impl": "triton", "unavailable": f"exit {done.returncode}: {tail[0][:300]}"}
+
+
+def run_triton(args) -> None:
+    """The reference's own GPU backend (Triton, unmodified, from baseline/_ref) on the same
+    workload and step as this library's arm, on one GPU (rank 0 only)."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    if not torch.cuda.is_available():
+        print(json.dumps({"impl": "triton", "unavailable": "no CUDA device"}), flush=True)
+        return
+    ref = reference_package("triton")
+    if ref is None:
+        print(json.dumps({"impl": "triton", "unavailable": "the reference package is not installed "
+                          "under baseline/_ref"}), flush=True)
+        return
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    world_cpu, mvp_cpu, tri_cpu, attr_cpu, tex_cpu, target_cpu = build_scene(
+        args.views, args.res, args.subdiv, args.tex, 0, 1)
+    res = args.res
+    ctx = ref.RasterizeContext(dev)
+    tri, attr, mvp, target = (t.to(dev) for t in (tri_cpu, attr_cpu, mvp_cpu, target_cpu))
+    tex = tex_cpu.to(dev).requires_grad_(True)
+    verts = world_cpu.to(dev).requires_grad_(True)
+
+    def step():
+        verts.grad = None
+        tex.grad = None
+        # World to clip as diffrast's examples do it (examples/common.py:320-323).
+        pos = torch.nn.functional.pad(verts, (0, 1), value=1.0) @ mvp.transpose(-1, -2)
+        rast, rast_db = ref.rasterize(ctx, pos, tri, (res, res))
+        out, out_da = ref.interpolate(attr, rast, tri, rast_db=rast_db, diff_attrs="all")
+        color = ref.texture(tex, out[..., 0:2], out_da[..., 0:4], filter_mode="linear-mipmap-linear")
+        image = ref.antialias(color, rast, pos, tri)
+        loss = torch.nn.functional.mse_loss(image, target)
+        loss.backward()
+        return loss
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    with ClockSampler(gpu_id(dev)) as clocks:
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            step()
+        end.record()
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / args.steps
+    import triton
+
+    line = {
+        "impl": "triton", "metric": METRIC, "value": round(args.views * res * res / (ms / 1e3) / 1e6, 1),
+        "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 2), "higher_is_better": True, "dtype": "f32",
+        "backend": f"the reference's Triton backend, unmodified (diffrast {ref.__version__}, "
+                   f"triton {triton.__version__}), eager launches as the reference runs them",
+        "config": {"workload": f"BASELINE config 5: {args.views} views {res}x{res}, "
+                               f"icosphere-{args.subdiv}, tex {args.tex}^2x3 linear-mipmap-linear, "
+                               "antialias, MSE, fwd+bwd to tex and pos (same as this library's arm)"},
+        "peak_mem_gb": round(torch.cuda.max_memory_allocated(dev) / 1e9, 1),
+        "clocks": clocks.summary(),
+    }  # fmt: skip
+    print(json.dumps(line), flush=True)
 
 
 def run_reference(args) -> None:
@@ -572,13 +808,16 @@ def main() -> None:
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=10)
     parser.add_argument("--warmup", type=int, default=3)
-    parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    parser.add_argument("--impl", choices=["ours", "reference", "triton"], default="ours")
     parser.add_argument("--views", type=int, default=64)
     parser.add_argument("--res", type=int, default=1024)
     parser.add_argument("--subdiv", type=int, default=8)
     parser.add_argument("--tex", type=int, default=4096)
     parser.add_argument("--cpu-res", type=int, default=8)
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-gpu-reference", action="store_true",
+                        help="skip the reference Triton backend and the config-1 pair")
+    parser.add_argument("--triton-steps", type=int, default=5)
     parser.add_argument("--eager", action="store_true",
                         help="launch every step's kernels from Python instead of replaying a CUDA "
                              "graph of the step")
@@ -587,6 +826,8 @@ def main() -> None:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.impl == "triton":
+        run_triton(args)
     else:
         run_ours(args)
 

@@ -8,6 +8,7 @@ build a graph (``create_graph=True``) raises, like the reference's first-order g
 from __future__ import annotations
 
 import functools
+import weakref
 
 import torch
 from torch import Tensor
@@ -50,39 +51,138 @@ def _slice_gradient(src: Tensor, spec: tuple[int, int] | None, want: bool):
     return torch.empty(src.shape, dtype=src.dtype, device=src.device), spec[0]
 
 
+class CoordinatePort:
+    """Hand-over of compact coordinate gradients from texture lookups to the interpolation whose
+    output channels they read.
+
+    ``interpolate`` returns, next to ``out`` and ``out_da``, a zero-size ``sink`` tensor of its
+    autograd node, and attaches this port to both outputs. A lookup given channel slices of them
+    (``out[..., 0:2]``, ``out_da[..., 0:4]``) depends on ``sink`` instead of the outputs; its
+    backward pass leaves its compact uv / uv_da gradients in ``pending`` and returns an empty
+    gradient for ``sink``, and the interpolation's backward pass reads them from there. So no
+    zero-padded gradient records of the whole outputs are written or read. Entries are tagged
+    with the autograd graph task that made them: a backward pass only ever uses its own.
+    """
+
+    def __init__(self, sink: Tensor, pending: dict) -> None:
+        self.sink = sink
+        self.pending = pending
+
+
+class Route:
+    """How a lookup's coordinate gradients leave it: through ``pending`` of a
+    :class:`CoordinatePort`, for uv and uv_da as requested at the forward pass."""
+
+    def __init__(self, pending: dict, want_uv: bool, want_da: bool) -> None:
+        self.pending = pending
+        self.want_uv = want_uv
+        self.want_da = want_da
+
+    def deliver(self, key, uv_first, g_uv, da_first, g_da) -> None:
+        self.pending[(torch._C._current_graph_task_id(), key)] = (uv_first, g_uv, da_first, g_da)
+
+
+def _take_pending(pending: dict) -> list:
+    """The hand-overs delivered to ``pending`` in the running backward pass; clears ``pending``
+    (entries of other, finished passes are stale)."""
+    task = torch._C._current_graph_task_id()
+    mine = [v for k, v in pending.items() if k[0] == task]
+    pending.clear()
+    return mine
+
+
+class PositionPort:
+    """Hand-over of antialias's position gradient to the rasterization that made its ``rast``.
+
+    Both ops differentiate the same clip positions; without the hand-over, each fills a gradient
+    buffer of the positions' size with zeros, scatters into it, and autograd adds the two. With
+    it, ``rasterize`` returns a zero-size ``sink`` next to rast, rast_db and the keys, and this
+    port is attached to rast; an antialias pass given that rast and the same ``pos`` tensor
+    depends on ``sink`` instead of ``pos``, leaves its position gradient in ``pending``, and the
+    rasterizer's backward pass accumulates its own scatter into that buffer.
+    """
+
+    def __init__(self, sink: Tensor, pending: dict, pos: Tensor) -> None:
+        self.sink = sink
+        self.pending = pending
+        self.pos = weakref.ref(pos)
+
+
+def _collect(pending: dict, channels: int, da_channels: int, grad_out, grad_out_da):
+    """The coordinate gradients delivered in this backward pass (consumed), as at most one compact
+    part per output plus whole images for anything that does not fit that form."""
+    mine = _take_pending(pending)
+    parts: dict[str, tuple[int, Tensor]] = {}
+    for uv_first, g_uv, da_first, g_da in mine:
+        for name, first, g in (("out", uv_first, g_uv), ("da", da_first, g_da)):
+            if g is None:
+                continue
+            held = parts.get(name)
+            if held is None:
+                parts[name] = (first, g)
+            elif held[0] == first and held[1].shape == g.shape:
+                parts[name] = (first, held[1] + g)
+            else:  # different channel ranges: fold into the whole image
+                width = channels if name == "out" else da_channels
+                full = grad_out if name == "out" else grad_out_da
+                if full is None:
+                    full = torch.zeros((*g.shape[:3], width), device=g.device)
+                else:
+                    full = full.clone()
+                full[..., first:first + g.shape[-1]] += g
+                if name == "out":
+                    grad_out = full
+                else:
+                    grad_out_da = full
+    return parts.get("out"), parts.get("da"), grad_out, grad_out_da
+
+
 class Rasterize(torch.autograd.Function):
-    """Visibility, then rast / rast_db; gradients reach pos through the barycentric resolve."""
+    """Visibility, then rast / rast_db; gradients reach pos through the barycentric resolve.
+    Returns ``(rast, rast_db, keys, sink)``; ``sink`` receives antialias's position gradient
+    (:class:`PositionPort`)."""
 
     @staticmethod
     def forward(ctx, pos: Tensor, tri: Tensor, height: int, width: int, grad_db: bool,
-                prev_keys: Tensor | None, ranges: K.RangeTable | None):
+                prev_keys: Tensor | None, ranges: K.RangeTable | None, pending: dict):
         keys = K.raster_keys(pos, tri, height, width, prev_keys, ranges)
         rast, rast_db = K.resolve_fwd(pos, tri, keys)
         # Unused outputs (keys always, rast_db often) get no zero-filled gradient.
         ctx.set_materialize_grads(False)
         ctx.save_for_backward(_saveable(pos), _saveable(tri), keys)
         ctx.grad_db = grad_db
+        ctx.pending = pending
         ctx.mark_non_differentiable(keys)
         if not grad_db:
             ctx.mark_non_differentiable(rast_db)
-        return rast, rast_db, keys
+        return rast, rast_db, keys, pos.new_empty(0)
 
     @staticmethod
     @first_order("rasterize")
-    def backward(ctx, grad_rast, grad_db, _grad_keys):
+    def backward(ctx, grad_rast, grad_db, _grad_keys, grad_sink):
         pos, tri, keys = ctx.saved_tensors
-        if grad_rast is None:
-            grad_rast = torch.zeros((*keys.shape, 4), dtype=pos.dtype, device=pos.device)
+        start = None
+        if grad_sink is not None:
+            for g in _take_pending(ctx.pending):
+                start = g if start is None else start + g
         use_db = ctx.grad_db and grad_db is not None
-        grad_pos = K.resolve_bwd(pos, tri, keys, K.aligned(grad_rast),
-                                 K.aligned(grad_db) if use_db else None)
-        return grad_pos, None, None, None, None, None, None
+        if grad_rast is None and not use_db and start is not None:
+            grad_pos = start
+        else:
+            if grad_rast is None:
+                grad_rast = torch.zeros((*keys.shape, 4), dtype=pos.dtype, device=pos.device)
+            grad_pos = K.resolve_bwd(pos, tri, keys, K.aligned(grad_rast),
+                                     K.aligned(grad_db) if use_db else None, start=start)
+        return grad_pos, None, None, None, None, None, None, None
 
 
 class Interpolate(torch.autograd.Function):
+    """Returns ``(out, out_da, sink)``: ``sink`` is the zero-size tensor through which lookups
+    that read channel slices of the outputs hand their gradients back (:class:`CoordinatePort`)."""
+
     @staticmethod
     def forward(ctx, attr: Tensor, rast: Tensor, rast_db: Tensor | None, tri: Tensor,
-                diff: Tensor | None):
+                diff: Tensor | None, pending: dict):
         attr3 = (attr if attr.ndim == 3 else attr[None]).contiguous()
         channels = attr3.shape[2]
         # Rows padded to 16 bytes for the forward kernel's vector loads.
@@ -94,27 +194,38 @@ class Interpolate(torch.autograd.Function):
         ctx.channels = channels
         ctx.has_da = diff is not None
         ctx.rast_db_given = rast_db is not None
+        ctx.pending = pending
         if diff is None:
             ctx.mark_non_differentiable(out_da)
-        return out, out_da
+        return out, out_da, rast.new_empty(0)
 
     @staticmethod
     @first_order("interpolate")
-    def backward(ctx, grad_out, grad_out_da):
+    def backward(ctx, grad_out, grad_out_da, grad_sink):
         attr3, rast, rast_db, tri, diff = ctx.saved_tensors
-        if grad_out is None:
-            grad_out = torch.zeros((*rast.shape[:3], ctx.channels), device=rast.device)
-        use_da = ctx.has_da and grad_out_da is not None
+        part = part_da = None
+        if grad_sink is not None:
+            num_da = 0 if diff is None else 2 * diff.shape[0]
+            part, part_da, grad_out, grad_out_da = _collect(ctx.pending, ctx.channels, num_da,
+                                                            grad_out, grad_out_da)
+        use_da = ctx.has_da and (grad_out_da is not None or part_da is not None)
+        if not use_da:
+            grad_out_da = part_da = None
         need_attr = ctx.needs_input_grad[0]
         grad_attr, grad_rast, grad_db = K.interpolate_bwd(
-            attr3, rast, rast_db, tri, diff if use_da else None, grad_out.contiguous(),
-            grad_out_da.contiguous() if use_da else None, need_attr,
+            attr3, rast, rast_db, tri, diff if use_da else None,
+            None if grad_out is None else grad_out.contiguous(),
+            grad_out_da.contiguous() if grad_out_da is not None else None, need_attr,
+            part=None if part is None else part[1].contiguous(),
+            part_first=0 if part is None else part[0],
+            part_da=None if part_da is None else part_da[1].contiguous(),
+            da_first=0 if part_da is None else part_da[0],
         )
         if not ctx.rast_db_given:
             grad_db = None
         if grad_attr is not None:
             grad_attr = grad_attr.view(ctx.attr_shape)
-        return grad_attr, grad_rast, grad_db, None, None
+        return grad_attr, grad_rast, grad_db, None, None, None
 
 
 class MipChain(torch.autograd.Function):
@@ -153,18 +264,22 @@ class Texture(torch.autograd.Function):
     uv_da and the level-of-detail bias as the filter mode allows.
 
     uv and uv_da may be passed as the wider tensors they are channel slices of (``uv_spec`` /
-    ``da_spec`` = (first channel, count)), such as interpolate's outputs: their gradients are then
-    written straight into gradients of the wider tensors instead of being copied there by the
-    slices' own backward."""
+    ``da_spec`` = (first channel, count)), such as interpolate's outputs. With a ``route`` (the
+    outputs of :func:`diffrast_b200.interpolate`), they arrive detached and their compact
+    gradients go back through the interpolation's :class:`CoordinatePort` (``sink`` is its
+    zero-size tensor); otherwise the gradients are written straight into gradients of the wider
+    tensors instead of being copied there by the slices' own backward."""
 
     @staticmethod
-    def forward(ctx, uv_src, da_src, bias, mode: int, boundary: int, uv_spec, da_spec, *levels):
+    def forward(ctx, uv_src, da_src, bias, mode: int, boundary: int, uv_spec, da_spec, route,
+                sink, *levels):
         levels = [lv.contiguous() for lv in levels]
         out = K.texture_fwd(list(levels), _take(uv_src, uv_spec), _take(da_src, da_spec), bias,
                             mode, boundary)
         ctx.save_for_backward(*(_saveable(t) for t in (uv_src, da_src, bias, *levels)))
         ctx.settings = (mode, boundary, da_src is not None, bias is not None, len(levels))
         ctx.specs = (uv_spec, da_spec)
+        ctx.route = route
         return out
 
     @staticmethod
@@ -172,23 +287,31 @@ class Texture(torch.autograd.Function):
     def backward(ctx, grad_out):
         mode, boundary, has_da, has_bias, count = ctx.settings
         uv_spec, da_spec = ctx.specs
+        route = ctx.route
         saved = ctx.saved_tensors
         uv_src, da_src, bias, levels = saved[0], saved[1], saved[2], list(saved[3:])
         need = ctx.needs_input_grad
-        want_uv = need[0] and mode > 0
-        want_da = need[1] and has_da and mode == 3
+        want_uv = (route.want_uv if route is not None else need[0]) and mode > 0
+        want_da = (route.want_da if route is not None else need[1]) and has_da and mode == 3
         want_bias = need[2] and has_bias and mode == 3
-        g_uv_src, uv_first = _slice_gradient(uv_src, uv_spec, want_uv)
-        g_da_src, da_first = _slice_gradient(da_src, da_spec, want_da)
+        g_uv_src = g_da_src = None
+        uv_first = da_first = -1
+        if route is None:
+            g_uv_src, uv_first = _slice_gradient(uv_src, uv_spec, want_uv)
+            g_da_src, da_first = _slice_gradient(da_src, da_spec, want_da)
         grads, g_uv, g_da, g_bias = K.texture_bwd(levels, _take(uv_src, uv_spec),
                                                   _take(da_src, da_spec), bias, mode, boundary,
                                                   grad_out.contiguous(), want_uv, want_da,
                                                   want_bias, grad_uv=g_uv_src, grad_da=g_da_src,
                                                   uv_first=uv_first, da_first=da_first)
+        level_grads = [g if need[9 + i] else None for i, g in enumerate(grads)]
+        if route is not None:
+            route.deliver(id(ctx), uv_spec[0], g_uv, None if da_spec is None else da_spec[0], g_da)
+            sink = grad_out.new_empty(0) if need[8] else None
+            return (None, None, g_bias, None, None, None, None, None, sink, *level_grads)
         g_uv = g_uv_src if uv_spec is not None else g_uv
         g_da = g_da_src if da_spec is not None else g_da
-        level_grads = [g if need[7 + i] else None for i, g in enumerate(grads)]
-        return (g_uv, g_da, g_bias, None, None, None, None, *level_grads)
+        return (g_uv, g_da, g_bias, None, None, None, None, None, None, *level_grads)
 
 
 class TextureChain(torch.autograd.Function):
@@ -201,7 +324,7 @@ class TextureChain(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, uv_src, da_src, bias, mode: int, boundary: int, count: int, tex: Tensor,
-                uv_spec=None, da_spec=None):
+                uv_spec=None, da_spec=None, route=None, sink=None):
         tex = tex.contiguous()
         levels = [tex]
         for _ in range(count):
@@ -212,6 +335,7 @@ class TextureChain(torch.autograd.Function):
         ctx.levels = levels[1:]
         ctx.settings = (mode, boundary)
         ctx.specs = (uv_spec, da_spec)
+        ctx.route = route
         return out
 
     @staticmethod
@@ -219,22 +343,25 @@ class TextureChain(torch.autograd.Function):
     def backward(ctx, grad_out):
         mode, boundary = ctx.settings
         uv_spec, da_spec = ctx.specs
+        route = ctx.route
         uv_src, da_src, bias, tex = ctx.saved_tensors
         levels = [tex, *ctx.levels]
         need = ctx.needs_input_grad
-        want_uv = need[0] and mode > 0
-        want_da = need[1] and da_src is not None and mode == 3
+        want_uv = (route.want_uv if route is not None else need[0]) and mode > 0
+        want_da = ((route.want_da if route is not None else need[1]) and da_src is not None
+                   and mode == 3)
         want_bias = need[2] and bias is not None and mode == 3
-        g_uv_src, uv_first = _slice_gradient(uv_src, uv_spec, want_uv)
-        g_da_src, da_first = _slice_gradient(da_src, da_spec, want_da)
+        g_uv_src = g_da_src = None
+        uv_first = da_first = -1
+        if route is None:
+            g_uv_src, uv_first = _slice_gradient(uv_src, uv_spec, want_uv)
+            g_da_src, da_first = _slice_gradient(da_src, da_spec, want_da)
         grads, g_uv, g_da, g_bias = K.texture_bwd(levels, _take(uv_src, uv_spec),
                                                   _take(da_src, da_spec), bias, mode, boundary,
                                                   grad_out.contiguous(), want_uv, want_da,
                                                   want_bias, keep_padded=True, grad_uv=g_uv_src,
                                                   grad_da=g_da_src, uv_first=uv_first,
                                                   da_first=da_first)
-        g_uv = g_uv_src if uv_spec is not None else g_uv
-        g_da = g_da_src if da_spec is not None else g_da
         grad_tex = None
         if need[6]:
             padded = grads[0].shape[-1] != tex.shape[-1]
@@ -248,21 +375,36 @@ class TextureChain(torch.autograd.Function):
             grad_tex = grads[0]
             if grad_tex.shape[-1] != tex.shape[-1]:
                 grad_tex = grad_tex[..., : tex.shape[-1]].contiguous()
-        return g_uv, g_da, g_bias, None, None, None, grad_tex, None, None
+        if route is not None:
+            route.deliver(id(ctx), uv_spec[0], g_uv, None if da_spec is None else da_spec[0], g_da)
+            sink = grad_out.new_empty(0) if need[10] else None
+            return None, None, g_bias, None, None, None, grad_tex, None, None, None, sink
+        g_uv = g_uv_src if uv_spec is not None else g_uv
+        g_da = g_da_src if da_spec is not None else g_da
+        return g_uv, g_da, g_bias, None, None, None, grad_tex, None, None, None, None
+
+
+def _deliver(route, grad_pos):
+    """Leave ``grad_pos`` for the rasterizer (``route`` is its port's ``pending``)."""
+    route[(torch._C._current_graph_task_id(), id(grad_pos))] = grad_pos
 
 
 class Antialias(torch.autograd.Function):
+    """With a ``route`` (``pending`` of a :class:`PositionPort`; ``pos`` then arrives detached and
+    ``sink`` is the port's), the position gradient goes to the rasterizer's backward pass."""
+
     @staticmethod
     def forward(ctx, color: Tensor, rast: Tensor, pos: Tensor, tri: Tensor, opposite: Tensor,
-                boost: float):
+                boost: float, route=None, sink=None):
         pos3 = pos if pos.ndim == 3 else pos[None]
         # The pair records (about 25 bytes per pixel) spare the backward pass the edge tests.
         out, pairs = K.antialias_fwd(color, rast, pos3, tri, opposite,
-                                     record_pairs=any(ctx.needs_input_grad[:3]))
+                                     record_pairs=any(ctx.needs_input_grad[:3]) or route is not None)
         saved = (color, rast, pos3, tri, opposite, pairs)
         ctx.save_for_backward(*(_saveable(t) for t in saved))
         ctx.boost = boost
         ctx.pos_shape = pos.shape
+        ctx.route = route
         return out
 
     @staticmethod
@@ -271,16 +413,20 @@ class Antialias(torch.autograd.Function):
         color, rast, pos3, tri, opposite, pairs = ctx.saved_tensors
         grad_color, grad_pos = K.antialias_bwd(color, rast, pos3, tri, opposite,
                                                grad_out.contiguous(), ctx.boost, pairs)
-        return grad_color, None, grad_pos.view(ctx.pos_shape), None, None, None
+        grad_pos = grad_pos.view(ctx.pos_shape)
+        if ctx.route is not None:
+            _deliver(ctx.route, grad_pos)
+            return grad_color, None, None, None, None, None, None, grad_pos.new_empty(0)
+        return grad_color, None, grad_pos, None, None, None, None, None
 
 
 class AntialiasMSE(torch.autograd.Function):
     """Antialias with the squared-error loss ``scale * sum (out - target)^2`` fused into its
-    passes; returns ``(out, loss)``."""
+    passes; returns ``(out, loss)``. ``route`` / ``sink`` as for :class:`Antialias`."""
 
     @staticmethod
     def forward(ctx, color: Tensor, rast: Tensor, pos: Tensor, tri: Tensor, opposite: Tensor,
-                target: Tensor, scale: float, boost: float):
+                target: Tensor, scale: float, boost: float, route=None, sink=None):
         pos3 = pos if pos.ndim == 3 else pos[None]
         out, residual, pairs, partial = K.antialias_mse_fwd(color, rast, pos3, tri, opposite, target)
         loss = partial.sum() * scale
@@ -288,6 +434,7 @@ class AntialiasMSE(torch.autograd.Function):
         saved = (color, rast, pos3, tri, opposite, pairs, residual)
         ctx.save_for_backward(*(_saveable(t) for t in saved))
         ctx.scale, ctx.boost, ctx.pos_shape = scale, boost, pos.shape
+        ctx.route = route
         return out, loss
 
     @staticmethod
@@ -299,7 +446,12 @@ class AntialiasMSE(torch.autograd.Function):
         grad_color, grad_pos = K.antialias_mse_bwd(
             color, rast, pos3, tri, opposite, residual, grad_loss.detach().float().contiguous(),
             ctx.scale, None if grad_out is None else grad_out.contiguous(), ctx.boost, pairs)
-        return grad_color, None, grad_pos.view(ctx.pos_shape), None, None, None, None, None
+        grad_pos = grad_pos.view(ctx.pos_shape)
+        if ctx.route is not None:
+            _deliver(ctx.route, grad_pos)
+            return (grad_color, None, None, None, None, None, None, None, None,
+                    grad_pos.new_empty(0))
+        return grad_color, None, grad_pos, None, None, None, None, None, None, None
 
 
 class ToClip(torch.autograd.Function):

@@ -9,6 +9,7 @@ from __future__ import annotations
 
 import contextlib
 import functools
+import os
 from ctypes import byref, c_int64
 from typing import NamedTuple
 
@@ -21,21 +22,32 @@ from diffrast_b200 import _native as N
 # events around its launches on the current stream, keyed by stage name. bench.py uses this to
 # time the dominant kernel inside its timed region.
 timings: dict[str, list] | None = None
+# With DIFFRAST_B200_NVTX=1 every wrapper's launches are also enclosed in an NVTX range named
+# after its stage ("diffrast_b200.<stage>"), for profilers that filter or group by NVTX.
+nvtx = os.environ.get("DIFFRAST_B200_NVTX", "0") not in ("", "0")
 
 
 def timed(name: str):
+    label = f"diffrast_b200.{name}"
+
     def decorate(fn):
         @functools.wraps(fn)
         def wrapper(*args, **kwargs):
-            if timings is None:
-                return fn(*args, **kwargs)
-            start = torch.cuda.Event(enable_timing=True)
-            end = torch.cuda.Event(enable_timing=True)
-            start.record()
-            out = fn(*args, **kwargs)
-            end.record()
-            timings.setdefault(name, []).append((start, end))
-            return out
+            if nvtx:
+                torch.cuda.nvtx.range_push(label)
+            try:
+                if timings is None:
+                    return fn(*args, **kwargs)
+                start = torch.cuda.Event(enable_timing=True)
+                end = torch.cuda.Event(enable_timing=True)
+                start.record()
+                out = fn(*args, **kwargs)
+                end.record()
+                timings.setdefault(name, []).append((start, end))
+                return out
+            finally:
+                if nvtx:
+                    torch.cuda.nvtx.range_pop()
 
         return wrapper
 
@@ -233,9 +245,14 @@ def resolve_fwd(pos: Tensor, tri: Tensor, keys: Tensor) -> tuple[Tensor, Tensor]
 
 @timed("resolve_bwd")
 def resolve_bwd(pos: Tensor, tri: Tensor, keys: Tensor, grad_rast: Tensor,
-                grad_db: Tensor | None) -> Tensor:
+                grad_db: Tensor | None, start: Tensor | None = None) -> Tensor:
+    """Position gradient of rast / rast_db, accumulated into ``start`` (a gradient of pos's
+    shape that other ops produced, updated in place) or into zeros."""
     batch, height, width = keys.shape
-    grad_pos = torch.zeros_like(pos)
+    if start is not None and start.shape == pos.shape and start.is_contiguous():
+        grad_pos = start
+    else:
+        grad_pos = torch.zeros_like(pos) if start is None else start.reshape(pos.shape).clone()
     N.check(
         N.lib().dr_raster_resolve_bwd(pos.data_ptr(), pos.shape[0], tri.data_ptr(),
                                       keys.data_ptr(), batch, pos.shape[1], tri.shape[0], height,
@@ -293,22 +310,39 @@ def interpolate_fwd(attr3: Tensor, rast: Tensor, rast_db: Tensor | None, tri: Te
 
 
 @timed("interpolate_bwd")
-def interpolate_bwd(attr3, rast, rast_db, tri, diff, grad_out, grad_out_da, need_attr):
-    """Gradients of attr (``attr3`` unpadded, ``[attr_batch, V, channels]``), rast and rast_db."""
+def interpolate_bwd(attr3, rast, rast_db, tri, diff, grad_out, grad_out_da, need_attr,
+                    part=None, part_first=0, part_da=None, da_first=0):
+    """Gradients of attr (``attr3`` unpadded, ``[attr_batch, V, channels]``), rast and rast_db.
+
+    ``grad_out`` / ``grad_out_da`` are whole gradient images or None; ``part`` (``[batch, h, w,
+    k]``, contiguous) adds the gradient of out channels ``part_first ..``, ``part_da`` that of
+    out_da channels ``da_first ..``."""
     batch, height, width, _ = rast.shape
     channels = attr3.shape[2]
     num_diff = 0 if diff is None else diff.shape[0]
     grad_attr = torch.zeros_like(attr3) if need_attr else None
     grad_rast = torch.empty_like(rast)
-    grad_db = torch.empty_like(rast) if grad_out_da is not None else None
-    N.check(
-        N.lib().dr_interpolate_bwd(attr3.data_ptr(), attr3.shape[0], attr3.shape[1], channels,
-                                   rast.data_ptr(), N.ptr(rast_db), tri.data_ptr(), tri.shape[0],
-                                   N.ptr(diff), num_diff, batch, height, width,
-                                   grad_out.data_ptr(), N.ptr(grad_out_da), N.ptr(grad_attr),
-                                   grad_rast.data_ptr(), N.ptr(grad_db), N.stream(rast.device)),
-        "dr_interpolate_bwd",
-    )  # fmt: skip
+    has_da = grad_out_da is not None or part_da is not None
+    grad_db = torch.empty_like(rast) if has_da else None
+    lib = N.lib()
+    if part is None and part_da is None:
+        if grad_out is None:
+            grad_out = torch.zeros((*rast.shape[:3], channels), device=rast.device)
+        status = lib.dr_interpolate_bwd(
+            attr3.data_ptr(), attr3.shape[0], attr3.shape[1], channels, rast.data_ptr(),
+            N.ptr(rast_db), tri.data_ptr(), tri.shape[0], N.ptr(diff), num_diff, batch, height,
+            width, grad_out.data_ptr(), N.ptr(grad_out_da), N.ptr(grad_attr),
+            grad_rast.data_ptr(), N.ptr(grad_db), N.stream(rast.device))
+        N.check(status, "dr_interpolate_bwd")
+    else:
+        status = lib.dr_interpolate_bwd_parts(
+            attr3.data_ptr(), attr3.shape[0], attr3.shape[1], channels, rast.data_ptr(),
+            N.ptr(rast_db), tri.data_ptr(), tri.shape[0], N.ptr(diff), num_diff, batch, height,
+            width, N.ptr(grad_out), N.ptr(grad_out_da), N.ptr(part), part_first,
+            0 if part is None else part.shape[-1], N.ptr(part_da), da_first,
+            0 if part_da is None else part_da.shape[-1], N.ptr(grad_attr), grad_rast.data_ptr(),
+            N.ptr(grad_db), N.stream(rast.device))
+        N.check(status, "dr_interpolate_bwd_parts")
     return grad_attr, grad_rast, grad_db
 
 

@@ -65,6 +65,11 @@ _SIGNATURES = {
         [_P, c_int64, c_int64, c_int32, _P, _P, _P, c_int64, _P, c_int32, c_int64, c_int32,
          c_int32, _P, _P, _P, _P, _P, _P],
     ),
+    "dr_interpolate_bwd_parts": (
+        c_int,
+        [_P, c_int64, c_int64, c_int32, _P, _P, _P, c_int64, _P, c_int32, c_int64, c_int32,
+         c_int32, _P, _P, _P, c_int32, c_int32, _P, c_int32, c_int32, _P, _P, _P, _P],
+    ),
     "dr_texture_fwd": (
         c_int,
         [_P, _P, _P, _P, c_int32, c_int32, _P, c_int64, _P, c_int64, _P, c_int64, c_int32,

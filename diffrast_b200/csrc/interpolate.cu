@@ -190,12 +190,32 @@ __device__ __forceinline__ void scatter_attr(float* __restrict__ grad_attr, long
   if (active && (peers & ((1u << lane) - 1u)) == 0u) red_add(grad_attr + row * channels + c, v[0]);
 }
 
+// The gradients of interpolate's outputs, given in pieces: whole pixel records of out
+// ([P, channels]) and out_da ([P, 2 num_diff]), either of which may be missing, plus compact
+// channel ranges handed over by a consumer that read a channel slice of an output (part:
+// [P, part_count] for out channels part_first ..; part_da: [P, da_count] for out_da channels
+// da_first ..), as texture does with interpolated uv and uv_da. Missing pieces are zero, and
+// channels no piece covers are not visited when no whole record is given.
+struct GradParts {
+  const float* out;
+  const float* out_da;
+  const float* part;
+  int part_first, part_count;
+  const float* part_da;
+  int da_first, da_count;
+};
+
+__device__ __forceinline__ float part_value(const float* __restrict__ part, int first, int count,
+                                            long long p, int c) {
+  const int i = c - first;
+  return (part != nullptr && i >= 0 && i < count) ? part[p * count + i] : 0.0f;
+}
+
 __global__ void __launch_bounds__(256, 6) interp_bwd_kernel(
     const float* __restrict__ attr, long long attr_batch, long long num_vert, int channels,
     const float4* __restrict__ rast, const float4* __restrict__ rast_db, const int* __restrict__ tri,
     int num_tri, const int* __restrict__ diff, int num_diff, long long total,
-    long long pixels_per_image, const float* __restrict__ grad_out,
-    const float* __restrict__ grad_out_da, float* __restrict__ grad_attr,
+    long long pixels_per_image, const GradParts gp, float* __restrict__ grad_attr,
     float4* __restrict__ grad_rast, float4* __restrict__ grad_db) {
   const long long p = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   const bool in_range = p < total;
@@ -219,11 +239,16 @@ __global__ void __launch_bounds__(256, 6) interp_bwd_kernel(
     }
   }
 
+  // Channels that can carry a gradient (uniform over the grid).
+  const int c_lo = gp.out != nullptr ? 0 : max(0, gp.part_first);
+  const int c_hi = gp.out != nullptr ? channels
+                                     : (gp.part != nullptr ? min(channels, gp.part_first + gp.part_count) : 0);
   float gu = 0.0f, gv = 0.0f;
-  for (int c = 0; c < channels; ++c) {
+  for (int c = c_lo; c < c_hi; ++c) {
     float g = 0.0f, x0 = 0.0f, x1 = 0.0f, x2 = 0.0f;
     if (k.covered) {
-      g = grad_out[p * channels + c];
+      if (gp.out != nullptr) g = gp.out[p * channels + c];
+      g += part_value(gp.part, gp.part_first, gp.part_count, p, c);
       x0 = __ldg(a0 + c);
       x1 = __ldg(a1 + c);
       x2 = __ldg(a2 + c);
@@ -238,16 +263,24 @@ __global__ void __launch_bounds__(256, 6) interp_bwd_kernel(
   }
   if (in_range) grad_rast[p] = make_float4(gu, gv, 0.0f, 0.0f);
 
-  if (grad_out_da == nullptr) return;
+  if (gp.out_da == nullptr && gp.part_da == nullptr) return;
+  // Differentiated channel pairs (2 j, 2 j + 1) that can carry a gradient.
+  const int j_lo = gp.out_da != nullptr ? 0 : max(0, gp.da_first) / 2;
+  const int j_hi = gp.out_da != nullptr ? num_diff
+                                        : min(num_diff, (gp.da_first + gp.da_count + 1) / 2);
   const float4 d = k.covered ? rast_db[p] : make_float4(0.f, 0.f, 0.f, 0.f);
   float g_dudx = 0.0f, g_dudy = 0.0f, g_dvdx = 0.0f, g_dvdy = 0.0f;
-  for (int j = 0; j < num_diff; ++j) {
+  for (int j = j_lo; j < j_hi; ++j) {
     float gx = 0.0f, gy = 0.0f, du = 0.0f, dv = 0.0f;
     int c = 0;
     if (k.covered) {
       c = __ldg(diff + j);
-      gx = grad_out_da[(p * num_diff + j) * 2];
-      gy = grad_out_da[(p * num_diff + j) * 2 + 1];
+      if (gp.out_da != nullptr) {
+        gx = gp.out_da[(p * num_diff + j) * 2];
+        gy = gp.out_da[(p * num_diff + j) * 2 + 1];
+      }
+      gx += part_value(gp.part_da, gp.da_first, gp.da_count, p, 2 * j);
+      gy += part_value(gp.part_da, gp.da_first, gp.da_count, p, 2 * j + 1);
       const float x2 = __ldg(a2 + c);
       du = __ldg(a0 + c) - x2;
       dv = __ldg(a1 + c) - x2;
@@ -319,6 +352,36 @@ extern "C" int dr_interpolate_fwd(const float* attr, int64_t attr_batch, int64_t
   return launch_status();
 }
 
+namespace dr {
+namespace {
+
+int launch_interp_bwd(const float* attr, int64_t attr_batch, int64_t num_vert, int32_t channels,
+                      const float* rast, const float* rast_db, const int32_t* tri,
+                      int64_t num_tri, const int32_t* diff, int32_t num_diff, int64_t batch,
+                      int32_t height, int32_t width, const GradParts& gp, float* grad_attr,
+                      float* grad_rast, float* grad_db, cudaStream_t s) {
+  const bool any_da = gp.out_da != nullptr || gp.part_da != nullptr;
+  if (bad_interp_args(attr, attr_batch, num_vert, channels, rast, rast_db, tri, num_tri, diff,
+                      any_da ? num_diff : 0, batch, height, width) ||
+      grad_rast == nullptr || (any_da && (grad_db == nullptr || num_diff == 0)) ||
+      (gp.part != nullptr && (gp.part_first < 0 || gp.part_count < 1 ||
+                              gp.part_first + gp.part_count > channels)) ||
+      (gp.part_da != nullptr && (gp.da_first < 0 || gp.da_count < 1 ||
+                                 gp.da_first + gp.da_count > 2 * num_diff)))
+    return DR_ERR_INVALID_ARGUMENT;
+  const long long total = batch * static_cast<long long>(height) * width;
+  if (total == 0) return DR_OK;
+  interp_bwd_kernel<<<blocks_for(total, 256), 256, 0, s>>>(
+      attr, attr_batch, num_vert, channels, reinterpret_cast<const float4*>(rast),
+      reinterpret_cast<const float4*>(rast_db), tri, static_cast<int>(num_tri), diff,
+      any_da ? num_diff : 0, total, static_cast<long long>(height) * width, gp, grad_attr,
+      reinterpret_cast<float4*>(grad_rast), reinterpret_cast<float4*>(grad_db));
+  return launch_status();
+}
+
+}  // namespace
+}  // namespace dr
+
 extern "C" int dr_interpolate_bwd(const float* attr, int64_t attr_batch, int64_t num_vert,
                                   int32_t channels, const float* rast, const float* rast_db,
                                   const int32_t* tri, int64_t num_tri, const int32_t* diff,
@@ -326,18 +389,26 @@ extern "C" int dr_interpolate_bwd(const float* attr, int64_t attr_batch, int64_t
                                   const float* grad_out, const float* grad_out_da,
                                   float* grad_attr, float* grad_rast, float* grad_db,
                                   void* stream) {
-  if (bad_interp_args(attr, attr_batch, num_vert, channels, rast, rast_db, tri, num_tri, diff,
-                      grad_out_da != nullptr ? num_diff : 0, batch, height, width) ||
-      grad_out == nullptr || grad_rast == nullptr ||
-      (grad_out_da != nullptr && (grad_db == nullptr || num_diff == 0)))
-    return DR_ERR_INVALID_ARGUMENT;
-  const long long total = batch * static_cast<long long>(height) * width;
-  if (total == 0) return DR_OK;
-  interp_bwd_kernel<<<blocks_for(total, 256), 256, 0, as_stream(stream)>>>(
-      attr, attr_batch, num_vert, channels, reinterpret_cast<const float4*>(rast),
-      reinterpret_cast<const float4*>(rast_db), tri, static_cast<int>(num_tri), diff,
-      grad_out_da != nullptr ? num_diff : 0, total, static_cast<long long>(height) * width,
-      grad_out, grad_out_da, grad_attr, reinterpret_cast<float4*>(grad_rast),
-      reinterpret_cast<float4*>(grad_db));
-  return launch_status();
+  if (grad_out == nullptr) return DR_ERR_INVALID_ARGUMENT;
+  const GradParts gp{grad_out, grad_out_da, nullptr, 0, 0, nullptr, 0, 0};
+  return launch_interp_bwd(attr, attr_batch, num_vert, channels, rast, rast_db, tri, num_tri,
+                           diff, num_diff, batch, height, width, gp, grad_attr, grad_rast,
+                           grad_db, as_stream(stream));
+}
+
+extern "C" int dr_interpolate_bwd_parts(const float* attr, int64_t attr_batch, int64_t num_vert,
+                                        int32_t channels, const float* rast, const float* rast_db,
+                                        const int32_t* tri, int64_t num_tri, const int32_t* diff,
+                                        int32_t num_diff, int64_t batch, int32_t height,
+                                        int32_t width, const float* grad_out,
+                                        const float* grad_out_da, const float* part,
+                                        int32_t part_first, int32_t part_count,
+                                        const float* part_da, int32_t da_first, int32_t da_count,
+                                        float* grad_attr, float* grad_rast, float* grad_db,
+                                        void* stream) {
+  const GradParts gp{grad_out, grad_out_da, part, part_first, part_count,
+                     part_da, da_first, da_count};
+  return launch_interp_bwd(attr, attr_batch, num_vert, channels, rast, rast_db, tri, num_tri,
+                           diff, num_diff, batch, height, width, gp, grad_attr, grad_rast,
+                           grad_db, as_stream(stream));
 }

@@ -82,11 +82,16 @@ def rasterize_layer(
         empty = pos.new_zeros(views, height, width, 4)
         keys = torch.full((views, height, width), EMPTY_KEY, dtype=torch.int64, device=pos.device)
         return empty, empty.clone(), keys
+    pending: dict = {}
     with torch.cuda.device(pos.device):
-        rast, rast_db, keys = F.Rasterize.apply(
+        rast, rast_db, keys, sink = F.Rasterize.apply(
             K.aligned(pos if ranges is None else pos[None]), tri.contiguous(), height, width,
-            bool(grad_db), previous, ranges,
+            bool(grad_db), previous, ranges, pending,
         )
+    if sink.requires_grad and ranges is None:
+        # An antialias pass over this rast and the same pos hands its position gradient to this
+        # rasterization's backward pass (see _functions.PositionPort).
+        rast._dr_pos_port = F.PositionPort(sink, pending, pos)
     return rast, rast_db, keys
 
 
@@ -188,10 +193,18 @@ def interpolate(
         return out, attr.new_zeros(batch, height, width, 2 * len(channels))
     with torch.cuda.device(rast.device):
         diff = K.diff_table(tuple(channels), rast.device)
-        return F.Interpolate.apply(
+        pending: dict = {}
+        out, out_da, sink = F.Interpolate.apply(
             attr, K.aligned(rast), None if rast_db is None else K.aligned(rast_db),
-            tri.contiguous(), diff,
+            tri.contiguous(), diff, pending,
         )
+    if sink.requires_grad:
+        # Lookups that read channel slices of out / out_da hand their gradients back through
+        # this port instead of through whole gradient images (see _functions.CoordinatePort).
+        port = F.CoordinatePort(sink, pending)
+        out._dr_port = port
+        out_da._dr_port = port
+    return out, out_da
 
 
 def _diff_channels(diff_attrs, num_channels: int) -> list[int]:
@@ -314,10 +327,11 @@ def texture(
             mip_level_bias = None if mip_level_bias is None else mip_level_bias.detach()
         uv_src, uv_spec = _channel_slice(uv)
         da_src, da_spec = _channel_slice(uv_da)
+        route, sink, uv_src, da_src = _route(uv_src, uv_spec, da_src, da_spec, _needs_grad(uv_da))
         with torch.cuda.device(uv.device):
             return F.TextureChain.apply(
                 uv_src, da_src, None if mip_level_bias is None else mip_level_bias.contiguous(),
-                mode, _BOUNDARY_INDEX[boundary_mode], count, tex, uv_spec, da_spec,
+                mode, _BOUNDARY_INDEX[boundary_mode], count, tex, uv_spec, da_spec, route, sink,
             )
     if mipmapped:
         if given is None:
@@ -338,11 +352,30 @@ def texture(
     # kernels read them in place through their pixel stride.
     uv_src, uv_spec = _channel_slice(uv)
     da_src, da_spec = _channel_slice(uv_da)
+    route, sink, uv_src, da_src = _route(uv_src, uv_spec, da_src, da_spec, _needs_grad(uv_da))
     with torch.cuda.device(uv.device):
         return F.Texture.apply(
             uv_src, da_src, None if mip_level_bias is None else mip_level_bias.contiguous(), mode,
-            _BOUNDARY_INDEX[boundary_mode], uv_spec, da_spec, *levels,
+            _BOUNDARY_INDEX[boundary_mode], uv_spec, da_spec, route, sink, *levels,
         )
+
+
+def _needs_grad(t: Tensor | None) -> bool:
+    return t is not None and t.requires_grad and torch.is_grad_enabled()
+
+
+def _route(uv_src, uv_spec, da_src, da_spec, has_da: bool):
+    """``(route, sink, uv_src, da_src)`` for a lookup whose uv (and uv_da, if given) are channel
+    slices of the outputs of one :func:`interpolate` call: its coordinate gradients then go back
+    through that call's port, and uv_src / da_src enter the lookup detached. ``(None, None,
+    uv_src, da_src)`` otherwise."""
+    port = getattr(uv_src, "_dr_port", None) if uv_spec is not None else None
+    if port is None:
+        return None, None, uv_src, da_src
+    if has_da and (da_spec is None or getattr(da_src, "_dr_port", None) is not port):
+        return None, None, uv_src, da_src
+    route = F.Route(port.pending, want_uv=True, want_da=has_da)
+    return route, port.sink, uv_src.detach(), None if da_src is None else da_src.detach()
 
 
 def _channel_slice(t: Tensor | None):
@@ -455,11 +488,22 @@ def antialias(
     topology = _check_antialias_inputs(color, rast, pos, tri, topology_hash, pos_gradient_boost)
     if tri.shape[0] == 0 or color.numel() == 0:
         return color.clone()
+    route, sink, pos = _position_route(rast, pos)
     with torch.cuda.device(color.device):
         return F.Antialias.apply(
             color.contiguous(), K.aligned(rast.detach()), K.aligned(pos), tri.contiguous(),
-            topology.opposite(tri), float(pos_gradient_boost),
+            topology.opposite(tri), float(pos_gradient_boost), route, sink,
         )
+
+
+def _position_route(rast: Tensor, pos: Tensor):
+    """``(route, sink, pos)`` for an antialias pass over ``rast`` from :func:`rasterize` with the
+    very ``pos`` tensor it was rasterized from: the position gradient then goes to the
+    rasterizer's backward pass and ``pos`` enters detached. ``(None, None, pos)`` otherwise."""
+    port = getattr(rast, "_dr_pos_port", None)
+    if port is None or port.pos() is not pos or pos.ndim != 3 or not _needs_grad(pos):
+        return None, None, pos
+    return port.pending, port.sink, pos.detach()
 
 
 def antialias_mse(
@@ -495,10 +539,12 @@ def antialias_mse(
     if color.numel() == 0:
         return color.clone(), color.new_zeros(()) + 0.0 * color.sum()
     opposite = topology.opposite(tri) if topology is not None else tri.new_zeros(0)
+    route, sink, pos = _position_route(rast, pos)
     with torch.cuda.device(color.device):
         return F.AntialiasMSE.apply(
             color.contiguous(), K.aligned(rast.detach()), K.aligned(pos), tri.contiguous(),
             opposite, target.detach().contiguous(), float(scale), float(pos_gradient_boost),
+            route, sink,
         )
 
 

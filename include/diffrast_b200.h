@@ -180,6 +180,24 @@ int dr_interpolate_bwd(const float* attr, int64_t attr_batch, int64_t num_vert, 
                        const float* grad_out_da, float* grad_attr, float* grad_rast,
                        float* grad_db, void* stream);
 
+/* dr_interpolate_bwd with the output gradients given in pieces (no counterpart in the
+ * reference, whose consumers hand back whole gradient images): grad_out [batch, h, w, channels]
+ * and grad_out_da [batch, h, w, 2 num_diff] may each be NULL, and compact channel ranges may be
+ * added: part [batch, h, w, part_count] holds the gradient of out channels part_first ..
+ * part_first + part_count - 1, part_da [batch, h, w, da_count] that of out_da channels da_first ..
+ * (either NULL to omit). Whatever is not given counts as zero. A lookup that read uv and uv_da
+ * as channel slices of out and out_da hands its compact coordinate gradients over this way, so
+ * no zero-padded gradient records are written or read. grad_db is written when grad_out_da or
+ * part_da is given. */
+int dr_interpolate_bwd_parts(const float* attr, int64_t attr_batch, int64_t num_vert,
+                             int32_t channels, const float* rast, const float* rast_db,
+                             const int32_t* tri, int64_t num_tri, const int32_t* diff,
+                             int32_t num_diff, int64_t batch, int32_t height, int32_t width,
+                             const float* grad_out, const float* grad_out_da, const float* part,
+                             int32_t part_first, int32_t part_count, const float* part_da,
+                             int32_t da_first, int32_t da_count, float* grad_attr,
+                             float* grad_rast, float* grad_db, void* stream);
+
 /* ---------------------------------------------------------------------------------------------
  * Texture (reference.py:149-194, :491-672; _cube.py:44-143; _triton_texture.py:37-549).
  * Level l has `level_ptr[l]` -> [tex_batch(, 6), level_h[l], level_w[l], channels]; its batch

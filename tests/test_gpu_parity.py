@@ -481,8 +481,9 @@ def test_edge_neighbours_match_golden():
 
 
 def test_texture_of_interpolated_slices_routes_gradients(ctx):
-    """uv = out[..., 0:2] and uv_da = out_da[..., 0:4] of interpolate: the lookup writes their
-    gradients straight into the gradients of out and out_da; the result equals passing copies."""
+    """uv = out[..., 0:2] and uv_da = out_da[..., 0:4] of interpolate: the lookup hands its compact
+    coordinate gradients back to the interpolation (no whole gradient images); the result equals
+    passing copies."""
     sc = scenes.config1_scene(seed=2)
     pos, tri = sc["pos"].cuda(), sc["tri"].cuda()
     gen = torch.Generator().manual_seed(5)
@@ -506,6 +507,95 @@ def test_texture_of_interpolated_slices_routes_gradients(ctx):
             results.append((color, *grads))
         for ours, ref in zip(results[0], results[1]):
             grad_close(ours, ref, 1e-5)
+
+
+def test_coordinate_port_with_other_consumers_and_retained_graphs(ctx):
+    """The hand-over of lookup gradients to interpolate (a zero-size port output) against copies
+    of the slices, where it is hardest: other ops also use out and out_da, two lookups read
+    different slices of one interpolation, a lookup reads uv without uv_da (and one reads uv_da
+    that is not interpolate's), and a retained graph is differentiated twice, first only with
+    respect to the texture (so the interpolation's backward does not run that time)."""
+    sc = scenes.config1_scene(seed=3)
+    pos, tri = sc["pos"].cuda(), sc["tri"].cuda()
+    gen = torch.Generator().manual_seed(11)
+    attr = torch.cat([sc["uv"], torch.rand(sc["uv"].shape[0], 4, generator=gen)], -1).cuda()
+    tex = torch.rand(1, 32, 32, 3, generator=gen).cuda()
+    w1, w2, w3 = (torch.randn(1, 40, 40, k, generator=gen).cuda() for k in (3, 3, 6))
+    rast, rast_db = dr.rasterize(ctx, pos, tri, (40, 40))
+    foreign_da = torch.rand(1, 40, 40, 4, generator=gen).cuda() * 0.01
+
+    def run(copy: bool, case: str):
+        a = attr.clone().requires_grad_(True)
+        t = tex.clone().requires_grad_(True)
+        out, out_da = dr.interpolate(a, rast, tri, rast_db=rast_db, diff_attrs="all")
+
+        def s(x):
+            return x.clone() if copy else x
+
+        mode = "linear-mipmap-linear"
+        if case == "other_consumers":
+            color = dr.texture(t, s(out[..., 0:2]), s(out_da[..., 0:4]), filter_mode=mode)
+            loss = (color * w1).sum() + (out[..., 2:6] ** 2).sum() + (out_da * w3[..., :1]).sum()
+        elif case == "two_lookups":
+            c1 = dr.texture(t, s(out[..., 0:2]), s(out_da[..., 0:4]), filter_mode=mode)
+            c2 = dr.texture(t, s(out[..., 2:4]), s(out_da[..., 4:8]), filter_mode=mode)
+            c3 = dr.texture(t, s(out[..., 0:2]), s(out_da[..., 0:4]), filter_mode="linear")
+            loss = (c1 * w1).sum() + (c2 * w2).sum() + (c3 * w1).sum()
+        elif case == "uv_only":
+            c1 = dr.texture(t, s(out[..., 1:3]), filter_mode="linear")
+            c2 = dr.texture(t, s(out[..., 0:2]), foreign_da, filter_mode=mode)
+            loss = (c1 * w1).sum() + (c2 * w2).sum()
+        else:  # retained graph
+            color = dr.texture(t, s(out[..., 0:2]), s(out_da[..., 0:4]), filter_mode=mode)
+            loss = (color * w1).sum()
+            first = torch.autograd.grad(loss, [t], retain_graph=True)[0]
+            return (first, *torch.autograd.grad(loss, [a, t]))
+        return torch.autograd.grad(loss, [a, t])
+
+    for case in ("other_consumers", "two_lookups", "uv_only", "retained"):
+        ours, ref = run(False, case), run(True, case)
+        for x, y in zip(ours, ref):
+            grad_close(x, y, 1e-5)
+
+
+def test_position_port_matches_separate_gradients(ctx):
+    """Antialias hands its position gradient to the rasterizer's backward pass when it gets the
+    rast and the very pos tensor of one rasterize call; against a copy of pos (no hand-over,
+    autograd adds the two gradients): plain and fused-loss antialias, two antialias passes over one
+    rast, rast_db and interpolation in the loss or not, and a retained graph differentiated first
+    with respect to the colour only."""
+    sc = scenes.config5_small(views=2)
+    gen = torch.Generator().manual_seed(21)
+    pos0, tri = sc["pos"].cuda(), sc["tri"].cuda()
+    attr = sc["attr"].cuda()
+    color0 = torch.rand(2, 64, 64, 3, generator=gen).cuda()
+    target = sc["target"].cuda()
+    w = torch.randn(2, 64, 64, 3, generator=gen).cuda()
+
+    def run(copy: bool, case: str):
+        pos = pos0.clone().requires_grad_(True)
+        color = color0.clone().requires_grad_(True)
+        rast, rast_db = dr.rasterize(ctx, pos, tri, (64, 64))
+        p_aa = pos.clone() if copy else pos
+        if case == "plain":
+            loss = (dr.antialias(color, rast, p_aa, tri) * w).sum()
+        elif case == "fused":
+            out, _ = dr.interpolate(attr, rast, tri, rast_db=rast_db, diff_attrs="all")
+            _, loss = dr.antialias_mse(color * out[..., 2:5], rast, p_aa, tri, target)
+        elif case == "twice":
+            loss = (dr.antialias(color, rast, p_aa, tri) * w).sum() + \
+                (dr.antialias(color * 2, rast, p_aa, tri, pos_gradient_boost=3.0) ** 2).sum()
+        else:  # retained graph, antialias only (no gradient reaches rast itself)
+            loss = (dr.antialias(color, rast, p_aa, tri) * w).sum()
+            first = torch.autograd.grad(loss, [color], retain_graph=True)[0]
+            return (first, *torch.autograd.grad(loss, [pos, color]))
+        return torch.autograd.grad(loss, [pos, color])
+
+    for case in ("plain", "fused", "twice", "retained"):
+        ours, ref = run(False, case), run(True, case)
+        for x, y in zip(ours, ref):
+            grad_close(x, y, 1e-5)
+        assert ours[-2].abs().sum() > 0
 
 
 def test_config1_pipeline_matches_oracle(ctx):

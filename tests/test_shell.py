@@ -158,6 +158,8 @@ def test_context_device_resolution():
 def clean_aliases():
     names = ("nvdiffrast", "nvdiffrast.torch", "diffrast", "diffrast.torch")
     saved = {n: sys.modules.get(n) for n in names}
+    for n in names:  # another test may have imported the real package under one of these names
+        sys.modules.pop(n, None)
     yield
     for alias in compat._ALIASES.values():
         alias.saved.clear()
