@@ -628,10 +628,11 @@ __global__ void __launch_bounds__(256, 5) aa_bwd_recorded_kernel(const AaCtx a,
                                                               const int4* __restrict__ rec_verts,
                                                               const Upstream u, float boost,
                                                               float* __restrict__ grad_color,
-                                                              float* __restrict__ grad_pos) {
+                                                              float* __restrict__ grad_pos,
+                                                              int row0) {
   const int col = blockIdx.x * blockDim.x + threadIdx.x;
   if (col >= a.width) return;
-  const int row = blockIdx.y;
+  const int row = row0 + static_cast<int>(blockIdx.y);
   const long long b = blockIdx.z;
   const long long p = (b * a.height + row) * a.width + col;
   const long long w = a.width;
@@ -775,23 +776,27 @@ PairRecords pair_records(void* pairs, long long pixels) {
 template <int kMode>
 void launch_recorded(const AaCtx& a, const PairRecords& rec, const Upstream& u, float boost,
                      float* grad_color, float* grad_pos, long long batch, cudaStream_t s) {
-  const dim3 grid((a.width + 255) / 256, a.height, static_cast<unsigned>(batch));
-  switch (a.channels) {
-    case 1:
-      aa_bwd_recorded_kernel<1, kMode><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, u, boost,
-                                                            grad_color, grad_pos);
-      break;
-    case 3:
-      aa_bwd_recorded_kernel<3, kMode><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, u, boost,
-                                                            grad_color, grad_pos);
-      break;
-    case 4:
-      aa_bwd_recorded_kernel<4, kMode><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, u, boost,
-                                                            grad_color, grad_pos);
-      break;
-    default:
-      aa_bwd_recorded_kernel<0, kMode><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, u, boost,
-                                                            grad_color, grad_pos);
+  // Rows in y, launched 65535 at a time for taller images.
+  for (int r0 = 0; r0 < a.height; r0 += 65535) {
+    const dim3 grid((a.width + 255) / 256, static_cast<unsigned>(min(a.height - r0, 65535)),
+                    static_cast<unsigned>(batch));
+    switch (a.channels) {
+      case 1:
+        aa_bwd_recorded_kernel<1, kMode><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, u,
+                                                              boost, grad_color, grad_pos, r0);
+        break;
+      case 3:
+        aa_bwd_recorded_kernel<3, kMode><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, u,
+                                                              boost, grad_color, grad_pos, r0);
+        break;
+      case 4:
+        aa_bwd_recorded_kernel<4, kMode><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, u,
+                                                              boost, grad_color, grad_pos, r0);
+        break;
+      default:
+        aa_bwd_recorded_kernel<0, kMode><<<grid, 256, 0, s>>>(a, rec.t, rec.code, rec.verts, u,
+                                                              boost, grad_color, grad_pos, r0);
+    }
   }
 }
 
@@ -942,7 +947,7 @@ extern "C" int dr_antialias_mse_bwd(const float* color, const float* rast, const
       (num_tri > 0 && grad_pos == nullptr))
     return DR_ERR_INVALID_ARGUMENT;
   if (pair_bytes < pair_record_bytes(total)) return DR_ERR_WORKSPACE_TOO_SMALL;
-  if (batch > 65535 || height > 65535) return DR_ERR_TOO_LARGE;
+  if (batch > 65535) return DR_ERR_TOO_LARGE;
   const AaCtx a = make_ctx(color, rast, pos, pos_batch, num_vert, tri, num_tri, opposite, height,
                            width, channels);
   const PairRecords rec = pair_records(const_cast<void*>(pairs), total);
@@ -979,7 +984,6 @@ extern "C" int dr_antialias_bwd(const float* color, const float* rast, const flo
                            width, channels);
   if (batch > 65535) return DR_ERR_TOO_LARGE;
   if (pairs != nullptr) {
-    if (height > 65535) return DR_ERR_TOO_LARGE;
     launch_recorded<kGradOnly>(a, pair_records(const_cast<void*>(pairs), total),
                            Upstream{grad_out, nullptr, nullptr, 0.0f}, pos_gradient_boost,
                            grad_color, grad_pos, batch, as_stream(stream));

@@ -763,18 +763,19 @@ struct PixelTri {
   float px, py;
 };
 
-// Pixel (view b, row, col) of the resolve kernels' grid: columns in x, rows in y, views in z
-// (from view b0 on).
+// Pixel (view b, row, col) of the resolve kernels' grid: columns in x, rows in y (from row0 on),
+// views in z (from view b0 on). Images with more rows or views than a grid dimension holds
+// (65535) take several launches.
 struct ResolvePixel {
   int b, row, col;
   long long p;
   bool inside;
 };
 
-__device__ __forceinline__ ResolvePixel resolve_pixel(int b0, int height, int width) {
+__device__ __forceinline__ ResolvePixel resolve_pixel(int b0, int row0, int height, int width) {
   ResolvePixel r;
   r.col = blockIdx.x * blockDim.x + threadIdx.x;
-  r.row = blockIdx.y;
+  r.row = row0 + static_cast<int>(blockIdx.y);
   r.b = b0 + static_cast<int>(blockIdx.z);
   r.inside = r.col < width;
   r.p = (static_cast<long long>(r.b) * height + r.row) * width + r.col;
@@ -837,9 +838,9 @@ __global__ void __launch_bounds__(256) poison_keys_kernel(const unsigned long lo
 
 __global__ void __launch_bounds__(kResolveThreads) resolve_fwd_kernel(
     const float* __restrict__ pos, const int* __restrict__ tri, const long long* __restrict__ keys,
-    int b0, long long pos_stride, int height, int width, float4* __restrict__ rast,
+    int b0, int row0, long long pos_stride, int height, int width, float4* __restrict__ rast,
     float4* __restrict__ rast_db) {
-  const int row = blockIdx.y;
+  const int row = row0 + static_cast<int>(blockIdx.y);
   const long long b = b0 + static_cast<long long>(blockIdx.z);
   const long long row_start = (b * height + row) * width;
   const long long base = b * pos_stride;
@@ -913,9 +914,10 @@ __device__ __forceinline__ void cross3(const float u[3], const float v[3], float
 
 __global__ void __launch_bounds__(256) resolve_bwd_kernel(
     const float* __restrict__ pos, const int* __restrict__ tri, const long long* __restrict__ keys,
-    int b0, long long pos_stride, int height, int width, const float4* __restrict__ grad_rast,
-    const float4* __restrict__ grad_db, float* __restrict__ grad_pos) {
-  const ResolvePixel rp = resolve_pixel(b0, height, width);
+    int b0, int row0, long long pos_stride, int height, int width,
+    const float4* __restrict__ grad_rast, const float4* __restrict__ grad_db,
+    float* __restrict__ grad_pos) {
+  const ResolvePixel rp = resolve_pixel(b0, row0, height, width);
   const long long p = rp.p;
   PixelTri q;
   if (rp.inside) {
@@ -1308,15 +1310,16 @@ extern "C" int dr_raster_resolve_fwd(const float* pos, int64_t pos_batch, const 
     return DR_ERR_INVALID_ARGUMENT;
   const long long total = batch * static_cast<long long>(height) * width;
   if (total == 0) return DR_OK;
-  if (height > 65535) return DR_ERR_TOO_LARGE;
-  for (long long b0 = 0; b0 < batch; b0 += 65535) {
-    const dim3 grid((width + kResolveThreads * kResolvePix - 1) / (kResolveThreads * kResolvePix),
-                    height, static_cast<unsigned>(min(batch - b0, 65535LL)));
-    resolve_fwd_kernel<<<grid, kResolveThreads, 0, as_stream(stream)>>>(
-        pos, tri, reinterpret_cast<const long long*>(keys), static_cast<int>(b0),
-        pos_stride(pos_batch, num_vert), height, width, reinterpret_cast<float4*>(rast),
-        reinterpret_cast<float4*>(rast_db));
-  }
+  for (long long b0 = 0; b0 < batch; b0 += 65535)
+    for (int r0 = 0; r0 < height; r0 += 65535) {
+      const dim3 grid((width + kResolveThreads * kResolvePix - 1) / (kResolveThreads * kResolvePix),
+                      static_cast<unsigned>(min(height - r0, 65535)),
+                      static_cast<unsigned>(min(batch - b0, 65535LL)));
+      resolve_fwd_kernel<<<grid, kResolveThreads, 0, as_stream(stream)>>>(
+          pos, tri, reinterpret_cast<const long long*>(keys), static_cast<int>(b0), r0,
+          pos_stride(pos_batch, num_vert), height, width, reinterpret_cast<float4*>(rast),
+          reinterpret_cast<float4*>(rast_db));
+    }
   return launch_status();
 }
 
@@ -1330,13 +1333,15 @@ extern "C" int dr_raster_resolve_bwd(const float* pos, int64_t pos_batch, const 
     return DR_ERR_INVALID_ARGUMENT;
   const long long total = batch * static_cast<long long>(height) * width;
   if (total == 0) return DR_OK;
-  if (height > 65535) return DR_ERR_TOO_LARGE;
-  for (long long b0 = 0; b0 < batch; b0 += 65535) {
-    const dim3 grid((width + 255) / 256, height, static_cast<unsigned>(min(batch - b0, 65535LL)));
-    resolve_bwd_kernel<<<grid, 256, 0, as_stream(stream)>>>(
-        pos, tri, reinterpret_cast<const long long*>(keys), static_cast<int>(b0),
-        pos_stride(pos_batch, num_vert), height, width, reinterpret_cast<const float4*>(grad_rast),
-        reinterpret_cast<const float4*>(grad_db), grad_pos);
-  }
+  for (long long b0 = 0; b0 < batch; b0 += 65535)
+    for (int r0 = 0; r0 < height; r0 += 65535) {
+      const dim3 grid((width + 255) / 256, static_cast<unsigned>(min(height - r0, 65535)),
+                      static_cast<unsigned>(min(batch - b0, 65535LL)));
+      resolve_bwd_kernel<<<grid, 256, 0, as_stream(stream)>>>(
+          pos, tri, reinterpret_cast<const long long*>(keys), static_cast<int>(b0), r0,
+          pos_stride(pos_batch, num_vert), height, width,
+          reinterpret_cast<const float4*>(grad_rast), reinterpret_cast<const float4*>(grad_db),
+          grad_pos);
+    }
   return launch_status();
 }
