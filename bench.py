@@ -342,8 +342,19 @@ def run_ours(args) -> None:
         _, loss = dr.antialias_mse(color, rast, pos, tri, target_in, topology_hash=topo,
                                    scale=1.0 / (args.views * res * res * TEX_CHANNELS))
         loss.backward()
-        reducer.wait()
+        if comm_events is not None:
+            # Exposed communication: how long the compute stream waits for the gradient sums
+            # after its own last backward kernel.
+            before, after = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            before.record()
+            reducer.wait()
+            after.record()
+            comm_events.append((before, after))
+        else:
+            reducer.wait()
         return loss
+
+    comm_events = None
 
     for _ in range(args.warmup):
         step(mvp, target)
@@ -369,9 +380,15 @@ def run_ours(args) -> None:
     # Stage times: CUDA events around every launch of an eagerly launched timed pass (a kernel
     # runs the same whether Python or a graph launches it).
     with ClockSampler(gpu_id(dev)) as clocks:
+        comm_events = [] if world > 1 else None
         with K.record_timings() as stages:
             ms_eager = timed_loop(lambda: step(mvp, target))
         torch.cuda.synchronize()
+    exposed = [b.elapsed_time(a) for b, a in comm_events] if comm_events else []
+    comm_events = None
+    exposed_ms = torch.tensor([sum(exposed) / max(1, len(exposed))], device=dev)
+    if world > 1:
+        dist.all_reduce(exposed_ms, op=dist.ReduceOp.MAX)
     stage_ms = {name: sum(s.elapsed_time(e) for s, e in pairs) / args.steps for name, pairs in stages.items()}
     stage_calls = {name: len(pairs) / args.steps for name, pairs in stages.items()}
 
@@ -562,6 +579,12 @@ def run_ours(args) -> None:
                                              tex_bytes) / (ms / 1e3) / 1e9 / peak, 4),
         },
         "stages_ms": {k: round(v, 3) for k, v in sorted(stage_ms.items(), key=lambda kv: -kv[1])},
+        "comm": {
+            "allreduce_bytes_per_step": (tex.numel() + verts.numel()) * 4 if world > 1 else 0,
+            "exposed_ms_per_step": round(exposed_ms.item(), 3),
+            "how": "eager timing pass: CUDA events on the compute stream before and after the wait "
+                   "for the texture and position gradient all-reduces (max over ranks)",
+        },
         "clocks": clock,
     }
     if world == 1 and not args.no_cpu_baseline:

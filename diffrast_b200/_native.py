@@ -8,13 +8,19 @@ that :func:`check` turns into a ``RuntimeError`` naming the call.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_int64, c_size_t, c_void_p
 from pathlib import Path
 
 import torch
 
-LIBRARY = Path(__file__).resolve().parent / "_lib" / "libdiffrast_b200.so"
+LIBDIR = Path(__file__).resolve().parent / "_lib"
+# DIFFRAST_B200_CHECK=1 loads the checked build: every index read from the data (tri, rast ids,
+# keys, opposite vertices, attribute rows, texel offsets) is bounds-checked on the device, and
+# every call synchronizes and raises on the first recorded fault (slow; for debugging).
+CHECKED = os.environ.get("DIFFRAST_B200_CHECK", "0") not in ("", "0")
+LIBRARY = LIBDIR / ("libdiffrast_b200_checked.so" if CHECKED else "libdiffrast_b200.so")
 
 FILTER_MODES = ("nearest", "linear", "linear-mipmap-nearest", "linear-mipmap-linear")
 BOUNDARY_MODES = ("wrap", "clamp", "zero", "cube")
@@ -111,6 +117,9 @@ _SIGNATURES = {
         [_P, _P, _P, c_int64, c_int64, _P, c_int64, _P, c_int64, c_int32, c_int32, c_int32, _P,
          _P, c_float, _P, c_float, _P, c_size_t, _P, _P, _P],
     ),
+    "dr_checked_build": (c_int, []),
+    "dr_check_faults": (c_int, [POINTER(ctypes.c_uint64)]),
+    "dr_check_site_name": (c_char_p, [c_int]),
     "dr_to_clip_fwd": (c_int, [_P, c_int64, _P, c_int64, _P, _P]),
     "dr_to_clip_bwd": (c_int, [_P, _P, c_int64, _P, c_int64, _P, _P, _P]),
 }
@@ -132,8 +141,9 @@ def lib() -> ctypes.CDLL:
     with _lock:
         if _lib is None:
             if not LIBRARY.exists():
+                how = " --checked" if CHECKED else ""
                 raise ImportError(
-                    f"{LIBRARY} is missing; build it with `python -m diffrast_b200.build` "
+                    f"{LIBRARY} is missing; build it with `python -m diffrast_b200.build{how}` "
                     "(needs nvcc). diffrast_b200 has no CPU fallback."
                 )
             handle = ctypes.CDLL(str(LIBRARY))
@@ -149,6 +159,34 @@ def check(status: int, call: str) -> None:
     if status != 0:
         message = lib().dr_status_string(status).decode()
         raise RuntimeError(f"diffrast_b200: {call} failed with status {status}: {message}")
+    if CHECKED:
+        check_faults(call)
+
+
+class BoundsFault(RuntimeError):
+    """A bounds check of the checked build failed: ``site`` names the kind of index, ``index``
+    its value (the low 48 bits)."""
+
+    def __init__(self, call: str, site: str, index: int) -> None:
+        super().__init__(f"diffrast_b200: {call}: out-of-bounds {site}: {index}")
+        self.site = site
+        self.index = index
+
+
+def check_faults(call: str = "a kernel") -> None:
+    """Raise :class:`BoundsFault` if a checked-build kernel recorded an out-of-bounds index since
+    the last check (synchronizes the device; a no-op for the ordinary build)."""
+    fault = ctypes.c_uint64(0)
+    status = lib().dr_check_faults(ctypes.byref(fault))
+    if status != 0:
+        message = lib().dr_status_string(status).decode()
+        raise RuntimeError(f"diffrast_b200: dr_check_faults failed with status {status}: {message}")
+    if fault.value:
+        site = lib().dr_check_site_name(fault.value >> 48).decode()
+        index = fault.value & 0xFFFFFFFFFFFF
+        if index >= 1 << 47:
+            index -= 1 << 48  # negative indices come back sign-extended
+        raise BoundsFault(call, site, index)
 
 
 def ptr(t: torch.Tensor | None) -> int | None:

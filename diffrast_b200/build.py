@@ -21,6 +21,9 @@ CSRC = PACKAGE / "csrc"
 BUILD = PACKAGE / "_build"
 LIBDIR = PACKAGE / "_lib"
 LIBRARY = LIBDIR / "libdiffrast_b200.so"
+# The checked build (every data-dependent index bounds-checked, faults recorded instead of taken;
+# loaded with DIFFRAST_B200_CHECK=1).
+CHECKED_LIBRARY = LIBDIR / "libdiffrast_b200_checked.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = [
@@ -48,17 +51,21 @@ def _stale(target: Path, deps: list[Path]) -> bool:
     return any(d.stat().st_mtime > t for d in deps)
 
 
-def build(verbose: bool = False, ptxas_verbose: bool = False) -> Path:
-    """Compile and link the library; returns its path."""
-    BUILD.mkdir(exist_ok=True)
+def build(verbose: bool = False, ptxas_verbose: bool = False, checked: bool = False) -> Path:
+    """Compile and link the library (the checked variant with ``checked``); returns its path."""
+    build_dir = BUILD / "checked" if checked else BUILD
+    library = CHECKED_LIBRARY if checked else LIBRARY
+    build_dir.mkdir(parents=True, exist_ok=True)
     LIBDIR.mkdir(exist_ok=True)
     sources = sorted(CSRC.glob("*.cu"))
     headers = sorted(CSRC.glob("*.cuh")) + sorted((ROOT / "include").glob("*.h"))
     compiler = nvcc()
     extra = ["-Xptxas", "-v"] if ptxas_verbose else []
+    if checked:
+        extra.append("-DDR_CHECKED=1")
 
     def compile_one(src: Path) -> tuple[Path, str]:
-        obj = BUILD / (src.stem + ".o")
+        obj = build_dir / (src.stem + ".o")
         if ptxas_verbose or _stale(obj, [src, *headers, Path(__file__)]):
             cmd = [compiler, *ARCH, *FLAGS, *extra, "-c", str(src), "-o", str(obj)]
             res = subprocess.run(cmd, capture_output=True, text=True)
@@ -75,15 +82,15 @@ def build(verbose: bool = False, ptxas_verbose: bool = False) -> Path:
         for _, log in results:
             if log:
                 print(log, file=sys.stderr)
-    if _stale(LIBRARY, objects):
-        tmp = LIBRARY.with_suffix(".so.tmp")
+    if _stale(library, objects):
+        tmp = library.with_suffix(".so.tmp")
         cmd = [compiler, *ARCH, "-shared", "-cudart", "static", *map(str, objects), "-o", str(tmp)]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError(f"linking failed:\n{res.stdout}\n{res.stderr}")
-        os.replace(tmp, LIBRARY)
-    return LIBRARY
+        os.replace(tmp, library)
+    return library
 
 
 if __name__ == "__main__":
-    print(build(verbose=True, ptxas_verbose="-v" in sys.argv))
+    print(build(verbose=True, ptxas_verbose="-v" in sys.argv, checked="--checked" in sys.argv))

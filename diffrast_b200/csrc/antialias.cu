@@ -60,7 +60,8 @@ __device__ __forceinline__ Tri2 load_tri(const AaCtx& a, long long pb, int t) {
   Tri2 v;
   const long long base = pb * a.num_vert;
   for (int k = 0; k < 3; ++k) {
-    v.idx[k] = __ldg(a.tri + 3 * static_cast<long long>(t) + k);
+    v.idx[k] = static_cast<int>(
+        checked_index(__ldg(a.tri + 3 * static_cast<long long>(t) + k), a.num_vert, kSiteVertex));
     const float4 p = __ldg(reinterpret_cast<const float4*>(a.pos) + base + v.idx[k]);
     v.x[k] = p.x;
     v.y[k] = p.y;
@@ -104,7 +105,8 @@ __device__ __forceinline__ bool silhouette_of(const AaCtx& a, long long pb, cons
     l[c] = __fmaf_rn(A[ci], B[cj], -mul(A[cj], B[ci]));
   }
   const float s1 = side_sign(l, make_float4(v.x[k], v.y[k], 0.0f, v.w[k]));
-  const float s2 = side_sign(l, __ldg(reinterpret_cast<const float4*>(a.pos) + pb * a.num_vert + opp));
+  const float s2 = side_sign(l, __ldg(reinterpret_cast<const float4*>(a.pos) + pb * a.num_vert +
+                                      checked_index(opp, a.num_vert, kSiteOpposite)));
   return mul(s1, s2) > 0.0f;
 }
 
@@ -268,7 +270,9 @@ struct PairRecords {
 
 // Vertex (edge + k) % 3 of the pair's owning triangle: k = 1, 2 give the crossed edge's ends.
 __device__ __forceinline__ int edge_vertex(const AaCtx& a, const Pair& r, int k) {
-  return __ldg(a.tri + 3 * static_cast<long long>(r.owner) + (r.edge + k) % 3);
+  return static_cast<int>(checked_index(
+      __ldg(a.tri + 3 * static_cast<long long>(r.owner) + (r.edge + k) % 3), a.num_vert,
+      kSiteVertex));
 }
 
 // Blend coefficients (bp, bq) of a recorded pair, as eval_pair forms them from t.
@@ -322,7 +326,8 @@ __device__ __forceinline__ PairOutcome decide_pair(int id_p, int id_q, float zp,
 }
 
 __device__ __forceinline__ int owner_vertex(const AaCtx& a, int owner, int edge, int k) {
-  return __ldg(a.tri + 3 * static_cast<long long>(owner) + (edge + k) % 3);
+  return static_cast<int>(checked_index(
+      __ldg(a.tri + 3 * static_cast<long long>(owner) + (edge + k) % 3), a.num_vert, kSiteVertex));
 }
 
 // Squared-error loss fused into the antialias passes: the forward pass writes the residual
@@ -398,7 +403,8 @@ __global__ void __launch_bounds__(kFwdX * kFwdY, 3) aa_fwd_kernel(const AaCtx a,
     float4 po[4];
 #pragma unroll
     for (int d = 0; d < 4; ++d)
-      po[d] = opp[d] >= 0 ? __ldg(reinterpret_cast<const float4*>(a.pos) + pb * a.num_vert + opp[d])
+      po[d] = opp[d] >= 0 ? __ldg(reinterpret_cast<const float4*>(a.pos) + pb * a.num_vert +
+                                  checked_index(opp[d], a.num_vert, kSiteOpposite))
                           : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int d = 0; d < 4; ++d)
@@ -492,6 +498,8 @@ __global__ void __launch_bounds__(kFwdX * kFwdY, 3) aa_fwd_kernel(const AaCtx a,
 __device__ __forceinline__ void edge_gradient(const AaCtx& a, float* grad_pos, long long pb, int vi,
                                               int vj, const Pair& r, float grad_t) {
   const long long base = pb * a.num_vert;
+  vi = static_cast<int>(checked_index(vi, a.num_vert, kSiteVertex));
+  vj = static_cast<int>(checked_index(vj, a.num_vert, kSiteVertex));
   const float4 pi = __ldg(reinterpret_cast<const float4*>(a.pos) + base + vi);
   const float4 pj = __ldg(reinterpret_cast<const float4*>(a.pos) + base + vj);
   const float ai_s = pi.x - r.sx * pi.w, aj_s = pj.x - r.sx * pj.w;
@@ -995,3 +1003,4 @@ extern "C" int dr_antialias_bwd(const float* color, const float* rast, const flo
                                                                         grad_color, grad_pos);
   return launch_status();
 }
+DR_DEFINE_FAULT_QUERY(antialias)

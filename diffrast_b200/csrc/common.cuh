@@ -13,7 +13,59 @@
 
 #include "../../include/diffrast_b200.h"
 
+// Checked build (nvcc -DDR_CHECKED=1, loaded with DIFFRAST_B200_CHECK=1): every index that comes
+// from the data (vertex indices read from tri, triangle ids read from rast or the visibility keys,
+// opposite vertices, attribute rows, texel offsets, key offsets) is checked against the size of
+// the buffer it addresses before the access. A failed check does not trap: it records
+// (site << 48) | index in this translation unit's fault word (the first one wins) and the access
+// goes to element 0 instead, so the kernel finishes and the host reports the fault
+// (dr_check_faults). Ordinary builds compile the checks away.
+#ifndef DR_CHECKED
+#define DR_CHECKED 0
+#endif
+
 namespace dr {
+
+// Sites of the checked build's bounds checks (the high 16 bits of a fault record).
+enum CheckSite : int {
+  kSiteTriangle = 1,    // triangle index into tri (from rast, keys or a work list)
+  kSiteVertex = 2,      // vertex index read from tri, into pos or attr rows
+  kSiteOpposite = 3,    // vertex index read from the opposite-vertex table
+  kSiteTexel = 4,       // texel offset into a texture level (or its gradient)
+  kSitePixel = 5,       // pixel offset into the visibility keys
+  kSiteAttrRow = 6,     // attribute row (view * vertices + vertex)
+};
+
+#if DR_CHECKED
+static __device__ unsigned long long g_fault;
+
+__device__ __forceinline__ long long checked_index(long long index, long long bound, int site) {
+  if (index >= 0 && index < bound) return index;
+  atomicCAS(&g_fault, 0ull,
+            (static_cast<unsigned long long>(site) << 48) |
+                (static_cast<unsigned long long>(index) & 0xFFFFFFFFFFFFull));
+  return 0;
+}
+
+// Reads and clears this translation unit's fault word (after the device has finished).
+#define DR_DEFINE_FAULT_QUERY(unit)                                                        \
+  extern "C" int dr_fault_##unit(uint64_t* fault) {                                       \
+    unsigned long long value = 0, zero = 0;                                                \
+    cudaError_t err = cudaMemcpyFromSymbol(&value, ::dr::g_fault, sizeof(value));         \
+    if (err == cudaSuccess) err = cudaMemcpyToSymbol(::dr::g_fault, &zero, sizeof(zero)); \
+    *fault = value;                                                                        \
+    return static_cast<int>(err);                                                          \
+  }
+#else
+__device__ __forceinline__ long long checked_index(long long index, long long, int) {
+  return index;
+}
+#define DR_DEFINE_FAULT_QUERY(unit)                    \
+  extern "C" int dr_fault_##unit(uint64_t* fault) {   \
+    *fault = 0;                                        \
+    return 0;                                          \
+  }
+#endif
 
 // Empty visibility key: no triangle covers the pixel (INT64_MAX, as a signed 64-bit key).
 constexpr long long kEmptyKey = 0x7FFFFFFFFFFFFFFFLL;

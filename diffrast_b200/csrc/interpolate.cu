@@ -37,9 +37,10 @@ __device__ __forceinline__ Corners corners(const int* __restrict__ tri, int t, l
   if (k.covered) {
     const long long view = attr_batch == 1 ? 0 : pixel / pixels_per_image;
     const long long base = view * num_vert;
-    k.row0 = base + __ldg(tri + 3 * static_cast<long long>(t));
-    k.row1 = base + __ldg(tri + 3 * static_cast<long long>(t) + 1);
-    k.row2 = base + __ldg(tri + 3 * static_cast<long long>(t) + 2);
+    const int* vt = tri + 3 * static_cast<long long>(t);
+    k.row0 = base + checked_index(__ldg(vt), num_vert, kSiteVertex);
+    k.row1 = base + checked_index(__ldg(vt + 1), num_vert, kSiteVertex);
+    k.row2 = base + checked_index(__ldg(vt + 2), num_vert, kSiteVertex);
   }
   return k;
 }
@@ -412,3 +413,4 @@ extern "C" int dr_interpolate_bwd_parts(const float* attr, int64_t attr_batch, i
                            diff, num_diff, batch, height, width, gp, grad_attr, grad_rast,
                            grad_db, as_stream(stream));
 }
+DR_DEFINE_FAULT_QUERY(interpolate)

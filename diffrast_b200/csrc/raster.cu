@@ -44,7 +44,21 @@ struct Items {
   const int* range_start;
   const long long* range_first;
   long long pos_stride;  // vertices between the positions of consecutive views
+  long long num_vert;    // vertices of one view's positions (bounds checks only)
 };
+
+// Sizes that bound the indices read from tri and from the keys (checked build only).
+struct Bounds {
+  int num_tri;
+  long long num_vert;
+};
+
+// Vertex index k of triangle t, both checked against their buffers in the checked build.
+__device__ __forceinline__ int tri_vertex(const int* __restrict__ tri, long long t, int k,
+                                          int num_tri, long long num_vert) {
+  t = checked_index(t, num_tri, kSiteTriangle);
+  return static_cast<int>(checked_index(__ldg(tri + 3 * t + k), num_vert, kSiteVertex));
+}
 
 __device__ __forceinline__ void locate(const Items& it, long long g, int& b, int& t) {
   if (it.range_start == nullptr) {
@@ -272,9 +286,9 @@ __global__ void __launch_bounds__(256, 4) setup_kernel(
     float nx[3] = {0.f, 0.f, 0.f}, ny[3] = {0.f, 0.f, 0.f};
     if (g < total) {
       locate(items, g, b, t);
-      const int i0 = __ldg(tri + 3 * static_cast<long long>(t));
-      const int i1 = __ldg(tri + 3 * static_cast<long long>(t) + 1);
-      const int i2 = __ldg(tri + 3 * static_cast<long long>(t) + 2);
+      const int i0 = tri_vertex(tri, t, 0, items.num_tri, items.num_vert);
+      const int i1 = tri_vertex(tri, t, 1, items.num_tri, items.num_vert);
+      const int i2 = tri_vertex(tri, t, 2, items.num_tri, items.num_vert);
       const long long base = static_cast<long long>(b) * items.pos_stride;
       v0 = load_vert(pos, base + i0);
       v1 = load_vert(pos, base + i1);
@@ -477,8 +491,9 @@ __global__ void __launch_bounds__(256, 4) setup_kernel(
                                            __int_as_float(rec.w), __float_as_int(aux.z), aux.x,
                                            aux.y);
         if (key == kEmptyKey) continue;
-        const long long off =
-            (static_cast<long long>(__float_as_int(aux.w)) * height + y) * width + col;
+        const long long off = checked_index(
+            (static_cast<long long>(__float_as_int(aux.w)) * height + y) * width + col,
+            static_cast<long long>(items.items) * height * width, kSitePixel);
         if (prev != nullptr && !(key > __ldg(prev + off))) continue;
         atomicMin(keys + off, key);
       }
@@ -681,7 +696,7 @@ __global__ void __launch_bounds__(1024) scan_kernel(const unsigned* __restrict__
 
 __global__ void __launch_bounds__(256) tile_kernel(
     const float* __restrict__ pos, const int* __restrict__ tri, long long pos_stride,
-    int height, int width, int tiles_x, int tiles_per_image, int num_tiles,
+    const Bounds bd, int height, int width, int tiles_x, int tiles_per_image, int num_tiles,
     const float* __restrict__ centres,
     const long long* __restrict__ prev, long long* __restrict__ keys, const int* __restrict__ pairs,
     const Binned* __restrict__ binned, const unsigned* __restrict__ tile_offset,
@@ -725,9 +740,9 @@ __global__ void __launch_bounds__(256) tile_kernel(
       const int b = rec.b, t = rec.t;
       const long long base = static_cast<long long>(b) * pos_stride;
       const float4* p4 = reinterpret_cast<const float4*>(pos);
-      sv[0][threadIdx.x] = __ldg(p4 + base + __ldg(tri + 3 * static_cast<long long>(t)));
-      sv[1][threadIdx.x] = __ldg(p4 + base + __ldg(tri + 3 * static_cast<long long>(t) + 1));
-      sv[2][threadIdx.x] = __ldg(p4 + base + __ldg(tri + 3 * static_cast<long long>(t) + 2));
+      sv[0][threadIdx.x] = __ldg(p4 + base + tri_vertex(tri, t, 0, bd.num_tri, bd.num_vert));
+      sv[1][threadIdx.x] = __ldg(p4 + base + tri_vertex(tri, t, 1, bd.num_tri, bd.num_vert));
+      sv[2][threadIdx.x] = __ldg(p4 + base + tri_vertex(tri, t, 2, bd.num_tri, bd.num_vert));
       st[threadIdx.x] = t;
       sbox[threadIdx.x] = make_int4(rec.c0, rec.c1, rec.r0, rec.r1);
     }
@@ -785,8 +800,8 @@ __device__ __forceinline__ ResolvePixel resolve_pixel(int b0, int row0, int heig
 __device__ __forceinline__ PixelTri pixel_triangle(const float* __restrict__ pos,
                                                    const int* __restrict__ tri,
                                                    const long long* __restrict__ keys,
-                                                   const ResolvePixel& rp, long long pos_stride, int height,
-                                                   int width) {
+                                                   const ResolvePixel& rp, long long pos_stride,
+                                                   const Bounds& bd, int height, int width) {
   PixelTri r;
   const long long key = keys[rp.p];
   r.covered = key != kEmptyKey;
@@ -796,9 +811,9 @@ __device__ __forceinline__ PixelTri pixel_triangle(const float* __restrict__ pos
   r.py = pixel_centre(row, height);
   r.t = static_cast<int>(key & 0xFFFFFFFFLL);
   if (r.covered) {
-    r.i0 = __ldg(tri + 3 * static_cast<long long>(r.t));
-    r.i1 = __ldg(tri + 3 * static_cast<long long>(r.t) + 1);
-    r.i2 = __ldg(tri + 3 * static_cast<long long>(r.t) + 2);
+    r.i0 = tri_vertex(tri, r.t, 0, bd.num_tri, bd.num_vert);
+    r.i1 = tri_vertex(tri, r.t, 1, bd.num_tri, bd.num_vert);
+    r.i2 = tri_vertex(tri, r.t, 2, bd.num_tri, bd.num_vert);
     const long long base = static_cast<long long>(r.b) * pos_stride;
     r.v0 = load_vert(pos, base + r.i0);
     r.v1 = load_vert(pos, base + r.i1);
@@ -838,8 +853,8 @@ __global__ void __launch_bounds__(256) poison_keys_kernel(const unsigned long lo
 
 __global__ void __launch_bounds__(kResolveThreads) resolve_fwd_kernel(
     const float* __restrict__ pos, const int* __restrict__ tri, const long long* __restrict__ keys,
-    int b0, int row0, long long pos_stride, int height, int width, float4* __restrict__ rast,
-    float4* __restrict__ rast_db) {
+    int b0, int row0, long long pos_stride, const Bounds bd, int height, int width,
+    float4* __restrict__ rast, float4* __restrict__ rast_db) {
   const int row = row0 + static_cast<int>(blockIdx.y);
   const long long b = b0 + static_cast<long long>(blockIdx.z);
   const long long row_start = (b * height + row) * width;
@@ -853,9 +868,10 @@ __global__ void __launch_bounds__(kResolveThreads) resolve_fwd_kernel(
   int idx[kResolvePix][3];
 #pragma unroll
   for (int i = 0; i < kResolvePix; ++i) {
-    const long long t3 = 3 * (key[i] & 0xFFFFFFFFLL);
+    const long long t = key[i] & 0xFFFFFFFFLL;
 #pragma unroll
-    for (int k = 0; k < 3; ++k) idx[i][k] = key[i] != kEmptyKey ? __ldg(tri + t3 + k) : 0;
+    for (int k = 0; k < 3; ++k)
+      idx[i][k] = key[i] != kEmptyKey ? tri_vertex(tri, t, k, bd.num_tri, bd.num_vert) : 0;
   }
   Vert v[kResolvePix][3];
 #pragma unroll
@@ -914,14 +930,14 @@ __device__ __forceinline__ void cross3(const float u[3], const float v[3], float
 
 __global__ void __launch_bounds__(256) resolve_bwd_kernel(
     const float* __restrict__ pos, const int* __restrict__ tri, const long long* __restrict__ keys,
-    int b0, int row0, long long pos_stride, int height, int width,
+    int b0, int row0, long long pos_stride, const Bounds bd, int height, int width,
     const float4* __restrict__ grad_rast, const float4* __restrict__ grad_db,
     float* __restrict__ grad_pos) {
   const ResolvePixel rp = resolve_pixel(b0, row0, height, width);
   const long long p = rp.p;
   PixelTri q;
   if (rp.inside) {
-    q = pixel_triangle(pos, tri, keys, rp, pos_stride, height, width);
+    q = pixel_triangle(pos, tri, keys, rp, pos_stride, bd, height, width);
   } else {
     q.covered = false;
     q.b = 0;
@@ -1128,7 +1144,7 @@ extern "C" int dr_raster_setup(const float* pos, int64_t pos_batch, const int32_
   centres_kernel<<<blocks_for(height + width, 256), 256, 0, s>>>(l.centres, height, width);
   const Items items = {static_cast<int>(num_tri), static_cast<int>(batch), range_start,
                        reinterpret_cast<const long long*>(range_first),
-                       pos_stride(pos_batch, num_vert)};
+                       pos_stride(pos_batch, num_vert), num_vert};
   if (occlusion_workspace != nullptr) {
     const OcclusionLayout ol = occlusion_layout(occlusion_workspace, batch, height, width);
     err = cudaMemsetAsync(ol.count, 0, sizeof(unsigned long long), s);
@@ -1176,7 +1192,7 @@ extern "C" int dr_raster_occluded(const float* pos, int64_t pos_batch, const int
                                  ol.tile_max);
   const Items items = {static_cast<int>(num_tri), static_cast<int>(batch), range_start,
                        reinterpret_cast<const long long*>(range_first),
-                       pos_stride(pos_batch, num_vert)};
+                       pos_stride(pos_batch, num_vert), num_vert};
   // Nothing is binned here (every record is a small triangle), so the list is not touched.
   const unsigned grid = static_cast<unsigned>(
       min(static_cast<long long>(blocks_for(total, 256)),
@@ -1214,7 +1230,8 @@ namespace {
 // Stage 2 with either host counts (dc.count_on_device null: num_binned and num_pairs exact) or the
 // setup counters read on the device (num_binned and num_pairs are then capacities).
 int launch_tiles(const float* pos, int64_t pos_batch, const int32_t* tri, int64_t batch,
-                 int64_t num_vert, int32_t height, int32_t width, const int64_t* prev_keys,
+                 int64_t num_vert, int64_t num_tri, int32_t height, int32_t width,
+                 const int64_t* prev_keys,
                  int64_t* keys, const void* setup_workspace, int64_t num_binned,
                  int64_t num_pairs, void* bin_workspace, size_t bin_workspace_bytes,
                  const DeviceCounts& dc, cudaStream_t s) {
@@ -1242,7 +1259,8 @@ int launch_tiles(const float* pos, int64_t pos_batch, const int32_t* tri, int64_
                                       bl.item_offset);
   bin_kernel<true><<<bin_blocks, 256, 0, s>>>(sl.binned, num_binned, tiles_x, tiles_per_image,
                                               bl.tile_cursor, bl.tile_offset, bl.pairs, dc, nt);
-  tile_kernel<<<148 * 8, 256, 0, s>>>(pos, tri, pos_stride(pos_batch, num_vert), height, width,
+  tile_kernel<<<148 * 8, 256, 0, s>>>(pos, tri, pos_stride(pos_batch, num_vert),
+                                      Bounds{static_cast<int>(num_tri), num_vert}, height, width,
                                       tiles_x, tiles_per_image, nt, sl.centres,
                                       reinterpret_cast<const long long*>(prev_keys),
                                       reinterpret_cast<long long*>(keys), bl.pairs, sl.binned,
@@ -1263,7 +1281,7 @@ extern "C" int dr_raster_tiles(const float* pos, int64_t pos_batch, const int32_
     return DR_ERR_INVALID_ARGUMENT;
   if (num_pairs >= (1LL << 31)) return DR_ERR_TOO_LARGE;
   if (num_binned == 0 || num_pairs == 0) return DR_OK;
-  return launch_tiles(pos, pos_batch, tri, batch, num_vert, height, width, prev_keys, keys,
+  return launch_tiles(pos, pos_batch, tri, batch, num_vert, num_tri, height, width, prev_keys, keys,
                       setup_workspace, num_binned, num_pairs, bin_workspace, bin_workspace_bytes,
                       DeviceCounts{nullptr, 0, 0, nullptr}, as_stream(stream));
 }
@@ -1284,7 +1302,7 @@ extern "C" int dr_raster_tiles_device(const float* pos, int64_t pos_batch, const
   SetupLayout sl = setup_layout(setup_workspace, height, width);
   const DeviceCounts dc{sl.counters, binned_capacity, pair_capacity,
                         reinterpret_cast<unsigned long long*>(overflow)};
-  return launch_tiles(pos, pos_batch, tri, batch, num_vert, height, width, prev_keys, keys,
+  return launch_tiles(pos, pos_batch, tri, batch, num_vert, num_tri, height, width, prev_keys, keys,
                       setup_workspace, binned_capacity > 0 ? binned_capacity : 1, pair_capacity,
                       bin_workspace, bin_workspace_bytes, dc, as_stream(stream));
 }
@@ -1317,8 +1335,8 @@ extern "C" int dr_raster_resolve_fwd(const float* pos, int64_t pos_batch, const 
                       static_cast<unsigned>(min(batch - b0, 65535LL)));
       resolve_fwd_kernel<<<grid, kResolveThreads, 0, as_stream(stream)>>>(
           pos, tri, reinterpret_cast<const long long*>(keys), static_cast<int>(b0), r0,
-          pos_stride(pos_batch, num_vert), height, width, reinterpret_cast<float4*>(rast),
-          reinterpret_cast<float4*>(rast_db));
+          pos_stride(pos_batch, num_vert), Bounds{static_cast<int>(num_tri), num_vert}, height,
+          width, reinterpret_cast<float4*>(rast), reinterpret_cast<float4*>(rast_db));
     }
   return launch_status();
 }
@@ -1339,9 +1357,10 @@ extern "C" int dr_raster_resolve_bwd(const float* pos, int64_t pos_batch, const 
                       static_cast<unsigned>(min(batch - b0, 65535LL)));
       resolve_bwd_kernel<<<grid, 256, 0, as_stream(stream)>>>(
           pos, tri, reinterpret_cast<const long long*>(keys), static_cast<int>(b0), r0,
-          pos_stride(pos_batch, num_vert), height, width,
-          reinterpret_cast<const float4*>(grad_rast), reinterpret_cast<const float4*>(grad_db),
-          grad_pos);
+          pos_stride(pos_batch, num_vert), Bounds{static_cast<int>(num_tri), num_vert}, height,
+          width, reinterpret_cast<const float4*>(grad_rast),
+          reinterpret_cast<const float4*>(grad_db), grad_pos);
     }
   return launch_status();
 }
+DR_DEFINE_FAULT_QUERY(raster)

@@ -28,6 +28,7 @@ struct Levels {
   const float* ptr[DR_MAX_LEVELS];
   float* grad[DR_MAX_LEVELS];
   long long bstride[DR_MAX_LEVELS];  // batch stride in texels (0 when shared by all views)
+  long long texels[DR_MAX_LEVELS];   // texels of the whole level buffer (bounds checks only)
   int h[DR_MAX_LEVELS];
   int w[DR_MAX_LEVELS];
   int num_levels;
@@ -247,7 +248,7 @@ __device__ __forceinline__ long long texel_offset(const Levels& L, int l, long l
   }
   long long texel = static_cast<long long>(row) * w + col;
   if (B == DR_BOUNDARY_CUBE) texel += static_cast<long long>(face) * h * w;
-  return view * L.bstride[l] + texel;
+  return checked_index(view * L.bstride[l] + texel, L.texels[l], kSiteTexel);
 }
 
 struct Footprint {
@@ -315,10 +316,10 @@ __device__ __forceinline__ Footprint bilinear_footprint(const Levels& L, int l, 
     const long long base = view * L.bstride[l];
     const long long row0 = base + static_cast<long long>(r0) * w;
     const long long row1 = base + static_cast<long long>(r1) * w;
-    f.off[0] = row0 + c0;
-    f.off[1] = row0 + c1;
-    f.off[2] = row1 + c0;
-    f.off[3] = row1 + c1;
+    f.off[0] = checked_index(row0 + c0, L.texels[l], kSiteTexel);
+    f.off[1] = checked_index(row0 + c1, L.texels[l], kSiteTexel);
+    f.off[2] = checked_index(row1 + c0, L.texels[l], kSiteTexel);
+    f.off[3] = checked_index(row1 + c1, L.texels[l], kSiteTexel);
     f.ok[0] = okr0 && okc0;
     f.ok[1] = okr0 && okc1;
     f.ok[2] = okr1 && okc0;
@@ -466,7 +467,9 @@ __device__ __forceinline__ void prepare(const Levels& L, int channels, const flo
       const int row = min(max(static_cast<int>(floorf(y)), 0), h - 1);
       const int col = min(max(static_cast<int>(floorf(x)), 0), w - 1);
       k.near_ok = true;
-      k.near_off = view * L.bstride[0] + (static_cast<long long>(k.face) * h + row) * w + col;
+      k.near_off = checked_index(
+          view * L.bstride[0] + (static_cast<long long>(k.face) * h + row) * w + col, L.texels[0],
+          kSiteTexel);
     } else {
       k.near_off = texel_offset<B>(L, 0, view, 0, static_cast<int>(floorf(y)),
                                    static_cast<int>(floorf(x)), channels, k.near_ok);
@@ -1078,7 +1081,8 @@ void dispatch(int mode, int boundary, F&& f) {
 
 int make_levels(const float* const* level_ptr, float* const* grad_ptr, const int32_t* level_h,
                 const int32_t* level_w, const int64_t* level_batch_stride, int32_t num_levels,
-                int32_t channels, int32_t filter_mode, int32_t boundary_mode, Levels& L) {
+                int32_t channels, int32_t filter_mode, int32_t boundary_mode, int64_t batch,
+                Levels& L) {
   if (channels < 1) return DR_ERR_INVALID_ARGUMENT;
   if (num_levels < 1 || num_levels > DR_MAX_LEVELS || level_ptr == nullptr || level_h == nullptr ||
       level_w == nullptr || level_batch_stride == nullptr)
@@ -1093,6 +1097,10 @@ int make_levels(const float* const* level_ptr, float* const* grad_ptr, const int
     L.h[l] = used ? level_h[l] : 1;
     L.w[l] = used ? level_w[l] : 1;
     L.bstride[l] = used ? level_batch_stride[l] / channels : 0;
+    // A level is shared by all views (stride 0) or holds one image per view.
+    const long long image = static_cast<long long>(L.h[l]) * L.w[l] *
+                            (boundary_mode == DR_BOUNDARY_CUBE ? 6 : 1);
+    L.texels[l] = L.bstride[l] > 0 ? L.bstride[l] * (batch > 0 ? batch : 1) : image;
     if (used && (L.ptr[l] == nullptr || L.h[l] < 1 || L.w[l] < 1 || L.bstride[l] < 0))
       return DR_ERR_INVALID_ARGUMENT;
     if (used && grad_ptr != nullptr && L.grad[l] == nullptr) return DR_ERR_INVALID_ARGUMENT;
@@ -1115,7 +1123,7 @@ extern "C" int dr_texture_fwd(const float* const* level_ptr, const int32_t* leve
                               int32_t boundary_mode, float* out, void* stream) {
   Levels L;
   int status = make_levels(level_ptr, nullptr, level_h, level_w, level_batch_stride, num_levels,
-                           channels, filter_mode, boundary_mode, L);
+                           channels, filter_mode, boundary_mode, batch, L);
   if (status != DR_OK) return status;
   if (channels < 1 || batch < 0 || height < 0 || width < 0) return DR_ERR_INVALID_ARGUMENT;
   const long long total = batch * static_cast<long long>(height) * width;
@@ -1147,7 +1155,7 @@ extern "C" int dr_texture_bwd(const float* const* level_ptr, float* const* grad_
   if (grad_level_ptr == nullptr) return DR_ERR_INVALID_ARGUMENT;
   Levels L;
   int status = make_levels(level_ptr, grad_level_ptr, level_h, level_w, level_batch_stride,
-                           num_levels, channels, filter_mode, boundary_mode, L);
+                           num_levels, channels, filter_mode, boundary_mode, batch, L);
   if (status != DR_OK) return status;
   if (channels < 1 || batch < 0 || height < 0 || width < 0) return DR_ERR_INVALID_ARGUMENT;
   const long long total = batch * static_cast<long long>(height) * width;
@@ -1218,3 +1226,4 @@ extern "C" int dr_mip_downsample_bwd(const float* grad_dst, int64_t images, int3
       grad_dst, h, w, channels, grad_src, aligned16, out, out_channels);
   return launch_status();
 }
+DR_DEFINE_FAULT_QUERY(texture)

@@ -151,3 +151,4 @@ extern "C" int dr_to_clip_bwd(const float* grad_out, const float* positions, int
   }
   return launch_status();
 }
+DR_DEFINE_FAULT_QUERY(transform)

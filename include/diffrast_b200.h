@@ -48,6 +48,19 @@ extern "C" {
 int dr_version(void);
 const char* dr_status_string(int status);
 
+/* Bounds-checked build (libdiffrast_b200_checked.so, compiled with -DDR_CHECKED=1; no
+ * counterpart in the reference, which has no debug build). Every index its kernels read from the
+ * data (vertex indices in tri, triangle ids in rast and the visibility keys, opposite vertices,
+ * attribute rows, texel offsets, key offsets) is checked against the buffer it addresses. A failed
+ * check records (site << 48) | (index & 0xFFFFFFFFFFFF) in a device word (the first one wins)
+ * and the access goes to element 0 instead, so no kernel faults. dr_checked_build() is 1 for that
+ * library, 0 for the ordinary one; dr_check_faults() synchronizes the device, returns the first
+ * record since the last call in *fault (0: none, always 0 in the ordinary build) and clears it;
+ * dr_check_site_name() names a record's site (*fault >> 48). */
+int dr_checked_build(void);
+int dr_check_faults(uint64_t* fault);
+const char* dr_check_site_name(int site);
+
 /* ---------------------------------------------------------------------------------------------
  * Rasterize: visibility (three stages) and resolve.
  * Replaces the visibility pass of backends/triton.py:21-40 (rasterize_layer) and

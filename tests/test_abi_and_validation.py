@@ -195,7 +195,8 @@ def test_binding_matches_the_header_argument_by_argument():
         assert len(params) == len(argtypes), name
         for param, ctype in zip(params, argtypes, strict=True):
             if "*" in param:
-                expected = {ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64)}
+                expected = {ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64),
+                            ctypes.POINTER(ctypes.c_uint64)}
             elif param.startswith(("int64_t", "size_t")):
                 expected = {ctypes.c_int64, ctypes.c_size_t}
             elif param.startswith(("int32_t", "int ")):
