@@ -6,6 +6,10 @@
 // float32 arithmetic of diffrast's reference backend (src/diffrast/backends/reference.py:293-365,
 // :675-765), so triangle ids and the antialias edge set agree bit for bit. Everything else (the
 // barycentric resolve, interpolation, texturing, gradients) uses ordinary float arithmetic.
+//
+// Cache policy: per-pixel streams that a kernel reads or writes once (rast, rast_db, keys, uv,
+// uv_da, upstream gradients, outputs) use the evict-first hints (__ldcs / __stcs), so that they do
+// not push the data the kernels gather many times (vertices, attribute rows, texels) out of L2.
 #pragma once
 
 #include <cstdint>

@@ -87,10 +87,10 @@ __device__ __forceinline__ void store_block(float* __restrict__ dst, const float
   if (aligned) {
     const int vec = count / 4;
     for (int i = threadIdx.x; i < vec; i += blockDim.x)
-      reinterpret_cast<float4*>(dst)[i] = reinterpret_cast<const float4*>(src)[i];
-    for (int i = vec * 4 + threadIdx.x; i < count; i += blockDim.x) dst[i] = src[i];
+      __stcs(reinterpret_cast<float4*>(dst) + i, reinterpret_cast<const float4*>(src)[i]);
+    for (int i = vec * 4 + threadIdx.x; i < count; i += blockDim.x) __stcs(dst + i, src[i]);
   } else {
-    for (int i = threadIdx.x; i < count; i += blockDim.x) dst[i] = src[i];
+    for (int i = threadIdx.x; i < count; i += blockDim.x) __stcs(dst + i, src[i]);
   }
 }
 
@@ -119,8 +119,8 @@ __global__ void __launch_bounds__(kInterpThreads) interp_fwd_kernel(
 #pragma unroll
   for (int i = 0; i < kInterpPix; ++i) {
     const long long p = first + i * kInterpThreads + threadIdx.x;
-    r[i] = p < total ? rast[p] : make_float4(0.f, 0.f, 0.f, 0.f);
-    d[i] = p < total && num_diff > 0 ? rast_db[p] : make_float4(0.f, 0.f, 0.f, 0.f);
+    r[i] = p < total ? __ldcs(rast + p) : make_float4(0.f, 0.f, 0.f, 0.f);
+    d[i] = p < total && num_diff > 0 ? __ldcs(rast_db + p) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   Corners k[kInterpPix];
 #pragma unroll
@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(256, 6) interp_bwd_kernel(
     float4* __restrict__ grad_rast, float4* __restrict__ grad_db) {
   const long long p = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   const bool in_range = p < total;
-  const float4 r = in_range ? rast[p] : make_float4(0.f, 0.f, 0.f, 0.f);
+  const float4 r = in_range ? __ldcs(rast + p) : make_float4(0.f, 0.f, 0.f, 0.f);
   const int t = in_range ? rast_triangle(r.w, num_tri) : -1;
   const Corners k = corners(tri, t, p, pixels_per_image, attr_batch, num_vert);
   const float u = r.x, v = r.y, w2 = 1.0f - u - v;
@@ -262,14 +262,14 @@ __global__ void __launch_bounds__(256, 6) interp_bwd_kernel(
       scatter_attr(grad_attr, k.row2, peers[2], k.covered, channels, c, g * w2);
     }
   }
-  if (in_range) grad_rast[p] = make_float4(gu, gv, 0.0f, 0.0f);
+  if (in_range) __stcs(grad_rast + p, make_float4(gu, gv, 0.0f, 0.0f));
 
   if (gp.out_da == nullptr && gp.part_da == nullptr) return;
   // Differentiated channel pairs (2 j, 2 j + 1) that can carry a gradient.
   const int j_lo = gp.out_da != nullptr ? 0 : max(0, gp.da_first) / 2;
   const int j_hi = gp.out_da != nullptr ? num_diff
                                         : min(num_diff, (gp.da_first + gp.da_count + 1) / 2);
-  const float4 d = k.covered ? rast_db[p] : make_float4(0.f, 0.f, 0.f, 0.f);
+  const float4 d = k.covered ? __ldcs(rast_db + p) : make_float4(0.f, 0.f, 0.f, 0.f);
   float g_dudx = 0.0f, g_dudy = 0.0f, g_dvdx = 0.0f, g_dvdy = 0.0f;
   for (int j = j_lo; j < j_hi; ++j) {
     float gx = 0.0f, gy = 0.0f, du = 0.0f, dv = 0.0f;
@@ -300,7 +300,7 @@ __global__ void __launch_bounds__(256, 6) interp_bwd_kernel(
       scatter_attr(grad_attr, k.row2, peers[2], k.covered, channels, c, -(g0 + g1));
     }
   }
-  if (in_range) grad_db[p] = make_float4(g_dudx, g_dudy, g_dvdx, g_dvdy);
+  if (in_range) __stcs(grad_db + p, make_float4(g_dudx, g_dudy, g_dvdx, g_dvdy));
 }
 
 bool bad_interp_args(const float* attr, int64_t attr_batch, int64_t num_vert, int32_t channels,

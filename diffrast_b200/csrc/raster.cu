@@ -863,7 +863,7 @@ __global__ void __launch_bounds__(kResolveThreads) resolve_fwd_kernel(
 #pragma unroll
   for (int i = 0; i < kResolvePix; ++i) {
     const int col = blockIdx.x * (kResolveThreads * kResolvePix) + i * kResolveThreads + threadIdx.x;
-    key[i] = col < width ? keys[row_start + col] : kEmptyKey;
+    key[i] = col < width ? __ldcs(keys + row_start + col) : kEmptyKey;
   }
   int idx[kResolvePix][3];
 #pragma unroll
@@ -905,7 +905,7 @@ __global__ void __launch_bounds__(kResolveThreads) resolve_fwd_kernel(
     const float u = e0 / s, vv = e1 / s;
     const float ew = e0 * v0.w + e1 * v1.w + e2 * v2.w;
     const float depth = (e0 * v0.z + e1 * v1.z + e2 * v2.z) / ew;
-    rast[p] = make_float4(u, vv, depth, static_cast<float>((key[i] & 0xFFFFFFFFLL) + 1));
+    __stcs(rast + p, make_float4(u, vv, depth, static_cast<float>((key[i] & 0xFFFFFFFFLL) + 1)));
     if (rast_db != nullptr) {
       // de/dpx = c x w and de/dpy = w x a (reference.py:281-290).
       const float dx0 = c1 * v2.w - c2 * v1.w, dx1 = c2 * v0.w - c0 * v2.w;
@@ -916,8 +916,8 @@ __global__ void __launch_bounds__(kResolveThreads) resolve_fwd_kernel(
       const float inv_s = 1.0f / s;
       const float scale_x = 2.0f / static_cast<float>(width) * inv_s;
       const float scale_y = 2.0f / static_cast<float>(height) * inv_s;
-      rast_db[p] = make_float4((dx0 - u * sx) * scale_x, (dy0 - u * sy) * scale_y,
-                               (dx1 - vv * sx) * scale_x, (dy1 - vv * sy) * scale_y);
+      __stcs(rast_db + p, make_float4((dx0 - u * sx) * scale_x, (dy0 - u * sy) * scale_y,
+                                      (dx1 - vv * sx) * scale_x, (dy1 - vv * sy) * scale_y));
     }
   }
 }

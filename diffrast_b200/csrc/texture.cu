@@ -429,9 +429,9 @@ __device__ __forceinline__ void prepare(const Levels& L, int channels, const flo
     k.v = k.cube.t;
     for (int i = 0; i < 4; ++i) k.da[i] = k.has_da ? k.cube.st_da[i] : 0.0f;
   } else {
-    k.u = uv[p * st.uv];
-    k.v = uv[p * st.uv + 1];
-    for (int i = 0; i < 4; ++i) k.da[i] = k.has_da ? uv_da[p * st.uv_da + i] : 0.0f;
+    k.u = __ldcs(uv + p * st.uv);
+    k.v = __ldcs(uv + p * st.uv + 1);
+    for (int i = 0; i < 4; ++i) k.da[i] = k.has_da ? __ldcs(uv_da + p * st.uv_da + i) : 0.0f;
   }
   k.bad = false;
   k.lo = k.hi = 0;
@@ -443,7 +443,7 @@ __device__ __forceinline__ void prepare(const Levels& L, int channels, const flo
       float lx, ly;
       lod = add(lod, level_of_detail(k.da, L.h[0], L.w[0], lx, ly));
     }
-    if (bias != nullptr) lod = add(lod, bias[p]);
+    if (bias != nullptr) lod = add(lod, __ldcs(bias + p));
     k.bad = lod != lod;
     if (k.bad) lod = 0.0f;
     k.lod_raw = lod;
@@ -537,7 +537,7 @@ __global__ void __launch_bounds__(256) texture_fwd_kernel(
       }
       if (k.bad) value = kNaN;
       if (!k.valid) value = 0.0f;
-      o[c] = value;
+      if (staged) o[c] = value; else __stcs(o + c, value);
     }
   }
   if (!staged) return;
@@ -682,7 +682,7 @@ __device__ __forceinline__ void texture_bwd_tile(
       float g[4];
       bool any_g = false;
       for (int cc = 0; cc < 4; ++cc) {
-        g[cc] = live && cc < group ? grad_out[p * channels + c0 + cc] : 0.0f;
+        g[cc] = live && cc < group ? __ldcs(grad_out + p * channels + c0 + cc) : 0.0f;
         any_g |= g[cc] != 0.0f;
       }
 #pragma unroll
@@ -757,7 +757,7 @@ __device__ __forceinline__ void texture_bwd_tile(
     float g[4];
     bool any_g = false;
     for (int cc = 0; cc < 4; ++cc) {
-      g[cc] = live && cc < group ? grad_out[p * channels + c0 + cc] : 0.0f;
+      g[cc] = live && cc < group ? __ldcs(grad_out + p * channels + c0 + cc) : 0.0f;
       any_g |= g[cc] != 0.0f;
     }
     for (int t = 0; t < 8; ++t) {
