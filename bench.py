@@ -305,9 +305,9 @@ def run_ours(args) -> None:
     work = torch.cuda.Stream(dev)
     torch.cuda.set_stream(work)
     if world > 1:
-        from datetime import timedelta
+        from diffrast_b200.distributed import init_process_group
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+        init_process_group(dev, timeout_s=300)
     if args.views % world:
         raise SystemExit(f"--views {args.views} must be divisible by the number of GPUs {world}")
 

@@ -14,6 +14,21 @@ import torch.distributed as dist
 from torch import Tensor
 
 
+def init_process_group(device: torch.device, timeout_s: float = 300.0) -> None:
+    """Join the job's process group (NCCL, rank and size from the environment) for view
+    parallelism on ``device``.
+
+    The NCCL collectives get a high-priority stream: the gradient all-reduces issued during the
+    backward pass then take SMs as the running backward kernels' blocks finish, instead of waiting
+    behind every block those kernels still have queued, so the transfer overlaps them.
+    """
+    from datetime import timedelta
+
+    options = dist.ProcessGroupNCCL.Options(is_high_priority_stream=True)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=timeout_s), device_id=device,
+                            pg_options=options)
+
+
 def view_shard(num_views: int, rank: int, world_size: int) -> slice:
     """Views of ``rank``: contiguous, sizes differing by at most one, covering all ``num_views``."""
     if world_size < 1 or not 0 <= rank < world_size:
