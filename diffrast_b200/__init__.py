@@ -2,8 +2,8 @@
 
 The public names are those of ``diffrast`` (``src/diffrast/__init__.py:21-41``): switching is
 changing the import (``import diffrast_b200 as dr``, or ``diffrast_b200.torch``). ``to_clip`` (the
-world-to-clip transform of diffrast's examples) and ``antialias_mse`` (antialias with a fused
-squared-error loss) are additions.
+world-to-clip transform of diffrast's examples), ``antialias_mse`` (antialias with a fused
+squared-error loss) and ``lambert`` (shading from interpolated normals) are additions.
 """
 
 from diffrast_b200.backends import get_backend_name, set_backend
@@ -21,6 +21,7 @@ from diffrast_b200.ops import (
     antialias_construct_topology_hash,
     antialias_mse,
     interpolate,
+    lambert,
     rasterize,
     texture,
     texture_construct_mip,
@@ -47,6 +48,7 @@ __all__ = [
     "install_as_diffrast",
     "install_as_nvdiffrast",
     "interpolate",
+    "lambert",
     "rasterize",
     "set_backend",
     "set_log_level",

@@ -454,6 +454,26 @@ class AntialiasMSE(torch.autograd.Function):
         return grad_color, None, grad_pos, None, None, None, None, None, None, None
 
 
+class Lambert(torch.autograd.Function):
+    """Lambert shading of ``color`` by the unit normal and light; the light is a constant."""
+
+    @staticmethod
+    def forward(ctx, color: Tensor, normal: Tensor, light: Tensor, ambient: float):
+        out = K.lambert_fwd(color, normal, light, ambient)
+        ctx.save_for_backward(*(_saveable(t) for t in (color, normal, light)))
+        ctx.ambient = ambient
+        return out
+
+    @staticmethod
+    @first_order("lambert")
+    def backward(ctx, grad_out):
+        color, normal, light = ctx.saved_tensors
+        need = ctx.needs_input_grad
+        grad_color, grad_normal = K.lambert_bwd(color, normal, light, ctx.ambient,
+                                                grad_out.contiguous(), need[0], need[1])
+        return grad_color, grad_normal, None, None
+
+
 class ToClip(torch.autograd.Function):
     """World-to-clip transform of shared positions by per-view matrices."""
 

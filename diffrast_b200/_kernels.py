@@ -539,6 +539,40 @@ def antialias_bwd(color, rast, pos3, tri, opposite, grad_out, boost, pairs=None)
     return grad_color, grad_pos
 
 
+@timed("lambert_fwd")
+def lambert_fwd(color: Tensor, normal: Tensor, light: Tensor, ambient: float) -> Tensor:
+    """``color * (ambient + max(0, n . l))``; ``normal`` ``[batch, h, w, 3]`` with any uniform
+    pixel stride (a channel slice of interpolate's output is read in place)."""
+    batch, height, width, channels = color.shape
+    normal, stride = pixel_rows(normal)
+    out = torch.empty_like(color)
+    N.check(
+        N.lib().dr_lambert_fwd(color.data_ptr(), normal.data_ptr(), stride, light.data_ptr(),
+                               light.shape[0], float(ambient), batch, height, width, channels,
+                               out.data_ptr(), N.stream(color.device)),
+        "dr_lambert_fwd",
+    )  # fmt: skip
+    return out
+
+
+@timed("lambert_bwd")
+def lambert_bwd(color, normal, light, ambient, grad_out, need_color: bool, need_normal: bool):
+    """Gradients of color and normal (contiguous ``[batch, h, w, 3]``), None where not needed."""
+    batch, height, width, channels = color.shape
+    normal, stride = pixel_rows(normal)
+    grad_color = torch.empty_like(color) if need_color else None
+    grad_normal = (torch.empty((batch, height, width, 3), dtype=torch.float32, device=color.device)
+                   if need_normal else None)
+    N.check(
+        N.lib().dr_lambert_bwd(color.data_ptr(), normal.data_ptr(), stride, light.data_ptr(),
+                               light.shape[0], float(ambient), batch, height, width, channels,
+                               grad_out.data_ptr(), N.ptr(grad_color), N.ptr(grad_normal),
+                               N.stream(color.device)),
+        "dr_lambert_bwd",
+    )  # fmt: skip
+    return grad_color, grad_normal
+
+
 @timed("to_clip_fwd")
 def to_clip_fwd(positions: Tensor, matrix: Tensor) -> Tensor:
     """``[batch, V, 4]`` clip positions of ``positions`` ``[V, 3]`` under ``matrix``

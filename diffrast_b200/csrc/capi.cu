@@ -30,6 +30,7 @@ extern "C" int dr_fault_interpolate(uint64_t* fault);
 extern "C" int dr_fault_texture(uint64_t* fault);
 extern "C" int dr_fault_antialias(uint64_t* fault);
 extern "C" int dr_fault_transform(uint64_t* fault);
+extern "C" int dr_fault_shading(uint64_t* fault);
 
 extern "C" int dr_checked_build(void) { return DR_CHECKED; }
 
@@ -40,7 +41,8 @@ extern "C" int dr_check_faults(uint64_t* fault) {
   cudaError_t err = cudaDeviceSynchronize();
   if (err != cudaSuccess) return static_cast<int>(err);
   int (*const units[])(uint64_t*) = {dr_fault_raster, dr_fault_interpolate, dr_fault_texture,
-                                     dr_fault_antialias, dr_fault_transform};
+                                     dr_fault_antialias, dr_fault_transform,
+                                     dr_fault_shading};
   for (auto query : units) {
     uint64_t value = 0;
     const int status = query(&value);

@@ -587,6 +587,45 @@ def antialias_construct_topology_hash(tri: Tensor) -> TopologyHash:
 # ---------------------------------------------------------------------------------------------
 
 
+def lambert(color: Tensor, normal: Tensor, light_dir: Tensor, ambient: float = 0.0) -> Tensor:
+    """Shade ``color`` by the interpolated ``normal`` under a directional light, in one pass.
+
+    Returns ``color * (ambient + max(0, n . l))`` with ``n`` the unit normal of each pixel and
+    ``l`` the unit light direction: ``color`` is ``[batch, height, width, channels]``, ``normal``
+    ``[batch, height, width, 3]`` (a channel slice of :func:`interpolate`'s output such as
+    ``out[..., 2:5]`` is read in place), ``light_dir`` ``[3]`` or ``[batch, 3]`` (normalised here).
+    A zero normal (background) gets the ambient term alone. Differentiable in ``color`` and
+    ``normal``; the light is a constant. Not part of diffrast's API: the shading that its examples
+    write with torch elementwise ops, fused forward and backward.
+    """
+    _check(color, "color", ndim=4, dtype=torch.float32)
+    _check(normal, "normal", ndim=4, last=3, dtype=torch.float32,
+           layout="[batch, height, width, 3]")
+    if normal.shape[:3] != color.shape[:3]:
+        raise ValueError(
+            f"normal must match color in batch, height and width, got {tuple(normal.shape)} and "
+            f"{tuple(color.shape)}."
+        )
+    if not isinstance(light_dir, Tensor) or light_dir.dtype != torch.float32:
+        raise TypeError("light_dir must be a torch.float32 tensor of shape [3] or [batch, 3].")
+    light = light_dir.reshape(1, 3) if light_dir.ndim == 1 else light_dir
+    if light.ndim != 2 or light.shape[1] != 3 or light.shape[0] not in (1, color.shape[0]):
+        raise ValueError(
+            f"light_dir must have shape [3] or [batch, 3], got {tuple(light_dir.shape)}."
+        )
+    if not isinstance(ambient, SupportsFloat):
+        raise TypeError(f"ambient must be a number, got {ambient!r}.")
+    if color.shape[0] > 65535:
+        raise ValueError(f"lambert takes at most 65535 views, got {color.shape[0]}.")
+    _check_devices(color=color, normal=normal, light_dir=light_dir)
+    require_cuda(color.device)
+    if color.numel() == 0:
+        return color.clone()
+    with torch.cuda.device(color.device):
+        return F.Lambert.apply(color.contiguous(), normal, light.detach().contiguous(),
+                               float(ambient))
+
+
 def to_clip(positions: Tensor, matrix: Tensor) -> Tensor:
     """Transform ``[vertices, 3]`` positions by ``[batch, 4, 4]`` matrices to clip space.
 

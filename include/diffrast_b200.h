@@ -371,6 +371,24 @@ int dr_to_clip_bwd(const float* grad_clip, const float* positions, int64_t num_v
                    const float* matrices, int64_t batch, float* grad_positions,
                    float* grad_matrices, void* stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * Lambert shading from interpolated normals (the optional shading of a fused fit step; no
+ * counterpart in the reference, whose examples shade with torch elementwise ops).
+ * color [batch, h, w, channels]; normal: 3 floats per pixel, normal_stride floats apart (>= 3, so
+ * a channel slice of interpolate's output is read in place); light [light_batch, 3] with
+ * light_batch 1 or batch (normalised here). out = color * (ambient + max(0, n . l)) with n, l the
+ * unit normal and light; a zero normal shades with the ambient term alone. The backward pass
+ * writes grad_color [batch, h, w, channels] and grad_normal [batch, h, w, 3] (either may be NULL);
+ * the light gets no gradient. batch at most 65535.
+ * ------------------------------------------------------------------------------------------- */
+int dr_lambert_fwd(const float* color, const float* normal, int64_t normal_stride,
+                   const float* light, int64_t light_batch, float ambient, int64_t batch,
+                   int32_t height, int32_t width, int32_t channels, float* out, void* stream);
+int dr_lambert_bwd(const float* color, const float* normal, int64_t normal_stride,
+                   const float* light, int64_t light_batch, float ambient, int64_t batch,
+                   int32_t height, int32_t width, int32_t channels, const float* grad_out,
+                   float* grad_color, float* grad_normal, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

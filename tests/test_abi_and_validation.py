@@ -206,3 +206,17 @@ def test_binding_matches_the_header_argument_by_argument():
             else:
                 raise AssertionError(f"{name}: unexpected parameter {param!r}")
             assert ctype in expected, (name, param, ctype)
+
+
+def test_lambert_validation():
+    color = torch.zeros(1, 4, 4, 3)
+    with pytest.raises(ValueError, match="normal must match color"):
+        dr.lambert(color, torch.zeros(1, 4, 5, 3), torch.ones(3))
+    with pytest.raises(ValueError, match="light_dir must have shape"):
+        dr.lambert(color, torch.zeros(1, 4, 4, 3), torch.ones(2, 3))
+    with pytest.raises(TypeError, match="light_dir must be a torch.float32 tensor"):
+        dr.lambert(color, torch.zeros(1, 4, 4, 3), torch.ones(3, dtype=torch.float64))
+    with pytest.raises(TypeError, match="ambient must be a number"):
+        dr.lambert(color, torch.zeros(1, 4, 4, 3), torch.ones(3), ambient="x")
+    with pytest.raises(RuntimeError, match="CUDA devices only"):
+        dr.lambert(color, torch.zeros(1, 4, 4, 3), torch.ones(3))
