@@ -84,7 +84,9 @@ class Route:
 
 def _take_pending(pending: dict) -> list:
     """The hand-overs delivered to ``pending`` in the running backward pass; clears ``pending``
-    (entries of other, finished passes are stale)."""
+    (entries of other, finished passes are stale, and dropping them frees their gradients). Two
+    backward passes through the same graph must therefore not run at the same time (in two
+    threads); one after the other, with ``retain_graph=True``, they are independent."""
     task = torch._C._current_graph_task_id()
     mine = [v for k, v in pending.items() if k[0] == task]
     pending.clear()

@@ -104,6 +104,19 @@ def aligned(t: Tensor) -> Tensor:
     return t
 
 
+def zeros(shape, device: torch.device) -> Tensor:
+    """A float32 tensor of zeros made with one device memset on the current stream (the
+    gradient buffers the backward scatters accumulate into)."""
+    t = torch.empty(shape, dtype=torch.float32, device=device)
+    if t.numel():
+        N.check(N.lib().dr_zero(t.data_ptr(), t.numel() * 4, N.stream(device)), "dr_zero")
+    return t
+
+
+def zeros_like(t: Tensor) -> Tensor:
+    return zeros(t.shape, t.device)
+
+
 def _scratch(nbytes: int, device: torch.device) -> Tensor:
     return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
 
@@ -252,7 +265,7 @@ def resolve_bwd(pos: Tensor, tri: Tensor, keys: Tensor, grad_rast: Tensor,
     if start is not None and start.shape == pos.shape and start.is_contiguous():
         grad_pos = start
     else:
-        grad_pos = torch.zeros_like(pos) if start is None else start.reshape(pos.shape).clone()
+        grad_pos = zeros_like(pos) if start is None else start.reshape(pos.shape).clone()
     N.check(
         N.lib().dr_raster_resolve_bwd(pos.data_ptr(), pos.shape[0], tri.data_ptr(),
                                       keys.data_ptr(), batch, pos.shape[1], tri.shape[0], height,
@@ -320,7 +333,7 @@ def interpolate_bwd(attr3, rast, rast_db, tri, diff, grad_out, grad_out_da, need
     batch, height, width, _ = rast.shape
     channels = attr3.shape[2]
     num_diff = 0 if diff is None else diff.shape[0]
-    grad_attr = torch.zeros_like(attr3) if need_attr else None
+    grad_attr = zeros_like(attr3) if need_attr else None
     grad_rast = torch.empty_like(rast)
     has_da = grad_out_da is not None or part_da is not None
     grad_db = torch.empty_like(rast) if has_da else None
@@ -408,8 +421,14 @@ def texture_bwd(levels, uv, uv_da, bias, mode, boundary, grad_out, want_uv, want
     # Three-channel gradients are accumulated in four-channel buffers, so that each texel takes
     # one 16-byte vector reduction; the padding is dropped afterwards.
     stride = 4 if channels == 3 else channels
-    grads = [torch.zeros((*lv.shape[:-1], stride), dtype=torch.float32, device=lv.device)
-             for lv in levels]
+    # One buffer (one memset) for the gradients of all levels; each level's part is a multiple
+    # of 16 bytes long when stride is 4, so every level stays aligned for vector reductions.
+    sizes = [lv[..., 0].numel() * stride for lv in levels]
+    flat = zeros(sum(sizes), levels[0].device)
+    grads, at = [], 0
+    for lv, size in zip(levels, sizes):
+        grads.append(flat[at:at + size].view(*lv.shape[:-1], stride))
+        at += size
     if want_uv and grad_uv is None:
         grad_uv = torch.empty(uv.shape, dtype=torch.float32, device=uv.device)
     if want_da and grad_da is None:
@@ -526,7 +545,7 @@ def antialias_bwd(color, rast, pos3, tri, opposite, grad_out, boost, pairs=None)
     tests (same result)."""
     batch, height, width, channels = color.shape
     grad_color = torch.empty_like(color)
-    grad_pos = torch.zeros_like(pos3)
+    grad_pos = zeros_like(pos3)
     N.check(
         N.lib().dr_antialias_bwd(color.data_ptr(), rast.data_ptr(), pos3.data_ptr(), pos3.shape[0],
                                  pos3.shape[1], tri.data_ptr(), tri.shape[0],
@@ -631,7 +650,7 @@ def antialias_mse_bwd(color, rast, pos3, tri, opposite, residual, loss_grad, sca
     ``loss_grad``, a device scalar) plus ``grad_out`` (the output's own gradient, or None)."""
     batch, height, width, channels = color.shape
     grad_color = torch.empty_like(color)
-    grad_pos = torch.zeros_like(pos3)
+    grad_pos = zeros_like(pos3)
     N.check(
         N.lib().dr_antialias_mse_bwd(color.data_ptr(), rast.data_ptr(), pos3.data_ptr(),
                                      pos3.shape[0], pos3.shape[1], tri.data_ptr(), tri.shape[0],

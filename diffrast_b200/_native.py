@@ -125,6 +125,7 @@ _SIGNATURES = {
         [_P, _P, c_int64, _P, c_int64, c_float, c_int64, c_int32, c_int32, c_int32, _P, _P, _P,
          _P],
     ),
+    "dr_zero": (c_int, [_P, c_size_t, _P]),
     "dr_checked_build": (c_int, []),
     "dr_check_faults": (c_int, [POINTER(ctypes.c_uint64)]),
     "dr_check_site_name": (c_char_p, [c_int]),

@@ -70,3 +70,9 @@ extern "C" const char* dr_check_site_name(int site) {
       return "unknown site";
   }
 }
+
+extern "C" int dr_zero(void* ptr, size_t bytes, void* stream) {
+  if (bytes == 0) return DR_OK;
+  if (ptr == nullptr) return DR_ERR_INVALID_ARGUMENT;
+  return static_cast<int>(cudaMemsetAsync(ptr, 0, bytes, reinterpret_cast<cudaStream_t>(stream)));
+}

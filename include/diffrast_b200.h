@@ -57,6 +57,10 @@ const char* dr_status_string(int status);
  * library, 0 for the ordinary one; dr_check_faults() synchronizes the device, returns the first
  * record since the last call in *fault (0: none, always 0 in the ordinary build) and clears it;
  * dr_check_site_name() names a record's site (*fault >> 48). */
+/* Zeroes `bytes` bytes of device memory at ptr on the stream (cudaMemsetAsync): the gradient
+ * buffers that the backward scatters accumulate into. No counterpart in the reference. */
+int dr_zero(void* ptr, size_t bytes, void* stream);
+
 int dr_checked_build(void);
 int dr_check_faults(uint64_t* fault);
 const char* dr_check_site_name(int site);
