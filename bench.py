@@ -191,14 +191,39 @@ class ClockSampler:
 def measured_traffic(stage: str, pixels: int) -> int | None:
     """DRAM bytes of one launch of `stage`: bytes per pixel from a committed ncu capture
     (profiles/dram_bytes_per_pixel.txt) times the pixels of the launch, or None."""
-    path = ROOT / "profiles" / "dram_bytes_per_pixel.txt"
+    per_px = profiled_per_pixel("dram_bytes_per_pixel.txt", stage)
+    return None if per_px is None else int(per_px * pixels)
+
+
+def profiled_per_pixel(name: str, stage: str) -> float | None:
+    """Per-pixel figure of `stage` in the committed ncu summary ``profiles/<name>``, or None."""
+    path = ROOT / "profiles" / name
     if not path.exists():
         return None
     for line in path.read_text().splitlines():
         parts = line.split()
         if len(parts) == 2 and not line.startswith("#") and parts[0] == stage:
-            return int(float(parts[1]) * pixels)
+            return float(parts[1])
     return None
+
+
+def issue_roofline(stage: str, pixels: int, ms_per_launch: float, clocks: dict, dev) -> dict | None:
+    """Warp-instruction issue rate of one launch of `stage` against the SMs' issue peak (four
+    schedulers per SM, one warp instruction each per cycle, at the median SM clock sampled during
+    the timing): the bound of a stage that is limited by instructions, not bytes."""
+    per_px = profiled_per_pixel("warp_instructions_per_pixel.txt", stage)
+    mhz = clocks.get("sm_mhz") or clocks.get("sm_max_mhz")
+    if per_px is None or not mhz:
+        return None
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    achieved = per_px * pixels / (ms_per_launch / 1e3)
+    peak = sms * 4 * mhz * 1e6
+    return {"bound": "issue", "kernel": stage, "achieved": round(achieved / 1e9, 1),
+            "peak": round(peak / 1e9, 1), "unit": "G warp instructions/s",
+            "frac": round(achieved / peak, 4),
+            "instructions_source": "ncu smsp__inst_executed.sum per pixel on the 8-view case "
+                                   "(profiles/warp_instructions_per_pixel.txt), scaled to this "
+                                   "launch's pixels"}  # fmt: skip
 
 
 def gpu_id(dev: torch.device) -> str:
@@ -573,6 +598,7 @@ def run_ours(args) -> None:
             "algorithmic_bytes_per_launch": int(per_launch_bytes),
             "ms_per_launch": round(per_launch_ms, 4),
         },
+        "issue_roofline": issue_roofline(dominant, pixels, per_launch_ms, clock, dev),
         "step_roofline": {
             "algorithmic_bytes": step_bytes(pixels, num_vert, views, stack_bytes - tex_bytes, tex_bytes),
             "frac_of_peak": round(step_bytes(pixels, num_vert, views, stack_bytes - tex_bytes,
@@ -597,9 +623,12 @@ def run_ours(args) -> None:
                         "linear, antialias, MSE, fwd+bwd to tex and pos",
             "gpu": config1_gpu(dev), "cpu_reference": config1_cpu(), "same_config": True,
         }
-        # The reference's own GPU backend on this workload, in its own process.
+        # The reference's own GPU backend on this workload (and on config 1), in its own process.
         torch.cuda.empty_cache()
-        line["gpu_reference"] = gpu_reference_line(args)
+        gpu_ref = gpu_reference_line(args)
+        if "config1" in gpu_ref:
+            line["config1"]["triton"] = gpu_ref.pop("config1")
+        line["gpu_reference"] = gpu_ref
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -806,7 +835,44 @@ def run_triton(args) -> None:
         "peak_mem_gb": round(torch.cuda.max_memory_allocated(dev) / 1e9, 1),
         "clocks": clocks.summary(),
     }  # fmt: skip
+    line["config1"] = triton_config1(ref, dev)
     print(json.dumps(line), flush=True)
+
+
+def triton_config1(ref, dev: torch.device, steps: int = 50) -> dict:
+    """BASELINE configuration 1 in full through the reference's Triton backend (the same op
+    sequence as config1_gpu, with antialias followed by mse_loss as the reference's API has
+    no fused loss), eager as the reference runs it."""
+    import scenes
+
+    sc = scenes.config1_scene(seed=0)
+    res = sc["resolution"]
+    ctx = ref.RasterizeContext(dev)
+    pos = sc["pos"].to(dev).requires_grad_(True)
+    tex = sc["tex"].to(dev).requires_grad_(True)
+    tri, uv, target = sc["tri"].to(dev), sc["uv"].to(dev), sc["target"].to(dev)
+
+    def step():
+        pos.grad = None
+        tex.grad = None
+        rast, _ = ref.rasterize(ctx, pos, tri, res)
+        uvp, _ = ref.interpolate(uv, rast, tri)
+        color = ref.texture(tex, uvp, filter_mode="linear")
+        image = ref.antialias(color, rast, pos, tri)
+        torch.nn.functional.mse_loss(image, target).backward()
+
+    for _ in range(5):
+        step()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / steps
+    return {"value": round(res[0] * res[1] / (ms / 1e3) / 1e6, 1), "unit": UNIT,
+            "ms_per_step": round(ms, 3), "steps": steps, "launch": "eager (the reference's API)"}
 
 
 def run_reference(args) -> None:
