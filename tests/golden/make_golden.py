@@ -2,7 +2,7 @@
 
 Run in a container where the reference is importable (its ``src`` directory on ``sys.path``)::
 
-    DIFFRAST_REFERENCE_SRC=<path to diffrast/src> python tests/golden/make_golden.py
+    DIFFRAST_REFERENCE_SRC=<path to diffrast/src> python tests/golden/make_golden.py [maker ...]
 
 Every fixture stores its seeded inputs next to the reference's outputs and gradients (reference
 backend, CPU, float32), compressed with NumPy. The tests never import the reference: they read
@@ -194,10 +194,24 @@ def make_topology():
     save("topology", tri=tri, neighbours=nb, tri_fan=extra, neighbours_fan=nb2)
 
 
+def make_bench_scene():
+    """The displaced grid of the reference's benchmarks (``benchmarks/bench_rasterize.py``, next
+    to ``src``), which ``scenes.displaced_grid`` restates for ``bench_configs.py``."""
+    sys.path.insert(0, str(Path(SRC).resolve().parent / "benchmarks"))
+    from bench_rasterize import grid_mesh
+
+    pos, tri = grid_mesh(200, 3, torch.device("cpu"))
+    n = round((pos.shape[1]) ** 0.5) - 1
+    steps = torch.linspace(0, 1, n + 1)
+    uv = torch.stack(torch.meshgrid(steps, steps, indexing="xy"), -1).reshape(-1, 2)
+    save("bench_grid", num_tri=np.array(200), views=np.array(3), pos=pos, tri=tri, uv=uv)
+
+
+MAKERS = {"raster": make_raster, "interpolate": make_interpolate, "texture": make_texture,
+          "cube": make_cube, "antialias": make_antialias, "topology": make_topology,
+          "bench_scene": make_bench_scene}  # fmt: skip
+
 if __name__ == "__main__":
-    make_raster()
-    make_interpolate()
-    make_texture()
-    make_cube()
-    make_antialias()
-    make_topology()
+    # python make_golden.py [maker ...]: all fixtures, or only the named makers'.
+    for name in sys.argv[1:] or MAKERS:
+        MAKERS[name]()

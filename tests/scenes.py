@@ -176,6 +176,43 @@ def spherical_uv(verts):
     return torch.stack([u, v], -1).float()
 
 
+def displaced_grid(num_tri: int, views: int):
+    """The scene of the reference's rasterize and pipeline benchmarks
+    (benchmarks/bench_rasterize.py:19-53, bench_pipeline.py:25-28), restated.
+
+    An ``(n + 1)^2``-vertex grid over ``[-1, 1]^2`` in the x-z plane, ``n = round(sqrt(num_tri /
+    2))``, lifted by ``y = 0.1 sin(6x) cos(5z)``, two triangles per cell (all cells' ``(a, b, d)``
+    triangles, then all their ``(a, d, c)`` ones), seen by ``views`` cameras turned about the y
+    axis in equal steps, moved by ``(0, -0.6, 2.2)`` and projected with focal length 1.5, near
+    0.1 and far 10 (``w`` is the camera-space z). Returns clip positions ``[views, V, 4]``, ``tri``
+    and the planar texture coordinates ``((x + 1) / 2, (z + 1) / 2)`` of each vertex.
+    """
+    n = max(1, round(math.sqrt(num_tri / 2)))
+    s = torch.linspace(-1, 1, n + 1)
+    z, x = torch.meshgrid(s, s, indexing="ij")  # vertex i * (n + 1) + j sits at (s[j], s[i])
+    world = torch.stack([x, 0.1 * torch.sin(6 * x) * torch.cos(5 * z), z], -1).reshape(-1, 3)
+    idx = torch.arange((n + 1) ** 2).view(n + 1, n + 1)
+    a, b = idx[:-1, :-1], idx[:-1, 1:]
+    c, d = idx[1:, :-1], idx[1:, 1:]
+    tri = torch.cat([torch.stack([a, b, d], -1), torch.stack([a, d, c], -1)]).reshape(-1, 3).int()
+    near, far, focal = 0.1, 10.0, 1.5
+    project = torch.tensor([[focal, 0, 0, 0], [0, focal, 0, 0],
+                            [0, 0, (far + near) / (far - near), -2 * far * near / (far - near)],
+                            [0, 0, 1, 0]])  # fmt: skip
+    clips = []
+    for k in range(views):
+        angle = 2 * math.pi * k / max(views, 1)
+        turn = torch.eye(4)
+        turn[0, 0], turn[0, 2] = math.cos(angle), math.sin(angle)
+        turn[2, 0], turn[2, 2] = -math.sin(angle), math.cos(angle)
+        turn[:3, 3] = torch.tensor([0.0, -0.6, 2.2])
+        clips.append(to_clip(world, (project @ turn)[None])[0])
+    t = torch.linspace(0, 1, n + 1)
+    tv, tu = torch.meshgrid(t, t, indexing="ij")
+    uv = torch.stack([tu, tv], -1).reshape(-1, 2)
+    return torch.stack(clips).contiguous(), tri, uv.contiguous()
+
+
 def config1_scene(seed=0):
     """icosphere-3 under a random rotation, 1 view at 256x256."""
     gen = torch.Generator().manual_seed(seed)
