@@ -9,6 +9,7 @@ from __future__ import annotations
 
 import functools
 import weakref
+from typing import NamedTuple
 
 import torch
 from torch import Tensor
@@ -62,24 +63,108 @@ class CoordinatePort:
     gradient for ``sink``, and the interpolation's backward pass reads them from there. So no
     zero-padded gradient records of the whole outputs are written or read. Entries are tagged
     with the autograd graph task that made them: a backward pass only ever uses its own.
+
+    The port also describes the interpolation (``geometry``, set by its forward pass), so that a
+    2D lookup can run the interpolation's backward pass for its coordinates inside its own
+    (``dr_texture_bwd_interp``) and hand over gradients of rast and rast_db instead
+    (:class:`Chained`).
     """
 
-    def __init__(self, sink: Tensor, pending: dict) -> None:
+    def __init__(self, sink: Tensor | None, pending: dict, diff_channels: tuple = ()) -> None:
         self.sink = sink
         self.pending = pending
+        self.diff_channels = diff_channels
+        self.geometry: InterpGeometry | None = None
+
+
+class InterpGeometry:
+    """What produced an interpolation's outputs, as the fused texture backward pass reads it:
+    ``attr`` ``[batch or 1, vertices, channels]`` (contiguous), ``rast``, ``tri``, and whether
+    attr needs a gradient (the fused pass computes none). The tensors are the interpolation's
+    saved tensors; its backward pass releases them here (a later backward pass through a retained
+    graph then hands over compact coordinate gradients instead), so that the outputs, which keep
+    the port, do not keep them alive after the graph has freed its own copies."""
+
+    def __init__(self, attr: Tensor, rast: Tensor, tri: Tensor, attr_needs_grad: bool) -> None:
+        self._tensors: tuple | None = (attr, rast, tri)
+        self.attr_needs_grad = attr_needs_grad
+
+    def tensors(self):
+        """``(attr, rast, tri)``, or None once released."""
+        return self._tensors
+
+    def release(self) -> None:
+        self._tensors = None
+
+
+class Chained(NamedTuple):
+    """A lookup's coordinate gradients already chained through the interpolation: gradients of
+    rast and rast_db (``grad_db`` None when uv_da got none)."""
+
+    grad_rast: Tensor
+    grad_db: Tensor | None
+
+
+class ChainArgs(NamedTuple):
+    """Arguments of the fused texture backward pass: the interpolation's tensors and the
+    attribute channels of uv (cu, cv) and of uv_da's two derivative pairs (du, dv)."""
+
+    attr: Tensor
+    rast: Tensor
+    tri: Tensor
+    cu: int
+    cv: int
+    du: int
+    dv: int
+
+
+# Whether 2D lookups of interpolated coordinates run the interpolation's backward pass for them
+# inside their own (tests switch it off to compare against the separate passes).
+FUSE_INTERPOLATION_BACKWARD = True
 
 
 class Route:
     """How a lookup's coordinate gradients leave it: through ``pending`` of a
     :class:`CoordinatePort`, for uv and uv_da as requested at the forward pass."""
 
-    def __init__(self, pending: dict, want_uv: bool, want_da: bool) -> None:
+    def __init__(self, pending: dict, want_uv: bool, want_da: bool,
+                 port: CoordinatePort | None = None) -> None:
         self.pending = pending
         self.want_uv = want_uv
         self.want_da = want_da
+        self.port = port
 
     def deliver(self, key, uv_first, g_uv, da_first, g_da) -> None:
         self.pending[(torch._C._current_graph_task_id(), key)] = (uv_first, g_uv, da_first, g_da)
+
+    def deliver_chained(self, key, grad_rast, grad_db) -> None:
+        self.pending[(torch._C._current_graph_task_id(), key)] = Chained(grad_rast, grad_db)
+
+    def chain(self, uv_spec, da_spec, mode: int, boundary: int, want_da: bool) -> ChainArgs | None:
+        """The fused backward pass's arguments when it applies: a 2D lookup of two consecutive
+        interpolated channels (and of two whole derivative pairs), an interpolation whose
+        attributes need no gradient and whose tensors are alive, and no other lookup of this
+        backward pass fused with the same interpolation. None otherwise."""
+        port = self.port
+        if (not FUSE_INTERPOLATION_BACKWARD or port is None or port.geometry is None
+                or boundary == 3 or mode < 1 or uv_spec is None or uv_spec[1] != 2
+                or port.geometry.attr_needs_grad):
+            return None
+        if want_da and (da_spec is None or da_spec[1] != 4 or da_spec[0] % 2
+                        or da_spec[0] // 2 + 2 > len(port.diff_channels)):
+            return None
+        task = torch._C._current_graph_task_id()
+        if any(k[0] == task and isinstance(v, Chained) for k, v in self.pending.items()):
+            return None
+        got = port.geometry.tensors()
+        if got is None:
+            return None
+        attr, rast, tri = got
+        du = dv = 0
+        if want_da:
+            du = port.diff_channels[da_spec[0] // 2]
+            dv = port.diff_channels[da_spec[0] // 2 + 1]
+        return ChainArgs(attr, rast, tri, uv_spec[0], uv_spec[0] + 1, du, dv)
 
 
 def _take_pending(pending: dict) -> list:
@@ -112,10 +197,12 @@ class PositionPort:
 
 def _collect(pending: dict, channels: int, da_channels: int, grad_out, grad_out_da):
     """The coordinate gradients delivered in this backward pass (consumed), as at most one compact
-    part per output plus whole images for anything that does not fit that form."""
+    part per output plus whole images for anything that does not fit that form, and the
+    hand-overs already chained through the interpolation (:class:`Chained`)."""
     mine = _take_pending(pending)
+    chained = [v for v in mine if isinstance(v, Chained)]
     parts: dict[str, tuple[int, Tensor]] = {}
-    for uv_first, g_uv, da_first, g_da in mine:
+    for uv_first, g_uv, da_first, g_da in (v for v in mine if not isinstance(v, Chained)):
         for name, first, g in (("out", uv_first, g_uv), ("da", da_first, g_da)):
             if g is None:
                 continue
@@ -136,7 +223,7 @@ def _collect(pending: dict, channels: int, da_channels: int, grad_out, grad_out_
                     grad_out = full
                 else:
                     grad_out_da = full
-    return parts.get("out"), parts.get("da"), grad_out, grad_out_da
+    return parts.get("out"), parts.get("da"), grad_out, grad_out_da, chained
 
 
 class Rasterize(torch.autograd.Function):
@@ -184,19 +271,22 @@ class Interpolate(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, attr: Tensor, rast: Tensor, rast_db: Tensor | None, tri: Tensor,
-                diff: Tensor | None, pending: dict):
+                diff: Tensor | None, port: CoordinatePort):
         attr3 = (attr if attr.ndim == 3 else attr[None]).contiguous()
         channels = attr3.shape[2]
         # Rows padded to 16 bytes for the forward kernel's vector loads.
         attr_rows, _ = K.padded_rows(attr3)
         out, out_da = K.interpolate_fwd(attr_rows, rast, rast_db, tri, diff, channels)
         ctx.set_materialize_grads(False)
-        ctx.save_for_backward(*(_saveable(t) for t in (attr3, rast, rast_db, tri, diff)))
+        saved = tuple(_saveable(t) for t in (attr3, rast, rast_db, tri, diff))
+        ctx.save_for_backward(*saved)
         ctx.attr_shape = attr.shape
         ctx.channels = channels
         ctx.has_da = diff is not None
         ctx.rast_db_given = rast_db is not None
-        ctx.pending = pending
+        ctx.pending = port.pending
+        ctx.geometry = port.geometry = InterpGeometry(saved[0], saved[1], saved[3],
+                                                      ctx.needs_input_grad[0])
         if diff is None:
             ctx.mark_non_differentiable(out_da)
         return out, out_da, rast.new_empty(0)
@@ -205,15 +295,26 @@ class Interpolate(torch.autograd.Function):
     @first_order("interpolate")
     def backward(ctx, grad_out, grad_out_da, grad_sink):
         attr3, rast, rast_db, tri, diff = ctx.saved_tensors
+        ctx.geometry.release()
         part = part_da = None
+        chained: list[Chained] = []
         if grad_sink is not None:
             num_da = 0 if diff is None else 2 * diff.shape[0]
-            part, part_da, grad_out, grad_out_da = _collect(ctx.pending, ctx.channels, num_da,
-                                                            grad_out, grad_out_da)
+            part, part_da, grad_out, grad_out_da, chained = _collect(
+                ctx.pending, ctx.channels, num_da, grad_out, grad_out_da)
+        need_attr = ctx.needs_input_grad[0]
+        c_rast = c_db = None
+        for c in chained:
+            c_rast = c.grad_rast if c_rast is None else c_rast + c.grad_rast
+            if c.grad_db is not None:
+                c_db = c.grad_db if c_db is None else c_db + c.grad_db
+        if chained and part is None and part_da is None and grad_out is None \
+                and grad_out_da is None and not need_attr:
+            # Everything was chained inside the lookups' backward passes.
+            return None, c_rast, c_db if ctx.rast_db_given else None, None, None, None
         use_da = ctx.has_da and (grad_out_da is not None or part_da is not None)
         if not use_da:
             grad_out_da = part_da = None
-        need_attr = ctx.needs_input_grad[0]
         grad_attr, grad_rast, grad_db = K.interpolate_bwd(
             attr3, rast, rast_db, tri, diff if use_da else None,
             None if grad_out is None else grad_out.contiguous(),
@@ -223,6 +324,10 @@ class Interpolate(torch.autograd.Function):
             part_da=None if part_da is None else part_da[1].contiguous(),
             da_first=0 if part_da is None else part_da[0],
         )
+        if c_rast is not None:
+            grad_rast = c_rast if grad_rast is None else grad_rast.add_(c_rast)
+        if c_db is not None:
+            grad_db = c_db if grad_db is None else grad_db.add_(c_db)
         if not ctx.rast_db_given:
             grad_db = None
         if grad_attr is not None:
@@ -301,14 +406,23 @@ class Texture(torch.autograd.Function):
         if route is None:
             g_uv_src, uv_first = _slice_gradient(uv_src, uv_spec, want_uv)
             g_da_src, da_first = _slice_gradient(da_src, da_spec, want_da)
-        grads, g_uv, g_da, g_bias = K.texture_bwd(levels, _take(uv_src, uv_spec),
-                                                  _take(da_src, da_spec), bias, mode, boundary,
-                                                  grad_out.contiguous(), want_uv, want_da,
-                                                  want_bias, grad_uv=g_uv_src, grad_da=g_da_src,
-                                                  uv_first=uv_first, da_first=da_first)
+        chain = route.chain(uv_spec, da_spec, mode, boundary, want_da) if route is not None else None
+        if chain is not None:
+            grads, g_rast, g_db, g_bias = K.texture_bwd_chained(
+                levels, _take(uv_src, uv_spec), _take(da_src, da_spec), bias, mode, boundary,
+                grad_out.contiguous(), want_da, want_bias, chain)
+        else:
+            grads, g_uv, g_da, g_bias = K.texture_bwd(
+                levels, _take(uv_src, uv_spec), _take(da_src, da_spec), bias, mode, boundary,
+                grad_out.contiguous(), want_uv, want_da, want_bias, grad_uv=g_uv_src,
+                grad_da=g_da_src, uv_first=uv_first, da_first=da_first)
         level_grads = [g if need[9 + i] else None for i, g in enumerate(grads)]
         if route is not None:
-            route.deliver(id(ctx), uv_spec[0], g_uv, None if da_spec is None else da_spec[0], g_da)
+            if chain is not None:
+                route.deliver_chained(id(ctx), g_rast, g_db)
+            else:
+                route.deliver(id(ctx), uv_spec[0], g_uv,
+                              None if da_spec is None else da_spec[0], g_da)
             sink = grad_out.new_empty(0) if need[8] else None
             return (None, None, g_bias, None, None, None, None, None, sink, *level_grads)
         g_uv = g_uv_src if uv_spec is not None else g_uv
@@ -358,12 +472,16 @@ class TextureChain(torch.autograd.Function):
         if route is None:
             g_uv_src, uv_first = _slice_gradient(uv_src, uv_spec, want_uv)
             g_da_src, da_first = _slice_gradient(da_src, da_spec, want_da)
-        grads, g_uv, g_da, g_bias = K.texture_bwd(levels, _take(uv_src, uv_spec),
-                                                  _take(da_src, da_spec), bias, mode, boundary,
-                                                  grad_out.contiguous(), want_uv, want_da,
-                                                  want_bias, keep_padded=True, grad_uv=g_uv_src,
-                                                  grad_da=g_da_src, uv_first=uv_first,
-                                                  da_first=da_first)
+        chain = route.chain(uv_spec, da_spec, mode, boundary, want_da) if route is not None else None
+        if chain is not None:
+            grads, g_rast, g_db, g_bias = K.texture_bwd_chained(
+                levels, _take(uv_src, uv_spec), _take(da_src, da_spec), bias, mode, boundary,
+                grad_out.contiguous(), want_da, want_bias, chain, keep_padded=True)
+        else:
+            grads, g_uv, g_da, g_bias = K.texture_bwd(
+                levels, _take(uv_src, uv_spec), _take(da_src, da_spec), bias, mode, boundary,
+                grad_out.contiguous(), want_uv, want_da, want_bias, keep_padded=True,
+                grad_uv=g_uv_src, grad_da=g_da_src, uv_first=uv_first, da_first=da_first)
         grad_tex = None
         if need[6]:
             padded = grads[0].shape[-1] != tex.shape[-1]
@@ -378,7 +496,11 @@ class TextureChain(torch.autograd.Function):
             if grad_tex.shape[-1] != tex.shape[-1]:
                 grad_tex = grad_tex[..., : tex.shape[-1]].contiguous()
         if route is not None:
-            route.deliver(id(ctx), uv_spec[0], g_uv, None if da_spec is None else da_spec[0], g_da)
+            if chain is not None:
+                route.deliver_chained(id(ctx), g_rast, g_db)
+            else:
+                route.deliver(id(ctx), uv_spec[0], g_uv,
+                              None if da_spec is None else da_spec[0], g_da)
             sink = grad_out.new_empty(0) if need[10] else None
             return None, None, g_bias, None, None, None, grad_tex, None, None, None, sink
         g_uv = g_uv_src if uv_spec is not None else g_uv

@@ -418,17 +418,7 @@ def texture_bwd(levels, uv, uv_da, bias, mode, boundary, grad_out, want_uv, want
     whose channels c.. receive it and whose other channels are set to zero."""
     batch, height, width = uv.shape[:3]
     channels = levels[0].shape[-1]
-    # Three-channel gradients are accumulated in four-channel buffers, so that each texel takes
-    # one 16-byte vector reduction; the padding is dropped afterwards.
-    stride = 4 if channels == 3 else channels
-    # One buffer (one memset) for the gradients of all levels; each level's part is a multiple
-    # of 16 bytes long when stride is 4, so every level stays aligned for vector reductions.
-    sizes = [lv[..., 0].numel() * stride for lv in levels]
-    flat = zeros(sum(sizes), levels[0].device)
-    grads, at = [], 0
-    for lv, size in zip(levels, sizes):
-        grads.append(flat[at:at + size].view(*lv.shape[:-1], stride))
-        at += size
+    grads, stride = _level_gradients(levels)
     if want_uv and grad_uv is None:
         grad_uv = torch.empty(uv.shape, dtype=torch.float32, device=uv.device)
     if want_da and grad_da is None:
@@ -456,6 +446,57 @@ def texture_bwd(levels, uv, uv_da, bias, mode, boundary, grad_out, want_uv, want
     if stride != channels and not keep_padded:
         grads = [g[..., :channels].contiguous() for g in grads]
     return grads, grad_uv, grad_da, grad_bias
+
+
+def _level_gradients(levels):
+    """Zeroed gradient buffers of all levels and their channel stride. Three-channel gradients
+    are accumulated in four-channel buffers, so that each texel takes one 16-byte vector
+    reduction (the caller drops the padding). One buffer (one memset) holds all levels; each
+    level's part is a multiple of 16 bytes long when the stride is 4, so every level stays
+    aligned for vector reductions."""
+    channels = levels[0].shape[-1]
+    stride = 4 if channels == 3 else channels
+    sizes = [lv[..., 0].numel() * stride for lv in levels]
+    flat = zeros(sum(sizes), levels[0].device)
+    grads, at = [], 0
+    for lv, size in zip(levels, sizes):
+        grads.append(flat[at:at + size].view(*lv.shape[:-1], stride))
+        at += size
+    return grads, stride
+
+
+@timed("texture_bwd")
+def texture_bwd_chained(levels, uv, uv_da, bias, mode, boundary, grad_out, want_da, want_bias,
+                        chain, keep_padded=False):
+    """Texture backward with the interpolation's backward for the coordinates fused in
+    (``dr_texture_bwd_interp``): level gradients, the bias gradient as wanted, and in place of
+    the coordinate gradients ``(grad_rast, grad_db)`` of the interpolation ``chain`` that made uv
+    and uv_da (``grad_db`` None unless ``want_da``)."""
+    batch, height, width = uv.shape[:3]
+    channels = levels[0].shape[-1]
+    grads, stride = _level_gradients(levels)
+    rast = chain.rast
+    grad_rast = torch.empty(rast.shape, dtype=torch.float32, device=rast.device)
+    grad_db = torch.empty(rast.shape, dtype=torch.float32, device=rast.device) if want_da else None
+    uv, uv_stride = pixel_rows(uv)
+    uv_da, da_stride = pixel_rows(uv_da)
+    grad_bias = torch.empty_like(bias) if want_bias else None
+    hs, ws, bs = _level_tables(levels, boundary == 3)
+    attr = chain.attr
+    N.check(
+        N.lib().dr_texture_bwd_interp(
+            N.pointer_array([lv.data_ptr() for lv in levels]),
+            N.pointer_array([g.data_ptr() for g in grads]), hs, ws, bs, len(levels), channels,
+            stride, uv.data_ptr(), uv_stride, N.ptr(uv_da), da_stride, N.ptr(bias), batch, height,
+            width, mode, boundary, grad_out.data_ptr(), N.ptr(grad_bias), rast.data_ptr(),
+            chain.tri.data_ptr(), chain.tri.shape[0], attr.data_ptr(), attr.shape[0],
+            attr.shape[1], attr.shape[2], chain.cu, chain.cv, chain.du, chain.dv,
+            grad_rast.data_ptr(), N.ptr(grad_db), N.stream(uv.device)),
+        "dr_texture_bwd_interp",
+    )  # fmt: skip
+    if stride != channels and not keep_padded:
+        grads = [g[..., :channels].contiguous() for g in grads]
+    return grads, grad_rast, grad_db, grad_bias
 
 
 def _images(level: Tensor) -> int:

@@ -206,6 +206,14 @@ __device__ __forceinline__ long long coverage_key(const Vert& v0, const Vert& v1
   return coverage_key(v0, v1, v2, px, py, tri, r.x, r.y);
 }
 
+// Triangle index of a rast pixel: round(id + 1) - 1 (round half to even, like torch.round), or
+// -1 for background, negative values and ids past the end of tri (reference.py:127-129).
+__device__ __forceinline__ int rast_triangle(float id_plus_one, int num_tri) {
+  const float r = rintf(id_plus_one);
+  if (!(r >= 1.0f) || r > static_cast<float>(num_tri)) return -1;
+  return static_cast<int>(r) - 1;
+}
+
 // Status of the launches just made on this thread.
 inline int launch_status() {
   cudaError_t err = cudaGetLastError();

@@ -15,14 +15,6 @@
 namespace dr {
 namespace {
 
-// Triangle index of a rast pixel: round(id + 1) - 1 (round half to even, like torch.round), or
-// -1 for background, negative values and ids past the end of tri (reference.py:127-129).
-__device__ __forceinline__ int rast_triangle(float id_plus_one, int num_tri) {
-  const float r = rintf(id_plus_one);
-  if (!(r >= 1.0f) || r > static_cast<float>(num_tri)) return -1;
-  return static_cast<int>(r) - 1;
-}
-
 struct Corners {
   bool covered;
   long long row0, row1, row2;  // attribute rows (view * num_vert + vertex)

@@ -595,6 +595,66 @@ __device__ __forceinline__ void write_record(float* __restrict__ out, long long 
   for (int i = first + N; i < stride; ++i) rec[i] = 0.0f;
 }
 
+// The interpolation that produced a 2D lookup's coordinates, for the texture backward pass with
+// the interpolation's backward pass for them fused in: uv = attribute channels (cu, cv)
+// interpolated with rast's barycentrics, uv_da = the screen derivatives of channels (du, dv)
+// from rast_db. The coordinate gradients are chained into gradients of rast (b0, b1; z and the
+// id get zero) and of rast_db instead of being written out. grad_rast null: not fused.
+struct InterpChain {
+  const float4* rast;
+  const int* tri;
+  const float* attr;            // [views or 1, vertices, attr_channels]
+  long long attr_view_stride;   // floats between the views' attribute tables (0: shared)
+  long long num_vert;
+  int attr_channels, num_tri;
+  int cu, cv, du, dv;
+  float4* grad_rast;
+  float4* grad_db;              // null when uv_da carries no gradient
+};
+
+// Gradients of rast and rast_db at pixel p from those of the lookup's coordinates, with the
+// arithmetic and order of the interpolation backward kernel given the same coordinate
+// gradients: d out_c / d b0 = a0_c - a2_c, d out_c / d b1 = a1_c - a2_c, and the derivative
+// channels likewise with rast_db's (d b / dX, d b / dY).
+__device__ __forceinline__ void chain_interpolation(const InterpChain& c, long long p,
+                                                    long long view, const float (&g_uv)[2],
+                                                    const float (&g_da)[4]) {
+  const float4 r = __ldcs(c.rast + p);
+  const int t = rast_triangle(r.w, c.num_tri);
+  float gu = 0.0f, gv = 0.0f;
+  float g_dudx = 0.0f, g_dudy = 0.0f, g_dvdx = 0.0f, g_dvdy = 0.0f;
+  if (t >= 0) {
+    const int* vt = c.tri + 3 * static_cast<long long>(t);
+    const float* base = c.attr + view * c.attr_view_stride;
+    const float* a0 = base + checked_index(__ldg(vt), c.num_vert, kSiteVertex) * c.attr_channels;
+    const float* a1 = base + checked_index(__ldg(vt + 1), c.num_vert, kSiteVertex) * c.attr_channels;
+    const float* a2 = base + checked_index(__ldg(vt + 2), c.num_vert, kSiteVertex) * c.attr_channels;
+    const int ch[2] = {c.cu, c.cv};
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float x0 = __ldg(a0 + ch[i]), x1 = __ldg(a1 + ch[i]), x2 = __ldg(a2 + ch[i]);
+      gu += g_uv[i] * (x0 - x2);
+      gv += g_uv[i] * (x1 - x2);
+    }
+    if (c.grad_db != nullptr) {
+      const int dch[2] = {c.du, c.dv};
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const float gx = g_da[2 * j], gy = g_da[2 * j + 1];
+        const float x2 = __ldg(a2 + dch[j]);
+        const float du = __ldg(a0 + dch[j]) - x2;
+        const float dv = __ldg(a1 + dch[j]) - x2;
+        g_dudx += gx * du;
+        g_dudy += gy * du;
+        g_dvdx += gx * dv;
+        g_dvdy += gy * dv;
+      }
+    }
+  }
+  __stcs(c.grad_rast + p, make_float4(gu, gv, 0.0f, 0.0f));
+  if (c.grad_db != nullptr) __stcs(c.grad_db + p, make_float4(g_dudx, g_dudy, g_dvdx, g_dvdy));
+}
+
 // A quad that a whole warp added to (lane 0 keeps it): pixels that all read the same four texels
 // (a background that samples one point, a magnified region) accumulate here across the tiles a
 // warp visits and reach global memory once, instead of every warp reducing into the same four
@@ -644,7 +704,8 @@ __device__ __forceinline__ void texture_bwd_tile(
     const float* __restrict__ uv_da, const float* __restrict__ bias, const Strides& st, int height,
     int width, const float* __restrict__ grad_out, float* __restrict__ grad_uv,
     float* __restrict__ grad_uv_da, float* __restrict__ grad_bias, const GradLayout& gst,
-    int col, int row, long long view, HotQuad& hot, HotQuad& incoming, bool& pending) {
+    const InterpChain& chain, int col, int row, long long view, HotQuad& hot, HotQuad& incoming,
+    bool& pending) {
   const bool inside = row < height && col < width;
   const long long p = (view * height + row) * width + col;
   Lookup<MODE, B> k;
@@ -784,7 +845,8 @@ __device__ __forceinline__ void texture_bwd_tile(
   }
   }
   if (!inside) return;
-  const bool coord_grads = grad_uv != nullptr || grad_uv_da != nullptr || grad_bias != nullptr;
+  const bool coord_grads = grad_uv != nullptr || grad_uv_da != nullptr || grad_bias != nullptr ||
+                           chain.grad_rast != nullptr;
   if (!coord_grads) return;
   float g_fx_lo = 0.f, g_fy_lo = 0.f, g_fx_hi = 0.f, g_fy_hi = 0.f, g_frac = 0.f;
   if (live && MODE != DR_FILTER_NEAREST) {
@@ -849,6 +911,10 @@ __device__ __forceinline__ void texture_bwd_tile(
     if (grad_uv_da != nullptr) write_record<6>(grad_uv_da, p, gst.uv_da, gst.da_first, g_dir_da);
   } else {
     const float g_uv[2] = {g_u, g_v};
+    if (chain.grad_rast != nullptr) {
+      chain_interpolation(chain, p, view, g_uv, g_da);
+      return;
+    }
     if (grad_uv != nullptr) write_record<2>(grad_uv, p, gst.uv, gst.uv_first, g_uv);
     if (grad_uv_da != nullptr) write_record<4>(grad_uv_da, p, gst.uv_da, gst.da_first, g_da);
   }
@@ -862,7 +928,7 @@ __global__ void __launch_bounds__(256, B == DR_BOUNDARY_CUBE ? 2 : 3) texture_bw
     const float* __restrict__ uv_da, const float* __restrict__ bias, const Strides st, int height,
     int width, const float* __restrict__ grad_out, float* __restrict__ grad_uv,
     float* __restrict__ grad_uv_da, float* __restrict__ grad_bias, const GradLayout gst,
-    long long tiles_x, long long tiles_per_view, long long tiles) {
+    const InterpChain chain, long long tiles_x, long long tiles_per_view, long long tiles) {
   constexpr int NC = RGB ? 3 : 4;
   __shared__ HotQuad hot[8][2];
   const int warp = threadIdx.x >> 5;
@@ -878,8 +944,8 @@ __global__ void __launch_bounds__(256, B == DR_BOUNDARY_CUBE ? 2 : 3) texture_bw
     const int col = static_cast<int>((in_view - ty * tiles_x) * 16) + (threadIdx.x & 15);
     const int row = static_cast<int>(ty * 16) + (threadIdx.x >> 4);
     texture_bwd_tile<MODE, B, RGB>(L, channels, grad_stride, uv, uv_da, bias, st, height, width,
-                                   grad_out, grad_uv, grad_uv_da, grad_bias, gst, col, row, view,
-                                   hot[warp][held], hot[warp][held ^ 1], pending);
+                                   grad_out, grad_uv, grad_uv_da, grad_bias, gst, chain, col,
+                                   row, view, hot[warp][held], hot[warp][held ^ 1], pending);
     if (pending) {  // lane 0 only: the new quad replaces the held one
       flush_quad<NC>(L, hot[warp][held], channels, grad_stride);
       held ^= 1;
@@ -1041,7 +1107,7 @@ template <int MODE, int B>
 void launch_bwd(const Levels& L, int channels, int grad_stride, const float* uv,
                 const float* uv_da, const float* bias, Strides st, int batch, int height,
                 int width, const float* grad_out, float* grad_uv, float* grad_uv_da,
-                float* grad_bias, GradLayout gst, cudaStream_t s) {
+                float* grad_bias, GradLayout gst, const InterpChain& chain, cudaStream_t s) {
   const long long tiles_x = (width + 15) / 16;
   const long long tiles_per_view = tiles_x * ((height + 15) / 16);
   const long long tiles = tiles_per_view * batch;
@@ -1050,7 +1116,7 @@ void launch_bwd(const Levels& L, int channels, int grad_stride, const float* uv,
     const long long grid = min(tiles, static_cast<long long>(resident_blocks(kernel, 256)));
     kernel<<<static_cast<unsigned>(grid), 256, 0, s>>>(L, channels, grad_stride, uv, uv_da, bias,
                                                       st, height, width, grad_out, grad_uv,
-                                                      grad_uv_da, grad_bias, gst, tiles_x,
+                                                      grad_uv_da, grad_bias, gst, chain, tiles_x,
                                                       tiles_per_view, tiles);
   };
   if (quads && channels == 3 && grad_stride == 4)
@@ -1142,7 +1208,9 @@ extern "C" int dr_texture_fwd(const float* const* level_ptr, const int32_t* leve
   return launch_status();
 }
 
-extern "C" int dr_texture_bwd(const float* const* level_ptr, float* const* grad_level_ptr,
+namespace {
+
+int texture_bwd_impl(const float* const* level_ptr, float* const* grad_level_ptr,
                               const int32_t* level_h, const int32_t* level_w,
                               const int64_t* level_batch_stride, int32_t num_levels,
                               int32_t channels, int32_t grad_channel_stride, const float* uv,
@@ -1151,7 +1219,8 @@ extern "C" int dr_texture_bwd(const float* const* level_ptr, float* const* grad_
                               int32_t filter_mode, int32_t boundary_mode, const float* grad_out,
                               float* grad_uv, int64_t grad_uv_stride, int32_t grad_uv_first,
                               float* grad_uv_da, int64_t grad_uv_da_stride,
-                              int32_t grad_uv_da_first, float* grad_bias, void* stream) {
+                              int32_t grad_uv_da_first, float* grad_bias, const InterpChain& chain,
+                              void* stream) {
   if (grad_level_ptr == nullptr) return DR_ERR_INVALID_ARGUMENT;
   Levels L;
   int status = make_levels(level_ptr, grad_level_ptr, level_h, level_w, level_batch_stride,
@@ -1185,9 +1254,76 @@ extern "C" int dr_texture_bwd(const float* const* level_ptr, float* const* grad_
     launch_bwd<decltype(m)::value, decltype(b)::value>(L, channels, grad_channel_stride, uv, uv_da,
                                                        bias, st, static_cast<int>(batch), height,
                                                        width, grad_out, grad_uv, grad_uv_da,
-                                                       grad_bias, gst, s);
+                                                       grad_bias, gst, chain, s);
   });
   return launch_status();
+}
+
+}  // namespace
+
+extern "C" int dr_texture_bwd(const float* const* level_ptr, float* const* grad_level_ptr,
+                              const int32_t* level_h, const int32_t* level_w,
+                              const int64_t* level_batch_stride, int32_t num_levels,
+                              int32_t channels, int32_t grad_channel_stride, const float* uv,
+                              int64_t uv_stride, const float* uv_da, int64_t uv_da_stride,
+                              const float* bias, int64_t batch, int32_t height, int32_t width,
+                              int32_t filter_mode, int32_t boundary_mode, const float* grad_out,
+                              float* grad_uv, int64_t grad_uv_stride, int32_t grad_uv_first,
+                              float* grad_uv_da, int64_t grad_uv_da_stride,
+                              int32_t grad_uv_da_first, float* grad_bias, void* stream) {
+  const InterpChain none = {};
+  return texture_bwd_impl(level_ptr, grad_level_ptr, level_h, level_w, level_batch_stride,
+                          num_levels, channels, grad_channel_stride, uv, uv_stride, uv_da,
+                          uv_da_stride, bias, batch, height, width, filter_mode, boundary_mode,
+                          grad_out, grad_uv, grad_uv_stride, grad_uv_first, grad_uv_da,
+                          grad_uv_da_stride, grad_uv_da_first, grad_bias, none, stream);
+}
+
+extern "C" int dr_texture_bwd_interp(
+    const float* const* level_ptr, float* const* grad_level_ptr, const int32_t* level_h,
+    const int32_t* level_w, const int64_t* level_batch_stride, int32_t num_levels,
+    int32_t channels, int32_t grad_channel_stride, const float* uv, int64_t uv_stride,
+    const float* uv_da, int64_t uv_da_stride, const float* bias, int64_t batch, int32_t height,
+    int32_t width, int32_t filter_mode, int32_t boundary_mode, const float* grad_out,
+    float* grad_bias, const float* rast, const int32_t* tri, int64_t num_tri, const float* attr,
+    int64_t attr_batch, int64_t num_vert, int32_t attr_channels, int32_t cu, int32_t cv,
+    int32_t du, int32_t dv, float* grad_rast, float* grad_db, void* stream) {
+  if (boundary_mode == DR_BOUNDARY_CUBE || filter_mode < 1 || filter_mode > 3)
+    return DR_ERR_INVALID_ARGUMENT;
+  if (batch < 0 || height < 0 || width < 0 || num_tri < 0 || num_tri >= (1LL << 31) ||
+      num_vert < 0 || attr_channels < 1)
+    return DR_ERR_INVALID_ARGUMENT;
+  if (attr_batch != 1 && attr_batch != batch) return DR_ERR_INVALID_ARGUMENT;
+  if (cu < 0 || cu >= attr_channels || cv < 0 || cv >= attr_channels) return DR_ERR_INVALID_ARGUMENT;
+  if (grad_db != nullptr && (uv_da == nullptr || filter_mode != 3 || du < 0 ||
+                             du >= attr_channels || dv < 0 || dv >= attr_channels))
+    return DR_ERR_INVALID_ARGUMENT;
+  const long long total = batch * static_cast<long long>(height) * width;
+  if (total > 0) {
+    const uintptr_t align = reinterpret_cast<uintptr_t>(rast) | reinterpret_cast<uintptr_t>(grad_rast) |
+                            reinterpret_cast<uintptr_t>(grad_db);
+    if (rast == nullptr || grad_rast == nullptr || (align & 15u) != 0) return DR_ERR_INVALID_ARGUMENT;
+    if (num_tri > 0 && tri == nullptr) return DR_ERR_INVALID_ARGUMENT;
+    if (num_vert > 0 && attr == nullptr) return DR_ERR_INVALID_ARGUMENT;
+  }
+  InterpChain chain;
+  chain.rast = reinterpret_cast<const float4*>(rast);
+  chain.tri = tri;
+  chain.attr = attr;
+  chain.attr_view_stride = attr_batch == 1 ? 0 : num_vert * attr_channels;
+  chain.num_vert = num_vert;
+  chain.attr_channels = attr_channels;
+  chain.num_tri = static_cast<int>(num_tri);
+  chain.cu = cu;
+  chain.cv = cv;
+  chain.du = du;
+  chain.dv = dv;
+  chain.grad_rast = reinterpret_cast<float4*>(grad_rast);
+  chain.grad_db = reinterpret_cast<float4*>(grad_db);
+  return texture_bwd_impl(level_ptr, grad_level_ptr, level_h, level_w, level_batch_stride,
+                          num_levels, channels, grad_channel_stride, uv, uv_stride, uv_da,
+                          uv_da_stride, bias, batch, height, width, filter_mode, boundary_mode,
+                          grad_out, nullptr, 0, -1, nullptr, 0, -1, grad_bias, chain, stream);
 }
 
 extern "C" int dr_mip_downsample(const float* src, int64_t images, int32_t h, int32_t w,

@@ -193,15 +193,15 @@ def interpolate(
         return out, attr.new_zeros(batch, height, width, 2 * len(channels))
     with torch.cuda.device(rast.device):
         diff = K.diff_table(tuple(channels), rast.device)
-        pending: dict = {}
+        port = F.CoordinatePort(None, {}, tuple(channels))
         out, out_da, sink = F.Interpolate.apply(
             attr, K.aligned(rast), None if rast_db is None else K.aligned(rast_db),
-            tri.contiguous(), diff, pending,
+            tri.contiguous(), diff, port,
         )
     if sink.requires_grad:
         # Lookups that read channel slices of out / out_da hand their gradients back through
         # this port instead of through whole gradient images (see _functions.CoordinatePort).
-        port = F.CoordinatePort(sink, pending)
+        port.sink = sink
         out._dr_port = port
         out_da._dr_port = port
     return out, out_da
@@ -374,7 +374,7 @@ def _route(uv_src, uv_spec, da_src, da_spec, has_da: bool):
         return None, None, uv_src, da_src
     if has_da and (da_spec is None or getattr(da_src, "_dr_port", None) is not port):
         return None, None, uv_src, da_src
-    route = F.Route(port.pending, want_uv=True, want_da=has_da)
+    route = F.Route(port.pending, want_uv=True, want_da=has_da, port=port)
     return route, port.sink, uv_src.detach(), None if da_src is None else da_src.detach()
 
 

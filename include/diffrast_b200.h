@@ -251,6 +251,29 @@ int dr_texture_bwd(const float* const* level_ptr, float* const* grad_level_ptr,
                    int32_t grad_uv_first, float* grad_uv_da, int64_t grad_uv_da_stride,
                    int32_t grad_uv_da_first, float* grad_bias, void* stream);
 
+/* dr_texture_bwd with the interpolation's backward pass for the lookup's coordinates fused in
+ * (no counterpart in the reference, whose texture and interpolate backward passes run apart,
+ * backends/_triton_texture.py and _triton_interpolate.py). uv and uv_da must be what
+ * dr_interpolate_fwd made of rast, rast_db, tri and attr [attr_batch, num_vert, attr_channels]:
+ * uv = attribute channels (cu, cv), uv_da = the derivative pairs of channels (du, dv). In place of
+ * grad_uv and grad_uv_da, their gradients are chained through that interpolation and written as
+ * grad_rast [batch, height, width, 4] (b0, b1, then zeros for z and the id) and grad_db
+ * [batch, height, width, 4] (NULL when uv_da gets no gradient; then uv_da may still be given for
+ * the level of detail) -- what dr_interpolate_bwd would write for the same coordinate gradients
+ * and no attribute gradient. 2D textures only (not boundary mode 3), filter modes 1-3; rast,
+ * grad_rast and grad_db 16-byte aligned. */
+int dr_texture_bwd_interp(const float* const* level_ptr, float* const* grad_level_ptr,
+                          const int32_t* level_h, const int32_t* level_w,
+                          const int64_t* level_batch_stride, int32_t num_levels, int32_t channels,
+                          int32_t grad_channel_stride, const float* uv, int64_t uv_stride,
+                          const float* uv_da, int64_t uv_da_stride, const float* bias,
+                          int64_t batch, int32_t height, int32_t width, int32_t filter_mode,
+                          int32_t boundary_mode, const float* grad_out, float* grad_bias,
+                          const float* rast, const int32_t* tri, int64_t num_tri,
+                          const float* attr, int64_t attr_batch, int64_t num_vert,
+                          int32_t attr_channels, int32_t cu, int32_t cv, int32_t du, int32_t dv,
+                          float* grad_rast, float* grad_db, void* stream);
+
 /* One mip step (reference.py:449-488): dst [images, (h + 1) / 2, (w + 1) / 2, channels] from
  * src [images, h, w, channels] by area weights; `images` = tex_batch, or 6 * tex_batch for a cube. */
 int dr_mip_downsample(const float* src, int64_t images, int32_t h, int32_t w, int32_t channels,

@@ -7,6 +7,8 @@ accumulated with atomics rel/abs 1e-3 (scaled by the largest gradient where they
 magnitudes).
 """
 
+import functools
+
 import pytest
 import torch
 
@@ -556,6 +558,82 @@ def test_coordinate_port_with_other_consumers_and_retained_graphs(ctx):
         ours, ref = run(False, case), run(True, case)
         for x, y in zip(ours, ref):
             grad_close(x, y, 1e-5)
+
+
+def test_lookup_with_fused_interpolation_backward(ctx):
+    """A 2D lookup of interpolated channels whose attributes need no gradient runs the
+    interpolation's backward pass for its coordinates inside its own (dr_texture_bwd_interp) and
+    hands over gradients of rast and rast_db. Against the separate passes (fusion off: compact
+    coordinate gradients, then the interpolation backward kernel) the gradients are bit-identical
+    (rast's and rast_db's) where the lookup is their only source; against copies of the slices (no hand-over at all)
+    they agree within float32 rounding, also where the chained gradients are combined with other
+    consumers' or with a second lookup's, where attributes need a gradient (no fusion), and in a
+    retained graph differentiated twice (the second pass hands over compact gradients)."""
+    from diffrast_b200 import _functions as F
+
+    sc = scenes.config5_small(views=2)
+    gen = torch.Generator().manual_seed(31)
+    pos, tri = sc["pos"].cuda(), sc["tri"].cuda()
+    attr = torch.cat([sc["attr"], torch.rand(sc["attr"].shape[0], 3, generator=gen)], -1).cuda()
+    per_view = torch.stack([attr, attr.flip(-1)]).contiguous()  # [views, V, C]: attr_batch 2
+    tex = torch.rand(1, 32, 32, 3, generator=gen).cuda()
+    w1, w2 = (torch.randn(2, 64, 64, 3, generator=gen).cuda() for _ in range(2))
+    w_da = torch.randn(2, 64, 64, 16, generator=gen).cuda()
+    rast0, db0 = (x.detach() for x in dr.rasterize(ctx, pos, tri, (64, 64)))
+
+    def run(how: str, case: str):
+        F.FUSE_INTERPOLATION_BACKWARD = how != "separate"
+        try:
+            r = rast0.clone().requires_grad_(True)
+            d = db0.clone().requires_grad_(True)
+            t = tex.clone().requires_grad_(True)
+            a = (per_view if case == "attr_batch" else attr).clone()
+            if case == "attr_grad":
+                a.requires_grad_(True)
+            out, out_da = dr.interpolate(a, r, tri, rast_db=d, diff_attrs="all")
+
+            def s(x):
+                return x.clone() if how == "copy" else x
+
+            mode = "linear-mipmap-linear"
+            uv, uv_da = s(out[..., 0:2]), s(out_da[..., 0:4])
+            if case in ("chain", "attr_batch", "attr_grad", "retained"):
+                loss = (dr.texture(t, uv, uv_da, filter_mode=mode) * w1).sum()
+            elif case == "stack":
+                color = dr.texture(t, uv, uv_da, mip=dr.texture_construct_mip(t), filter_mode=mode)
+                loss = (color * w1).sum()
+            elif case == "linear":
+                loss = (dr.texture(t, uv, filter_mode="linear") * w1).sum()
+            elif case == "mip_nearest":
+                loss = (dr.texture(t, uv, uv_da, filter_mode="linear-mipmap-nearest") * w1).sum()
+            elif case == "offset":
+                color = dr.texture(t, s(out[..., 5:7]), s(out_da[..., 10:14]), filter_mode=mode)
+                loss = (color * w1).sum()
+            elif case == "other_consumers":
+                loss = (dr.texture(t, uv, uv_da, filter_mode=mode) * w1).sum() + \
+                    (out[..., 2:] ** 2).sum() + (out_da * w_da).sum()
+            else:  # two lookups of one interpolation: the second hands over compact gradients
+                c2 = dr.texture(t, s(out[..., 3:5]), s(out_da[..., 6:10]), filter_mode=mode)
+                loss = (dr.texture(t, uv, uv_da, filter_mode=mode) * w1).sum() + (c2 * w2).sum()
+            leaves = [r, d, t] + ([a] if case == "attr_grad" else [])
+            grad = functools.partial(torch.autograd.grad, allow_unused=True, materialize_grads=True)
+            if case == "retained":
+                first = grad(loss, leaves, retain_graph=True)
+                return (*first, *grad(loss, leaves))
+            return grad(loss, leaves)
+        finally:
+            F.FUSE_INTERPOLATION_BACKWARD = True
+
+    exact = ("chain", "stack", "linear", "mip_nearest", "offset", "attr_batch")
+    for case in exact + ("other_consumers", "two_lookups", "attr_grad", "retained"):
+        fused, separate, copied = (run(how, case) for how in ("fused", "separate", "copy"))
+        for i, (x, y, z) in enumerate(zip(fused, separate, copied)):
+            if case in exact and i < 2:  # rast, rast_db (the texel gradients use atomics)
+                assert torch.equal(x, y), case
+            grad_close(x, z, 1e-5)
+        assert fused[0].abs().sum() > 0, case
+        if case not in ("linear", "mip_nearest"):
+            assert fused[1].abs().sum() > 0, case
 
 
 def test_position_port_matches_separate_gradients(ctx):
