@@ -12,7 +12,7 @@ the median of individually synchronised steps, each step bracketed by CUDA event
 arm is timed eagerly (as the reference's API runs) and again replaying a CUDA graph of the step.
 One JSON line per case:
 
-    python bench_configs.py [--cases c1 c2 c3 c4 grid] [--repeats 10] [--warmup-s 2]
+    python bench_configs.py [--cases c1 c2 c3 c4 grid] [--repeats 10] [--warmup-s 2] [--no-triton]
 """
 
 from __future__ import annotations
@@ -273,7 +273,8 @@ def run_case(case, dev, ours, ref, repeats: int, warmup_s: float) -> dict:
         torch.cuda.empty_cache()
         torch.cuda.reset_peak_memory_stats(dev)
     if ref is None:
-        line["triton"] = {"unavailable": "the reference package is not installed under baseline/_ref"}
+        line["triton"] = {"unavailable": "not run (--no-triton) or the reference package is not "
+                                         "installed under baseline/_ref"}
     ours_v = line["ours"].get("fwd_bwd", {}).get("value")
     ref_v = line["triton"].get("fwd_bwd", {}).get("value")
     if ours_v and ref_v:
@@ -286,6 +287,7 @@ def main() -> None:
     parser.add_argument("--cases", nargs="+", default=["c1", "c2", "c3", "c4", "grid"])
     parser.add_argument("--repeats", type=int, default=10)
     parser.add_argument("--warmup-s", type=float, default=2.0)
+    parser.add_argument("--no-triton", action="store_true", help="time this library's arm only")
     args = parser.parse_args()
     if not torch.cuda.is_available():
         raise SystemExit("bench_configs.py needs a CUDA device")
@@ -293,7 +295,7 @@ def main() -> None:
     torch.cuda.set_device(dev)
     import diffrast_b200 as ours
 
-    ref = reference_package("triton")
+    ref = None if args.no_triton else reference_package("triton")
     cases = []
     for name in args.cases:
         if name == "grid":

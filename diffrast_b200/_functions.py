@@ -340,11 +340,7 @@ class MipChain(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, tex: Tensor, count: int):
-        levels = []
-        level = tex
-        for _ in range(count):
-            level = K.mip_down(level)
-            levels.append(level)
+        levels = K.mip_build(tex, count)
         ctx.shapes = [tex.shape, *(lv.shape for lv in levels)]
         ctx.device = tex.device
         return tuple(levels)
@@ -442,9 +438,7 @@ class TextureChain(torch.autograd.Function):
     def forward(ctx, uv_src, da_src, bias, mode: int, boundary: int, count: int, tex: Tensor,
                 uv_spec=None, da_spec=None, route=None, sink=None):
         tex = tex.contiguous()
-        levels = [tex]
-        for _ in range(count):
-            levels.append(K.mip_down(levels[-1]))
+        levels = [tex, *K.mip_build(tex, count)]
         out = K.texture_fwd(levels, _take(uv_src, uv_spec), _take(da_src, da_spec), bias, mode,
                             boundary)
         ctx.save_for_backward(*(_saveable(t) for t in (uv_src, da_src, bias, tex)))
@@ -485,12 +479,12 @@ class TextureChain(torch.autograd.Function):
         grad_tex = None
         if need[6]:
             padded = grads[0].shape[-1] != tex.shape[-1]
-            for level in range(len(grads) - 2, -1, -1):
-                # The last step writes the base gradient without the padding channel.
-                last = level == 0 and padded
-                out = torch.empty(tex.shape, dtype=torch.float32, device=tex.device) if last else None
-                K.mip_down_bwd(grads[level + 1], grads[level], out)
-                if last:
+            if len(grads) > 1:
+                # The whole adjoint chain at once; with padding, the base gradient is written
+                # without the padding channel.
+                out = torch.empty(tex.shape, dtype=torch.float32, device=tex.device) if padded else None
+                K.mip_build_bwd(grads, out)
+                if padded:
                     grads[0] = out
             grad_tex = grads[0]
             if grad_tex.shape[-1] != tex.shape[-1]:

@@ -513,6 +513,36 @@ def mip_down(level: Tensor) -> Tensor:
     return out
 
 
+@timed("mip_build")
+def mip_build(tex: Tensor, count: int) -> list[Tensor]:
+    """Levels 1 .. count of ``tex`` (``[.., h, w, C]``, contiguous), each its own tensor, made by
+    ``dr_mip_build`` (runs of even halvings several levels per launch)."""
+    h, w, c = tex.shape[-3], tex.shape[-2], tex.shape[-1]
+    levels, lh, lw = [], h, w
+    for _ in range(count):
+        lh, lw = (lh + 1) // 2, (lw + 1) // 2
+        levels.append(torch.empty((*tex.shape[:-3], lh, lw, c), dtype=torch.float32,
+                                  device=tex.device))
+    if count:
+        N.check(N.lib().dr_mip_build(tex.data_ptr(), _images(tex), h, w, c, count,
+                                     N.pointer_array([lv.data_ptr() for lv in levels]),
+                                     N.stream(tex.device)), "dr_mip_build")  # fmt: skip
+    return levels
+
+
+@timed("mip_adjoint")
+def mip_build_bwd(grads: list[Tensor], out: Tensor | None = None) -> None:
+    """Pushes the gradients of levels 1.. (``grads[1:]``) down into the base gradient
+    ``grads[0]`` in place, or, given ``out`` (fewer channels: without the padding), writes the
+    base result there instead; the coarser buffers are left in an unspecified state."""
+    base = grads[0]
+    h, w, c = base.shape[-3], base.shape[-2], base.shape[-1]
+    N.check(N.lib().dr_mip_build_bwd(N.pointer_array([g.data_ptr() for g in grads]),
+                                     _images(base), h, w, c, len(grads) - 1, N.ptr(out),
+                                     0 if out is None else out.shape[-1],
+                                     N.stream(base.device)), "dr_mip_build_bwd")  # fmt: skip
+
+
 @timed("mip_adjoint")
 def mip_down_bwd(grad_coarse: Tensor, grad_fine: Tensor, out: Tensor | None = None) -> None:
     """Adds the adjoint of one mip step of ``grad_coarse`` into ``grad_fine`` (in place), or,

@@ -94,6 +94,8 @@ _SIGNATURES = {
          c_int32, c_int32, c_int32, c_int32, c_int32, _P, _P, _P],
     ),
     "dr_mip_downsample": (c_int, [_P, c_int64, c_int32, c_int32, c_int32, _P, _P]),
+    "dr_mip_build": (c_int, [_P, c_int64, c_int32, c_int32, c_int32, c_int32, _P, _P]),
+    "dr_mip_build_bwd": (c_int, [_P, c_int64, c_int32, c_int32, c_int32, c_int32, _P, c_int32, _P]),
     "dr_mip_downsample_bwd": (c_int, [_P, c_int64, c_int32, c_int32, c_int32, _P, _P, c_int32, _P]),
     "dr_edge_neighbours_workspace_bytes": (c_size_t, [c_int64]),
     "dr_edge_neighbours": (c_int, [_P, c_int64, _P, _P, c_size_t, _P]),

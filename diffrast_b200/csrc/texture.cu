@@ -1091,6 +1091,67 @@ __global__ void __launch_bounds__(256) mip_down_bwd_kernel(const float* __restri
   }
 }
 
+// Several levels of an even mip chain in one launch: a block reduces a 2^n x 2^n tile of the
+// source level (n <= kChainLevels) to one texel of level source + n through shared memory and
+// writes every intermediate level's texels of the tile. The averages are mip_down_even_kernel's,
+// in its order, so the levels are bit for bit those of one launch per level. Grid: source tiles
+// across in x, down in y, images in z.
+constexpr int kChainLevels = 6;
+
+struct ChainLevels {
+  float* level[kChainLevels];
+};
+
+template <int C>
+__global__ void __launch_bounds__(256) mip_chain_even_kernel(const float* __restrict__ src, int h,
+                                                             int w, int n, ChainLevels dst) {
+  __shared__ float buf[32 * 32 * C];
+  const long long img = blockIdx.z;
+  int side = (1 << n) / 2;  // texels per side of the tile in the level being made
+  int lh = h / 2, lw = w / 2;
+  int y0 = blockIdx.y * side, x0 = blockIdx.x * side;  // the tile's first texel in that level
+  for (int i = threadIdx.x; i < side * side; i += blockDim.x) {
+    const int j = i / side, k = i - j * side;
+    const float* a = src + ((img * h + 2 * (y0 + j)) * static_cast<long long>(w) + 2 * (x0 + k)) * C;
+    const float* b = a + static_cast<long long>(w) * C;
+    float* out = dst.level[0] + ((img * lh + y0 + j) * static_cast<long long>(lw) + x0 + k) * C;
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      const float v = 0.25f * ((__ldg(a + c) + __ldg(a + C + c)) + (__ldg(b + c) + __ldg(b + C + c)));
+      out[c] = v;
+      buf[i * C + c] = v;
+    }
+  }
+  for (int l = 1; l < n; ++l) {
+    const int ns = side / 2;  // at most 16, so at most one texel per thread
+    const int t = threadIdx.x;
+    float v[C];
+    __syncthreads();
+    if (t < ns * ns) {
+      const int j = t / ns, k = t - j * ns;
+      const float* a = buf + (2 * j * side + 2 * k) * C;
+      const float* b = a + side * C;
+#pragma unroll
+      for (int c = 0; c < C; ++c) v[c] = 0.25f * ((a[c] + a[C + c]) + (b[c] + b[C + c]));
+    }
+    __syncthreads();
+    lh /= 2;
+    lw /= 2;
+    y0 /= 2;
+    x0 /= 2;
+    if (t < ns * ns) {
+      const int j = t / ns, k = t - j * ns;
+      float* out = dst.level[l] + ((img * lh + y0 + j) * static_cast<long long>(lw) + x0 + k) * C;
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        out[c] = v[c];
+        buf[t * C + c] = v[c];
+      }
+    }
+    side = ns;
+  }
+}
+
 template <int MODE, int B>
 void launch_fwd(const Levels& L, int channels, const float* uv, const float* uv_da,
                 const float* bias, Strides st, long long total, long long ppi, float* out,
@@ -1362,4 +1423,95 @@ extern "C" int dr_mip_downsample_bwd(const float* grad_dst, int64_t images, int3
       grad_dst, h, w, channels, grad_src, aligned16, out, out_channels);
   return launch_status();
 }
+namespace {
+
+// Sizes of level l of a chain whose base is h x w (the reference's rounding up).
+void level_size(int h, int w, int l, int& lh, int& lw) {
+  lh = h;
+  lw = w;
+  for (int i = 0; i < l; ++i) {
+    lh = (lh + 1) / 2;
+    lw = (lw + 1) / 2;
+  }
+}
+
+// Largest n <= limit such that halving h x w n times stays even every time.
+int even_run(int h, int w, int limit) {
+  int n = 0;
+  while (n < limit && h % 2 == 0 && w % 2 == 0) {
+    h /= 2;
+    w /= 2;
+    ++n;
+  }
+  return n;
+}
+
+}  // namespace
+
+extern "C" int dr_mip_build(const float* src, int64_t images, int32_t h, int32_t w,
+                            int32_t channels, int32_t levels, float* const* dst, void* stream) {
+  if (images < 0 || h < 1 || w < 1 || channels < 1 || levels < 0 || levels > DR_MAX_LEVELS - 1 ||
+      src == nullptr || (levels > 0 && dst == nullptr))
+    return DR_ERR_INVALID_ARGUMENT;
+  for (int l = 0; l < levels; ++l)
+    if (dst[l] == nullptr) return DR_ERR_INVALID_ARGUMENT;
+  if (images == 0 || levels == 0) return DR_OK;
+  cudaStream_t s = as_stream(stream);
+  const float* cur = src;
+  int ch = h, cw = w;
+  for (int l = 0; l < levels;) {
+    const int n = even_run(ch, cw, min(kChainLevels, levels - l));
+    if (n >= 2 && channels <= 4 && images <= 65535 && (ch >> n) <= 65535) {
+      ChainLevels cl = {};
+      for (int i = 0; i < n; ++i) cl.level[i] = dst[l + i];
+      const dim3 grid(static_cast<unsigned>(cw >> n), static_cast<unsigned>(ch >> n),
+                      static_cast<unsigned>(images));
+      switch (channels) {
+        case 1: mip_chain_even_kernel<1><<<grid, 256, 0, s>>>(cur, ch, cw, n, cl); break;
+        case 2: mip_chain_even_kernel<2><<<grid, 256, 0, s>>>(cur, ch, cw, n, cl); break;
+        case 3: mip_chain_even_kernel<3><<<grid, 256, 0, s>>>(cur, ch, cw, n, cl); break;
+        default: mip_chain_even_kernel<4><<<grid, 256, 0, s>>>(cur, ch, cw, n, cl); break;
+      }
+      const int status = launch_status();
+      if (status != DR_OK) return status;
+      cur = dst[l + n - 1];
+      ch >>= n;
+      cw >>= n;
+      l += n;
+      continue;
+    }
+    const int status = dr_mip_downsample(cur, images, ch, cw, channels, dst[l], stream);
+    if (status != DR_OK) return status;
+    cur = dst[l];
+    ch = (ch + 1) / 2;
+    cw = (cw + 1) / 2;
+    ++l;
+  }
+  return DR_OK;
+}
+
+extern "C" int dr_mip_build_bwd(float* const* grad_levels, int64_t images, int32_t h, int32_t w,
+                                int32_t channels, int32_t levels, float* out, int32_t out_channels,
+                                void* stream) {
+  if (images < 0 || h < 1 || w < 1 || channels < 1 || levels < 0 || levels > DR_MAX_LEVELS - 1 ||
+      grad_levels == nullptr)
+    return DR_ERR_INVALID_ARGUMENT;
+  for (int l = 0; l <= levels; ++l)
+    if (grad_levels[l] == nullptr) return DR_ERR_INVALID_ARGUMENT;
+  if (out != nullptr && (out_channels < 1 || out_channels > channels || levels == 0))
+    return DR_ERR_INVALID_ARGUMENT;
+  if (images == 0 || levels == 0) return DR_OK;
+  // One step per level, coarsest first. (A single pass over the base that reads every coarser
+  // level per texel was slower on config 5: 0.31 against 0.20 ms.)
+  for (int l = levels; l > 0; --l) {
+    int lh, lw;
+    level_size(h, w, l - 1, lh, lw);
+    const int status = dr_mip_downsample_bwd(grad_levels[l], images, lh, lw, channels,
+                                             grad_levels[l - 1], l == 1 ? out : nullptr,
+                                             out_channels, stream);
+    if (status != DR_OK) return status;
+  }
+  return DR_OK;
+}
+
 DR_DEFINE_FAULT_QUERY(texture)

@@ -327,7 +327,8 @@ def texture(
             mip_level_bias = None if mip_level_bias is None else mip_level_bias.detach()
         uv_src, uv_spec = _channel_slice(uv)
         da_src, da_spec = _channel_slice(uv_da)
-        route, sink, uv_src, da_src = _route(uv_src, uv_spec, da_src, da_spec, _needs_grad(uv_da))
+        route, sink, uv_src, uv_spec, da_src, da_spec = _route(uv_src, uv_spec, da_src, da_spec,
+                                                               _needs_grad(uv_da))
         with torch.cuda.device(uv.device):
             return F.TextureChain.apply(
                 uv_src, da_src, None if mip_level_bias is None else mip_level_bias.contiguous(),
@@ -352,7 +353,8 @@ def texture(
     # kernels read them in place through their pixel stride.
     uv_src, uv_spec = _channel_slice(uv)
     da_src, da_spec = _channel_slice(uv_da)
-    route, sink, uv_src, da_src = _route(uv_src, uv_spec, da_src, da_spec, _needs_grad(uv_da))
+    route, sink, uv_src, uv_spec, da_src, da_spec = _route(uv_src, uv_spec, da_src, da_spec,
+                                                           _needs_grad(uv_da))
     with torch.cuda.device(uv.device):
         return F.Texture.apply(
             uv_src, da_src, None if mip_level_bias is None else mip_level_bias.contiguous(), mode,
@@ -365,17 +367,26 @@ def _needs_grad(t: Tensor | None) -> bool:
 
 
 def _route(uv_src, uv_spec, da_src, da_spec, has_da: bool):
-    """``(route, sink, uv_src, da_src)`` for a lookup whose uv (and uv_da, if given) are channel
-    slices of the outputs of one :func:`interpolate` call: its coordinate gradients then go back
-    through that call's port, and uv_src / da_src enter the lookup detached. ``(None, None,
-    uv_src, da_src)`` otherwise."""
-    port = getattr(uv_src, "_dr_port", None) if uv_spec is not None else None
-    if port is None:
-        return None, None, uv_src, da_src
-    if has_da and (da_spec is None or getattr(da_src, "_dr_port", None) is not port):
-        return None, None, uv_src, da_src
+    """``(route, sink, uv_src, uv_spec, da_src, da_spec)`` for a lookup whose uv (and uv_da, if
+    given) are the outputs of one :func:`interpolate` call or channel slices of them: its
+    coordinate gradients then go back through that call's port, and uv_src / da_src enter the
+    lookup detached (a whole output counts as the slice of all its channels). ``(None, None,
+    uv_src, uv_spec, da_src, da_spec)`` otherwise."""
+    unrouted = None, None, uv_src, uv_spec, da_src, da_spec
+    port = getattr(uv_src, "_dr_port", None)
+    if port is None or not (uv_spec is not None or _needs_grad(uv_src)):
+        return unrouted
+    if has_da and (getattr(da_src, "_dr_port", None) is not port
+                   or not (da_spec is not None or _needs_grad(da_src))):
+        return unrouted
+    if uv_spec is None:
+        uv_spec = (0, uv_src.shape[-1])
+    if has_da and da_spec is None:
+        da_spec = (0, da_src.shape[-1])
     route = F.Route(port.pending, want_uv=True, want_da=has_da, port=port)
-    return route, port.sink, uv_src.detach(), None if da_src is None else da_src.detach()
+    return (route, port.sink, uv_src.detach(), uv_spec,
+            None if da_src is None else da_src.detach(), da_spec)
+
 
 
 def _channel_slice(t: Tensor | None):

@@ -287,6 +287,25 @@ int dr_mip_downsample_bwd(const float* grad_dst, int64_t images, int32_t h, int3
                           int32_t channels, float* grad_src, float* out, int32_t out_channels,
                           void* stream);
 
+/* The whole mip chain at once (reference.py:433-488; texture_construct_mip, ops.py:239-265):
+ * levels 1 .. levels of src [images, h, w, channels] into dst[0 .. levels - 1], each
+ * [images, h_l, w_l, channels] with h_l = (h_{l-1} + 1) / 2 (and w_l likewise), values equal to
+ * repeated dr_mip_downsample. Runs of even halvings with at most 4 channels take one launch per
+ * up to 6 levels. levels <= DR_MAX_LEVELS - 1. No counterpart in the reference's interface, which
+ * builds the chain step by step. */
+int dr_mip_build(const float* src, int64_t images, int32_t h, int32_t w, int32_t channels,
+                 int32_t levels, float* const* dst, void* stream);
+
+/* The adjoint of dr_mip_build: pushes the gradients of levels 1 .. levels (grad_levels[1 ..],
+ * `channels` floats per texel, e.g. 4-channel padded) down into the base gradient grad_levels[0],
+ * as repeated dr_mip_downsample_bwd from the coarsest level would (same values); with out non-NULL
+ * the base result goes to out [images, h, w, out_channels] instead (levels >= 1 then) and
+ * grad_levels[0] is left unchanged. The contents of grad_levels[1 ..] afterwards are unspecified
+ * (they hold the partial sums). */
+int dr_mip_build_bwd(float* const* grad_levels, int64_t images, int32_t h, int32_t w,
+                     int32_t channels, int32_t levels, float* out, int32_t out_channels,
+                     void* stream);
+
 /* ---------------------------------------------------------------------------------------------
  * Antialias (reference.py:202-265, :675-814; topology.py; _triton_antialias.py).
  * neighbours [num_tri, 3] int64 from dr_edge_neighbours (reference.py:768-787); opposite

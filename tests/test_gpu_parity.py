@@ -353,6 +353,48 @@ def test_mip_chain_gradient_matches_oracle():
         grad_close(grads[1], grads[0], 1e-4)
 
 
+def test_whole_mip_chain_equals_one_step_at_a_time():
+    """dr_mip_build (runs of even halvings several levels per launch) and dr_mip_build_bwd (the
+    adjoint chain in one call) against one dr_mip_downsample / dr_mip_downsample_bwd call per
+    level: bit-identical, for power-of-two, partly even and odd sizes, 1 to 5 channels, several
+    images, in place and into an unpadded output."""
+    from diffrast_b200 import _kernels as K
+
+    gen = torch.Generator().manual_seed(17)
+    shapes = [(1, 256, 256, 3), (2, 128, 64, 1), (1, 96, 40, 4), (3, 48, 48, 5), (1, 1, 64, 2),
+              (12, 32, 32, 3), (1, 4096, 8, 3)]
+    for shape in shapes:
+        tex = torch.rand(shape, generator=gen).cuda()
+        count = 0
+        h, w = shape[1], shape[2]
+        while h > 1 or w > 1:
+            h, w = (h + 1) // 2, (w + 1) // 2
+            count += 1
+        whole = K.mip_build(tex, count)
+        steps, level = [], tex
+        for _ in range(count):
+            level = K.mip_down(level)
+            steps.append(level)
+        for a, b in zip(whole, steps):
+            assert torch.equal(a, b), shape
+        stride = 4 if shape[-1] == 3 else shape[-1]
+        grads = [torch.randn((*lv.shape[:-1], stride), generator=gen).cuda()
+                 for lv in [tex, *steps]]
+        for unpadded in (False, True):
+            ref = [g.clone() for g in grads]
+            out_ref = torch.empty(shape, device=CUDA) if unpadded else None
+            for level in range(len(ref) - 2, -1, -1):
+                K.mip_down_bwd(ref[level + 1], ref[level], out_ref if level == 0 else None)
+            got = [g.clone() for g in grads]
+            out = torch.empty(shape, device=CUDA) if unpadded else None
+            K.mip_build_bwd(got, out)
+            if unpadded:
+                assert torch.equal(out, out_ref), shape
+                assert torch.equal(got[0], grads[0]), shape  # left unchanged
+            else:
+                assert torch.equal(got[0], ref[0]), shape
+
+
 @pytest.mark.parametrize("name", golden_names("cube_"))
 def test_cube_texture_matches_golden(name):
     g = load_golden(name)
@@ -565,7 +607,8 @@ def test_lookup_with_fused_interpolation_backward(ctx):
     interpolation's backward pass for its coordinates inside its own (dr_texture_bwd_interp) and
     hands over gradients of rast and rast_db. Against the separate passes (fusion off: compact
     coordinate gradients, then the interpolation backward kernel) the gradients are bit-identical
-    (rast's and rast_db's) where the lookup is their only source; against copies of the slices (no hand-over at all)
+    (rast's and rast_db's) where the lookup is their only source (also when it reads the
+    interpolation's outputs whole rather than channel slices of them); against copies of the slices (no hand-over at all)
     they agree within float32 rounding, also where the chained gradients are combined with other
     consumers' or with a second lookup's, where attributes need a gradient (no fusion), and in a
     retained graph differentiated twice (the second pass hands over compact gradients)."""
@@ -597,7 +640,11 @@ def test_lookup_with_fused_interpolation_backward(ctx):
 
             mode = "linear-mipmap-linear"
             uv, uv_da = s(out[..., 0:2]), s(out_da[..., 0:4])
-            if case in ("chain", "attr_batch", "attr_grad", "retained"):
+            if case == "whole":  # interpolate's outputs themselves, as the reference's benchmark
+                out, out_da = dr.interpolate(a[..., 0:2].contiguous(), r, tri, rast_db=d,
+                                             diff_attrs="all")
+                uv, uv_da = s(out), s(out_da)
+            if case in ("chain", "whole", "attr_batch", "attr_grad", "retained"):
                 loss = (dr.texture(t, uv, uv_da, filter_mode=mode) * w1).sum()
             elif case == "stack":
                 color = dr.texture(t, uv, uv_da, mip=dr.texture_construct_mip(t), filter_mode=mode)
@@ -624,7 +671,7 @@ def test_lookup_with_fused_interpolation_backward(ctx):
         finally:
             F.FUSE_INTERPOLATION_BACKWARD = True
 
-    exact = ("chain", "stack", "linear", "mip_nearest", "offset", "attr_batch")
+    exact = ("chain", "whole", "stack", "linear", "mip_nearest", "offset", "attr_batch")
     for case in exact + ("other_consumers", "two_lookups", "attr_grad", "retained"):
         fused, separate, copied = (run(how, case) for how in ("fused", "separate", "copy"))
         for i, (x, y, z) in enumerate(zip(fused, separate, copied)):
