@@ -55,7 +55,7 @@ LAUNCHES = {
 
 
 def stage_bytes(pixels: int, num_vert: int, views: int, stack_bytes: int, tex_bytes: int,
-                fused_interp: bool = False) -> dict:
+                fused: int = 0) -> dict:
     """Algorithmic bytes per launch of each stage: API-level tensor reads and writes, fp32.
 
     Per pixel (C attribute channels, D differentiated channels, Ct texture channels):
@@ -65,9 +65,11 @@ def stage_bytes(pixels: int, num_vert: int, views: int, stack_bytes: int, tex_by
     antialias reads colour and rast (4Ct + 16) and writes 4Ct, backward reads 8Ct + 16 and writes
     4Ct. Per call: clip positions (16 B per vertex and view) for the rasterizer and the transform
     that writes them (its backward reads their gradient), the mip stack for the build and its
-    adjoint. With ``fused_interp`` the texture backward runs the interpolation's backward for the
+    adjoint. With ``fused`` = 1 the texture backward runs the interpolation's backward for the
     coordinates (no interpolation backward launch): it reads the upstream gradient, uv, uv_da and
-    rast and writes the gradients of rast and rast_db, 4Ct + 24 + 16 + 32.
+    rast and writes the gradients of rast and rast_db, 4Ct + 24 + 16 + 32; with 2 the
+    rasterizer's backward too (no resolve backward launch): it reads the keys instead of rast and
+    writes no per-pixel gradient, 4Ct + 24 + 8, plus the clip positions and their gradient.
     """
     c, d, ct = ATTR_CHANNELS, DIFF_CHANNELS, TEX_CHANNELS
     pos_bytes = views * num_vert * 16
@@ -79,8 +81,8 @@ def stage_bytes(pixels: int, num_vert: int, views: int, stack_bytes: int, tex_by
         "texture_fwd": pixels * (24 + 4 * ct),
         "antialias_fwd": pixels * (16 + 8 * ct),
         "antialias_bwd": pixels * (16 + 12 * ct),
-        "texture_bwd": pixels * ((4 * ct + 24 + 16 + 32) if fused_interp else (48 + 4 * ct))
-                       + 2 * tex_bytes,
+        "texture_bwd": pixels * (48 + 4 * ct, 4 * ct + 24 + 16 + 32, 4 * ct + 24 + 8)[fused]
+                       + 2 * tex_bytes + (2 * pos_bytes if fused == 2 else 0),
         "mip_adjoint": 2 * stack_bytes + tex_bytes,
         "interpolate_bwd": pixels * (64 + 4 * c + 8 * d),
         "resolve_bwd": pixels * (8 + 32) + 2 * pos_bytes,
@@ -555,8 +557,8 @@ def run_ours(args) -> None:
     stack_bytes = int(tex_bytes * 4 / 3)
     pixels = views * res * res
     num_vert = verts.shape[0]
-    algo = stage_bytes(pixels, num_vert, views, stack_bytes - tex_bytes, tex_bytes,
-                       fused_interp="interpolate_bwd" not in stage_ms)
+    fused = 0 if "interpolate_bwd" in stage_ms else (1 if "resolve_bwd" in stage_ms else 2)
+    algo = stage_bytes(pixels, num_vert, views, stack_bytes - tex_bytes, tex_bytes, fused=fused)
     dominant = max(stage_ms, key=stage_ms.get)
     per_launch_ms = stage_ms[dominant] / max(1.0, stage_calls[dominant])
     # Stages launched several times per step (one mip level per launch) are costed per step.

@@ -105,9 +105,21 @@ class Chained(NamedTuple):
     grad_db: Tensor | None
 
 
+class RasterChain(NamedTuple):
+    """The rasterization part of a fused texture backward pass: the clip positions and keys the
+    rasterizer used, whether rast_db's gradient reaches the positions, and the position gradient
+    buffer to accumulate into."""
+
+    pos: Tensor
+    keys: Tensor
+    grad_db: bool
+    grad_pos: Tensor
+
+
 class ChainArgs(NamedTuple):
     """Arguments of the fused texture backward pass: the interpolation's tensors and the
-    attribute channels of uv (cu, cv) and of uv_da's two derivative pairs (du, dv)."""
+    attribute channels of uv (cu, cv) and of uv_da's two derivative pairs (du, dv); with
+    ``raster``, the rasterizer's backward pass runs in it as well."""
 
     attr: Tensor
     rast: Tensor
@@ -116,11 +128,15 @@ class ChainArgs(NamedTuple):
     cv: int
     du: int
     dv: int
+    raster: RasterChain | None = None
 
 
 # Whether 2D lookups of interpolated coordinates run the interpolation's backward pass for them
-# inside their own (tests switch it off to compare against the separate passes).
+# inside their own, and whether they run the rasterizer's backward pass there too when the
+# interpolation read rasterize's own rast (tests switch them off to compare against the
+# separate passes).
 FUSE_INTERPOLATION_BACKWARD = True
+FUSE_RASTERIZE_BACKWARD = True
 
 
 class Route:
@@ -128,11 +144,14 @@ class Route:
     :class:`CoordinatePort`, for uv and uv_da as requested at the forward pass."""
 
     def __init__(self, pending: dict, want_uv: bool, want_da: bool,
-                 port: CoordinatePort | None = None) -> None:
+                 port: CoordinatePort | None = None, pos_port: PositionPort | None = None) -> None:
         self.pending = pending
         self.want_uv = want_uv
         self.want_da = want_da
         self.port = port
+        # The rasterization that made the interpolation's rast, when the lookup depends on its
+        # sink (so that the rasterizer's backward pass runs and collects the position gradient).
+        self.pos_port = pos_port
 
     def deliver(self, key, uv_first, g_uv, da_first, g_da) -> None:
         self.pending[(torch._C._current_graph_task_id(), key)] = (uv_first, g_uv, da_first, g_da)
@@ -164,7 +183,28 @@ class Route:
         if want_da:
             du = port.diff_channels[da_spec[0] // 2]
             dv = port.diff_channels[da_spec[0] // 2 + 1]
-        return ChainArgs(attr, rast, tri, uv_spec[0], uv_spec[0] + 1, du, dv)
+        return ChainArgs(attr, rast, tri, uv_spec[0], uv_spec[0] + 1, du, dv,
+                         self._raster_chain(rast, tri, task))
+
+    def _raster_chain(self, rast, tri, task) -> RasterChain | None:
+        """The rasterization part when it applies: the interpolation read the very rast of a
+        rasterize call over the same tri, whose sink this lookup depends on. The position
+        gradient buffer is the one antialias already left for that rasterization in this backward
+        pass, or a new zeroed one left there."""
+        pp = self.pos_port
+        if not FUSE_RASTERIZE_BACKWARD or pp is None or pp.raster is None:
+            return None
+        r = pp.raster.tensors()
+        if r is None or getattr(rast, "_dr_pos_port", None) is not pp:
+            return None
+        pos, r_tri, keys, grad_db = r
+        if r_tri is not tri:
+            return None
+        grad_pos = next((v for k, v in pp.pending.items() if k[0] == task), None)
+        if grad_pos is None:
+            grad_pos = K.zeros(pos.shape, pos.device)
+            pp.pending[(task, id(self))] = grad_pos
+        return RasterChain(pos, keys, grad_db, grad_pos)
 
 
 def _take_pending(pending: dict) -> list:
@@ -187,12 +227,32 @@ class PositionPort:
     port is attached to rast; an antialias pass given that rast and the same ``pos`` tensor
     depends on ``sink`` instead of ``pos``, leaves its position gradient in ``pending``, and the
     rasterizer's backward pass accumulates its own scatter into that buffer.
+
+    It also describes the rasterization (``raster``, set by its forward pass) for a texture
+    lookup of coordinates interpolated from this rast, which can run the rasterizer's backward
+    pass inside its own (:meth:`Route.chain`).
     """
 
-    def __init__(self, sink: Tensor, pending: dict, pos: Tensor) -> None:
+    def __init__(self, sink: Tensor | None, pending: dict, pos: Tensor) -> None:
         self.sink = sink
         self.pending = pending
         self.pos = weakref.ref(pos)
+        self.raster: RasterGeometry | None = None
+
+
+class RasterGeometry:
+    """The rasterizer's clip positions (as its kernels read them), tri, keys and whether rast_db
+    is differentiable; its backward pass releases them here, like :class:`InterpGeometry`."""
+
+    def __init__(self, pos: Tensor, tri: Tensor, keys: Tensor, grad_db: bool) -> None:
+        self._tensors: tuple | None = (pos, tri, keys, grad_db)
+
+    def tensors(self):
+        """``(pos, tri, keys, grad_db)``, or None once released."""
+        return self._tensors
+
+    def release(self) -> None:
+        self._tensors = None
 
 
 def _collect(pending: dict, channels: int, da_channels: int, grad_out, grad_out_da):
@@ -233,14 +293,18 @@ class Rasterize(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, pos: Tensor, tri: Tensor, height: int, width: int, grad_db: bool,
-                prev_keys: Tensor | None, ranges: K.RangeTable | None, pending: dict):
+                prev_keys: Tensor | None, ranges: K.RangeTable | None, port: PositionPort):
         keys = K.raster_keys(pos, tri, height, width, prev_keys, ranges)
         rast, rast_db = K.resolve_fwd(pos, tri, keys)
         # Unused outputs (keys always, rast_db often) get no zero-filled gradient.
         ctx.set_materialize_grads(False)
-        ctx.save_for_backward(_saveable(pos), _saveable(tri), keys)
+        saved = (_saveable(pos), _saveable(tri), keys)
+        ctx.save_for_backward(*saved)
         ctx.grad_db = grad_db
-        ctx.pending = pending
+        ctx.pending = port.pending
+        ctx.geometry = None
+        if ranges is None:
+            ctx.geometry = port.raster = RasterGeometry(saved[0], saved[1], keys, grad_db)
         ctx.mark_non_differentiable(keys)
         if not grad_db:
             ctx.mark_non_differentiable(rast_db)
@@ -250,6 +314,8 @@ class Rasterize(torch.autograd.Function):
     @first_order("rasterize")
     def backward(ctx, grad_rast, grad_db, _grad_keys, grad_sink):
         pos, tri, keys = ctx.saved_tensors
+        if ctx.geometry is not None:
+            ctx.geometry.release()
         start = None
         if grad_sink is not None:
             for g in _take_pending(ctx.pending):
@@ -304,8 +370,9 @@ class Interpolate(torch.autograd.Function):
                 ctx.pending, ctx.channels, num_da, grad_out, grad_out_da)
         need_attr = ctx.needs_input_grad[0]
         c_rast = c_db = None
-        for c in chained:
-            c_rast = c.grad_rast if c_rast is None else c_rast + c.grad_rast
+        for c in chained:  # (None, None): the lookup went on through the rasterizer too
+            if c.grad_rast is not None:
+                c_rast = c.grad_rast if c_rast is None else c_rast + c.grad_rast
             if c.grad_db is not None:
                 c_db = c.grad_db if c_db is None else c_db + c.grad_db
         if chained and part is None and part_da is None and grad_out is None \
@@ -375,7 +442,7 @@ class Texture(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, uv_src, da_src, bias, mode: int, boundary: int, uv_spec, da_spec, route,
-                sink, *levels):
+                sink, pos_sink, *levels):
         levels = [lv.contiguous() for lv in levels]
         out = K.texture_fwd(list(levels), _take(uv_src, uv_spec), _take(da_src, da_spec), bias,
                             mode, boundary)
@@ -412,7 +479,7 @@ class Texture(torch.autograd.Function):
                 levels, _take(uv_src, uv_spec), _take(da_src, da_spec), bias, mode, boundary,
                 grad_out.contiguous(), want_uv, want_da, want_bias, grad_uv=g_uv_src,
                 grad_da=g_da_src, uv_first=uv_first, da_first=da_first)
-        level_grads = [g if need[9 + i] else None for i, g in enumerate(grads)]
+        level_grads = [g if need[10 + i] else None for i, g in enumerate(grads)]
         if route is not None:
             if chain is not None:
                 route.deliver_chained(id(ctx), g_rast, g_db)
@@ -420,10 +487,13 @@ class Texture(torch.autograd.Function):
                 route.deliver(id(ctx), uv_spec[0], g_uv,
                               None if da_spec is None else da_spec[0], g_da)
             sink = grad_out.new_empty(0) if need[8] else None
-            return (None, None, g_bias, None, None, None, None, None, sink, *level_grads)
+            pos_sink = grad_out.new_empty(0) if need[9] and chain is not None \
+                and chain.raster is not None else None
+            return (None, None, g_bias, None, None, None, None, None, sink, pos_sink,
+                    *level_grads)
         g_uv = g_uv_src if uv_spec is not None else g_uv
         g_da = g_da_src if da_spec is not None else g_da
-        return (g_uv, g_da, g_bias, None, None, None, None, None, None, *level_grads)
+        return (g_uv, g_da, g_bias, None, None, None, None, None, None, None, *level_grads)
 
 
 class TextureChain(torch.autograd.Function):
@@ -436,7 +506,7 @@ class TextureChain(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, uv_src, da_src, bias, mode: int, boundary: int, count: int, tex: Tensor,
-                uv_spec=None, da_spec=None, route=None, sink=None):
+                uv_spec=None, da_spec=None, route=None, sink=None, pos_sink=None):
         tex = tex.contiguous()
         levels = [tex, *K.mip_build(tex, count)]
         out = K.texture_fwd(levels, _take(uv_src, uv_spec), _take(da_src, da_spec), bias, mode,
@@ -496,10 +566,12 @@ class TextureChain(torch.autograd.Function):
                 route.deliver(id(ctx), uv_spec[0], g_uv,
                               None if da_spec is None else da_spec[0], g_da)
             sink = grad_out.new_empty(0) if need[10] else None
-            return None, None, g_bias, None, None, None, grad_tex, None, None, None, sink
+            pos_sink = grad_out.new_empty(0) if need[11] and chain is not None \
+                and chain.raster is not None else None
+            return None, None, g_bias, None, None, None, grad_tex, None, None, None, sink, pos_sink
         g_uv = g_uv_src if uv_spec is not None else g_uv
         g_da = g_da_src if da_spec is not None else g_da
-        return g_uv, g_da, g_bias, None, None, None, grad_tex, None, None, None, None
+        return g_uv, g_da, g_bias, None, None, None, grad_tex, None, None, None, None, None
 
 
 def _deliver(route, grad_pos):

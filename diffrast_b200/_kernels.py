@@ -471,29 +471,38 @@ def texture_bwd_chained(levels, uv, uv_da, bias, mode, boundary, grad_out, want_
     """Texture backward with the interpolation's backward for the coordinates fused in
     (``dr_texture_bwd_interp``): level gradients, the bias gradient as wanted, and in place of
     the coordinate gradients ``(grad_rast, grad_db)`` of the interpolation ``chain`` that made uv
-    and uv_da (``grad_db`` None unless ``want_da``)."""
+    and uv_da (``grad_db`` None unless ``want_da``). With ``chain.raster`` the rasterizer's
+    backward pass runs too (``dr_texture_bwd_resolve``): the position gradient is accumulated
+    into ``chain.raster.grad_pos`` and ``(None, None)`` stand for rast's and rast_db's."""
     batch, height, width = uv.shape[:3]
     channels = levels[0].shape[-1]
     grads, stride = _level_gradients(levels)
     rast = chain.rast
-    grad_rast = torch.empty(rast.shape, dtype=torch.float32, device=rast.device)
-    grad_db = torch.empty(rast.shape, dtype=torch.float32, device=rast.device) if want_da else None
     uv, uv_stride = pixel_rows(uv)
     uv_da, da_stride = pixel_rows(uv_da)
     grad_bias = torch.empty_like(bias) if want_bias else None
     hs, ws, bs = _level_tables(levels, boundary == 3)
     attr = chain.attr
-    N.check(
-        N.lib().dr_texture_bwd_interp(
-            N.pointer_array([lv.data_ptr() for lv in levels]),
-            N.pointer_array([g.data_ptr() for g in grads]), hs, ws, bs, len(levels), channels,
-            stride, uv.data_ptr(), uv_stride, N.ptr(uv_da), da_stride, N.ptr(bias), batch, height,
-            width, mode, boundary, grad_out.data_ptr(), N.ptr(grad_bias), rast.data_ptr(),
-            chain.tri.data_ptr(), chain.tri.shape[0], attr.data_ptr(), attr.shape[0],
-            attr.shape[1], attr.shape[2], chain.cu, chain.cv, chain.du, chain.dv,
-            grad_rast.data_ptr(), N.ptr(grad_db), N.stream(uv.device)),
-        "dr_texture_bwd_interp",
-    )  # fmt: skip
+    common = (N.pointer_array([lv.data_ptr() for lv in levels]),
+              N.pointer_array([g.data_ptr() for g in grads]), hs, ws, bs, len(levels), channels,
+              stride, uv.data_ptr(), uv_stride, N.ptr(uv_da), da_stride, N.ptr(bias), batch,
+              height, width, mode, boundary, grad_out.data_ptr(), N.ptr(grad_bias),
+              rast.data_ptr(), chain.tri.data_ptr(), chain.tri.shape[0], attr.data_ptr(),
+              attr.shape[0], attr.shape[1], attr.shape[2], chain.cu, chain.cv, chain.du,
+              chain.dv)  # fmt: skip
+    grad_rast = grad_db = None
+    if chain.raster is None:
+        grad_rast = torch.empty(rast.shape, dtype=torch.float32, device=rast.device)
+        grad_db = torch.empty(rast.shape, dtype=torch.float32, device=rast.device) if want_da else None
+        N.check(N.lib().dr_texture_bwd_interp(*common, grad_rast.data_ptr(), N.ptr(grad_db),
+                                              N.stream(uv.device)), "dr_texture_bwd_interp")
+    else:
+        r = chain.raster
+        pos = r.pos
+        N.check(N.lib().dr_texture_bwd_resolve(*common, r.keys.data_ptr(), pos.data_ptr(),
+                                               pos.shape[0], pos.shape[1],
+                                               int(r.grad_db and want_da), r.grad_pos.data_ptr(),
+                                               N.stream(uv.device)), "dr_texture_bwd_resolve")
     if stride != channels and not keep_padded:
         grads = [g[..., :channels].contiguous() for g in grads]
     return grads, grad_rast, grad_db, grad_bias

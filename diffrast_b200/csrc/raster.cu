@@ -21,6 +21,7 @@
 #include <cstdint>
 
 #include "common.cuh"
+#include "resolve_adjoint.cuh"
 #include "warp_reduce.cuh"
 
 namespace dr {
@@ -922,12 +923,6 @@ __global__ void __launch_bounds__(kResolveThreads) resolve_fwd_kernel(
   }
 }
 
-__device__ __forceinline__ void cross3(const float u[3], const float v[3], float out[3]) {
-  out[0] = u[1] * v[2] - u[2] * v[1];
-  out[1] = u[2] * v[0] - u[0] * v[2];
-  out[2] = u[0] * v[1] - u[1] * v[0];
-}
-
 __global__ void __launch_bounds__(256) resolve_bwd_kernel(
     const float* __restrict__ pos, const int* __restrict__ tri, const long long* __restrict__ keys,
     int b0, int row0, long long pos_stride, const Bounds bd, int height, int width,
@@ -945,82 +940,9 @@ __global__ void __launch_bounds__(256) resolve_bwd_kernel(
   }
   float gv[3][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
   if (q.covered) {
-    const float w[3] = {q.v0.w, q.v1.w, q.v2.w};
-    const float z[3] = {q.v0.z, q.v1.z, q.v2.z};
-    const float a[3] = {q.v0.x - q.px * w[0], q.v1.x - q.px * w[1], q.v2.x - q.px * w[2]};
-    const float c[3] = {q.v0.y - q.py * w[0], q.v1.y - q.py * w[1], q.v2.y - q.py * w[2]};
-    float e[3];
-    cross3(a, c, e);
-    const float s = e[0] + e[1] + e[2];
-    const float inv_s = 1.0f / s;
-    const float b[3] = {e[0] * inv_s, e[1] * inv_s, e[2] * inv_s};
-    const float ew = e[0] * w[0] + e[1] * w[1] + e[2] * w[2];
-    const float inv_ew = 1.0f / ew;
-    const float depth = (e[0] * z[0] + e[1] * z[1] + e[2] * z[2]) * inv_ew;
     const float4 gr = grad_rast[p];
-    float gb[3] = {gr.x, gr.y, 0.0f};
-    float gs = 0.0f;
-    float ga[3] = {0.f, 0.f, 0.f}, gc[3] = {0.f, 0.f, 0.f}, gw[3] = {0.f, 0.f, 0.f};
-    if (grad_db != nullptr) {
-      float dx[3], dy[3];
-      cross3(c, w, dx);
-      cross3(w, a, dy);
-      const float sx = dx[0] + dx[1] + dx[2], sy = dy[0] + dy[1] + dy[2];
-      const float4 gd = grad_db[p];
-      const float scale_x = 2.0f / static_cast<float>(width), scale_y = 2.0f / static_cast<float>(height);
-      // Gradients of db_dx_k = (dx_k - b_k sx) / s and db_dy_k, k = 0, 1.
-      const float gbx[3] = {gd.x * scale_x, gd.z * scale_x, 0.0f};
-      const float gby[3] = {gd.y * scale_y, gd.w * scale_y, 0.0f};
-      const float dbx0 = (dx[0] - b[0] * sx) * inv_s, dbx1 = (dx[1] - b[1] * sx) * inv_s;
-      const float dby0 = (dy[0] - b[0] * sy) * inv_s, dby1 = (dy[1] - b[1] * sy) * inv_s;
-      const float shared_x = (gbx[0] * b[0] + gbx[1] * b[1]) * inv_s;
-      const float shared_y = (gby[0] * b[0] + gby[1] * b[1]) * inv_s;
-      float gdx[3], gdy[3];
-      for (int k = 0; k < 3; ++k) {
-        gdx[k] = gbx[k] * inv_s - shared_x;
-        gdy[k] = gby[k] * inv_s - shared_y;
-      }
-      gb[0] -= (gbx[0] * sx + gby[0] * sy) * inv_s;
-      gb[1] -= (gbx[1] * sx + gby[1] * sy) * inv_s;
-      gs -= (gbx[0] * dbx0 + gbx[1] * dbx1 + gby[0] * dby0 + gby[1] * dby1) * inv_s;
-      // dx = c x w: dL/dc += w x gdx, dL/dw += gdx x c. dy = w x a: dL/dw += a x gdy,
-      // dL/da += gdy x w.
-      float t[3];
-      cross3(w, gdx, t);
-      for (int k = 0; k < 3; ++k) gc[k] += t[k];
-      cross3(gdx, c, t);
-      for (int k = 0; k < 3; ++k) gw[k] += t[k];
-      cross3(a, gdy, t);
-      for (int k = 0; k < 3; ++k) gw[k] += t[k];
-      cross3(gdy, w, t);
-      for (int k = 0; k < 3; ++k) ga[k] += t[k];
-    }
-    // b = e / s with s = sum(e).
-    gs -= (gb[0] * b[0] + gb[1] * b[1] + gb[2] * b[2]) * inv_s;
-    float ge[3];
-    for (int k = 0; k < 3; ++k) ge[k] = gb[k] * inv_s + gs;
-    // depth = (e . z) / (e . w).
-    const float g_ew = gr.z * inv_ew;
-    float gz[3];
-    for (int k = 0; k < 3; ++k) {
-      ge[k] += g_ew * (z[k] - depth * w[k]);
-      gz[k] = g_ew * e[k];
-      gw[k] -= g_ew * depth * e[k];
-    }
-    // e = a x c.
-    float t[3];
-    cross3(c, ge, t);
-    for (int k = 0; k < 3; ++k) ga[k] += t[k];
-    cross3(ge, a, t);
-    for (int k = 0; k < 3; ++k) gc[k] += t[k];
-    // a = x - px w, c = y - py w.
-    for (int k = 0; k < 3; ++k) {
-      gw[k] -= q.px * ga[k] + q.py * gc[k];
-      gv[k][0] = ga[k];
-      gv[k][1] = gc[k];
-      gv[k][2] = gz[k];
-      gv[k][3] = gw[k];
-    }
+    const float4 gd = grad_db != nullptr ? grad_db[p] : make_float4(0.f, 0.f, 0.f, 0.f);
+    resolve_adjoint(q.v0, q.v1, q.v2, q.px, q.py, gr, grad_db != nullptr, gd, width, height, gv);
   }
   const long long base = static_cast<long long>(q.b) * pos_stride;
   // Lanes showing the same triangle (a warp covers 32 pixels of one row) sum their vertex

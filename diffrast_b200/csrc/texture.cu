@@ -19,6 +19,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "resolve_adjoint.cuh"
 #include "warp_reduce.cuh"
 
 namespace dr {
@@ -610,25 +611,51 @@ struct InterpChain {
   int cu, cv, du, dv;
   float4* grad_rast;
   float4* grad_db;              // null when uv_da carries no gradient
+  // The rasterizer's backward pass as well (grad_pos non-null; grad_rast and grad_db are then
+  // null): the pixel's triangle comes from the rasterizer's keys, and the gradients of the
+  // triangle's clip-space vertices for this pixel's rast / rast_db gradients are added to
+  // grad_pos, warp-aggregated, as the rasterizer's backward kernel would add them.
+  const long long* keys;
+  const float* pos;             // [views or 1, pos_num_vert, 4]
+  long long pos_view_stride;    // vertices between the views' positions (0: shared)
+  long long pos_num_vert;
+  float* grad_pos;
+  bool resolve_db;              // rast_db's gradient reaches the positions
 };
 
 // Gradients of rast and rast_db at pixel p from those of the lookup's coordinates, with the
 // arithmetic and order of the interpolation backward kernel given the same coordinate
 // gradients: d out_c / d b0 = a0_c - a2_c, d out_c / d b1 = a1_c - a2_c, and the derivative
-// channels likewise with rast_db's (d b / dX, d b / dY).
+// channels likewise with rast_db's (d b / dX, d b / dY). With c.grad_pos they go on through the
+// rasterizer's backward pass into the positions; then every lane of the warp must call this
+// (inside = false for pixels past the image).
+template <bool RESOLVE>
 __device__ __forceinline__ void chain_interpolation(const InterpChain& c, long long p,
-                                                    long long view, const float (&g_uv)[2],
+                                                    long long view, int col, int row, int width,
+                                                    int height, bool inside,
+                                                    const float (&g_uv)[2],
                                                     const float (&g_da)[4]) {
-  const float4 r = __ldcs(c.rast + p);
-  const int t = rast_triangle(r.w, c.num_tri);
+  int t = -1;
+  if (inside) {
+    if (RESOLVE) {
+      const long long key = __ldcs(c.keys + p);
+      t = key != kEmptyKey ? static_cast<int>(key & 0xFFFFFFFFLL) : -1;
+    } else {
+      t = rast_triangle(__ldcs(c.rast + p).w, c.num_tri);
+    }
+  }
   float gu = 0.0f, gv = 0.0f;
   float g_dudx = 0.0f, g_dudy = 0.0f, g_dvdx = 0.0f, g_dvdy = 0.0f;
+  long long i0 = 0, i1 = 0, i2 = 0;
   if (t >= 0) {
     const int* vt = c.tri + 3 * static_cast<long long>(t);
+    i0 = __ldg(vt);
+    i1 = __ldg(vt + 1);
+    i2 = __ldg(vt + 2);
     const float* base = c.attr + view * c.attr_view_stride;
-    const float* a0 = base + checked_index(__ldg(vt), c.num_vert, kSiteVertex) * c.attr_channels;
-    const float* a1 = base + checked_index(__ldg(vt + 1), c.num_vert, kSiteVertex) * c.attr_channels;
-    const float* a2 = base + checked_index(__ldg(vt + 2), c.num_vert, kSiteVertex) * c.attr_channels;
+    const float* a0 = base + checked_index(i0, c.num_vert, kSiteVertex) * c.attr_channels;
+    const float* a1 = base + checked_index(i1, c.num_vert, kSiteVertex) * c.attr_channels;
+    const float* a2 = base + checked_index(i2, c.num_vert, kSiteVertex) * c.attr_channels;
     const int ch[2] = {c.cu, c.cv};
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
@@ -636,7 +663,7 @@ __device__ __forceinline__ void chain_interpolation(const InterpChain& c, long l
       gu += g_uv[i] * (x0 - x2);
       gv += g_uv[i] * (x1 - x2);
     }
-    if (c.grad_db != nullptr) {
+    if (c.grad_db != nullptr || c.resolve_db) {
       const int dch[2] = {c.du, c.dv};
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
@@ -651,8 +678,42 @@ __device__ __forceinline__ void chain_interpolation(const InterpChain& c, long l
       }
     }
   }
-  __stcs(c.grad_rast + p, make_float4(gu, gv, 0.0f, 0.0f));
-  if (c.grad_db != nullptr) __stcs(c.grad_db + p, make_float4(g_dudx, g_dudy, g_dvdx, g_dvdy));
+  if constexpr (!RESOLVE) {
+    if (!inside) return;
+    __stcs(c.grad_rast + p, make_float4(gu, gv, 0.0f, 0.0f));
+    if (c.grad_db != nullptr) __stcs(c.grad_db + p, make_float4(g_dudx, g_dudy, g_dvdx, g_dvdy));
+    return;
+  } else {
+  float gvert[3][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  const long long pbase = view * c.pos_view_stride;
+  if (t >= 0) {
+    i0 = checked_index(i0, c.pos_num_vert, kSiteVertex);
+    i1 = checked_index(i1, c.pos_num_vert, kSiteVertex);
+    i2 = checked_index(i2, c.pos_num_vert, kSiteVertex);
+    const Vert v0 = load_vert(c.pos, pbase + i0), v1 = load_vert(c.pos, pbase + i1),
+               v2 = load_vert(c.pos, pbase + i2);
+    resolve_adjoint(v0, v1, v2, pixel_centre(col, width), pixel_centre(row, height),
+                    make_float4(gu, gv, 0.0f, 0.0f), c.resolve_db,
+                    make_float4(g_dudx, g_dudy, g_dvdx, g_dvdy), width, height, gvert);
+  }
+  // Lanes showing the same triangle (a warp covers 16 x 2 pixels of one view) sum their vertex
+  // gradients first; one of them adds the sums with three vector reductions.
+  const unsigned act = __ballot_sync(0xffffffffu, t >= 0);
+  if (act == 0u) return;
+  const unsigned lane = threadIdx.x & 31u;
+  unsigned peers = 1u << lane;
+  if (t >= 0) peers = __match_any_sync(act, t);
+  float v[12];
+#pragma unroll
+  for (int k = 0; k < 3; ++k)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) v[4 * k + q] = gvert[k][q];
+  segmented_sum<12>(peers, v);
+  if (t < 0 || (peers & ((1u << lane) - 1u)) != 0u) return;
+  red_add_v4(c.grad_pos + (pbase + i0) * 4, v[0], v[1], v[2], v[3]);
+  red_add_v4(c.grad_pos + (pbase + i1) * 4, v[4], v[5], v[6], v[7]);
+  red_add_v4(c.grad_pos + (pbase + i2) * 4, v[8], v[9], v[10], v[11]);
+  }
 }
 
 // A quad that a whole warp added to (lane 0 keeps it): pixels that all read the same four texels
@@ -698,7 +759,9 @@ __device__ __forceinline__ void flush_quad(const Levels& L, HotQuad& h, int chan
 // reduction and one lane issues a single reduction per texel: a 16-byte vector reduction into a
 // gradient level padded to 4 channels (grad_stride 4), scalar reductions otherwise. RGB: exactly
 // three channels into a padded level, so the lanes reduce 3 values per tap instead of 4.
-template <int MODE, int B, bool RGB>
+// CHAIN: 0 coordinate gradients written out, 1 chained through the interpolation (grad_rast /
+// grad_db), 2 through the rasterizer as well (grad_pos).
+template <int MODE, int B, bool RGB, int CHAIN>
 __device__ __forceinline__ void texture_bwd_tile(
     const Levels& L, int channels, int grad_stride, const float* __restrict__ uv,
     const float* __restrict__ uv_da, const float* __restrict__ bias, const Strides& st, int height,
@@ -844,9 +907,12 @@ __device__ __forceinline__ void texture_bwd_tile(
     }
   }
   }
-  if (!inside) return;
+  // With the interpolation (and rasterizer) chained in, every lane takes part in the epilogue's
+  // warp reductions, pixels past the image included (inside = false; they read and write nothing).
+  constexpr bool chained = CHAIN != 0;
+  if (!inside && !chained) return;
   const bool coord_grads = grad_uv != nullptr || grad_uv_da != nullptr || grad_bias != nullptr ||
-                           chain.grad_rast != nullptr;
+                           chained;
   if (!coord_grads) return;
   float g_fx_lo = 0.f, g_fy_lo = 0.f, g_fx_hi = 0.f, g_fy_hi = 0.f, g_frac = 0.f;
   if (live && MODE != DR_FILTER_NEAREST) {
@@ -901,18 +967,19 @@ __device__ __forceinline__ void texture_bwd_tile(
     const float top = static_cast<float>(L.num_levels - 1);
     if (k.lod_raw >= 0.0f && k.lod_raw <= top) g_lod = g_frac;
   }
-  if (grad_bias != nullptr) grad_bias[p] = g_lod;
+  if (grad_bias != nullptr && inside) grad_bias[p] = g_lod;
   float g_da[4] = {0.f, 0.f, 0.f, 0.f};
-  if (k.has_da && g_lod != 0.0f) level_of_detail_bwd(k.da, L.h[0], L.w[0], g_lod, g_da);
+  if (live && k.has_da && g_lod != 0.0f) level_of_detail_bwd(k.da, L.h[0], L.w[0], g_lod, g_da);
   if (B == DR_BOUNDARY_CUBE) {
     float g_dir[3] = {0.f, 0.f, 0.f}, g_dir_da[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (live) cube_project_bwd(k.cube, g_u, g_v, k.has_da ? g_da : nullptr, g_dir, g_dir_da);
-    if (grad_uv != nullptr) write_record<3>(grad_uv, p, gst.uv, gst.uv_first, g_dir);
-    if (grad_uv_da != nullptr) write_record<6>(grad_uv_da, p, gst.uv_da, gst.da_first, g_dir_da);
+    if (grad_uv != nullptr && inside) write_record<3>(grad_uv, p, gst.uv, gst.uv_first, g_dir);
+    if (grad_uv_da != nullptr && inside)
+      write_record<6>(grad_uv_da, p, gst.uv_da, gst.da_first, g_dir_da);
   } else {
     const float g_uv[2] = {g_u, g_v};
-    if (chain.grad_rast != nullptr) {
-      chain_interpolation(chain, p, view, g_uv, g_da);
+    if constexpr (chained) {
+      chain_interpolation<CHAIN == 2>(chain, p, view, col, row, width, height, inside, g_uv, g_da);
       return;
     }
     if (grad_uv != nullptr) write_record<2>(grad_uv, p, gst.uv, gst.uv_first, g_uv);
@@ -922,7 +989,7 @@ __device__ __forceinline__ void texture_bwd_tile(
 
 // Persistent blocks walk the 16 x 16 pixel tiles of all views; each warp keeps its hot quad across
 // the tiles it visits and flushes it at the end.
-template <int MODE, int B, bool RGB>
+template <int MODE, int B, bool RGB, int CHAIN>
 __global__ void __launch_bounds__(256, B == DR_BOUNDARY_CUBE ? 2 : 3) texture_bwd_kernel(
     const Levels L, int channels, int grad_stride, const float* __restrict__ uv,
     const float* __restrict__ uv_da, const float* __restrict__ bias, const Strides st, int height,
@@ -943,7 +1010,7 @@ __global__ void __launch_bounds__(256, B == DR_BOUNDARY_CUBE ? 2 : 3) texture_bw
     const long long ty = in_view / tiles_x;
     const int col = static_cast<int>((in_view - ty * tiles_x) * 16) + (threadIdx.x & 15);
     const int row = static_cast<int>(ty * 16) + (threadIdx.x >> 4);
-    texture_bwd_tile<MODE, B, RGB>(L, channels, grad_stride, uv, uv_da, bias, st, height, width,
+    texture_bwd_tile<MODE, B, RGB, CHAIN>(L, channels, grad_stride, uv, uv_da, bias, st, height, width,
                                    grad_out, grad_uv, grad_uv_da, grad_bias, gst, chain, col,
                                    row, view, hot[warp][held], hot[warp][held ^ 1], pending);
     if (pending) {  // lane 0 only: the new quad replaces the held one
@@ -1180,10 +1247,23 @@ void launch_bwd(const Levels& L, int channels, int grad_stride, const float* uv,
                                                       grad_uv_da, grad_bias, gst, chain, tiles_x,
                                                       tiles_per_view, tiles);
   };
-  if (quads && channels == 3 && grad_stride == 4)
-    launch(texture_bwd_kernel<MODE, B, quads>);
+  const bool rgb = quads && channels == 3 && grad_stride == 4;
+  if constexpr (B != DR_BOUNDARY_CUBE && MODE != DR_FILTER_NEAREST) {
+    if (chain.grad_pos != nullptr) {
+      if (rgb) launch(texture_bwd_kernel<MODE, B, true, 2>);
+      else launch(texture_bwd_kernel<MODE, B, false, 2>);
+      return;
+    }
+    if (chain.grad_rast != nullptr) {
+      if (rgb) launch(texture_bwd_kernel<MODE, B, true, 1>);
+      else launch(texture_bwd_kernel<MODE, B, false, 1>);
+      return;
+    }
+  }
+  if (rgb)
+    launch(texture_bwd_kernel<MODE, B, quads, 0>);
   else
-    launch(texture_bwd_kernel<MODE, B, false>);
+    launch(texture_bwd_kernel<MODE, B, false, 0>);
 }
 
 template <int B, typename F>
@@ -1340,15 +1420,14 @@ extern "C" int dr_texture_bwd(const float* const* level_ptr, float* const* grad_
                           grad_uv_da_stride, grad_uv_da_first, grad_bias, none, stream);
 }
 
-extern "C" int dr_texture_bwd_interp(
-    const float* const* level_ptr, float* const* grad_level_ptr, const int32_t* level_h,
-    const int32_t* level_w, const int64_t* level_batch_stride, int32_t num_levels,
-    int32_t channels, int32_t grad_channel_stride, const float* uv, int64_t uv_stride,
-    const float* uv_da, int64_t uv_da_stride, const float* bias, int64_t batch, int32_t height,
-    int32_t width, int32_t filter_mode, int32_t boundary_mode, const float* grad_out,
-    float* grad_bias, const float* rast, const int32_t* tri, int64_t num_tri, const float* attr,
-    int64_t attr_batch, int64_t num_vert, int32_t attr_channels, int32_t cu, int32_t cv,
-    int32_t du, int32_t dv, float* grad_rast, float* grad_db, void* stream) {
+namespace {
+
+// The interpolation part of an InterpChain from the entry points' arguments, validated.
+int interp_chain(int32_t filter_mode, int32_t boundary_mode, int64_t batch, int32_t height,
+                 int32_t width, const float* uv_da, const float* rast, const int32_t* tri,
+                 int64_t num_tri, const float* attr, int64_t attr_batch, int64_t num_vert,
+                 int32_t attr_channels, int32_t cu, int32_t cv, int32_t du, int32_t dv,
+                 bool want_db, InterpChain& chain) {
   if (boundary_mode == DR_BOUNDARY_CUBE || filter_mode < 1 || filter_mode > 3)
     return DR_ERR_INVALID_ARGUMENT;
   if (batch < 0 || height < 0 || width < 0 || num_tri < 0 || num_tri >= (1LL << 31) ||
@@ -1356,18 +1435,16 @@ extern "C" int dr_texture_bwd_interp(
     return DR_ERR_INVALID_ARGUMENT;
   if (attr_batch != 1 && attr_batch != batch) return DR_ERR_INVALID_ARGUMENT;
   if (cu < 0 || cu >= attr_channels || cv < 0 || cv >= attr_channels) return DR_ERR_INVALID_ARGUMENT;
-  if (grad_db != nullptr && (uv_da == nullptr || filter_mode != 3 || du < 0 ||
-                             du >= attr_channels || dv < 0 || dv >= attr_channels))
+  if (want_db && (uv_da == nullptr || filter_mode != 3 || du < 0 || du >= attr_channels ||
+                  dv < 0 || dv >= attr_channels))
     return DR_ERR_INVALID_ARGUMENT;
-  const long long total = batch * static_cast<long long>(height) * width;
-  if (total > 0) {
-    const uintptr_t align = reinterpret_cast<uintptr_t>(rast) | reinterpret_cast<uintptr_t>(grad_rast) |
-                            reinterpret_cast<uintptr_t>(grad_db);
-    if (rast == nullptr || grad_rast == nullptr || (align & 15u) != 0) return DR_ERR_INVALID_ARGUMENT;
+  if (batch * static_cast<long long>(height) * width > 0) {
+    if (rast == nullptr || (reinterpret_cast<uintptr_t>(rast) & 15u) != 0)
+      return DR_ERR_INVALID_ARGUMENT;
     if (num_tri > 0 && tri == nullptr) return DR_ERR_INVALID_ARGUMENT;
     if (num_vert > 0 && attr == nullptr) return DR_ERR_INVALID_ARGUMENT;
   }
-  InterpChain chain;
+  chain = InterpChain{};
   chain.rast = reinterpret_cast<const float4*>(rast);
   chain.tri = tri;
   chain.attr = attr;
@@ -1379,8 +1456,65 @@ extern "C" int dr_texture_bwd_interp(
   chain.cv = cv;
   chain.du = du;
   chain.dv = dv;
+  return DR_OK;
+}
+
+}  // namespace
+
+extern "C" int dr_texture_bwd_interp(
+    const float* const* level_ptr, float* const* grad_level_ptr, const int32_t* level_h,
+    const int32_t* level_w, const int64_t* level_batch_stride, int32_t num_levels,
+    int32_t channels, int32_t grad_channel_stride, const float* uv, int64_t uv_stride,
+    const float* uv_da, int64_t uv_da_stride, const float* bias, int64_t batch, int32_t height,
+    int32_t width, int32_t filter_mode, int32_t boundary_mode, const float* grad_out,
+    float* grad_bias, const float* rast, const int32_t* tri, int64_t num_tri, const float* attr,
+    int64_t attr_batch, int64_t num_vert, int32_t attr_channels, int32_t cu, int32_t cv,
+    int32_t du, int32_t dv, float* grad_rast, float* grad_db, void* stream) {
+  InterpChain chain;
+  const int status = interp_chain(filter_mode, boundary_mode, batch, height, width, uv_da, rast,
+                                  tri, num_tri, attr, attr_batch, num_vert, attr_channels, cu, cv,
+                                  du, dv, grad_db != nullptr, chain);
+  if (status != DR_OK) return status;
+  const uintptr_t align = reinterpret_cast<uintptr_t>(grad_rast) | reinterpret_cast<uintptr_t>(grad_db);
+  if (batch * static_cast<long long>(height) * width > 0 && (grad_rast == nullptr || (align & 15u) != 0))
+    return DR_ERR_INVALID_ARGUMENT;
   chain.grad_rast = reinterpret_cast<float4*>(grad_rast);
   chain.grad_db = reinterpret_cast<float4*>(grad_db);
+  return texture_bwd_impl(level_ptr, grad_level_ptr, level_h, level_w, level_batch_stride,
+                          num_levels, channels, grad_channel_stride, uv, uv_stride, uv_da,
+                          uv_da_stride, bias, batch, height, width, filter_mode, boundary_mode,
+                          grad_out, nullptr, 0, -1, nullptr, 0, -1, grad_bias, chain, stream);
+}
+
+extern "C" int dr_texture_bwd_resolve(
+    const float* const* level_ptr, float* const* grad_level_ptr, const int32_t* level_h,
+    const int32_t* level_w, const int64_t* level_batch_stride, int32_t num_levels,
+    int32_t channels, int32_t grad_channel_stride, const float* uv, int64_t uv_stride,
+    const float* uv_da, int64_t uv_da_stride, const float* bias, int64_t batch, int32_t height,
+    int32_t width, int32_t filter_mode, int32_t boundary_mode, const float* grad_out,
+    float* grad_bias, const float* rast, const int32_t* tri, int64_t num_tri, const float* attr,
+    int64_t attr_batch, int64_t num_vert, int32_t attr_channels, int32_t cu, int32_t cv,
+    int32_t du, int32_t dv, const int64_t* keys, const float* pos, int64_t pos_batch,
+    int64_t pos_num_vert, int32_t rast_db_gradient, float* grad_pos, void* stream) {
+  const bool want_db = rast_db_gradient != 0;
+  InterpChain chain;
+  const int status = interp_chain(filter_mode, boundary_mode, batch, height, width, uv_da, rast,
+                                  tri, num_tri, attr, attr_batch, num_vert, attr_channels, cu, cv,
+                                  du, dv, want_db, chain);
+  if (status != DR_OK) return status;
+  if (pos_batch != 1 && pos_batch != batch) return DR_ERR_INVALID_ARGUMENT;
+  if (pos_num_vert < 0 || num_tri > (1LL << 24)) return DR_ERR_INVALID_ARGUMENT;
+  if (batch * static_cast<long long>(height) * width > 0) {
+    const uintptr_t align = reinterpret_cast<uintptr_t>(pos) | reinterpret_cast<uintptr_t>(grad_pos);
+    if (keys == nullptr || pos == nullptr || grad_pos == nullptr || (align & 15u) != 0)
+      return DR_ERR_INVALID_ARGUMENT;
+  }
+  chain.keys = reinterpret_cast<const long long*>(keys);
+  chain.pos = pos;
+  chain.pos_view_stride = pos_batch == 1 ? 0 : pos_num_vert;
+  chain.pos_num_vert = pos_num_vert;
+  chain.grad_pos = grad_pos;
+  chain.resolve_db = want_db;
   return texture_bwd_impl(level_ptr, grad_level_ptr, level_h, level_w, level_batch_stride,
                           num_levels, channels, grad_channel_stride, uv, uv_stride, uv_da,
                           uv_da_stride, bias, batch, height, width, filter_mode, boundary_mode,

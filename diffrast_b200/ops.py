@@ -82,16 +82,18 @@ def rasterize_layer(
         empty = pos.new_zeros(views, height, width, 4)
         keys = torch.full((views, height, width), EMPTY_KEY, dtype=torch.int64, device=pos.device)
         return empty, empty.clone(), keys
-    pending: dict = {}
+    port = F.PositionPort(None, {}, pos)
     with torch.cuda.device(pos.device):
         rast, rast_db, keys, sink = F.Rasterize.apply(
             K.aligned(pos if ranges is None else pos[None]), tri.contiguous(), height, width,
-            bool(grad_db), previous, ranges, pending,
+            bool(grad_db), previous, ranges, port,
         )
     if sink.requires_grad and ranges is None:
         # An antialias pass over this rast and the same pos hands its position gradient to this
-        # rasterization's backward pass (see _functions.PositionPort).
-        rast._dr_pos_port = F.PositionPort(sink, pending, pos)
+        # rasterization's backward pass, and a lookup of coordinates interpolated from this rast
+        # may run that backward pass itself (see _functions.PositionPort).
+        port.sink = sink
+        rast._dr_pos_port = port
     return rast, rast_db, keys
 
 
@@ -328,11 +330,12 @@ def texture(
         uv_src, uv_spec = _channel_slice(uv)
         da_src, da_spec = _channel_slice(uv_da)
         route, sink, uv_src, uv_spec, da_src, da_spec = _route(uv_src, uv_spec, da_src, da_spec,
-                                                               _needs_grad(uv_da))
+                                                               _needs_grad(uv_da), cube)
         with torch.cuda.device(uv.device):
             return F.TextureChain.apply(
                 uv_src, da_src, None if mip_level_bias is None else mip_level_bias.contiguous(),
                 mode, _BOUNDARY_INDEX[boundary_mode], count, tex, uv_spec, da_spec, route, sink,
+                _pos_sink(route),
             )
     if mipmapped:
         if given is None:
@@ -354,11 +357,12 @@ def texture(
     uv_src, uv_spec = _channel_slice(uv)
     da_src, da_spec = _channel_slice(uv_da)
     route, sink, uv_src, uv_spec, da_src, da_spec = _route(uv_src, uv_spec, da_src, da_spec,
-                                                           _needs_grad(uv_da))
+                                                           _needs_grad(uv_da), cube)
     with torch.cuda.device(uv.device):
         return F.Texture.apply(
             uv_src, da_src, None if mip_level_bias is None else mip_level_bias.contiguous(), mode,
-            _BOUNDARY_INDEX[boundary_mode], uv_spec, da_spec, route, sink, *levels,
+            _BOUNDARY_INDEX[boundary_mode], uv_spec, da_spec, route, sink, _pos_sink(route),
+            *levels,
         )
 
 
@@ -366,7 +370,7 @@ def _needs_grad(t: Tensor | None) -> bool:
     return t is not None and t.requires_grad and torch.is_grad_enabled()
 
 
-def _route(uv_src, uv_spec, da_src, da_spec, has_da: bool):
+def _route(uv_src, uv_spec, da_src, da_spec, has_da: bool, cube: bool = False):
     """``(route, sink, uv_src, uv_spec, da_src, da_spec)`` for a lookup whose uv (and uv_da, if
     given) are the outputs of one :func:`interpolate` call or channel slices of them: its
     coordinate gradients then go back through that call's port, and uv_src / da_src enter the
@@ -383,9 +387,22 @@ def _route(uv_src, uv_spec, da_src, da_spec, has_da: bool):
         uv_spec = (0, uv_src.shape[-1])
     if has_da and da_spec is None:
         da_spec = (0, da_src.shape[-1])
-    route = F.Route(port.pending, want_uv=True, want_da=has_da, port=port)
+    # A 2D lookup of coordinates interpolated from rasterize's own rast also depends on that
+    # rasterization's sink, so that its backward pass may run the rasterizer's backward pass
+    # (the rasterizer's backward pass then collects the position gradient it leaves).
+    pos_port = None
+    geometry = port.geometry.tensors() if port.geometry is not None and not cube else None
+    if geometry is not None:
+        candidate = getattr(geometry[1], "_dr_pos_port", None)
+        if candidate is not None and candidate.sink is not None and candidate.sink.requires_grad:
+            pos_port = candidate
+    route = F.Route(port.pending, want_uv=True, want_da=has_da, port=port, pos_port=pos_port)
     return (route, port.sink, uv_src.detach(), uv_spec,
             None if da_src is None else da_src.detach(), da_spec)
+
+
+def _pos_sink(route) -> Tensor | None:
+    return None if route is None or route.pos_port is None else route.pos_port.sink
 
 
 

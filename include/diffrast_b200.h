@@ -287,6 +287,29 @@ int dr_mip_downsample_bwd(const float* grad_dst, int64_t images, int32_t h, int3
                           int32_t channels, float* grad_src, float* out, int32_t out_channels,
                           void* stream);
 
+/* dr_texture_bwd_interp with the rasterizer's backward pass fused in as well (no counterpart in
+ * the reference). rast, tri and pos must be what dr_raster_setup / dr_raster_resolve_fwd made
+ * keys and rast from (pos [pos_batch, pos_num_vert, 4], pos_batch 1 or batch; at most 2^24
+ * triangles), and attr's rows are those of the same vertex indices. In place of grad_rast and
+ * grad_db, the gradients of the pixel's triangle's clip-space vertices are ACCUMULATED into
+ * grad_pos (like pos) with warp-aggregated vector reductions -- what dr_raster_resolve_bwd would
+ * add for the rast / rast_db gradients dr_texture_bwd_interp would write (rast_db's only when
+ * rast_db_gradient is nonzero, which needs filter mode 3 and uv_da). The pixel's triangle is read
+ * from keys. pos and grad_pos 16-byte aligned. */
+int dr_texture_bwd_resolve(const float* const* level_ptr, float* const* grad_level_ptr,
+                           const int32_t* level_h, const int32_t* level_w,
+                           const int64_t* level_batch_stride, int32_t num_levels,
+                           int32_t channels, int32_t grad_channel_stride, const float* uv,
+                           int64_t uv_stride, const float* uv_da, int64_t uv_da_stride,
+                           const float* bias, int64_t batch, int32_t height, int32_t width,
+                           int32_t filter_mode, int32_t boundary_mode, const float* grad_out,
+                           float* grad_bias, const float* rast, const int32_t* tri,
+                           int64_t num_tri, const float* attr, int64_t attr_batch,
+                           int64_t num_vert, int32_t attr_channels, int32_t cu, int32_t cv,
+                           int32_t du, int32_t dv, const int64_t* keys, const float* pos,
+                           int64_t pos_batch, int64_t pos_num_vert, int32_t rast_db_gradient,
+                           float* grad_pos, void* stream);
+
 /* The whole mip chain at once (reference.py:433-488; texture_construct_mip, ops.py:239-265):
  * levels 1 .. levels of src [images, h, w, channels] into dst[0 .. levels - 1], each
  * [images, h_l, w_l, channels] with h_l = (h_{l-1} + 1) / 2 (and w_l likewise), values equal to

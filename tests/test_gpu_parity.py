@@ -683,6 +683,61 @@ def test_lookup_with_fused_interpolation_backward(ctx):
             assert fused[1].abs().sum() > 0, case
 
 
+def test_lookup_with_fused_rasterizer_backward(ctx):
+    """A lookup of coordinates interpolated from rasterize's own rast also runs the rasterizer's
+    backward pass in its own (dr_texture_bwd_resolve), adding the position gradient to the
+    buffer the rasterizer's backward pass collects. Position and texture gradients against the
+    interpolation-only fusion, the separate passes and copies (no hand-over at all), within
+    float32 rounding (the position gradient is accumulated with atomics): with the fused-loss
+    antialias (whose position gradient is the buffer), without antialias, with another gradient
+    reaching rast (its depth), without a differentiable rast_db, with a bilinear lookup (no
+    rast_db gradient from it), and through a retained graph differentiated twice."""
+    from diffrast_b200 import _functions as F
+
+    sc = scenes.config5_small(views=2)
+    gen = torch.Generator().manual_seed(41)
+    pos0, tri = sc["pos"].cuda(), sc["tri"].cuda()
+    attr = sc["attr"].cuda()
+    tex0 = torch.rand(1, 32, 32, 3, generator=gen).cuda()
+    target = sc["target"].cuda()
+    w = torch.randn(2, 64, 64, 3, generator=gen).cuda()
+
+    def run(how: str, case: str):
+        F.FUSE_INTERPOLATION_BACKWARD = how in ("fused", "interp_only")
+        F.FUSE_RASTERIZE_BACKWARD = how == "fused"
+        try:
+            pos = pos0.clone().requires_grad_(True)
+            tex = tex0.clone().requires_grad_(True)
+            rast, rast_db = dr.rasterize(ctx, pos, tri, (64, 64), grad_db=case != "no_db")
+            r_in = rast.clone() if how == "copy" else rast
+            out, out_da = dr.interpolate(attr, r_in, tri, rast_db=rast_db, diff_attrs="all")
+            uv, uv_da = out[..., 0:2], out_da[..., 0:4]
+            if how == "copy":
+                uv, uv_da = uv.clone(), uv_da.clone()
+            mode = "linear" if case == "linear" else "linear-mipmap-linear"
+            color = dr.texture(tex, uv, uv_da if mode != "linear" else None, filter_mode=mode)
+            if case in ("aa_mse", "retained"):
+                _, loss = dr.antialias_mse(color, rast, pos, tri, target)
+            else:
+                loss = (color * w).sum()
+            if case == "depth_too":
+                loss = loss + (rast[..., 2] ** 2).sum()
+            grad = functools.partial(torch.autograd.grad, allow_unused=True, materialize_grads=True)
+            if case == "retained":
+                first = grad(loss, [pos, tex], retain_graph=True)
+                return (*first, *grad(loss, [pos, tex]))
+            return grad(loss, [pos, tex])
+        finally:
+            F.FUSE_INTERPOLATION_BACKWARD = F.FUSE_RASTERIZE_BACKWARD = True
+
+    for case in ("aa_mse", "plain", "depth_too", "no_db", "linear", "retained"):
+        results = {how: run(how, case) for how in ("fused", "interp_only", "separate", "copy")}
+        for how in ("interp_only", "separate", "copy"):
+            for x, y in zip(results["fused"], results[how]):
+                grad_close(x, y, 1e-5)
+        assert results["fused"][0].abs().sum() > 0, case
+
+
 def test_position_port_matches_separate_gradients(ctx):
     """Antialias hands its position gradient to the rasterizer's backward pass when it gets the
     rast and the very pos tensor of one rasterize call; against a copy of pos (no hand-over,
