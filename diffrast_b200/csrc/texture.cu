@@ -646,7 +646,7 @@ __device__ __forceinline__ void chain_interpolation(const InterpChain& c, long l
   }
   float gu = 0.0f, gv = 0.0f;
   float g_dudx = 0.0f, g_dudy = 0.0f, g_dvdx = 0.0f, g_dvdy = 0.0f;
-  long long i0 = 0, i1 = 0, i2 = 0;
+  int i0 = 0, i1 = 0, i2 = 0;
   if (t >= 0) {
     const int* vt = c.tri + 3 * static_cast<long long>(t);
     i0 = __ldg(vt);
@@ -687,9 +687,9 @@ __device__ __forceinline__ void chain_interpolation(const InterpChain& c, long l
   float gvert[3][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
   const long long pbase = view * c.pos_view_stride;
   if (t >= 0) {
-    i0 = checked_index(i0, c.pos_num_vert, kSiteVertex);
-    i1 = checked_index(i1, c.pos_num_vert, kSiteVertex);
-    i2 = checked_index(i2, c.pos_num_vert, kSiteVertex);
+    i0 = static_cast<int>(checked_index(i0, c.pos_num_vert, kSiteVertex));
+    i1 = static_cast<int>(checked_index(i1, c.pos_num_vert, kSiteVertex));
+    i2 = static_cast<int>(checked_index(i2, c.pos_num_vert, kSiteVertex));
     const Vert v0 = load_vert(c.pos, pbase + i0), v1 = load_vert(c.pos, pbase + i1),
                v2 = load_vert(c.pos, pbase + i2);
     resolve_adjoint(v0, v1, v2, pixel_centre(col, width), pixel_centre(row, height),
