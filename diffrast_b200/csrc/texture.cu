@@ -626,9 +626,9 @@ struct InterpChain {
 // Gradients of rast and rast_db at pixel p from those of the lookup's coordinates, with the
 // arithmetic and order of the interpolation backward kernel given the same coordinate
 // gradients: d out_c / d b0 = a0_c - a2_c, d out_c / d b1 = a1_c - a2_c, and the derivative
-// channels likewise with rast_db's (d b / dX, d b / dY). With c.grad_pos they go on through the
-// rasterizer's backward pass into the positions; then every lane of the warp must call this
-// (inside = false for pixels past the image).
+// channels likewise with rast_db's (d b / dX, d b / dY). With RESOLVE they go on through the
+// rasterizer's backward pass into the positions (inside = false for pixels past the image: they
+// read and write nothing).
 template <bool RESOLVE>
 __device__ __forceinline__ void chain_interpolation(const InterpChain& c, long long p,
                                                     long long view, int col, int row, int width,
@@ -696,23 +696,13 @@ __device__ __forceinline__ void chain_interpolation(const InterpChain& c, long l
                     make_float4(gu, gv, 0.0f, 0.0f), c.resolve_db,
                     make_float4(g_dudx, g_dudy, g_dvdx, g_dvdy), width, height, gvert);
   }
-  // Lanes showing the same triangle (a warp covers 16 x 2 pixels of one view) sum their vertex
-  // gradients first; one of them adds the sums with three vector reductions.
-  const unsigned act = __ballot_sync(0xffffffffu, t >= 0);
-  if (act == 0u) return;
-  const unsigned lane = threadIdx.x & 31u;
-  unsigned peers = 1u << lane;
-  if (t >= 0) peers = __match_any_sync(act, t);
-  float v[12];
-#pragma unroll
-  for (int k = 0; k < 3; ++k)
-#pragma unroll
-    for (int q = 0; q < 4; ++q) v[4 * k + q] = gvert[k][q];
-  segmented_sum<12>(peers, v);
-  if (t < 0 || (peers & ((1u << lane) - 1u)) != 0u) return;
-  red_add_v4(c.grad_pos + (pbase + i0) * 4, v[0], v[1], v[2], v[3]);
-  red_add_v4(c.grad_pos + (pbase + i1) * 4, v[4], v[5], v[6], v[7]);
-  red_add_v4(c.grad_pos + (pbase + i2) * 4, v[8], v[9], v[10], v[11]);
+  // Each pixel adds its own three vector reductions: a warp covers 16 x 2 pixels, where a
+  // triangle (about four pixels on config 5) repeats too rarely for a warp-level merge to pay
+  // for its shuffles (5.39 ms with it, 5.27 without).
+  if (t < 0) return;
+  red_add_v4(c.grad_pos + (pbase + i0) * 4, gvert[0][0], gvert[0][1], gvert[0][2], gvert[0][3]);
+  red_add_v4(c.grad_pos + (pbase + i1) * 4, gvert[1][0], gvert[1][1], gvert[1][2], gvert[1][3]);
+  red_add_v4(c.grad_pos + (pbase + i2) * 4, gvert[2][0], gvert[2][1], gvert[2][2], gvert[2][3]);
   }
 }
 
@@ -907,8 +897,8 @@ __device__ __forceinline__ void texture_bwd_tile(
     }
   }
   }
-  // With the interpolation (and rasterizer) chained in, every lane takes part in the epilogue's
-  // warp reductions, pixels past the image included (inside = false; they read and write nothing).
+  // With the interpolation (and rasterizer) chained in, pixels past the image go on to the
+  // epilogue too (inside = false; they read and write nothing).
   constexpr bool chained = CHAIN != 0;
   if (!inside && !chained) return;
   const bool coord_grads = grad_uv != nullptr || grad_uv_da != nullptr || grad_bias != nullptr ||

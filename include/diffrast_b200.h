@@ -292,7 +292,7 @@ int dr_mip_downsample_bwd(const float* grad_dst, int64_t images, int32_t h, int3
  * keys and rast from (pos [pos_batch, pos_num_vert, 4], pos_batch 1 or batch; at most 2^24
  * triangles), and attr's rows are those of the same vertex indices. In place of grad_rast and
  * grad_db, the gradients of the pixel's triangle's clip-space vertices are ACCUMULATED into
- * grad_pos (like pos) with warp-aggregated vector reductions -- what dr_raster_resolve_bwd would
+ * grad_pos (like pos) with vector reductions -- what dr_raster_resolve_bwd would
  * add for the rast / rast_db gradients dr_texture_bwd_interp would write (rast_db's only when
  * rast_db_gradient is nonzero, which needs filter mode 3 and uv_da). The pixel's triangle is read
  * from keys. pos and grad_pos 16-byte aligned. */
