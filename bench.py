@@ -45,13 +45,31 @@ import torch.distributed as dist  # noqa: E402
 METRIC = "fwd+bwd Mpixel/s of rasterize→interpolate→texture→antialias at 1/2/4/8 B200"
 UNIT = "Mpixel/s"
 ATTR_CHANNELS, DIFF_CHANNELS, TEX_CHANNELS = 5, 5, 3
-# Kernels each wrapper launches per call (the visibility stage adds 4 when it bins triangles).
+# Kernels each wrapper launches per call (the visibility stage adds 4 when it bins triangles; the
+# mip stages depend on the texture size, see mip_launches).
 LAUNCHES = {
     "raster_visibility": 2, "resolve_fwd": 1, "resolve_bwd": 1, "interpolate_fwd": 1,
     "interpolate_bwd": 1, "texture_fwd": 1, "texture_bwd": 1, "mip_build": 1, "mip_adjoint": 1,
     "edge_neighbours": 2, "antialias_fwd": 1, "antialias_bwd": 1, "to_clip_fwd": 1,
     "to_clip_bwd": 1,
 }  # fmt: skip
+
+
+def mip_launches(h: int, w: int, channels: int) -> tuple[int, int]:
+    """Kernels of one dr_mip_build call (runs of even halvings, up to six levels per launch, with
+    at most 4 channels; one launch per other level) and of one dr_mip_build_bwd call (one per
+    level) for an h x w texture's full chain."""
+    levels, build, lh, lw = 0, 0, h, w
+    while lh > 1 or lw > 1:
+        n = 0
+        while n < 6 and (lh >> n) % 2 == 0 and (lw >> n) % 2 == 0 and (lh >> n, lw >> n) != (1, 1):
+            n += 1
+        step = n if n >= 2 and channels <= 4 else 1
+        for _ in range(step):
+            lh, lw = (lh + 1) // 2, (lw + 1) // 2
+        levels += step
+        build += 1
+    return build, levels
 
 
 def stage_bytes(pixels: int, num_vert: int, views: int, stack_bytes: int, tex_bytes: int,
@@ -565,7 +583,9 @@ def run_ours(args) -> None:
     per_launch_bytes = algo.get(dominant, 0) / max(1.0, stage_calls[dominant])
     peak, peak_kind = peaks()
     achieved = per_launch_bytes / (per_launch_ms / 1e3) / 1e9
-    launches = sum(LAUNCHES.get(n, 1) * c for n, c in stage_calls.items())
+    per_call = dict(LAUNCHES)
+    per_call["mip_build"], per_call["mip_adjoint"] = mip_launches(args.tex, args.tex, TEX_CHANNELS)
+    launches = sum(per_call.get(n, 1) * c for n, c in stage_calls.items())
     clock = clocks.summary()
     line = {
         "metric": METRIC,
