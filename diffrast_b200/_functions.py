@@ -137,6 +137,34 @@ class ChainArgs(NamedTuple):
 # separate passes).
 FUSE_INTERPOLATION_BACKWARD = True
 FUSE_RASTERIZE_BACKWARD = True
+# Whether such a lookup splits its backward pass: the texel gradients in its own backward pass,
+# the chained coordinate part in the interpolation's, which autograd runs after the texture's
+# gradient is complete. The texture gradient is then final (and can be reduced across GPUs while
+# the chained part runs) before the position gradient work; one fused pass is faster where
+# nothing waits for the texture gradient. diffrast_b200.distributed.OverlappedGradientSum turns it
+# on when it sums gradients across more than one rank.
+DEFER_CHAINED_BACKWARD = False
+
+
+class Deferred(NamedTuple):
+    """A lookup's chained coordinate part, left for the interpolation's backward pass to run:
+    the inputs of the chained texture backward kernel without texel gradients."""
+
+    levels: list
+    uv: Tensor
+    uv_da: Tensor | None
+    bias: Tensor | None
+    mode: int
+    boundary: int
+    grad_out: Tensor
+    want_da: bool
+    chain: ChainArgs
+
+
+def _run_deferred(d: Deferred) -> Chained:
+    _, g_rast, g_db, _ = K.texture_bwd_chained(d.levels, d.uv, d.uv_da, d.bias, d.mode, d.boundary,
+                                               d.grad_out, d.want_da, False, d.chain, texels=False)
+    return Chained(g_rast, g_db)
 
 
 class Route:
@@ -159,6 +187,9 @@ class Route:
     def deliver_chained(self, key, grad_rast, grad_db) -> None:
         self.pending[(torch._C._current_graph_task_id(), key)] = Chained(grad_rast, grad_db)
 
+    def deliver_deferred(self, key, deferred: Deferred) -> None:
+        self.pending[(torch._C._current_graph_task_id(), key)] = deferred
+
     def chain(self, uv_spec, da_spec, mode: int, boundary: int, want_da: bool) -> ChainArgs | None:
         """The fused backward pass's arguments when it applies: a 2D lookup of two consecutive
         interpolated channels (and of two whole derivative pairs), an interpolation whose
@@ -173,7 +204,7 @@ class Route:
                         or da_spec[0] // 2 + 2 > len(port.diff_channels)):
             return None
         task = torch._C._current_graph_task_id()
-        if any(k[0] == task and isinstance(v, Chained) for k, v in self.pending.items()):
+        if any(k[0] == task and isinstance(v, (Chained, Deferred)) for k, v in self.pending.items()):
             return None
         got = port.geometry.tensors()
         if got is None:
@@ -259,7 +290,7 @@ def _collect(pending: dict, channels: int, da_channels: int, grad_out, grad_out_
     """The coordinate gradients delivered in this backward pass (consumed), as at most one compact
     part per output plus whole images for anything that does not fit that form, and the
     hand-overs already chained through the interpolation (:class:`Chained`)."""
-    mine = _take_pending(pending)
+    mine = [_run_deferred(v) if isinstance(v, Deferred) else v for v in _take_pending(pending)]
     chained = [v for v in mine if isinstance(v, Chained)]
     parts: dict[str, tuple[int, Tensor]] = {}
     for uv_first, g_uv, da_first, g_da in (v for v in mine if not isinstance(v, Chained)):
@@ -470,7 +501,12 @@ class Texture(torch.autograd.Function):
             g_uv_src, uv_first = _slice_gradient(uv_src, uv_spec, want_uv)
             g_da_src, da_first = _slice_gradient(da_src, da_spec, want_da)
         chain = route.chain(uv_spec, da_spec, mode, boundary, want_da) if route is not None else None
-        if chain is not None:
+        deferred = chain is not None and DEFER_CHAINED_BACKWARD
+        if deferred:
+            grads, _, _, g_bias = K.texture_bwd(
+                levels, _take(uv_src, uv_spec), _take(da_src, da_spec), bias, mode, boundary,
+                grad_out.contiguous(), False, False, want_bias)
+        elif chain is not None:
             grads, g_rast, g_db, g_bias = K.texture_bwd_chained(
                 levels, _take(uv_src, uv_spec), _take(da_src, da_spec), bias, mode, boundary,
                 grad_out.contiguous(), want_da, want_bias, chain)
@@ -481,7 +517,11 @@ class Texture(torch.autograd.Function):
                 grad_da=g_da_src, uv_first=uv_first, da_first=da_first)
         level_grads = [g if need[10 + i] else None for i, g in enumerate(grads)]
         if route is not None:
-            if chain is not None:
+            if deferred:
+                route.deliver_deferred(id(ctx), Deferred(
+                    levels, _take(uv_src, uv_spec), _take(da_src, da_spec), bias, mode, boundary,
+                    grad_out.contiguous(), want_da, chain))
+            elif chain is not None:
                 route.deliver_chained(id(ctx), g_rast, g_db)
             else:
                 route.deliver(id(ctx), uv_spec[0], g_uv,
@@ -537,7 +577,12 @@ class TextureChain(torch.autograd.Function):
             g_uv_src, uv_first = _slice_gradient(uv_src, uv_spec, want_uv)
             g_da_src, da_first = _slice_gradient(da_src, da_spec, want_da)
         chain = route.chain(uv_spec, da_spec, mode, boundary, want_da) if route is not None else None
-        if chain is not None:
+        deferred = chain is not None and DEFER_CHAINED_BACKWARD
+        if deferred:
+            grads, _, _, g_bias = K.texture_bwd(
+                levels, _take(uv_src, uv_spec), _take(da_src, da_spec), bias, mode, boundary,
+                grad_out.contiguous(), False, False, want_bias, keep_padded=True)
+        elif chain is not None:
             grads, g_rast, g_db, g_bias = K.texture_bwd_chained(
                 levels, _take(uv_src, uv_spec), _take(da_src, da_spec), bias, mode, boundary,
                 grad_out.contiguous(), want_da, want_bias, chain, keep_padded=True)
@@ -560,7 +605,11 @@ class TextureChain(torch.autograd.Function):
             if grad_tex.shape[-1] != tex.shape[-1]:
                 grad_tex = grad_tex[..., : tex.shape[-1]].contiguous()
         if route is not None:
-            if chain is not None:
+            if deferred:
+                route.deliver_deferred(id(ctx), Deferred(
+                    levels, _take(uv_src, uv_spec), _take(da_src, da_spec), bias, mode, boundary,
+                    grad_out.contiguous(), want_da, chain))
+            elif chain is not None:
                 route.deliver_chained(id(ctx), g_rast, g_db)
             else:
                 route.deliver(id(ctx), uv_spec[0], g_uv,

@@ -467,16 +467,20 @@ def _level_gradients(levels):
 
 @timed("texture_bwd")
 def texture_bwd_chained(levels, uv, uv_da, bias, mode, boundary, grad_out, want_da, want_bias,
-                        chain, keep_padded=False):
+                        chain, keep_padded=False, texels=True):
     """Texture backward with the interpolation's backward for the coordinates fused in
     (``dr_texture_bwd_interp``): level gradients, the bias gradient as wanted, and in place of
     the coordinate gradients ``(grad_rast, grad_db)`` of the interpolation ``chain`` that made uv
     and uv_da (``grad_db`` None unless ``want_da``). With ``chain.raster`` the rasterizer's
     backward pass runs too (``dr_texture_bwd_resolve``): the position gradient is accumulated
-    into ``chain.raster.grad_pos`` and ``(None, None)`` stand for rast's and rast_db's."""
+    into ``chain.raster.grad_pos`` and ``(None, None)`` stand for rast's and rast_db's. With
+    ``texels`` False no texel gradient is computed (the level list returned is empty)."""
     batch, height, width = uv.shape[:3]
     channels = levels[0].shape[-1]
-    grads, stride = _level_gradients(levels)
+    if texels:
+        grads, stride = _level_gradients(levels)
+    else:
+        grads, stride = [], (4 if channels == 3 else channels)
     rast = chain.rast
     uv, uv_stride = pixel_rows(uv)
     uv_da, da_stride = pixel_rows(uv_da)
@@ -484,7 +488,8 @@ def texture_bwd_chained(levels, uv, uv_da, bias, mode, boundary, grad_out, want_
     hs, ws, bs = _level_tables(levels, boundary == 3)
     attr = chain.attr
     common = (N.pointer_array([lv.data_ptr() for lv in levels]),
-              N.pointer_array([g.data_ptr() for g in grads]), hs, ws, bs, len(levels), channels,
+              N.pointer_array([g.data_ptr() for g in grads]) if grads else None, hs, ws, bs,
+              len(levels), channels,
               stride, uv.data_ptr(), uv_stride, N.ptr(uv_da), da_stride, N.ptr(bias), batch,
               height, width, mode, boundary, grad_out.data_ptr(), N.ptr(grad_bias),
               rast.data_ptr(), chain.tri.data_ptr(), chain.tri.shape[0], attr.data_ptr(),

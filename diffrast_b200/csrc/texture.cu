@@ -786,7 +786,10 @@ __device__ __forceinline__ void texture_bwd_tile(
   }
   const unsigned lane = threadIdx.x & 31u;
   const bool vector = grad_stride == 4 && channels <= 4;
-  if (B != DR_BOUNDARY_CUBE && MODE != DR_FILTER_NEAREST) {
+  // Without gradient levels (a chained pass run on its own, after the texel gradients were
+  // accumulated by an earlier pass) only the coordinate part below runs.
+  if (L.grad[0] == nullptr) {
+  } else if (B != DR_BOUNDARY_CUBE && MODE != DR_FILTER_NEAREST) {
     // Off a cube, a level's four taps form a quad that (off[0], off[3]) identifies (off[0] alone
     // when wrapping): lanes sharing a quad sum all four taps' contributions at once, with one
     // match per level instead of one per tap.
@@ -1352,7 +1355,9 @@ int texture_bwd_impl(const float* const* level_ptr, float* const* grad_level_ptr
                               float* grad_uv_da, int64_t grad_uv_da_stride,
                               int32_t grad_uv_da_first, float* grad_bias, const InterpChain& chain,
                               void* stream) {
-  if (grad_level_ptr == nullptr) return DR_ERR_INVALID_ARGUMENT;
+  // No gradient levels: the chained coordinate part alone (texel gradients not computed).
+  if (grad_level_ptr == nullptr && chain.grad_rast == nullptr && chain.grad_pos == nullptr)
+    return DR_ERR_INVALID_ARGUMENT;
   Levels L;
   int status = make_levels(level_ptr, grad_level_ptr, level_h, level_w, level_batch_stride,
                            num_levels, channels, filter_mode, boundary_mode, batch, L);
@@ -1376,7 +1381,7 @@ int texture_bwd_impl(const float* const* level_ptr, float* const* grad_level_ptr
   if (gst.uv < uv_width || gst.uv_da < da_width) return DR_ERR_INVALID_ARGUMENT;
   if (gst.uv_first + uv_width > gst.uv || gst.da_first + da_width > gst.uv_da)
     return DR_ERR_INVALID_ARGUMENT;
-  if (grad_channel_stride == 4) {
+  if (grad_channel_stride == 4 && grad_level_ptr != nullptr) {
     for (int l = 0; l < num_levels; ++l)
       if ((reinterpret_cast<uintptr_t>(grad_level_ptr[l]) & 15u) != 0) return DR_ERR_INVALID_ARGUMENT;
   }

@@ -75,6 +75,13 @@ class OverlappedGradientSum:
         self._pending: list = []
         self._done: set[int] = set()
         self._hooks = [t.register_post_accumulate_grad_hook(self._reduce) for t in self.tensors]
+        if self._active() and dist.get_world_size(group) > 1:
+            # Texture lookups then complete the texture gradient before their position gradient
+            # work (which runs in the interpolation's backward pass), so that the texture's
+            # all-reduce overlaps it (see diffrast_b200._functions.DEFER_CHAINED_BACKWARD).
+            from diffrast_b200 import _functions
+
+            _functions.DEFER_CHAINED_BACKWARD = True
 
     def _active(self) -> bool:
         return dist.is_available() and dist.is_initialized()

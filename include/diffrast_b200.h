@@ -261,7 +261,10 @@ int dr_texture_bwd(const float* const* level_ptr, float* const* grad_level_ptr,
  * [batch, height, width, 4] (NULL when uv_da gets no gradient; then uv_da may still be given for
  * the level of detail) -- what dr_interpolate_bwd would write for the same coordinate gradients
  * and no attribute gradient. 2D textures only (not boundary mode 3), filter modes 1-3; rast,
- * grad_rast and grad_db 16-byte aligned. */
+ * grad_rast and grad_db 16-byte aligned. grad_level_ptr may be NULL: then no texel gradient is
+ * computed, only the chained part (run on its own after a dr_texture_bwd call without coordinate
+ * gradients has accumulated the texel gradients, so that the texture gradient is final, and can
+ * be reduced across GPUs, before this part runs). The same holds for dr_texture_bwd_resolve. */
 int dr_texture_bwd_interp(const float* const* level_ptr, float* const* grad_level_ptr,
                           const int32_t* level_h, const int32_t* level_w,
                           const int64_t* level_batch_stride, int32_t num_levels, int32_t channels,

@@ -626,6 +626,7 @@ def test_lookup_with_fused_interpolation_backward(ctx):
 
     def run(how: str, case: str):
         F.FUSE_INTERPOLATION_BACKWARD = how != "separate"
+        F.DEFER_CHAINED_BACKWARD = how == "deferred"
         try:
             r = rast0.clone().requires_grad_(True)
             d = db0.clone().requires_grad_(True)
@@ -670,14 +671,17 @@ def test_lookup_with_fused_interpolation_backward(ctx):
             return grad(loss, leaves)
         finally:
             F.FUSE_INTERPOLATION_BACKWARD = True
+            F.DEFER_CHAINED_BACKWARD = False
 
     exact = ("chain", "whole", "stack", "linear", "mip_nearest", "offset", "attr_batch")
     for case in exact + ("other_consumers", "two_lookups", "attr_grad", "retained"):
-        fused, separate, copied = (run(how, case) for how in ("fused", "separate", "copy"))
-        for i, (x, y, z) in enumerate(zip(fused, separate, copied)):
+        fused, deferred, separate, copied = (run(how, case)
+                                             for how in ("fused", "deferred", "separate", "copy"))
+        for i, (x, d, y, z) in enumerate(zip(fused, deferred, separate, copied)):
             if case in exact and i < 2:  # rast, rast_db (the texel gradients use atomics)
-                assert torch.equal(x, y), case
+                assert torch.equal(x, y) and torch.equal(d, y), case
             grad_close(x, z, 1e-5)
+            grad_close(d, z, 1e-5)
         assert fused[0].abs().sum() > 0, case
         if case not in ("linear", "mip_nearest"):
             assert fused[1].abs().sum() > 0, case
@@ -688,7 +692,8 @@ def test_lookup_with_fused_rasterizer_backward(ctx):
     backward pass in its own (dr_texture_bwd_resolve), adding the position gradient to the
     buffer the rasterizer's backward pass collects. Position and texture gradients against the
     interpolation-only fusion, the separate passes and copies (no hand-over at all), within
-    float32 rounding (the position gradient is accumulated with atomics): with the fused-loss
+    float32 rounding (the position gradient is accumulated with atomics), and with the chained
+    part deferred to the interpolation's backward pass (as on several GPUs): with the fused-loss
     antialias (whose position gradient is the buffer), without antialias, with another gradient
     reaching rast (its depth), without a differentiable rast_db, with a bilinear lookup (no
     rast_db gradient from it), and through a retained graph differentiated twice."""
@@ -703,8 +708,9 @@ def test_lookup_with_fused_rasterizer_backward(ctx):
     w = torch.randn(2, 64, 64, 3, generator=gen).cuda()
 
     def run(how: str, case: str):
-        F.FUSE_INTERPOLATION_BACKWARD = how in ("fused", "interp_only")
-        F.FUSE_RASTERIZE_BACKWARD = how == "fused"
+        F.FUSE_INTERPOLATION_BACKWARD = how in ("fused", "deferred", "interp_only")
+        F.FUSE_RASTERIZE_BACKWARD = how in ("fused", "deferred")
+        F.DEFER_CHAINED_BACKWARD = how == "deferred"
         try:
             pos = pos0.clone().requires_grad_(True)
             tex = tex0.clone().requires_grad_(True)
@@ -729,10 +735,12 @@ def test_lookup_with_fused_rasterizer_backward(ctx):
             return grad(loss, [pos, tex])
         finally:
             F.FUSE_INTERPOLATION_BACKWARD = F.FUSE_RASTERIZE_BACKWARD = True
+            F.DEFER_CHAINED_BACKWARD = False
 
+    hows = ("fused", "deferred", "interp_only", "separate", "copy")
     for case in ("aa_mse", "plain", "depth_too", "no_db", "linear", "retained"):
-        results = {how: run(how, case) for how in ("fused", "interp_only", "separate", "copy")}
-        for how in ("interp_only", "separate", "copy"):
+        results = {how: run(how, case) for how in hows}
+        for how in hows[1:]:
             for x, y in zip(results["fused"], results[how]):
                 grad_close(x, y, 1e-5)
         assert results["fused"][0].abs().sum() > 0, case
