@@ -137,34 +137,28 @@ class ChainArgs(NamedTuple):
 # separate passes).
 FUSE_INTERPOLATION_BACKWARD = True
 FUSE_RASTERIZE_BACKWARD = True
-# Whether such a lookup splits its backward pass: the texel gradients in its own backward pass,
-# the chained coordinate part in the interpolation's, which autograd runs after the texture's
-# gradient is complete. The texture gradient is then final (and can be reduced across GPUs while
-# the chained part runs) before the position gradient work; one fused pass is faster where
-# nothing waits for the texture gradient. diffrast_b200.distributed.OverlappedGradientSum turns it
-# on when it sums gradients across more than one rank.
+# Whether a lookup that would run the rasterizer's backward pass in its own splits it instead:
+# texel and compact coordinate gradients in its own backward pass, the chained position part
+# (dr_texture_chain_bwd) in the interpolation's, which autograd runs after the texture's gradient
+# is complete. The texture gradient is then final, and can be reduced across GPUs while the
+# position part runs; one fused pass is faster where nothing waits for the texture gradient.
+# diffrast_b200.distributed.OverlappedGradientSum turns it on from DEFER_RANKS ranks on.
 DEFER_CHAINED_BACKWARD = False
 
 
 class Deferred(NamedTuple):
-    """A lookup's chained coordinate part, left for the interpolation's backward pass to run:
-    the inputs of the chained texture backward kernel without texel gradients."""
+    """A lookup's chained position part, left for the interpolation's backward pass to run: its
+    compact coordinate gradients and the chain (``dr_texture_chain_bwd``)."""
 
-    levels: list
-    uv: Tensor
-    uv_da: Tensor | None
-    bias: Tensor | None
-    mode: int
-    boundary: int
-    grad_out: Tensor
+    g_uv: Tensor
+    g_da: Tensor | None
     want_da: bool
     chain: ChainArgs
 
 
 def _run_deferred(d: Deferred) -> Chained:
-    _, g_rast, g_db, _ = K.texture_bwd_chained(d.levels, d.uv, d.uv_da, d.bias, d.mode, d.boundary,
-                                               d.grad_out, d.want_da, False, d.chain, texels=False)
-    return Chained(g_rast, g_db)
+    K.texture_chain_bwd(d.g_uv, d.g_da, d.want_da, d.chain)
+    return Chained(None, None)
 
 
 class Route:
@@ -214,8 +208,10 @@ class Route:
         if want_da:
             du = port.diff_channels[da_spec[0] // 2]
             dv = port.diff_channels[da_spec[0] // 2 + 1]
-        return ChainArgs(attr, rast, tri, uv_spec[0], uv_spec[0] + 1, du, dv,
-                         self._raster_chain(rast, tri, task))
+        raster = self._raster_chain(rast, tri, task)
+        if DEFER_CHAINED_BACKWARD and raster is None:
+            return None  # deferred: the interpolation's backward pass takes compact parts
+        return ChainArgs(attr, rast, tri, uv_spec[0], uv_spec[0] + 1, du, dv, raster)
 
     def _raster_chain(self, rast, tri, task) -> RasterChain | None:
         """The rasterization part when it applies: the interpolation read the very rast of a
@@ -503,9 +499,9 @@ class Texture(torch.autograd.Function):
         chain = route.chain(uv_spec, da_spec, mode, boundary, want_da) if route is not None else None
         deferred = chain is not None and DEFER_CHAINED_BACKWARD
         if deferred:
-            grads, _, _, g_bias = K.texture_bwd(
+            grads, g_uv, g_da, g_bias = K.texture_bwd(
                 levels, _take(uv_src, uv_spec), _take(da_src, da_spec), bias, mode, boundary,
-                grad_out.contiguous(), False, False, want_bias)
+                grad_out.contiguous(), True, want_da, want_bias)
         elif chain is not None:
             grads, g_rast, g_db, g_bias = K.texture_bwd_chained(
                 levels, _take(uv_src, uv_spec), _take(da_src, da_spec), bias, mode, boundary,
@@ -518,9 +514,7 @@ class Texture(torch.autograd.Function):
         level_grads = [g if need[10 + i] else None for i, g in enumerate(grads)]
         if route is not None:
             if deferred:
-                route.deliver_deferred(id(ctx), Deferred(
-                    levels, _take(uv_src, uv_spec), _take(da_src, da_spec), bias, mode, boundary,
-                    grad_out.contiguous(), want_da, chain))
+                route.deliver_deferred(id(ctx), Deferred(g_uv, g_da, want_da, chain))
             elif chain is not None:
                 route.deliver_chained(id(ctx), g_rast, g_db)
             else:
@@ -579,9 +573,9 @@ class TextureChain(torch.autograd.Function):
         chain = route.chain(uv_spec, da_spec, mode, boundary, want_da) if route is not None else None
         deferred = chain is not None and DEFER_CHAINED_BACKWARD
         if deferred:
-            grads, _, _, g_bias = K.texture_bwd(
+            grads, g_uv, g_da, g_bias = K.texture_bwd(
                 levels, _take(uv_src, uv_spec), _take(da_src, da_spec), bias, mode, boundary,
-                grad_out.contiguous(), False, False, want_bias, keep_padded=True)
+                grad_out.contiguous(), True, want_da, want_bias, keep_padded=True)
         elif chain is not None:
             grads, g_rast, g_db, g_bias = K.texture_bwd_chained(
                 levels, _take(uv_src, uv_spec), _take(da_src, da_spec), bias, mode, boundary,
@@ -606,9 +600,7 @@ class TextureChain(torch.autograd.Function):
                 grad_tex = grad_tex[..., : tex.shape[-1]].contiguous()
         if route is not None:
             if deferred:
-                route.deliver_deferred(id(ctx), Deferred(
-                    levels, _take(uv_src, uv_spec), _take(da_src, da_spec), bias, mode, boundary,
-                    grad_out.contiguous(), want_da, chain))
+                route.deliver_deferred(id(ctx), Deferred(g_uv, g_da, want_da, chain))
             elif chain is not None:
                 route.deliver_chained(id(ctx), g_rast, g_db)
             else:

@@ -448,6 +448,26 @@ def texture_bwd(levels, uv, uv_da, bias, mode, boundary, grad_out, want_uv, want
     return grads, grad_uv, grad_da, grad_bias
 
 
+@timed("texture_chain")
+def texture_chain_bwd(g_uv: Tensor, g_da: Tensor | None, want_da: bool, chain) -> None:
+    """The chained position part of a lookup on its own (``dr_texture_chain_bwd``): from its
+    compact coordinate gradients, the interpolation's and the rasterizer's backward passes,
+    accumulated into ``chain.raster.grad_pos``."""
+    batch, height, width = g_uv.shape[:3]
+    r = chain.raster
+    attr = chain.attr
+    N.check(
+        N.lib().dr_texture_chain_bwd(
+            g_uv.contiguous().data_ptr(), N.ptr(g_da.contiguous() if g_da is not None else None),
+            batch, height, width, chain.tri.data_ptr(), chain.tri.shape[0], attr.data_ptr(),
+            attr.shape[0], attr.shape[1], attr.shape[2], chain.cu, chain.cv, chain.du, chain.dv,
+            r.keys.data_ptr(), r.pos.data_ptr(), r.pos.shape[0], r.pos.shape[1],
+            int(r.grad_db and want_da and g_da is not None), r.grad_pos.data_ptr(),
+            N.stream(g_uv.device)),
+        "dr_texture_chain_bwd",
+    )  # fmt: skip
+
+
 def _level_gradients(levels):
     """Zeroed gradient buffers of all levels and their channel stride. Three-channel gradients
     are accumulated in four-channel buffers, so that each texel takes one 16-byte vector
@@ -467,20 +487,16 @@ def _level_gradients(levels):
 
 @timed("texture_bwd")
 def texture_bwd_chained(levels, uv, uv_da, bias, mode, boundary, grad_out, want_da, want_bias,
-                        chain, keep_padded=False, texels=True):
+                        chain, keep_padded=False):
     """Texture backward with the interpolation's backward for the coordinates fused in
     (``dr_texture_bwd_interp``): level gradients, the bias gradient as wanted, and in place of
     the coordinate gradients ``(grad_rast, grad_db)`` of the interpolation ``chain`` that made uv
     and uv_da (``grad_db`` None unless ``want_da``). With ``chain.raster`` the rasterizer's
     backward pass runs too (``dr_texture_bwd_resolve``): the position gradient is accumulated
-    into ``chain.raster.grad_pos`` and ``(None, None)`` stand for rast's and rast_db's. With
-    ``texels`` False no texel gradient is computed (the level list returned is empty)."""
+    into ``chain.raster.grad_pos`` and ``(None, None)`` stand for rast's and rast_db's."""
     batch, height, width = uv.shape[:3]
     channels = levels[0].shape[-1]
-    if texels:
-        grads, stride = _level_gradients(levels)
-    else:
-        grads, stride = [], (4 if channels == 3 else channels)
+    grads, stride = _level_gradients(levels)
     rast = chain.rast
     uv, uv_stride = pixel_rows(uv)
     uv_da, da_stride = pixel_rows(uv_da)
@@ -488,8 +504,7 @@ def texture_bwd_chained(levels, uv, uv_da, bias, mode, boundary, grad_out, want_
     hs, ws, bs = _level_tables(levels, boundary == 3)
     attr = chain.attr
     common = (N.pointer_array([lv.data_ptr() for lv in levels]),
-              N.pointer_array([g.data_ptr() for g in grads]) if grads else None, hs, ws, bs,
-              len(levels), channels,
+              N.pointer_array([g.data_ptr() for g in grads]), hs, ws, bs, len(levels), channels,
               stride, uv.data_ptr(), uv_stride, N.ptr(uv_da), da_stride, N.ptr(bias), batch,
               height, width, mode, boundary, grad_out.data_ptr(), N.ptr(grad_bias),
               rast.data_ptr(), chain.tri.data_ptr(), chain.tri.shape[0], attr.data_ptr(),

@@ -99,6 +99,11 @@ _SIGNATURES = {
          c_int32, c_int32, c_int32, c_int32, _P, _P, _P, _P, c_int64, _P, c_int64, c_int64,
          c_int32, c_int32, c_int32, c_int32, c_int32, _P, _P, c_int64, c_int64, c_int32, _P, _P],
     ),
+    "dr_texture_chain_bwd": (
+        c_int,
+        [_P, _P, c_int64, c_int32, c_int32, _P, c_int64, _P, c_int64, c_int64, c_int32, c_int32,
+         c_int32, c_int32, c_int32, _P, _P, c_int64, c_int64, c_int32, _P, _P],
+    ),
     "dr_mip_downsample": (c_int, [_P, c_int64, c_int32, c_int32, c_int32, _P, _P]),
     "dr_mip_build": (c_int, [_P, c_int64, c_int32, c_int32, c_int32, c_int32, _P, _P]),
     "dr_mip_build_bwd": (c_int, [_P, c_int64, c_int32, c_int32, c_int32, c_int32, _P, c_int32, _P]),

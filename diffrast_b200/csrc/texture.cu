@@ -706,6 +706,36 @@ __device__ __forceinline__ void chain_interpolation(const InterpChain& c, long l
   }
 }
 
+// The chained position part of a lookup on its own, from its compact coordinate gradients
+// (g_uv [pixels, 2], g_da [pixels, 4] or null) written by an earlier texture backward pass: the
+// interpolation's and the rasterizer's backward passes for them, into c.grad_pos. One thread per
+// pixel; grid: columns in x, rows in y, views in z (short blocks, so that a concurrent all-reduce
+// gets SMs as they finish).
+__global__ void __launch_bounds__(256) chain_parts_kernel(const InterpChain c,
+                                                          const float2* __restrict__ g_uv,
+                                                          const float4* __restrict__ g_da,
+                                                          int height, int width) {
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  const int row = blockIdx.y;
+  const long long view = blockIdx.z;
+  const bool inside = col < width;
+  const long long p = (view * height + row) * width + col;
+  float guv[2] = {0.f, 0.f}, gda[4] = {0.f, 0.f, 0.f, 0.f};
+  if (inside) {
+    const float2 u = __ldcs(g_uv + p);
+    guv[0] = u.x;
+    guv[1] = u.y;
+    if (g_da != nullptr) {
+      const float4 d = __ldcs(g_da + p);
+      gda[0] = d.x;
+      gda[1] = d.y;
+      gda[2] = d.z;
+      gda[3] = d.w;
+    }
+  }
+  chain_interpolation<true>(c, p, view, col, row, width, height, inside, guv, gda);
+}
+
 // A quad that a whole warp added to (lane 0 keeps it): pixels that all read the same four texels
 // (a background that samples one point, a magnified region) accumulate here across the tiles a
 // warp visits and reach global memory once, instead of every warp reducing into the same four
@@ -786,10 +816,7 @@ __device__ __forceinline__ void texture_bwd_tile(
   }
   const unsigned lane = threadIdx.x & 31u;
   const bool vector = grad_stride == 4 && channels <= 4;
-  // Without gradient levels (a chained pass run on its own, after the texel gradients were
-  // accumulated by an earlier pass) only the coordinate part below runs.
-  if (L.grad[0] == nullptr) {
-  } else if (B != DR_BOUNDARY_CUBE && MODE != DR_FILTER_NEAREST) {
+  if (B != DR_BOUNDARY_CUBE && MODE != DR_FILTER_NEAREST) {
     // Off a cube, a level's four taps form a quad that (off[0], off[3]) identifies (off[0] alone
     // when wrapping): lanes sharing a quad sum all four taps' contributions at once, with one
     // match per level instead of one per tap.
@@ -1355,9 +1382,7 @@ int texture_bwd_impl(const float* const* level_ptr, float* const* grad_level_ptr
                               float* grad_uv_da, int64_t grad_uv_da_stride,
                               int32_t grad_uv_da_first, float* grad_bias, const InterpChain& chain,
                               void* stream) {
-  // No gradient levels: the chained coordinate part alone (texel gradients not computed).
-  if (grad_level_ptr == nullptr && chain.grad_rast == nullptr && chain.grad_pos == nullptr)
-    return DR_ERR_INVALID_ARGUMENT;
+  if (grad_level_ptr == nullptr) return DR_ERR_INVALID_ARGUMENT;
   Levels L;
   int status = make_levels(level_ptr, grad_level_ptr, level_h, level_w, level_batch_stride,
                            num_levels, channels, filter_mode, boundary_mode, batch, L);
@@ -1381,7 +1406,7 @@ int texture_bwd_impl(const float* const* level_ptr, float* const* grad_level_ptr
   if (gst.uv < uv_width || gst.uv_da < da_width) return DR_ERR_INVALID_ARGUMENT;
   if (gst.uv_first + uv_width > gst.uv || gst.da_first + da_width > gst.uv_da)
     return DR_ERR_INVALID_ARGUMENT;
-  if (grad_channel_stride == 4 && grad_level_ptr != nullptr) {
+  if (grad_channel_stride == 4) {
     for (int l = 0; l < num_levels; ++l)
       if ((reinterpret_cast<uintptr_t>(grad_level_ptr[l]) & 15u) != 0) return DR_ERR_INVALID_ARGUMENT;
   }
@@ -1514,6 +1539,57 @@ extern "C" int dr_texture_bwd_resolve(
                           num_levels, channels, grad_channel_stride, uv, uv_stride, uv_da,
                           uv_da_stride, bias, batch, height, width, filter_mode, boundary_mode,
                           grad_out, nullptr, 0, -1, nullptr, 0, -1, grad_bias, chain, stream);
+}
+
+extern "C" int dr_texture_chain_bwd(const float* grad_uv, const float* grad_uv_da, int64_t batch,
+                                    int32_t height, int32_t width, const int32_t* tri,
+                                    int64_t num_tri, const float* attr, int64_t attr_batch,
+                                    int64_t num_vert, int32_t attr_channels, int32_t cu,
+                                    int32_t cv, int32_t du, int32_t dv, const int64_t* keys,
+                                    const float* pos, int64_t pos_batch, int64_t pos_num_vert,
+                                    int32_t rast_db_gradient, float* grad_pos, void* stream) {
+  const bool want_db = rast_db_gradient != 0;
+  if (batch < 0 || height < 0 || width < 0 || num_tri < 0 || num_tri > (1LL << 24) ||
+      num_vert < 0 || pos_num_vert < 0 || attr_channels < 1)
+    return DR_ERR_INVALID_ARGUMENT;
+  if ((attr_batch != 1 && attr_batch != batch) || (pos_batch != 1 && pos_batch != batch))
+    return DR_ERR_INVALID_ARGUMENT;
+  if (cu < 0 || cu >= attr_channels || cv < 0 || cv >= attr_channels) return DR_ERR_INVALID_ARGUMENT;
+  if (want_db && (grad_uv_da == nullptr || du < 0 || du >= attr_channels || dv < 0 ||
+                  dv >= attr_channels))
+    return DR_ERR_INVALID_ARGUMENT;
+  const long long total = batch * static_cast<long long>(height) * width;
+  if (total == 0) return DR_OK;
+  const uintptr_t align = reinterpret_cast<uintptr_t>(pos) | reinterpret_cast<uintptr_t>(grad_pos) |
+                          reinterpret_cast<uintptr_t>(grad_uv_da);
+  if (grad_uv == nullptr || keys == nullptr || pos == nullptr || grad_pos == nullptr ||
+      (align & 15u) != 0 || (reinterpret_cast<uintptr_t>(grad_uv) & 7u) != 0)
+    return DR_ERR_INVALID_ARGUMENT;
+  if (num_tri > 0 && tri == nullptr) return DR_ERR_INVALID_ARGUMENT;
+  if (num_vert > 0 && attr == nullptr) return DR_ERR_INVALID_ARGUMENT;
+  if (batch > 65535 || height > 65535) return DR_ERR_TOO_LARGE;
+  InterpChain c = {};
+  c.tri = tri;
+  c.attr = attr;
+  c.attr_view_stride = attr_batch == 1 ? 0 : num_vert * attr_channels;
+  c.num_vert = num_vert;
+  c.attr_channels = attr_channels;
+  c.num_tri = static_cast<int>(num_tri);
+  c.cu = cu;
+  c.cv = cv;
+  c.du = du;
+  c.dv = dv;
+  c.keys = reinterpret_cast<const long long*>(keys);
+  c.pos = pos;
+  c.pos_view_stride = pos_batch == 1 ? 0 : pos_num_vert;
+  c.pos_num_vert = pos_num_vert;
+  c.grad_pos = grad_pos;
+  c.resolve_db = want_db;
+  const dim3 grid((width + 255) / 256, static_cast<unsigned>(height), static_cast<unsigned>(batch));
+  chain_parts_kernel<<<grid, 256, 0, as_stream(stream)>>>(
+      c, reinterpret_cast<const float2*>(grad_uv),
+      want_db ? reinterpret_cast<const float4*>(grad_uv_da) : nullptr, height, width);
+  return launch_status();
 }
 
 extern "C" int dr_mip_downsample(const float* src, int64_t images, int32_t h, int32_t w,

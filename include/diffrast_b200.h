@@ -261,10 +261,7 @@ int dr_texture_bwd(const float* const* level_ptr, float* const* grad_level_ptr,
  * [batch, height, width, 4] (NULL when uv_da gets no gradient; then uv_da may still be given for
  * the level of detail) -- what dr_interpolate_bwd would write for the same coordinate gradients
  * and no attribute gradient. 2D textures only (not boundary mode 3), filter modes 1-3; rast,
- * grad_rast and grad_db 16-byte aligned. grad_level_ptr may be NULL: then no texel gradient is
- * computed, only the chained part (run on its own after a dr_texture_bwd call without coordinate
- * gradients has accumulated the texel gradients, so that the texture gradient is final, and can
- * be reduced across GPUs, before this part runs). The same holds for dr_texture_bwd_resolve. */
+ * grad_rast and grad_db 16-byte aligned. */
 int dr_texture_bwd_interp(const float* const* level_ptr, float* const* grad_level_ptr,
                           const int32_t* level_h, const int32_t* level_w,
                           const int64_t* level_batch_stride, int32_t num_levels, int32_t channels,
@@ -312,6 +309,21 @@ int dr_texture_bwd_resolve(const float* const* level_ptr, float* const* grad_lev
                            int32_t du, int32_t dv, const int64_t* keys, const float* pos,
                            int64_t pos_batch, int64_t pos_num_vert, int32_t rast_db_gradient,
                            float* grad_pos, void* stream);
+
+/* The chained position part of dr_texture_bwd_resolve on its own (no counterpart in the
+ * reference): from a lookup's compact coordinate gradients grad_uv [batch, height, width, 2] and
+ * grad_uv_da [batch, height, width, 4] (as dr_texture_bwd writes them with grad_uv_first = -1),
+ * the interpolation's and the rasterizer's backward passes, ACCUMULATED into grad_pos like
+ * dr_texture_bwd_resolve does (arguments as there). Lets a caller complete the texture gradient
+ * first (dr_texture_bwd without the chain) and run this while that gradient is being reduced
+ * across GPUs. One thread per pixel in short blocks; batch and height at most 65535. */
+int dr_texture_chain_bwd(const float* grad_uv, const float* grad_uv_da, int64_t batch,
+                         int32_t height, int32_t width, const int32_t* tri, int64_t num_tri,
+                         const float* attr, int64_t attr_batch, int64_t num_vert,
+                         int32_t attr_channels, int32_t cu, int32_t cv, int32_t du, int32_t dv,
+                         const int64_t* keys, const float* pos, int64_t pos_batch,
+                         int64_t pos_num_vert, int32_t rast_db_gradient, float* grad_pos,
+                         void* stream);
 
 /* The whole mip chain at once (reference.py:433-488; texture_construct_mip, ops.py:239-265):
  * levels 1 .. levels of src [images, h, w, channels] into dst[0 .. levels - 1], each
