@@ -142,7 +142,7 @@ FUSE_RASTERIZE_BACKWARD = True
 # (dr_texture_chain_bwd) in the interpolation's, which autograd runs after the texture's gradient
 # is complete. The texture gradient is then final, and can be reduced across GPUs while the
 # position part runs; one fused pass is faster where nothing waits for the texture gradient.
-# diffrast_b200.distributed.OverlappedGradientSum turns it on from DEFER_RANKS ranks on.
+# diffrast_b200.distributed.OverlappedGradientSum turns it on when it sums across ranks.
 DEFER_CHAINED_BACKWARD = False
 
 

@@ -58,11 +58,11 @@ def sum_gradients(tensors: list[Tensor], group=None, bucket_bytes: int = 64 << 2
             dist.all_reduce(flat[start : start + step], group=group)
 
 
-# Ranks from which OverlappedGradientSum splits the texture lookups' fused backward pass (its
-# cost, the lookup set up twice, shrinks with the views per rank; the all-reduce it hides does
-# not): on 2 GPUs the fused pass with the all-reduce exposed is faster (11.27 against 11.61 ms
-# per step on config 5).
-DEFER_RANKS = 4
+# Ranks from which OverlappedGradientSum splits the texture lookups' fused backward pass: the
+# split costs a compact coordinate-gradient hand-over (on config 5, 1.96 + 0.86 ms against 2.63 ms
+# fused on 2 GPUs) and hides the texture gradient's all-reduce behind the position part (exposed
+# 0.47 -> 0.06 ms): 11.27 -> 11.01 ms per step on 2 GPUs, 6.20 -> 5.91 ms on 4.
+DEFER_RANKS = 2
 
 
 class OverlappedGradientSum:
