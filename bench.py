@@ -342,7 +342,7 @@ def build_scene(views_total: int, res: int, subdiv: int, tex_size: int, rank: in
 def run_ours(args) -> None:
     import diffrast_b200 as dr
     from diffrast_b200 import _kernels as K
-    from diffrast_b200.distributed import OverlappedGradientSum
+    from diffrast_b200.distributed import NextStepGradientSum, OverlappedGradientSum
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -371,17 +371,36 @@ def run_ours(args) -> None:
     mvp = mvp_cpu.to(dev)
     target = target_cpu.to(dev)
     topo = dr.antialias_construct_topology_hash(tri)
-    # The texture gradient's all-reduce starts as soon as the texture backward has produced it and
-    # overlaps the interpolation and rasterization backward passes; the positions' follows the
-    # transform's backward at the end of the step (no-ops on one GPU).
-    reducer = OverlappedGradientSum([tex, verts])
+    # On several GPUs the texture gradient's all-reduce runs during the next step's transform,
+    # rasterization and interpolation, which do not read the texture, and completes before its
+    # lookup (where an optimizer would apply it): synchronous data parallelism with the sum moved
+    # from the end of one step to the start of the next (the last step's sum runs after the timed
+    # steps, inside the timed region). The positions' all-reduce follows the transform's backward
+    # at the end of the step. On one GPU both are no-ops.
+    tex_sum = NextStepGradientSum(tex) if world > 1 else None
+    reducer = OverlappedGradientSum([verts] if world > 1 else [tex, verts], split_lookups=False)
+
+    def waited(wait):
+        if comm_events is None:
+            wait()
+            return
+        # Exposed communication: how long the compute stream waits for the sums.
+        before, after = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        before.record()
+        wait()
+        after.record()
+        comm_events.append((before, after))
 
     def step(mvp_in, target_in, before_loss=None):
+        if tex_sum is not None:
+            tex_sum.start()
         verts.grad = None
         tex.grad = None
         pos = dr.to_clip(verts, mvp_in)
         rast, rast_db = dr.rasterize(ctx, pos, tri, (res, res))
         out, out_da = dr.interpolate(attr, rast, tri, rast_db=rast_db, diff_attrs="all")
+        if tex_sum is not None:
+            waited(tex_sum.wait)
         color = dr.texture(tex, out[..., 0:2], out_da[..., 0:4], filter_mode="linear-mipmap-linear")
         # Antialias and the MSE against the target in one pass (dr.antialias_mse fuses the loss
         # into the antialias kernels); the mean runs over the whole job's pixels, so that the
@@ -391,17 +410,16 @@ def run_ours(args) -> None:
         _, loss = dr.antialias_mse(color, rast, pos, tri, target_in, topology_hash=topo,
                                    scale=1.0 / (args.views * res * res * TEX_CHANNELS))
         loss.backward()
-        if comm_events is not None:
-            # Exposed communication: how long the compute stream waits for the gradient sums
-            # after its own last backward kernel.
-            before, after = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            before.record()
-            reducer.wait()
-            after.record()
-            comm_events.append((before, after))
-        else:
-            reducer.wait()
+        waited(reducer.wait)
+        if tex_sum is not None:
+            tex_sum.hold()
         return loss
+
+    def last_sum():
+        """The last step's texture sum (inside the timed region)."""
+        if tex_sum is not None:
+            tex_sum.start()
+            waited(tex_sum.wait)
 
     comm_events = None
 
@@ -417,6 +435,7 @@ def run_ours(args) -> None:
         start.record()
         for _ in range(args.steps):
             body()
+        last_sum()
         end.record()
         torch.cuda.synchronize()
         if world > 1:
@@ -435,7 +454,7 @@ def run_ours(args) -> None:
         torch.cuda.synchronize()
     exposed = [b.elapsed_time(a) for b, a in comm_events] if comm_events else []
     comm_events = None
-    exposed_ms = torch.tensor([sum(exposed) / max(1, len(exposed))], device=dev)
+    exposed_ms = torch.tensor([sum(exposed) / args.steps], device=dev)
     if world > 1:
         dist.all_reduce(exposed_ms, op=dist.ReduceOp.MAX)
     stage_ms = {name: sum(s.elapsed_time(e) for s, e in pairs) / args.steps for name, pairs in stages.items()}
@@ -542,6 +561,7 @@ def run_ours(args) -> None:
     e2e_start, e2e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2e_start.record()
     e2e_loop()
+    last_sum()
     e2e_end.record()
     torch.cuda.synchronize()
     if world > 1:
@@ -635,8 +655,10 @@ def run_ours(args) -> None:
         "comm": {
             "allreduce_bytes_per_step": (tex.numel() + verts.numel()) * 4 if world > 1 else 0,
             "exposed_ms_per_step": round(exposed_ms.item(), 3),
-            "how": "eager timing pass: CUDA events on the compute stream before and after the wait "
-                   "for the texture and position gradient all-reduces (max over ranks)",
+            "how": "eager timing pass: CUDA events on the compute stream around its waits for the "
+                   "gradient all-reduces (the texture's, run during the next step's transform, "
+                   "rasterization and interpolation, waited before its lookup; the positions', at "
+                   "the end of the step), per step, max over ranks",
         },
         "clocks": clock,
     }

@@ -74,17 +74,19 @@ class OverlappedGradientSum:
     :meth:`wait` after ``backward()`` and before reading the gradients; it also reduces, with
     zeros, the tensors that received no gradient, so that every rank issues the same
     collectives. Every rank must run the same graph (the hooks then fire in the same order).
-    Without an initialised process group it does nothing.
+    Without an initialised process group it does nothing. ``split_lookups`` (for a texture among
+    ``tensors``) lets the lookups' backward passes complete the texture gradient first.
     """
 
-    def __init__(self, tensors: list[Tensor], group=None, bucket_bytes: int = 64 << 20) -> None:
+    def __init__(self, tensors: list[Tensor], group=None, bucket_bytes: int = 64 << 20,
+                 split_lookups: bool = True) -> None:
         self.tensors = list(tensors)
         self.group = group
         self.bucket_bytes = bucket_bytes
         self._pending: list = []
         self._done: set[int] = set()
         self._hooks = [t.register_post_accumulate_grad_hook(self._reduce) for t in self.tensors]
-        if self._active():
+        if self._active() and split_lookups:
             # From DEFER_RANKS ranks on, texture lookups complete the texture gradient before
             # their position gradient work (which then runs in the interpolation's backward pass),
             # so that the texture's all-reduce overlaps it (see
@@ -129,3 +131,62 @@ class OverlappedGradientSum:
         for h in self._hooks:
             h.remove()
         self._hooks.clear()
+
+
+class NextStepGradientSum:
+    """Sums a tensor's gradient across ranks while the next step's forward pass runs, up to the
+    tensor's first use in that step.
+
+    The texture of a render-and-fit step is first read by the texture lookup, after the transform,
+    the rasterization and the interpolation, none of which needs it. Its gradient sum can
+    therefore run during those passes instead of after the backward pass, where little work is
+    left to hide it behind: :meth:`hold` at the end of a step copies the local gradient into a
+    reduction buffer, :meth:`start` at the start of the next step issues its all-reduces, and
+    :meth:`wait`, before the tensor's first use (after which an optimizer would apply
+    :attr:`buffer`), completes them. This is the order of synchronous data parallelism, with the
+    sum moved from the end of one step to the start of the next; after the last step, :meth:`start`
+    and :meth:`wait` complete the last sum. Every rank must make the same calls. Without an
+    initialised process group it only copies.
+    """
+
+    def __init__(self, tensor: Tensor, group=None, bucket_bytes: int = 64 << 20) -> None:
+        self.tensor = tensor
+        self.group = group
+        self.bucket_bytes = bucket_bytes
+        self.buffer: Tensor | None = None
+        self._held = False
+        self._work: list = []
+
+    def _active(self) -> bool:
+        return dist.is_available() and dist.is_initialized()
+
+    def hold(self) -> None:
+        """Takes this step's local gradient (zeros when there is none) for the next sum."""
+        if self.buffer is None:
+            self.buffer = torch.zeros_like(self.tensor)
+        if self.tensor.grad is None:
+            self.buffer.zero_()
+        else:
+            self.buffer.copy_(self.tensor.grad)
+        self._held = True
+
+    def start(self) -> None:
+        """Issues the all-reduces of the held gradient, asynchronously (nothing when none is held)."""
+        if not self._held:
+            return
+        self._held = False
+        if not self._active():
+            return
+        flat = self.buffer.view(-1)
+        step = max(1, self.bucket_bytes // flat.element_size())
+        for first in range(0, flat.numel(), step):
+            self._work.append(
+                dist.all_reduce(flat[first : first + step], group=self.group, async_op=True)
+            )
+
+    def wait(self) -> None:
+        """Completes the sum (the current stream waits for it): :attr:`buffer` then holds the
+        previous step's gradient summed over the ranks."""
+        for work in self._work:
+            work.wait()
+        self._work.clear()

@@ -1,6 +1,7 @@
 """Data-parallel host logic on CPU with two gloo ranks: views are sharded, the texture and position
-gradients of each shard are summed across ranks, and the result equals the gradient of the whole
-batch on one process. The CPU oracle stands in for the kernels (the kernels need a GPU)."""
+gradients of each shard are summed across ranks (at the end of the step, from the backward pass's
+hooks, or during the next step), and the result equals the gradient of the whole batch on one
+process. The CPU oracle stands in for the kernels (the kernels need a GPU)."""
 
 import os
 import socket
@@ -12,7 +13,8 @@ import torch.multiprocessing as mp
 
 import oracle
 import scenes
-from diffrast_b200.distributed import OverlappedGradientSum, sum_gradients, view_shard
+from diffrast_b200.distributed import (NextStepGradientSum, OverlappedGradientSum, sum_gradients,
+                                      view_shard)
 
 
 def test_view_shard_covers_every_view_once():
@@ -68,7 +70,24 @@ def _rank(rank: int, world: int, port: int, results) -> None:
             reducer.wait()
             overlapped.append(tex2.grad.clone())
         reducer.remove()
-        results[rank] = (tex.grad.clone(), shard, p.grad.clone(), overlapped, unused.grad.clone())
+        # The texture's sum moved to the next step, before its first use: step k's loss is scaled
+        # by k + 1, so each sum must be that step's gradient and no other.
+        tex3 = tex.detach().clone().requires_grad_(True)
+        pipe = NextStepGradientSum(tex3, bucket_bytes=256)
+        pipelined = []
+        for step in range(3):
+            pipe.start()
+            pipe.wait()
+            if step > 0:
+                pipelined.append(pipe.buffer.clone())
+            tex3.grad = None
+            ((step + 1) * _loss(pos[shard].clone(), tri, tex3, uv, target[shard])).backward()
+            pipe.hold()
+        pipe.start()
+        pipe.wait()
+        pipelined.append(pipe.buffer.clone())
+        results[rank] = (tex.grad.clone(), shard, p.grad.clone(), overlapped, unused.grad.clone(),
+                         pipelined)
     finally:
         dist.destroy_process_group()
 
@@ -88,9 +107,12 @@ def test_two_ranks_sum_to_the_full_batch_gradient():
     p = pos.clone().requires_grad_(True)
     _loss(p, tri, tex, uv, target).backward()
     for rank in range(2):
-        tex_grad, shard, pos_grad, overlapped, unused_grad = results[rank]
+        tex_grad, shard, pos_grad, overlapped, unused_grad, pipelined = results[rank]
         torch.testing.assert_close(tex_grad, tex.grad, atol=1e-5, rtol=1e-5)
         torch.testing.assert_close(pos_grad, p.grad[shard], atol=1e-5, rtol=1e-5)
         for g in overlapped:
             torch.testing.assert_close(g, tex.grad, atol=1e-5, rtol=1e-5)
         assert torch.equal(unused_grad, torch.zeros(3))
+        assert len(pipelined) == 3
+        for k, g in enumerate(pipelined):
+            torch.testing.assert_close(g, (k + 1) * tex.grad, atol=1e-5, rtol=1e-5)
