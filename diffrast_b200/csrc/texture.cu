@@ -500,8 +500,11 @@ __device__ __forceinline__ void store_block(float* __restrict__ dst, const float
 }
 
 // One thread per pixel; with `staged` the block's 256 output pixels (one contiguous range) go
-// through shared memory so that the global stores are coalesced float4s.
-template <int MODE, int B>
+// through shared memory so that the global stores are coalesced float4s. NC > 0: exactly NC
+// channels, known at compile time, so that the channel loop unrolls and every channel's texel
+// gathers are in flight together (a runtime loop waits for each channel's gathers in turn); the
+// arithmetic of each channel is the same either way.
+template <int MODE, int B, int NC>
 __global__ void __launch_bounds__(256) texture_fwd_kernel(
     const Levels L, int channels, const float* __restrict__ uv, const float* __restrict__ uv_da,
     const float* __restrict__ bias, const Strides st, long long total, long long pixels_per_image,
@@ -524,21 +527,28 @@ __global__ void __launch_bounds__(256) texture_fwd_kernel(
     }
     Lookup<MODE, B> k;
     prepare<MODE, B>(L, channels, uv, uv_da, bias, st, p, view, k);
-    for (int c = 0; c < channels; ++c) {
+    const int nch = NC > 0 ? NC : channels;
+    auto channel = [&](int c) {
       float value;
       if (MODE == DR_FILTER_NEAREST) {
-        value = k.near_ok ? __ldg(L.ptr[0] + k.near_off * channels + c) : 0.0f;
+        value = k.near_ok ? __ldg(L.ptr[0] + k.near_off * nch + c) : 0.0f;
       } else {
         float t[4];
-        value = bilinear_value<B>(L.ptr[k.lo], k.f_lo, channels, c, t);
+        value = bilinear_value<B>(L.ptr[k.lo], k.f_lo, nch, c, t);
         if (MODE == DR_FILTER_LINEAR_MIPMAP_LINEAR) {
-          const float above = bilinear_value<B>(L.ptr[k.hi], k.f_hi, channels, c, t);
+          const float above = bilinear_value<B>(L.ptr[k.hi], k.f_hi, nch, c, t);
           value = add(mul(value, sub(1.0f, k.frac)), mul(above, k.frac));
         }
       }
       if (k.bad) value = kNaN;
       if (!k.valid) value = 0.0f;
       if (staged) o[c] = value; else __stcs(o + c, value);
+    };
+    if constexpr (NC > 0) {
+#pragma unroll
+      for (int c = 0; c < NC; ++c) channel(c);
+    } else {
+      for (int c = 0; c < channels; ++c) channel(c);
     }
   }
   if (!staged) return;
@@ -937,11 +947,15 @@ __device__ __forceinline__ void texture_bwd_tile(
   float g_fx_lo = 0.f, g_fy_lo = 0.f, g_fx_hi = 0.f, g_fy_hi = 0.f, g_frac = 0.f;
   if (live && MODE != DR_FILTER_NEAREST) {
     const float w_hi = k.frac, w_lo = 1.0f - k.frac;
-    for (int c = 0; c < channels; ++c) {
-      const float g = grad_out[p * channels + c];
+    // With RGB the channel count is known at compile time and the loop unrolls, so that all
+    // channels' texel gathers are in flight together.
+    const int nch = RGB ? 3 : channels;
+#pragma unroll
+    for (int c = 0; c < (RGB ? 3 : channels); ++c) {
+      const float g = grad_out[p * nch + c];
       const float g_lo = MODE == DR_FILTER_LINEAR_MIPMAP_LINEAR ? g * w_lo : g;
       float t[4];
-      const float lower = bilinear_value<B>(L.ptr[k.lo], k.f_lo, channels, c, t);
+      const float lower = bilinear_value<B>(L.ptr[k.lo], k.f_lo, nch, c, t);
       {
         const Footprint& f = k.f_lo;
         float dfx = (1.0f - f.fy) * (t[1] - t[0]) + f.fy * (t[3] - t[2]);
@@ -955,7 +969,7 @@ __device__ __forceinline__ void texture_bwd_tile(
         g_fy_lo += g_lo * dfy;
       }
       if (MODE == DR_FILTER_LINEAR_MIPMAP_LINEAR) {
-        const float upper = bilinear_value<B>(L.ptr[k.hi], k.f_hi, channels, c, t);
+        const float upper = bilinear_value<B>(L.ptr[k.hi], k.f_hi, nch, c, t);
         const Footprint& f = k.f_hi;
         float dfx = (1.0f - f.fy) * (t[1] - t[0]) + f.fy * (t[3] - t[2]);
         float dfy = (1.0f - f.fx) * (t[2] - t[0]) + f.fx * (t[3] - t[1]);
@@ -1375,8 +1389,12 @@ void launch_fwd(const Levels& L, int channels, const float* uv, const float* uv_
   // block barrier of staging costs more (3 channels on config 5: 1.78 ms staged, 1.64 ms direct).
   const size_t stage_bytes = sizeof(float) * 256 * static_cast<size_t>(channels);
   const bool staged = channels > 4 && stage_bytes <= 48 * 1024;
-  texture_fwd_kernel<MODE, B><<<blocks_for(total, 256), 256, staged ? stage_bytes : 0, s>>>(
-      L, channels, uv, uv_da, bias, st, total, ppi, out, staged);
+  if (channels == 3 && !staged)
+    texture_fwd_kernel<MODE, B, 3><<<blocks_for(total, 256), 256, 0, s>>>(
+        L, channels, uv, uv_da, bias, st, total, ppi, out, false);
+  else
+    texture_fwd_kernel<MODE, B, 0><<<blocks_for(total, 256), 256, staged ? stage_bytes : 0, s>>>(
+        L, channels, uv, uv_da, bias, st, total, ppi, out, staged);
 }
 
 template <int MODE, int B>
