@@ -340,7 +340,9 @@ struct FusedLoss {
 };
 
 // One block per 30 x 14 output pixels of a view (a 32 x 16 thread tile with a one-pixel halo).
-template <bool kLoss>
+// NC > 0: exactly NC colour channels, known at compile time: constant address arithmetic in the
+// blend loop, which stays rolled (unrolled, its loads spill under the 40-register cap).
+template <bool kLoss, int NC>
 __global__ void __launch_bounds__(kFwdX * kFwdY, 3) aa_fwd_kernel(const AaCtx a,
                                                                    float* __restrict__ out,
                                                                    PairRecords rec,
@@ -463,8 +465,8 @@ __global__ void __launch_bounds__(kFwdX * kFwdY, 3) aa_fwd_kernel(const AaCtx a,
     // (second), lower pair (first), upper pair (second).
     const float k[4] = {right.bp, left.bq, down.bp, up.bq};
     const long long other[4] = {p + 1, p - 1, p + a.width, p - a.width};
-    const int C = a.channels;
-    for (int c = 0; c < C; ++c) {
+    const int C = NC > 0 ? NC : a.channels;
+    auto blend = [&](int c) {
       const float self = __ldg(a.color + p * C + c);
       float value = self;
       for (int i = 0; i < 4; ++i) {
@@ -476,6 +478,12 @@ __global__ void __launch_bounds__(kFwdX * kFwdY, 3) aa_fwd_kernel(const AaCtx a,
         loss.residual[p * C + c] = d;
         sq = fmaf(d, d, sq);
       }
+    };
+    if constexpr (NC > 0) {
+#pragma unroll 1
+      for (int c = 0; c < NC; ++c) blend(c);
+    } else {
+      for (int c = 0; c < C; ++c) blend(c);
     }
   }
   if (kLoss) {
@@ -907,8 +915,12 @@ extern "C" int dr_antialias_fwd(const float* color, const float* rast, const flo
   const AaCtx a = make_ctx(color, rast, pos, pos_batch, num_vert, tri, num_tri, opposite, height,
                            width, channels);
   if (batch > 65535) return DR_ERR_TOO_LARGE;
-  aa_fwd_kernel<false><<<fwd_grid(batch, height, width), kFwdX * kFwdY, 0, as_stream(stream)>>>(
-      a, out, pair_records(pairs, total), FusedLoss{nullptr, nullptr, nullptr});
+  if (channels == 3)
+    aa_fwd_kernel<false, 3><<<fwd_grid(batch, height, width), kFwdX * kFwdY, 0, as_stream(stream)>>>(
+        a, out, pair_records(pairs, total), FusedLoss{nullptr, nullptr, nullptr});
+  else
+    aa_fwd_kernel<false, 0><<<fwd_grid(batch, height, width), kFwdX * kFwdY, 0, as_stream(stream)>>>(
+        a, out, pair_records(pairs, total), FusedLoss{nullptr, nullptr, nullptr});
   return launch_status();
 }
 
@@ -933,8 +945,12 @@ extern "C" int dr_antialias_mse_fwd(const float* color, const float* rast, const
   if (batch > 65535) return DR_ERR_TOO_LARGE;
   const AaCtx a = make_ctx(color, rast, pos, pos_batch, num_vert, tri, num_tri, opposite, height,
                            width, channels);
-  aa_fwd_kernel<true><<<fwd_grid(batch, height, width), kFwdX * kFwdY, 0, as_stream(stream)>>>(
-      a, out, pair_records(pairs, total), FusedLoss{target, residual, partial_sums});
+  if (channels == 3)
+    aa_fwd_kernel<true, 3><<<fwd_grid(batch, height, width), kFwdX * kFwdY, 0, as_stream(stream)>>>(
+        a, out, pair_records(pairs, total), FusedLoss{target, residual, partial_sums});
+  else
+    aa_fwd_kernel<true, 0><<<fwd_grid(batch, height, width), kFwdX * kFwdY, 0, as_stream(stream)>>>(
+        a, out, pair_records(pairs, total), FusedLoss{target, residual, partial_sums});
   return launch_status();
 }
 
