@@ -657,6 +657,8 @@ __device__ __forceinline__ void chain_interpolation(const InterpChain& c, long l
   float gu = 0.0f, gv = 0.0f;
   float g_dudx = 0.0f, g_dudy = 0.0f, g_dvdx = 0.0f, g_dvdy = 0.0f;
   int i0 = 0, i1 = 0, i2 = 0;
+  Vert v0 = {0.f, 0.f, 0.f, 1.f}, v1 = v0, v2 = v0;
+  const long long pbase = view * c.pos_view_stride;
   if (t >= 0) {
     const int* vt = c.tri + 3 * static_cast<long long>(t);
     i0 = __ldg(vt);
@@ -666,21 +668,40 @@ __device__ __forceinline__ void chain_interpolation(const InterpChain& c, long l
     const float* a0 = base + checked_index(i0, c.num_vert, kSiteVertex) * c.attr_channels;
     const float* a1 = base + checked_index(i1, c.num_vert, kSiteVertex) * c.attr_channels;
     const float* a2 = base + checked_index(i2, c.num_vert, kSiteVertex) * c.attr_channels;
-    const int ch[2] = {c.cu, c.cv};
+    // Every gather of the pixel is issued once its triangle's indices are in: the coordinate and
+    // (when rast_db's gradient is wanted) derivative channels of the three attribute rows and,
+    // with RESOLVE, the three vertices; the arithmetic below is unchanged.
+    const bool want_db = c.grad_db != nullptr || c.resolve_db;
+    const int ch[2] = {c.cu, c.cv}, dch[2] = {c.du, c.dv};
+    float x[2][3], xd[2][3];
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
-      const float x0 = __ldg(a0 + ch[i]), x1 = __ldg(a1 + ch[i]), x2 = __ldg(a2 + ch[i]);
-      gu += g_uv[i] * (x0 - x2);
-      gv += g_uv[i] * (x1 - x2);
+      x[i][0] = __ldg(a0 + ch[i]);
+      x[i][1] = __ldg(a1 + ch[i]);
+      x[i][2] = __ldg(a2 + ch[i]);
+      xd[i][0] = want_db ? __ldg(a0 + dch[i]) : 0.0f;
+      xd[i][1] = want_db ? __ldg(a1 + dch[i]) : 0.0f;
+      xd[i][2] = want_db ? __ldg(a2 + dch[i]) : 0.0f;
     }
-    if (c.grad_db != nullptr || c.resolve_db) {
-      const int dch[2] = {c.du, c.dv};
+    if constexpr (RESOLVE) {
+      i0 = static_cast<int>(checked_index(i0, c.pos_num_vert, kSiteVertex));
+      i1 = static_cast<int>(checked_index(i1, c.pos_num_vert, kSiteVertex));
+      i2 = static_cast<int>(checked_index(i2, c.pos_num_vert, kSiteVertex));
+      v0 = load_vert(c.pos, pbase + i0);
+      v1 = load_vert(c.pos, pbase + i1);
+      v2 = load_vert(c.pos, pbase + i2);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      gu += g_uv[i] * (x[i][0] - x[i][2]);
+      gv += g_uv[i] * (x[i][1] - x[i][2]);
+    }
+    if (want_db) {
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
         const float gx = g_da[2 * j], gy = g_da[2 * j + 1];
-        const float x2 = __ldg(a2 + dch[j]);
-        const float du = __ldg(a0 + dch[j]) - x2;
-        const float dv = __ldg(a1 + dch[j]) - x2;
+        const float du = xd[j][0] - xd[j][2];
+        const float dv = xd[j][1] - xd[j][2];
         g_dudx += gx * du;
         g_dudy += gy * du;
         g_dvdx += gx * dv;
@@ -695,17 +716,10 @@ __device__ __forceinline__ void chain_interpolation(const InterpChain& c, long l
     return;
   } else {
   float gvert[3][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-  const long long pbase = view * c.pos_view_stride;
-  if (t >= 0) {
-    i0 = static_cast<int>(checked_index(i0, c.pos_num_vert, kSiteVertex));
-    i1 = static_cast<int>(checked_index(i1, c.pos_num_vert, kSiteVertex));
-    i2 = static_cast<int>(checked_index(i2, c.pos_num_vert, kSiteVertex));
-    const Vert v0 = load_vert(c.pos, pbase + i0), v1 = load_vert(c.pos, pbase + i1),
-               v2 = load_vert(c.pos, pbase + i2);
+  if (t >= 0)
     resolve_adjoint(v0, v1, v2, pixel_centre(col, width), pixel_centre(row, height),
                     make_float4(gu, gv, 0.0f, 0.0f), c.resolve_db,
                     make_float4(g_dudx, g_dudy, g_dvdx, g_dvdy), width, height, gvert);
-  }
   // Each pixel adds its own three vector reductions: a warp covers 16 x 2 pixels, where a
   // triangle (about four pixels on config 5) repeats too rarely for a warp-level merge to pay
   // for its shuffles (5.39 ms with it, 5.27 without).
