@@ -57,9 +57,10 @@ LAUNCHES = {
 
 def mip_launches(h: int, w: int, channels: int) -> tuple[int, int]:
     """Kernels of one dr_mip_build call (runs of even halvings, up to six levels per launch, with
-    at most 4 channels; one launch per other level) and of one dr_mip_build_bwd call (one per
-    level) for an h x w texture's full chain."""
-    levels, build, lh, lw = 0, 0, h, w
+    at most 4 channels; one launch per other level) and of one dr_mip_build_bwd call (the same
+    steps undone: one launch per run, its 16-byte aligned, at most 4-channel padded gradient
+    levels taking the run kernel; one per other level) for an h x w texture's full chain."""
+    build, lh, lw = 0, h, w
     while lh > 1 or lw > 1:
         n = 0
         while n < 6 and (lh >> n) % 2 == 0 and (lw >> n) % 2 == 0 and (lh >> n, lw >> n) != (1, 1):
@@ -67,9 +68,8 @@ def mip_launches(h: int, w: int, channels: int) -> tuple[int, int]:
         step = n if n >= 2 and channels <= 4 else 1
         for _ in range(step):
             lh, lw = (lh + 1) // 2, (lw + 1) // 2
-        levels += step
         build += 1
-    return build, levels
+    return build, build
 
 
 def stage_bytes(pixels: int, num_vert: int, views: int, stack_bytes: int, tex_bytes: int,
